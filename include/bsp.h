@@ -1,0 +1,203 @@
+/*
+ * bsp.h -- C ABI of the B200 block-sparse SpMM / SDDMM library (libbsp.so).
+ *
+ * This is the drop-in boundary for the reference's block-sparse hot path
+ * (salmanra/Tenstorrent-WH-BlockSpMM).  Every entry point below names the
+ * reference interface it replaces (file:line inside the reference project).
+ * Plain pointers and sizes only: no C++ or torch types cross this boundary.
+ *
+ * Layout (all row-major, bf16 = raw 16-bit brain-float bit patterns):
+ *   BSR matrix  H x W with R x C blocks:
+ *     row_ptr[H/R + 1] int32, col_idx[nnzb] int32,
+ *     values[nnzb * R * C]: block b occupies values[b*R*C .. (b+1)*R*C), row-major.
+ *     This is the reference's bsr_matrix (sparse_common/bsr_matrix.hpp:202-213)
+ *     without the tt-metal tilize step (test_block_spmm.cpp:77-78): blocks are
+ *     row-major, so no tilize/untilize is needed.
+ *   Dense matrix: row-major with a leading dimension (elements).
+ *
+ * Requirements checked by every call (BSP_ERR_INVALID_ARG otherwise):
+ *   R % 32 == 0, C % 32 == 0, H % R == 0, W % C == 0      (reference: TT_ASSERTs,
+ *     block_spmm/inc/host_code/bsr_spmm_multicore_load_balanced_new_DM.cpp:67-69)
+ *   N % 8 == 0, leading dimensions % 8 == 0 (bf16) / % 4 (f32),
+ *   device pointers 16-byte aligned.
+ *
+ * Streams are passed as `void*` (a cudaStream_t; NULL = legacy default stream).
+ * Execute calls are stream-ordered and asynchronous; device-side errors (a
+ * kernel wait that timed out) are latched in the device and reported by
+ * bsp_device_synchronize / bsp_device_get_error.
+ */
+#ifndef BSP_H_
+#define BSP_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define BSP_VERSION_MAJOR 0
+#define BSP_VERSION_MINOR 1
+
+/* Status codes.  The reference reports errors by TT_ASSERT/TT_THROW
+ * exceptions (e.g. load_balanced_new_DM.cpp:67-69); the C ABI returns codes
+ * and keeps a per-thread message (bsp_last_error_string). */
+typedef enum bsp_status {
+  BSP_OK = 0,
+  BSP_ERR_INVALID_ARG = 1,
+  BSP_ERR_UNSUPPORTED = 2,
+  BSP_ERR_CUDA = 3,
+  BSP_ERR_TIMEOUT = 4,   /* a bounded in-kernel wait gave up; see bsp_device_get_error */
+  BSP_ERR_NCCL = 5,
+  BSP_ERR_ALLOC = 6,
+  BSP_ERR_STATE = 7
+} bsp_status;
+
+/* Dataflow strategies of the reference, re-expressed for one B200 CTA:
+ *   NAIVE: each work unit (block-row x 128-column tile) loads its own A blocks
+ *          and B slices.  Reference "Naive",
+ *          block_spmm/inc/host_code/bsr_spmm_multicore_load_balanced_new_DM.cpp:6-536
+ *          and block_sddmm/inc/host_code/bsr_sddmm_multicore_naive.cpp:6-352.
+ *   SNF:   an A block is loaded once and multiplied against several 128-column
+ *          tiles of B (the reuse that store-and-forward along a core row gives).
+ *          Reference "SnF in0", block_spmm/inc/host_code/bsr_spmm_multicore_snf.cpp:16-781.
+ *   DDA:   SNF plus: a B slice is loaded once and shared by every block-row of
+ *          a row group that has a block in that column (the reuse that the
+ *          chain of direct addressing gives).  Reference "SnF in0 + CDA in1",
+ *          block_spmm/inc/host_code/bsr_spmm_multicore_snfin0_cdain1.cpp:8-843;
+ *          for SDDMM the A row panel is kept on chip across a row's blocks,
+ *          block_sddmm/inc/host_code/bsr_sddmm_multicore_CDA.cpp:28-490. */
+typedef enum bsp_strategy { BSP_NAIVE = 0, BSP_SNF = 1, BSP_DDA = 2 } bsp_strategy;
+
+typedef enum bsp_dtype { BSP_BF16 = 0, BSP_F32 = 1 } bsp_dtype;
+
+/* A BSR matrix whose arrays live in device memory (caller-owned). */
+typedef struct bsp_bsr_desc {
+  int64_t rows;           /* H */
+  int64_t cols;           /* W */
+  int32_t R;              /* block rows */
+  int32_t C;              /* block cols */
+  int64_t nnzb;           /* number of stored blocks */
+  const int32_t* row_ptr; /* device, rows/R + 1 entries */
+  const int32_t* col_idx; /* device, nnzb entries */
+  const void* values;     /* device, nnzb*R*C bf16 (may be NULL for an SDDMM mask) */
+} bsp_bsr_desc;
+
+/* Options.  Zero-initialise and set what you need; 0 means "library default". */
+typedef struct bsp_spmm_opts {
+  int32_t no_load_balance; /* 1: contiguous unit split, the reference's *_no_lb
+                              variants (block_spmm/inc/host_code.hpp:113-161) */
+  int32_t group_rows;      /* DDA: block-rows per row group (B-slice sharing) */
+  int32_t n_tiles;         /* SNF/DDA: 128-column tiles per work unit (A reuse) */
+  int32_t max_ctas;        /* cap on persistent CTAs (default: all SMs) */
+  int32_t timeout_ms;      /* bound on every in-kernel wait (default 2000) */
+  int32_t reserved[3];
+} bsp_spmm_opts;
+
+typedef bsp_spmm_opts bsp_sddmm_opts;
+
+/* ---- device context ---------------------------------------------------
+ * Replaces the reference's IDevice* (tt-metal CreateDevice/CloseDevice,
+ * block_spmm/src/test_block_spmm.cpp:52).  Holds SM count, the tensor-map
+ * encoder and a small device status word written by the kernels. */
+typedef struct bsp_device bsp_device;
+
+bsp_status bsp_device_open(int ordinal, bsp_device** out);
+bsp_status bsp_device_close(bsp_device* dev);
+/* cudaDeviceSynchronize + read and clear the kernels' latched status word. */
+bsp_status bsp_device_synchronize(bsp_device* dev);
+/* Latched device status bits (0 = none) without clearing; stream-synchronous. */
+bsp_status bsp_device_get_error(bsp_device* dev, uint32_t* bits);
+int bsp_device_sm_count(const bsp_device* dev);
+
+const char* bsp_last_error_string(void);
+const char* bsp_status_string(bsp_status s);
+
+/* ---- SpMM: C[M x N] = A_bsr[M x K] * B[K x N] ---------------------------
+ * Replaces HostCodeFunctionPtr (block_spmm/inc/host_code.hpp:165-177) and the
+ * three planners behind it.  A plan is the reference planner's output (row
+ * folding, serpentine load balance, tiling: load_balanced_new_DM.cpp:50-393)
+ * for one sparsity pattern and one N; it owns a small device-side schedule.
+ * Every element of C is written, including the rows of empty block-rows
+ * (the reference leaves those to the caller's zero-initialised buffer,
+ * load_balanced_new_DM.cpp:524-531). */
+typedef struct bsp_spmm_plan bsp_spmm_plan;
+
+/* host_row_ptr / host_col_idx: host copies of A's pattern; pass NULL to have
+ * the plan copy them from A (synchronous D2H). */
+bsp_status bsp_spmm_plan_create(bsp_device* dev, const bsp_bsr_desc* A, const int32_t* host_row_ptr,
+                                const int32_t* host_col_idx, int64_t N, bsp_dtype c_type,
+                                bsp_strategy strategy, const bsp_spmm_opts* opts,
+                                bsp_spmm_plan** out);
+/* A must have the pattern the plan was built for; values may differ. */
+bsp_status bsp_spmm_execute(const bsp_spmm_plan* plan, const bsp_bsr_desc* A, const void* B,
+                            int64_t ldb, void* C, int64_t ldc, void* stream);
+bsp_status bsp_spmm_plan_destroy(bsp_spmm_plan* plan);
+/* Plan facts: [0]=units [1]=ctas [2]=group_rows [3]=n_tiles [4]=sub-row height
+ * [5]=k chunk [6]=pipeline stages [7]=steps [8]=plan device bytes. */
+bsp_status bsp_spmm_plan_info(const bsp_spmm_plan* plan, int64_t info[16]);
+
+/* One-shot: plan, execute on `stream`, synchronise, destroy. */
+bsp_status bsp_spmm(bsp_device* dev, const bsp_bsr_desc* A, const void* B, int64_t ldb, void* C,
+                    int64_t ldc, bsp_dtype c_type, int64_t N, bsp_strategy strategy,
+                    const bsp_spmm_opts* opts, void* stream);
+
+/* Host-buffer entry point, the semantics of the reference planners: host
+ * arrays in, host C out (M x N bf16, row-major, fully written).  Copies in,
+ * plans, runs, copies out, synchronises (block_spmm/inc/host_code/
+ * bsr_spmm_multicore_load_balanced_new_DM.cpp:502-535).  Device buffers come
+ * from a grow-only workspace held by `dev`. */
+bsp_status bsp_spmm_host(bsp_device* dev, int64_t M, int64_t K, int32_t R, int32_t C, int64_t nnzb,
+                         const int32_t* row_ptr, const int32_t* col_idx, const uint16_t* values,
+                         const uint16_t* B, int64_t N, uint16_t* C_out, bsp_strategy strategy,
+                         const bsp_spmm_opts* opts);
+
+/* ---- SDDMM: out = mask (.) (A[M x K] * B[K x N]) on mask's pattern --------
+ * Replaces SDDMMHostCodeFunctionPtr (block_sddmm/inc/host_code.hpp:104-115):
+ * out_values[b*R*C + r*C + c] for every mask block b, in mask order; the output
+ * pattern is the mask's pattern (bsr_sddmm_multicore_naive.cpp:333-346).
+ * mask->values may be NULL: every mask value is 1 (pure sampling). */
+typedef struct bsp_sddmm_plan bsp_sddmm_plan;
+
+bsp_status bsp_sddmm_plan_create(bsp_device* dev, const bsp_bsr_desc* mask,
+                                 const int32_t* host_row_ptr, const int32_t* host_col_idx,
+                                 int64_t K, bsp_strategy strategy, const bsp_sddmm_opts* opts,
+                                 bsp_sddmm_plan** out);
+bsp_status bsp_sddmm_execute(const bsp_sddmm_plan* plan, const bsp_bsr_desc* mask, const void* A,
+                             int64_t lda, const void* B, int64_t ldb, void* out_values,
+                             void* stream);
+bsp_status bsp_sddmm_plan_destroy(bsp_sddmm_plan* plan);
+bsp_status bsp_sddmm_plan_info(const bsp_sddmm_plan* plan, int64_t info[16]);
+
+bsp_status bsp_sddmm(bsp_device* dev, const bsp_bsr_desc* mask, const void* A, int64_t lda,
+                     const void* B, int64_t ldb, int64_t K, void* out_values,
+                     bsp_strategy strategy, const bsp_sddmm_opts* opts, void* stream);
+
+/* Host-buffer SDDMM (reference semantics: host containers in, host BSR out
+ * with the mask's pattern; bsr_sddmm_multicore_naive.cpp:6-352).
+ * mask_values may be NULL (all ones). */
+bsp_status bsp_sddmm_host(bsp_device* dev, int64_t M, int64_t N, int32_t R, int32_t C,
+                          int64_t nnzb, const int32_t* row_ptr, const int32_t* col_idx,
+                          const uint16_t* mask_values, const uint16_t* A, const uint16_t* B,
+                          int64_t K, uint16_t* out_values, bsp_strategy strategy,
+                          const bsp_sddmm_opts* opts);
+
+/* ---- multi-GPU helpers (host logic; the exchange itself is NCCL) --------
+ * Contiguous block-row ranges for `parts` GPUs balanced by nonzero-block
+ * count (a generalisation of the reference's serpentine balancer,
+ * block_spmm/inc/host_code/bsr_spmm_multicore_load_balanced_new_DM.cpp:346-393,
+ * to ranges, so that each GPU's C row-panel is contiguous for the all-gather).
+ * bounds[parts + 1]: GPU p owns block-rows [bounds[p], bounds[p+1]). */
+bsp_status bsp_partition_rows(const int32_t* row_ptr, int64_t n_block_rows, int32_t parts,
+                              int64_t* bounds);
+
+/* The reference's serpentine balancer, exposed for tests: rows sorted by
+ * work, heaviest first (`perm`), dealt to `parts` workers in zig-zag passes.
+ * owner[k] / slot[k]: worker and position of perm[k].
+ * (block_spmm/inc/host_code.hpp:225-235 + load_balanced_new_DM.cpp:346-393) */
+bsp_status bsp_serpentine_assign(int64_t n, int32_t parts, int32_t* owner, int32_t* slot);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* BSP_H_ */

@@ -1,0 +1,257 @@
+"""CPU checkers for the block-sparse SpMM / SDDMM path.
+
+TEST INFRASTRUCTURE ONLY.  Only tests/, ``__graft_entry__.smoke()`` and the
+cpu_baseline / reference legs of ``bench.py`` import this package, and only as
+the checker or the timed CPU baseline.  The product library never does.
+
+Two checkers live here:
+
+* ``liboracle.so`` (built from ``bsp_oracle.c``): my restatement of the
+  reference golden, reference lines cited in the C source.
+* ``_ref/libref_golden.so``: the reference's own golden
+  (``sparse_common/bsr_matrix.hpp``), compiled from the reference sources in
+  place by ``oracle/Makefile``.  It pins the restatement; it is optional at run
+  time (absent when the reference sources were not available to build it).
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+_ORACLE_SO = os.path.join(HERE, "liboracle.so")
+_REF_SO = os.path.join(HERE, "_ref", "libref_golden.so")
+
+_i64 = ctypes.c_int64
+_i32 = ctypes.c_int32
+_p = ctypes.c_void_p
+
+_lib = None
+_ref = None
+
+
+def build(quiet: bool = True) -> None:
+    """Compile the checkers (oracle/Makefile)."""
+    out = subprocess.run(["make", "-C", HERE], capture_output=True, text=True)
+    if out.returncode != 0:
+        raise RuntimeError("oracle build failed:\n" + out.stdout + out.stderr)
+    if not quiet:
+        print(out.stdout)
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(_ORACLE_SO):
+            build()
+        _lib = ctypes.CDLL(_ORACLE_SO)
+        P, I = _p, _i64
+        _lib.bsp_oracle_spmm_bf16_mt.argtypes = [I, I, I, I, P, P, P, I, P, P, I, I, _i32]
+        _lib.bsp_oracle_spmm_f32.argtypes = [I, I, I, I, P, P, P, I, P, P, I, I]
+        _lib.bsp_oracle_sddmm_bf16_mt.argtypes = [I, I, I, I, P, P, P, I, P, P, P, I, I, _i32]
+        _lib.bsp_oracle_sddmm_f32.argtypes = [I, I, I, I, P, P, P, I, P, P, P, I, I]
+        _lib.bsp_oracle_serpentine.argtypes = [I, I, P, P]
+    return _lib
+
+
+def ref_available() -> bool:
+    return os.path.exists(_REF_SO)
+
+
+def ref():
+    """The reference's own golden (None when it was not built)."""
+    global _ref
+    if _ref is None and ref_available():
+        _ref = ctypes.CDLL(_REF_SO)
+        P, I = _p, _i64
+        _ref.ref_spmm_bf16.argtypes = [I, I, I, I, I, P, P, P, I, P, P]
+        _ref.ref_omp_spmm_bf16.argtypes = [I, I, I, I, I, P, P, P, I, P, P]
+        _ref.ref_spmm_f32.argtypes = [I, I, I, I, I, P, P, P, I, P, P]
+        _ref.ref_sddmm_bf16.argtypes = [I, I, I, I, I, P, P, P, I, P, P, P, P, P]
+        _ref.ref_sddmm_f32.argtypes = [I, I, I, I, I, P, P, P, I, P, P, P]
+        _ref.ref_pcc_bf16.argtypes = [P, P, I]
+        _ref.ref_pcc_bf16.restype = ctypes.c_float
+        _ref.ref_bsr_generate.argtypes = [I, I, I, I, I, _i32, _i32, ctypes.c_uint32, P, P, P]
+        _ref.ref_bsr_generate.restype = _i64
+        _ref.ref_dense_generate.argtypes = [I, I, _i32, ctypes.c_uint32, P]
+        _ref.ref_spmm_bf16_timed.argtypes = [I, I, I, I, P, P, P, I, P, I, I, _i32, _i32]
+        _ref.ref_spmm_bf16_timed.restype = ctypes.c_double
+        _ref.ref_sddmm_bf16_timed.argtypes = [I, I, I, I, P, P, P, I, P, P, I, I, _i32, _i32]
+        _ref.ref_sddmm_bf16_timed.restype = ctypes.c_double
+    return _ref
+
+
+def _ptr(a):
+    return None if a is None else a.ctypes.data
+
+
+def _c(a, dt):
+    return None if a is None else np.ascontiguousarray(a, dtype=dt)
+
+
+# ---- bf16 helpers (raw uint16 bit patterns) -------------------------------
+
+def f32_to_bf16(x: np.ndarray) -> np.ndarray:
+    """Round-to-nearest-even f32 -> bf16 bits (NaN kept quiet)."""
+    u = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32).astype(np.uint64)
+    nan = (u & 0x7FFFFFFF) > 0x7F800000
+    r = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+    r[nan] = ((u[nan] >> 16) | 0x40).astype(np.uint16)
+    return r
+
+
+def bf16_to_f32(b: np.ndarray) -> np.ndarray:
+    return (np.ascontiguousarray(b, dtype=np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+# ---- the restatement -------------------------------------------------------
+
+def spmm_bf16(indptr, indices, data, H, W, R, C, B, N, threads=None, rows=None):
+    """C = A_bsr @ B, bf16 bits in / out (see bsp_oracle_spmm_bf16)."""
+    indptr, indices = _c(indptr, np.int32), _c(indices, np.int32)
+    data, B = _c(data, np.uint16), _c(B, np.uint16)
+    out = np.zeros((H, N), dtype=np.uint16)
+    r0, r1 = rows if rows is not None else (0, H // R)
+    lib().bsp_oracle_spmm_bf16_mt(H, W, R, C, _ptr(indptr), _ptr(indices), _ptr(data), N,
+                                  _ptr(B), _ptr(out), r0, r1, threads or os.cpu_count() or 1)
+    return out
+
+
+def spmm_f32(indptr, indices, data, H, W, R, C, B, N):
+    indptr, indices = _c(indptr, np.int32), _c(indices, np.int32)
+    data, B = _c(data, np.float32), _c(B, np.float32)
+    out = np.zeros((H, N), dtype=np.float32)
+    lib().bsp_oracle_spmm_f32(H, W, R, C, _ptr(indptr), _ptr(indices), _ptr(data), N, _ptr(B),
+                              _ptr(out), 0, H // R)
+    return out
+
+
+def sddmm_bf16(indptr, indices, mask_data, H, W, R, C, A, B, K, threads=None):
+    """out_blocks = mask (.) (A @ B) on the mask pattern, bf16 bits."""
+    indptr, indices = _c(indptr, np.int32), _c(indices, np.int32)
+    mask_data, A, B = _c(mask_data, np.uint16), _c(A, np.uint16), _c(B, np.uint16)
+    nnzb = int(indptr[-1])
+    out = np.zeros(nnzb * R * C, dtype=np.uint16)
+    lib().bsp_oracle_sddmm_bf16_mt(H, W, R, C, _ptr(indptr), _ptr(indices), _ptr(mask_data), K,
+                                   _ptr(A), _ptr(B), _ptr(out), 0, H // R,
+                                   threads or os.cpu_count() or 1)
+    return out
+
+
+def sddmm_f32(indptr, indices, mask_data, H, W, R, C, A, B, K):
+    indptr, indices = _c(indptr, np.int32), _c(indices, np.int32)
+    mask_data, A, B = _c(mask_data, np.float32), _c(A, np.float32), _c(B, np.float32)
+    nnzb = int(indptr[-1])
+    out = np.zeros(nnzb * R * C, dtype=np.float32)
+    lib().bsp_oracle_sddmm_f32(H, W, R, C, _ptr(indptr), _ptr(indices), _ptr(mask_data), K,
+                               _ptr(A), _ptr(B), _ptr(out), 0, H // R)
+    return out
+
+
+def serpentine(n: int, parts: int):
+    """(owner, slot) per position of the heaviest-first permutation."""
+    owner = np.zeros(n, dtype=np.int32)
+    slot = np.zeros(n, dtype=np.int32)
+    lib().bsp_oracle_serpentine(n, parts, _ptr(owner), _ptr(slot))
+    return owner, slot
+
+
+# ---- the reference golden (oracle/_ref) -----------------------------------
+
+def ref_spmm_bf16(indptr, indices, data, H, W, R, C, B, N, omp_variant=False):
+    r = ref()
+    indptr, indices = _c(indptr, np.int32), _c(indices, np.int32)
+    data, B = _c(data, np.uint16), _c(B, np.uint16)
+    out = np.zeros((H, N), dtype=np.uint16)
+    fn = r.ref_omp_spmm_bf16 if omp_variant else r.ref_spmm_bf16
+    fn(H, W, R, C, int(indptr[-1]), _ptr(indptr), _ptr(indices), _ptr(data), N, _ptr(B), _ptr(out))
+    return out
+
+
+def ref_spmm_f32(indptr, indices, data, H, W, R, C, B, N):
+    r = ref()
+    indptr, indices = _c(indptr, np.int32), _c(indices, np.int32)
+    data, B = _c(data, np.float32), _c(B, np.float32)
+    out = np.zeros((H, N), dtype=np.float32)
+    r.ref_spmm_f32(H, W, R, C, int(indptr[-1]), _ptr(indptr), _ptr(indices), _ptr(data), N,
+                   _ptr(B), _ptr(out))
+    return out
+
+
+def ref_sddmm_bf16(indptr, indices, mask_data, H, W, R, C, A, B, K):
+    """Returns (out_blocks, out_indptr, out_indices) from the reference golden."""
+    r = ref()
+    indptr, indices = _c(indptr, np.int32), _c(indices, np.int32)
+    nnzb = int(indptr[-1])
+    if mask_data is None:
+        mask_data = np.full(nnzb * R * C, 0x3F80, dtype=np.uint16)  # 1.0
+    mask_data, A, B = _c(mask_data, np.uint16), _c(A, np.uint16), _c(B, np.uint16)
+    out = np.zeros(nnzb * R * C, dtype=np.uint16)
+    oip = np.zeros(H // R + 1, dtype=np.int32)
+    oix = np.zeros(max(nnzb, 1), dtype=np.int32)
+    r.ref_sddmm_bf16(H, W, R, C, nnzb, _ptr(indptr), _ptr(indices), _ptr(mask_data), K, _ptr(A),
+                     _ptr(B), _ptr(out), _ptr(oip), _ptr(oix))
+    return out, oip, oix[:nnzb]
+
+
+def ref_sddmm_f32(indptr, indices, mask_data, H, W, R, C, A, B, K):
+    r = ref()
+    indptr, indices = _c(indptr, np.int32), _c(indices, np.int32)
+    nnzb = int(indptr[-1])
+    if mask_data is None:
+        mask_data = np.ones(nnzb * R * C, dtype=np.float32)
+    mask_data, A, B = _c(mask_data, np.float32), _c(A, np.float32), _c(B, np.float32)
+    out = np.zeros(nnzb * R * C, dtype=np.float32)
+    r.ref_sddmm_f32(H, W, R, C, nnzb, _ptr(indptr), _ptr(indices), _ptr(mask_data), K, _ptr(A),
+                    _ptr(B), _ptr(out))
+    return out
+
+
+def ref_pcc(a_bf16, b_bf16) -> float:
+    a, b = _c(a_bf16.ravel(), np.uint16), _c(b_bf16.ravel(), np.uint16)
+    return float(ref().ref_pcc_bf16(_ptr(a), _ptr(b), a.size))
+
+
+FILL_ROW, FILL_COL, FILL_DIAG, FILL_TRIL, FILL_MULTI_DIAG = 1, 2, 3, 4, 5
+RAND, UNIFORM, ARANGE, ID = 0, 1, 2, 3
+
+
+def ref_generate_bsr(H, W, R, C, nblocks, fill, content, seed=42):
+    """The reference's own pattern generator; returns (indptr, indices, data_f32)."""
+    r = ref()
+    n = r.ref_bsr_generate(H, W, R, C, nblocks, fill, content, seed, None, None, None)
+    if n < 0:
+        raise ValueError("bad generator arguments")
+    ip = np.zeros(H // R + 1, dtype=np.int32)
+    ix = np.zeros(max(n, 1), dtype=np.int32)
+    d = np.zeros(max(n, 1) * R * C, dtype=np.float32)
+    r.ref_bsr_generate(H, W, R, C, nblocks, fill, content, seed, _ptr(ip), _ptr(ix), _ptr(d))
+    return ip, ix[:n], d[: n * R * C]
+
+
+def ref_generate_dense(H, W, content, seed=42):
+    out = np.zeros((H, W), dtype=np.float32)
+    ref().ref_dense_generate(H, W, content, seed, _ptr(out))
+    return out
+
+
+def ref_spmm_timed(indptr, indices, data, H, W, R, C, B, N, rows, threads, reps=1) -> float:
+    """Seconds per call of the reference golden over block-rows ``rows``."""
+    indptr, indices = _c(indptr, np.int32), _c(indices, np.int32)
+    data, B = _c(data, np.uint16), _c(B, np.uint16)
+    return float(ref().ref_spmm_bf16_timed(H, W, R, C, _ptr(indptr), _ptr(indices), _ptr(data),
+                                           N, _ptr(B), rows[0], rows[1], threads, reps))
+
+
+def ref_sddmm_timed(indptr, indices, mask_data, H, W, R, C, A, B, K, rows, threads, reps=1) -> float:
+    indptr, indices = _c(indptr, np.int32), _c(indices, np.int32)
+    nnzb = int(indptr[-1])
+    if mask_data is None:
+        mask_data = np.full(nnzb * R * C, 0x3F80, dtype=np.uint16)
+    mask_data, A, B = _c(mask_data, np.uint16), _c(A, np.uint16), _c(B, np.uint16)
+    return float(ref().ref_sddmm_bf16_timed(H, W, R, C, _ptr(indptr), _ptr(indices),
+                                            _ptr(mask_data), K, _ptr(A), _ptr(B), rows[0],
+                                            rows[1], threads, reps))

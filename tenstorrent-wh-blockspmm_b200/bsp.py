@@ -1,0 +1,374 @@
+"""Python binding of libbsp.so (the C ABI in include/bsp.h), via ctypes.
+
+Device memory comes from torch tensors (torch is plumbing here: allocation,
+streams, NCCL); every multiply runs in libbsp's sm_100a kernels.  There is no
+CPU or torch fallback: if libbsp.so is missing or the call fails, this raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from dataclasses import dataclass
+from typing import Optional
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libbsp.so")
+
+BSP_OK, BSP_ERR_INVALID_ARG, BSP_ERR_UNSUPPORTED, BSP_ERR_CUDA, BSP_ERR_TIMEOUT = 0, 1, 2, 3, 4
+NAIVE, SNF, DDA = 0, 1, 2
+BF16, F32 = 0, 1
+STRATEGIES = {"naive": NAIVE, "snf": SNF, "dda": DDA}
+
+# Every symbol the header declares (checked by the CPU test suite).
+EXPORTS = [
+    "bsp_device_open", "bsp_device_close", "bsp_device_synchronize", "bsp_device_get_error",
+    "bsp_device_sm_count", "bsp_last_error_string", "bsp_status_string",
+    "bsp_spmm_plan_create", "bsp_spmm_execute", "bsp_spmm_plan_destroy", "bsp_spmm_plan_info",
+    "bsp_spmm", "bsp_spmm_host",
+    "bsp_sddmm_plan_create", "bsp_sddmm_execute", "bsp_sddmm_plan_destroy",
+    "bsp_sddmm_plan_info", "bsp_sddmm", "bsp_sddmm_host",
+    "bsp_partition_rows", "bsp_serpentine_assign",
+]
+
+
+class BspError(RuntimeError):
+    def __init__(self, status: int, msg: str):
+        super().__init__(f"bsp error {status}: {msg}")
+        self.status = status
+
+
+class BsrDesc(ctypes.Structure):
+    _fields_ = [
+        ("rows", ctypes.c_int64), ("cols", ctypes.c_int64),
+        ("R", ctypes.c_int32), ("C", ctypes.c_int32),
+        ("nnzb", ctypes.c_int64),
+        ("row_ptr", ctypes.c_void_p), ("col_idx", ctypes.c_void_p), ("values", ctypes.c_void_p),
+    ]
+
+
+class Opts(ctypes.Structure):
+    _fields_ = [
+        ("no_load_balance", ctypes.c_int32), ("group_rows", ctypes.c_int32),
+        ("n_tiles", ctypes.c_int32), ("max_ctas", ctypes.c_int32),
+        ("timeout_ms", ctypes.c_int32), ("reserved", ctypes.c_int32 * 3),
+    ]
+
+
+_lib = None
+
+
+def lib():
+    """Load libbsp.so (raises if it was not built)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise RuntimeError(f"libbsp.so not built at {LIB_PATH}; run __graft_entry__.build()")
+    L = ctypes.CDLL(LIB_PATH)
+    P, I64, I32 = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int32
+    S = ctypes.c_int
+    sig = {
+        "bsp_device_open": (S, [ctypes.c_int, ctypes.POINTER(P)]),
+        "bsp_device_close": (S, [P]),
+        "bsp_device_synchronize": (S, [P]),
+        "bsp_device_get_error": (S, [P, ctypes.POINTER(ctypes.c_uint32)]),
+        "bsp_device_sm_count": (ctypes.c_int, [P]),
+        "bsp_last_error_string": (ctypes.c_char_p, []),
+        "bsp_status_string": (ctypes.c_char_p, [S]),
+        "bsp_spmm_plan_create": (S, [P, ctypes.POINTER(BsrDesc), P, P, I64, S, S,
+                                     ctypes.POINTER(Opts), ctypes.POINTER(P)]),
+        "bsp_spmm_execute": (S, [P, ctypes.POINTER(BsrDesc), P, I64, P, I64, P]),
+        "bsp_spmm_plan_destroy": (S, [P]),
+        "bsp_spmm_plan_info": (S, [P, ctypes.POINTER(I64)]),
+        "bsp_spmm": (S, [P, ctypes.POINTER(BsrDesc), P, I64, P, I64, S, I64, S,
+                         ctypes.POINTER(Opts), P]),
+        "bsp_spmm_host": (S, [P, I64, I64, I32, I32, I64, P, P, P, P, I64, P, S,
+                              ctypes.POINTER(Opts)]),
+        "bsp_sddmm_plan_create": (S, [P, ctypes.POINTER(BsrDesc), P, P, I64, S,
+                                      ctypes.POINTER(Opts), ctypes.POINTER(P)]),
+        "bsp_sddmm_execute": (S, [P, ctypes.POINTER(BsrDesc), P, I64, P, I64, P, P]),
+        "bsp_sddmm_plan_destroy": (S, [P]),
+        "bsp_sddmm_plan_info": (S, [P, ctypes.POINTER(I64)]),
+        "bsp_sddmm": (S, [P, ctypes.POINTER(BsrDesc), P, I64, P, I64, I64, P, S,
+                          ctypes.POINTER(Opts), P]),
+        "bsp_sddmm_host": (S, [P, I64, I64, I32, I32, I64, P, P, P, P, P, I64, P, S,
+                               ctypes.POINTER(Opts)]),
+        "bsp_partition_rows": (S, [P, I64, I32, P]),
+        "bsp_serpentine_assign": (S, [I64, I32, P, P]),
+    }
+    for name, (res, args) in sig.items():
+        fn = getattr(L, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = L
+    return L
+
+
+def _check(status: int):
+    if status != BSP_OK:
+        raise BspError(status, lib().bsp_last_error_string().decode())
+
+
+def make_opts(**kw) -> Opts:
+    o = Opts()
+    for k, v in kw.items():
+        if v is not None:
+            setattr(o, k, int(v))
+    return o
+
+
+def _ptr(a) -> Optional[int]:
+    if a is None:
+        return None
+    if hasattr(a, "data_ptr"):
+        return a.data_ptr()
+    return a.ctypes.data
+
+
+# ------------------------------------------------------------------ device --
+class Device:
+    """A B200 (sm_100a) opened through the library (reference: IDevice*)."""
+
+    def __init__(self, ordinal: int = 0):
+        h = ctypes.c_void_p()
+        _check(lib().bsp_device_open(ordinal, ctypes.byref(h)))
+        self.handle = h
+        self.ordinal = ordinal
+
+    @property
+    def sm_count(self) -> int:
+        return lib().bsp_device_sm_count(self.handle)
+
+    def synchronize(self):
+        _check(lib().bsp_device_synchronize(self.handle))
+
+    def status_bits(self) -> int:
+        v = ctypes.c_uint32()
+        _check(lib().bsp_device_get_error(self.handle, ctypes.byref(v)))
+        return v.value
+
+    def close(self):
+        if self.handle:
+            lib().bsp_device_close(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+_default = {}
+
+
+def device(ordinal: int = 0) -> Device:
+    if ordinal not in _default:
+        _default[ordinal] = Device(ordinal)
+    return _default[ordinal]
+
+
+# ---------------------------------------------------------------- BSR data --
+@dataclass
+class DeviceBSR:
+    """A BSR matrix resident on the GPU (torch tensors) plus its host pattern."""
+
+    rows: int
+    cols: int
+    R: int
+    C: int
+    row_ptr: "object"   # torch int32 cuda
+    col_idx: "object"   # torch int32 cuda
+    values: "object"    # torch bf16 cuda, [nnzb*R*C] (or None for a pattern-only mask)
+    h_row_ptr: np.ndarray
+    h_col_idx: np.ndarray
+
+    @property
+    def nnzb(self) -> int:
+        return int(self.h_row_ptr[-1])
+
+    def desc(self) -> BsrDesc:
+        return BsrDesc(self.rows, self.cols, self.R, self.C, self.nnzb,
+                       _ptr(self.row_ptr), _ptr(self.col_idx), _ptr(self.values))
+
+    @staticmethod
+    def from_host(rows, cols, R, C, row_ptr, col_idx, values_bf16_bits=None, device_index=0):
+        import torch
+        dev = torch.device("cuda", device_index)
+        rp = np.ascontiguousarray(row_ptr, dtype=np.int32)
+        ci = np.ascontiguousarray(col_idx, dtype=np.int32)
+        t_rp = torch.from_numpy(rp).to(dev)
+        t_ci = torch.from_numpy(ci if ci.size else np.zeros(1, np.int32)).to(dev)
+        t_v = None
+        if values_bf16_bits is not None:
+            v = np.ascontiguousarray(values_bf16_bits, dtype=np.uint16).ravel()
+            if v.size == 0:
+                v = np.zeros(8, np.uint16)
+            t_v = torch.from_numpy(v.view(np.int16)).to(dev).view(torch.bfloat16)
+        return DeviceBSR(rows, cols, R, C, t_rp, t_ci, t_v, rp, ci)
+
+
+def to_device_bf16(bits: np.ndarray, device_index=0):
+    import torch
+    a = np.ascontiguousarray(bits, dtype=np.uint16)
+    return torch.from_numpy(a.view(np.int16)).to(torch.device("cuda", device_index)).view(torch.bfloat16)
+
+
+def to_host_bits(t) -> np.ndarray:
+    import torch
+    return t.contiguous().view(torch.int16).cpu().numpy().view(np.uint16)
+
+
+def _stream_ptr(stream) -> Optional[int]:
+    if stream is None:
+        import torch
+        return torch.cuda.current_stream().cuda_stream
+    return stream.cuda_stream if hasattr(stream, "cuda_stream") else int(stream)
+
+
+# -------------------------------------------------------------------- SpMM --
+class SpmmPlan:
+    """Reusable SpMM plan for one pattern and one N (reference: the planner)."""
+
+    def __init__(self, dev: Device, A: DeviceBSR, N: int, strategy=NAIVE, c_type=BF16, opts=None):
+        self.dev, self.N, self.c_type = dev, N, c_type
+        self._desc = A.desc()
+        h = ctypes.c_void_p()
+        o = opts if opts is not None else Opts()
+        _check(lib().bsp_spmm_plan_create(dev.handle, ctypes.byref(self._desc),
+                                          _ptr(A.h_row_ptr), _ptr(A.h_col_idx), N, c_type,
+                                          strategy, ctypes.byref(o), ctypes.byref(h)))
+        self.handle = h
+
+    def info(self) -> dict:
+        arr = (ctypes.c_int64 * 16)()
+        _check(lib().bsp_spmm_plan_info(self.handle, arr))
+        keys = ["units", "ctas", "group_rows", "n_tiles", "slab", "kc", "stages", "steps",
+                "plan_bytes", "smem_bytes", "tmem_cols"]
+        return {k: int(arr[i]) for i, k in enumerate(keys)}
+
+    def execute(self, A: DeviceBSR, B, C, stream=None):
+        d = A.desc()
+        _check(lib().bsp_spmm_execute(self.handle, ctypes.byref(d), _ptr(B), B.stride(0), _ptr(C),
+                                      C.stride(0), _stream_ptr(stream)))
+
+    def close(self):
+        if self.handle:
+            lib().bsp_spmm_plan_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def spmm(A: DeviceBSR, B, strategy=NAIVE, c_type=BF16, opts=None, dev: Device = None):
+    """One-shot C = A @ B on the GPU (B: torch bf16 cuda [K, N]); returns C."""
+    import torch
+    dev = dev or device(B.device.index or 0)
+    N = B.shape[1]
+    C = torch.empty((A.rows, N), dtype=torch.float32 if c_type == F32 else torch.bfloat16,
+                    device=B.device)
+    plan = SpmmPlan(dev, A, N, strategy, c_type, opts)
+    plan.execute(A, B, C)
+    dev.synchronize()
+    plan.close()
+    return C
+
+
+def spmm_host(M, K, R, C, row_ptr, col_idx, values, B, N, strategy=NAIVE, opts=None,
+              dev: Device = None, out=None) -> np.ndarray:
+    """Host buffers in, host C out (reference planner semantics)."""
+    dev = dev or device(0)
+    rp = np.ascontiguousarray(row_ptr, dtype=np.int32)
+    ci = np.ascontiguousarray(col_idx, dtype=np.int32)
+    v = np.ascontiguousarray(values, dtype=np.uint16)
+    b = np.ascontiguousarray(B, dtype=np.uint16)
+    o = out if out is not None else np.empty((M, N), dtype=np.uint16)
+    opt = opts if opts is not None else Opts()
+    _check(lib().bsp_spmm_host(dev.handle, M, K, R, C, int(rp[-1]), _ptr(rp), _ptr(ci), _ptr(v),
+                               _ptr(b), N, _ptr(o), strategy, ctypes.byref(opt)))
+    return o
+
+
+# ------------------------------------------------------------------- SDDMM --
+class SddmmPlan:
+    def __init__(self, dev: Device, mask: DeviceBSR, K: int, strategy=NAIVE, opts=None):
+        self.dev, self.K = dev, K
+        self._desc = mask.desc()
+        h = ctypes.c_void_p()
+        o = opts if opts is not None else Opts()
+        _check(lib().bsp_sddmm_plan_create(dev.handle, ctypes.byref(self._desc),
+                                           _ptr(mask.h_row_ptr), _ptr(mask.h_col_idx), K,
+                                           strategy, ctypes.byref(o), ctypes.byref(h)))
+        self.handle = h
+
+    def info(self) -> dict:
+        arr = (ctypes.c_int64 * 16)()
+        _check(lib().bsp_sddmm_plan_info(self.handle, arr))
+        keys = ["units", "ctas", "_2", "_3", "slab", "kc", "stages", "_7", "plan_bytes",
+                "smem_bytes", "tmem_cols"]
+        return {k: int(arr[i]) for i, k in enumerate(keys) if not k.startswith("_")}
+
+    def execute(self, mask: DeviceBSR, A, B, out, stream=None):
+        d = mask.desc()
+        _check(lib().bsp_sddmm_execute(self.handle, ctypes.byref(d), _ptr(A), A.stride(0), _ptr(B),
+                                       B.stride(0), _ptr(out), _stream_ptr(stream)))
+
+    def close(self):
+        if self.handle:
+            lib().bsp_sddmm_plan_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def sddmm(mask: DeviceBSR, A, B, strategy=NAIVE, opts=None, dev: Device = None):
+    """One-shot out = mask (.) (A @ B) on the mask's pattern; returns bf16 block values."""
+    import torch
+    dev = dev or device(A.device.index or 0)
+    out = torch.empty(max(mask.nnzb * mask.R * mask.C, 8), dtype=torch.bfloat16, device=A.device)
+    plan = SddmmPlan(dev, mask, A.shape[1], strategy, opts)
+    plan.execute(mask, A, B, out)
+    dev.synchronize()
+    plan.close()
+    return out[: mask.nnzb * mask.R * mask.C]
+
+
+def sddmm_host(M, N, R, C, row_ptr, col_idx, mask_values, A, B, K, strategy=NAIVE, opts=None,
+               dev: Device = None, out=None) -> np.ndarray:
+    dev = dev or device(0)
+    rp = np.ascontiguousarray(row_ptr, dtype=np.int32)
+    ci = np.ascontiguousarray(col_idx, dtype=np.int32)
+    mv = None if mask_values is None else np.ascontiguousarray(mask_values, dtype=np.uint16)
+    a = np.ascontiguousarray(A, dtype=np.uint16)
+    b = np.ascontiguousarray(B, dtype=np.uint16)
+    nnzb = int(rp[-1])
+    o = out if out is not None else np.empty(nnzb * R * C, dtype=np.uint16)
+    opt = opts if opts is not None else Opts()
+    _check(lib().bsp_sddmm_host(dev.handle, M, N, R, C, nnzb, _ptr(rp), _ptr(ci), _ptr(mv),
+                                _ptr(a), _ptr(b), K, _ptr(o), strategy, ctypes.byref(opt)))
+    return o
+
+
+# ----------------------------------------------------------------- helpers --
+def partition_rows(row_ptr: np.ndarray, parts: int) -> np.ndarray:
+    rp = np.ascontiguousarray(row_ptr, dtype=np.int32)
+    bounds = np.zeros(parts + 1, dtype=np.int64)
+    _check(lib().bsp_partition_rows(_ptr(rp), rp.size - 1, parts, _ptr(bounds)))
+    return bounds
+
+
+def serpentine_assign(n: int, parts: int):
+    owner = np.zeros(max(n, 1), dtype=np.int32)
+    slot = np.zeros(max(n, 1), dtype=np.int32)
+    _check(lib().bsp_serpentine_assign(n, parts, _ptr(owner), _ptr(slot)))
+    return owner[:n], slot[:n]

@@ -1,0 +1,164 @@
+// Internal types shared by the host planner, the C ABI and the kernels.
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+#include <vector>
+
+#include "bsp.h"
+
+namespace bsp {
+
+constexpr int kMaxGroupRows = 8;   // DDA row-group size limit
+constexpr int kMaxNTiles = 4;      // SNF/DDA n-tiles per unit limit
+constexpr int kTileN = 128;        // dense columns per MMA (MMA M dimension)
+constexpr int kTmemCols = 512;     // TMEM columns per SM
+constexpr int kSmemBudget = 227 * 1024;
+
+// ---- SpMM schedule ----------------------------------------------------------
+// One unit = a group of `nrows` consecutive block-rows x a sub-row slab of
+// height Rs x `nt` consecutive 128-column tiles of C.  Its steps (one per
+// distinct column of the group, in order) list, per member row, the block to
+// multiply (or -1).
+struct SpmmUnit {
+  int32_t row0;        // first block-row of the group
+  int32_t nrows;       // block-rows in the group (1..G)
+  int32_t r_off;       // first row of the Rs-high slab inside each block
+  int32_t n0;          // first column of C covered
+  int32_t nt;          // 128-column tiles covered (1..NT)
+  int32_t step_begin;  // steps [step_begin, step_end) in the step table
+  int32_t step_end;
+  int32_t row_mask;    // bit g: block-row row0+g has at least one block
+};
+static_assert(sizeof(SpmmUnit) == 32, "unit layout");
+
+struct SpmmKernelParams {
+  CUtensorMap tm_a;  // A values as [nnzb*R rows, C cols] bf16, box {kc, Rs}
+  CUtensorMap tm_b;  // B [K rows, N cols] bf16, box {64, kc}, 128B swizzle
+  CUtensorMap tm_c;  // C [M rows, N cols] bf16|f32, box {32, 32}
+  const SpmmUnit* units;        // in CTA order
+  const int32_t* cta_begin;     // [grid + 1]
+  const int32_t* steps;         // [nsteps][1 + G]: col, blk[G]
+  unsigned int* status;
+  uint64_t timeout_ns;
+  int32_t R, C, Rs, kc, nkc, G, NT, step_stride;
+  int32_t c_f32;                // C element type is f32
+  int32_t stages;               // pipeline depth
+  int32_t stage_bytes;          // bytes per pipeline stage (1024-aligned)
+  int32_t b_bytes;              // bytes of the B part of a stage (NT tiles)
+  int32_t a_swizzle_mode;       // descriptor layout code of the A chunk (2 = 128B, 4 = 64B)
+  int32_t acc_cols;             // TMEM columns of one accumulator set (NT*G*Rs)
+  int32_t tmem_cols;            // TMEM columns allocated
+  int32_t N;                    // C columns
+};
+
+// ---- SDDMM schedule ---------------------------------------------------------
+// One unit = one block-row slab (Rs rows) x up to 4 output segments, each 32
+// consecutive output columns of one mask block.
+struct SddmmUnit {
+  int32_t row;        // block-row i
+  int32_t r_off;      // first row of the Rs-high slab
+  int32_t nseg;       // valid segments (1..4)
+  int32_t pad;
+  int32_t blk[4];     // mask block index of each segment
+  int32_t col[4];     // absolute first column (j*C + c0) of each segment
+};
+static_assert(sizeof(SddmmUnit) == 48, "unit layout");
+
+struct SddmmKernelParams {
+  CUtensorMap tm_a;  // A [M rows, K cols] bf16, box {kc, Rs}
+  CUtensorMap tm_b;  // B [K rows, N cols] bf16, box {32, kc}, 64B swizzle
+  const SddmmUnit* units;
+  const int32_t* cta_begin;
+  const uint16_t* mask_vals;  // may be null
+  uint16_t* out_vals;
+  unsigned int* status;
+  uint64_t timeout_ns;
+  int32_t R, C, Rs, kc, nkc;
+  int32_t stages, stage_bytes, a_bytes;
+  int32_t a_swizzle_mode;
+  int32_t tmem_cols;
+  int32_t keep_a;  // DDA: A slab of the row stays resident across units of a row run
+};
+
+// ---- host objects -------------------------------------------------------------
+typedef CUresult (*PFN_encodeTiled)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                    const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                    const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                    CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+}  // namespace bsp
+
+struct bsp_device {
+  int ordinal = 0;
+  int sm_count = 0;
+  int max_smem_optin = 0;
+  unsigned int* d_status = nullptr;  // device status word(s)
+  bsp::PFN_encodeTiled encode = nullptr;
+  // grow-only workspace for the host-buffer entry points
+  void* ws = nullptr;
+  size_t ws_bytes = 0;
+  void* pinned = nullptr;
+  size_t pinned_bytes = 0;
+};
+
+struct bsp_spmm_plan {
+  bsp_device* dev = nullptr;
+  int64_t M = 0, K = 0, N = 0, nnzb = 0;
+  int32_t R = 0, C = 0, Rs = 0, kc = 0, G = 1, NT = 1;
+  bsp_dtype c_type = BSP_BF16;
+  bsp_strategy strategy = BSP_NAIVE;
+  int32_t grid = 0, stages = 0, stage_bytes = 0, smem_bytes = 0, tmem_cols = 0;
+  int64_t n_units = 0, n_steps = 0;
+  uint64_t timeout_ns = 0;
+  void* d_blob = nullptr;  // units | cta_begin | steps
+  size_t blob_bytes = 0;
+  bsp::SpmmUnit* d_units = nullptr;
+  int32_t* d_cta_begin = nullptr;
+  int32_t* d_steps = nullptr;
+  // host copies (tests and the no-allocation variant reuse them)
+  std::vector<bsp::SpmmUnit> h_units;
+  std::vector<int32_t> h_cta_begin;
+  std::vector<int32_t> h_steps;
+};
+
+struct bsp_sddmm_plan {
+  bsp_device* dev = nullptr;
+  int64_t M = 0, N = 0, K = 0, nnzb = 0;
+  int32_t R = 0, C = 0, Rs = 0, kc = 0;
+  bsp_strategy strategy = BSP_NAIVE;
+  int32_t grid = 0, stages = 0, stage_bytes = 0, smem_bytes = 0, tmem_cols = 0, keep_a = 0;
+  int64_t n_units = 0;
+  uint64_t timeout_ns = 0;
+  void* d_blob = nullptr;
+  size_t blob_bytes = 0;
+  bsp::SddmmUnit* d_units = nullptr;
+  int32_t* d_cta_begin = nullptr;
+  std::vector<bsp::SddmmUnit> h_units;
+  std::vector<int32_t> h_cta_begin;
+};
+
+namespace bsp {
+// error plumbing (capi.cpp)
+bsp_status set_error(bsp_status s, const std::string& msg);
+bsp_status cuda_check(cudaError_t e, const char* what);
+
+// planners (planner.cpp); pure host logic, testable without a GPU
+bsp_status plan_spmm_host(bsp_spmm_plan* p, const int32_t* row_ptr, const int32_t* col_idx,
+                          int sm_count, int max_smem, const bsp_spmm_opts* opts);
+bsp_status plan_sddmm_host(bsp_sddmm_plan* p, const int32_t* row_ptr, const int32_t* col_idx,
+                           int sm_count, int max_smem, const bsp_sddmm_opts* opts);
+void serpentine_order(const std::vector<int64_t>& weight, int parts,
+                      std::vector<std::vector<int32_t>>* per_part);
+
+// kernel launchers (spmm.cu / sddmm.cu)
+bsp_status launch_spmm(const bsp_spmm_plan* p, const bsp_bsr_desc* A, const void* B, int64_t ldb,
+                       void* C, int64_t ldc, cudaStream_t stream);
+bsp_status launch_sddmm(const bsp_sddmm_plan* p, const bsp_bsr_desc* mask, const void* A,
+                        int64_t lda, const void* B, int64_t ldb, void* out, cudaStream_t stream);
+bsp_status encode_2d(bsp_device* dev, CUtensorMap* tm, CUtensorMapDataType dt, int esize,
+                     const void* ptr, uint64_t inner, uint64_t outer, uint64_t row_stride_elems,
+                     uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swz);
+}  // namespace bsp

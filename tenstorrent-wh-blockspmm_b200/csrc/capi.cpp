@@ -1,0 +1,537 @@
+// C ABI of libbsp.so (declared in include/bsp.h).
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdio>
+#include <cstring>
+#include <new>
+#include <string>
+#include <vector>
+
+#include "bsp_internal.h"
+
+namespace bsp {
+
+static thread_local std::string g_last_error;
+
+bsp_status set_error(bsp_status s, const std::string& msg) {
+  g_last_error = msg;
+  return s;
+}
+
+bsp_status cuda_check(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return BSP_OK;
+  return set_error(BSP_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+bsp_status encode_2d(bsp_device* dev, CUtensorMap* tm, CUtensorMapDataType dt, int esize,
+                     const void* ptr, uint64_t inner, uint64_t outer, uint64_t row_stride_elems,
+                     uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swz) {
+  if (reinterpret_cast<uintptr_t>(ptr) % 16)
+    return set_error(BSP_ERR_INVALID_ARG, "device pointers must be 16-byte aligned");
+  if ((row_stride_elems * esize) % 16)
+    return set_error(BSP_ERR_INVALID_ARG, "row strides must be multiples of 16 bytes");
+  const cuuint64_t dims[2] = {inner, outer};
+  const cuuint64_t strides[1] = {row_stride_elems * static_cast<uint64_t>(esize)};
+  const cuuint32_t box[2] = {box_inner, box_outer};
+  const cuuint32_t estr[2] = {1, 1};
+  CUresult r = dev->encode(tm, dt, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return set_error(BSP_ERR_INVALID_ARG,
+                     "cuTensorMapEncodeTiled failed (code " + std::to_string(int(r)) + ")");
+  return BSP_OK;
+}
+
+static bsp_status check_desc(const bsp_bsr_desc* A, bool need_values) {
+  if (!A) return set_error(BSP_ERR_INVALID_ARG, "null BSR descriptor");
+  if (A->R <= 0 || A->C <= 0 || A->rows <= 0 || A->cols <= 0 || A->nnzb < 0)
+    return set_error(BSP_ERR_INVALID_ARG, "bad BSR dimensions");
+  if (A->rows % A->R || A->cols % A->C)
+    return set_error(BSP_ERR_INVALID_ARG, "rows % R and cols % C must be 0");
+  if (!A->row_ptr || (A->nnzb > 0 && !A->col_idx))
+    return set_error(BSP_ERR_INVALID_ARG, "BSR row_ptr / col_idx missing");
+  if (need_values && A->nnzb > 0 && !A->values)
+    return set_error(BSP_ERR_INVALID_ARG, "BSR values missing");
+  if (A->values && reinterpret_cast<uintptr_t>(A->values) % 16)
+    return set_error(BSP_ERR_INVALID_ARG, "BSR values must be 16-byte aligned");
+  return BSP_OK;
+}
+
+// Pattern arrays on the host: use the caller's copies or fetch them.
+static bsp_status host_pattern(const bsp_bsr_desc* A, const int32_t* hrp, const int32_t* hci,
+                               std::vector<int32_t>* rp, std::vector<int32_t>* ci,
+                               const int32_t** rp_out, const int32_t** ci_out) {
+  const int64_t nbr = A->rows / A->R;
+  if (hrp && (hci || A->nnzb == 0)) {
+    *rp_out = hrp;
+    *ci_out = hci;
+    return BSP_OK;
+  }
+  rp->resize(nbr + 1);
+  ci->resize(std::max<int64_t>(A->nnzb, 1));
+  bsp_status s = cuda_check(cudaMemcpy(rp->data(), A->row_ptr, sizeof(int32_t) * (nbr + 1),
+                                       cudaMemcpyDeviceToHost),
+                            "copy row_ptr to host");
+  if (s != BSP_OK) return s;
+  if (A->nnzb > 0) {
+    s = cuda_check(cudaMemcpy(ci->data(), A->col_idx, sizeof(int32_t) * A->nnzb,
+                              cudaMemcpyDeviceToHost),
+                   "copy col_idx to host");
+    if (s != BSP_OK) return s;
+  }
+  *rp_out = rp->data();
+  *ci_out = ci->data();
+  return BSP_OK;
+}
+
+static size_t align256(size_t x) { return (x + 255) / 256 * 256; }
+
+// Upload the plan tables as one device allocation.
+static bsp_status upload_blob(const std::vector<std::pair<const void*, size_t>>& parts,
+                              void** blob, size_t* bytes, std::vector<void*>* ptrs) {
+  size_t total = 0;
+  for (auto& pr : parts) total += align256(pr.second);
+  total = std::max<size_t>(total, 256);
+  void* d = nullptr;
+  if (cudaMalloc(&d, total) != cudaSuccess)
+    return set_error(BSP_ERR_ALLOC, "cudaMalloc of the plan tables failed");
+  std::vector<uint8_t> h(total, 0);
+  size_t off = 0;
+  ptrs->clear();
+  for (auto& pr : parts) {
+    if (pr.second) memcpy(h.data() + off, pr.first, pr.second);
+    ptrs->push_back(static_cast<uint8_t*>(d) + off);
+    off += align256(pr.second);
+  }
+  cudaError_t e = cudaMemcpy(d, h.data(), total, cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) {
+    cudaFree(d);
+    return cuda_check(e, "upload plan tables");
+  }
+  *blob = d;
+  *bytes = total;
+  return BSP_OK;
+}
+
+static bsp_status ws_reserve(bsp_device* dev, size_t bytes) {
+  if (dev->ws_bytes >= bytes) return BSP_OK;
+  if (dev->ws) cudaFree(dev->ws);
+  dev->ws = nullptr;
+  dev->ws_bytes = 0;
+  if (cudaMalloc(&dev->ws, bytes) != cudaSuccess)
+    return set_error(BSP_ERR_ALLOC, "cudaMalloc of the host-path workspace failed");
+  dev->ws_bytes = bytes;
+  return BSP_OK;
+}
+
+}  // namespace bsp
+
+using namespace bsp;
+
+extern "C" {
+
+const char* bsp_last_error_string(void) { return g_last_error.c_str(); }
+
+const char* bsp_status_string(bsp_status s) {
+  switch (s) {
+    case BSP_OK: return "ok";
+    case BSP_ERR_INVALID_ARG: return "invalid argument";
+    case BSP_ERR_UNSUPPORTED: return "unsupported";
+    case BSP_ERR_CUDA: return "cuda error";
+    case BSP_ERR_TIMEOUT: return "device wait timed out";
+    case BSP_ERR_NCCL: return "nccl error";
+    case BSP_ERR_ALLOC: return "allocation failed";
+    case BSP_ERR_STATE: return "bad state";
+  }
+  return "unknown";
+}
+
+bsp_status bsp_device_open(int ordinal, bsp_device** out) {
+  if (!out) return set_error(BSP_ERR_INVALID_ARG, "null output");
+  *out = nullptr;
+  int n = 0;
+  bsp_status s = cuda_check(cudaGetDeviceCount(&n), "cudaGetDeviceCount");
+  if (s != BSP_OK) return s;
+  if (ordinal < 0 || ordinal >= n) return set_error(BSP_ERR_INVALID_ARG, "no such device");
+  s = cuda_check(cudaSetDevice(ordinal), "cudaSetDevice");
+  if (s != BSP_OK) return s;
+  cudaDeviceProp prop;
+  s = cuda_check(cudaGetDeviceProperties(&prop, ordinal), "cudaGetDeviceProperties");
+  if (s != BSP_OK) return s;
+  if (prop.major != 10)
+    return set_error(BSP_ERR_UNSUPPORTED, "libbsp is built for sm_100a (B200); this device is sm_" +
+                                              std::to_string(prop.major * 10 + prop.minor));
+  bsp_device* d = new (std::nothrow) bsp_device();
+  if (!d) return set_error(BSP_ERR_ALLOC, "host allocation failed");
+  d->ordinal = ordinal;
+  d->sm_count = prop.multiProcessorCount;
+  d->max_smem_optin = static_cast<int>(prop.sharedMemPerBlockOptin);
+  void* fn = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) !=
+          cudaSuccess ||
+      q != cudaDriverEntryPointSuccess || !fn) {
+    delete d;
+    return set_error(BSP_ERR_CUDA, "cuTensorMapEncodeTiled not available from the driver");
+  }
+  d->encode = reinterpret_cast<PFN_encodeTiled>(fn);
+  if (cudaMalloc(&d->d_status, 64) != cudaSuccess) {
+    delete d;
+    return set_error(BSP_ERR_ALLOC, "cudaMalloc of the status word failed");
+  }
+  cudaMemset(d->d_status, 0, 64);
+  *out = d;
+  return BSP_OK;
+}
+
+bsp_status bsp_device_close(bsp_device* dev) {
+  if (!dev) return BSP_OK;
+  cudaSetDevice(dev->ordinal);
+  if (dev->d_status) cudaFree(dev->d_status);
+  if (dev->ws) cudaFree(dev->ws);
+  if (dev->pinned) cudaFreeHost(dev->pinned);
+  delete dev;
+  return BSP_OK;
+}
+
+int bsp_device_sm_count(const bsp_device* dev) { return dev ? dev->sm_count : 0; }
+
+bsp_status bsp_device_get_error(bsp_device* dev, uint32_t* bits) {
+  if (!dev || !bits) return set_error(BSP_ERR_INVALID_ARG, "null argument");
+  return cuda_check(cudaMemcpy(bits, dev->d_status, 4, cudaMemcpyDeviceToHost), "read status");
+}
+
+bsp_status bsp_device_synchronize(bsp_device* dev) {
+  if (!dev) return set_error(BSP_ERR_INVALID_ARG, "null device");
+  bsp_status s = cuda_check(cudaDeviceSynchronize(), "cudaDeviceSynchronize");
+  if (s != BSP_OK) return s;
+  uint32_t bits = 0;
+  s = cuda_check(cudaMemcpy(&bits, dev->d_status, 4, cudaMemcpyDeviceToHost), "read status");
+  if (s != BSP_OK) return s;
+  if (bits) {
+    cudaMemset(dev->d_status, 0, 4);
+    char msg[128];
+    snprintf(msg, sizeof(msg), "a kernel wait timed out (status bits 0x%x)", bits);
+    return set_error(BSP_ERR_TIMEOUT, msg);
+  }
+  return BSP_OK;
+}
+
+// ---------------------------------------------------------------- SpMM ----
+bsp_status bsp_spmm_plan_create(bsp_device* dev, const bsp_bsr_desc* A, const int32_t* host_row_ptr,
+                                const int32_t* host_col_idx, int64_t N, bsp_dtype c_type,
+                                bsp_strategy strategy, const bsp_spmm_opts* opts,
+                                bsp_spmm_plan** out) {
+  if (!dev || !out) return set_error(BSP_ERR_INVALID_ARG, "null argument");
+  *out = nullptr;
+  bsp_status s = check_desc(A, false);
+  if (s != BSP_OK) return s;
+  if (c_type != BSP_BF16 && c_type != BSP_F32)
+    return set_error(BSP_ERR_INVALID_ARG, "C type must be BSP_BF16 or BSP_F32");
+  std::vector<int32_t> rp, ci;
+  const int32_t *prp = nullptr, *pci = nullptr;
+  s = host_pattern(A, host_row_ptr, host_col_idx, &rp, &ci, &prp, &pci);
+  if (s != BSP_OK) return s;
+  bsp_spmm_plan* p = new (std::nothrow) bsp_spmm_plan();
+  if (!p) return set_error(BSP_ERR_ALLOC, "host allocation failed");
+  p->dev = dev;
+  p->M = A->rows;
+  p->K = A->cols;
+  p->N = N;
+  p->R = A->R;
+  p->C = A->C;
+  p->nnzb = A->nnzb;
+  p->c_type = c_type;
+  p->strategy = strategy;
+  s = plan_spmm_host(p, prp, pci, dev->sm_count, dev->max_smem_optin, opts);
+  if (s != BSP_OK) {
+    delete p;
+    return s;
+  }
+  std::vector<void*> ptrs;
+  s = upload_blob({{p->h_units.data(), p->h_units.size() * sizeof(SpmmUnit)},
+                   {p->h_cta_begin.data(), p->h_cta_begin.size() * sizeof(int32_t)},
+                   {p->h_steps.data(), p->h_steps.size() * sizeof(int32_t)}},
+                  &p->d_blob, &p->blob_bytes, &ptrs);
+  if (s != BSP_OK) {
+    delete p;
+    return s;
+  }
+  p->d_units = static_cast<SpmmUnit*>(ptrs[0]);
+  p->d_cta_begin = static_cast<int32_t*>(ptrs[1]);
+  p->d_steps = static_cast<int32_t*>(ptrs[2]);
+  *out = p;
+  return BSP_OK;
+}
+
+bsp_status bsp_spmm_execute(const bsp_spmm_plan* plan, const bsp_bsr_desc* A, const void* B,
+                            int64_t ldb, void* C, int64_t ldc, void* stream) {
+  if (!plan || !B || !C) return set_error(BSP_ERR_INVALID_ARG, "null argument");
+  bsp_status s = check_desc(A, true);
+  if (s != BSP_OK) return s;
+  if (A->rows != plan->M || A->cols != plan->K || A->R != plan->R || A->C != plan->C ||
+      A->nnzb != plan->nnzb)
+    return set_error(BSP_ERR_INVALID_ARG, "A does not match the plan's pattern");
+  if (ldb < plan->N || ldc < plan->N)
+    return set_error(BSP_ERR_INVALID_ARG, "leading dimensions must be >= N");
+  return launch_spmm(plan, A, B, ldb, C, ldc, static_cast<cudaStream_t>(stream));
+}
+
+bsp_status bsp_spmm_plan_destroy(bsp_spmm_plan* plan) {
+  if (!plan) return BSP_OK;
+  if (plan->d_blob) cudaFree(plan->d_blob);
+  delete plan;
+  return BSP_OK;
+}
+
+bsp_status bsp_spmm_plan_info(const bsp_spmm_plan* p, int64_t info[16]) {
+  if (!p || !info) return set_error(BSP_ERR_INVALID_ARG, "null argument");
+  memset(info, 0, sizeof(int64_t) * 16);
+  info[0] = p->n_units;
+  info[1] = p->grid;
+  info[2] = p->G;
+  info[3] = p->NT;
+  info[4] = p->Rs;
+  info[5] = p->kc;
+  info[6] = p->stages;
+  info[7] = p->n_steps;
+  info[8] = static_cast<int64_t>(p->blob_bytes);
+  info[9] = p->smem_bytes;
+  info[10] = p->tmem_cols;
+  return BSP_OK;
+}
+
+bsp_status bsp_spmm(bsp_device* dev, const bsp_bsr_desc* A, const void* B, int64_t ldb, void* C,
+                    int64_t ldc, bsp_dtype c_type, int64_t N, bsp_strategy strategy,
+                    const bsp_spmm_opts* opts, void* stream) {
+  bsp_spmm_plan* p = nullptr;
+  bsp_status s = bsp_spmm_plan_create(dev, A, nullptr, nullptr, N, c_type, strategy, opts, &p);
+  if (s != BSP_OK) return s;
+  s = bsp_spmm_execute(p, A, B, ldb, C, ldc, stream);
+  if (s == BSP_OK) s = cuda_check(cudaStreamSynchronize(static_cast<cudaStream_t>(stream)), "sync");
+  bsp_spmm_plan_destroy(p);
+  if (s == BSP_OK) s = bsp_device_synchronize(dev);
+  return s;
+}
+
+bsp_status bsp_spmm_host(bsp_device* dev, int64_t M, int64_t K, int32_t R, int32_t C, int64_t nnzb,
+                         const int32_t* row_ptr, const int32_t* col_idx, const uint16_t* values,
+                         const uint16_t* B, int64_t N, uint16_t* C_out, bsp_strategy strategy,
+                         const bsp_spmm_opts* opts) {
+  if (!dev || !row_ptr || !B || !C_out || (nnzb > 0 && (!col_idx || !values)))
+    return set_error(BSP_ERR_INVALID_ARG, "null argument");
+  if (R <= 0 || C <= 0 || M % R || K % C) return set_error(BSP_ERR_INVALID_ARG, "bad dimensions");
+  const int64_t nbr = M / R;
+  const size_t b_val = align256(sizeof(uint16_t) * nnzb * R * C);
+  const size_t b_rp = align256(sizeof(int32_t) * (nbr + 1));
+  const size_t b_ci = align256(sizeof(int32_t) * std::max<int64_t>(nnzb, 1));
+  const size_t b_B = align256(sizeof(uint16_t) * K * N);
+  const size_t b_C = align256(sizeof(uint16_t) * M * N);
+  bsp_status s = ws_reserve(dev, b_val + b_rp + b_ci + b_B + b_C);
+  if (s != BSP_OK) return s;
+  uint8_t* w = static_cast<uint8_t*>(dev->ws);
+  void* d_val = w;
+  int32_t* d_rp = reinterpret_cast<int32_t*>(w + b_val);
+  int32_t* d_ci = reinterpret_cast<int32_t*>(w + b_val + b_rp);
+  void* d_B = w + b_val + b_rp + b_ci;
+  void* d_C = w + b_val + b_rp + b_ci + b_B;
+  cudaStream_t stream = nullptr;
+  if ((s = cuda_check(cudaMemcpyAsync(d_B, B, sizeof(uint16_t) * K * N, cudaMemcpyHostToDevice, stream), "H2D B")) != BSP_OK) return s;
+  if ((s = cuda_check(cudaMemcpyAsync(d_rp, row_ptr, sizeof(int32_t) * (nbr + 1), cudaMemcpyHostToDevice, stream), "H2D row_ptr")) != BSP_OK) return s;
+  if (nnzb > 0) {
+    if ((s = cuda_check(cudaMemcpyAsync(d_ci, col_idx, sizeof(int32_t) * nnzb, cudaMemcpyHostToDevice, stream), "H2D col_idx")) != BSP_OK) return s;
+    if ((s = cuda_check(cudaMemcpyAsync(d_val, values, sizeof(uint16_t) * nnzb * R * C, cudaMemcpyHostToDevice, stream), "H2D values")) != BSP_OK) return s;
+  }
+  bsp_bsr_desc A{M, K, R, C, nnzb, d_rp, d_ci, d_val};
+  bsp_spmm_plan* p = nullptr;
+  s = bsp_spmm_plan_create(dev, &A, row_ptr, col_idx, N, BSP_BF16, strategy, opts, &p);
+  if (s != BSP_OK) return s;
+  s = bsp_spmm_execute(p, &A, d_B, N, d_C, N, stream);
+  if (s == BSP_OK)
+    s = cuda_check(cudaMemcpyAsync(C_out, d_C, sizeof(uint16_t) * M * N, cudaMemcpyDeviceToHost, stream), "D2H C");
+  if (s == BSP_OK) s = cuda_check(cudaStreamSynchronize(stream), "sync");
+  bsp_spmm_plan_destroy(p);
+  if (s == BSP_OK) s = bsp_device_synchronize(dev);
+  return s;
+}
+
+// --------------------------------------------------------------- SDDMM ----
+bsp_status bsp_sddmm_plan_create(bsp_device* dev, const bsp_bsr_desc* mask,
+                                 const int32_t* host_row_ptr, const int32_t* host_col_idx,
+                                 int64_t K, bsp_strategy strategy, const bsp_sddmm_opts* opts,
+                                 bsp_sddmm_plan** out) {
+  if (!dev || !out) return set_error(BSP_ERR_INVALID_ARG, "null argument");
+  *out = nullptr;
+  bsp_status s = check_desc(mask, false);
+  if (s != BSP_OK) return s;
+  std::vector<int32_t> rp, ci;
+  const int32_t *prp = nullptr, *pci = nullptr;
+  s = host_pattern(mask, host_row_ptr, host_col_idx, &rp, &ci, &prp, &pci);
+  if (s != BSP_OK) return s;
+  bsp_sddmm_plan* p = new (std::nothrow) bsp_sddmm_plan();
+  if (!p) return set_error(BSP_ERR_ALLOC, "host allocation failed");
+  p->dev = dev;
+  p->M = mask->rows;
+  p->N = mask->cols;
+  p->K = K;
+  p->R = mask->R;
+  p->C = mask->C;
+  p->nnzb = mask->nnzb;
+  p->strategy = strategy;
+  s = plan_sddmm_host(p, prp, pci, dev->sm_count, dev->max_smem_optin, opts);
+  if (s != BSP_OK) {
+    delete p;
+    return s;
+  }
+  std::vector<void*> ptrs;
+  s = upload_blob({{p->h_units.data(), p->h_units.size() * sizeof(SddmmUnit)},
+                   {p->h_cta_begin.data(), p->h_cta_begin.size() * sizeof(int32_t)}},
+                  &p->d_blob, &p->blob_bytes, &ptrs);
+  if (s != BSP_OK) {
+    delete p;
+    return s;
+  }
+  p->d_units = static_cast<SddmmUnit*>(ptrs[0]);
+  p->d_cta_begin = static_cast<int32_t*>(ptrs[1]);
+  *out = p;
+  return BSP_OK;
+}
+
+bsp_status bsp_sddmm_execute(const bsp_sddmm_plan* plan, const bsp_bsr_desc* mask, const void* A,
+                             int64_t lda, const void* B, int64_t ldb, void* out_values,
+                             void* stream) {
+  if (!plan || !A || !B || (!out_values && plan->nnzb > 0))
+    return set_error(BSP_ERR_INVALID_ARG, "null argument");
+  bsp_status s = check_desc(mask, false);
+  if (s != BSP_OK) return s;
+  if (mask->rows != plan->M || mask->cols != plan->N || mask->R != plan->R ||
+      mask->C != plan->C || mask->nnzb != plan->nnzb)
+    return set_error(BSP_ERR_INVALID_ARG, "mask does not match the plan's pattern");
+  if (lda < plan->K || ldb < plan->N)
+    return set_error(BSP_ERR_INVALID_ARG, "leading dimensions too small");
+  if (reinterpret_cast<uintptr_t>(out_values) % 16)
+    return set_error(BSP_ERR_INVALID_ARG, "out_values must be 16-byte aligned");
+  return launch_sddmm(plan, mask, A, lda, B, ldb, out_values, static_cast<cudaStream_t>(stream));
+}
+
+bsp_status bsp_sddmm_plan_destroy(bsp_sddmm_plan* plan) {
+  if (!plan) return BSP_OK;
+  if (plan->d_blob) cudaFree(plan->d_blob);
+  delete plan;
+  return BSP_OK;
+}
+
+bsp_status bsp_sddmm_plan_info(const bsp_sddmm_plan* p, int64_t info[16]) {
+  if (!p || !info) return set_error(BSP_ERR_INVALID_ARG, "null argument");
+  memset(info, 0, sizeof(int64_t) * 16);
+  info[0] = p->n_units;
+  info[1] = p->grid;
+  info[4] = p->Rs;
+  info[5] = p->kc;
+  info[6] = p->stages;
+  info[8] = static_cast<int64_t>(p->blob_bytes);
+  info[9] = p->smem_bytes;
+  info[10] = p->tmem_cols;
+  return BSP_OK;
+}
+
+bsp_status bsp_sddmm(bsp_device* dev, const bsp_bsr_desc* mask, const void* A, int64_t lda,
+                     const void* B, int64_t ldb, int64_t K, void* out_values,
+                     bsp_strategy strategy, const bsp_sddmm_opts* opts, void* stream) {
+  bsp_sddmm_plan* p = nullptr;
+  bsp_status s = bsp_sddmm_plan_create(dev, mask, nullptr, nullptr, K, strategy, opts, &p);
+  if (s != BSP_OK) return s;
+  s = bsp_sddmm_execute(p, mask, A, lda, B, ldb, out_values, stream);
+  if (s == BSP_OK) s = cuda_check(cudaStreamSynchronize(static_cast<cudaStream_t>(stream)), "sync");
+  bsp_sddmm_plan_destroy(p);
+  if (s == BSP_OK) s = bsp_device_synchronize(dev);
+  return s;
+}
+
+bsp_status bsp_sddmm_host(bsp_device* dev, int64_t M, int64_t N, int32_t R, int32_t C,
+                          int64_t nnzb, const int32_t* row_ptr, const int32_t* col_idx,
+                          const uint16_t* mask_values, const uint16_t* A, const uint16_t* B,
+                          int64_t K, uint16_t* out_values, bsp_strategy strategy,
+                          const bsp_sddmm_opts* opts) {
+  if (!dev || !row_ptr || !A || !B || (nnzb > 0 && (!col_idx || !out_values)))
+    return set_error(BSP_ERR_INVALID_ARG, "null argument");
+  if (R <= 0 || C <= 0 || M % R || N % C) return set_error(BSP_ERR_INVALID_ARG, "bad dimensions");
+  const int64_t nbr = M / R;
+  const size_t blk = sizeof(uint16_t) * nnzb * R * C;
+  const size_t b_mask = mask_values ? align256(blk) : 0;
+  const size_t b_out = align256(std::max<size_t>(blk, 16));
+  const size_t b_rp = align256(sizeof(int32_t) * (nbr + 1));
+  const size_t b_ci = align256(sizeof(int32_t) * std::max<int64_t>(nnzb, 1));
+  const size_t b_A = align256(sizeof(uint16_t) * M * K);
+  const size_t b_B = align256(sizeof(uint16_t) * K * N);
+  bsp_status s = ws_reserve(dev, b_mask + b_out + b_rp + b_ci + b_A + b_B);
+  if (s != BSP_OK) return s;
+  uint8_t* w = static_cast<uint8_t*>(dev->ws);
+  void* d_out = w;
+  void* d_mask = mask_values ? w + b_out : nullptr;
+  int32_t* d_rp = reinterpret_cast<int32_t*>(w + b_out + b_mask);
+  int32_t* d_ci = reinterpret_cast<int32_t*>(w + b_out + b_mask + b_rp);
+  void* d_A = w + b_out + b_mask + b_rp + b_ci;
+  void* d_B = w + b_out + b_mask + b_rp + b_ci + b_A;
+  cudaStream_t stream = nullptr;
+  if ((s = cuda_check(cudaMemcpyAsync(d_A, A, sizeof(uint16_t) * M * K, cudaMemcpyHostToDevice, stream), "H2D A")) != BSP_OK) return s;
+  if ((s = cuda_check(cudaMemcpyAsync(d_B, B, sizeof(uint16_t) * K * N, cudaMemcpyHostToDevice, stream), "H2D B")) != BSP_OK) return s;
+  if ((s = cuda_check(cudaMemcpyAsync(d_rp, row_ptr, sizeof(int32_t) * (nbr + 1), cudaMemcpyHostToDevice, stream), "H2D row_ptr")) != BSP_OK) return s;
+  if (nnzb > 0) {
+    if ((s = cuda_check(cudaMemcpyAsync(d_ci, col_idx, sizeof(int32_t) * nnzb, cudaMemcpyHostToDevice, stream), "H2D col_idx")) != BSP_OK) return s;
+    if (mask_values &&
+        (s = cuda_check(cudaMemcpyAsync(d_mask, mask_values, blk, cudaMemcpyHostToDevice, stream), "H2D mask")) != BSP_OK)
+      return s;
+  }
+  bsp_bsr_desc mask{M, N, R, C, nnzb, d_rp, d_ci, d_mask};
+  bsp_sddmm_plan* p = nullptr;
+  s = bsp_sddmm_plan_create(dev, &mask, row_ptr, col_idx, K, strategy, opts, &p);
+  if (s != BSP_OK) return s;
+  s = bsp_sddmm_execute(p, &mask, d_A, K, d_B, N, d_out, stream);
+  if (s == BSP_OK && nnzb > 0)
+    s = cuda_check(cudaMemcpyAsync(out_values, d_out, blk, cudaMemcpyDeviceToHost, stream), "D2H out");
+  if (s == BSP_OK) s = cuda_check(cudaStreamSynchronize(stream), "sync");
+  bsp_sddmm_plan_destroy(p);
+  if (s == BSP_OK) s = bsp_device_synchronize(dev);
+  return s;
+}
+
+// ----------------------------------------------------------- helpers ----
+bsp_status bsp_partition_rows(const int32_t* row_ptr, int64_t n_block_rows, int32_t parts,
+                              int64_t* bounds) {
+  if (!row_ptr || !bounds || parts < 1 || n_block_rows < 0)
+    return set_error(BSP_ERR_INVALID_ARG, "bad arguments");
+  // Balance blocks plus one unit per row (every row costs its C writes).
+  const int64_t total = row_ptr[n_block_rows] + n_block_rows;
+  bounds[0] = 0;
+  int64_t r = 0;
+  for (int p = 1; p < parts; ++p) {
+    const int64_t target = total * p / parts;
+    while (r < n_block_rows && row_ptr[r] + r < target) ++r;
+    bounds[p] = r;
+  }
+  bounds[parts] = n_block_rows;
+  for (int p = 1; p <= parts; ++p) bounds[p] = std::max(bounds[p], bounds[p - 1]);
+  return BSP_OK;
+}
+
+bsp_status bsp_serpentine_assign(int64_t n, int32_t parts, int32_t* owner, int32_t* slot) {
+  if (n < 0 || parts < 1 || (n > 0 && (!owner || !slot)))
+    return set_error(BSP_ERR_INVALID_ARG, "bad arguments");
+  // weights n-1 .. 0 make the heaviest-first permutation the identity
+  std::vector<int64_t> w(n);
+  for (int64_t i = 0; i < n; ++i) w[i] = n - i;
+  std::vector<std::vector<int32_t>> per;
+  serpentine_order(w, parts, &per);
+  for (int p = 0; p < parts; ++p)
+    for (size_t k = 0; k < per[p].size(); ++k) {
+      owner[per[p][k]] = p;
+      slot[per[p][k]] = static_cast<int32_t>(k);
+    }
+  return BSP_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,333 @@
+// Host-side planners: the B200 counterpart of the reference planners' host
+// logic (row folding, tiling, core assignment, load balancing).
+//
+//   reference                                          here
+//   fold empty rows (load_balanced_new_DM.cpp:50-61)   empty rows become zero-fill units
+//   N per core (host_code_utils.cpp:32-66)             fixed 128-column tiles (MMA M)
+//   core grid (load_balanced_new_DM.cpp:71-107)        one persistent CTA per SM
+//   serpentine LB (load_balanced_new_DM.cpp:346-393)   serpentine_order() over work units
+//   no-LB variant (load_balanced_new_DM.cpp:339-344)   contiguous split (opts.no_load_balance)
+//   SDDMM even split (bsr_sddmm_multicore_naive.cpp:266-310)  4-segment units, same balancer
+//
+// Nothing here touches the GPU, so every branch is testable on CPU.
+#include <algorithm>
+#include <cstring>
+#include <numeric>
+#include <string>
+
+#include "bsp_internal.h"
+
+namespace bsp {
+
+int spmm_smem_bytes(int stages, int stage_bytes, bool c_f32);
+int sddmm_smem_bytes(int stages, int stage_bytes);
+
+namespace {
+
+int pow2_at_least(int x) {
+  int p = 32;
+  while (p < x) p <<= 1;
+  return p;
+}
+
+// Largest multiple of 32 that divides R and is <= 256 (the MMA N limit).
+int slab_height(int R) {
+  if (R <= 256) return R;
+  for (int d = 256; d >= 32; d -= 32)
+    if (R % d == 0) return d;
+  return 32;
+}
+
+}  // namespace
+
+// The reference's zig-zag balancer generalised to any item list: items sorted
+// by weight (heaviest first, ties by index), then each pass deals the next
+// `parts` heaviest items to parts 0..P-1 and the `parts` lightest remaining
+// ones to parts P-1..0 (load_balanced_new_DM.cpp:371-393).
+void serpentine_order(const std::vector<int64_t>& weight, int parts,
+                      std::vector<std::vector<int32_t>>* per_part) {
+  const int64_t n = static_cast<int64_t>(weight.size());
+  std::vector<int32_t> perm(n);
+  std::iota(perm.begin(), perm.end(), 0);
+  std::stable_sort(perm.begin(), perm.end(),
+                   [&](int32_t a, int32_t b) { return weight[a] > weight[b]; });
+  per_part->assign(parts, {});
+  int64_t assigned = 0, it = 1;
+  while (assigned < n) {
+    int64_t k = std::min<int64_t>(parts, n - assigned);
+    int64_t sub = 0;
+    for (int64_t w = 0; w < k; ++w) {
+      if (assigned++ >= n) break;
+      (*per_part)[w].push_back(perm[parts * (it - 1) + sub]);
+      ++sub;
+    }
+    k = std::min<int64_t>(parts, n - assigned);
+    sub = parts - k;
+    for (int64_t w = parts; w > parts - k; --w) {
+      if (assigned++ >= n) break;
+      (*per_part)[w - 1].push_back(perm[n - parts * it + sub]);
+      ++sub;
+    }
+    ++it;
+  }
+}
+
+static void contiguous_split(int64_t n, int parts, std::vector<std::vector<int32_t>>* per_part) {
+  per_part->assign(parts, {});
+  for (int p = 0; p < parts; ++p) {
+    const int64_t b = n * p / parts, e = n * (p + 1) / parts;
+    for (int64_t i = b; i < e; ++i) (*per_part)[p].push_back(static_cast<int32_t>(i));
+  }
+}
+
+static bsp_status check_pattern(const int32_t* row_ptr, const int32_t* col_idx, int64_t nbr,
+                                int64_t nbc, int64_t nnzb) {
+  if (row_ptr[0] != 0) return set_error(BSP_ERR_INVALID_ARG, "row_ptr[0] must be 0");
+  for (int64_t i = 0; i < nbr; ++i)
+    if (row_ptr[i + 1] < row_ptr[i])
+      return set_error(BSP_ERR_INVALID_ARG, "row_ptr must be non-decreasing");
+  if (row_ptr[nbr] != nnzb)
+    return set_error(BSP_ERR_INVALID_ARG, "row_ptr[last] must equal nnzb");
+  for (int64_t b = 0; b < nnzb; ++b)
+    if (col_idx[b] < 0 || col_idx[b] >= nbc)
+      return set_error(BSP_ERR_INVALID_ARG, "col_idx out of range at block " + std::to_string(b));
+  return BSP_OK;
+}
+
+bsp_status plan_spmm_host(bsp_spmm_plan* p, const int32_t* row_ptr, const int32_t* col_idx,
+                          int sm_count, int max_smem, const bsp_spmm_opts* opts) {
+  bsp_spmm_opts o;
+  memset(&o, 0, sizeof(o));
+  if (opts) o = *opts;
+  const int64_t M = p->M, K = p->K, N = p->N;
+  const int R = p->R, C = p->C;
+  if (R <= 0 || C <= 0 || R % 32 || C % 32)
+    return set_error(BSP_ERR_INVALID_ARG, "block dims R, C must be positive multiples of 32");
+  if (M <= 0 || K <= 0 || M % R || K % C)
+    return set_error(BSP_ERR_INVALID_ARG, "M % R and K % C must be 0");
+  if (N <= 0 || N % 8) return set_error(BSP_ERR_INVALID_ARG, "N must be a positive multiple of 8");
+  if (p->nnzb < 0 || p->nnzb * R >= (int64_t(1) << 31) || K >= (int64_t(1) << 31) ||
+      M >= (int64_t(1) << 31) || N >= (int64_t(1) << 31))
+    return set_error(BSP_ERR_UNSUPPORTED, "matrix too large for 32-bit TMA coordinates");
+  const int64_t nbr = M / R, nbc = K / C;
+  bsp_status st = check_pattern(row_ptr, col_idx, nbr, nbc, p->nnzb);
+  if (st != BSP_OK) return st;
+
+  const int Rs = slab_height(R);
+  const int kc = (C % 64 == 0) ? 64 : 32;
+  const int ntiles_total = static_cast<int>((N + kTileN - 1) / kTileN);
+  int G = 1, NT = 1;
+  switch (p->strategy) {
+    case BSP_NAIVE:
+      break;
+    case BSP_SNF:
+      NT = o.n_tiles > 0 ? o.n_tiles : std::min({kMaxNTiles, 256 / Rs, ntiles_total});
+      break;
+    case BSP_DDA:
+      NT = o.n_tiles > 0 ? o.n_tiles : std::min({2, 256 / Rs, ntiles_total});
+      NT = std::max(NT, 1);
+      G = o.group_rows > 0 ? o.group_rows : std::max(1, std::min(kMaxGroupRows, 256 / (NT * Rs)));
+      break;
+    default:
+      return set_error(BSP_ERR_INVALID_ARG, "unknown strategy");
+  }
+  NT = std::max(1, std::min(NT, ntiles_total));
+  if (G < 1 || G > kMaxGroupRows || NT > kMaxNTiles)
+    return set_error(BSP_ERR_INVALID_ARG, "group_rows must be 1..8 and n_tiles 1..4");
+  if (2 * NT * G * Rs > kTmemCols)
+    return set_error(BSP_ERR_INVALID_ARG,
+                     "2 * n_tiles * group_rows * slab height exceeds the 512 TMEM columns");
+  p->Rs = Rs;
+  p->kc = kc;
+  p->G = G;
+  p->NT = NT;
+
+  // ---- steps and units ----
+  const int stride = 1 + G;
+  std::vector<int32_t>& steps = p->h_steps;
+  steps.clear();
+  std::vector<SpmmUnit> units;
+  std::vector<int64_t> weight;
+  const int nkc = C / kc;
+  const int esz = p->c_type == BSP_F32 ? 4 : 2;
+  std::vector<std::pair<int32_t, int32_t>> cols;  // (col, g) for a group
+  for (int64_t r0 = 0; r0 < nbr; r0 += G) {
+    const int nrows = static_cast<int>(std::min<int64_t>(G, nbr - r0));
+    const int32_t s_begin = static_cast<int32_t>(steps.size() / stride);
+    int32_t mask = 0;
+    for (int g = 0; g < nrows; ++g)
+      if (row_ptr[r0 + g + 1] > row_ptr[r0 + g]) mask |= 1 << g;
+    if (G == 1) {
+      for (int32_t b = row_ptr[r0]; b < row_ptr[r0 + 1]; ++b) {
+        steps.push_back(col_idx[b]);
+        steps.push_back(b);
+      }
+    } else {
+      // merge the member rows' blocks by column: one step per distinct column
+      // (a repeated column inside one row opens a new step)
+      std::vector<std::pair<int32_t, int32_t>> items;  // (col, block)
+      std::vector<int8_t> owner;
+      for (int g = 0; g < nrows; ++g)
+        for (int32_t b = row_ptr[r0 + g]; b < row_ptr[r0 + g + 1]; ++b)
+          items.push_back({col_idx[b], b});
+      std::stable_sort(items.begin(), items.end(),
+                       [](const std::pair<int32_t, int32_t>& a,
+                          const std::pair<int32_t, int32_t>& b) { return a.first < b.first; });
+      int64_t cur = -1;
+      for (const auto& it : items) {
+        int g = 0;
+        while (!(it.second >= row_ptr[r0 + g] && it.second < row_ptr[r0 + g + 1])) ++g;
+        const bool open = cur >= 0 && steps[cur * stride] == it.first &&
+                          steps[cur * stride + 1 + g] < 0;
+        if (!open) {
+          cur = static_cast<int64_t>(steps.size() / stride);
+          steps.push_back(it.first);
+          for (int k = 0; k < G; ++k) steps.push_back(-1);
+        }
+        steps[cur * stride + 1 + g] = it.second;
+      }
+    }
+    const int32_t s_end = static_cast<int32_t>(steps.size() / stride);
+    // bytes this group's steps stage per 128-column tile, for the balancer
+    int64_t a_blocks = 0;
+    for (int32_t s = s_begin; s < s_end; ++s)
+      for (int g = 0; g < G; ++g) a_blocks += steps[s * stride + 1 + g] >= 0;
+    for (int r_off = 0; r_off < R; r_off += Rs) {
+      for (int t0 = 0; t0 < ntiles_total; t0 += NT) {
+        SpmmUnit u;
+        u.row0 = static_cast<int32_t>(r0);
+        u.nrows = nrows;
+        u.r_off = r_off;
+        u.n0 = t0 * kTileN;
+        u.nt = std::min(NT, ntiles_total - t0);
+        u.step_begin = s_begin;
+        u.step_end = s_end;
+        u.row_mask = mask;
+        units.push_back(u);
+        const int64_t smem_in = int64_t(nkc) * ((s_end - s_begin) * int64_t(u.nt) * kc * kTileN * 2 +
+                                                a_blocks * int64_t(Rs) * kc * 2);
+        const int64_t out = int64_t(nrows) * u.nt * kTileN * Rs * esz;
+        weight.push_back(smem_in + out);
+      }
+    }
+  }
+  p->n_steps = static_cast<int64_t>(steps.size() / stride);
+  if (steps.empty()) {  // keep a valid (never read) table
+    steps.push_back(0);
+    for (int k = 0; k < G; ++k) steps.push_back(-1);
+  }
+
+  // ---- CTA assignment ----
+  int grid = o.max_ctas > 0 ? std::min(o.max_ctas, sm_count) : sm_count;
+  grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(grid, units.size())));
+  std::vector<std::vector<int32_t>> per;
+  if (o.no_load_balance)
+    contiguous_split(static_cast<int64_t>(units.size()), grid, &per);
+  else
+    serpentine_order(weight, grid, &per);
+  p->h_units.clear();
+  p->h_cta_begin.assign(1, 0);
+  for (int c = 0; c < grid; ++c) {
+    for (int32_t idx : per[c]) p->h_units.push_back(units[idx]);
+    p->h_cta_begin.push_back(static_cast<int32_t>(p->h_units.size()));
+  }
+  p->n_units = static_cast<int64_t>(units.size());
+  p->grid = grid;
+
+  // ---- shared memory / TMEM ----
+  int stage_bytes = NT * kc * 256 + G * Rs * kc * 2;
+  stage_bytes = (stage_bytes + 1023) / 1024 * 1024;
+  const int fixed = spmm_smem_bytes(0, stage_bytes, p->c_type == BSP_F32);
+  int stages = (max_smem - fixed) / stage_bytes;
+  stages = std::min(stages, 32);
+  if (stages < 2)
+    return set_error(BSP_ERR_UNSUPPORTED, "block too large: fewer than 2 pipeline stages fit");
+  p->stage_bytes = stage_bytes;
+  p->stages = stages;
+  p->smem_bytes = spmm_smem_bytes(stages, stage_bytes, p->c_type == BSP_F32);
+  p->tmem_cols = pow2_at_least(2 * NT * G * Rs);
+  p->timeout_ns = static_cast<uint64_t>(o.timeout_ms > 0 ? o.timeout_ms : 2000) * 1000000ull;
+  return BSP_OK;
+}
+
+bsp_status plan_sddmm_host(bsp_sddmm_plan* p, const int32_t* row_ptr, const int32_t* col_idx,
+                           int sm_count, int max_smem, const bsp_sddmm_opts* opts) {
+  bsp_sddmm_opts o;
+  memset(&o, 0, sizeof(o));
+  if (opts) o = *opts;
+  const int64_t M = p->M, N = p->N, K = p->K;
+  const int R = p->R, C = p->C;
+  if (R <= 0 || C <= 0 || R % 32 || C % 32)
+    return set_error(BSP_ERR_INVALID_ARG, "block dims R, C must be positive multiples of 32");
+  if (M <= 0 || N <= 0 || M % R || N % C)
+    return set_error(BSP_ERR_INVALID_ARG, "M % R and N % C must be 0");
+  if (K <= 0 || K % 32) return set_error(BSP_ERR_INVALID_ARG, "K must be a positive multiple of 32");
+  if (M >= (int64_t(1) << 31) || N >= (int64_t(1) << 31) || K >= (int64_t(1) << 31) ||
+      p->nnzb < 0 || p->nnzb >= (int64_t(1) << 31))
+    return set_error(BSP_ERR_UNSUPPORTED, "matrix too large for 32-bit coordinates");
+  const int64_t nbr = M / R, nbc = N / C;
+  bsp_status st = check_pattern(row_ptr, col_idx, nbr, nbc, p->nnzb);
+  if (st != BSP_OK) return st;
+  if (p->strategy != BSP_NAIVE && p->strategy != BSP_DDA && p->strategy != BSP_SNF)
+    return set_error(BSP_ERR_INVALID_ARG, "unknown strategy");
+
+  const int Rs = slab_height(R);
+  const int kc = (K % 64 == 0) ? 64 : 32;
+  p->Rs = Rs;
+  p->kc = kc;
+  p->keep_a = 0;
+
+  std::vector<SddmmUnit> units;
+  for (int64_t i = 0; i < nbr; ++i) {
+    for (int r_off = 0; r_off < R; r_off += Rs) {
+      SddmmUnit u;
+      memset(&u, 0, sizeof(u));
+      u.row = static_cast<int32_t>(i);
+      u.r_off = r_off;
+      for (int32_t b = row_ptr[i]; b < row_ptr[i + 1]; ++b) {
+        for (int c0 = 0; c0 < C; c0 += 32) {
+          u.blk[u.nseg] = b;
+          u.col[u.nseg] = col_idx[b] * C + c0;
+          if (++u.nseg == 4) {
+            units.push_back(u);
+            u.nseg = 0;
+          }
+        }
+      }
+      if (u.nseg > 0) units.push_back(u);
+    }
+  }
+  int grid = o.max_ctas > 0 ? std::min(o.max_ctas, sm_count) : sm_count;
+  grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(grid, units.size())));
+  std::vector<std::vector<int32_t>> per;
+  if (o.no_load_balance || p->strategy == BSP_DDA) {
+    // DDA keeps a block-row's units together on one CTA, so that the row's
+    // A slab is reused from L2/smem by consecutive units.
+    contiguous_split(static_cast<int64_t>(units.size()), grid, &per);
+  } else {
+    std::vector<int64_t> w(units.size());
+    for (size_t k = 0; k < units.size(); ++k) w[k] = units[k].nseg;
+    serpentine_order(w, grid, &per);
+  }
+  p->h_units.clear();
+  p->h_cta_begin.assign(1, 0);
+  for (int c = 0; c < grid; ++c) {
+    for (int32_t idx : per[c]) p->h_units.push_back(units[idx]);
+    p->h_cta_begin.push_back(static_cast<int32_t>(p->h_units.size()));
+  }
+  p->n_units = static_cast<int64_t>(units.size());
+  p->grid = grid;
+
+  int stage_bytes = Rs * kc * 2 + 4 * kc * 64;
+  stage_bytes = (stage_bytes + 1023) / 1024 * 1024;
+  int stages = std::min(32, (max_smem - sddmm_smem_bytes(0, stage_bytes)) / stage_bytes);
+  if (stages < 2) return set_error(BSP_ERR_UNSUPPORTED, "block too large for the pipeline");
+  p->stage_bytes = stage_bytes;
+  p->stages = stages;
+  p->smem_bytes = sddmm_smem_bytes(stages, stage_bytes);
+  p->tmem_cols = pow2_at_least(2 * Rs);
+  p->timeout_ns = static_cast<uint64_t>(o.timeout_ms > 0 ? o.timeout_ms : 2000) * 1000000ull;
+  return BSP_OK;
+}
+
+}  // namespace bsp

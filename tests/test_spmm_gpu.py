@@ -1,0 +1,213 @@
+"""SpMM parity on the GPU: libbsp (through the C ABI) vs the CPU oracle.
+
+Cases mirror the reference's own SpMM registry (block_spmm/inc/test_suite.hpp:
+single blocks, diagonal/row/column fills, nonsquare and tall/wide blocks, empty
+rows, wide N, large R) at sizes the oracle finishes in seconds, plus
+BASELINE config 1 in full.  Bar: max relative error <= 1e-2 against the
+bf16 golden (oracle restatement of bsr_matrix::spmm_bfloat16) and a normwise
+error <= 1e-5 of the f32 output against the float golden.
+"""
+import numpy as np
+import pytest
+
+import oracle
+from helpers import TOL, assert_bf16_close, normwise, pcc, rand_bsr, rand_dense
+
+pytestmark = pytest.mark.gpu
+
+
+def _bsp():
+    import bsp
+
+    return bsp
+
+
+STRATS = ["naive", "snf", "dda"]
+
+# (M, K, N, R, C, density)
+CASES = [
+    (1024, 1024, 256, 32, 32, 0.10),
+    (256, 256, 256, 64, 64, 0.5),
+    (256, 256, 256, 64, 32, 0.4),       # test_2_blocks_nonsquare-like
+    (256, 256, 256, 32, 64, 0.4),
+    (512, 512, 128, 128, 32, 0.3),      # tall blocks
+    (256, 512, 96, 32, 128, 0.3),       # wide blocks
+    (512, 256, 384, 256, 64, 0.5),      # big block
+    (1024, 512, 64, 512, 64, 0.5),      # R > 256: two 256-row slabs per block
+    (1024, 256, 32, 1024, 64, 0.6),     # test_huge-like R = 1024, N = 32
+    (4096, 256, 40, 32, 32, 0.2),       # many rows, N not a multiple of 32
+    (128, 4096, 8, 32, 32, 0.5),        # long rows (K = 4096), N = 8
+    (384, 384, 200, 96, 64, 0.4),       # R = 96 (three 32-row chunks), N % 128 != 0
+]
+
+
+def _run(bsp, M, K, N, R, C, rp, ci, vals, B, strategy, c_type=0, opts=None):
+    import torch
+
+    A = bsp.DeviceBSR.from_host(M, K, R, C, rp, ci, vals)
+    Bd = bsp.to_device_bf16(B)
+    out = bsp.spmm(A, Bd, strategy=bsp.STRATEGIES[strategy], c_type=c_type, opts=opts)
+    if c_type == bsp.F32:
+        return out.cpu().numpy()
+    return bsp.to_host_bits(out)
+
+
+@pytest.mark.parametrize("case", CASES, ids=[f"{c[0]}x{c[1]}x{c[2]}_R{c[3]}C{c[4]}" for c in CASES])
+@pytest.mark.parametrize("strategy", STRATS)
+def test_spmm_parity(case, strategy):
+    bsp = _bsp()
+    M, K, N, R, C, p = case
+    rng = np.random.default_rng(abs(hash((case, 1))) % 2**32)
+    rp, ci, vals = rand_bsr(rng, M, K, R, C, p, empty_rows=(0,) if M // R > 2 else ())
+    B = rand_dense(rng, K, N)
+    gold = oracle.spmm_bf16(rp, ci, vals, M, K, R, C, B, N)
+    out = _run(bsp, M, K, N, R, C, rp, ci, vals, B, strategy)
+    assert_bf16_close(out, gold, what=f"{case} {strategy}")
+    assert pcc(oracle.bf16_to_f32(out), oracle.bf16_to_f32(gold)) >= 0.99
+
+
+@pytest.mark.parametrize("strategy", STRATS)
+def test_spmm_f32_output_vs_float_golden(strategy):
+    bsp = _bsp()
+    M, K, N, R, C = 512, 512, 256, 32, 32
+    rng = np.random.default_rng(11)
+    rp, ci, vals = rand_bsr(rng, M, K, R, C, 0.3, empty_rows=(3,))
+    B = rand_dense(rng, K, N)
+    gold = oracle.spmm_f32(rp, ci, oracle.bf16_to_f32(vals), M, K, R, C, oracle.bf16_to_f32(B), N)
+    out = _run(bsp, M, K, N, R, C, rp, ci, vals, B, strategy, c_type=bsp.F32)
+    assert normwise(out, gold) <= 1e-5
+    e = np.abs(out - gold) / np.maximum(np.abs(gold), 1e-3 * np.abs(gold).max())
+    assert e.max() <= 1e-4
+
+
+def test_spmm_torch_fp32_reference():
+    """Cross-check against a plain PyTorch fp32 dense product of the same op."""
+    import torch
+
+    bsp = _bsp()
+    M, K, N, R, C = 1024, 1024, 512, 32, 32
+    rng = np.random.default_rng(5)
+    rp, ci, vals = rand_bsr(rng, M, K, R, C, 0.2)
+    B = rand_dense(rng, K, N)
+    dense = np.zeros((M, K), np.float32)
+    v = oracle.bf16_to_f32(vals).reshape(-1, R, C)
+    for i in range(M // R):
+        for b in range(rp[i], rp[i + 1]):
+            dense[i * R:(i + 1) * R, ci[b] * C:(ci[b] + 1) * C] = v[b]
+    ref = (torch.from_numpy(dense).cuda() @ torch.from_numpy(oracle.bf16_to_f32(B)).cuda()).cpu().numpy()
+    out = _run(bsp, M, K, N, R, C, rp, ci, vals, B, "dda", c_type=bsp.F32)
+    assert normwise(out, ref) <= 1e-5
+
+
+@pytest.mark.parametrize("strategy", STRATS)
+def test_spmm_empty_matrix_writes_zeros(strategy):
+    import torch
+
+    bsp = _bsp()
+    M, K, N, R, C = 256, 256, 128, 32, 32
+    rp = np.zeros(M // R + 1, np.int32)
+    ci = np.zeros(0, np.int32)
+    A = bsp.DeviceBSR.from_host(M, K, R, C, rp, ci, np.zeros(0, np.uint16))
+    B = bsp.to_device_bf16(rand_dense(np.random.default_rng(0), K, N))
+    C_ = torch.full((M, N), 7.0, dtype=torch.bfloat16, device="cuda")
+    plan = bsp.SpmmPlan(bsp.device(), A, N, bsp.STRATEGIES[strategy])
+    plan.execute(A, B, C_)
+    bsp.device().synchronize()
+    assert torch.count_nonzero(C_).item() == 0
+
+
+@pytest.mark.parametrize("strategy", STRATS)
+def test_spmm_overwrites_stale_output(strategy):
+    """Every element of C is written, the rows of empty block-rows included."""
+    import torch
+
+    bsp = _bsp()
+    M, K, N, R, C = 512, 256, 256, 32, 32
+    rng = np.random.default_rng(3)
+    rp, ci, vals = rand_bsr(rng, M, K, R, C, 0.2, empty_rows=(0, 1, 5, 15))
+    B = rand_dense(rng, K, N)
+    gold = oracle.spmm_bf16(rp, ci, vals, M, K, R, C, B, N)
+    A = bsp.DeviceBSR.from_host(M, K, R, C, rp, ci, vals)
+    C_ = torch.full((M, N), float("nan"), dtype=torch.bfloat16, device="cuda")
+    plan = bsp.SpmmPlan(bsp.device(), A, N, bsp.STRATEGIES[strategy])
+    plan.execute(A, bsp.to_device_bf16(B), C_)
+    bsp.device().synchronize()
+    assert_bf16_close(bsp.to_host_bits(C_), gold)
+
+
+def test_spmm_duplicate_and_unsorted_columns():
+    """A row may list columns out of order and even twice (both blocks count)."""
+    bsp = _bsp()
+    M, K, N, R, C = 128, 256, 128, 32, 32
+    rp = np.array([0, 3, 3, 6, 7], np.int32)
+    ci = np.array([5, 1, 5, 7, 0, 7, 2], np.int32)
+    rng = np.random.default_rng(9)
+    vals = oracle.f32_to_bf16(rng.uniform(-1, 1, ci.size * R * C).astype(np.float32))
+    B = rand_dense(rng, K, N)
+    gold = oracle.spmm_bf16(rp, ci, vals, M, K, R, C, B, N)
+    for s in STRATS:
+        out = _run(bsp, M, K, N, R, C, rp, ci, vals, B, s, opts=bsp.make_opts(group_rows=4) if s == "dda" else None)
+        assert_bf16_close(out, gold, what=s)
+
+
+@pytest.mark.parametrize("opts", [dict(no_load_balance=1), dict(max_ctas=3), dict(group_rows=8, n_tiles=1),
+                                  dict(group_rows=2, n_tiles=4), dict(n_tiles=3)])
+def test_spmm_schedule_options(opts):
+    bsp = _bsp()
+    M, K, N, R, C = 1024, 512, 384, 32, 32
+    rng = np.random.default_rng(21)
+    rp, ci, vals = rand_bsr(rng, M, K, R, C, 0.15, empty_rows=(4, 5, 6))
+    B = rand_dense(rng, K, N)
+    gold = oracle.spmm_bf16(rp, ci, vals, M, K, R, C, B, N)
+    strat = "dda" if "group_rows" in opts else "snf"
+    out = _run(bsp, M, K, N, R, C, rp, ci, vals, B, strat, opts=bsp.make_opts(**opts))
+    assert_bf16_close(out, gold, what=str(opts))
+
+
+def test_spmm_strided_operands():
+    import torch
+
+    bsp = _bsp()
+    M, K, N, R, C = 256, 256, 128, 32, 32
+    rng = np.random.default_rng(4)
+    rp, ci, vals = rand_bsr(rng, M, K, R, C, 0.4)
+    B = rand_dense(rng, K, N)
+    gold = oracle.spmm_bf16(rp, ci, vals, M, K, R, C, B, N)
+    A = bsp.DeviceBSR.from_host(M, K, R, C, rp, ci, vals)
+    Bbig = torch.zeros((K, N + 64), dtype=torch.bfloat16, device="cuda")
+    Bbig[:, :N] = bsp.to_device_bf16(B)
+    Cbig = torch.zeros((M, N + 32), dtype=torch.bfloat16, device="cuda")
+    plan = bsp.SpmmPlan(bsp.device(), A, N, bsp.DDA)
+    plan.execute(A, Bbig[:, :N], Cbig[:, :N])
+    bsp.device().synchronize()
+    assert_bf16_close(bsp.to_host_bits(Cbig[:, :N]), gold)
+    assert torch.count_nonzero(Cbig[:, N:]).item() == 0
+
+
+@pytest.mark.parametrize("strategy", STRATS)
+def test_spmm_host_buffer_api(strategy):
+    """The reference-semantics entry point: host arrays in, host C out."""
+    bsp = _bsp()
+    M, K, N, R, C = 1024, 1024, 256, 32, 32
+    rng = np.random.default_rng(1234 + 0)
+    rp, ci, vals = rand_bsr(rng, M, K, R, C, 0.10)
+    B = rand_dense(rng, K, N)
+    gold = oracle.spmm_bf16(rp, ci, vals, M, K, R, C, B, N)
+    out = bsp.spmm_host(M, K, R, C, rp, ci, vals, B, N, strategy=bsp.STRATEGIES[strategy])
+    assert_bf16_close(out, gold)
+
+
+def test_spmm_rejects_bad_arguments():
+    bsp = _bsp()
+    M, K, R, C = 256, 256, 32, 32
+    rp = np.zeros(M // R + 1, np.int32)
+    A = bsp.DeviceBSR.from_host(M, K, R, C, rp, np.zeros(0, np.int32), np.zeros(0, np.uint16))
+    with pytest.raises(bsp.BspError):
+        bsp.SpmmPlan(bsp.device(), A, 100, bsp.NAIVE)  # N % 8 != 0
+    bad = bsp.DeviceBSR.from_host(M, K, 48, 32, np.zeros(M // 48 + 1, np.int32), np.zeros(0, np.int32), None)
+    with pytest.raises(bsp.BspError):
+        bsp.SpmmPlan(bsp.device(), bad, 128, bsp.NAIVE)  # R % 32 != 0
+    rp2 = np.array([0, 1, 1, 1, 1, 1, 1, 1, 1], np.int32)
+    A2 = bsp.DeviceBSR.from_host(M, K, R, C, rp2, np.array([99], np.int32), np.zeros(R * C, np.uint16))
+    with pytest.raises(bsp.BspError):
+        bsp.SpmmPlan(bsp.device(), A2, 128, bsp.NAIVE)  # column index out of range

@@ -91,7 +91,11 @@ typedef struct bsp_spmm_opts {
   int32_t n_tiles;         /* SNF/DDA: 128-column tiles per work unit (A reuse) */
   int32_t max_ctas;        /* cap on persistent CTAs (default: all SMs) */
   int32_t timeout_ms;      /* bound on every in-kernel wait (default 2000) */
-  int32_t reserved[3];
+  int32_t group_mma;       /* DDA: 1 (default) one MMA over the row group's stacked
+                              blocks, absent blocks zero-filled; 2 one MMA per
+                              present block */
+  int32_t producers;       /* TMA-issuing warps per CTA (1..4, default 4) */
+  int32_t reserved[1];
 } bsp_spmm_opts;
 
 typedef bsp_spmm_opts bsp_sddmm_opts;

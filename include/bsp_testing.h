@@ -1,0 +1,40 @@
+/*
+ * bsp_testing.h -- host-only inspection of the planners in libbsp.so.
+ *
+ * No counterpart in the reference (its planners run inline in each host-code
+ * function).  These entry points run the SpMM / SDDMM planner on the host,
+ * without a GPU, and return the schedule it would upload, so that its
+ * invariants (every output tile written once, every block multiplied once per
+ * tile, balanced CTA lists) can be tested on a CPU-only machine.
+ */
+#ifndef BSP_TESTING_H_
+#define BSP_TESTING_H_
+#include "bsp.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* info[16]: as bsp_spmm_plan_info.  With null output buffers only `info` is
+ * filled (use it to size them): units_out[info[0] * 8] (row0, nrows, r_off,
+ * n0, nt, step_begin, step_end, row_mask per unit, in CTA order),
+ * cta_begin_out[info[1] + 1], steps_out[info[7] * (1 + info[2])]
+ * (column, then the block index of each group row or -1). */
+bsp_status bsp_spmm_plan_inspect(int64_t M, int64_t K, int32_t R, int32_t C, int64_t nnzb,
+                                 const int32_t* row_ptr, const int32_t* col_idx, int64_t N,
+                                 bsp_dtype c_type, bsp_strategy strategy,
+                                 const bsp_spmm_opts* opts, int32_t sm_count, int32_t max_smem,
+                                 int64_t info[16], int32_t* units_out, int32_t* cta_begin_out,
+                                 int32_t* steps_out);
+
+/* units_out[info[0] * 12] (row, r_off, nseg, pad, blk[4], col[4] per unit). */
+bsp_status bsp_sddmm_plan_inspect(int64_t M, int64_t N, int32_t R, int32_t C, int64_t nnzb,
+                                  const int32_t* row_ptr, const int32_t* col_idx, int64_t K,
+                                  bsp_strategy strategy, const bsp_sddmm_opts* opts,
+                                  int32_t sm_count, int32_t max_smem, int64_t info[16],
+                                  int32_t* units_out, int32_t* cta_begin_out);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* BSP_TESTING_H_ */

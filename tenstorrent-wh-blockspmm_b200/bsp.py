@@ -52,7 +52,8 @@ class Opts(ctypes.Structure):
     _fields_ = [
         ("no_load_balance", ctypes.c_int32), ("group_rows", ctypes.c_int32),
         ("n_tiles", ctypes.c_int32), ("max_ctas", ctypes.c_int32),
-        ("timeout_ms", ctypes.c_int32), ("reserved", ctypes.c_int32 * 3),
+        ("timeout_ms", ctypes.c_int32), ("group_mma", ctypes.c_int32),
+        ("producers", ctypes.c_int32), ("reserved", ctypes.c_int32 * 1),
     ]
 
 
@@ -246,7 +247,7 @@ class SpmmPlan:
         arr = (ctypes.c_int64 * 16)()
         _check(lib().bsp_spmm_plan_info(self.handle, arr))
         keys = ["units", "ctas", "group_rows", "n_tiles", "slab", "kc", "stages", "steps",
-                "plan_bytes", "smem_bytes", "tmem_cols"]
+                "plan_bytes", "smem_bytes", "tmem_cols", "variant", "producers"]
         return {k: int(arr[i]) for i, k in enumerate(keys)}
 
     def execute(self, A: DeviceBSR, B, C, stream=None):

@@ -36,13 +36,15 @@ static_assert(sizeof(SpmmUnit) == 32, "unit layout");
 
 struct SpmmKernelParams {
   CUtensorMap tm_a;  // A values as [nnzb*R rows, C cols] bf16, box {kc, Rs}
-  CUtensorMap tm_b;  // B [K rows, N cols] bf16, box {64, kc}, 128B swizzle
-  CUtensorMap tm_c;  // C [M rows, N cols] bf16|f32, box {32, 32}
+  CUtensorMap tm_b;  // B: 3-D {64 cols, K rows, N/64 blocks} box {64, kc, 2*NT}
+                     // (b3d) or 2-D [K rows, N cols] box {64, kc}; 128B swizzle
   const SpmmUnit* units;        // in CTA order
   const int32_t* cta_begin;     // [grid + 1]
   const int32_t* steps;         // [nsteps][1 + G]: col, blk[G]
   unsigned int* status;
   uint64_t timeout_ns;
+  void* c_ptr;                  // C, row-major
+  int64_t ldc;                  // C leading dimension (elements)
   int32_t R, C, Rs, kc, nkc, G, NT, step_stride;
   int32_t c_f32;                // C element type is f32
   int32_t stages;               // pipeline depth
@@ -52,6 +54,26 @@ struct SpmmKernelParams {
   int32_t acc_cols;             // TMEM columns of one accumulator set (NT*G*Rs)
   int32_t tmem_cols;            // TMEM columns allocated
   int32_t N;                    // C columns
+  int32_t stacked;              // DDA: one MMA over the group's stacked blocks
+  int32_t nprod;                // producer warps issuing stages round-robin
+  int32_t b3d;                  // tm_b is the 3-D view (one box per step)
+  const int4* stage_list;       // row-stacked kernel: per-CTA pipeline stages (2 x int4 each)
+  const int32_t* cta_stage_begin;  // [grid + 1]
+};
+
+// Row-stacked kernel stage descriptor, precomputed by the planner so that a
+// producer warp issues a stage without any arithmetic or dependent loads.
+//   w[0] ky: B row coordinate (block column * C + k-chunk offset)
+//   w[1] bz: first 64-column block of the unit (3-D map) or first column (2-D)
+//   w[2] flags: bits 0-3 present entries, 4-7 entry slots to zero first,
+//        bit 12 first stage of a unit, 13 last, 14 unit without blocks,
+//        bits 16-18 number of present entries
+//   w[3] ax: A column coordinate (k-chunk offset)
+//   w[4..7] ay[g]: A row coordinate of entry g's block slab (or -1)
+enum : int32_t {
+  RS_F_FIRST = 1 << 12,
+  RS_F_LAST = 1 << 13,
+  RS_F_EMPTY = 1 << 14,
 };
 
 // ---- SDDMM schedule ---------------------------------------------------------
@@ -107,10 +129,12 @@ struct bsp_device {
 struct bsp_spmm_plan {
   bsp_device* dev = nullptr;
   int64_t M = 0, K = 0, N = 0, nnzb = 0;
-  int32_t R = 0, C = 0, Rs = 0, kc = 0, G = 1, NT = 1;
+  int32_t R = 0, C = 0, Rs = 0, kc = 0, G = 1, NT = 1, stacked = 0;
   bsp_dtype c_type = BSP_BF16;
   bsp_strategy strategy = BSP_NAIVE;
-  int32_t grid = 0, stages = 0, stage_bytes = 0, smem_bytes = 0, tmem_cols = 0;
+  int32_t grid = 0, stages = 0, stage_bytes = 0, smem_bytes = 0, tmem_cols = 0, nprod = 1;
+  int32_t variant = 0;      // 0: swap-AB kernel (spmm.cu), 1: row-stacked kernel (spmm_rowstack.cu)
+  int32_t step_stride = 2;  // int32 words per step-table entry (1 + G)
   int64_t n_units = 0, n_steps = 0;
   uint64_t timeout_ns = 0;
   void* d_blob = nullptr;  // units | cta_begin | steps
@@ -118,10 +142,14 @@ struct bsp_spmm_plan {
   bsp::SpmmUnit* d_units = nullptr;
   int32_t* d_cta_begin = nullptr;
   int32_t* d_steps = nullptr;
+  int4* d_stage_list = nullptr;
+  int32_t* d_cta_stage_begin = nullptr;
   // host copies (tests and the no-allocation variant reuse them)
   std::vector<bsp::SpmmUnit> h_units;
   std::vector<int32_t> h_cta_begin;
   std::vector<int32_t> h_steps;
+  std::vector<int32_t> h_stage_list;       // row-stacked kernel: 8 words per stage
+  std::vector<int32_t> h_cta_stage_begin;  // row-stacked kernel
 };
 
 struct bsp_sddmm_plan {
@@ -161,4 +189,16 @@ bsp_status launch_sddmm(const bsp_sddmm_plan* p, const bsp_bsr_desc* mask, const
 bsp_status encode_2d(bsp_device* dev, CUtensorMap* tm, CUtensorMapDataType dt, int esize,
                      const void* ptr, uint64_t inner, uint64_t outer, uint64_t row_stride_elems,
                      uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swz);
+// rank-D tiled map; strides_bytes[rank-1] are the strides of dims 1..rank-1
+bsp_status encode_nd(bsp_device* dev, CUtensorMap* tm, CUtensorMapDataType dt, int rank,
+                     const void* ptr, const uint64_t* dims, const uint64_t* strides_bytes,
+                     const uint32_t* box, CUtensorMapSwizzle swz);
+int spmm_threads();
+int spmm_max_producers();
+int rowstack_max_producers();
+int rowstack_max_stages();
+bsp_status launch_spmm_rowstack(const bsp_spmm_plan* p, const bsp_bsr_desc* A, const void* B,
+                                int64_t ldb, void* C, int64_t ldc, cudaStream_t stream);
+bsp_status plan_spmm_rowstack(bsp_spmm_plan* p, const int32_t* row_ptr, const int32_t* col_idx,
+                              int sm_count, int max_smem, const bsp_spmm_opts* opts);
 }  // namespace bsp

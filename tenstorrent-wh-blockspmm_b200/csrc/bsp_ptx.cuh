@@ -62,25 +62,30 @@ enum : unsigned int {
   ST_BAD_PLAN = 1u << 4,
 };
 
-// Wait for the phase with parity `parity` of `bar` to complete.  Gives up
-// after ctl.timeout_ns (or as soon as another role has given up), latches
-// `who` into the global status word, raises the abort flag and returns false.
-static __device__ __noinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity, const WaitCtl& ctl,
-                                               unsigned int who) {
-#pragma unroll 1
-  for (int i = 0; i < 256; ++i)
-    if (mbar_try_wait(bar, parity)) return true;
+// Slow path of a bounded wait: poll until the phase completes, another role
+// has aborted, or ctl.timeout_ns has passed (then latch `who` into the global
+// status word, raise the abort flag and return false).
+static __device__ __noinline__ bool mbar_wait_slow(uint32_t bar, uint32_t parity,
+                                                   volatile int* abort_flag, unsigned int* status,
+                                                   uint64_t timeout_ns, unsigned int who) {
   const uint64_t t0 = globaltimer_ns();
 #pragma unroll 1
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (*ctl.abort_flag) return false;
-    if (globaltimer_ns() - t0 > ctl.timeout_ns) {
-      *ctl.abort_flag = 1;
-      atomicOr(ctl.status, who);
+    if (*abort_flag) return false;
+    if (globaltimer_ns() - t0 > timeout_ns) {
+      *abort_flag = 1;
+      atomicOr(status, who);
       return false;
     }
   }
+}
+
+// Wait for the phase with parity `parity` of `bar` to complete (bounded).
+__device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity, const WaitCtl& ctl,
+                                                  unsigned int who) {
+  if (mbar_try_wait(bar, parity)) return true;
+  return mbar_wait_slow(bar, parity, ctl.abort_flag, ctl.status, ctl.timeout_ns, who);
 }
 
 // ---- TMA --------------------------------------------------------------------
@@ -94,6 +99,15 @@ __device__ __forceinline__ void tma_load_2d(uint32_t smem_dst, const void* tmap,
       "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
       " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_dst),
       "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_load_3d(uint32_t smem_dst, const void* tmap, int32_t x,
+                                            int32_t y, int32_t z, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(smem_dst),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(z), "r"(bar)
       : "memory");
 }
 

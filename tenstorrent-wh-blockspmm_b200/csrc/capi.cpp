@@ -45,6 +45,35 @@ bsp_status encode_2d(bsp_device* dev, CUtensorMap* tm, CUtensorMapDataType dt, i
   return BSP_OK;
 }
 
+bsp_status encode_nd(bsp_device* dev, CUtensorMap* tm, CUtensorMapDataType dt, int rank,
+                     const void* ptr, const uint64_t* dims, const uint64_t* strides_bytes,
+                     const uint32_t* box, CUtensorMapSwizzle swz) {
+  if (reinterpret_cast<uintptr_t>(ptr) % 16)
+    return set_error(BSP_ERR_INVALID_ARG, "device pointers must be 16-byte aligned");
+  cuuint64_t d[5];
+  cuuint64_t s[4];
+  cuuint32_t b[5];
+  cuuint32_t e[5];
+  for (int i = 0; i < rank; ++i) {
+    d[i] = dims[i];
+    b[i] = box[i];
+    e[i] = 1;
+    if (i > 0) {
+      if (strides_bytes[i - 1] % 16)
+        return set_error(BSP_ERR_INVALID_ARG, "row strides must be multiples of 16 bytes");
+      s[i - 1] = strides_bytes[i - 1];
+    }
+  }
+  CUresult r = dev->encode(tm, dt, static_cast<cuuint32_t>(rank), const_cast<void*>(ptr), d, s, b,
+                           e, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return set_error(BSP_ERR_INVALID_ARG,
+                     "cuTensorMapEncodeTiled (rank " + std::to_string(rank) + ") failed (code " +
+                         std::to_string(int(r)) + ")");
+  return BSP_OK;
+}
+
 static bsp_status check_desc(const bsp_bsr_desc* A, bool need_values) {
   if (!A) return set_error(BSP_ERR_INVALID_ARG, "null BSR descriptor");
   if (A->R <= 0 || A->C <= 0 || A->rows <= 0 || A->cols <= 0 || A->nnzb < 0)
@@ -254,7 +283,9 @@ bsp_status bsp_spmm_plan_create(bsp_device* dev, const bsp_bsr_desc* A, const in
   std::vector<void*> ptrs;
   s = upload_blob({{p->h_units.data(), p->h_units.size() * sizeof(SpmmUnit)},
                    {p->h_cta_begin.data(), p->h_cta_begin.size() * sizeof(int32_t)},
-                   {p->h_steps.data(), p->h_steps.size() * sizeof(int32_t)}},
+                   {p->h_steps.data(), p->h_steps.size() * sizeof(int32_t)},
+                   {p->h_stage_list.data(), p->h_stage_list.size() * sizeof(int32_t)},
+                   {p->h_cta_stage_begin.data(), p->h_cta_stage_begin.size() * sizeof(int32_t)}},
                   &p->d_blob, &p->blob_bytes, &ptrs);
   if (s != BSP_OK) {
     delete p;
@@ -263,6 +294,8 @@ bsp_status bsp_spmm_plan_create(bsp_device* dev, const bsp_bsr_desc* A, const in
   p->d_units = static_cast<SpmmUnit*>(ptrs[0]);
   p->d_cta_begin = static_cast<int32_t*>(ptrs[1]);
   p->d_steps = static_cast<int32_t*>(ptrs[2]);
+  p->d_stage_list = static_cast<int4*>(ptrs[3]);
+  p->d_cta_stage_begin = static_cast<int32_t*>(ptrs[4]);
   *out = p;
   return BSP_OK;
 }
@@ -277,6 +310,8 @@ bsp_status bsp_spmm_execute(const bsp_spmm_plan* plan, const bsp_bsr_desc* A, co
     return set_error(BSP_ERR_INVALID_ARG, "A does not match the plan's pattern");
   if (ldb < plan->N || ldc < plan->N)
     return set_error(BSP_ERR_INVALID_ARG, "leading dimensions must be >= N");
+  if (plan->variant == 1)
+    return launch_spmm_rowstack(plan, A, B, ldb, C, ldc, static_cast<cudaStream_t>(stream));
   return launch_spmm(plan, A, B, ldb, C, ldc, static_cast<cudaStream_t>(stream));
 }
 
@@ -301,6 +336,8 @@ bsp_status bsp_spmm_plan_info(const bsp_spmm_plan* p, int64_t info[16]) {
   info[8] = static_cast<int64_t>(p->blob_bytes);
   info[9] = p->smem_bytes;
   info[10] = p->tmem_cols;
+  info[11] = p->variant;
+  info[12] = p->nprod;
   return BSP_OK;
 }
 
@@ -531,6 +568,64 @@ bsp_status bsp_serpentine_assign(int64_t n, int32_t parts, int32_t* owner, int32
       owner[per[p][k]] = p;
       slot[per[p][k]] = static_cast<int32_t>(k);
     }
+  return BSP_OK;
+}
+
+}  // extern "C"
+
+// ------------------------------------------------ host-only inspection ----
+#include "bsp_testing.h"
+
+extern "C" {
+
+bsp_status bsp_spmm_plan_inspect(int64_t M, int64_t K, int32_t R, int32_t C, int64_t nnzb,
+                                 const int32_t* row_ptr, const int32_t* col_idx, int64_t N,
+                                 bsp_dtype c_type, bsp_strategy strategy,
+                                 const bsp_spmm_opts* opts, int32_t sm_count, int32_t max_smem,
+                                 int64_t info[16], int32_t* units_out, int32_t* cta_begin_out,
+                                 int32_t* steps_out) {
+  if (!row_ptr || !info || (nnzb > 0 && !col_idx) || R <= 0 || C <= 0)
+    return set_error(BSP_ERR_INVALID_ARG, "bad arguments");
+  bsp_spmm_plan p;
+  p.M = M;
+  p.K = K;
+  p.N = N;
+  p.R = R;
+  p.C = C;
+  p.nnzb = nnzb;
+  p.c_type = c_type;
+  p.strategy = strategy;
+  bsp_status s = plan_spmm_host(&p, row_ptr, col_idx, sm_count, max_smem, opts);
+  if (s != BSP_OK) return s;
+  bsp_spmm_plan_info(&p, info);
+  if (units_out) memcpy(units_out, p.h_units.data(), p.h_units.size() * sizeof(SpmmUnit));
+  if (cta_begin_out)
+    memcpy(cta_begin_out, p.h_cta_begin.data(), p.h_cta_begin.size() * sizeof(int32_t));
+  if (steps_out) memcpy(steps_out, p.h_steps.data(), p.n_steps * (1 + p.G) * sizeof(int32_t));
+  return BSP_OK;
+}
+
+bsp_status bsp_sddmm_plan_inspect(int64_t M, int64_t N, int32_t R, int32_t C, int64_t nnzb,
+                                  const int32_t* row_ptr, const int32_t* col_idx, int64_t K,
+                                  bsp_strategy strategy, const bsp_sddmm_opts* opts,
+                                  int32_t sm_count, int32_t max_smem, int64_t info[16],
+                                  int32_t* units_out, int32_t* cta_begin_out) {
+  if (!row_ptr || !info || (nnzb > 0 && !col_idx) || R <= 0 || C <= 0)
+    return set_error(BSP_ERR_INVALID_ARG, "bad arguments");
+  bsp_sddmm_plan p;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.R = R;
+  p.C = C;
+  p.nnzb = nnzb;
+  p.strategy = strategy;
+  bsp_status s = plan_sddmm_host(&p, row_ptr, col_idx, sm_count, max_smem, opts);
+  if (s != BSP_OK) return s;
+  bsp_sddmm_plan_info(&p, info);
+  if (units_out) memcpy(units_out, p.h_units.data(), p.h_units.size() * sizeof(SddmmUnit));
+  if (cta_begin_out)
+    memcpy(cta_begin_out, p.h_cta_begin.data(), p.h_cta_begin.size() * sizeof(int32_t));
   return BSP_OK;
 }
 

@@ -112,6 +112,11 @@ bsp_status plan_spmm_host(bsp_spmm_plan* p, const int32_t* row_ptr, const int32_
   const int64_t nbr = M / R, nbc = K / C;
   bsp_status st = check_pattern(row_ptr, col_idx, nbr, nbc, p->nnzb);
   if (st != BSP_OK) return st;
+  // DDA runs on the row-stacked kernel unless the caller asks for one of the
+  // swap-AB variants (group_mma 2: one MMA per block, 3: stacked swap-AB).
+  if (p->strategy == BSP_DDA && o.group_mma != 2 && o.group_mma != 3)
+    return plan_spmm_rowstack(p, row_ptr, col_idx, sm_count, max_smem, opts);
+  p->variant = 0;
 
   const int Rs = slab_height(R);
   const int kc = (C % 64 == 0) ? 64 : 32;
@@ -141,9 +146,13 @@ bsp_status plan_spmm_host(bsp_spmm_plan* p, const int32_t* row_ptr, const int32_
   p->kc = kc;
   p->G = G;
   p->NT = NT;
+  // Stacked issue (one MMA of N = G*Rs per k-step and tile) covers G = 1 too;
+  // only DDA with group_mma = 2 issues one MMA per present block.
+  p->stacked = (G == 1 || o.group_mma != 2) ? 1 : 0;
 
   // ---- steps and units ----
   const int stride = 1 + G;
+  p->step_stride = stride;
   std::vector<int32_t>& steps = p->h_steps;
   steps.clear();
   std::vector<SpmmUnit> units;
@@ -242,11 +251,192 @@ bsp_status plan_spmm_host(bsp_spmm_plan* p, const int32_t* row_ptr, const int32_
   stages = std::min(stages, 32);
   if (stages < 2)
     return set_error(BSP_ERR_UNSUPPORTED, "block too large: fewer than 2 pipeline stages fit");
+  // Producer warps issue stages round-robin; each owns stage slots congruent
+  // to it, so the ring length is a multiple of their number.
+  int nprod = std::min(spmm_max_producers(), stages);
+  if (o.producers > 0) nprod = std::min(nprod, o.producers);
+  stages = stages / nprod * nprod;
+  p->nprod = nprod;
   p->stage_bytes = stage_bytes;
   p->stages = stages;
   p->smem_bytes = spmm_smem_bytes(stages, stage_bytes, p->c_type == BSP_F32);
   p->tmem_cols = pow2_at_least(2 * NT * G * Rs);
   p->timeout_ns = static_cast<uint64_t>(o.timeout_ms > 0 ? o.timeout_ms : 2000) * 1000000ull;
+  return BSP_OK;
+}
+
+// Row-stacked schedule (spmm_rowstack.cu).  An "entry" is an Rs-row slab of a
+// block-row (Rs = 128, 64 or 32, the largest that divides R); G = 128 / Rs
+// consecutive entries form the 128 rows of one MMA.  A unit is one entry group
+// x 256 output columns; its steps are the distinct block-columns of the
+// group's rows, each listing per entry the block to multiply (or -1).
+bsp_status plan_spmm_rowstack(bsp_spmm_plan* p, const int32_t* row_ptr, const int32_t* col_idx,
+                              int sm_count, int max_smem, const bsp_spmm_opts* opts) {
+  bsp_spmm_opts o;
+  memset(&o, 0, sizeof(o));
+  if (opts) o = *opts;
+  const int R = p->R, C = p->C;
+  const int64_t nbr = p->M / R;
+  const int Rs = (R % 128 == 0) ? 128 : (R % 64 == 0) ? 64 : 32;
+  const int slabs = R / Rs;
+  const int G = 128 / Rs;
+  const int kc = (C % 64 == 0) ? 64 : 32;
+  const int nkc = C / kc;
+  const int64_t n_entries = nbr * slabs;
+  const int ntiles = static_cast<int>((p->N + 255) / 256);
+  if (n_entries >= (int64_t(1) << 31))
+    return set_error(BSP_ERR_UNSUPPORTED, "too many block-rows");
+  p->variant = 1;
+  p->Rs = Rs;
+  p->kc = kc;
+  p->G = G;
+  p->NT = 2;  // 256 columns = two 128-column tiles
+  p->stacked = 1;
+  const int stride = 1 + G;
+  p->step_stride = stride;
+  std::vector<int32_t>& steps = p->h_steps;
+  steps.clear();
+  std::vector<SpmmUnit> units;
+  std::vector<int64_t> weight;
+  const int esz = p->c_type == BSP_F32 ? 4 : 2;
+  std::vector<std::pair<int32_t, int32_t>> items;  // (col, g * 2^24-free: block id)
+  std::vector<int8_t> item_g;
+  for (int64_t e0 = 0; e0 < n_entries; e0 += G) {
+    const int nent = static_cast<int>(std::min<int64_t>(G, n_entries - e0));
+    const int32_t s_begin = static_cast<int32_t>(steps.size() / stride);
+    int32_t mask = 0;
+    items.clear();
+    item_g.clear();
+    for (int g = 0; g < nent; ++g) {
+      const int64_t i = (e0 + g) / slabs;
+      if (row_ptr[i + 1] > row_ptr[i]) mask |= 1 << g;
+      for (int32_t b = row_ptr[i]; b < row_ptr[i + 1]; ++b) {
+        items.push_back({col_idx[b], b});
+        item_g.push_back(static_cast<int8_t>(g));
+      }
+    }
+    std::vector<int32_t> order(items.size());
+    std::iota(order.begin(), order.end(), 0);
+    std::stable_sort(order.begin(), order.end(),
+                     [&](int32_t a, int32_t b) { return items[a].first < items[b].first; });
+    int64_t cur = -1;
+    int64_t a_loads = 0;
+    for (int32_t k : order) {
+      const int g = item_g[k];
+      const bool open = cur >= 0 && steps[cur * stride] == items[k].first &&
+                        steps[cur * stride + 1 + g] < 0;
+      if (!open) {
+        cur = static_cast<int64_t>(steps.size() / stride);
+        steps.push_back(items[k].first);
+        for (int q = 0; q < G; ++q) steps.push_back(-1);
+      }
+      steps[cur * stride + 1 + g] = items[k].second;
+      ++a_loads;
+    }
+    const int32_t s_end = static_cast<int32_t>(steps.size() / stride);
+    for (int t = 0; t < ntiles; ++t) {
+      SpmmUnit u;
+      u.row0 = static_cast<int32_t>(e0);
+      u.nrows = nent;
+      u.r_off = 0;
+      u.n0 = t * 256;
+      u.nt = 1;
+      u.step_begin = s_begin;
+      u.step_end = s_end;
+      u.row_mask = mask;
+      units.push_back(u);
+      const int64_t smem_in = int64_t(nkc) * ((s_end - s_begin) * int64_t(kc) * 256 * 2 +
+                                              a_loads * int64_t(Rs) * kc * 2 / std::max(1, 1));
+      weight.push_back(smem_in + int64_t(nent) * Rs * 256 * esz + 4096);
+    }
+  }
+  p->n_steps = static_cast<int64_t>(steps.size() / stride);
+  if (steps.empty()) {
+    steps.push_back(0);
+    for (int q = 0; q < G; ++q) steps.push_back(-1);
+  }
+  int grid = o.max_ctas > 0 ? std::min(o.max_ctas, sm_count) : sm_count;
+  grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(grid, units.size())));
+  std::vector<std::vector<int32_t>> per;
+  if (o.no_load_balance)
+    contiguous_split(static_cast<int64_t>(units.size()), grid, &per);
+  else
+    serpentine_order(weight, grid, &per);
+  p->h_units.clear();
+  p->h_cta_begin.assign(1, 0);
+  for (int c = 0; c < grid; ++c) {
+    for (int32_t idx : per[c]) p->h_units.push_back(units[idx]);
+    p->h_cta_begin.push_back(static_cast<int32_t>(p->h_units.size()));
+  }
+  p->n_units = static_cast<int64_t>(units.size());
+  p->grid = grid;
+  int stage_bytes = 4 * kc * 128 + G * Rs * kc * 2;
+  stage_bytes = (stage_bytes + 1023) / 1024 * 1024;
+  int stages = std::min(rowstack_max_stages(), (max_smem - 2048) / stage_bytes);
+  if (stages < 2) return set_error(BSP_ERR_UNSUPPORTED, "block too large for the pipeline");
+  int nprod = std::min(rowstack_max_producers(), stages);
+  if (o.producers > 0) nprod = std::min(nprod, o.producers);
+  stages = stages / nprod * nprod;
+  p->nprod = nprod;
+  p->stage_bytes = stage_bytes;
+  p->stages = stages;
+  p->smem_bytes = 2048 + stages * stage_bytes;
+  p->tmem_cols = 512;
+  p->timeout_ns = static_cast<uint64_t>(o.timeout_ms > 0 ? o.timeout_ms : 2000) * 1000000ull;
+
+  // ---- per-CTA stage lists ----
+  // The kernel's smem ring is in lockstep with each CTA's stage sequence
+  // (stage k uses slot k % stages), so the host can tell exactly which entry
+  // slots still hold an older block and must be zeroed before a stage where
+  // that entry is absent.
+  const bool b3d = (p->N % 64 == 0);
+  const uint32_t all = (1u << G) - 1u;
+  p->h_stage_list.clear();
+  p->h_cta_stage_begin.assign(1, 0);
+  std::vector<uint32_t> dirty(stages);
+  for (int c = 0; c < grid; ++c) {
+    std::fill(dirty.begin(), dirty.end(), all);  // unknown contents until first written
+    int64_t k = 0;
+    for (int32_t ui = p->h_cta_begin[c]; ui < p->h_cta_begin[c + 1]; ++ui) {
+      const SpmmUnit& u = p->h_units[ui];
+      const int nsteps = u.step_end - u.step_begin;
+      if (nsteps == 0) {
+        const int32_t e[8] = {0, 0, RS_F_FIRST | RS_F_LAST | RS_F_EMPTY, 0, -1, -1, -1, -1};
+        p->h_stage_list.insert(p->h_stage_list.end(), e, e + 8);
+        ++k;
+        continue;
+      }
+      int slab_off[4] = {0, 0, 0, 0};
+      for (int g = 0; g < G; ++g) slab_off[g] = static_cast<int>((u.row0 + g) % slabs) * Rs;
+      const int nst = nsteps * nkc;
+      for (int s = 0; s < nst; ++s) {
+        const int j = s / nkc, kci = s % nkc;
+        const int32_t* st = &steps[static_cast<size_t>(u.step_begin + j) * stride];
+        uint32_t present = 0;
+        int np = 0;
+        int32_t ay[4] = {-1, -1, -1, -1};
+        for (int g = 0; g < G; ++g)
+          if (g < u.nrows && st[1 + g] >= 0) {
+            present |= 1u << g;
+            ++np;
+            ay[g] = st[1 + g] * R + slab_off[g];
+          }
+        const int slot = static_cast<int>(k % stages);
+        const uint32_t zero = ~present & all & dirty[slot];
+        dirty[slot] = present;
+        int32_t flags = static_cast<int32_t>(present | (zero << 4) | (uint32_t(np) << 16));
+        if (s == 0) flags |= RS_F_FIRST;
+        if (s == nst - 1) flags |= RS_F_LAST;
+        const int32_t e[8] = {st[0] * C + kci * kc, b3d ? u.n0 / 64 : u.n0, flags, kci * kc,
+                              ay[0], ay[1], ay[2], ay[3]};
+        p->h_stage_list.insert(p->h_stage_list.end(), e, e + 8);
+        ++k;
+      }
+    }
+    if (p->h_stage_list.size() / 8 >= (size_t(1) << 31))
+      return set_error(BSP_ERR_UNSUPPORTED, "schedule too long");
+    p->h_cta_stage_begin.push_back(static_cast<int32_t>(p->h_stage_list.size() / 8));
+  }
   return BSP_OK;
 }
 

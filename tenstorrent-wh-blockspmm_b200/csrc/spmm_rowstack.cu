@@ -1,0 +1,422 @@
+// BSR SpMM on sm_100a tensor cores, "row-stacked" form used by the DDA
+// strategy:  C[M x N] = A_bsr[M x K] * B[K x N].
+//
+// The tensor pipe takes ~135 cycles per M=128 x K=16 MMA whatever N is (up to
+// 256), so only N = 256 MMAs reach full rate.  This kernel therefore keeps the
+// natural orientation and fills the MMA with block-sparse structure:
+//   MMA M = 128 output rows = G = 128/Rs "entries" (an entry is an Rs-row slab
+//           of one block-row) stacked on top of each other; at each step the
+//           entries' blocks of the same block-column j are loaded side by side
+//           (K-major operand, absent entries zero-filled), so ONE load of the
+//           dense slice B[j*C : (j+1)*C, n0 : n0+256] serves every entry that
+//           has a block in column j -- the B-slice sharing the reference's
+//           chain of direct addressing gives (block_spmm/kernels/dataflow/
+//           reader_in1_chain_of_direct_addressing.cpp:257-367), here inside
+//           one CTA's shared memory;
+//   MMA N = 256 dense columns (MN-major B operand, four 64-column 128B-swizzle
+//           boxes from one 3-D TMA load), so every A block is reused across
+//           256 columns (the store-and-forward reuse of in0);
+//   MMA K = C, in chunks of kc per pipeline stage, 16 per MMA.
+// The fp32 accumulator (128 lanes = output rows x 256 columns) sits in TMEM,
+// double-buffered; an epilogue thread owns one output row and writes 32
+// consecutive columns per TMEM load with 16-byte vector stores.
+//
+// Warp roles (256 threads, one CTA per SM, persistent over its unit list):
+//   warp 0      TMEM allocator + MMA issuer (one thread), alone on its SM
+//               sub-partition apart from one mostly-idle epilogue warp
+//   warps 1..3  TMA producers: warp w owns every nprod-th pipeline stage and
+//               touches only the metadata of its own stages
+//   warps 4..7  epilogue (TMEM lane quarters 0..3)
+// Every wait is bounded (see bsp_ptx.cuh).
+#include <cuda_bf16.h>
+
+#include <type_traits>
+
+#include "bsp_internal.h"
+#include "bsp_ptx.cuh"
+
+namespace bsp {
+using namespace dev;
+
+namespace {
+
+constexpr int kRsMmaWarp = 0;
+constexpr int kRsProd0 = 1;
+constexpr int kRsMaxProducers = 3;
+constexpr int kRsEpi0 = 4;
+constexpr int kRsThreads = 8 * 32;
+constexpr int kRsMaxStages = 30;
+constexpr int kRsN = 256;       // MMA N: dense columns per unit
+constexpr int kRsMaxG = 4;      // entries per stack (128 / 32)
+
+struct RsSmemHeader {
+  uint64_t full[kRsMaxStages];
+  uint64_t empty[kRsMaxStages];
+  uint64_t acc_full[2];
+  uint64_t acc_empty[2];
+  uint64_t drain;
+  uint32_t info[kRsMaxStages];
+  uint32_t tmem_base;
+  int abort_flag;
+};
+static_assert(sizeof(RsSmemHeader) <= 1024, "header must fit its 1 KiB slot");
+
+enum : uint32_t {
+  RS_FIRST = 1u << 12,
+  RS_LAST = 1u << 13,
+  RS_EMPTY = 1u << 14,
+};
+
+__device__ __forceinline__ uint32_t baddr(const uint64_t* b) { return smem_u32(b); }
+
+__device__ __noinline__ bool rs_drain_wait(uint32_t bar, uint32_t parity, const WaitCtl& ctl) {
+  int zero = 0;
+  WaitCtl c2{&zero, ctl.status, ctl.timeout_ns};
+  return mbar_wait_bounded(bar, parity, c2, ST_TIMEOUT_DRAIN);
+}
+
+// Producer warp pw (0-based among producers): issues the CTA's pipeline
+// stages pw, pw + nprod, pw + 2*nprod, ... from the precomputed stage list.
+// 32 of its stages are fetched at once (lane l holds the l-th) and broadcast
+// by shuffles, so the issuing lane never waits on global memory per stage.
+__device__ __forceinline__ void rs_producer(const SpmmKernelParams& p, RsSmemHeader* hdr,
+                                           uint8_t* gbase, uint32_t base, uint32_t stage0,
+                                           const WaitCtl& ctl, int pw, int lane) {
+  const int P = p.nprod;
+  const int k_begin = p.cta_stage_begin[blockIdx.x];
+  const int n = p.cta_stage_begin[blockIdx.x + 1] - k_begin;
+  const uint32_t a_slot = static_cast<uint32_t>(p.Rs * p.kc * 2);
+  const uint32_t b_blk = static_cast<uint32_t>(p.kc * 128);  // one 64-column block
+  const uint32_t b_bytes = 4u * b_blk;
+  int stage = pw;
+  uint32_t phase = 0;
+  uint32_t armed = 0, armed_parity = 0;
+  bool ok = true;
+#pragma unroll 1
+  for (int k0 = pw; k0 < n && ok; k0 += 32 * P) {
+    int4 w0 = make_int4(0, 0, 0, 0), w1 = make_int4(-1, -1, -1, -1);
+    const int kl = k0 + lane * P;
+    if (kl < n) {
+      const int4* e = p.stage_list + 2 * static_cast<size_t>(k_begin + kl);
+      w0 = __ldg(e);
+      w1 = __ldg(e + 1);
+    }
+    const int cnt = min(32, (n - k0 + P - 1) / P);
+#pragma unroll 1
+    for (int j = 0; j < cnt; ++j) {
+      const int ky = __shfl_sync(0xffffffffu, w0.x, j);
+      const int bz = __shfl_sync(0xffffffffu, w0.y, j);
+      const int flags = __shfl_sync(0xffffffffu, w0.z, j);
+      const int ax = __shfl_sync(0xffffffffu, w0.w, j);
+      int ay[kRsMaxG];
+      ay[0] = __shfl_sync(0xffffffffu, w1.x, j);
+      ay[1] = __shfl_sync(0xffffffffu, w1.y, j);
+      ay[2] = __shfl_sync(0xffffffffu, w1.z, j);
+      ay[3] = __shfl_sync(0xffffffffu, w1.w, j);
+      if (lane == 0)
+        ok = mbar_wait_bounded(baddr(&hdr->empty[stage]), phase ^ 1u, ctl, ST_TIMEOUT_PRODUCER);
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) break;
+      const uint32_t sb = stage0 + static_cast<uint32_t>(stage) * p.stage_bytes;
+      const uint32_t zero = (static_cast<uint32_t>(flags) >> 4) & 0xFu;
+      if (zero) {
+        // entries absent from this step whose slot still holds an older block
+#pragma unroll 1
+        for (uint32_t m = zero; m; m &= m - 1) {
+          const int g = __ffs(m) - 1;
+          uint4* dst = reinterpret_cast<uint4*>(gbase + (sb + b_bytes + g * a_slot - base));
+          for (uint32_t i = lane; i < a_slot / 16; i += 32) dst[i] = make_uint4(0, 0, 0, 0);
+        }
+        fence_proxy_async_smem();
+      }
+      __syncwarp();
+      if (lane == 0) {
+        hdr->info[stage] = static_cast<uint32_t>(flags) & (RS_FIRST | RS_LAST | RS_EMPTY);
+        const uint32_t full = baddr(&hdr->full[stage]);
+        if (flags & RS_EMPTY) {
+          mbar_arrive(full);
+        } else {
+          const uint32_t np = (static_cast<uint32_t>(flags) >> 16) & 7u;
+          mbar_arrive_expect_tx(full, b_bytes + np * a_slot);
+          if (p.b3d) {
+            tma_load_3d(sb, &p.tm_b, 0, ky, bz, full);
+          } else {
+#pragma unroll
+            for (int h = 0; h < 4; ++h) tma_load_2d(sb + h * b_blk, &p.tm_b, bz + h * 64, ky, full);
+          }
+#pragma unroll
+          for (int g = 0; g < kRsMaxG; ++g)
+            if ((flags >> g) & 1) tma_load_2d(sb + b_bytes + g * a_slot, &p.tm_a, ax, ay[g], full);
+        }
+        armed |= 1u << stage;
+        armed_parity = (armed_parity & ~(1u << stage)) | (phase << stage);
+      }
+      stage += P;
+      if (stage >= p.stages) {
+        stage -= p.stages;
+        phase ^= 1u;
+      }
+    }
+  }
+  if (lane == 0) {
+#pragma unroll 1
+    for (int s = 0; s < p.stages; ++s)
+      if (armed & (1u << s)) rs_drain_wait(baddr(&hdr->full[s]), (armed_parity >> s) & 1u, ctl);
+  }
+  __syncwarp();
+}
+
+template <int kKS>
+__device__ __forceinline__ void rs_mma(const SpmmKernelParams& p, RsSmemHeader* hdr,
+                                       uint32_t stage0, uint32_t tmem_base, int u_begin, int u_end,
+                                       const WaitCtl& ctl) {
+  int stage = 0;
+  uint32_t phase = 0;
+  int acc = 0;
+  uint32_t acc_phase = 0;
+  int units_left = u_end - u_begin;
+  // A (stacked entries): K-major, rows of kc*2 bytes; B: MN-major 128B swizzle,
+  // LBO = one 64-column block (kc rows x 128 B), SBO = 8 k-rows.
+  const uint32_t idesc = idesc_bf16_f32(128, kRsN, /*a K-major*/ 0, /*b MN-major*/ 1);
+  const uint32_t b_bytes = static_cast<uint32_t>(4 * p.kc * 128);
+  const uint32_t a_sbo = (p.a_swizzle_mode == 2) ? 1024u : 512u;
+  const uint64_t adesc0 = smem_desc(stage0 + b_bytes, 16u, a_sbo, static_cast<uint32_t>(p.a_swizzle_mode));
+  const uint64_t bdesc0 = smem_desc(stage0, static_cast<uint32_t>(p.kc * 128), 1024u, 2u);
+  const uint32_t stage16 = static_cast<uint32_t>(p.stage_bytes) >> 4;
+  const uint32_t full0 = baddr(&hdr->full[0]);
+  const uint32_t empty0 = baddr(&hdr->empty[0]);
+  uint32_t soff = 0;
+  uint32_t d0 = tmem_base;
+#pragma unroll 1
+  while (units_left > 0) {
+    if (!mbar_wait_bounded(full0 + stage * 8, phase, ctl, ST_TIMEOUT_MMA)) break;
+    const uint32_t info = hdr->info[stage];
+    const bool first = (info & RS_FIRST) != 0;
+    if (first) {
+      if (!mbar_wait_bounded(baddr(&hdr->acc_empty[acc]), acc_phase ^ 1u, ctl, ST_TIMEOUT_MMA))
+        break;
+      tc_fence_after();
+      d0 = tmem_base + static_cast<uint32_t>(acc * kRsN);
+    }
+    if (!(info & RS_EMPTY)) {
+      const uint64_t ad = adesc0 + soff, bd = bdesc0 + soff;
+#pragma unroll
+      for (int k = 0; k < kKS; ++k)
+        mma_bf16(d0, ad + k * 2u, bd + k * 128u, idesc, (k > 0 || !first) ? 1u : 0u);
+    }
+    mma_commit(empty0 + stage * 8);
+    if (info & RS_LAST) {
+      mma_commit(baddr(&hdr->acc_full[acc]));
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1u;
+      --units_left;
+    }
+    soff += stage16;
+    if (++stage == p.stages) {
+      stage = 0;
+      soff = 0;
+      phase ^= 1u;
+    }
+  }
+  mma_commit(baddr(&hdr->drain));
+  rs_drain_wait(baddr(&hdr->drain), 0, ctl);
+}
+
+// Epilogue warp with TMEM lane quarter q: lanes 32q..32q+31 are output rows of
+// entry g = 32q / Rs; each thread writes its row, 32 columns per TMEM load.
+template <bool kF32>
+__device__ __forceinline__ void rs_epilogue(const SpmmKernelParams& p, RsSmemHeader* hdr,
+                                           uint32_t tmem_base, int u_begin, int u_end,
+                                           const WaitCtl& ctl, int warp, int lane) {
+  const int q = warp & 3;
+  const int g = (32 * q) / p.Rs;
+  const int rrow = (32 * q) % p.Rs + lane;
+  const int slabs = p.R / p.Rs;
+  int acc = 0;
+  uint32_t acc_phase = 0;
+  SpmmUnit nxt;
+  if (u_begin < u_end) nxt = p.units[u_begin];
+#pragma unroll 1
+  for (int u = u_begin; u < u_end; ++u) {
+    const SpmmUnit un = nxt;
+    if (u + 1 < u_end) nxt = p.units[u + 1];
+    if (!mbar_wait_bounded(baddr(&hdr->acc_full[acc]), acc_phase, ctl, ST_TIMEOUT_EPILOGUE)) break;
+    tc_fence_after();
+    if (g < un.nrows) {
+      const int e = un.row0 + g;
+      const int64_t row = static_cast<int64_t>(e / slabs) * p.R + (e % slabs) * p.Rs + rrow;
+      const bool present = (un.row_mask >> g) & 1;
+#pragma unroll 1
+      for (int c = 0; c < kRsN / 32; ++c) {
+        const int n = un.n0 + c * 32;
+        if (n >= p.N) break;
+        uint32_t v[32];
+        if (present) {
+          tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
+                                 static_cast<uint32_t>(acc * kRsN + c * 32),
+                             v);
+          tmem_ld_wait();
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = 0u;
+        }
+        if constexpr (kF32) {
+          float* dst = static_cast<float*>(p.c_ptr) + row * p.ldc + n;
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            if (n + 4 * i < p.N)
+              reinterpret_cast<uint4*>(dst)[i] = make_uint4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+        } else {
+          __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(p.c_ptr) + row * p.ldc + n;
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            if (n + 8 * i < p.N) {
+              uint32_t w[4];
+#pragma unroll
+              for (int h = 0; h < 4; ++h) {
+                const __nv_bfloat162 b2 = __floats2bfloat162_rn(__uint_as_float(v[8 * i + 2 * h]),
+                                                                __uint_as_float(v[8 * i + 2 * h + 1]));
+                w[h] = *reinterpret_cast<const uint32_t*>(&b2);
+              }
+              reinterpret_cast<uint4*>(dst)[i] = make_uint4(w[0], w[1], w[2], w[3]);
+            }
+          }
+        }
+      }
+    }
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(baddr(&hdr->acc_empty[acc]));
+    acc ^= 1;
+    if (acc == 0) acc_phase ^= 1u;
+  }
+}
+
+template <bool kF32>
+__global__ void __launch_bounds__(kRsThreads, 1) spmm_rowstack_tcgen05(const __grid_constant__ SpmmKernelParams p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  uint8_t* gbase = smem_raw + (base - raw);
+  RsSmemHeader* hdr = reinterpret_cast<RsSmemHeader*>(gbase);
+  const uint32_t stage0 = base + 1024u;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int u_begin = p.cta_begin[blockIdx.x];
+  const int u_end = p.cta_begin[blockIdx.x + 1];
+
+  if (threadIdx.x == 32) {
+    for (int s = 0; s < p.stages; ++s) {
+      mbar_init(baddr(&hdr->full[s]), 1);
+      mbar_init(baddr(&hdr->empty[s]), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(baddr(&hdr->acc_full[a]), 1);
+      mbar_init(baddr(&hdr->acc_empty[a]), 4);
+    }
+    mbar_init(baddr(&hdr->drain), 1);
+    hdr->abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&p.tm_a);
+    tma_prefetch_desc(&p.tm_b);
+  }
+  if (warp == kRsMmaWarp) {
+    tmem_alloc(smem_u32(&hdr->tmem_base), static_cast<uint32_t>(p.tmem_cols));
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = hdr->tmem_base;
+  const WaitCtl ctl{&hdr->abort_flag, p.status, p.timeout_ns};
+
+  if (warp == kRsMmaWarp) {
+    if (lane == 0) {
+      if (p.kc == 32) rs_mma<2>(p, hdr, stage0, tmem_base, u_begin, u_end, ctl);
+      else rs_mma<4>(p, hdr, stage0, tmem_base, u_begin, u_end, ctl);
+    }
+  } else if (warp < kRsEpi0) {
+    if (warp - kRsProd0 < p.nprod) rs_producer(p, hdr, gbase, base, stage0, ctl, warp - kRsProd0, lane);
+  } else {
+    rs_epilogue<kF32>(p, hdr, tmem_base, u_begin, u_end, ctl, warp, lane);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kRsMmaWarp) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, static_cast<uint32_t>(p.tmem_cols));
+  }
+}
+
+}  // namespace
+
+int rowstack_max_producers() { return kRsMaxProducers; }
+int rowstack_max_stages() { return kRsMaxStages; }
+
+bsp_status launch_spmm_rowstack(const bsp_spmm_plan* p, const bsp_bsr_desc* A, const void* B,
+                                int64_t ldb, void* C, int64_t ldc, cudaStream_t stream) {
+  bsp_device* dev = p->dev;
+  const bool f32 = p->c_type == BSP_F32;
+  if (p->n_units == 0 || p->M == 0 || p->N == 0) return BSP_OK;
+  if (reinterpret_cast<uintptr_t>(C) % 16 || (ldc * (f32 ? 4 : 2)) % 16)
+    return set_error(BSP_ERR_INVALID_ARG, "C must be 16-byte aligned with 16-byte row pitch");
+  SpmmKernelParams kp;
+  memset(&kp, 0, sizeof(kp));
+  bsp_status st;
+  const CUtensorMapSwizzle a_swz = p->kc == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+  if (p->nnzb > 0) {
+    st = encode_2d(dev, &kp.tm_a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, A->values, p->C,
+                   static_cast<uint64_t>(p->nnzb) * p->R, p->C, p->kc, p->Rs, a_swz);
+  } else {
+    st = encode_2d(dev, &kp.tm_a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, B, p->N, p->K, ldb, p->kc,
+                   p->Rs, a_swz);
+  }
+  if (st != BSP_OK) return st;
+  const bool b3d = (p->N % 64 == 0);
+  if (b3d) {
+    const uint64_t dims[3] = {64, static_cast<uint64_t>(p->K), static_cast<uint64_t>(p->N / 64)};
+    const uint64_t strides[2] = {static_cast<uint64_t>(ldb) * 2, 128};
+    const uint32_t box[3] = {64, static_cast<uint32_t>(p->kc), 4};
+    st = encode_nd(dev, &kp.tm_b, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, B, dims, strides, box,
+                   CU_TENSOR_MAP_SWIZZLE_128B);
+  } else {
+    st = encode_2d(dev, &kp.tm_b, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, B, p->N, p->K, ldb, 64,
+                   p->kc, CU_TENSOR_MAP_SWIZZLE_128B);
+  }
+  if (st != BSP_OK) return st;
+  kp.units = p->d_units;
+  kp.cta_begin = p->d_cta_begin;
+  kp.steps = p->d_steps;
+  kp.status = dev->d_status;
+  kp.timeout_ns = p->timeout_ns;
+  kp.c_ptr = C;
+  kp.ldc = ldc;
+  kp.R = p->R;
+  kp.C = p->C;
+  kp.Rs = p->Rs;
+  kp.kc = p->kc;
+  kp.nkc = p->C / p->kc;
+  kp.G = p->G;
+  kp.NT = 2;
+  kp.step_stride = p->step_stride;
+  kp.c_f32 = f32;
+  kp.stages = p->stages;
+  kp.stage_bytes = p->stage_bytes;
+  kp.b_bytes = 4 * p->kc * 128;
+  kp.a_swizzle_mode = p->kc == 64 ? 2 : 4;
+  kp.acc_cols = kRsN;
+  kp.stacked = 1;
+  kp.tmem_cols = p->tmem_cols;
+  kp.N = static_cast<int32_t>(p->N);
+  kp.nprod = p->nprod;
+  kp.b3d = b3d;
+  kp.stage_list = p->d_stage_list;
+  kp.cta_stage_begin = p->d_cta_stage_begin;
+  auto kern = f32 ? spmm_rowstack_tcgen05<true> : spmm_rowstack_tcgen05<false>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, p->smem_bytes);
+  if (e != cudaSuccess) return cuda_check(e, "cudaFuncSetAttribute(spmm rowstack)");
+  kern<<<p->grid, kRsThreads, p->smem_bytes, stream>>>(kp);
+  return cuda_check(cudaGetLastError(), "spmm rowstack kernel launch");
+}
+
+}  // namespace bsp

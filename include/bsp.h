@@ -94,8 +94,9 @@ typedef struct bsp_spmm_opts {
   int32_t group_mma;       /* DDA: 1 (default) one MMA over the row group's stacked
                               blocks, absent blocks zero-filled; 2 one MMA per
                               present block */
-  int32_t producers;       /* TMA-issuing warps per CTA (1..4, default 4) */
-  int32_t reserved[1];
+  int32_t producers;       /* TMA-issuing warps per CTA (default: as many as fit) */
+  int32_t steps_per_stage; /* DDA: block-columns per pipeline stage, 1 or 2
+                              (default 2 for 32-wide blocks, else 1) */
 } bsp_spmm_opts;
 
 typedef bsp_spmm_opts bsp_sddmm_opts;

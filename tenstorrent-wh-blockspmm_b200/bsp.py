@@ -53,7 +53,7 @@ class Opts(ctypes.Structure):
         ("no_load_balance", ctypes.c_int32), ("group_rows", ctypes.c_int32),
         ("n_tiles", ctypes.c_int32), ("max_ctas", ctypes.c_int32),
         ("timeout_ms", ctypes.c_int32), ("group_mma", ctypes.c_int32),
-        ("producers", ctypes.c_int32), ("reserved", ctypes.c_int32 * 1),
+        ("producers", ctypes.c_int32), ("steps_per_stage", ctypes.c_int32),
     ]
 
 

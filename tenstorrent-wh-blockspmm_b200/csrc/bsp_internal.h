@@ -57,24 +57,29 @@ struct SpmmKernelParams {
   int32_t stacked;              // DDA: one MMA over the group's stacked blocks
   int32_t nprod;                // producer warps issuing stages round-robin
   int32_t b3d;                  // tm_b is the 3-D view (one box per step)
-  const int4* stage_list;       // row-stacked kernel: per-CTA pipeline stages (2 x int4 each)
+  const int4* stage_list;       // row-stacked kernel: per-CTA pipeline stages (4 x int4 each)
   const int32_t* cta_stage_begin;  // [grid + 1]
+  int32_t sub_bytes;            // row-stacked: bytes of one sub-step (B slice + entry slots)
 };
 
-// Row-stacked kernel stage descriptor, precomputed by the planner so that a
-// producer warp issues a stage without any arithmetic or dependent loads.
-//   w[0] ky: B row coordinate (block column * C + k-chunk offset)
+// Row-stacked kernel stage descriptor (16 words), precomputed by the planner
+// so that a producer warp issues a stage without arithmetic or dependent
+// loads.  A stage carries one or two "sub-steps" (consecutive block-columns of
+// the same unit), each a B slice plus the entries' blocks.
+//   w[0] flags: bits 0-3 / 4-7 entries present in sub-step 0 / 1,
+//        8-11 / 12-15 entry slots of sub-step 0 / 1 to zero first,
+//        16-19 present blocks in total, RS_F_* bits below
 //   w[1] bz: first 64-column block of the unit (3-D map) or first column (2-D)
-//   w[2] flags: bits 0-3 present entries, 4-7 entry slots to zero first,
-//        bit 12 first stage of a unit, 13 last, 14 unit without blocks,
-//        bits 16-18 number of present entries
-//   w[3] ax: A column coordinate (k-chunk offset)
-//   w[4..7] ay[g]: A row coordinate of entry g's block slab (or -1)
+//   w[2] ax: A column coordinate (k-chunk offset)
+//   w[3], w[4] ky: B row coordinate of sub-step 0, 1 (block column * C + k offset)
+//   w[5..8], w[9..12] ay[g]: A row of entry g's block slab in sub-step 0, 1 (or -1)
 enum : int32_t {
-  RS_F_FIRST = 1 << 12,
-  RS_F_LAST = 1 << 13,
-  RS_F_EMPTY = 1 << 14,
+  RS_F_FIRST = 1 << 24,  // first stage of a unit
+  RS_F_LAST = 1 << 25,   // last stage of a unit
+  RS_F_EMPTY = 1 << 26,  // unit without blocks: nothing to load or multiply
+  RS_F_TWO = 1 << 27,    // the stage carries two sub-steps
 };
+constexpr int kRsStageWords = 16;
 
 // ---- SDDMM schedule ---------------------------------------------------------
 // One unit = one block-row slab (Rs rows) x up to 4 output segments, each 32
@@ -134,6 +139,7 @@ struct bsp_spmm_plan {
   bsp_strategy strategy = BSP_NAIVE;
   int32_t grid = 0, stages = 0, stage_bytes = 0, smem_bytes = 0, tmem_cols = 0, nprod = 1;
   int32_t variant = 0;      // 0: swap-AB kernel (spmm.cu), 1: row-stacked kernel (spmm_rowstack.cu)
+  int32_t nsub = 1, sub_bytes = 0;  // row-stacked: sub-steps per stage and their size
   int32_t step_stride = 2;  // int32 words per step-table entry (1 + G)
   int64_t n_units = 0, n_steps = 0;
   uint64_t timeout_ns = 0;
@@ -148,8 +154,16 @@ struct bsp_spmm_plan {
   std::vector<bsp::SpmmUnit> h_units;
   std::vector<int32_t> h_cta_begin;
   std::vector<int32_t> h_steps;
-  std::vector<int32_t> h_stage_list;       // row-stacked kernel: 8 words per stage
+  std::vector<int32_t> h_stage_list;       // row-stacked kernel: 16 words per stage
   std::vector<int32_t> h_cta_stage_begin;  // row-stacked kernel
+  // launch cache: kernel parameters (tensor maps) for the last operand set
+  mutable bool kp_valid = false;
+  mutable bool attr_set = false;
+  mutable const void* kp_a = nullptr;
+  mutable const void* kp_b = nullptr;
+  mutable const void* kp_c = nullptr;
+  mutable int64_t kp_ldb = 0, kp_ldc = 0;
+  mutable bsp::SpmmKernelParams kp;
 };
 
 struct bsp_sddmm_plan {

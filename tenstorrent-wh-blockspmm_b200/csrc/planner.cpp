@@ -370,13 +370,35 @@ bsp_status plan_spmm_rowstack(bsp_spmm_plan* p, const int32_t* row_ptr, const in
   }
   p->n_units = static_cast<int64_t>(units.size());
   p->grid = grid;
-  int stage_bytes = 4 * kc * 128 + G * Rs * kc * 2;
+  // With 32-wide blocks a step is only two MMAs; a stage then carries two
+  // consecutive steps so that each barrier round trip moves four MMAs.
+  // One block-column per stage keeps the ring deepest, which measured faster
+  // than two per stage on B200; two remain available for 32-wide blocks.
+  int nsub = 1;
+  if (o.steps_per_stage == 2 && nkc == 1) nsub = 2;
+  const int sub_bytes = 4 * kc * 128 + G * Rs * kc * 2;
+  p->sub_bytes = sub_bytes;
+  p->nsub = nsub;
+  int stage_bytes = nsub * sub_bytes;
   stage_bytes = (stage_bytes + 1023) / 1024 * 1024;
-  int stages = std::min(rowstack_max_stages(), (max_smem - 2048) / stage_bytes);
-  if (stages < 2) return set_error(BSP_ERR_UNSUPPORTED, "block too large for the pipeline");
-  int nprod = std::min(rowstack_max_producers(), stages);
-  if (o.producers > 0) nprod = std::min(nprod, o.producers);
-  stages = stages / nprod * nprod;
+  const int max_stages = std::min(rowstack_max_stages(), (max_smem - 2048) / stage_bytes);
+  if (max_stages < 2) return set_error(BSP_ERR_UNSUPPORTED, "block too large for the pipeline");
+  // Each producer warp owns the ring slots congruent to it, so the ring length
+  // is a multiple of the producer count: pick the count that keeps the most
+  // stages (ties: more producers).
+  int nprod = 1, stages = max_stages;
+  if (o.producers > 0) {
+    nprod = std::min({o.producers, rowstack_max_producers(), max_stages});
+    stages = max_stages / nprod * nprod;
+  } else {
+    for (int q = 2; q <= std::min(rowstack_max_producers(), max_stages); ++q) {
+      const int sq = max_stages / q * q;
+      if (sq >= stages - (stages > 6 ? 1 : 0)) {  // accept losing one stage of a deep ring
+        nprod = q;
+        stages = sq;
+      }
+    }
+  }
   p->nprod = nprod;
   p->stage_bytes = stage_bytes;
   p->stages = stages;
@@ -391,9 +413,10 @@ bsp_status plan_spmm_rowstack(bsp_spmm_plan* p, const int32_t* row_ptr, const in
   // that entry is absent.
   const bool b3d = (p->N % 64 == 0);
   const uint32_t all = (1u << G) - 1u;
+  const int W = kRsStageWords;
   p->h_stage_list.clear();
   p->h_cta_stage_begin.assign(1, 0);
-  std::vector<uint32_t> dirty(stages);
+  std::vector<uint32_t> dirty(static_cast<size_t>(stages) * nsub);  // per (slot, sub-step)
   for (int c = 0; c < grid; ++c) {
     std::fill(dirty.begin(), dirty.end(), all);  // unknown contents until first written
     int64_t k = 0;
@@ -401,41 +424,52 @@ bsp_status plan_spmm_rowstack(bsp_spmm_plan* p, const int32_t* row_ptr, const in
       const SpmmUnit& u = p->h_units[ui];
       const int nsteps = u.step_end - u.step_begin;
       if (nsteps == 0) {
-        const int32_t e[8] = {0, 0, RS_F_FIRST | RS_F_LAST | RS_F_EMPTY, 0, -1, -1, -1, -1};
-        p->h_stage_list.insert(p->h_stage_list.end(), e, e + 8);
+        int32_t e[kRsStageWords] = {RS_F_FIRST | RS_F_LAST | RS_F_EMPTY};
+        p->h_stage_list.insert(p->h_stage_list.end(), e, e + W);
         ++k;
         continue;
       }
       int slab_off[4] = {0, 0, 0, 0};
       for (int g = 0; g < G; ++g) slab_off[g] = static_cast<int>((u.row0 + g) % slabs) * Rs;
-      const int nst = nsteps * nkc;
-      for (int s = 0; s < nst; ++s) {
-        const int j = s / nkc, kci = s % nkc;
-        const int32_t* st = &steps[static_cast<size_t>(u.step_begin + j) * stride];
-        uint32_t present = 0;
-        int np = 0;
-        int32_t ay[4] = {-1, -1, -1, -1};
-        for (int g = 0; g < G; ++g)
-          if (g < u.nrows && st[1 + g] >= 0) {
-            present |= 1u << g;
-            ++np;
-            ay[g] = st[1 + g] * R + slab_off[g];
-          }
+      // the unit's (step, k-chunk) sequence, nsub of them per stage
+      const int nitems = nsteps * nkc;
+      for (int s0 = 0; s0 < nitems; s0 += nsub) {
+        const int nin = std::min(nsub, nitems - s0);
+        int32_t e[kRsStageWords];
+        for (int q = 0; q < W; ++q) e[q] = (q >= 5 && q <= 12) ? -1 : 0;
+        uint32_t flags = 0, np = 0;
         const int slot = static_cast<int>(k % stages);
-        const uint32_t zero = ~present & all & dirty[slot];
-        dirty[slot] = present;
-        int32_t flags = static_cast<int32_t>(present | (zero << 4) | (uint32_t(np) << 16));
-        if (s == 0) flags |= RS_F_FIRST;
-        if (s == nst - 1) flags |= RS_F_LAST;
-        const int32_t e[8] = {st[0] * C + kci * kc, b3d ? u.n0 / 64 : u.n0, flags, kci * kc,
-                              ay[0], ay[1], ay[2], ay[3]};
-        p->h_stage_list.insert(p->h_stage_list.end(), e, e + 8);
+        for (int sub = 0; sub < nin; ++sub) {
+          const int s = s0 + sub;
+          const int j = s / nkc, kci = s % nkc;
+          const int32_t* st = &steps[static_cast<size_t>(u.step_begin + j) * stride];
+          uint32_t present = 0;
+          for (int g = 0; g < G; ++g)
+            if (g < u.nrows && st[1 + g] >= 0) {
+              present |= 1u << g;
+              ++np;
+              e[5 + 4 * sub + g] = st[1 + g] * R + slab_off[g];
+            }
+          uint32_t& d = dirty[static_cast<size_t>(slot) * nsub + sub];
+          const uint32_t zero = ~present & all & d;
+          d = present;
+          flags |= (present << (4 * sub)) | (zero << (8 + 4 * sub));
+          e[3 + sub] = st[0] * C + kci * kc;
+          e[2] = kci * kc;  // a stage never mixes k-chunks when nsub == 2 (nkc == 1)
+        }
+        flags |= np << 16;
+        if (s0 == 0) flags |= RS_F_FIRST;
+        if (s0 + nin >= nitems) flags |= RS_F_LAST;
+        if (nin == 2) flags |= RS_F_TWO;
+        e[0] = static_cast<int32_t>(flags);
+        e[1] = b3d ? u.n0 / 64 : u.n0;
+        p->h_stage_list.insert(p->h_stage_list.end(), e, e + W);
         ++k;
       }
     }
-    if (p->h_stage_list.size() / 8 >= (size_t(1) << 31))
+    if (p->h_stage_list.size() / W >= (size_t(1) << 31))
       return set_error(BSP_ERR_UNSUPPORTED, "schedule too long");
-    p->h_cta_stage_begin.push_back(static_cast<int32_t>(p->h_stage_list.size() / 8));
+    p->h_cta_stage_begin.push_back(static_cast<int32_t>(p->h_stage_list.size() / W));
   }
   return BSP_OK;
 }

@@ -62,9 +62,10 @@ struct RsSmemHeader {
 static_assert(sizeof(RsSmemHeader) <= 1024, "header must fit its 1 KiB slot");
 
 enum : uint32_t {
-  RS_FIRST = 1u << 12,
-  RS_LAST = 1u << 13,
-  RS_EMPTY = 1u << 14,
+  RS_FIRST = static_cast<uint32_t>(RS_F_FIRST),
+  RS_LAST = static_cast<uint32_t>(RS_F_LAST),
+  RS_EMPTY = static_cast<uint32_t>(RS_F_EMPTY),
+  RS_TWO = static_cast<uint32_t>(RS_F_TWO),
 };
 
 __device__ __forceinline__ uint32_t baddr(const uint64_t* b) { return smem_u32(b); }
@@ -77,8 +78,8 @@ __device__ __noinline__ bool rs_drain_wait(uint32_t bar, uint32_t parity, const 
 
 // Producer warp pw (0-based among producers): issues the CTA's pipeline
 // stages pw, pw + nprod, pw + 2*nprod, ... from the precomputed stage list.
-// 32 of its stages are fetched at once (lane l holds the l-th) and broadcast
-// by shuffles, so the issuing lane never waits on global memory per stage.
+// 32 of its stages are fetched at once (lane l holds the l-th, 64 bytes) and
+// broadcast by shuffles, so the issuing lane never waits on global memory.
 __device__ __forceinline__ void rs_producer(const SpmmKernelParams& p, RsSmemHeader* hdr,
                                            uint8_t* gbase, uint32_t base, uint32_t stage0,
                                            const WaitCtl& ctl, int pw, int lane) {
@@ -88,65 +89,83 @@ __device__ __forceinline__ void rs_producer(const SpmmKernelParams& p, RsSmemHea
   const uint32_t a_slot = static_cast<uint32_t>(p.Rs * p.kc * 2);
   const uint32_t b_blk = static_cast<uint32_t>(p.kc * 128);  // one 64-column block
   const uint32_t b_bytes = 4u * b_blk;
+  const uint32_t sub_bytes = static_cast<uint32_t>(p.sub_bytes);
   int stage = pw;
   uint32_t phase = 0;
   uint32_t armed = 0, armed_parity = 0;
   bool ok = true;
 #pragma unroll 1
   for (int k0 = pw; k0 < n && ok; k0 += 32 * P) {
-    int4 w0 = make_int4(0, 0, 0, 0), w1 = make_int4(-1, -1, -1, -1);
+    int4 w0 = make_int4(0, 0, 0, 0), w1 = w0, w2 = w0, w3 = w0;
     const int kl = k0 + lane * P;
     if (kl < n) {
-      const int4* e = p.stage_list + 2 * static_cast<size_t>(k_begin + kl);
+      const int4* e = p.stage_list + 4 * static_cast<size_t>(k_begin + kl);
       w0 = __ldg(e);
       w1 = __ldg(e + 1);
+      w2 = __ldg(e + 2);
+      w3 = __ldg(e + 3);
     }
     const int cnt = min(32, (n - k0 + P - 1) / P);
 #pragma unroll 1
     for (int j = 0; j < cnt; ++j) {
-      const int ky = __shfl_sync(0xffffffffu, w0.x, j);
-      const int bz = __shfl_sync(0xffffffffu, w0.y, j);
-      const int flags = __shfl_sync(0xffffffffu, w0.z, j);
-      const int ax = __shfl_sync(0xffffffffu, w0.w, j);
-      int ay[kRsMaxG];
-      ay[0] = __shfl_sync(0xffffffffu, w1.x, j);
-      ay[1] = __shfl_sync(0xffffffffu, w1.y, j);
-      ay[2] = __shfl_sync(0xffffffffu, w1.z, j);
-      ay[3] = __shfl_sync(0xffffffffu, w1.w, j);
+      const uint32_t flags = static_cast<uint32_t>(__shfl_sync(0xffffffffu, w0.x, j));
       if (lane == 0)
         ok = mbar_wait_bounded(baddr(&hdr->empty[stage]), phase ^ 1u, ctl, ST_TIMEOUT_PRODUCER);
       ok = __shfl_sync(0xffffffffu, ok, 0);
       if (!ok) break;
       const uint32_t sb = stage0 + static_cast<uint32_t>(stage) * p.stage_bytes;
-      const uint32_t zero = (static_cast<uint32_t>(flags) >> 4) & 0xFu;
+      const uint32_t zero = (flags >> 8) & 0xFFu;
       if (zero) {
-        // entries absent from this step whose slot still holds an older block
+        // entry slots absent from their sub-step that still hold an older block
 #pragma unroll 1
         for (uint32_t m = zero; m; m &= m - 1) {
-          const int g = __ffs(m) - 1;
-          uint4* dst = reinterpret_cast<uint4*>(gbase + (sb + b_bytes + g * a_slot - base));
+          const int bit = __ffs(m) - 1;
+          const uint32_t off = sb + (bit >> 2) * sub_bytes + b_bytes + (bit & 3) * a_slot;
+          uint4* dst = reinterpret_cast<uint4*>(gbase + (off - base));
           for (uint32_t i = lane; i < a_slot / 16; i += 32) dst[i] = make_uint4(0, 0, 0, 0);
         }
         fence_proxy_async_smem();
       }
+      // coordinates of this stage (all lanes take part in the shuffles)
+      const int bz = __shfl_sync(0xffffffffu, w0.y, j);
+      const int ax = __shfl_sync(0xffffffffu, w0.z, j);
+      const int ky0 = __shfl_sync(0xffffffffu, w0.w, j);
+      const int ky1 = __shfl_sync(0xffffffffu, w1.x, j);
+      int ay[8];
+      ay[0] = __shfl_sync(0xffffffffu, w1.y, j);
+      ay[1] = __shfl_sync(0xffffffffu, w1.z, j);
+      ay[2] = __shfl_sync(0xffffffffu, w1.w, j);
+      ay[3] = __shfl_sync(0xffffffffu, w2.x, j);
+      ay[4] = __shfl_sync(0xffffffffu, w2.y, j);
+      ay[5] = __shfl_sync(0xffffffffu, w2.z, j);
+      ay[6] = __shfl_sync(0xffffffffu, w2.w, j);
+      ay[7] = __shfl_sync(0xffffffffu, w3.x, j);
       __syncwarp();
       if (lane == 0) {
-        hdr->info[stage] = static_cast<uint32_t>(flags) & (RS_FIRST | RS_LAST | RS_EMPTY);
+        hdr->info[stage] = flags & static_cast<uint32_t>(RS_FIRST | RS_LAST | RS_EMPTY | RS_TWO);
         const uint32_t full = baddr(&hdr->full[stage]);
         if (flags & RS_EMPTY) {
           mbar_arrive(full);
         } else {
-          const uint32_t np = (static_cast<uint32_t>(flags) >> 16) & 7u;
-          mbar_arrive_expect_tx(full, b_bytes + np * a_slot);
-          if (p.b3d) {
-            tma_load_3d(sb, &p.tm_b, 0, ky, bz, full);
-          } else {
+          const uint32_t nsub = (flags & RS_TWO) ? 2u : 1u;
+          const uint32_t np = (flags >> 16) & 0xFu;
+          mbar_arrive_expect_tx(full, nsub * b_bytes + np * a_slot);
 #pragma unroll
-            for (int h = 0; h < 4; ++h) tma_load_2d(sb + h * b_blk, &p.tm_b, bz + h * 64, ky, full);
+          for (uint32_t q = 0; q < 2; ++q) {
+            if (q >= nsub) break;
+            const uint32_t qb = sb + q * sub_bytes;
+            const int ky = q ? ky1 : ky0;
+            if (p.b3d) {
+              tma_load_3d(qb, &p.tm_b, 0, ky, bz, full);
+            } else {
+#pragma unroll
+              for (int h = 0; h < 4; ++h) tma_load_2d(qb + h * b_blk, &p.tm_b, bz + h * 64, ky, full);
+            }
+#pragma unroll
+            for (int g = 0; g < kRsMaxG; ++g)
+              if ((flags >> (4 * q + g)) & 1u)
+                tma_load_2d(qb + b_bytes + g * a_slot, &p.tm_a, ax, ay[4 * q + g], full);
           }
-#pragma unroll
-          for (int g = 0; g < kRsMaxG; ++g)
-            if ((flags >> g) & 1) tma_load_2d(sb + b_bytes + g * a_slot, &p.tm_a, ax, ay[g], full);
         }
         armed |= 1u << stage;
         armed_parity = (armed_parity & ~(1u << stage)) | (phase << stage);
@@ -176,13 +195,15 @@ __device__ __forceinline__ void rs_mma(const SpmmKernelParams& p, RsSmemHeader* 
   uint32_t acc_phase = 0;
   int units_left = u_end - u_begin;
   // A (stacked entries): K-major, rows of kc*2 bytes; B: MN-major 128B swizzle,
-  // LBO = one 64-column block (kc rows x 128 B), SBO = 8 k-rows.
+  // LBO = one 64-column block (kc rows x 128 B), SBO = 8 k-rows; a 16-row
+  // k-step of B is 2048 bytes, a 16-column k-step of A is 32 bytes.
   const uint32_t idesc = idesc_bf16_f32(128, kRsN, /*a K-major*/ 0, /*b MN-major*/ 1);
   const uint32_t b_bytes = static_cast<uint32_t>(4 * p.kc * 128);
   const uint32_t a_sbo = (p.a_swizzle_mode == 2) ? 1024u : 512u;
   const uint64_t adesc0 = smem_desc(stage0 + b_bytes, 16u, a_sbo, static_cast<uint32_t>(p.a_swizzle_mode));
   const uint64_t bdesc0 = smem_desc(stage0, static_cast<uint32_t>(p.kc * 128), 1024u, 2u);
   const uint32_t stage16 = static_cast<uint32_t>(p.stage_bytes) >> 4;
+  const uint32_t sub16 = static_cast<uint32_t>(p.sub_bytes) >> 4;
   const uint32_t full0 = baddr(&hdr->full[0]);
   const uint32_t empty0 = baddr(&hdr->empty[0]);
   uint32_t soff = 0;
@@ -203,6 +224,11 @@ __device__ __forceinline__ void rs_mma(const SpmmKernelParams& p, RsSmemHeader* 
 #pragma unroll
       for (int k = 0; k < kKS; ++k)
         mma_bf16(d0, ad + k * 2u, bd + k * 128u, idesc, (k > 0 || !first) ? 1u : 0u);
+      if (info & RS_TWO) {
+#pragma unroll
+        for (int k = 0; k < kKS; ++k)
+          mma_bf16(d0, ad + sub16 + k * 2u, bd + sub16 + k * 128u, idesc, 1u);
+      }
     }
     mma_commit(empty0 + stage * 8);
     if (info & RS_LAST) {
@@ -360,7 +386,20 @@ bsp_status launch_spmm_rowstack(const bsp_spmm_plan* p, const bsp_bsr_desc* A, c
   if (p->n_units == 0 || p->M == 0 || p->N == 0) return BSP_OK;
   if (reinterpret_cast<uintptr_t>(C) % 16 || (ldc * (f32 ? 4 : 2)) % 16)
     return set_error(BSP_ERR_INVALID_ARG, "C must be 16-byte aligned with 16-byte row pitch");
-  SpmmKernelParams kp;
+  auto kern = f32 ? spmm_rowstack_tcgen05<true> : spmm_rowstack_tcgen05<false>;
+  if (!p->attr_set) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, p->smem_bytes);
+    if (e != cudaSuccess) return cuda_check(e, "cudaFuncSetAttribute(spmm rowstack)");
+    p->attr_set = true;
+  }
+  // Same operands as the previous call: reuse the encoded tensor maps.
+  if (p->kp_valid && p->kp_a == A->values && p->kp_b == B && p->kp_c == C && p->kp_ldb == ldb &&
+      p->kp_ldc == ldc) {
+    kern<<<p->grid, kRsThreads, p->smem_bytes, stream>>>(p->kp);
+    return cuda_check(cudaGetLastError(), "spmm rowstack kernel launch");
+  }
+  SpmmKernelParams& kp = p->kp;
+  p->kp_valid = false;
   memset(&kp, 0, sizeof(kp));
   bsp_status st;
   const CUtensorMapSwizzle a_swz = p->kc == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
@@ -412,9 +451,13 @@ bsp_status launch_spmm_rowstack(const bsp_spmm_plan* p, const bsp_bsr_desc* A, c
   kp.b3d = b3d;
   kp.stage_list = p->d_stage_list;
   kp.cta_stage_begin = p->d_cta_stage_begin;
-  auto kern = f32 ? spmm_rowstack_tcgen05<true> : spmm_rowstack_tcgen05<false>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, p->smem_bytes);
-  if (e != cudaSuccess) return cuda_check(e, "cudaFuncSetAttribute(spmm rowstack)");
+  kp.sub_bytes = p->sub_bytes;
+  p->kp_valid = true;
+  p->kp_a = A->values;
+  p->kp_b = B;
+  p->kp_c = C;
+  p->kp_ldb = ldb;
+  p->kp_ldc = ldc;
   kern<<<p->grid, kRsThreads, p->smem_bytes, stream>>>(kp);
   return cuda_check(cudaGetLastError(), "spmm rowstack kernel launch");
 }

@@ -157,6 +157,16 @@ bsp_status bsp_spmm_host(bsp_device* dev, int64_t M, int64_t K, int32_t R, int32
                          const uint16_t* B, int64_t N, uint16_t* C_out, bsp_strategy strategy,
                          const bsp_spmm_opts* opts);
 
+/* bsp_spmm_host plus timing: after the first launch, `iters` more launches are
+ * timed with CUDA events; *ms_per_launch = their mean device time.  This is the
+ * is_profiling mode of the reference planners (1 + 10 EnqueueProgram calls,
+ * block_spmm/inc/host_code/bsr_spmm_multicore_load_balanced_new_DM.cpp:507-513). */
+bsp_status bsp_spmm_host_profile(bsp_device* dev, int64_t M, int64_t K, int32_t R, int32_t C,
+                                 int64_t nnzb, const int32_t* row_ptr, const int32_t* col_idx,
+                                 const uint16_t* values, const uint16_t* B, int64_t N,
+                                 uint16_t* C_out, bsp_strategy strategy, const bsp_spmm_opts* opts,
+                                 int32_t iters, double* ms_per_launch);
+
 /* ---- SDDMM: out = mask (.) (A[M x K] * B[K x N]) on mask's pattern --------
  * Replaces SDDMMHostCodeFunctionPtr (block_sddmm/inc/host_code.hpp:104-115):
  * out_values[b*R*C + r*C + c] for every mask block b, in mask order; the output
@@ -186,6 +196,15 @@ bsp_status bsp_sddmm_host(bsp_device* dev, int64_t M, int64_t N, int32_t R, int3
                           const uint16_t* mask_values, const uint16_t* A, const uint16_t* B,
                           int64_t K, uint16_t* out_values, bsp_strategy strategy,
                           const bsp_sddmm_opts* opts);
+
+/* bsp_sddmm_host plus timing of `iters` launches (see bsp_spmm_host_profile;
+ * reference: block_sddmm/inc/host_code/bsr_sddmm_multicore_naive.cpp, is_profiling). */
+bsp_status bsp_sddmm_host_profile(bsp_device* dev, int64_t M, int64_t N, int32_t R, int32_t C,
+                                  int64_t nnzb, const int32_t* row_ptr, const int32_t* col_idx,
+                                  const uint16_t* mask_values, const uint16_t* A,
+                                  const uint16_t* B, int64_t K, uint16_t* out_values,
+                                  bsp_strategy strategy, const bsp_sddmm_opts* opts, int32_t iters,
+                                  double* ms_per_launch);
 
 /* ---- multi-GPU helpers (host logic; the exchange itself is NCCL) --------
  * Contiguous block-row ranges for `parts` GPUs balanced by nonzero-block

@@ -19,13 +19,16 @@ extern "C" {
  * filled (use it to size them): units_out[info[0] * 8] (row0, nrows, r_off,
  * n0, nt, step_begin, step_end, row_mask per unit, in CTA order),
  * cta_begin_out[info[1] + 1], steps_out[info[7] * (1 + info[2])]
- * (column, then the block index of each group row or -1). */
+ * (column, then the block index of each group row or -1).  For the
+ * row-stacked kernel (info[11] == 1) stage_list_out[info[13] * 16] and
+ * cta_stage_begin_out[info[1] + 1] receive the per-CTA stage descriptors. */
 bsp_status bsp_spmm_plan_inspect(int64_t M, int64_t K, int32_t R, int32_t C, int64_t nnzb,
                                  const int32_t* row_ptr, const int32_t* col_idx, int64_t N,
                                  bsp_dtype c_type, bsp_strategy strategy,
                                  const bsp_spmm_opts* opts, int32_t sm_count, int32_t max_smem,
                                  int64_t info[16], int32_t* units_out, int32_t* cta_begin_out,
-                                 int32_t* steps_out);
+                                 int32_t* steps_out, int32_t* stage_list_out,
+                                 int32_t* cta_stage_begin_out);
 
 /* units_out[info[0] * 12] (row, r_off, nseg, pad, blk[4], col[4] per unit). */
 bsp_status bsp_sddmm_plan_inspect(int64_t M, int64_t N, int32_t R, int32_t C, int64_t nnzb,

@@ -29,7 +29,8 @@ EXPORTS = [
     "bsp_spmm", "bsp_spmm_host",
     "bsp_sddmm_plan_create", "bsp_sddmm_execute", "bsp_sddmm_plan_destroy",
     "bsp_sddmm_plan_info", "bsp_sddmm", "bsp_sddmm_host",
-    "bsp_partition_rows", "bsp_serpentine_assign",
+    "bsp_partition_rows", "bsp_serpentine_assign", "bsp_spmm_host_profile",
+    "bsp_sddmm_host_profile", "bsp_spmm_plan_inspect", "bsp_sddmm_plan_inspect",
 ]
 
 
@@ -98,6 +99,14 @@ def lib():
                                ctypes.POINTER(Opts)]),
         "bsp_partition_rows": (S, [P, I64, I32, P]),
         "bsp_serpentine_assign": (S, [I64, I32, P, P]),
+        "bsp_spmm_host_profile": (S, [P, I64, I64, I32, I32, I64, P, P, P, P, I64, P, S,
+                                      ctypes.POINTER(Opts), I32, ctypes.POINTER(ctypes.c_double)]),
+        "bsp_sddmm_host_profile": (S, [P, I64, I64, I32, I32, I64, P, P, P, P, P, I64, P, S,
+                                       ctypes.POINTER(Opts), I32, ctypes.POINTER(ctypes.c_double)]),
+        "bsp_spmm_plan_inspect": (S, [I64, I64, I32, I32, I64, P, P, I64, S, S, ctypes.POINTER(Opts),
+                                      I32, I32, P, P, P, P, P, P]),
+        "bsp_sddmm_plan_inspect": (S, [I64, I64, I32, I32, I64, P, P, I64, S, ctypes.POINTER(Opts),
+                                       I32, I32, P, P, P]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -361,6 +370,51 @@ def sddmm_host(M, N, R, C, row_ptr, col_idx, mask_values, A, B, K, strategy=NAIV
 
 
 # ----------------------------------------------------------------- helpers --
+def inspect_spmm_plan(M, K, R, C, row_ptr, col_idx, N, strategy=NAIVE, c_type=BF16, opts=None,
+                      sm_count=148, max_smem=232448):
+    """Run the SpMM planner on the host only (no GPU) and return its schedule."""
+    rp = np.ascontiguousarray(row_ptr, dtype=np.int32)
+    ci = np.ascontiguousarray(col_idx, dtype=np.int32)
+    if ci.size == 0:
+        ci = np.zeros(1, np.int32)
+    info = np.zeros(16, np.int64)
+    o = opts if opts is not None else Opts()
+    args = (M, K, R, C, int(rp[-1]), _ptr(rp), _ptr(ci), N, c_type, strategy, ctypes.byref(o),
+            sm_count, max_smem, _ptr(info))
+    _check(lib().bsp_spmm_plan_inspect(*args, None, None, None, None, None))
+    units = np.zeros((int(info[0]), 8), np.int32)
+    cta = np.zeros(int(info[1]) + 1, np.int32)
+    steps = np.zeros((max(int(info[7]), 1), 1 + int(info[2])), np.int32)
+    stages = np.zeros((max(int(info[13]), 1), 16), np.int32)
+    cta_st = np.zeros(int(info[1]) + 1, np.int32)
+    _check(lib().bsp_spmm_plan_inspect(*args, _ptr(units), _ptr(cta), _ptr(steps), _ptr(stages),
+                                       _ptr(cta_st)))
+    keys = ["units", "ctas", "group_rows", "n_tiles", "slab", "kc", "stages", "steps",
+            "plan_bytes", "smem_bytes", "tmem_cols", "variant", "producers", "stage_list", "nsub"]
+    d = {k: int(info[i]) for i, k in enumerate(keys)}
+    d.update(unit_table=units, cta_begin=cta, step_table=steps[: int(info[7])],
+             stage_table=stages[: int(info[13])], cta_stage_begin=cta_st)
+    return d
+
+
+def inspect_sddmm_plan(M, N, R, C, row_ptr, col_idx, K, strategy=NAIVE, opts=None, sm_count=148,
+                       max_smem=232448):
+    rp = np.ascontiguousarray(row_ptr, dtype=np.int32)
+    ci = np.ascontiguousarray(col_idx, dtype=np.int32)
+    if ci.size == 0:
+        ci = np.zeros(1, np.int32)
+    info = np.zeros(16, np.int64)
+    o = opts if opts is not None else Opts()
+    args = (M, N, R, C, int(rp[-1]), _ptr(rp), _ptr(ci), K, strategy, ctypes.byref(o), sm_count,
+            max_smem, _ptr(info))
+    _check(lib().bsp_sddmm_plan_inspect(*args, None, None))
+    units = np.zeros((int(info[0]), 12), np.int32)
+    cta = np.zeros(int(info[1]) + 1, np.int32)
+    _check(lib().bsp_sddmm_plan_inspect(*args, _ptr(units), _ptr(cta)))
+    return dict(units=int(info[0]), ctas=int(info[1]), slab=int(info[4]), kc=int(info[5]),
+                stages=int(info[6]), unit_table=units, cta_begin=cta)
+
+
 def partition_rows(row_ptr: np.ndarray, parts: int) -> np.ndarray:
     rp = np.ascontiguousarray(row_ptr, dtype=np.int32)
     bounds = np.zeros(parts + 1, dtype=np.int64)

@@ -354,10 +354,41 @@ bsp_status bsp_spmm(bsp_device* dev, const bsp_bsr_desc* A, const void* B, int64
   return s;
 }
 
-bsp_status bsp_spmm_host(bsp_device* dev, int64_t M, int64_t K, int32_t R, int32_t C, int64_t nnzb,
-                         const int32_t* row_ptr, const int32_t* col_idx, const uint16_t* values,
-                         const uint16_t* B, int64_t N, uint16_t* C_out, bsp_strategy strategy,
-                         const bsp_spmm_opts* opts) {
+// Run `iters` timed launches after the first one; mean device ms per launch.
+static bsp_status time_launches(int32_t iters, double* ms_out, cudaStream_t stream,
+                                bsp_status (*launch)(const void*), const void* ctx) {
+  cudaEvent_t e0 = nullptr, e1 = nullptr;
+  bsp_status s = cuda_check(cudaEventCreate(&e0), "cudaEventCreate");
+  if (s == BSP_OK) s = cuda_check(cudaEventCreate(&e1), "cudaEventCreate");
+  if (s == BSP_OK) s = cuda_check(cudaEventRecord(e0, stream), "cudaEventRecord");
+  for (int32_t i = 0; s == BSP_OK && i < iters; ++i) s = launch(ctx);
+  if (s == BSP_OK) s = cuda_check(cudaEventRecord(e1, stream), "cudaEventRecord");
+  if (s == BSP_OK) s = cuda_check(cudaEventSynchronize(e1), "cudaEventSynchronize");
+  float ms = 0.f;
+  if (s == BSP_OK) s = cuda_check(cudaEventElapsedTime(&ms, e0, e1), "cudaEventElapsedTime");
+  if (s == BSP_OK && ms_out) *ms_out = iters > 0 ? ms / iters : 0.0;
+  if (e0) cudaEventDestroy(e0);
+  if (e1) cudaEventDestroy(e1);
+  return s;
+}
+
+struct SpmmLaunchCtx {
+  const bsp_spmm_plan* p;
+  const bsp_bsr_desc* A;
+  const void* B;
+  void* C;
+  int64_t N;
+};
+static bsp_status spmm_launch_ctx(const void* v) {
+  const SpmmLaunchCtx* c = static_cast<const SpmmLaunchCtx*>(v);
+  return bsp_spmm_execute(c->p, c->A, c->B, c->N, c->C, c->N, nullptr);
+}
+
+static bsp_status spmm_host_impl(bsp_device* dev, int64_t M, int64_t K, int32_t R, int32_t C,
+                                 int64_t nnzb, const int32_t* row_ptr, const int32_t* col_idx,
+                                 const uint16_t* values, const uint16_t* B, int64_t N,
+                                 uint16_t* C_out, bsp_strategy strategy, const bsp_spmm_opts* opts,
+                                 int32_t iters, double* ms_out) {
   if (!dev || !row_ptr || !B || !C_out || (nnzb > 0 && (!col_idx || !values)))
     return set_error(BSP_ERR_INVALID_ARG, "null argument");
   if (R <= 0 || C <= 0 || M % R || K % C) return set_error(BSP_ERR_INVALID_ARG, "bad dimensions");
@@ -387,12 +418,34 @@ bsp_status bsp_spmm_host(bsp_device* dev, int64_t M, int64_t K, int32_t R, int32
   s = bsp_spmm_plan_create(dev, &A, row_ptr, col_idx, N, BSP_BF16, strategy, opts, &p);
   if (s != BSP_OK) return s;
   s = bsp_spmm_execute(p, &A, d_B, N, d_C, N, stream);
+  if (s == BSP_OK && iters > 0) {
+    const SpmmLaunchCtx ctx{p, &A, d_B, d_C, N};
+    s = time_launches(iters, ms_out, stream, spmm_launch_ctx, &ctx);
+  }
   if (s == BSP_OK)
     s = cuda_check(cudaMemcpyAsync(C_out, d_C, sizeof(uint16_t) * M * N, cudaMemcpyDeviceToHost, stream), "D2H C");
   if (s == BSP_OK) s = cuda_check(cudaStreamSynchronize(stream), "sync");
   bsp_spmm_plan_destroy(p);
   if (s == BSP_OK) s = bsp_device_synchronize(dev);
   return s;
+}
+
+bsp_status bsp_spmm_host(bsp_device* dev, int64_t M, int64_t K, int32_t R, int32_t C, int64_t nnzb,
+                         const int32_t* row_ptr, const int32_t* col_idx, const uint16_t* values,
+                         const uint16_t* B, int64_t N, uint16_t* C_out, bsp_strategy strategy,
+                         const bsp_spmm_opts* opts) {
+  return spmm_host_impl(dev, M, K, R, C, nnzb, row_ptr, col_idx, values, B, N, C_out, strategy,
+                        opts, 0, nullptr);
+}
+
+bsp_status bsp_spmm_host_profile(bsp_device* dev, int64_t M, int64_t K, int32_t R, int32_t C,
+                                 int64_t nnzb, const int32_t* row_ptr, const int32_t* col_idx,
+                                 const uint16_t* values, const uint16_t* B, int64_t N,
+                                 uint16_t* C_out, bsp_strategy strategy, const bsp_spmm_opts* opts,
+                                 int32_t iters, double* ms_per_launch) {
+  if (iters < 1 || !ms_per_launch) return set_error(BSP_ERR_INVALID_ARG, "iters >= 1 and ms_per_launch required");
+  return spmm_host_impl(dev, M, K, R, C, nnzb, row_ptr, col_idx, values, B, N, C_out, strategy,
+                        opts, iters, ms_per_launch);
 }
 
 // --------------------------------------------------------------- SDDMM ----
@@ -488,11 +541,24 @@ bsp_status bsp_sddmm(bsp_device* dev, const bsp_bsr_desc* mask, const void* A, i
   return s;
 }
 
-bsp_status bsp_sddmm_host(bsp_device* dev, int64_t M, int64_t N, int32_t R, int32_t C,
-                          int64_t nnzb, const int32_t* row_ptr, const int32_t* col_idx,
-                          const uint16_t* mask_values, const uint16_t* A, const uint16_t* B,
-                          int64_t K, uint16_t* out_values, bsp_strategy strategy,
-                          const bsp_sddmm_opts* opts) {
+struct SddmmLaunchCtx {
+  const bsp_sddmm_plan* p;
+  const bsp_bsr_desc* mask;
+  const void* A;
+  const void* B;
+  void* out;
+  int64_t K, N;
+};
+static bsp_status sddmm_launch_ctx(const void* v) {
+  const SddmmLaunchCtx* c = static_cast<const SddmmLaunchCtx*>(v);
+  return bsp_sddmm_execute(c->p, c->mask, c->A, c->K, c->B, c->N, c->out, nullptr);
+}
+
+static bsp_status sddmm_host_impl(bsp_device* dev, int64_t M, int64_t N, int32_t R, int32_t C,
+                                  int64_t nnzb, const int32_t* row_ptr, const int32_t* col_idx,
+                                  const uint16_t* mask_values, const uint16_t* A, const uint16_t* B,
+                                  int64_t K, uint16_t* out_values, bsp_strategy strategy,
+                                  const bsp_sddmm_opts* opts, int32_t iters, double* ms_out) {
   if (!dev || !row_ptr || !A || !B || (nnzb > 0 && (!col_idx || !out_values)))
     return set_error(BSP_ERR_INVALID_ARG, "null argument");
   if (R <= 0 || C <= 0 || M % R || N % C) return set_error(BSP_ERR_INVALID_ARG, "bad dimensions");
@@ -528,12 +594,36 @@ bsp_status bsp_sddmm_host(bsp_device* dev, int64_t M, int64_t N, int32_t R, int3
   s = bsp_sddmm_plan_create(dev, &mask, row_ptr, col_idx, K, strategy, opts, &p);
   if (s != BSP_OK) return s;
   s = bsp_sddmm_execute(p, &mask, d_A, K, d_B, N, d_out, stream);
+  if (s == BSP_OK && iters > 0) {
+    const SddmmLaunchCtx ctx{p, &mask, d_A, d_B, d_out, K, N};
+    s = time_launches(iters, ms_out, stream, sddmm_launch_ctx, &ctx);
+  }
   if (s == BSP_OK && nnzb > 0)
     s = cuda_check(cudaMemcpyAsync(out_values, d_out, blk, cudaMemcpyDeviceToHost, stream), "D2H out");
   if (s == BSP_OK) s = cuda_check(cudaStreamSynchronize(stream), "sync");
   bsp_sddmm_plan_destroy(p);
   if (s == BSP_OK) s = bsp_device_synchronize(dev);
   return s;
+}
+
+bsp_status bsp_sddmm_host(bsp_device* dev, int64_t M, int64_t N, int32_t R, int32_t C,
+                          int64_t nnzb, const int32_t* row_ptr, const int32_t* col_idx,
+                          const uint16_t* mask_values, const uint16_t* A, const uint16_t* B,
+                          int64_t K, uint16_t* out_values, bsp_strategy strategy,
+                          const bsp_sddmm_opts* opts) {
+  return sddmm_host_impl(dev, M, N, R, C, nnzb, row_ptr, col_idx, mask_values, A, B, K,
+                         out_values, strategy, opts, 0, nullptr);
+}
+
+bsp_status bsp_sddmm_host_profile(bsp_device* dev, int64_t M, int64_t N, int32_t R, int32_t C,
+                                  int64_t nnzb, const int32_t* row_ptr, const int32_t* col_idx,
+                                  const uint16_t* mask_values, const uint16_t* A,
+                                  const uint16_t* B, int64_t K, uint16_t* out_values,
+                                  bsp_strategy strategy, const bsp_sddmm_opts* opts, int32_t iters,
+                                  double* ms_per_launch) {
+  if (iters < 1 || !ms_per_launch) return set_error(BSP_ERR_INVALID_ARG, "iters >= 1 and ms_per_launch required");
+  return sddmm_host_impl(dev, M, N, R, C, nnzb, row_ptr, col_idx, mask_values, A, B, K,
+                         out_values, strategy, opts, iters, ms_per_launch);
 }
 
 // ----------------------------------------------------------- helpers ----
@@ -583,7 +673,8 @@ bsp_status bsp_spmm_plan_inspect(int64_t M, int64_t K, int32_t R, int32_t C, int
                                  bsp_dtype c_type, bsp_strategy strategy,
                                  const bsp_spmm_opts* opts, int32_t sm_count, int32_t max_smem,
                                  int64_t info[16], int32_t* units_out, int32_t* cta_begin_out,
-                                 int32_t* steps_out) {
+                                 int32_t* steps_out, int32_t* stage_list_out,
+                                 int32_t* cta_stage_begin_out) {
   if (!row_ptr || !info || (nnzb > 0 && !col_idx) || R <= 0 || C <= 0)
     return set_error(BSP_ERR_INVALID_ARG, "bad arguments");
   bsp_spmm_plan p;
@@ -602,6 +693,12 @@ bsp_status bsp_spmm_plan_inspect(int64_t M, int64_t K, int32_t R, int32_t C, int
   if (cta_begin_out)
     memcpy(cta_begin_out, p.h_cta_begin.data(), p.h_cta_begin.size() * sizeof(int32_t));
   if (steps_out) memcpy(steps_out, p.h_steps.data(), p.n_steps * (1 + p.G) * sizeof(int32_t));
+  info[13] = static_cast<int64_t>(p.h_stage_list.size() / kRsStageWords);
+  info[14] = p.nsub;
+  if (stage_list_out && !p.h_stage_list.empty())
+    memcpy(stage_list_out, p.h_stage_list.data(), p.h_stage_list.size() * sizeof(int32_t));
+  if (cta_stage_begin_out && !p.h_cta_stage_begin.empty())
+    memcpy(cta_stage_begin_out, p.h_cta_stage_begin.data(), p.h_cta_stage_begin.size() * sizeof(int32_t));
   return BSP_OK;
 }
 

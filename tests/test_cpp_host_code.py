@@ -1,0 +1,34 @@
+"""The reference-named C++ host-code API (include/bsp/host_code.hpp) compiled
+into a driver that mirrors the reference's own test drivers."""
+import os
+import subprocess
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+PKG = os.path.join(ROOT, "tenstorrent-wh-blockspmm_b200")
+ORACLE = os.path.join(ROOT, "oracle")
+
+
+def _build(tmp_path):
+    exe = str(tmp_path / "test_host_code")
+    cmd = ["g++", "-std=c++17", "-O2", "-Wall", "-Werror", f"-I{ROOT}/include", f"-I{ORACLE}",
+           os.path.join(ROOT, "tests", "cpp", "test_host_code.cpp"), f"-L{PKG}", "-lbsp",
+           f"-L{ORACLE}", "-loracle", f"-Wl,-rpath,{PKG}", f"-Wl,-rpath,{ORACLE}", "-o", exe]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    return exe
+
+
+def test_host_code_header_compiles(tmp_path):
+    _build(tmp_path)
+
+
+@pytest.mark.gpu
+def test_host_code_registries_on_gpu(tmp_path):
+    exe = _build(tmp_path)
+    r = subprocess.run([exe], capture_output=True, text=True, timeout=600)
+    print(r.stdout)
+    assert r.returncode == 0, r.stdout + r.stderr
+    assert "FAIL" not in r.stdout
+    assert r.stdout.count("PASS") >= 6 * 6 + 10 * 2

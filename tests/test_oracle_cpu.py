@@ -1,0 +1,94 @@
+"""The oracle (my restatement of the reference golden) pinned three ways:
+bit-exact against the committed fixtures made by the reference's own golden
+(tests/golden/make_golden.py), bit-exact against that golden live when
+oracle/_ref was built here, and against closed-form known answers of the
+reference's own tests."""
+import glob
+import os
+
+import numpy as np
+import pytest
+
+import oracle
+
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+FIXTURES = sorted(glob.glob(os.path.join(GOLDEN, "*.npz")))
+
+
+def test_fixtures_present():
+    names = {os.path.basename(f)[:-4] for f in FIXTURES}
+    assert {"spmm_config1", "spmm_1_block_id", "sddmm_identity_mask_R32", "sddmm_random_p15"} <= names
+    assert len(FIXTURES) >= 20
+
+
+@pytest.mark.parametrize("path", FIXTURES, ids=[os.path.basename(f)[:-4] for f in FIXTURES])
+def test_oracle_reproduces_reference_fixture(path):
+    z = np.load(path)
+    H, W, R, C = (int(z[k]) for k in ("H", "W", "R", "C"))
+    ip, ix = z["indptr"], z["indices"]
+    if str(z["kind"]) == "spmm":
+        N = int(z["N"])
+        out = oracle.spmm_bf16(ip, ix, z["values"], H, W, R, C, z["B"], N, threads=2)
+        assert np.array_equal(out, z["out"])
+        f = oracle.spmm_f32(ip, ix, oracle.bf16_to_f32(z["values"]), H, W, R, C,
+                            oracle.bf16_to_f32(z["B"]), N)
+        assert np.array_equal(f, z["out_f32"])
+    else:
+        K = int(z["K"])
+        out = oracle.sddmm_bf16(ip, ix, z["mask"], H, W, R, C, z["A"], z["B"], K, threads=2)
+        assert np.array_equal(out, z["out"])
+        f = oracle.sddmm_f32(ip, ix, oracle.bf16_to_f32(z["mask"]), H, W, R, C,
+                             oracle.bf16_to_f32(z["A"]), oracle.bf16_to_f32(z["B"]), K)
+        assert np.array_equal(f, z["out_f32"])
+
+
+def test_known_answers():
+    """Closed forms of block_spmm/inc/test_suite.hpp test_1_block_* (32x32)."""
+    z = np.load(os.path.join(GOLDEN, "spmm_1_block_id.npz"))
+    assert np.array_equal(oracle.bf16_to_f32(z["out"]).reshape(32, 32), np.eye(32, dtype=np.float32))
+    z = np.load(os.path.join(GOLDEN, "spmm_1_block_uniform.npz"))
+    assert np.all(oracle.bf16_to_f32(z["out"]) == 32.0)
+    z = np.load(os.path.join(GOLDEN, "spmm_1_block_arange.npz"))
+    a = oracle.bf16_to_f32(z["values"]).reshape(32, 32).astype(np.float64)
+    expect = np.repeat(a.sum(1, keepdims=True), 32, axis=1)
+    got = oracle.bf16_to_f32(z["out"]).reshape(32, 32)
+    assert np.allclose(got, expect, rtol=2 ** -7)
+    # SDDMM identity mask: each output block is diag(A B) on that block
+    z = np.load(os.path.join(GOLDEN, "sddmm_identity_mask_R32.npz"))
+    A = oracle.bf16_to_f32(z["A"]).astype(np.float64)
+    B = oracle.bf16_to_f32(z["B"]).astype(np.float64)
+    full = A @ B
+    out = oracle.bf16_to_f32(z["out"]).reshape(-1, 32, 32)
+    for b in range(out.shape[0]):
+        d = np.diag(np.diag(full[b * 32:(b + 1) * 32, b * 32:(b + 1) * 32]))
+        assert np.allclose(out[b], d, rtol=2 ** -7, atol=0)
+
+
+@pytest.mark.skipif(not oracle.ref_available(), reason="reference golden not built here")
+@pytest.mark.parametrize("R,C,N,p", [(32, 32, 256, 0.1), (64, 32, 96, 0.3), (32, 64, 40, 0.5), (96, 64, 64, 0.4)])
+def test_oracle_matches_reference_golden_live(R, C, N, p):
+    rng = np.random.default_rng(R * C + N)
+    H, W = 8 * R, 8 * C
+    occ = rng.random((H // R, W // C)) < p
+    ip = np.concatenate([[0], np.cumsum(occ.sum(1))]).astype(np.int32)
+    ix = np.nonzero(occ)[1].astype(np.int32)
+    vals = oracle.f32_to_bf16(rng.uniform(-1, 1, ix.size * R * C).astype(np.float32))
+    B = oracle.f32_to_bf16(rng.uniform(-1, 1, (W, N)).astype(np.float32))
+    assert np.array_equal(oracle.spmm_bf16(ip, ix, vals, H, W, R, C, B, N),
+                          oracle.ref_spmm_bf16(ip, ix, vals, H, W, R, C, B, N))
+    K = 64
+    A = oracle.f32_to_bf16(rng.normal(0, 1, (H, K)).astype(np.float32))
+    Bs = oracle.f32_to_bf16(rng.normal(0, 1, (K, W)).astype(np.float32))
+    g, oip, oix = oracle.ref_sddmm_bf16(ip, ix, vals, H, W, R, C, A, Bs, K)
+    assert np.array_equal(oracle.sddmm_bf16(ip, ix, vals, H, W, R, C, A, Bs, K), g)
+    assert np.array_equal(oip, ip) and np.array_equal(oix, ix)
+
+
+def test_bf16_rounding_is_nearest_even():
+    x = np.array([1.0, 1.0 + 2 ** -8, 1.0 + 3 * 2 ** -8, -2.5, np.inf, 3.0e38], np.float32)
+    b = oracle.f32_to_bf16(x)
+    assert oracle.bf16_to_f32(b)[0] == 1.0
+    assert oracle.bf16_to_f32(b)[1] == 1.0           # tie to even
+    assert oracle.bf16_to_f32(b)[2] == 1.0 + 2 ** -6  # tie to even (up)
+    assert oracle.bf16_to_f32(b)[3] == -2.5
+    assert np.isinf(oracle.bf16_to_f32(b)[4])

@@ -1,0 +1,161 @@
+"""Planner invariants, checked on the CPU through the host-only inspect hook:
+every output tile is produced by exactly one work unit, every block is
+multiplied exactly once per tile, CTA lists partition the units, and the
+row-stacked kernel's precomputed stage list (TMA coordinates, zero masks,
+unit flags) is consistent with the schedule."""
+import numpy as np
+import pytest
+
+import bsp
+from helpers import rand_bsr
+
+STRATS = [("naive", {}), ("snf", {}), ("dda", {}), ("dda", dict(steps_per_stage=2)),
+          ("dda", dict(group_mma=2)), ("dda", dict(group_mma=3)), ("snf", dict(no_load_balance=1)),
+          ("dda", dict(no_load_balance=1, producers=2))]
+
+SHAPES = [(1024, 1024, 256, 32, 32, 0.1), (512, 768, 200, 32, 32, 0.3), (512, 512, 384, 64, 64, 0.4),
+          (768, 512, 128, 96, 32, 0.5), (1024, 512, 64, 512, 64, 0.5), (256, 256, 8, 32, 32, 0.0),
+          (4096, 4096, 4096, 32, 32, 0.05)]
+
+
+def _row_blocks(rp, i):
+    return list(range(int(rp[i]), int(rp[i + 1])))
+
+
+@pytest.mark.parametrize("shape", SHAPES, ids=[f"{s[0]}x{s[1]}x{s[2]}R{s[3]}C{s[4]}p{s[5]}" for s in SHAPES])
+@pytest.mark.parametrize("strategy,opts", STRATS, ids=[f"{s}{o}" for s, o in STRATS])
+def test_spmm_schedule_covers_work_exactly_once(shape, strategy, opts):
+    M, K, N, R, C, p = shape
+    rng = np.random.default_rng(int(M + K + N + R + 1000 * p))
+    rp, ci, _ = rand_bsr(rng, M, K, R, C, p)
+    plan = bsp.inspect_spmm_plan(M, K, R, C, rp, ci, N, bsp.STRATEGIES[strategy],
+                                 opts=bsp.make_opts(**opts))
+    units, cta, steps = plan["unit_table"], plan["cta_begin"], plan["step_table"]
+    assert cta[0] == 0 and cta[-1] == len(units) and np.all(np.diff(cta) >= 0)
+    assert plan["ctas"] <= 148 and plan["stages"] >= 2
+    G = plan["group_rows"]
+    nbr = M // R
+    if plan["variant"] == 1:
+        Rs = plan["slab"]
+        slabs = R // Rs
+        assert G * Rs == 128
+        covered = {}
+        for u in units:
+            row0, nent, _, n0, nt, sb, se, mask = (int(x) for x in u)
+            assert n0 % 256 == 0 and nt == 1
+            blocks = {g: [] for g in range(G)}
+            for s in range(sb, se):
+                for g in range(G):
+                    b = steps[s, 1 + g]
+                    if b >= 0:
+                        blocks[g].append(int(b))
+                        assert ci[b] == steps[s, 0]
+            for g in range(nent):
+                e = row0 + g
+                covered[(e, n0)] = covered.get((e, n0), 0) + 1
+                assert sorted(blocks[g]) == _row_blocks(rp, e // slabs)
+                assert bool((mask >> g) & 1) == (rp[e // slabs + 1] > rp[e // slabs])
+        assert len(covered) == nbr * slabs * ((N + 255) // 256)
+        assert all(v == 1 for v in covered.values())
+        _check_stage_list(plan, rp, ci, R, C, Rs, slabs, G)
+    else:
+        Rs = plan["slab"]
+        covered = {}
+        for u in units:
+            row0, nrows, r_off, n0, nt, sb, se, mask = (int(x) for x in u)
+            blocks = {g: [] for g in range(G)}
+            for s in range(sb, se):
+                for g in range(G):
+                    b = steps[s, 1 + g]
+                    if b >= 0:
+                        blocks[g].append(int(b))
+                        assert ci[b] == steps[s, 0]
+            for g in range(nrows):
+                assert sorted(blocks[g]) == _row_blocks(rp, row0 + g)
+                for t in range(nt):
+                    key = (row0 + g, r_off, n0 + 128 * t)
+                    covered[key] = covered.get(key, 0) + 1
+        assert len(covered) == nbr * (R // Rs) * ((N + 127) // 128)
+        assert all(v == 1 for v in covered.values())
+
+
+def _check_stage_list(plan, rp, ci, R, C, Rs, slabs, G):
+    """Replay each CTA's stage list against the units it runs."""
+    units, cta, st, cst = plan["unit_table"], plan["cta_begin"], plan["stage_table"], plan["cta_stage_begin"]
+    S, kc = plan["stages"], plan["kc"]
+    nkc = C // kc
+    FIRST, LAST, EMPTY, TWO = 1 << 24, 1 << 25, 1 << 26, 1 << 27
+    for c in range(plan["ctas"]):
+        rows = st[cst[c]:cst[c + 1]]
+        state = np.full((S, 2), (1 << G) - 1, dtype=np.int64)  # slot contents unknown at start
+        k = 0
+        for ui in range(cta[c], cta[c + 1]):
+            row0, nent, _, n0, _, sb, se, _ = (int(x) for x in units[ui])
+            items = [(j, kci) for j in range(sb, se) for kci in range(nkc)]
+            if not items:
+                assert rows[k, 0] & (FIRST | LAST | EMPTY) == FIRST | LAST | EMPTY
+                k += 1
+                continue
+            i = 0
+            first = True
+            while i < len(items):
+                f = int(rows[k, 0])
+                nsub = 2 if f & TWO else 1
+                assert bool(f & FIRST) == first and not f & EMPTY
+                first = False
+                np_total = 0
+                for q in range(nsub):
+                    j, kci = items[i + q]
+                    present = (f >> (4 * q)) & 0xF
+                    zero = (f >> (8 + 4 * q)) & 0xF
+                    for g in range(G):
+                        b = plan["step_table"][j, 1 + g]
+                        has = g < nent and b >= 0
+                        assert bool((present >> g) & 1) == has
+                        if has:
+                            np_total += 1
+                            assert rows[k, 5 + 4 * q + g] == b * R + ((row0 + g) % slabs) * Rs
+                            assert plan["step_table"][j, 0] * C + kci * kc == rows[k, 3 + q]
+                    # every absent slot must be zero when the MMA reads it
+                    slot = k % S
+                    stale = state[slot, q] & ~present & ((1 << G) - 1)
+                    assert stale & ~zero == 0
+                    state[slot, q] = present
+                assert (f >> 16) & 0xF == np_total
+                i += nsub
+                assert bool(f & LAST) == (i >= len(items))
+                k += 1
+        assert k == len(rows)
+
+
+@pytest.mark.parametrize("strategy", ["naive", "dda"])
+@pytest.mark.parametrize("R,C,K", [(32, 32, 256), (64, 32, 96), (32, 96, 64), (512, 64, 128)])
+def test_sddmm_schedule_covers_every_segment_once(strategy, R, C, K):
+    M, N = 4 * max(R, 128), 8 * C
+    rng = np.random.default_rng(R * 7 + C)
+    rp, ci, _ = rand_bsr(rng, M, N, R, C, 0.4)
+    plan = bsp.inspect_sddmm_plan(M, N, R, C, rp, ci, K, bsp.STRATEGIES[strategy])
+    seen = {}
+    Rs = plan["slab"]
+    for u in plan["unit_table"]:
+        row, r_off, nseg = int(u[0]), int(u[1]), int(u[2])
+        assert 1 <= nseg <= 4
+        for q in range(nseg):
+            b, col = int(u[4 + q]), int(u[8 + q])
+            assert rp[row] <= b < rp[row + 1]
+            assert col // C == ci[b] and col % 32 == 0
+            key = (b, col % C, r_off)
+            seen[key] = seen.get(key, 0) + 1
+    assert len(seen) == int(rp[-1]) * (C // 32) * (R // Rs)
+    assert all(v == 1 for v in seen.values())
+
+
+def test_planner_rejects_bad_shapes():
+    rp = np.zeros(9, np.int32)
+    with pytest.raises(bsp.BspError):
+        bsp.inspect_spmm_plan(256, 256, 48, 32, np.zeros(256 // 48 + 1, np.int32), [], 128)
+    with pytest.raises(bsp.BspError):
+        bsp.inspect_spmm_plan(256, 256, 32, 32, rp, [], 100)  # N % 8
+    bad = np.array([0, 2, 1, 1, 1, 1, 1, 1, 1], np.int32)  # decreasing row_ptr
+    with pytest.raises(bsp.BspError):
+        bsp.inspect_spmm_plan(256, 256, 32, 32, bad, [0, 1], 128)

@@ -167,6 +167,33 @@ bsp_status bsp_spmm_host_profile(bsp_device* dev, int64_t M, int64_t K, int32_t 
                                  uint16_t* C_out, bsp_strategy strategy, const bsp_spmm_opts* opts,
                                  int32_t iters, double* ms_per_launch);
 
+/* SpMM that allocates no device memory.  No counterpart in the reference.
+ *
+ * For callers that cannot call cudaMalloc: code whose device memory is owned
+ * up front by another allocator (a framework's caching allocator, a fixed
+ * memory pool) or a process with a fixed memory budget.  It runs the same
+ * Naive / SnF kernel as bsp_spmm_execute, but its scratch -- the work schedule
+ * and the status word -- lives in a 4 MiB array inside libbsp.so's device
+ * image, which every GPU that loads the library holds until the process exits.
+ * The caller passes A (device arrays plus host copies of its pattern), B and C.
+ *   - Schedules larger than the array (very large or very sparse-row-heavy
+ *     patterns) are refused with BSP_ERR_UNSUPPORTED and a message.
+ *   - All calls share the array; the previous call's contents stay in it, and
+ *     each call rewrites the schedule and clears the status word.  Calls that
+ *     overlap on the GPU (other streams or host threads on the same device)
+ *     race on it.
+ *   - The first call on a device looks up the array's device address
+ *     (cudaGetSymbolAddress) with that device current; make that first call
+ *     before any stream capture.
+ *   - The call is synchronous: it returns after the kernel has finished, and
+ *     reports kernel wait timeouts as BSP_ERR_TIMEOUT.
+ * strategy must be BSP_NAIVE or BSP_SNF.  The device is the current CUDA
+ * device; no bsp_device is needed. */
+bsp_status bsp_spmm_noalloc(const bsp_bsr_desc* A, const int32_t* host_row_ptr,
+                            const int32_t* host_col_idx, const void* B, int64_t ldb, void* C,
+                            int64_t ldc, int64_t N, bsp_dtype c_type, bsp_strategy strategy,
+                            void* stream);
+
 /* ---- SDDMM: out = mask (.) (A[M x K] * B[K x N]) on mask's pattern --------
  * Replaces SDDMMHostCodeFunctionPtr (block_sddmm/inc/host_code.hpp:104-115):
  * out_values[b*R*C + r*C + c] for every mask block b, in mask order; the output

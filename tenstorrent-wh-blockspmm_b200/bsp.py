@@ -31,6 +31,7 @@ EXPORTS = [
     "bsp_sddmm_plan_info", "bsp_sddmm", "bsp_sddmm_host",
     "bsp_partition_rows", "bsp_serpentine_assign", "bsp_spmm_host_profile",
     "bsp_sddmm_host_profile", "bsp_spmm_plan_inspect", "bsp_sddmm_plan_inspect",
+    "bsp_spmm_noalloc",
 ]
 
 
@@ -105,6 +106,7 @@ def lib():
                                        ctypes.POINTER(Opts), I32, ctypes.POINTER(ctypes.c_double)]),
         "bsp_spmm_plan_inspect": (S, [I64, I64, I32, I32, I64, P, P, I64, S, S, ctypes.POINTER(Opts),
                                       I32, I32, P, P, P, P, P, P]),
+        "bsp_spmm_noalloc": (S, [ctypes.POINTER(BsrDesc), P, P, P, I64, P, I64, I64, S, S, P]),
         "bsp_sddmm_plan_inspect": (S, [I64, I64, I32, I32, I64, P, P, I64, S, ctypes.POINTER(Opts),
                                        I32, I32, P, P, P]),
     }

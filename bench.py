@@ -42,6 +42,9 @@ for _p in (ROOT, PKG):
 METRIC = "effective TFLOP/s (nnz blocks only), BSR SpMM density sweep"
 DENSITIES = [0.01, 0.05, 0.10, 0.25, 0.50]
 L2_FLUSH_BYTES = 256 << 20
+REF_TOTAL_BUDGET_S = 150.0
+WORKLOAD_SWEEP = ("BASELINE config 2: BSR SpMM 4096x4096x4096, 32x32 blocks, "
+                  "p in {0.01,0.05,0.10,0.25,0.50}")
 
 
 def f32_to_bf16(x: np.ndarray) -> np.ndarray:
@@ -192,33 +195,48 @@ def barrier(dist):
 
 
 # ------------------------------------------------------------ CPU baseline --
-def cpu_reference_time(cases, budget_s=12.0, threads=None):
-    """Time the reference golden (oracle/_ref) or, if absent, the oracle
-    restatement, on a bounded block-row sample of each case.  Returns
-    (flops_done, seconds, kind, cores, sample_description)."""
+def cpu_calibrate(cases, budget_s=12.0, threads=None):
+    """Pick, per case, how many leading block-rows the CPU golden can finish
+    in about budget_s / len(cases) seconds.  Returns (rows per case, kind)."""
     import oracle
 
     threads = threads or os.cpu_count() or 1
     kind = "reference" if oracle.ref_available() else "port"
-    # calibrate on a small slice of the densest case
-    per_case_budget = budget_s / len(cases)
-    total_f = total_t = 0.0
-    samples = []
+    per_case = budget_s / len(cases)
+    rows_out = []
     for c in cases:
         nbr = c["M"] // c["R"]
-        rows = max(threads, 1)
-        rows = min(rows, nbr)
+        rows = min(max(threads, 1), nbr)
         for _ in range(8):
             t = _cpu_time(c, rows, threads, kind)
-            if t >= per_case_budget / 4 or rows >= nbr:
+            if t >= per_case / 2 or rows >= nbr:
                 break
-            rows = min(nbr, int(rows * max(2.0, per_case_budget / 4 / max(t, 1e-4))))
-        t = _cpu_time(c, rows, threads, kind)
-        f = 2.0 * int(c["rp"][rows]) * c["R"] * c["C"] * c["N"]
-        total_f += f
-        total_t += t
-        samples.append(f"p={c['p']}: {rows}/{nbr} block-rows")
-    return total_f, total_t, kind, threads, "; ".join(samples)
+            rows = min(nbr, int(rows * min(16.0, max(1.5, per_case / max(t, 1e-4)))))
+        rows_out.append(rows)
+    return rows_out, kind
+
+
+def cpu_sample_time(cases, rows, kind, threads=None):
+    """Time the calibrated block-row sample of every case once.
+    Returns (effective flops done, seconds, sample description)."""
+    threads = threads or os.cpu_count() or 1
+    total_f = total_t = 0.0
+    samples = []
+    for c, r in zip(cases, rows):
+        total_t += _cpu_time(c, r, threads, kind)
+        total_f += 2.0 * int(c["rp"][r]) * c["R"] * c["C"] * c["N"]
+        samples.append(f"p={c['p']}: {r}/{c['M'] // c['R']} block-rows")
+    return total_f, total_t, "; ".join(samples)
+
+
+def cpu_reference_time(cases, budget_s=12.0, threads=None):
+    """Time the reference golden (oracle/_ref) or, if absent, the oracle
+    restatement, on a bounded block-row sample of each case.  Returns
+    (flops_done, seconds, kind, cores, sample_description)."""
+    threads = threads or os.cpu_count() or 1
+    rows, kind = cpu_calibrate(cases, budget_s, threads)
+    f, t, sample = cpu_sample_time(cases, rows, kind, threads)
+    return f, t, kind, threads, sample
 
 
 def _cpu_time(c, rows, threads, kind):
@@ -311,7 +329,8 @@ def run_bsp(args):
                 "unit": "GB/s", "frac": dom["gbs"] / peaks["hbm_gbs"]}
     roof["traffic"] = traffic_for(dom["p"], dom_run["bytes"])
     roof["peak_src"] = peaks["src"]
-    roof["kernel"] = f"spmm_bsr_tcgen05 p={dom['p']}"
+    variant = dom["plan"].get("variant", 0)
+    roof["kernel"] = f"{'spmm_rowstack_tcgen05' if variant == 1 else 'spmm_bsr_tcgen05'} p={dom['p']}"
     roof["algorithmic"] = dom_run["bytes"] if dom["bound"] == "hbm" else dom_run["flops"]
 
     # ---- e2e through the host-buffer C ABI (pinned host memory) ----
@@ -329,8 +348,7 @@ def run_bsp(args):
         "warmup": args.warmup, "ms_per_step": t_all / args.steps * 1e3, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded numpy: Bernoulli block occupancy, uniform[-1,1] values)",
-        "config": {"workload": "BASELINE config 2: BSR SpMM 4096x4096x4096, 32x32 blocks, "
-                               "p in {0.01,0.05,0.10,0.25,0.50}", "strategy": args.strategy,
+        "config": {"workload": WORKLOAD_SWEEP, "strategy": args.strategy,
                    "c_dtype": "bf16", "accumulate": "fp32",
                    "l2": "flushed (256 MiB write) before every timed launch",
                    "per_rank": "independent copy of the sweep per rank" if ws > 1 else None},
@@ -402,19 +420,22 @@ def traffic_for(p, algorithmic_bytes):
 
 # --------------------------------------------------------- reference arm --
 def run_reference(args):
+    """The reference arm: the reference's CPU golden on this box's host cores.
+    The whole run (calibration, warm-up and timed steps) is held to about
+    REF_TOTAL_BUDGET_S seconds by shrinking each step's block-row sample."""
     ws, rank, local = dist_env()
     if rank != 0:
         return
     cases = sweep_cases(0)
     threads = os.cpu_count() or 1
-    budget = max(2.0, min(args.cpu_budget, 12.0))
-    vals = []
-    kind = cores = sample = None
+    per_step = max(0.25, min(args.cpu_budget, REF_TOTAL_BUDGET_S / (args.steps + args.warmup + 2)))
+    rows, kind = cpu_calibrate(cases, budget_s=per_step, threads=threads)
+    sample = ""
     for _ in range(args.warmup):
-        cpu_reference_time(cases, budget_s=budget / 4, threads=threads)
+        cpu_sample_time(cases, rows, kind, threads)
     tot_f = tot_t = 0.0
     for _ in range(args.steps):
-        f, t, kind, cores, sample = cpu_reference_time(cases, budget_s=budget, threads=threads)
+        f, t, sample = cpu_sample_time(cases, rows, kind, threads)
         tot_f += f
         tot_t += t
     v = tot_f / tot_t / 1e12
@@ -422,10 +443,9 @@ def run_reference(args):
            "steps": args.steps, "warmup": args.warmup,
            "ms_per_step": tot_t / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-           "config": {"workload": "BASELINE config 2: BSR SpMM 4096x4096x4096, 32x32 blocks, "
-                                  "p in {0.01,0.05,0.10,0.25,0.50}", "strategy": "cpu golden"},
-           "cpu_baseline": {"value": v, "unit": "TFLOP/s", "cores": cores, "kind": kind,
-                            "sample": sample + " of each density"},
+           "config": {"workload": WORKLOAD_SWEEP, "strategy": "cpu golden"},
+           "cpu_baseline": {"value": v, "unit": "TFLOP/s", "cores": threads, "kind": kind,
+                            "sample": sample + " of each density, every step"},
            "e2e": {"value": v, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(out), flush=True)
 

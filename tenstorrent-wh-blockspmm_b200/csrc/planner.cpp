@@ -370,12 +370,12 @@ bsp_status plan_spmm_rowstack(bsp_spmm_plan* p, const int32_t* row_ptr, const in
   }
   p->n_units = static_cast<int64_t>(units.size());
   p->grid = grid;
-  // With 32-wide blocks a step is only two MMAs; a stage then carries two
-  // consecutive steps so that each barrier round trip moves four MMAs.
-  // One block-column per stage keeps the ring deepest, which measured faster
-  // than two per stage on B200; two remain available for 32-wide blocks.
+  // With 32-wide blocks a step is only two MMAs, and one full/empty barrier
+  // hand-off per stage costs about as long as two MMAs take.  A stage then
+  // carries two consecutive steps so that each hand-off moves four MMAs:
+  // on B200 that beats the deeper one-step ring at every density from 5%.
   int nsub = 1;
-  if (o.steps_per_stage == 2 && nkc == 1) nsub = 2;
+  if (nkc == 1 && o.steps_per_stage != 1) nsub = 2;
   const int sub_bytes = 4 * kc * 128 + G * Rs * kc * 2;
   p->sub_bytes = sub_bytes;
   p->nsub = nsub;

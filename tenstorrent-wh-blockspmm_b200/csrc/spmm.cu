@@ -154,10 +154,8 @@ __device__ __forceinline__ void spmm_producer(const SpmmKernelParams& p, SpmmSme
 #pragma unroll 1
         for (int kci = 0; kci < p.nkc; ++kci) {
           if (rr == pw) {
-            if (lane == 0)
-              ok = mbar_wait_bounded(bar_addr(&hdr->empty[stage]), phase ^ 1u, ctl,
-                                     ST_TIMEOUT_PRODUCER);
-            ok = __shfl_sync(0xffffffffu, ok, 0);
+            ok = __all_sync(0xffffffffu, mbar_wait_bounded(bar_addr(&hdr->empty[stage]), phase ^ 1u, ctl,
+                                                           ST_TIMEOUT_PRODUCER));
             if (!ok) break;
             const uint32_t sb = stage0 + static_cast<uint32_t>(stage) * p.stage_bytes;
             if (p.stacked) {
@@ -222,16 +220,17 @@ __device__ __forceinline__ void spmm_producer(const SpmmKernelParams& p, SpmmSme
   __syncwarp();
 }
 
-// MMA issuer (one thread): consumes stages in order, driven only by the
-// stage info words in shared memory.  The issuing thread's own instruction
-// latency bounds the whole kernel (~0.1 us of issue work per MMA in a naive
-// loop), so the loop is kept lean: k-steps per stage are a template constant,
-// descriptors are stage-0 templates moved by precomputed 16-byte offsets, and
-// stacked operands need one MMA per (k-step, tile).
+// MMA issuer: consumes stages in order, driven only by the stage info words
+// in shared memory.  The whole warp runs the loop and waits on the barriers;
+// lane 0 issues (a lone lane looping while its siblings sit at the CTA barrier
+// costs hundreds of cycles per stage).  The issuing lane's instruction latency
+// bounds the kernel, so the loop is kept lean: k-steps per stage are a
+// template constant, descriptors are stage-0 templates moved by precomputed
+// 16-byte offsets, and stacked operands need one MMA per (k-step, tile).
 template <int kKS, bool kStacked>
 __device__ __forceinline__ void spmm_mma(const SpmmKernelParams& p, SpmmSmemHeader* hdr,
                                          uint32_t stage0, uint32_t tmem_base, int u_begin,
-                                         int u_end, const WaitCtl& ctl) {
+                                         int u_end, const WaitCtl& ctl, int lane) {
   int stage = 0;
   uint32_t phase = 0;
   int acc = 0;
@@ -258,17 +257,19 @@ __device__ __forceinline__ void spmm_mma(const SpmmKernelParams& p, SpmmSmemHead
   uint32_t inited = 0;
 #pragma unroll 1
   while (units_left > 0) {
-    if (!mbar_wait_bounded(full0 + stage * 8, phase, ctl, ST_TIMEOUT_MMA)) break;
+    // lanes agree on every wait's outcome, so a timeout leaves the loop warp-wide
+    if (!__all_sync(0xffffffffu, mbar_wait_bounded(full0 + stage * 8, phase, ctl, ST_TIMEOUT_MMA))) break;
     const uint32_t info = hdr->info[stage];
     const bool first = (info & INFO_FIRST) != 0;
     if (first) {
-      if (!mbar_wait_bounded(bar_addr(&hdr->acc_empty[acc]), acc_phase ^ 1u, ctl, ST_TIMEOUT_MMA))
+      if (!__all_sync(0xffffffffu,
+                      mbar_wait_bounded(bar_addr(&hdr->acc_empty[acc]), acc_phase ^ 1u, ctl, ST_TIMEOUT_MMA)))
         break;
       d0 = tmem_base + static_cast<uint32_t>(acc * p.acc_cols);
       inited = 0;
     }
     tc_fence_after();
-    if (!(info & INFO_EMPTY)) {
+    if (lane == 0 && !(info & INFO_EMPTY)) {
       const int nt = static_cast<int>((info >> INFO_NT_SHIFT) & 7u);
       const uint64_t bd_s = bdesc0 + soff;
       const uint64_t ad_s = adesc0 + soff;
@@ -299,9 +300,12 @@ __device__ __forceinline__ void spmm_mma(const SpmmKernelParams& p, SpmmSmemHead
         }
       }
     }
-    mma_commit(empty0 + stage * 8);  // frees the stage when these MMAs finish
+    if (lane == 0) {
+      mma_commit(empty0 + stage * 8);  // frees the stage when these MMAs finish
+      if (info & INFO_LAST) mma_commit(bar_addr(&hdr->acc_full[acc]));
+    }
+    __syncwarp();
     if (info & INFO_LAST) {
-      mma_commit(bar_addr(&hdr->acc_full[acc]));
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1u;
       --units_left;
@@ -314,8 +318,11 @@ __device__ __forceinline__ void spmm_mma(const SpmmKernelParams& p, SpmmSmemHead
     }
   }
   // Drain every MMA we issued before TMEM is released.
-  mma_commit(bar_addr(&hdr->drain));
-  drain_wait(bar_addr(&hdr->drain), 0, ctl);
+  if (lane == 0) {
+    mma_commit(bar_addr(&hdr->drain));
+    drain_wait(bar_addr(&hdr->drain), 0, ctl);
+  }
+  __syncwarp();
 }
 
 // Epilogue warp: TMEM lane quarter q holds output columns n0 + 32q + lane of
@@ -429,14 +436,12 @@ __global__ void __launch_bounds__(kThreads, 1) spmm_bsr_tcgen05(const __grid_con
     if (warp < p.nprod)
       spmm_producer(p, hdr, gbase, base, stage0, u_begin, u_end, ctl, warp, lane);
   } else if (warp == kMmaWarp) {
-    if (lane == 0) {
-      if (p.kc == 32) {
-        if (p.stacked) spmm_mma<2, true>(p, hdr, stage0, tmem_base, u_begin, u_end, ctl);
-        else spmm_mma<2, false>(p, hdr, stage0, tmem_base, u_begin, u_end, ctl);
-      } else {
-        if (p.stacked) spmm_mma<4, true>(p, hdr, stage0, tmem_base, u_begin, u_end, ctl);
-        else spmm_mma<4, false>(p, hdr, stage0, tmem_base, u_begin, u_end, ctl);
-      }
+    if (p.kc == 32) {
+      if (p.stacked) spmm_mma<2, true>(p, hdr, stage0, tmem_base, u_begin, u_end, ctl, lane);
+      else spmm_mma<2, false>(p, hdr, stage0, tmem_base, u_begin, u_end, ctl, lane);
+    } else {
+      if (p.stacked) spmm_mma<4, true>(p, hdr, stage0, tmem_base, u_begin, u_end, ctl, lane);
+      else spmm_mma<4, false>(p, hdr, stage0, tmem_base, u_begin, u_end, ctl, lane);
     }
   } else {
     spmm_epilogue<kF32>(p, hdr, tmem_base, u_begin, u_end, ctl, warp, lane);

@@ -109,9 +109,8 @@ __device__ __forceinline__ void rs_producer(const SpmmKernelParams& p, RsSmemHea
 #pragma unroll 1
     for (int j = 0; j < cnt; ++j) {
       const uint32_t flags = static_cast<uint32_t>(__shfl_sync(0xffffffffu, w0.x, j));
-      if (lane == 0)
-        ok = mbar_wait_bounded(baddr(&hdr->empty[stage]), phase ^ 1u, ctl, ST_TIMEOUT_PRODUCER);
-      ok = __shfl_sync(0xffffffffu, ok, 0);
+      ok = mbar_wait_bounded(baddr(&hdr->empty[stage]), phase ^ 1u, ctl, ST_TIMEOUT_PRODUCER);
+      ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       const uint32_t sb = stage0 + static_cast<uint32_t>(stage) * p.stage_bytes;
       const uint32_t zero = (flags >> 8) & 0xFFu;
@@ -185,10 +184,13 @@ __device__ __forceinline__ void rs_producer(const SpmmKernelParams& p, RsSmemHea
   __syncwarp();
 }
 
+// The whole MMA warp runs this loop (every lane waits on the barriers, lane 0
+// issues): a lone lane looping while its 31 siblings sit at the CTA barrier
+// costs hundreds of cycles per pipeline stage in divergent-warp scheduling.
 template <int kKS>
 __device__ __forceinline__ void rs_mma(const SpmmKernelParams& p, RsSmemHeader* hdr,
                                        uint32_t stage0, uint32_t tmem_base, int u_begin, int u_end,
-                                       const WaitCtl& ctl) {
+                                       const WaitCtl& ctl, int lane) {
   int stage = 0;
   uint32_t phase = 0;
   int acc = 0;
@@ -210,29 +212,34 @@ __device__ __forceinline__ void rs_mma(const SpmmKernelParams& p, RsSmemHeader* 
   uint32_t d0 = tmem_base;
 #pragma unroll 1
   while (units_left > 0) {
-    if (!mbar_wait_bounded(full0 + stage * 8, phase, ctl, ST_TIMEOUT_MMA)) break;
+    // lanes agree on every wait's outcome, so a timeout leaves the loop warp-wide
+    if (!__all_sync(0xffffffffu, mbar_wait_bounded(full0 + stage * 8, phase, ctl, ST_TIMEOUT_MMA))) break;
     const uint32_t info = hdr->info[stage];
     const bool first = (info & RS_FIRST) != 0;
     if (first) {
-      if (!mbar_wait_bounded(baddr(&hdr->acc_empty[acc]), acc_phase ^ 1u, ctl, ST_TIMEOUT_MMA))
+      if (!__all_sync(0xffffffffu,
+                      mbar_wait_bounded(baddr(&hdr->acc_empty[acc]), acc_phase ^ 1u, ctl, ST_TIMEOUT_MMA)))
         break;
       tc_fence_after();
       d0 = tmem_base + static_cast<uint32_t>(acc * kRsN);
     }
-    if (!(info & RS_EMPTY)) {
-      const uint64_t ad = adesc0 + soff, bd = bdesc0 + soff;
-#pragma unroll
-      for (int k = 0; k < kKS; ++k)
-        mma_bf16(d0, ad + k * 2u, bd + k * 128u, idesc, (k > 0 || !first) ? 1u : 0u);
-      if (info & RS_TWO) {
+    if (lane == 0) {
+      if (!(info & RS_EMPTY)) {
+        const uint64_t ad = adesc0 + soff, bd = bdesc0 + soff;
 #pragma unroll
         for (int k = 0; k < kKS; ++k)
-          mma_bf16(d0, ad + sub16 + k * 2u, bd + sub16 + k * 128u, idesc, 1u);
+          mma_bf16(d0, ad + k * 2u, bd + k * 128u, idesc, (k > 0 || !first) ? 1u : 0u);
+        if (info & RS_TWO) {
+#pragma unroll
+          for (int k = 0; k < kKS; ++k)
+            mma_bf16(d0, ad + sub16 + k * 2u, bd + sub16 + k * 128u, idesc, 1u);
+        }
       }
+      mma_commit(empty0 + stage * 8);
+      if (info & RS_LAST) mma_commit(baddr(&hdr->acc_full[acc]));
     }
-    mma_commit(empty0 + stage * 8);
+    __syncwarp();
     if (info & RS_LAST) {
-      mma_commit(baddr(&hdr->acc_full[acc]));
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1u;
       --units_left;
@@ -244,8 +251,11 @@ __device__ __forceinline__ void rs_mma(const SpmmKernelParams& p, RsSmemHeader* 
       phase ^= 1u;
     }
   }
-  mma_commit(baddr(&hdr->drain));
-  rs_drain_wait(baddr(&hdr->drain), 0, ctl);
+  if (lane == 0) {
+    mma_commit(baddr(&hdr->drain));
+    rs_drain_wait(baddr(&hdr->drain), 0, ctl);
+  }
+  __syncwarp();
 }
 
 // Epilogue warp with TMEM lane quarter q: lanes 32q..32q+31 are output rows of
@@ -357,10 +367,8 @@ __global__ void __launch_bounds__(kRsThreads, 1) spmm_rowstack_tcgen05(const __g
   const WaitCtl ctl{&hdr->abort_flag, p.status, p.timeout_ns};
 
   if (warp == kRsMmaWarp) {
-    if (lane == 0) {
-      if (p.kc == 32) rs_mma<2>(p, hdr, stage0, tmem_base, u_begin, u_end, ctl);
-      else rs_mma<4>(p, hdr, stage0, tmem_base, u_begin, u_end, ctl);
-    }
+    if (p.kc == 32) rs_mma<2>(p, hdr, stage0, tmem_base, u_begin, u_end, ctl, lane);
+    else rs_mma<4>(p, hdr, stage0, tmem_base, u_begin, u_end, ctl, lane);
   } else if (warp < kRsEpi0) {
     if (warp - kRsProd0 < p.nprod) rs_producer(p, hdr, gbase, base, stage0, ctl, warp - kRsProd0, lane);
   } else {

@@ -221,9 +221,10 @@ __device__ __forceinline__ void spmm_producer(const SpmmKernelParams& p, SpmmSme
 }
 
 // MMA issuer: consumes stages in order, driven only by the stage info words
-// in shared memory.  The whole warp runs the loop and waits on the barriers;
-// lane 0 issues (a lone lane looping while its siblings sit at the CTA barrier
-// costs hundreds of cycles per stage).  The issuing lane's instruction latency
+// in shared memory.  The whole warp runs the loop without diverging: every
+// lane waits on the barriers and executes the MMA and commit instructions
+// predicated on lane 0 (a lone issuing lane costs hundreds of cycles per
+// stage in divergent-warp scheduling).  The issuing lane's instruction latency
 // bounds the kernel, so the loop is kept lean: k-steps per stage are a
 // template constant, descriptors are stage-0 templates moved by precomputed
 // 16-byte offsets, and stacked operands need one MMA per (k-step, tile).
@@ -255,6 +256,7 @@ __device__ __forceinline__ void spmm_mma(const SpmmKernelParams& p, SpmmSmemHead
   uint32_t soff = 0;
   uint32_t d0 = tmem_base;
   uint32_t inited = 0;
+  const uint32_t is0 = lane == 0 ? 1u : 0u;
 #pragma unroll 1
   while (units_left > 0) {
     // lanes agree on every wait's outcome, so a timeout leaves the loop warp-wide
@@ -269,7 +271,7 @@ __device__ __forceinline__ void spmm_mma(const SpmmKernelParams& p, SpmmSmemHead
       inited = 0;
     }
     tc_fence_after();
-    if (lane == 0 && !(info & INFO_EMPTY)) {
+    if (!(info & INFO_EMPTY)) {
       const int nt = static_cast<int>((info >> INFO_NT_SHIFT) & 7u);
       const uint64_t bd_s = bdesc0 + soff;
       const uint64_t ad_s = adesc0 + soff;
@@ -280,8 +282,8 @@ __device__ __forceinline__ void spmm_mma(const SpmmKernelParams& p, SpmmSmemHead
 #pragma unroll
           for (int t = 0; t < kMaxNTiles; ++t)
             if (t < nt)
-              mma_bf16(d0 + t * grp_cols, bd_s + t * tile16 + k * 128u, ad_s + k * 2u, idesc_grp,
-                       (k > 0 || !first) ? 1u : 0u);
+              mma_bf16_pred(d0 + t * grp_cols, bd_s + t * tile16 + k * 128u, ad_s + k * 2u, idesc_grp,
+                            (k > 0 || !first) ? 1u : 0u, is0);
       } else {
         const uint32_t present = info & INFO_PRESENT_MASK;
 #pragma unroll
@@ -292,20 +294,17 @@ __device__ __forceinline__ void spmm_mma(const SpmmKernelParams& p, SpmmSmemHead
             for (uint32_t m = present; m; m &= m - 1) {
               const int g = __ffs(m) - 1;
               const int slot = t * p.G + g;
-              mma_bf16(d0 + static_cast<uint32_t>(slot * p.Rs), bd_s + t * tile16 + k * 128u,
-                       ad_s + g * a_chunk16 + k * 2u, idesc_row, (inited >> slot) & 1u);
+              mma_bf16_pred(d0 + static_cast<uint32_t>(slot * p.Rs), bd_s + t * tile16 + k * 128u,
+                            ad_s + g * a_chunk16 + k * 2u, idesc_row, (inited >> slot) & 1u, is0);
               inited |= 1u << slot;
             }
           }
         }
       }
     }
-    if (lane == 0) {
-      mma_commit(empty0 + stage * 8);  // frees the stage when these MMAs finish
-      if (info & INFO_LAST) mma_commit(bar_addr(&hdr->acc_full[acc]));
-    }
-    __syncwarp();
+    mma_commit_pred(empty0 + stage * 8, is0);  // frees the stage when these MMAs finish
     if (info & INFO_LAST) {
+      mma_commit_pred(bar_addr(&hdr->acc_full[acc]), is0);
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1u;
       --units_left;

@@ -94,6 +94,7 @@ __device__ __forceinline__ void rs_producer(const SpmmKernelParams& p, RsSmemHea
   uint32_t phase = 0;
   uint32_t armed = 0, armed_parity = 0;
   bool ok = true;
+  const uint32_t is0 = lane == 0 ? 1u : 0u;
 #pragma unroll 1
   for (int k0 = pw; k0 < n && ok; k0 += 32 * P) {
     int4 w0 = make_int4(0, 0, 0, 0), w1 = w0, w2 = w0, w3 = w0;
@@ -139,31 +140,34 @@ __device__ __forceinline__ void rs_producer(const SpmmKernelParams& p, RsSmemHea
       ay[5] = __shfl_sync(0xffffffffu, w2.z, j);
       ay[6] = __shfl_sync(0xffffffffu, w2.w, j);
       ay[7] = __shfl_sync(0xffffffffu, w3.x, j);
-      __syncwarp();
-      if (lane == 0) {
+      // Lane 0 issues; every lane runs the same (uniform) control flow and the
+      // issuing instructions are predicated, so the warp never diverges here.
+      if (lane == 0)
         hdr->info[stage] = flags & static_cast<uint32_t>(RS_FIRST | RS_LAST | RS_EMPTY | RS_TWO);
+      __syncwarp();
+      {
         const uint32_t full = baddr(&hdr->full[stage]);
         if (flags & RS_EMPTY) {
-          mbar_arrive(full);
+          mbar_arrive_pred(full, is0);
         } else {
           const uint32_t nsub = (flags & RS_TWO) ? 2u : 1u;
           const uint32_t np = (flags >> 16) & 0xFu;
-          mbar_arrive_expect_tx(full, nsub * b_bytes + np * a_slot);
+          mbar_arrive_expect_tx_pred(full, nsub * b_bytes + np * a_slot, is0);
 #pragma unroll
           for (uint32_t q = 0; q < 2; ++q) {
             if (q >= nsub) break;
             const uint32_t qb = sb + q * sub_bytes;
             const int ky = q ? ky1 : ky0;
             if (p.b3d) {
-              tma_load_3d(qb, &p.tm_b, 0, ky, bz, full);
+              tma_load_3d_pred(qb, &p.tm_b, 0, ky, bz, full, is0);
             } else {
 #pragma unroll
-              for (int h = 0; h < 4; ++h) tma_load_2d(qb + h * b_blk, &p.tm_b, bz + h * 64, ky, full);
+              for (int h = 0; h < 4; ++h) tma_load_2d_pred(qb + h * b_blk, &p.tm_b, bz + h * 64, ky, full, is0);
             }
 #pragma unroll
             for (int g = 0; g < kRsMaxG; ++g)
               if ((flags >> (4 * q + g)) & 1u)
-                tma_load_2d(qb + b_bytes + g * a_slot, &p.tm_a, ax, ay[4 * q + g], full);
+                tma_load_2d_pred(qb + b_bytes + g * a_slot, &p.tm_a, ax, ay[4 * q + g], full, is0);
           }
         }
         armed |= 1u << stage;
@@ -184,9 +188,11 @@ __device__ __forceinline__ void rs_producer(const SpmmKernelParams& p, RsSmemHea
   __syncwarp();
 }
 
-// The whole MMA warp runs this loop (every lane waits on the barriers, lane 0
-// issues): a lone lane looping while its 31 siblings sit at the CTA barrier
-// costs hundreds of cycles per pipeline stage in divergent-warp scheduling.
+// The whole MMA warp runs this loop without diverging: every lane waits on the
+// barriers and executes the MMA and commit instructions predicated on lane 0.
+// A lone lane looping while its 31 siblings sit at the CTA barrier, or an
+// `if (lane == 0)` around the issue, costs hundreds of cycles per pipeline
+// stage on sm_100.
 template <int kKS>
 __device__ __forceinline__ void rs_mma(const SpmmKernelParams& p, RsSmemHeader* hdr,
                                        uint32_t stage0, uint32_t tmem_base, int u_begin, int u_end,
@@ -210,6 +216,7 @@ __device__ __forceinline__ void rs_mma(const SpmmKernelParams& p, RsSmemHeader* 
   const uint32_t empty0 = baddr(&hdr->empty[0]);
   uint32_t soff = 0;
   uint32_t d0 = tmem_base;
+  const uint32_t is0 = lane == 0 ? 1u : 0u;
 #pragma unroll 1
   while (units_left > 0) {
     // lanes agree on every wait's outcome, so a timeout leaves the loop warp-wide
@@ -223,23 +230,20 @@ __device__ __forceinline__ void rs_mma(const SpmmKernelParams& p, RsSmemHeader* 
       tc_fence_after();
       d0 = tmem_base + static_cast<uint32_t>(acc * kRsN);
     }
-    if (lane == 0) {
-      if (!(info & RS_EMPTY)) {
-        const uint64_t ad = adesc0 + soff, bd = bdesc0 + soff;
+    if (!(info & RS_EMPTY)) {
+      const uint64_t ad = adesc0 + soff, bd = bdesc0 + soff;
+#pragma unroll
+      for (int k = 0; k < kKS; ++k)
+        mma_bf16_pred(d0, ad + k * 2u, bd + k * 128u, idesc, (k > 0 || !first) ? 1u : 0u, is0);
+      if (info & RS_TWO) {
 #pragma unroll
         for (int k = 0; k < kKS; ++k)
-          mma_bf16(d0, ad + k * 2u, bd + k * 128u, idesc, (k > 0 || !first) ? 1u : 0u);
-        if (info & RS_TWO) {
-#pragma unroll
-          for (int k = 0; k < kKS; ++k)
-            mma_bf16(d0, ad + sub16 + k * 2u, bd + sub16 + k * 128u, idesc, 1u);
-        }
+          mma_bf16_pred(d0, ad + sub16 + k * 2u, bd + sub16 + k * 128u, idesc, 1u, is0);
       }
-      mma_commit(empty0 + stage * 8);
-      if (info & RS_LAST) mma_commit(baddr(&hdr->acc_full[acc]));
     }
-    __syncwarp();
+    mma_commit_pred(empty0 + stage * 8, is0);
     if (info & RS_LAST) {
+      mma_commit_pred(baddr(&hdr->acc_full[acc]), is0);
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1u;
       --units_left;

@@ -1,25 +1,39 @@
 #!/usr/bin/env python3
 """Benchmark: effective TFLOP/s (nonzero blocks only) of BSR SpMM / SDDMM.
 
-Default workload (N=1): BASELINE config 2, the SpMM density sweep.  A is
-4096x4096 bf16 BSR with 32x32 blocks at p in {0.01, 0.05, 0.10, 0.25, 0.50},
-B is 4096x4096 bf16, values uniform[-1,1] (seeded synthetic data), fp32
-accumulate, bf16 C.  One step = one SpMM per density (five launches), each
-preceded by an L2 flush (a 256 MiB write) so every launch reads HBM cold.
+Workloads (seeded synthetic data of the stated shapes and
+value distributions, generated with numpy):
 
-  python bench.py [--gpus N] [--steps K] [--warmup W] [--strategy dda]
-                  [--impl bsp|reference] [--workload sweep|cfg1|cfg3|cfg4|cfg5]
+  sweep (default)  config 2: A 4096x4096 bf16 BSR, 32x32 blocks, independent
+                   block occupancy p in {0.01, 0.05, 0.10, 0.25, 0.50}, B dense
+                   4096x4096, uniform[-1,1]; one step = one SpMM per density.
+  cfg1             config 1: A 1024x1024, p=0.10, B 1024x256.
+  cfg3             config 3: SDDMM, A 4096x256 and B 256x4096 N(0,1)/16, mask
+                   4096x4096 with 32x32 blocks at p=0.05 (pattern only).
+  cfg4             config 4: attention-shaped pair at sequence 16384, head 128,
+                   32x32 blocks: mask = band of 8 blocks + 4 global block-columns
+                   + Zipf(1.2) random blocks per block-row (capped at 64);
+                   one step = SDDMM (Q K^T under the mask) + SpMM (P V), P having
+                   the mask's pattern and row-normalised uniform[0,1] values.
+  cfg5             config 5: A 65536x65536, 64x64 blocks, Zipf(1.1) block-row
+                   counts at 1% mean density, B 65536x8192 uniform[-1,1]; A's
+                   block-rows are sharded over the GPUs by nonzero-block count
+                   and the C row-panels exchanged over NCCL (strong scaling).
 
-N > 1 (torchrun, one rank per GPU): every rank runs its own independent copy
-of the sweep (its own seed); no collective touches the data path; value =
-all ranks' effective FLOPs / max-over-ranks device time ("weak" scaling).
-The cfg5 workload is the strong-scaling one: A's block-rows are sharded by
-nonzero-block count and C row-panels are all-gathered with NCCL.
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--workload sweep]
+                  [--strategy auto] [--impl bsp|reference]
+
+fp32 accumulate, bf16 outputs.  Every timed launch is preceded by an L2 flush
+(a 256 MiB write) and timed with CUDA events on the launching stream.  For
+N > 1 (torchrun, one rank per GPU) the sweep/cfg1/cfg3/cfg4 workloads run an
+independent copy per rank (own seed, no collective on the data path: "weak"
+scaling); cfg5 splits one problem ("strong" scaling).  value = all ranks'
+effective FLOPs / max-over-ranks device time.
 
 --impl reference times the reference's own CPU golden (bsr_matrix::
-spmm_bfloat16, compiled from the reference sources into oracle/_ref; the
-oracle restatement if that library is absent) with all host threads, on a
-bounded sample of the same workload.
+spmm_bfloat16 / sddmm compiled from the reference sources into oracle/_ref;
+the oracle restatement when that library is absent) on all host threads, on
+a bounded block-row sample of the same workload.
 """
 from __future__ import annotations
 
@@ -29,6 +43,7 @@ import os
 import subprocess
 import sys
 import tempfile
+import threading
 import time
 
 import numpy as np
@@ -40,16 +55,45 @@ for _p in (ROOT, PKG):
         sys.path.insert(0, _p)
 
 METRIC = "effective TFLOP/s (nnz blocks only), BSR SpMM density sweep"
+METRICS = {
+    "sweep": METRIC,
+    "cfg1": "effective TFLOP/s (nnz blocks only), BSR SpMM",
+    "cfg3": "effective TFLOP/s (nnz blocks only), BSR SDDMM",
+    "cfg4": "effective TFLOP/s (nnz blocks only), BSR SDDMM + SpMM attention pair",
+    "cfg5": "effective TFLOP/s (nnz blocks only), multi-GPU BSR SpMM with C all-gather",
+}
+WORKLOAD_DESC = {
+    "sweep": "BASELINE config 2: BSR SpMM 4096x4096x4096, 32x32 blocks, p in {0.01,0.05,0.10,0.25,0.50}",
+    "cfg1": "BASELINE config 1: BSR SpMM 1024x1024 (p=0.10, 32x32 blocks) x 1024x256",
+    "cfg3": "BASELINE config 3: BSR SDDMM 4096x256 x 256x4096 under a 4096x4096 mask, 32x32 blocks, p=0.05",
+    "cfg4": "BASELINE config 4: SDDMM Q K^T + SpMM P V, seq 16384, head 128, 32x32 blocks, band+global+Zipf mask",
+    "cfg5": "BASELINE config 5: BSR SpMM 65536x65536 (64x64 blocks, Zipf(1.1) rows, 1% mean) x 65536x8192, "
+            "row panels sharded by nnz blocks + NCCL exchange of C",
+}
 DENSITIES = [0.01, 0.05, 0.10, 0.25, 0.50]
 L2_FLUSH_BYTES = 256 << 20
 REF_TOTAL_BUDGET_S = 150.0
-WORKLOAD_SWEEP = ("BASELINE config 2: BSR SpMM 4096x4096x4096, 32x32 blocks, "
-                  "p in {0.01,0.05,0.10,0.25,0.50}")
+WORKLOAD_SWEEP = WORKLOAD_DESC["sweep"]
 
 
 def f32_to_bf16(x: np.ndarray) -> np.ndarray:
-    u = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32).astype(np.uint64)
-    return ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+    """Round-to-nearest-even float32 -> bf16 bits (finite inputs: the sum stays
+    inside 32 bits)."""
+    u = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32)
+    return ((u + np.uint32(0x7FFF) + ((u >> np.uint32(16)) & np.uint32(1))) >> np.uint32(16)).astype(np.uint16)
+
+
+def uniform_bf16(rng, shape, lo=-1.0, hi=1.0, chunk_rows=2048):
+    """uniform[lo, hi) bf16 bits, generated in row chunks (bounded temporaries)."""
+    out = np.empty(shape, dtype=np.uint16)
+    flat = out.reshape(shape[0], -1)
+    for r0 in range(0, shape[0], chunk_rows):
+        r1 = min(shape[0], r0 + chunk_rows)
+        x = rng.random((r1 - r0, flat.shape[1]), dtype=np.float32)
+        x *= np.float32(hi - lo)
+        x += np.float32(lo)
+        flat[r0:r1] = f32_to_bf16(x)
+    return out
 
 
 def load_peaks():
@@ -63,85 +107,256 @@ def load_peaks():
             "src": "fallback"}
 
 
-# ------------------------------------------------------------- workloads --
-def gen_spmm_case(M, K, N, R, C, p, seed):
-    rng = np.random.default_rng(seed)
-    occ = rng.random((M // R, K // C)) < p
+# ------------------------------------------------------------- generators --
+def _pattern_from_occupancy(occ):
     rp = np.concatenate([[0], np.cumsum(occ.sum(1))]).astype(np.int32)
     ci = np.nonzero(occ)[1].astype(np.int32)
+    return rp, ci
+
+
+def _pattern_from_sets(cols_per_row):
+    counts = np.array([len(c) for c in cols_per_row], dtype=np.int64)
+    rp = np.concatenate([[0], np.cumsum(counts)]).astype(np.int32)
+    ci = (np.concatenate([np.sort(np.asarray(c, dtype=np.int32)) for c in cols_per_row])
+          if counts.sum() else np.zeros(0, np.int32))
+    return rp, ci.astype(np.int32)
+
+
+def gen_spmm_case(M, K, N, R, C, p, seed, name=None):
+    rng = np.random.default_rng(seed)
+    rp, ci = _pattern_from_occupancy(rng.random((M // R, K // C)) < p)
     vals = f32_to_bf16(rng.uniform(-1, 1, ci.size * R * C).astype(np.float32))
     B = f32_to_bf16(rng.uniform(-1, 1, (K, N)).astype(np.float32))
-    return dict(kind="spmm", M=M, K=K, N=N, R=R, C=C, p=p, rp=rp, ci=ci, vals=vals, B=B)
+    return dict(kind="spmm", name=name or f"p={p}", M=M, K=K, N=N, R=R, C=C, p=p, rp=rp, ci=ci,
+                vals=vals, B=B)
 
 
-def spmm_flops(c):
-    return 2.0 * int(c["rp"][-1]) * c["R"] * c["C"] * c["N"]
+def gen_sddmm_case(M, N, K, R, C, p, seed, scale=1.0 / 16, name=None):
+    """out = mask (.) (A @ B): A M x K, B K x N, mask M x N (pattern only)."""
+    rng = np.random.default_rng(seed)
+    rp, ci = _pattern_from_occupancy(rng.random((M // R, N // C)) < p)
+    A = f32_to_bf16((rng.standard_normal((M, K)) * scale).astype(np.float32))
+    B = f32_to_bf16((rng.standard_normal((K, N)) * scale).astype(np.float32))
+    return dict(kind="sddmm", name=name or f"sddmm p={p}", M=M, N=N, K=K, R=R, C=C, p=p, rp=rp,
+                ci=ci, mvals=None, A=A, B=B)
 
 
-def spmm_bytes(c, esz=2):
-    """Algorithmic bytes: A values + indices + each distinct B K-slice once + all of C."""
-    nnzb = int(c["rp"][-1])
-    ncols = np.unique(c["ci"]).size
-    return (2 * nnzb * c["R"] * c["C"] + 4 * (nnzb + c["M"] // c["R"] + 1)
-            + 2 * ncols * c["C"] * c["N"] + esz * c["M"] * c["N"])
+def gen_attention_mask(nb, rng, band=8, n_global=4, zipf_s=1.2, cap=64):
+    """Block pattern of config 4: per block-row i the band i-3..i+4, the first
+    n_global block-columns, and Zipf(zipf_s)-many (<= cap) uniform random
+    further block-columns."""
+    lo, hi = -(band // 2 - 1), band // 2
+    extra = np.minimum(rng.zipf(zipf_s, nb), cap)
+    rows = []
+    for i in range(nb):
+        s = set(range(max(0, i + lo), min(nb, i + hi + 1)))
+        s.update(range(min(n_global, nb)))
+        want = int(min(extra[i], nb - len(s)))
+        while want > 0:
+            for c in rng.integers(0, nb, size=2 * want + 4):
+                c = int(c)
+                if c not in s:
+                    s.add(c)
+                    want -= 1
+                    if want == 0:
+                        break
+        rows.append(sorted(s))
+    return _pattern_from_sets(rows)
 
 
-def sweep_cases(rank):
-    return [gen_spmm_case(4096, 4096, 4096, 32, 32, p, 1234 + 1 + 100 * rank + i)
-            for i, p in enumerate(DENSITIES)]
+def gen_cfg4(seed, S=16384, D=128, R=32):
+    rng = np.random.default_rng(seed)
+    nb = S // R
+    rp, ci = gen_attention_mask(nb, rng)
+    Q = f32_to_bf16(rng.standard_normal((S, D)).astype(np.float32))
+    Kt = f32_to_bf16(rng.standard_normal((D, S)).astype(np.float32))   # K^T, row-major D x S
+    V = f32_to_bf16(rng.standard_normal((S, D)).astype(np.float32))
+    # P: the mask's pattern with uniform[0,1] values normalised over each row
+    nnzb = int(rp[-1])
+    pv = rng.uniform(0, 1, (nnzb, R, R)).astype(np.float32)
+    row_of_block = np.repeat(np.arange(nb), np.diff(rp))
+    sums = np.zeros((nb, R), np.float64)
+    np.add.at(sums, row_of_block, pv.sum(axis=2))
+    pv /= sums[row_of_block][:, :, None].astype(np.float32)
+    sddmm = dict(kind="sddmm", name="sddmm QK^T", M=S, N=S, K=D, R=R, C=R, p=None, rp=rp, ci=ci,
+                 mvals=None, A=Q, B=Kt)
+    spmm = dict(kind="spmm", name="spmm PV", M=S, K=S, N=D, R=R, C=R, p=None, rp=rp, ci=ci,
+                vals=f32_to_bf16(pv.reshape(-1)), B=V)
+    return [sddmm, spmm]
+
+
+def gen_zipf_pattern(nbr, nbc, density, s, rng):
+    """Power-law block-row counts (Zipf's law over ranks: the k-th heaviest
+    block-row holds ~ A k^-s blocks, at most nbc, A set so that the mean
+    density is `density`), rows in random order, column indices uniform
+    without replacement."""
+    w = np.arange(1, nbr + 1, dtype=np.float64) ** -s
+    total = density * nbr * nbc
+    lo, hi = 0.0, total
+    for _ in range(100):                      # sum(min(nbc, A w)) is monotone in A
+        mid = 0.5 * (lo + hi)
+        if np.minimum(nbc, mid * w).sum() < total:
+            lo = mid
+        else:
+            hi = mid
+    counts = np.minimum(nbc, np.floor(hi * w)).astype(np.int64)
+    short = int(round(total)) - int(counts.sum())
+    for k in range(nbr):                      # hand out the rounding remainder
+        if short <= 0:
+            break
+        if counts[k] < nbc:
+            counts[k] += 1
+            short -= 1
+    counts = counts[rng.permutation(nbr)]
+    rows = [rng.choice(nbc, size=int(c), replace=False) for c in counts]
+    return _pattern_from_sets(rows)
+
+
+def gen_cfg5(seed, M=65536, K=65536, N=8192, R=64, C=64, density=0.01, s=1.1):
+    rng = np.random.default_rng(seed)
+    rp, ci = gen_zipf_pattern(M // R, K // C, density, s, rng)
+    vals = uniform_bf16(rng, (ci.size * R, C)).reshape(-1)
+    B = uniform_bf16(rng, (K, N))
+    return dict(kind="spmm", name="spmm cfg5", M=M, K=K, N=N, R=R, C=C, p=density, rp=rp, ci=ci,
+                vals=vals, B=B)
+
+
+def workload_ops(workload, rank):
+    """Host-side ops of one step of `workload` (rank picks the seed of the
+    independent per-rank copies)."""
+    base = 1234 + 1 + 100 * rank
+    if workload == "sweep":
+        return [gen_spmm_case(4096, 4096, 4096, 32, 32, p, base + i) for i, p in enumerate(DENSITIES)]
+    if workload == "cfg1":
+        return [gen_spmm_case(1024, 1024, 256, 32, 32, 0.10, base)]
+    if workload == "cfg3":
+        return [gen_sddmm_case(4096, 4096, 256, 32, 32, 0.05, base)]
+    if workload == "cfg4":
+        return gen_cfg4(base)
+    if workload == "cfg5":
+        return [gen_cfg5(1234)]   # one problem shared by all ranks
+    raise ValueError(workload)
+
+
+def op_flops(op):
+    """Effective FLOPs (reference formulas, GEMM_profiling/read_spmm_profiler.py:73
+    and read_sddmm_profiler.py:75)."""
+    nnzb = int(op["rp"][-1])
+    if op["kind"] == "spmm":
+        return 2.0 * nnzb * op["R"] * op["C"] * op["N"]
+    return 2.0 * nnzb * op["R"] * op["C"] * op["K"] + nnzb * op["R"] * op["C"]
+
+
+def op_bytes(op):
+    """Algorithmic HBM bytes: every operand byte the result depends on, read
+    once, plus the output written once."""
+    nnzb = int(op["rp"][-1])
+    R, C = op["R"], op["C"]
+    ncols = np.unique(op["ci"]).size
+    idx = 4 * (nnzb + op["M"] // R + 1)
+    if op["kind"] == "spmm":
+        return 2 * nnzb * R * C + idx + 2 * ncols * C * op["N"] + 2 * op["M"] * op["N"]
+    nrows = int(np.count_nonzero(np.diff(op["rp"])))
+    mask = 0 if op["mvals"] is None else 2 * nnzb * R * C
+    return mask + idx + 2 * nrows * R * op["K"] + 2 * ncols * C * op["K"] + 2 * nnzb * R * C
 
 
 # ---------------------------------------------------------------- clocks --
 class ClockSampler:
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    """SM clock and throttle reasons of the given GPUs, polled every 2 ms
+    from a background thread through NVML (nvidia-smi as a fallback)."""
+    NVML_REASONS = (("hw_slowdown", 0x8), ("sw_thermal_slowdown", 0x20),
+                    ("hw_thermal_slowdown", 0x40), ("sw_power_cap", 0x4))
 
-    def __init__(self, gpu_index: int):
-        self.proc = None
-        self.path = None
+    def __init__(self, pci_locations, period_s=0.002):
+        """pci_locations: (domain, bus, device) integers of each GPU to watch
+        (torch's device properties); NVML handles are matched by enumeration."""
+        self.rows = []
+        self.stop_ev = threading.Event()
+        self.thread = None
+        self.smi = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            by_loc = {}
+            for i in range(pynvml.nvmlDeviceGetCount()):
+                h = pynvml.nvmlDeviceGetHandleByIndex(i)
+                info = pynvml.nvmlDeviceGetPciInfo(h)
+                by_loc[(int(info.domain), int(info.bus), int(info.device))] = h
+            self.handles = [by_loc[tuple(int(v) for v in loc)] for loc in pci_locations]
+            self.smax = max(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
+                            for h in self.handles)
+            self.thread = threading.Thread(target=self._poll, args=(period_s,), daemon=True)
+            self.thread.start()
+        except Exception:
+            self.nv = None
+            self._start_smi(",".join(f"{int(d):08X}:{int(b):02X}:{int(v):02X}.0"
+                                     for d, b, v in pci_locations))
+
+    def _poll(self, period):
+        nv = self.nv
+        while not self.stop_ev.is_set():
+            for h in self.handles:
+                try:
+                    sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+                    reasons = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                    self.rows.append((float(sm), int(reasons)))
+                except Exception:
+                    pass
+            self.stop_ev.wait(period)
+
+    def _start_smi(self, bus_ids):
         try:
             fd, self.path = tempfile.mkstemp(suffix=".csv")
             os.close(fd)
             self.fh = open(self.path, "w")
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "100", "-i", str(gpu_index)], stdout=self.fh, stderr=subprocess.DEVNULL)
+            self.smi = subprocess.Popen(
+                ["nvidia-smi", "--query-gpu=clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,"
+                 "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+                 "clocks_event_reasons.sw_power_cap", "--format=csv,noheader,nounits", "-lms", "100",
+                 "-i", bus_ids],
+                stdout=self.fh, stderr=subprocess.DEVNULL)
         except Exception:
-            self.proc = None
+            self.smi = None
 
     def stop(self):
-        if self.proc is None:
+        if self.thread is not None:
+            self.stop_ev.set()
+            self.thread.join(timeout=5)
+            if not self.rows:
+                return None
+            reasons = set()
+            for _, bits in self.rows:
+                for name, bit in self.NVML_REASONS:
+                    if bits & bit:
+                        reasons.add(name)
+            return {"sm_mhz": float(np.median([r[0] for r in self.rows])),
+                    "sm_max_mhz": float(self.smax), "reasons": sorted(reasons),
+                    "samples": len(self.rows), "source": "nvml, 2 ms"}
+        if self.smi is None:
             return None
-        self.proc.terminate()
+        self.smi.terminate()
         try:
-            self.proc.wait(timeout=5)
+            self.smi.wait(timeout=5)
         except Exception:
-            self.proc.kill()
+            self.smi.kill()
         self.fh.close()
         rows = []
         with open(self.path) as f:
             for line in f:
                 parts = [x.strip() for x in line.split(",")]
-                if len(parts) < 9:
-                    continue
                 try:
-                    rows.append(dict(sm=float(parts[1]), smax=float(parts[2]), power=float(parts[3]),
-                                     hw=parts[5], hwt=parts[6], swt=parts[7], swp=parts[8]))
-                except ValueError:
+                    rows.append((float(parts[0]), float(parts[1]), parts[2:6]))
+                except (ValueError, IndexError):
                     continue
         os.unlink(self.path)
         if not rows:
             return None
-        reasons = set()
-        for r in rows:
-            for k, name in (("hw", "hw_slowdown"), ("hwt", "hw_thermal_slowdown"),
-                            ("swt", "sw_thermal_slowdown"), ("swp", "sw_power_cap")):
-                if r[k].lower().startswith("active"):
-                    reasons.add(name)
-        loaded = [r["sm"] for r in rows if r["power"] > 250] or [r["sm"] for r in rows]
-        return {"sm_mhz": float(np.median(loaded)), "sm_max_mhz": rows[0]["smax"],
-                "reasons": sorted(reasons), "samples": len(rows)}
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = {n for r in rows for n, v in zip(names, r[2]) if v.lower().startswith("active")}
+        return {"sm_mhz": float(np.median([r[0] for r in rows])), "sm_max_mhz": rows[0][1],
+                "reasons": sorted(reasons), "samples": len(rows), "source": "nvidia-smi, 100 ms"}
 
 
 # ------------------------------------------------------------- dist utils --
@@ -165,23 +380,13 @@ def init_dist(ws, local):
     return dist if ws > 1 else None
 
 
-def max_over_ranks(x: float, dist) -> float:
+def reduce_over_ranks(x: float, dist, op="max") -> float:
     if dist is None:
         return x
     import torch
 
     t = torch.tensor([x], dtype=torch.float64, device="cuda")
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    return float(t.item())
-
-
-def sum_over_ranks(x: float, dist) -> float:
-    if dist is None:
-        return x
-    import torch
-
-    t = torch.tensor([x], dtype=torch.float64, device="cuda")
-    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX if op == "max" else dist.ReduceOp.SUM)
     return float(t.item())
 
 
@@ -195,63 +400,119 @@ def barrier(dist):
 
 
 # ------------------------------------------------------------ CPU baseline --
-def cpu_calibrate(cases, budget_s=12.0, threads=None):
-    """Pick, per case, how many leading block-rows the CPU golden can finish
-    in about budget_s / len(cases) seconds.  Returns (rows per case, kind)."""
+def _cpu_time(op, rows, threads, kind):
+    """Seconds for the CPU golden (kind 'reference') or the oracle port over
+    block-rows [0, rows) of `op`."""
+    import oracle
+
+    if op["kind"] == "spmm":
+        args = (op["rp"], op["ci"], op["vals"], op["M"], op["K"], op["R"], op["C"], op["B"], op["N"])
+        if kind == "reference":
+            return oracle.ref_spmm_timed(*args, (0, rows), threads)
+        t0 = time.perf_counter()
+        oracle.spmm_bf16(*args, threads=threads, rows=(0, rows))
+        return time.perf_counter() - t0
+    args = (op["rp"], op["ci"], op["mvals"], op["M"], op["N"], op["R"], op["C"], op["A"], op["B"],
+            op["K"])
+    if kind == "reference":
+        return oracle.ref_sddmm_timed(*args, (0, rows), threads)
+    t0 = time.perf_counter()
+    oracle.sddmm_bf16(*args, threads=threads, rows=(0, rows))
+    return time.perf_counter() - t0
+
+
+def _sample_flops(op, rows):
+    nnzb = int(op["rp"][rows])
+    if op["kind"] == "spmm":
+        return 2.0 * nnzb * op["R"] * op["C"] * op["N"]
+    return 2.0 * nnzb * op["R"] * op["C"] * op["K"] + nnzb * op["R"] * op["C"]
+
+
+def cpu_calibrate(ops, budget_s=12.0, threads=None):
+    """Per op, how many leading block-rows the CPU golden finishes in about
+    budget_s / len(ops) seconds.  Returns (rows per op, kind)."""
     import oracle
 
     threads = threads or os.cpu_count() or 1
     kind = "reference" if oracle.ref_available() else "port"
-    per_case = budget_s / len(cases)
-    rows_out = []
-    for c in cases:
-        nbr = c["M"] // c["R"]
+    per_op = budget_s / len(ops)
+    out = []
+    for op in ops:
+        nbr = op["M"] // op["R"]
         rows = min(max(threads, 1), nbr)
         for _ in range(8):
-            t = _cpu_time(c, rows, threads, kind)
-            if t >= per_case / 2 or rows >= nbr:
+            t = _cpu_time(op, rows, threads, kind)
+            if t >= per_op / 2 or rows >= nbr:
                 break
-            rows = min(nbr, int(rows * min(16.0, max(1.5, per_case / max(t, 1e-4)))))
-        rows_out.append(rows)
-    return rows_out, kind
+            rows = min(nbr, int(rows * min(16.0, max(1.5, per_op / max(t, 1e-4)))))
+        out.append(rows)
+    return out, kind
 
 
-def cpu_sample_time(cases, rows, kind, threads=None):
-    """Time the calibrated block-row sample of every case once.
-    Returns (effective flops done, seconds, sample description)."""
+def cpu_sample_time(ops, rows, kind, threads=None):
     threads = threads or os.cpu_count() or 1
-    total_f = total_t = 0.0
-    samples = []
-    for c, r in zip(cases, rows):
-        total_t += _cpu_time(c, r, threads, kind)
-        total_f += 2.0 * int(c["rp"][r]) * c["R"] * c["C"] * c["N"]
-        samples.append(f"p={c['p']}: {r}/{c['M'] // c['R']} block-rows")
-    return total_f, total_t, "; ".join(samples)
-
-
-def cpu_reference_time(cases, budget_s=12.0, threads=None):
-    """Time the reference golden (oracle/_ref) or, if absent, the oracle
-    restatement, on a bounded block-row sample of each case.  Returns
-    (flops_done, seconds, kind, cores, sample_description)."""
-    threads = threads or os.cpu_count() or 1
-    rows, kind = cpu_calibrate(cases, budget_s, threads)
-    f, t, sample = cpu_sample_time(cases, rows, kind, threads)
-    return f, t, kind, threads, sample
-
-
-def _cpu_time(c, rows, threads, kind):
-    import oracle
-
-    if kind == "reference":
-        return oracle.ref_spmm_timed(c["rp"], c["ci"], c["vals"], c["M"], c["K"], c["R"], c["C"],
-                                     c["B"], c["N"], (0, rows), threads)
-    t0 = time.perf_counter()
-    oracle.spmm_bf16(c["rp"], c["ci"], c["vals"], c["M"], c["K"], c["R"], c["C"], c["B"], c["N"],
-                     threads=threads, rows=(0, rows))
-    return time.perf_counter() - t0
+    f = t = 0.0
+    desc = []
+    for op, r in zip(ops, rows):
+        t += _cpu_time(op, r, threads, kind)
+        f += _sample_flops(op, r)
+        desc.append(f"{op['name']}: {r}/{op['M'] // op['R']} block-rows")
+    return f, t, "; ".join(desc)
 
 
 # --------------------------------------------------------------- our arm --
+class DevOp:
+    """One op of the workload on the GPU: device operands, output, plan."""
+
+    def __init__(self, op, dev, strategy, local):
+        import torch
+
+        import bsp
+
+        self.op = op
+        self.kind = op["kind"]
+        if self.kind == "spmm":
+            self.A = bsp.DeviceBSR.from_host(op["M"], op["K"], op["R"], op["C"], op["rp"], op["ci"],
+                                             op["vals"], local)
+            self.B = bsp.to_device_bf16(op["B"], local)
+            self.out = torch.empty((op["M"], op["N"]), dtype=torch.bfloat16, device="cuda")
+            self.plan = bsp.SpmmPlan(dev, self.A, op["N"], strategy)
+        else:
+            self.mask = bsp.DeviceBSR.from_host(op["M"], op["N"], op["R"], op["C"], op["rp"], op["ci"],
+                                                op["mvals"], local)
+            self.Ad = bsp.to_device_bf16(op["A"], local)
+            self.Bd = bsp.to_device_bf16(op["B"], local)
+            self.out = torch.empty(max(int(op["rp"][-1]) * op["R"] * op["C"], 8), dtype=torch.bfloat16,
+                                   device="cuda")
+            self.plan = bsp.SddmmPlan(dev, self.mask, op["K"], strategy)
+
+    def run(self, stream):
+        if self.kind == "spmm":
+            self.plan.execute(self.A, self.B, self.out, stream)
+        else:
+            self.plan.execute(self.mask, self.Ad, self.Bd, self.out, stream)
+
+    def kernel(self):
+        if self.kind == "sddmm":
+            return "sddmm_bsr_tcgen05"
+        return "spmm_rowstack_tcgen05" if self.plan.info().get("variant", 0) == 1 else "spmm_bsr_tcgen05"
+
+    def close(self):
+        self.plan.close()
+
+
+def strategy_for(op, name):
+    """`--strategy auto`: DDA (row-stacked, N = 256 MMAs) for SpMM with N >= 256,
+    SnF (swap-AB, 128-column tiles) for narrower B, CDA for SDDMM."""
+    import bsp
+
+    if name != "auto":
+        return bsp.STRATEGIES[name]
+    if op["kind"] == "sddmm":
+        return bsp.DDA
+    return bsp.DDA if op["N"] >= 256 else bsp.SNF
+
+
 def run_bsp(args):
     import torch
 
@@ -261,19 +522,29 @@ def run_bsp(args):
     dist = init_dist(ws, local)
     peaks = load_peaks()
     dev = bsp.device(local)
-    strategy = bsp.STRATEGIES[args.strategy]
-    cases = sweep_cases(rank)
     stream = torch.cuda.current_stream()
     flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device="cuda")
+    sharded = args.workload == "cfg5"
+    ops = workload_ops(args.workload, rank)
 
-    runs = []
-    for c in cases:
-        A = bsp.DeviceBSR.from_host(c["M"], c["K"], c["R"], c["C"], c["rp"], c["ci"], c["vals"], local)
-        B = bsp.to_device_bf16(c["B"], local)
-        Cout = torch.empty((c["M"], c["N"]), dtype=torch.bfloat16, device="cuda")
-        plan = bsp.SpmmPlan(dev, A, c["N"], strategy)
-        runs.append(dict(case=c, A=A, B=B, C=Cout, plan=plan, flops=spmm_flops(c),
-                         bytes=spmm_bytes(c), times=[]))
+    shard = None
+    if sharded:
+        import bsp_dist
+
+        op = ops[0]
+        shard = bsp_dist.ShardedSpmm(dev, op["M"], op["K"], op["R"], op["C"], op["rp"], op["ci"],
+                                     op["vals"], op["N"], rank, ws, strategy_for(op, args.strategy))
+        Bd = bsp.to_device_bf16(op["B"], local)
+        Cfull = torch.empty((op["M"], op["N"]), dtype=torch.bfloat16, device="cuda")
+        runs = [dict(op=op, flops=shard.flops, bytes=op_bytes(op), times=[], name=op["name"],
+                     fn=lambda s: shard.run(Bd, Cfull, s, replicate=ws > 1),
+                     kernel="spmm_rowstack_tcgen05 + NCCL exchange of C row-panels")]
+    else:
+        runs = []
+        for op in ops:
+            d = DevOp(op, dev, strategy_for(op, args.strategy), local)
+            runs.append(dict(op=op, dev=d, flops=op_flops(op), bytes=op_bytes(op), times=[],
+                             name=op["name"], fn=d.run, kernel=d.kernel(), plan=d.plan.info()))
 
     def step(record):
         for r in runs:
@@ -282,7 +553,7 @@ def run_bsp(args):
                 e0 = torch.cuda.Event(enable_timing=True)
                 e1 = torch.cuda.Event(enable_timing=True)
                 e0.record(stream)
-            r["plan"].execute(r["A"], r["B"], r["C"], stream)
+            r["fn"](stream)
             if record:
                 e1.record(stream)
                 r["times"].append((e0, e1))
@@ -290,9 +561,12 @@ def run_bsp(args):
     for _ in range(args.warmup):
         step(False)
     dev.synchronize()
-    # quick self-check of the first density against the oracle on a few rows
     barrier(dist)
-    sampler = ClockSampler(local) if rank == 0 else None
+    sampler = None
+    if rank == 0:
+        devs = range(ws) if ws > 1 else [local]
+        props = [torch.cuda.get_device_properties(i) for i in devs]
+        sampler = ClockSampler([(p.pci_domain_id, p.pci_bus_id, p.pci_device_id) for p in props])
     for _ in range(args.steps):
         step(True)
     barrier(dist)
@@ -300,152 +574,195 @@ def run_bsp(args):
     dev.synchronize()
 
     per = []
-    total_t = 0.0
-    total_f = 0.0
+    total_t = total_f = 0.0
     for r in runs:
         ts = [a.elapsed_time(b) * 1e-3 for a, b in r["times"]]
         t = float(np.mean(ts))
         total_t += sum(ts)
         total_f += r["flops"] * len(ts)
-        c = r["case"]
         t_tc = r["flops"] / (peaks["bf16_tflops"] * 1e12)
         t_hbm = r["bytes"] / (peaks["hbm_gbs"] * 1e9)
-        per.append(dict(p=c["p"], nnzb=int(c["rp"][-1]), ms=t * 1e3,
-                        tflops=r["flops"] / t / 1e12, gbs=r["bytes"] / t / 1e9,
-                        bound="tensor" if t_tc >= t_hbm else "hbm",
-                        roofline_frac=max(t_tc, t_hbm) / t, plan=r["plan"].info()))
-    t_all = max_over_ranks(total_t, dist)
-    f_all = sum_over_ranks(total_f, dist)
+        d = dict(name=r["name"], nnzb=int(r["op"]["rp"][-1]), ms=t * 1e3,
+                 tflops=r["flops"] / t / 1e12, gbs=r["bytes"] / t / 1e9,
+                 bound="tensor" if t_tc >= t_hbm else "hbm", roofline_frac=max(t_tc, t_hbm) / t)
+        if "plan" in r:
+            d["units"] = r["plan"].get("units")
+        per.append(d)
+    t_all = reduce_over_ranks(total_t, dist, "max")
+    f_all = reduce_over_ranks(total_f, dist, "sum")
     value = f_all / t_all / 1e12
 
-    # dominant kernel = the launch with the largest share of device time
-    dom = max(per, key=lambda d: d["ms"])
-    dom_run = runs[[d["p"] for d in per].index(dom["p"])]
+    # dominant launch = the op with the largest share of device time
+    di = int(np.argmax([d["ms"] for d in per]))
+    dom, dom_run = per[di], runs[di]
     if dom["bound"] == "tensor":
         roof = {"bound": "tensor", "achieved": dom["tflops"], "peak": peaks["bf16_tflops"],
                 "unit": "TFLOP/s", "frac": dom["tflops"] / peaks["bf16_tflops"]}
     else:
         roof = {"bound": "hbm", "achieved": dom["gbs"], "peak": peaks["hbm_gbs"],
                 "unit": "GB/s", "frac": dom["gbs"] / peaks["hbm_gbs"]}
-    roof["traffic"] = traffic_for(dom["p"], dom_run["bytes"])
+    roof["traffic"] = traffic_for(args.workload, dom["name"])
     roof["peak_src"] = peaks["src"]
-    variant = dom["plan"].get("variant", 0)
-    roof["kernel"] = f"{'spmm_rowstack_tcgen05' if variant == 1 else 'spmm_bsr_tcgen05'} p={dom['p']}"
+    roof["kernel"] = f"{dom_run['kernel']} ({dom['name']})"
     roof["algorithmic"] = dom_run["bytes"] if dom["bound"] == "hbm" else dom_run["flops"]
 
-    # ---- e2e through the host-buffer C ABI (pinned host memory) ----
-    e2e = run_e2e(args, runs, dev, strategy, dist)
+    e2e = run_e2e(args, runs, dev, dist, shard)
 
-    # ---- CPU baseline (rank 0, N=1 only) ----
     cpu = None
     if ws == 1 and not args.no_cpu:
-        f, t, kind, cores, sample = cpu_reference_time(cases, budget_s=args.cpu_budget)
-        cpu = {"value": f / t / 1e12, "unit": "TFLOP/s", "cores": cores, "kind": kind,
-               "sample": sample + " of each density; golden bsr_matrix::spmm_bfloat16"}
+        host_ops = [r["op"] for r in runs]
+        rows, kind = cpu_calibrate(host_ops, budget_s=args.cpu_budget)
+        f, t, sample = cpu_sample_time(host_ops, rows, kind)
+        cpu = {"value": f / t / 1e12, "unit": "TFLOP/s", "cores": os.cpu_count() or 1, "kind": kind,
+               "sample": sample + ("; reference golden bsr_matrix::spmm_bfloat16 / sddmm"
+                                   if kind == "reference" else "; oracle restatement")}
 
     out = {
-        "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": ws, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": t_all / args.steps * 1e3, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-        "data": "synthetic (seeded numpy: Bernoulli block occupancy, uniform[-1,1] values)",
-        "config": {"workload": WORKLOAD_SWEEP, "strategy": args.strategy,
-                   "c_dtype": "bf16", "accumulate": "fp32",
+        "metric": METRICS[args.workload], "value": value, "unit": "TFLOP/s", "n_gpus": ws,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": t_all / args.steps * 1e3,
+        "higher_is_better": True, "scaling": "strong" if sharded else "weak", "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (seeded numpy, BASELINE config shapes and value distributions)",
+        "config": {"workload": WORKLOAD_DESC[args.workload], "name": args.workload,
+                   "strategy": args.strategy, "c_dtype": "bf16", "accumulate": "fp32",
                    "l2": "flushed (256 MiB write) before every timed launch",
-                   "per_rank": "independent copy of the sweep per rank" if ws > 1 else None},
+                   "per_rank": ("row panels of one problem, balanced by nonzero blocks" if sharded
+                                else "independent copy per rank") if ws > 1 else None},
         "roofline": roof, "cpu_baseline": cpu, "e2e": e2e,
-        "gpu_launches": args.steps * len(runs), "clocks": clocks,
-        "sweep": [{k: v for k, v in d.items() if k != "plan"} | {"units": d["plan"]["units"]}
-                  for d in per],
+        "gpu_launches": args.steps * len(runs), "clocks": clocks, "per_op": per,
     }
     if rank == 0:
         print(json.dumps(out), flush=True)
     for r in runs:
-        r["plan"].close()
+        if "dev" in r:
+            r["dev"].close()
+    if shard is not None:
+        shard.close()
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
 
 
-def run_e2e(args, runs, dev, strategy, dist):
-    """Same metric end to end: pinned host inputs -> H2D -> plan -> SpMM -> D2H."""
+def _pinned(a):
+    import torch
+
+    return torch.from_numpy(np.ascontiguousarray(a)).pin_memory().numpy()
+
+
+def run_e2e(args, runs, dev, dist, shard):
+    """The same metric end to end through the public API with host buffers:
+    every step copies the inputs from pinned host memory and reads the result
+    back (bsp_spmm_host / bsp_sddmm_host; cfg5: the B and A-panel copies, the
+    sharded SpMM with its NCCL exchange, and the full C back to the host)."""
     import torch
 
     import bsp
 
-    host = []
+    steps = max(1, min(args.steps, args.e2e_steps))
     h2d = d2h = 0
-    for r in runs:
-        c = r["case"]
+    if shard is not None:
+        op = runs[0]["op"]
+        hB = torch.from_numpy(np.ascontiguousarray(op["B"]).view(np.int16)).pin_memory()
+        hv = None
+        if shard.A is not None:
+            hv = torch.from_numpy(np.ascontiguousarray(shard.panel.values).view(np.int16)).pin_memory()
+        hout = torch.empty((op["M"], op["N"]), dtype=torch.int16).pin_memory()
+        Bd = torch.empty((op["K"], op["N"]), dtype=torch.bfloat16, device="cuda")
+        Cfull = torch.empty((op["M"], op["N"]), dtype=torch.bfloat16, device="cuda")
+        h2d = hB.numel() * 2 + (hv.numel() * 2 if hv is not None else 0)
+        d2h = hout.numel() * 2
 
-        def pin(a):
-            t = torch.from_numpy(np.ascontiguousarray(a)).pin_memory()
-            return t.numpy()
+        def one():
+            Bd.view(torch.int16).copy_(hB, non_blocking=True)
+            if hv is not None:
+                shard.A.values.view(torch.int16).copy_(hv, non_blocking=True)
+            shard.run(Bd, Cfull, None, replicate=dist is not None)
+            hout.copy_(Cfull.view(torch.int16), non_blocking=True)
+            torch.cuda.synchronize()
+    else:
+        host = []
+        for r in runs:
+            op = r["op"]
+            if op["kind"] == "spmm":
+                hc = dict(rp=_pinned(op["rp"]), ci=_pinned(op["ci"]), v=_pinned(op["vals"]),
+                          B=_pinned(op["B"]),
+                          out=torch.empty((op["M"], op["N"]), dtype=torch.int16).pin_memory()
+                          .numpy().view(np.uint16))
+                h2d += hc["rp"].nbytes + hc["ci"].nbytes + hc["v"].nbytes + hc["B"].nbytes
+            else:
+                nv = int(op["rp"][-1]) * op["R"] * op["C"]
+                hc = dict(rp=_pinned(op["rp"]), ci=_pinned(op["ci"]), A=_pinned(op["A"]), B=_pinned(op["B"]),
+                          out=torch.empty(max(nv, 1), dtype=torch.int16).pin_memory()
+                          .numpy().view(np.uint16)[:nv])
+                h2d += hc["rp"].nbytes + hc["ci"].nbytes + hc["A"].nbytes + hc["B"].nbytes
+            d2h += hc["out"].nbytes
+            host.append((op, hc, strategy_for(op, args.strategy)))
 
-        hc = dict(rp=pin(c["rp"]), ci=pin(c["ci"]), vals=pin(c["vals"]), B=pin(c["B"]),
-                  out=torch.empty((c["M"], c["N"]), dtype=torch.int16).pin_memory().numpy().view(np.uint16))
-        host.append((c, hc))
-        h2d += hc["rp"].nbytes + hc["ci"].nbytes + hc["vals"].nbytes + hc["B"].nbytes
-        d2h += hc["out"].nbytes
-    e2e_steps = max(1, min(args.steps, args.e2e_steps))
+        def one():
+            for op, hc, strat in host:
+                if op["kind"] == "spmm":
+                    bsp.spmm_host(op["M"], op["K"], op["R"], op["C"], hc["rp"], hc["ci"], hc["v"], hc["B"],
+                                  op["N"], strategy=strat, dev=dev, out=hc["out"])
+                else:
+                    bsp.sddmm_host(op["M"], op["N"], op["R"], op["C"], hc["rp"], hc["ci"], None, hc["A"],
+                                   hc["B"], op["K"], strategy=strat, dev=dev, out=hc["out"])
 
-    def one():
-        for c, hc in host:
-            bsp.spmm_host(c["M"], c["K"], c["R"], c["C"], hc["rp"], hc["ci"], hc["vals"], hc["B"],
-                          c["N"], strategy=strategy, dev=dev, out=hc["out"])
-
-    one()  # warm (workspace growth)
+    one()  # warm (workspace growth, first touch of pinned pages)
     barrier(dist)
     t0 = time.perf_counter()
-    for _ in range(e2e_steps):
+    for _ in range(steps):
         one()
-    t = time.perf_counter() - t0
-    t = max_over_ranks(t, dist)
-    f = sum_over_ranks(sum(r["flops"] for r in runs) * e2e_steps, dist)
+    t = reduce_over_ranks(time.perf_counter() - t0, dist, "max")
+    f = reduce_over_ranks(sum(r["flops"] for r in runs) * steps, dist, "sum")
     return {"value": f / t / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": int(h2d),
-            "d2h_bytes_per_step": int(d2h), "steps": e2e_steps,
-            "path": "bsp_spmm_host (C ABI, host buffers, synchronous)"}
+            "d2h_bytes_per_step": int(d2h), "steps": steps,
+            "path": ("bsp_dist.ShardedSpmm (host B and A values in, NCCL exchange, full C out)"
+                     if shard is not None else "bsp_spmm_host / bsp_sddmm_host (C ABI, host buffers)")}
 
 
-def traffic_for(p, algorithmic_bytes):
+def traffic_for(workload, name):
     """DRAM bytes per launch of the dominant kernel from the committed ncu
-    summary (profiles/spmm_traffic.json), if one was captured for this p."""
-    path = os.path.join(ROOT, "profiles", "spmm_traffic.json")
+    summary (profiles/traffic.json, keyed "<workload>:<op name>"), if one was
+    captured for it."""
+    path = os.path.join(ROOT, "profiles", "traffic.json")
     try:
         with open(path) as f:
             d = json.load(f)
-        return d.get(str(p))
+        return d.get(f"{workload}:{name}")
     except Exception:
         return None
 
 
 # --------------------------------------------------------- reference arm --
 def run_reference(args):
-    """The reference arm: the reference's CPU golden on this box's host cores.
-    The whole run (calibration, warm-up and timed steps) is held to about
-    REF_TOTAL_BUDGET_S seconds by shrinking each step's block-row sample."""
+    """The reference arm: the reference's CPU golden on this box's host cores,
+    the whole run (calibration, warm-up, timed steps) held to about
+    REF_TOTAL_BUDGET_S seconds by the size of each step's block-row sample."""
     ws, rank, local = dist_env()
     if rank != 0:
         return
-    cases = sweep_cases(0)
+    ops = workload_ops(args.workload, 0)
     threads = os.cpu_count() or 1
     per_step = max(0.25, min(args.cpu_budget, REF_TOTAL_BUDGET_S / (args.steps + args.warmup + 2)))
-    rows, kind = cpu_calibrate(cases, budget_s=per_step, threads=threads)
+    rows, kind = cpu_calibrate(ops, budget_s=per_step, threads=threads)
     sample = ""
     for _ in range(args.warmup):
-        cpu_sample_time(cases, rows, kind, threads)
+        cpu_sample_time(ops, rows, kind, threads)
     tot_f = tot_t = 0.0
     for _ in range(args.steps):
-        f, t, sample = cpu_sample_time(cases, rows, kind, threads)
+        f, t, sample = cpu_sample_time(ops, rows, kind, threads)
         tot_f += f
         tot_t += t
     v = tot_f / tot_t / 1e12
-    out = {"impl": "reference", "metric": METRIC, "value": v, "unit": "TFLOP/s", "n_gpus": ws,
-           "steps": args.steps, "warmup": args.warmup,
-           "ms_per_step": tot_t / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
-           "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-           "config": {"workload": WORKLOAD_SWEEP, "strategy": "cpu golden"},
+    out = {"impl": "reference", "metric": METRICS[args.workload], "value": v, "unit": "TFLOP/s",
+           "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
+           "ms_per_step": tot_t / args.steps * 1e3, "higher_is_better": True,
+           "scaling": "strong" if args.workload == "cfg5" else "weak", "vs_baseline": None,
+           "dtype": "bf16", "data": "synthetic",
+           "config": {"workload": WORKLOAD_DESC[args.workload], "name": args.workload,
+                      "strategy": "cpu golden"},
            "cpu_baseline": {"value": v, "unit": "TFLOP/s", "cores": threads, "kind": kind,
-                            "sample": sample + " of each density, every step"},
+                            "sample": sample + ", every step"},
            "e2e": {"value": v, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(out), flush=True)
 
@@ -456,7 +773,8 @@ def main():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="bsp", choices=["bsp", "reference"])
-    ap.add_argument("--strategy", default="dda", choices=["naive", "snf", "dda"])
+    ap.add_argument("--workload", default="sweep", choices=list(WORKLOAD_DESC))
+    ap.add_argument("--strategy", default="auto", choices=["auto", "naive", "snf", "dda"])
     ap.add_argument("--cpu-budget", type=float, default=12.0)
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--no-cpu", action="store_true")

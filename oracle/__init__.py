@@ -129,14 +129,17 @@ def spmm_f32(indptr, indices, data, H, W, R, C, B, N):
     return out
 
 
-def sddmm_bf16(indptr, indices, mask_data, H, W, R, C, A, B, K, threads=None):
-    """out_blocks = mask (.) (A @ B) on the mask pattern, bf16 bits."""
+def sddmm_bf16(indptr, indices, mask_data, H, W, R, C, A, B, K, threads=None, rows=None):
+    """out_blocks = mask (.) (A @ B) on the mask pattern, bf16 bits (only the
+    blocks of block-rows ``rows`` = (r0, r1) are computed when given)."""
     indptr, indices = _c(indptr, np.int32), _c(indices, np.int32)
-    mask_data, A, B = _c(mask_data, np.uint16), _c(A, np.uint16), _c(B, np.uint16)
+    mask_data = None if mask_data is None else _c(mask_data, np.uint16)
+    A, B = _c(A, np.uint16), _c(B, np.uint16)
     nnzb = int(indptr[-1])
     out = np.zeros(nnzb * R * C, dtype=np.uint16)
+    r0, r1 = rows if rows is not None else (0, H // R)
     lib().bsp_oracle_sddmm_bf16_mt(H, W, R, C, _ptr(indptr), _ptr(indices), _ptr(mask_data), K,
-                                   _ptr(A), _ptr(B), _ptr(out), 0, H // R,
+                                   _ptr(A), _ptr(B), _ptr(out), r0, r1,
                                    threads or os.cpu_count() or 1)
     return out
 

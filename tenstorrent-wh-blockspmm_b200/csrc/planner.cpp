@@ -375,7 +375,7 @@ bsp_status plan_spmm_rowstack(bsp_spmm_plan* p, const int32_t* row_ptr, const in
   // carries two consecutive steps so that each hand-off moves four MMAs:
   // on B200 that beats the deeper one-step ring at every density from 5%.
   int nsub = 1;
-  if (nkc == 1 && o.steps_per_stage != 1) nsub = 2;
+  if (kc == 32 && nkc == 1 && o.steps_per_stage != 1) nsub = 2;
   const int sub_bytes = 4 * kc * 128 + G * Rs * kc * 2;
   p->sub_bytes = sub_bytes;
   p->nsub = nsub;

@@ -30,7 +30,9 @@ bsp_status bsp_spmm_plan_inspect(int64_t M, int64_t K, int32_t R, int32_t C, int
                                  int32_t* steps_out, int32_t* stage_list_out,
                                  int32_t* cta_stage_begin_out);
 
-/* units_out[info[0] * 12] (row, r_off, nseg, pad, blk[4], col[4] per unit). */
+/* units_out[info[0] * info[12]]: info[11] == 0 (swap-AB kernel): 12 words per
+ * unit (row, r_off, nseg, pad, blk[4], col[4]); info[11] == 1 (row-stacked
+ * kernel): 44 words per unit (row0, nseg, pad[2], seg_col[8], blk[4][8]). */
 bsp_status bsp_sddmm_plan_inspect(int64_t M, int64_t N, int32_t R, int32_t C, int64_t nnzb,
                                   const int32_t* row_ptr, const int32_t* col_idx, int64_t K,
                                   bsp_strategy strategy, const bsp_sddmm_opts* opts,

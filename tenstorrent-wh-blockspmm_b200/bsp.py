@@ -323,7 +323,7 @@ class SddmmPlan:
         arr = (ctypes.c_int64 * 16)()
         _check(lib().bsp_sddmm_plan_info(self.handle, arr))
         keys = ["units", "ctas", "_2", "_3", "slab", "kc", "stages", "_7", "plan_bytes",
-                "smem_bytes", "tmem_cols"]
+                "smem_bytes", "tmem_cols", "variant", "_12", "nseg_max", "producers"]
         return {k: int(arr[i]) for i, k in enumerate(keys) if not k.startswith("_")}
 
     def execute(self, mask: DeviceBSR, A, B, out, stream=None):
@@ -410,11 +410,12 @@ def inspect_sddmm_plan(M, N, R, C, row_ptr, col_idx, K, strategy=NAIVE, opts=Non
     args = (M, N, R, C, int(rp[-1]), _ptr(rp), _ptr(ci), K, strategy, ctypes.byref(o), sm_count,
             max_smem, _ptr(info))
     _check(lib().bsp_sddmm_plan_inspect(*args, None, None))
-    units = np.zeros((int(info[0]), 12), np.int32)
+    units = np.zeros((max(int(info[0]), 1), int(info[12])), np.int32)
     cta = np.zeros(int(info[1]) + 1, np.int32)
     _check(lib().bsp_sddmm_plan_inspect(*args, _ptr(units), _ptr(cta)))
     return dict(units=int(info[0]), ctas=int(info[1]), slab=int(info[4]), kc=int(info[5]),
-                stages=int(info[6]), unit_table=units, cta_begin=cta)
+                stages=int(info[6]), variant=int(info[11]), nseg_max=int(info[13]),
+                producers=int(info[14]), unit_table=units[: int(info[0])], cta_begin=cta)
 
 
 def partition_rows(row_ptr: np.ndarray, parts: int) -> np.ndarray:

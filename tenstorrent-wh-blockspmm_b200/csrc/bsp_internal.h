@@ -94,6 +94,20 @@ struct SddmmUnit {
 };
 static_assert(sizeof(SddmmUnit) == 48, "unit layout");
 
+// Row-stacked SDDMM work unit: 128 consecutive output rows (4 slabs of 32,
+// one TMA box of A) against up to 8 gathered 32-column segments of B.  The
+// MMA computes the full 128 x (32 * nseg) tile; the epilogue keeps the
+// (slab, segment) pairs that the mask holds.
+constexpr int kSddmmRsMaxSeg = 8;
+struct SddmmRsUnit {
+  int32_t row0;                   // first output row (a multiple of 128)
+  int32_t nseg;                   // segments used (1..8)
+  int32_t pad[2];
+  int32_t seg_col[kSddmmRsMaxSeg];  // first column of each segment (j*C + c0), -1 unused
+  int32_t blk[4][kSddmmRsMaxSeg];   // mask block holding (slab q, segment s), -1 none
+};
+static_assert(sizeof(SddmmRsUnit) == 176, "unit layout");
+
 struct SddmmKernelParams {
   CUtensorMap tm_a;  // A [M rows, K cols] bf16, box {kc, Rs}
   CUtensorMap tm_b;  // B [K rows, N cols] bf16, box {32, kc}, 64B swizzle
@@ -108,6 +122,9 @@ struct SddmmKernelParams {
   int32_t a_swizzle_mode;
   int32_t tmem_cols;
   int32_t keep_a;  // DDA: A slab of the row stays resident across units of a row run
+  // row-stacked variant
+  const SddmmRsUnit* rs_units;
+  int32_t M, nseg_max, nprod, seg_bytes;
 };
 
 // ---- host objects -------------------------------------------------------------
@@ -180,6 +197,10 @@ struct bsp_sddmm_plan {
   int32_t* d_cta_begin = nullptr;
   std::vector<bsp::SddmmUnit> h_units;
   std::vector<int32_t> h_cta_begin;
+  // variant 1: row-stacked kernel (sddmm_rowstack.cu)
+  int32_t variant = 0, nseg_max = 0, nprod = 0;
+  bsp::SddmmRsUnit* d_rs_units = nullptr;
+  std::vector<bsp::SddmmRsUnit> h_rs_units;
 };
 
 namespace bsp {
@@ -200,6 +221,13 @@ bsp_status launch_spmm(const bsp_spmm_plan* p, const bsp_bsr_desc* A, const void
                        void* C, int64_t ldc, cudaStream_t stream);
 bsp_status launch_sddmm(const bsp_sddmm_plan* p, const bsp_bsr_desc* mask, const void* A,
                         int64_t lda, const void* B, int64_t ldb, void* out, cudaStream_t stream);
+bsp_status launch_sddmm_rowstack(const bsp_sddmm_plan* p, const bsp_bsr_desc* mask, const void* A,
+                                 int64_t lda, const void* B, int64_t ldb, void* out,
+                                 cudaStream_t stream);
+bsp_status plan_sddmm_rowstack(bsp_sddmm_plan* p, const int32_t* row_ptr, const int32_t* col_idx,
+                               int sm_count, int max_smem, const bsp_sddmm_opts* opts);
+int sddmm_rowstack_max_stages();
+int sddmm_rowstack_max_producers();
 bsp_status encode_2d(bsp_device* dev, CUtensorMap* tm, CUtensorMapDataType dt, int esize,
                      const void* ptr, uint64_t inner, uint64_t outer, uint64_t row_stride_elems,
                      uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swz);

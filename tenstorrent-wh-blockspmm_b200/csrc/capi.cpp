@@ -478,7 +478,8 @@ bsp_status bsp_sddmm_plan_create(bsp_device* dev, const bsp_bsr_desc* mask,
   }
   std::vector<void*> ptrs;
   s = upload_blob({{p->h_units.data(), p->h_units.size() * sizeof(SddmmUnit)},
-                   {p->h_cta_begin.data(), p->h_cta_begin.size() * sizeof(int32_t)}},
+                   {p->h_cta_begin.data(), p->h_cta_begin.size() * sizeof(int32_t)},
+                   {p->h_rs_units.data(), p->h_rs_units.size() * sizeof(SddmmRsUnit)}},
                   &p->d_blob, &p->blob_bytes, &ptrs);
   if (s != BSP_OK) {
     delete p;
@@ -486,6 +487,7 @@ bsp_status bsp_sddmm_plan_create(bsp_device* dev, const bsp_bsr_desc* mask,
   }
   p->d_units = static_cast<SddmmUnit*>(ptrs[0]);
   p->d_cta_begin = static_cast<int32_t*>(ptrs[1]);
+  p->d_rs_units = static_cast<SddmmRsUnit*>(ptrs[2]);
   *out = p;
   return BSP_OK;
 }
@@ -525,6 +527,10 @@ bsp_status bsp_sddmm_plan_info(const bsp_sddmm_plan* p, int64_t info[16]) {
   info[8] = static_cast<int64_t>(p->blob_bytes);
   info[9] = p->smem_bytes;
   info[10] = p->tmem_cols;
+  info[11] = p->variant;
+  info[12] = static_cast<int64_t>((p->variant == 1 ? sizeof(SddmmRsUnit) : sizeof(SddmmUnit)) / 4);
+  info[13] = p->nseg_max;
+  info[14] = p->nprod;
   return BSP_OK;
 }
 
@@ -720,7 +726,10 @@ bsp_status bsp_sddmm_plan_inspect(int64_t M, int64_t N, int32_t R, int32_t C, in
   bsp_status s = plan_sddmm_host(&p, row_ptr, col_idx, sm_count, max_smem, opts);
   if (s != BSP_OK) return s;
   bsp_sddmm_plan_info(&p, info);
-  if (units_out) memcpy(units_out, p.h_units.data(), p.h_units.size() * sizeof(SddmmUnit));
+  if (units_out) {
+    if (p.variant == 1) memcpy(units_out, p.h_rs_units.data(), p.h_rs_units.size() * sizeof(SddmmRsUnit));
+    else memcpy(units_out, p.h_units.data(), p.h_units.size() * sizeof(SddmmUnit));
+  }
   if (cta_begin_out)
     memcpy(cta_begin_out, p.h_cta_begin.data(), p.h_cta_begin.size() * sizeof(int32_t));
   return BSP_OK;

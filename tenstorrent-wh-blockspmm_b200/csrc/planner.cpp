@@ -11,6 +11,7 @@
 //
 // Nothing here touches the GPU, so every branch is testable on CPU.
 #include <algorithm>
+#include <climits>
 #include <cstring>
 #include <numeric>
 #include <string>
@@ -495,6 +496,10 @@ bsp_status plan_sddmm_host(bsp_sddmm_plan* p, const int32_t* row_ptr, const int3
   if (p->strategy != BSP_NAIVE && p->strategy != BSP_DDA && p->strategy != BSP_SNF)
     return set_error(BSP_ERR_INVALID_ARG, "unknown strategy");
 
+  // Default: the row-stacked kernel (N = 128/256 MMAs).  group_mma == 2 keeps
+  // the swap-AB kernel (one 4-segment unit per block-row slab).
+  if (o.group_mma != 2) return plan_sddmm_rowstack(p, row_ptr, col_idx, sm_count, max_smem, &o);
+  p->variant = 0;
   const int Rs = slab_height(R);
   const int kc = (K % 64 == 0) ? 64 : 32;
   p->Rs = Rs;
@@ -550,6 +555,173 @@ bsp_status plan_sddmm_host(bsp_sddmm_plan* p, const int32_t* row_ptr, const int3
   p->stages = stages;
   p->smem_bytes = sddmm_smem_bytes(stages, stage_bytes);
   p->tmem_cols = pow2_at_least(2 * Rs);
+  p->timeout_ns = static_cast<uint64_t>(o.timeout_ms > 0 ? o.timeout_ms : 2000) * 1000000ull;
+  return BSP_OK;
+}
+
+// Row-stacked SDDMM schedule.  Output rows are taken 128 at a time (one TMA
+// box of A, four 32-row slabs = TMEM lane quarters).  For each such group the
+// union of the mask's block-columns over the block-rows it touches is cut
+// into 32-column segments, and the segments into units of nseg_max (4 or 8,
+// MMA N = 128 or 256).  blk[q][s] names the mask block that slab q of
+// segment s lands in (-1: not in the mask; the tile is computed but not
+// written).  A block-column repeated within one mask row gets a second layer
+// of units, so every output block is written exactly once.
+bsp_status plan_sddmm_rowstack(bsp_sddmm_plan* p, const int32_t* row_ptr, const int32_t* col_idx,
+                               int sm_count, int max_smem, const bsp_sddmm_opts* opts) {
+  const bsp_sddmm_opts& o = *opts;
+  const int64_t M = p->M, K = p->K;
+  const int R = p->R, C = p->C;
+  const int kc = (K % 64 == 0) ? 64 : 32;
+  const int nkc = static_cast<int>(K / kc);
+  p->variant = 1;
+  p->Rs = 32;
+  p->kc = kc;
+  p->keep_a = 0;
+  const int64_t ngroups = (M + 127) / 128;
+  const int segs_per_block = C / 32;
+
+  // (block-column, block index) of every mask block of block-row br, sorted
+  // by column (stable: repeated columns keep their order, one layer each).
+  auto row_pairs = [&](int64_t br, std::vector<std::pair<int32_t, int32_t>>* out) {
+    out->clear();
+    for (int32_t b = row_ptr[br]; b < row_ptr[br + 1]; ++b) out->push_back({col_idx[b], b});
+    std::stable_sort(out->begin(), out->end(),
+                     [](const std::pair<int32_t, int32_t>& x, const std::pair<int32_t, int32_t>& y) {
+                       return x.first < y.first;
+                     });
+  };
+  struct GroupSegs {
+    int64_t g;
+    int layer;
+    std::vector<int32_t> cols;  // block-columns of this layer, ascending
+  };
+  std::vector<GroupSegs> layers;
+  std::vector<std::vector<std::pair<int32_t, int32_t>>> slab_pairs(4);
+  std::vector<int64_t> slab_br(4);
+  int64_t units8 = 0, units4 = 0;
+  std::vector<std::vector<std::pair<int32_t, int32_t>>> group_rows;
+  for (int64_t g = 0; g < ngroups; ++g) {
+    const int64_t r_lo = g * 128, r_hi = std::min<int64_t>(M, r_lo + 128);
+    const int64_t br0 = r_lo / R, br1 = (r_hi - 1) / R + 1;
+    group_rows.assign(static_cast<size_t>(br1 - br0), {});
+    int max_layer = 0;
+    for (int64_t br = br0; br < br1; ++br) {
+      auto& v = group_rows[static_cast<size_t>(br - br0)];
+      row_pairs(br, &v);
+      int run = 0;
+      for (size_t k = 0; k < v.size(); ++k) {
+        run = (k > 0 && v[k].first == v[k - 1].first) ? run + 1 : 0;
+        max_layer = std::max(max_layer, run);
+      }
+    }
+    for (int layer = 0; layer <= max_layer; ++layer) {
+      GroupSegs gs;
+      gs.g = g;
+      gs.layer = layer;
+      for (const auto& v : group_rows) {
+        int run = 0;
+        for (size_t k = 0; k < v.size(); ++k) {
+          run = (k > 0 && v[k].first == v[k - 1].first) ? run + 1 : 0;
+          if (run == layer) gs.cols.push_back(v[k].first);
+        }
+      }
+      std::sort(gs.cols.begin(), gs.cols.end());
+      gs.cols.erase(std::unique(gs.cols.begin(), gs.cols.end()), gs.cols.end());
+      if (gs.cols.empty()) continue;
+      const int64_t nseg = static_cast<int64_t>(gs.cols.size()) * segs_per_block;
+      units8 += (nseg + 7) / 8;
+      units4 += (nseg + 3) / 4;
+      layers.push_back(std::move(gs));
+    }
+  }
+  int nseg_max = 8;
+  if (o.n_tiles == 1) nseg_max = 4;
+  else if (o.n_tiles == 0 && units8 < sm_count && units4 > units8) nseg_max = 4;
+  p->nseg_max = nseg_max;
+
+  std::vector<SddmmRsUnit> units;
+  std::vector<int64_t> weight;
+  for (const GroupSegs& gs : layers) {
+    const int64_t row0 = gs.g * 128;
+    // per slab q: the (column, block) pairs of this layer
+    for (int q = 0; q < 4; ++q) {
+      slab_pairs[q].clear();
+      const int64_t row = row0 + 32 * q;
+      slab_br[q] = row < M ? row / R : -1;
+      if (slab_br[q] < 0) continue;
+      std::vector<std::pair<int32_t, int32_t>> v;
+      row_pairs(slab_br[q], &v);
+      int run = 0;
+      for (size_t k = 0; k < v.size(); ++k) {
+        run = (k > 0 && v[k].first == v[k - 1].first) ? run + 1 : 0;
+        if (run == gs.layer) slab_pairs[q].push_back(v[k]);
+      }
+    }
+    std::vector<int32_t> segs;
+    for (int32_t j : gs.cols)
+      for (int c0 = 0; c0 < C; c0 += 32) segs.push_back(static_cast<int32_t>(int64_t(j) * C + c0));
+    for (size_t s0 = 0; s0 < segs.size(); s0 += nseg_max) {
+      SddmmRsUnit u;
+      memset(&u, 0, sizeof(u));
+      u.row0 = static_cast<int32_t>(row0);
+      u.nseg = static_cast<int32_t>(std::min<size_t>(nseg_max, segs.size() - s0));
+      for (int s_ = 0; s_ < kSddmmRsMaxSeg; ++s_) {
+        u.seg_col[s_] = s_ < u.nseg ? segs[s0 + s_] : -1;
+        for (int q = 0; q < 4; ++q) {
+          u.blk[q][s_] = -1;
+          if (s_ >= u.nseg || slab_br[q] < 0) continue;
+          const int32_t j = u.seg_col[s_] / C;
+          const auto& sp = slab_pairs[q];
+          auto it = std::lower_bound(sp.begin(), sp.end(), std::make_pair(j, INT32_MIN));
+          if (it != sp.end() && it->first == j) u.blk[q][s_] = it->second;
+        }
+      }
+      units.push_back(u);
+      weight.push_back(static_cast<int64_t>(u.nseg) * nkc + 2);
+    }
+  }
+  int grid = o.max_ctas > 0 ? std::min(o.max_ctas, sm_count) : sm_count;
+  grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(grid, units.size())));
+  std::vector<std::vector<int32_t>> per;
+  if (o.no_load_balance || p->strategy == BSP_DDA) {
+    // CDA: a row group's units stay together on one CTA (A rows reused from L2)
+    contiguous_split(static_cast<int64_t>(units.size()), grid, &per);
+  } else {
+    serpentine_order(weight, grid, &per);
+  }
+  p->h_units.clear();
+  p->h_rs_units.clear();
+  p->h_cta_begin.assign(1, 0);
+  for (int c = 0; c < grid; ++c) {
+    for (int32_t idx : per[c]) p->h_rs_units.push_back(units[idx]);
+    p->h_cta_begin.push_back(static_cast<int32_t>(p->h_rs_units.size()));
+  }
+  p->n_units = static_cast<int64_t>(units.size());
+  p->grid = grid;
+
+  int stage_bytes = 128 * kc * 2 + nseg_max * kc * 64;
+  stage_bytes = (stage_bytes + 1023) / 1024 * 1024;
+  const int max_stages = std::min(sddmm_rowstack_max_stages(), (max_smem - 2048) / stage_bytes);
+  if (max_stages < 2) return set_error(BSP_ERR_UNSUPPORTED, "stage too large for the pipeline");
+  int nprod = 1, stages = max_stages;
+  if (o.producers > 0) {
+    nprod = std::min({o.producers, sddmm_rowstack_max_producers(), max_stages});
+    stages = max_stages / nprod * nprod;
+  } else {
+    for (int q = 2; q <= std::min(sddmm_rowstack_max_producers(), max_stages); ++q) {
+      const int sq = max_stages / q * q;
+      if (sq >= stages - (stages > 6 ? 1 : 0)) {
+        nprod = q;
+        stages = sq;
+      }
+    }
+  }
+  p->nprod = nprod;
+  p->stage_bytes = stage_bytes;
+  p->stages = stages;
+  p->smem_bytes = 2048 + stages * stage_bytes;
+  p->tmem_cols = pow2_at_least(2 * 32 * nseg_max);
   p->timeout_ns = static_cast<uint64_t>(o.timeout_ms > 0 ? o.timeout_ms : 2000) * 1000000ull;
   return BSP_OK;
 }

@@ -238,6 +238,7 @@ int sddmm_smem_bytes(int stages, int stage_bytes) { return 1024 + 1024 + stages 
 
 bsp_status launch_sddmm(const bsp_sddmm_plan* p, const bsp_bsr_desc* mask, const void* A,
                         int64_t lda, const void* B, int64_t ldb, void* out, cudaStream_t stream) {
+  if (p->variant == 1) return launch_sddmm_rowstack(p, mask, A, lda, B, ldb, out, stream);
   if (p->n_units == 0) return BSP_OK;
   bsp_device* dev = p->dev;
   SddmmKernelParams kp;

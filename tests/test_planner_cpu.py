@@ -128,13 +128,65 @@ def _check_stage_list(plan, rp, ci, R, C, Rs, slabs, G):
         assert k == len(rows)
 
 
+def _sddmm_rowstack_keys(plan, rp, ci, R, C):
+    """(block, column in block, row in block) of every 32x32 output tile the
+    row-stacked schedule writes, with multiplicity."""
+    seen = {}
+    for u in plan["unit_table"]:
+        row0, nseg = int(u[0]), int(u[1])
+        assert row0 % 128 == 0 and 1 <= nseg <= plan["nseg_max"] <= 8
+        seg_col = u[4:12]
+        blk = u[12:44].reshape(4, 8)
+        assert all(seg_col[s] >= 0 and seg_col[s] % 32 == 0 for s in range(nseg))
+        assert all(seg_col[s] == -1 for s in range(nseg, 8))
+        for q in range(4):
+            for s in range(8):
+                b = int(blk[q, s])
+                if b < 0:
+                    continue
+                assert s < nseg
+                br = (row0 + 32 * q) // R
+                assert rp[br] <= b < rp[br + 1]
+                assert ci[b] == seg_col[s] // C
+                key = (b, int(seg_col[s]) % C, (row0 + 32 * q) % R)
+                seen[key] = seen.get(key, 0) + 1
+    return seen
+
+
+@pytest.mark.parametrize("strategy", ["naive", "dda"])
+@pytest.mark.parametrize("R,C,K", [(32, 32, 256), (64, 32, 96), (32, 96, 64), (512, 64, 128)])
+def test_sddmm_rowstack_schedule_covers_every_tile_once(strategy, R, C, K):
+    M, N = 4 * max(R, 128), 8 * C
+    rng = np.random.default_rng(R * 7 + C)
+    rp, ci, _ = rand_bsr(rng, M, N, R, C, 0.4)
+    plan = bsp.inspect_sddmm_plan(M, N, R, C, rp, ci, K, bsp.STRATEGIES[strategy])
+    assert plan["variant"] == 1
+    seen = _sddmm_rowstack_keys(plan, rp, ci, R, C)
+    assert len(seen) == int(rp[-1]) * (C // 32) * (R // 32)
+    assert all(v == 1 for v in seen.values())
+    assert plan["cta_begin"][-1] == plan["units"]
+
+
+def test_sddmm_rowstack_repeated_columns_get_their_own_layer():
+    R = C = 32
+    M, N = 256, 256
+    rp = np.array([0, 3, 3, 5, 5, 5, 5, 5, 7], np.int32)
+    ci = np.array([2, 2, 5, 1, 1, 7, 7], np.int32)   # repeats in rows 0, 2 and 7
+    for n_tiles in (0, 1, 2):
+        plan = bsp.inspect_sddmm_plan(M, N, R, C, rp, ci, 64, bsp.NAIVE, opts=bsp.make_opts(n_tiles=n_tiles))
+        seen = _sddmm_rowstack_keys(plan, rp, ci, R, C)
+        assert len(seen) == int(rp[-1]) and all(v == 1 for v in seen.values())
+
+
 @pytest.mark.parametrize("strategy", ["naive", "dda"])
 @pytest.mark.parametrize("R,C,K", [(32, 32, 256), (64, 32, 96), (32, 96, 64), (512, 64, 128)])
 def test_sddmm_schedule_covers_every_segment_once(strategy, R, C, K):
     M, N = 4 * max(R, 128), 8 * C
     rng = np.random.default_rng(R * 7 + C)
     rp, ci, _ = rand_bsr(rng, M, N, R, C, 0.4)
-    plan = bsp.inspect_sddmm_plan(M, N, R, C, rp, ci, K, bsp.STRATEGIES[strategy])
+    plan = bsp.inspect_sddmm_plan(M, N, R, C, rp, ci, K, bsp.STRATEGIES[strategy],
+                                  opts=bsp.make_opts(group_mma=2))
+    assert plan["variant"] == 0
     seen = {}
     Rs = plan["slab"]
     for u in plan["unit_table"]:

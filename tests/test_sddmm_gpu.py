@@ -31,16 +31,22 @@ CASES = [
 ]
 
 
-def _run(bsp, M, N, K, R, C, rp, ci, mv, A, B, strategy):
+# kernel variants: the row-stacked kernel (default; N = 256 or 128 MMAs) and
+# the swap-AB kernel (one 4-segment unit per block-row slab, group_mma = 2)
+KERNELS = {"rowstack": {}, "rowstack_n128": {"n_tiles": 1}, "swapab": {"group_mma": 2}}
+
+
+def _run(bsp, M, N, K, R, C, rp, ci, mv, A, B, strategy, kernel="rowstack"):
     mask = bsp.DeviceBSR.from_host(M, N, R, C, rp, ci, mv)
     out = bsp.sddmm(mask, bsp.to_device_bf16(A), bsp.to_device_bf16(B),
-                    strategy=bsp.STRATEGIES[strategy])
+                    strategy=bsp.STRATEGIES[strategy], opts=bsp.make_opts(**KERNELS[kernel]))
     return bsp.to_host_bits(out)
 
 
 @pytest.mark.parametrize("case", CASES, ids=[f"{c[0]}x{c[1]}xK{c[2]}_R{c[3]}C{c[4]}_m{int(c[6])}" for c in CASES])
 @pytest.mark.parametrize("strategy", STRATS)
-def test_sddmm_parity(case, strategy):
+@pytest.mark.parametrize("kernel", list(KERNELS))
+def test_sddmm_parity(case, strategy, kernel):
     import bsp
 
     M, N, K, R, C, p, with_vals = case
@@ -51,10 +57,28 @@ def test_sddmm_parity(case, strategy):
     A = rand_dense(rng, M, K, "normal", 1 / 16)
     B = rand_dense(rng, K, N, "normal", 1 / 16)
     gold = oracle.sddmm_bf16(rp, ci, mv, M, N, R, C, A, B, K)
-    out = _run(bsp, M, N, K, R, C, rp, ci, mv, A, B, strategy)
-    assert_bf16_close(out, gold, what=f"{case} {strategy}")
+    out = _run(bsp, M, N, K, R, C, rp, ci, mv, A, B, strategy, kernel)
+    assert_bf16_close(out, gold, what=f"{case} {strategy} {kernel}")
     if gold.size > 1:
         assert pcc(oracle.bf16_to_f32(out), oracle.bf16_to_f32(gold)) > 0.99
+
+
+@pytest.mark.parametrize("kernel", list(KERNELS))
+def test_sddmm_repeated_columns_and_partial_row_group(kernel):
+    """A mask row naming one block-column twice gets both output blocks; 160
+    rows leave the last 128-row group a quarter full."""
+    import bsp
+
+    M, N, K, R, C = 160, 256, 96, 32, 32
+    rp = np.array([0, 3, 3, 5, 6, 8], np.int32)
+    ci = np.array([2, 2, 5, 1, 1, 7, 0, 0], np.int32)
+    rng = np.random.default_rng(11)
+    mv = oracle.f32_to_bf16(rng.uniform(-2, 2, ci.size * R * C).astype(np.float32))
+    A = rand_dense(rng, M, K, "normal", 1 / 8)
+    B = rand_dense(rng, K, N, "normal", 1 / 8)
+    gold = oracle.sddmm_bf16(rp, ci, mv, M, N, R, C, A, B, K)
+    out = _run(bsp, M, N, K, R, C, rp, ci, mv, A, B, "naive", kernel)
+    assert_bf16_close(out, gold, what=f"repeated columns {kernel}")
 
 
 @pytest.mark.parametrize("strategy", STRATS)

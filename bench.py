@@ -533,12 +533,16 @@ def run_bsp(args):
 
         op = ops[0]
         shard = bsp_dist.ShardedSpmm(dev, op["M"], op["K"], op["R"], op["C"], op["rp"], op["ci"],
-                                     op["vals"], op["N"], rank, ws, strategy_for(op, args.strategy))
+                                     op["vals"], op["N"], rank, ws, strategy_for(op, args.strategy),
+                                     fused=not args.nccl_exchange if ws > 1 else None)
         Bd = bsp.to_device_bf16(op["B"], local)
         Cfull = torch.empty((op["M"], op["N"]), dtype=torch.bfloat16, device="cuda")
+        shard.attach(Cfull)
+        kname = ("spmm_rowstack_tcgen05 (epilogue stores each C tile into every GPU's C over NVLink)"
+                 if shard.fused else "spmm_rowstack_tcgen05 + NCCL send/recv of C row-panels")
         runs = [dict(op=op, flops=shard.flops, bytes=op_bytes(op), times=[], name=op["name"],
-                     fn=lambda s: shard.run(Bd, Cfull, s, replicate=ws > 1),
-                     kernel="spmm_rowstack_tcgen05 + NCCL exchange of C row-panels")]
+                     fn=lambda s: shard.run(Bd, Cfull, s, replicate=ws > 1, sync_before=False),
+                     kernel=kname)]
     else:
         runs = []
         for op in ops:
@@ -546,9 +550,16 @@ def run_bsp(args):
             runs.append(dict(op=op, dev=d, flops=op_flops(op), bytes=op_bytes(op), times=[],
                              name=op["name"], fn=d.run, kernel=d.kernel(), plan=d.plan.info()))
 
+    sync = torch.zeros(1, dtype=torch.float32, device="cuda") if (sharded and dist is not None) else None
+
     def step(record):
         for r in runs:
             flush.zero_()
+            if sync is not None:
+                # line the ranks' streams up (outside the timed events): every
+                # rank's step then starts together and no rank's time includes
+                # waiting for a peer that is still flushing
+                dist.all_reduce(sync)
             if record:
                 e0 = torch.cuda.Event(enable_timing=True)
                 e1 = torch.cuda.Event(enable_timing=True)
@@ -669,6 +680,7 @@ def run_e2e(args, runs, dev, dist, shard):
         hout = torch.empty((op["M"], op["N"]), dtype=torch.int16).pin_memory()
         Bd = torch.empty((op["K"], op["N"]), dtype=torch.bfloat16, device="cuda")
         Cfull = torch.empty((op["M"], op["N"]), dtype=torch.bfloat16, device="cuda")
+        shard.attach(Cfull)   # collective: map the peers' copies of this C
         h2d = hB.numel() * 2 + (hv.numel() * 2 if hv is not None else 0)
         d2h = hout.numel() * 2
 
@@ -778,6 +790,8 @@ def main():
     ap.add_argument("--cpu-budget", type=float, default=12.0)
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--nccl-exchange", action="store_true",
+                    help="cfg5 with N > 1: exchange C panels by NCCL send/recv instead of the fused kernel")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -138,6 +138,28 @@ bsp_status bsp_spmm_plan_create(bsp_device* dev, const bsp_bsr_desc* A, const in
 bsp_status bsp_spmm_execute(const bsp_spmm_plan* plan, const bsp_bsr_desc* A, const void* B,
                             int64_t ldb, void* C, int64_t ldc, void* stream);
 bsp_status bsp_spmm_plan_destroy(bsp_spmm_plan* plan);
+
+/* Multi-GPU row-panel SpMM with the all-gather fused into the kernel.  No
+ * counterpart in the reference (it runs on one card).  Same as
+ * bsp_spmm_execute, and every C element the kernel writes is also stored into
+ * each of the n_peers (<= 7) other GPUs' C buffers, peer_C[i] pointing at the
+ * element of the peer's C that corresponds to C[0][0] (same ldc), mapped into
+ * this process over NVLink (bsp_ipc_import).  With A's block-rows split across
+ * the GPUs, each GPU then ends with the whole C without a separate collective;
+ * the caller synchronises the GPUs afterwards (any collective on the same
+ * stream) before reading C.  DDA (row-stacked) plans only. */
+bsp_status bsp_spmm_execute_replicated(const bsp_spmm_plan* plan, const bsp_bsr_desc* A, const void* B,
+                                       int64_t ldb, void* C, int64_t ldc, void* const* peer_C,
+                                       int32_t n_peers, void* stream);
+
+/* CUDA IPC of device buffers between the processes of one node (one process
+ * per GPU).  export: 64-byte handle of the allocation holding ptr, and ptr's
+ * byte offset in it; import: map a peer's allocation, returns its base (add
+ * the peer's offset); close: unmap. */
+#define BSP_IPC_HANDLE_BYTES 64
+bsp_status bsp_ipc_export(bsp_device* dev, const void* ptr, void* handle_out, int64_t* offset_out);
+bsp_status bsp_ipc_import(bsp_device* dev, const void* handle, void** base_out);
+bsp_status bsp_ipc_close(bsp_device* dev, void* base);
 /* Plan facts: [0]=units [1]=ctas [2]=group_rows [3]=n_tiles [4]=sub-row height
  * [5]=k chunk [6]=pipeline stages [7]=steps [8]=plan device bytes. */
 bsp_status bsp_spmm_plan_info(const bsp_spmm_plan* plan, int64_t info[16]);

@@ -31,8 +31,10 @@ EXPORTS = [
     "bsp_sddmm_plan_info", "bsp_sddmm", "bsp_sddmm_host",
     "bsp_partition_rows", "bsp_serpentine_assign", "bsp_spmm_host_profile",
     "bsp_sddmm_host_profile", "bsp_spmm_plan_inspect", "bsp_sddmm_plan_inspect",
-    "bsp_spmm_noalloc",
+    "bsp_spmm_noalloc", "bsp_spmm_execute_replicated", "bsp_ipc_export", "bsp_ipc_import",
+    "bsp_ipc_close",
 ]
+IPC_HANDLE_BYTES = 64
 
 
 class BspError(RuntimeError):
@@ -107,6 +109,11 @@ def lib():
         "bsp_spmm_plan_inspect": (S, [I64, I64, I32, I32, I64, P, P, I64, S, S, ctypes.POINTER(Opts),
                                       I32, I32, P, P, P, P, P, P]),
         "bsp_spmm_noalloc": (S, [ctypes.POINTER(BsrDesc), P, P, P, I64, P, I64, I64, S, S, P]),
+        "bsp_spmm_execute_replicated": (S, [P, ctypes.POINTER(BsrDesc), P, I64, P, I64,
+                                            ctypes.POINTER(ctypes.c_void_p), I32, P]),
+        "bsp_ipc_export": (S, [P, P, P, ctypes.POINTER(ctypes.c_int64)]),
+        "bsp_ipc_import": (S, [P, P, ctypes.POINTER(ctypes.c_void_p)]),
+        "bsp_ipc_close": (S, [P, P]),
         "bsp_sddmm_plan_inspect": (S, [I64, I64, I32, I32, I64, P, P, I64, S, ctypes.POINTER(Opts),
                                        I32, I32, P, P, P]),
     }
@@ -266,6 +273,15 @@ class SpmmPlan:
         _check(lib().bsp_spmm_execute(self.handle, ctypes.byref(d), _ptr(B), B.stride(0), _ptr(C),
                                       C.stride(0), _stream_ptr(stream)))
 
+    def execute_replicated(self, A: DeviceBSR, B, C, peer_ptrs, stream=None):
+        """execute(), and every C store repeated into the peers' C buffers
+        (device pointers of the element matching C[0][0] on each peer)."""
+        d = A.desc()
+        arr = (ctypes.c_void_p * max(len(peer_ptrs), 1))(*[int(x) for x in peer_ptrs])
+        _check(lib().bsp_spmm_execute_replicated(self.handle, ctypes.byref(d), _ptr(B), B.stride(0),
+                                                 _ptr(C), C.stride(0), arr, len(peer_ptrs),
+                                                 _stream_ptr(stream)))
+
     def close(self):
         if self.handle:
             lib().bsp_spmm_plan_destroy(self.handle)
@@ -416,6 +432,27 @@ def inspect_sddmm_plan(M, N, R, C, row_ptr, col_idx, K, strategy=NAIVE, opts=Non
     return dict(units=int(info[0]), ctas=int(info[1]), slab=int(info[4]), kc=int(info[5]),
                 stages=int(info[6]), variant=int(info[11]), nseg_max=int(info[13]),
                 producers=int(info[14]), unit_table=units[: int(info[0])], cta_begin=cta)
+
+
+def ipc_export(dev: Device, tensor):
+    """(64-byte handle, byte offset) that lets another process on this node map
+    the device allocation holding `tensor`."""
+    h = ctypes.create_string_buffer(IPC_HANDLE_BYTES)
+    off = ctypes.c_int64()
+    _check(lib().bsp_ipc_export(dev.handle, _ptr(tensor), h, ctypes.byref(off)))
+    return h.raw, int(off.value)
+
+
+def ipc_import(dev: Device, handle: bytes) -> int:
+    """Map a peer process's allocation into this one; returns its base address."""
+    base = ctypes.c_void_p()
+    buf = ctypes.create_string_buffer(bytes(handle), IPC_HANDLE_BYTES)
+    _check(lib().bsp_ipc_import(dev.handle, buf, ctypes.byref(base)))
+    return int(base.value)
+
+
+def ipc_close(dev: Device, base: int) -> None:
+    _check(lib().bsp_ipc_close(dev.handle, ctypes.c_void_p(base)))
 
 
 def partition_rows(row_ptr: np.ndarray, parts: int) -> np.ndarray:

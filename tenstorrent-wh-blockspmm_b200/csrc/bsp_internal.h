@@ -34,6 +34,8 @@ struct SpmmUnit {
 };
 static_assert(sizeof(SpmmUnit) == 32, "unit layout");
 
+constexpr int kMaxPeers = 7;   // one node: up to 8 GPUs
+
 struct SpmmKernelParams {
   CUtensorMap tm_a;  // A values as [nnzb*R rows, C cols] bf16, box {kc, Rs}
   CUtensorMap tm_b;  // B: 3-D {64 cols, K rows, N/64 blocks} box {64, kc, 2*NT}
@@ -60,6 +62,15 @@ struct SpmmKernelParams {
   const int4* stage_list;       // row-stacked kernel: per-CTA pipeline stages (4 x int4 each)
   const int32_t* cta_stage_begin;  // [grid + 1]
   int32_t sub_bytes;            // row-stacked: bytes of one sub-step (B slice + entry slots)
+  // Replicated output (row-stacked kernel): every C store is repeated into the
+  // n_peers other GPUs' C buffers (peer pointers mapped over NVLink, same
+  // layout and ldc), fusing the row-panel all-gather into the epilogue.
+  int32_t n_peers;
+  void* peer_c[kMaxPeers];
+  // byte offset (from the 1 KiB-aligned shared-memory base) of a 16 KiB area
+  // where each epilogue warp stages 32 rows x 128 bytes of C, so that peer
+  // stores leave as whole 128-byte lines; 0 = no area (16-byte peer stores)
+  int32_t xfer_off;
 };
 
 // Row-stacked kernel stage descriptor (16 words), precomputed by the planner
@@ -157,6 +168,7 @@ struct bsp_spmm_plan {
   int32_t grid = 0, stages = 0, stage_bytes = 0, smem_bytes = 0, tmem_cols = 0, nprod = 1;
   int32_t variant = 0;      // 0: swap-AB kernel (spmm.cu), 1: row-stacked kernel (spmm_rowstack.cu)
   int32_t nsub = 1, sub_bytes = 0;  // row-stacked: sub-steps per stage and their size
+  int32_t xfer_off = 0;     // row-stacked: shared-memory staging area for peer stores (0: none)
   int32_t step_stride = 2;  // int32 words per step-table entry (1 + G)
   int64_t n_units = 0, n_steps = 0;
   uint64_t timeout_ns = 0;
@@ -240,7 +252,8 @@ int spmm_max_producers();
 int rowstack_max_producers();
 int rowstack_max_stages();
 bsp_status launch_spmm_rowstack(const bsp_spmm_plan* p, const bsp_bsr_desc* A, const void* B,
-                                int64_t ldb, void* C, int64_t ldc, cudaStream_t stream);
+                                int64_t ldb, void* C, int64_t ldc, cudaStream_t stream,
+                                void* const* peer_c = nullptr, int n_peers = 0);
 bsp_status plan_spmm_rowstack(bsp_spmm_plan* p, const int32_t* row_ptr, const int32_t* col_idx,
                               int sm_count, int max_smem, const bsp_spmm_opts* opts);
 }  // namespace bsp

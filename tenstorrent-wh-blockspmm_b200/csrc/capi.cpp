@@ -315,6 +315,76 @@ bsp_status bsp_spmm_execute(const bsp_spmm_plan* plan, const bsp_bsr_desc* A, co
   return launch_spmm(plan, A, B, ldb, C, ldc, static_cast<cudaStream_t>(stream));
 }
 
+bsp_status bsp_spmm_execute_replicated(const bsp_spmm_plan* plan, const bsp_bsr_desc* A, const void* B,
+                                       int64_t ldb, void* C, int64_t ldc, void* const* peer_C,
+                                       int32_t n_peers, void* stream) {
+  if (!plan || !B || !C) return set_error(BSP_ERR_INVALID_ARG, "null argument");
+  bsp_status s = check_desc(A, true);
+  if (s != BSP_OK) return s;
+  if (A->rows != plan->M || A->cols != plan->K || A->R != plan->R || A->C != plan->C ||
+      A->nnzb != plan->nnzb)
+    return set_error(BSP_ERR_INVALID_ARG, "A does not match the plan's pattern");
+  if (ldb < plan->N || ldc < plan->N)
+    return set_error(BSP_ERR_INVALID_ARG, "leading dimensions must be >= N");
+  if (plan->variant != 1)
+    return set_error(BSP_ERR_UNSUPPORTED, "replicated output needs a DDA (row-stacked) plan");
+  return launch_spmm_rowstack(plan, A, B, ldb, C, ldc, static_cast<cudaStream_t>(stream), peer_C,
+                              n_peers);
+}
+
+// ---- CUDA IPC of output buffers (replicated multi-GPU output) --------------
+namespace {
+typedef CUresult (*PFN_getAddressRange)(CUdeviceptr*, size_t*, CUdeviceptr);
+
+struct DeviceScope {  // make dev current for the call, restore the caller's device after
+  int prev = -1;
+  explicit DeviceScope(int ordinal) {
+    if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+    if (prev != ordinal) cudaSetDevice(ordinal);
+  }
+  ~DeviceScope() {
+    int cur = -1;
+    if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+  }
+};
+}  // namespace
+
+bsp_status bsp_ipc_export(bsp_device* dev, const void* ptr, void* handle_out, int64_t* offset_out) {
+  if (!dev || !ptr || !handle_out || !offset_out) return set_error(BSP_ERR_INVALID_ARG, "null argument");
+  DeviceScope scope(dev->ordinal);
+  void* fn = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+      q != cudaDriverEntryPointSuccess || !fn)
+    return set_error(BSP_ERR_CUDA, "cuMemGetAddressRange not available from the driver");
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  if (reinterpret_cast<PFN_getAddressRange>(fn)(&base, &size, reinterpret_cast<CUdeviceptr>(ptr)) != CUDA_SUCCESS)
+    return set_error(BSP_ERR_INVALID_ARG, "pointer is not device memory of this process");
+  cudaIpcMemHandle_t h;
+  bsp_status s = cuda_check(cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base)), "cudaIpcGetMemHandle");
+  if (s != BSP_OK) return s;
+  static_assert(sizeof(h) == BSP_IPC_HANDLE_BYTES, "IPC handle size");
+  memcpy(handle_out, &h, sizeof(h));
+  *offset_out = static_cast<int64_t>(reinterpret_cast<CUdeviceptr>(ptr) - base);
+  return BSP_OK;
+}
+
+bsp_status bsp_ipc_import(bsp_device* dev, const void* handle, void** base_out) {
+  if (!dev || !handle || !base_out) return set_error(BSP_ERR_INVALID_ARG, "null argument");
+  DeviceScope scope(dev->ordinal);
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  return cuda_check(cudaIpcOpenMemHandle(base_out, h, cudaIpcMemLazyEnablePeerAccess),
+                    "cudaIpcOpenMemHandle");
+}
+
+bsp_status bsp_ipc_close(bsp_device* dev, void* base) {
+  if (!dev || !base) return set_error(BSP_ERR_INVALID_ARG, "null argument");
+  DeviceScope scope(dev->ordinal);
+  return cuda_check(cudaIpcCloseMemHandle(base), "cudaIpcCloseMemHandle");
+}
+
 bsp_status bsp_spmm_plan_destroy(bsp_spmm_plan* plan) {
   if (!plan) return BSP_OK;
   if (plan->d_blob) cudaFree(plan->d_blob);

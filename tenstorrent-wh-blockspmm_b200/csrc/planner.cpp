@@ -404,6 +404,13 @@ bsp_status plan_spmm_rowstack(bsp_spmm_plan* p, const int32_t* row_ptr, const in
   p->stage_bytes = stage_bytes;
   p->stages = stages;
   p->smem_bytes = 2048 + stages * stage_bytes;
+  // A 16 KiB staging area for replicated (multi-GPU) launches, when it fits
+  // beside the ring without costing a stage.
+  p->xfer_off = 0;
+  if (p->smem_bytes + 16384 <= max_smem) {
+    p->xfer_off = 1024 + stages * stage_bytes;
+    p->smem_bytes += 16384;
+  }
   p->tmem_cols = 512;
   p->timeout_ns = static_cast<uint64_t>(o.timeout_ms > 0 ? o.timeout_ms : 2000) * 1000000ull;
 

@@ -274,6 +274,13 @@ __device__ __forceinline__ void rs_epilogue(const SpmmKernelParams& p, RsSmemHea
   const int slabs = p.R / p.Rs;
   int acc = 0;
   uint32_t acc_phase = 0;
+  // Peer copies of C leave as whole 128-byte row segments: the warp's 32 rows
+  // x 128 bytes are staged in shared memory (16-byte pieces XOR-swizzled by
+  // row), then each store instruction writes 4 rows x 128 contiguous bytes.
+  constexpr int kEsz = kF32 ? 4 : 2;
+  constexpr int kChunksPerFlush = 128 / (32 * kEsz);  // 32-column chunks per 128-byte segment
+  const bool staged = p.n_peers > 0 && p.xfer_off > 0;
+  uint4* xf = reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(hdr) + p.xfer_off) + q * (32 * 8);
   SpmmUnit nxt;
   if (u_begin < u_end) nxt = p.units[u_begin];
 #pragma unroll 1
@@ -300,27 +307,66 @@ __device__ __forceinline__ void rs_epilogue(const SpmmKernelParams& p, RsSmemHea
 #pragma unroll
           for (int i = 0; i < 32; ++i) v[i] = 0u;
         }
+        const int64_t eo = row * p.ldc + n;  // element offset, the same in every peer's C
+        const int piece0 = (c % kChunksPerFlush) * (32 * kEsz / 16);  // first 16-byte piece of this chunk
         if constexpr (kF32) {
-          float* dst = static_cast<float*>(p.c_ptr) + row * p.ldc + n;
+          float* dst = static_cast<float*>(p.c_ptr) + eo;
 #pragma unroll
-          for (int i = 0; i < 8; ++i)
-            if (n + 4 * i < p.N)
-              reinterpret_cast<uint4*>(dst)[i] = make_uint4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+          for (int i = 0; i < 8; ++i) {
+            const uint4 val = make_uint4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+            if (n + 4 * i < p.N) {
+              reinterpret_cast<uint4*>(dst)[i] = val;
+              if (!staged) {
+#pragma unroll 1
+                for (int pp = 0; pp < p.n_peers; ++pp)
+                  reinterpret_cast<uint4*>(static_cast<float*>(p.peer_c[pp]) + eo)[i] = val;
+              }
+            }
+            if (staged) xf[lane * 8 + ((piece0 + i) ^ (lane & 7))] = val;
+          }
         } else {
-          __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(p.c_ptr) + row * p.ldc + n;
+          __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(p.c_ptr) + eo;
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
-            if (n + 8 * i < p.N) {
-              uint32_t w[4];
+            uint32_t w[4];
 #pragma unroll
-              for (int h = 0; h < 4; ++h) {
-                const __nv_bfloat162 b2 = __floats2bfloat162_rn(__uint_as_float(v[8 * i + 2 * h]),
-                                                                __uint_as_float(v[8 * i + 2 * h + 1]));
-                w[h] = *reinterpret_cast<const uint32_t*>(&b2);
+            for (int h = 0; h < 4; ++h) {
+              const __nv_bfloat162 b2 = __floats2bfloat162_rn(__uint_as_float(v[8 * i + 2 * h]),
+                                                              __uint_as_float(v[8 * i + 2 * h + 1]));
+              w[h] = *reinterpret_cast<const uint32_t*>(&b2);
+            }
+            const uint4 val = make_uint4(w[0], w[1], w[2], w[3]);
+            if (n + 8 * i < p.N) {
+              reinterpret_cast<uint4*>(dst)[i] = val;
+              if (!staged) {
+#pragma unroll 1
+                for (int pp = 0; pp < p.n_peers; ++pp)
+                  reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.peer_c[pp]) + eo)[i] = val;
               }
-              reinterpret_cast<uint4*>(dst)[i] = make_uint4(w[0], w[1], w[2], w[3]);
+            }
+            if (staged) xf[lane * 8 + ((piece0 + i) ^ (lane & 7))] = val;
+          }
+        }
+        // flush the staged 128-byte segments after the segment's last chunk
+        if (staged && (c % kChunksPerFlush == kChunksPerFlush - 1 || n + 32 >= p.N ||
+                       c == kRsN / 32 - 1)) {
+          __syncwarp();
+          const int nseg0 = un.n0 + (c - c % kChunksPerFlush) * 32;  // first column of the segment
+          const int64_t row_w = row - lane;                             // the warp's first row
+          const int pc = lane & 7;
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const int r = 4 * i + (lane >> 3);
+            const int col = nseg0 + pc * (16 / kEsz);
+            if (col < p.N && pc < (c % kChunksPerFlush + 1) * (32 * kEsz / 16)) {
+              const uint4 val = xf[r * 8 + (pc ^ (r & 7))];
+              const int64_t off = (row_w + r) * p.ldc + col;
+#pragma unroll 1
+              for (int pp = 0; pp < p.n_peers; ++pp)
+                *reinterpret_cast<uint4*>(static_cast<uint8_t*>(p.peer_c[pp]) + off * kEsz) = val;
             }
           }
+          __syncwarp();
         }
       }
     }
@@ -330,6 +376,8 @@ __device__ __forceinline__ void rs_epilogue(const SpmmKernelParams& p, RsSmemHea
     acc ^= 1;
     if (acc == 0) acc_phase ^= 1u;
   }
+  // peer stores are visible system-wide before this CTA retires
+  if (p.n_peers > 0) __threadfence_system();
 }
 
 template <bool kF32>
@@ -392,7 +440,13 @@ int rowstack_max_producers() { return kRsMaxProducers; }
 int rowstack_max_stages() { return kRsMaxStages; }
 
 bsp_status launch_spmm_rowstack(const bsp_spmm_plan* p, const bsp_bsr_desc* A, const void* B,
-                                int64_t ldb, void* C, int64_t ldc, cudaStream_t stream) {
+                                int64_t ldb, void* C, int64_t ldc, cudaStream_t stream,
+                                void* const* peer_c, int n_peers) {
+  if (n_peers < 0 || n_peers > kMaxPeers || (n_peers > 0 && !peer_c))
+    return set_error(BSP_ERR_INVALID_ARG, "n_peers must be 0..7 with a peer pointer each");
+  for (int i = 0; i < n_peers; ++i)
+    if (!peer_c[i] || reinterpret_cast<uintptr_t>(peer_c[i]) % 16)
+      return set_error(BSP_ERR_INVALID_ARG, "peer C pointers must be non-null and 16-byte aligned");
   bsp_device* dev = p->dev;
   const bool f32 = p->c_type == BSP_F32;
   if (p->n_units == 0 || p->M == 0 || p->N == 0) return BSP_OK;
@@ -405,8 +459,13 @@ bsp_status launch_spmm_rowstack(const bsp_spmm_plan* p, const bsp_bsr_desc* A, c
     p->attr_set = true;
   }
   // Same operands as the previous call: reuse the encoded tensor maps.
+  auto set_peers = [&](SpmmKernelParams& k) {
+    k.n_peers = n_peers;
+    for (int i = 0; i < kMaxPeers; ++i) k.peer_c[i] = i < n_peers ? peer_c[i] : nullptr;
+  };
   if (p->kp_valid && p->kp_a == A->values && p->kp_b == B && p->kp_c == C && p->kp_ldb == ldb &&
       p->kp_ldc == ldc) {
+    set_peers(p->kp);
     kern<<<p->grid, kRsThreads, p->smem_bytes, stream>>>(p->kp);
     return cuda_check(cudaGetLastError(), "spmm rowstack kernel launch");
   }
@@ -464,12 +523,14 @@ bsp_status launch_spmm_rowstack(const bsp_spmm_plan* p, const bsp_bsr_desc* A, c
   kp.stage_list = p->d_stage_list;
   kp.cta_stage_begin = p->d_cta_stage_begin;
   kp.sub_bytes = p->sub_bytes;
+  kp.xfer_off = p->xfer_off;
   p->kp_valid = true;
   p->kp_a = A->values;
   p->kp_b = B;
   p->kp_c = C;
   p->kp_ldb = ldb;
   p->kp_ldc = ldc;
+  set_peers(kp);
   kern<<<p->grid, kRsThreads, p->smem_bytes, stream>>>(kp);
   return cuda_check(cudaGetLastError(), "spmm rowstack kernel launch");
 }

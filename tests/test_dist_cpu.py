@@ -75,6 +75,58 @@ def _worker(rank, ws, port, seed, skew, q):
         q.put((rank, f"error: {e!r}", None))
 
 
+def _chunk_worker(rank, ws, port, seed, chunks, q):
+    """Chunked protocol: rank r computes chunk c of its panel, then round c of
+    the exchange starts; all rounds are waited at the end."""
+    import torch
+    import torch.distributed as dist
+
+    try:
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        dist.init_process_group("gloo", rank=rank, world_size=ws)
+        M, K, N, R, C, rp, ci, vals, B = _case(seed)
+        bounds = bsp_dist.shard_bounds(rp, ws)
+        cb = bsp_dist.chunk_bounds(rp, bounds, chunks)
+        assert cb[rank][0] == bounds[rank] and cb[rank][-1] == bounds[rank + 1]
+        Cfull = torch.full((M, N), -1, dtype=torch.int16)
+        reqs = []
+        for c in range(chunks):
+            c0, c1 = int(cb[rank][c]), int(cb[rank][c + 1])
+            if c1 > c0:
+                pan = bsp_dist.row_panel(rp, ci, vals, R, C, c0, c1)
+                part = oracle.spmm_bf16(pan.row_ptr, pan.col_idx, pan.values, (c1 - c0) * R, K, R, C, B, N)
+                Cfull[c0 * R:c1 * R] = torch.from_numpy(part.view(np.int16))
+            ranges = [(int(cb[r][c]) * R, int(cb[r][c + 1]) * R) for r in range(ws)]
+            reqs += bsp_dist.start_exchange(Cfull, ranges, rank, ws)
+        for req in reqs:
+            req.wait()
+        dist.barrier()
+        full = oracle.spmm_bf16(rp, ci, vals, M, K, R, C, B, N)
+        q.put((rank, bool(np.array_equal(Cfull.numpy().view(np.uint16), full)), None))
+        dist.destroy_process_group()
+    except Exception as e:
+        q.put((rank, f"error: {e!r}", None))
+
+
+@pytest.mark.parametrize("ws,chunks", [(2, 3), (3, 4)])
+def test_chunked_exchange_gloo(ws, chunks):
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_chunk_worker, args=(r, ws, port, 21 + ws, chunks, q)) for r in range(ws)]
+    for p in procs:
+        p.start()
+    results = [q.get(timeout=120) for _ in range(ws)]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank, ok, _ in results:
+        assert ok is True, (rank, ok)
+
+
 @pytest.mark.parametrize("ws,skew", [(2, False), (3, False), (2, True)])
 def test_sharded_exchange_gloo(ws, skew):
     import torch.multiprocessing as mp

@@ -1,0 +1,104 @@
+"""Sharded SpMM on 2 GPUs: row-panels by nonzero-block count, replicated C.
+
+Each rank runs the single-GPU kernel on its panel of A's block-rows and every
+rank ends with the whole C, either through the fused kernel (the epilogue
+stores each tile into both GPUs' C over NVLink) or through NCCL send/receive
+of the panels; every rank's C must match the oracle.  Needs two visible GPUs
+(skipped otherwise).
+"""
+import os
+import socket
+import sys
+
+import numpy as np
+import pytest
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(HERE)
+PKG = os.path.join(ROOT, "tenstorrent-wh-blockspmm_b200")
+for p in (ROOT, PKG, HERE):
+    if p not in sys.path:
+        sys.path.insert(0, p)
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _case():
+    import bench
+
+    rng = np.random.default_rng(5)
+    M = K = 2048
+    N, R, C = 512, 64, 64
+    rp, ci = bench.gen_zipf_pattern(M // R, K // C, 0.05, 1.1, rng)
+    vals = bench.uniform_bf16(rng, (ci.size * R, C)).reshape(-1)
+    B = bench.uniform_bf16(rng, (K, N))
+    return M, K, N, R, C, rp, ci, vals, B
+
+
+def _worker(rank, ws, port, q, fused):
+    from datetime import timedelta
+
+    import torch
+    import torch.distributed as dist
+
+    try:
+        import bsp
+        import bsp_dist
+        import oracle
+        from helpers import TOL, rel_err
+
+        torch.cuda.set_device(rank)
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+        dist.init_process_group("nccl", rank=rank, world_size=ws, timeout=timedelta(seconds=60),
+                                device_id=torch.device("cuda", rank))
+        M, K, N, R, C, rp, ci, vals, B = _case()
+        dev = bsp.device(rank)
+        sh = bsp_dist.ShardedSpmm(dev, M, K, R, C, rp, ci, vals, N, rank, ws, bsp.DDA, fused=fused)
+        Bd = bsp.to_device_bf16(B, rank)
+        Cfull = torch.full((M, N), float("nan"), dtype=torch.bfloat16, device="cuda")
+        sh.attach(Cfull)
+        for _ in range(2):   # twice: the second run overwrites the first
+            sh.run(Bd, Cfull)
+        torch.cuda.synchronize()
+        dev.synchronize()
+        got = oracle.bf16_to_f32(bsp.to_host_bits(Cfull).ravel())
+        gold = oracle.bf16_to_f32(oracle.spmm_bf16(rp, ci, vals, M, K, R, C, B, N).ravel())
+        err = float(rel_err(got, gold).max()) if np.all(np.isfinite(got)) else float("inf")
+        sh.close()
+        dist.barrier()
+        dist.destroy_process_group()
+        q.put((rank, err <= TOL, err, sh.bounds.tolist()))
+    except Exception as e:
+        q.put((rank, False, repr(e), None))
+
+
+@pytest.mark.parametrize("fused", [True, False], ids=["fused-epilogue-stores", "nccl-send-recv"])
+def test_sharded_spmm_two_gpus(fused):
+    import torch
+    import torch.multiprocessing as mp
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two visible GPUs")
+    ws = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, ws, port, q, fused)) for r in range(ws)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=300) for _ in range(ws)]
+    for p in procs:
+        p.join(timeout=120)
+    for rank, ok, err, bounds in res:
+        assert ok, (rank, err)
+    assert res[0][3] == res[1][3]

@@ -142,10 +142,10 @@ def gen_sddmm_case(M, N, K, R, C, p, seed, scale=1.0 / 16, name=None):
 
 
 def gen_attention_mask(nb, rng, band=8, n_global=4, zipf_s=1.2, cap=64):
-    """Block pattern of config 4: per block-row i the band i-3..i+4, the first
-    n_global block-columns, and Zipf(zipf_s)-many (<= cap) uniform random
-    further block-columns."""
-    lo, hi = -(band // 2 - 1), band // 2
+    """Block pattern of config 4: per block-row i the band i-4..i+3 (8 blocks),
+    the first n_global block-columns, and min(Zipf(zipf_s), cap) further
+    block-columns drawn uniformly without replacement."""
+    lo, hi = -(band // 2), band // 2 - 1
     extra = np.minimum(rng.zipf(zipf_s, nb), cap)
     rows = []
     for i in range(nb):

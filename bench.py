@@ -495,7 +495,8 @@ class DevOp:
     def kernel(self):
         if self.kind == "sddmm":
             return "sddmm_bsr_tcgen05"
-        return "spmm_rowstack_tcgen05" if self.plan.info().get("variant", 0) == 1 else "spmm_bsr_tcgen05"
+        return {1: "spmm_rowstack_tcgen05", 2: "spmm_pair_tcgen05"}.get(self.plan.info().get("variant", 0),
+                                                                      "spmm_bsr_tcgen05")
 
     def close(self):
         self.plan.close()

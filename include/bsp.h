@@ -160,8 +160,12 @@ bsp_status bsp_spmm_execute_replicated(const bsp_spmm_plan* plan, const bsp_bsr_
 bsp_status bsp_ipc_export(bsp_device* dev, const void* ptr, void* handle_out, int64_t* offset_out);
 bsp_status bsp_ipc_import(bsp_device* dev, const void* handle, void** base_out);
 bsp_status bsp_ipc_close(bsp_device* dev, void* base);
-/* Plan facts: [0]=units [1]=ctas [2]=group_rows [3]=n_tiles [4]=sub-row height
- * [5]=k chunk [6]=pipeline stages [7]=steps [8]=plan device bytes. */
+/* Plan facts: [0]=unit records (one per CTA of a pair for the CTA-pair
+ * kernel) [1]=ctas [2]=entries per CTA [3]=n_tiles [4]=sub-row height
+ * [5]=k chunk [6]=pipeline stages [7]=steps [8]=plan device bytes [9]=shared
+ * memory per CTA [10]=TMEM columns [11]=kernel variant (0 swap-AB, 1 row-
+ * stacked, 2 row-stacked on CTA pairs) [12]=producer warps [15]=int32 words
+ * per step-table entry. */
 bsp_status bsp_spmm_plan_info(const bsp_spmm_plan* plan, int64_t info[16]);
 
 /* One-shot: plan, execute on `stream`, synchronise, destroy. */

@@ -402,13 +402,14 @@ def inspect_spmm_plan(M, K, R, C, row_ptr, col_idx, N, strategy=NAIVE, c_type=BF
     _check(lib().bsp_spmm_plan_inspect(*args, None, None, None, None, None))
     units = np.zeros((int(info[0]), 8), np.int32)
     cta = np.zeros(int(info[1]) + 1, np.int32)
-    steps = np.zeros((max(int(info[7]), 1), 1 + int(info[2])), np.int32)
+    steps = np.zeros((max(int(info[7]), 1), int(info[15])), np.int32)
     stages = np.zeros((max(int(info[13]), 1), 16), np.int32)
     cta_st = np.zeros(int(info[1]) + 1, np.int32)
     _check(lib().bsp_spmm_plan_inspect(*args, _ptr(units), _ptr(cta), _ptr(steps), _ptr(stages),
                                        _ptr(cta_st)))
     keys = ["units", "ctas", "group_rows", "n_tiles", "slab", "kc", "stages", "steps",
-            "plan_bytes", "smem_bytes", "tmem_cols", "variant", "producers", "stage_list", "nsub"]
+            "plan_bytes", "smem_bytes", "tmem_cols", "variant", "producers", "stage_list", "nsub",
+            "step_stride"]
     d = {k: int(info[i]) for i, k in enumerate(keys)}
     d.update(unit_table=units, cta_begin=cta, step_table=steps[: int(info[7])],
              stage_table=stages[: int(info[13])], cta_stage_begin=cta_st)

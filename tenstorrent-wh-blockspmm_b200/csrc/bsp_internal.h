@@ -254,6 +254,11 @@ int rowstack_max_stages();
 bsp_status launch_spmm_rowstack(const bsp_spmm_plan* p, const bsp_bsr_desc* A, const void* B,
                                 int64_t ldb, void* C, int64_t ldc, cudaStream_t stream,
                                 void* const* peer_c = nullptr, int n_peers = 0);
+bsp_status plan_spmm_pair(bsp_spmm_plan* p, const int32_t* row_ptr, const int32_t* col_idx,
+                          int sm_count, int max_smem, const bsp_spmm_opts* opts);
+bsp_status launch_spmm_pair(const bsp_spmm_plan* p, const bsp_bsr_desc* A, const void* B, int64_t ldb,
+                            void* C, int64_t ldc, cudaStream_t stream, void* const* peer_c = nullptr,
+                            int n_peers = 0);
 bsp_status plan_spmm_rowstack(bsp_spmm_plan* p, const int32_t* row_ptr, const int32_t* col_idx,
                               int sm_count, int max_smem, const bsp_spmm_opts* opts);
 }  // namespace bsp

@@ -310,6 +310,8 @@ bsp_status bsp_spmm_execute(const bsp_spmm_plan* plan, const bsp_bsr_desc* A, co
     return set_error(BSP_ERR_INVALID_ARG, "A does not match the plan's pattern");
   if (ldb < plan->N || ldc < plan->N)
     return set_error(BSP_ERR_INVALID_ARG, "leading dimensions must be >= N");
+  if (plan->variant == 2)
+    return launch_spmm_pair(plan, A, B, ldb, C, ldc, static_cast<cudaStream_t>(stream));
   if (plan->variant == 1)
     return launch_spmm_rowstack(plan, A, B, ldb, C, ldc, static_cast<cudaStream_t>(stream));
   return launch_spmm(plan, A, B, ldb, C, ldc, static_cast<cudaStream_t>(stream));
@@ -326,6 +328,8 @@ bsp_status bsp_spmm_execute_replicated(const bsp_spmm_plan* plan, const bsp_bsr_
     return set_error(BSP_ERR_INVALID_ARG, "A does not match the plan's pattern");
   if (ldb < plan->N || ldc < plan->N)
     return set_error(BSP_ERR_INVALID_ARG, "leading dimensions must be >= N");
+  if (plan->variant == 2)
+    return launch_spmm_pair(plan, A, B, ldb, C, ldc, static_cast<cudaStream_t>(stream), peer_C, n_peers);
   if (plan->variant != 1)
     return set_error(BSP_ERR_UNSUPPORTED, "replicated output needs a DDA (row-stacked) plan");
   return launch_spmm_rowstack(plan, A, B, ldb, C, ldc, static_cast<cudaStream_t>(stream), peer_C,
@@ -408,6 +412,7 @@ bsp_status bsp_spmm_plan_info(const bsp_spmm_plan* p, int64_t info[16]) {
   info[10] = p->tmem_cols;
   info[11] = p->variant;
   info[12] = p->nprod;
+  info[15] = p->step_stride;  // int32 words per step-table entry
   return BSP_OK;
 }
 
@@ -768,7 +773,7 @@ bsp_status bsp_spmm_plan_inspect(int64_t M, int64_t K, int32_t R, int32_t C, int
   if (units_out) memcpy(units_out, p.h_units.data(), p.h_units.size() * sizeof(SpmmUnit));
   if (cta_begin_out)
     memcpy(cta_begin_out, p.h_cta_begin.data(), p.h_cta_begin.size() * sizeof(int32_t));
-  if (steps_out) memcpy(steps_out, p.h_steps.data(), p.n_steps * (1 + p.G) * sizeof(int32_t));
+  if (steps_out) memcpy(steps_out, p.h_steps.data(), p.n_steps * p.step_stride * sizeof(int32_t));
   info[13] = static_cast<int64_t>(p.h_stage_list.size() / kRsStageWords);
   info[14] = p.nsub;
   if (stage_list_out && !p.h_stage_list.empty())

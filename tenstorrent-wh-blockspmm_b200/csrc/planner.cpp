@@ -115,8 +115,39 @@ bsp_status plan_spmm_host(bsp_spmm_plan* p, const int32_t* row_ptr, const int32_
   if (st != BSP_OK) return st;
   // DDA runs on the row-stacked kernel unless the caller asks for one of the
   // swap-AB variants (group_mma 2: one MMA per block, 3: stacked swap-AB).
-  if (p->strategy == BSP_DDA && o.group_mma != 2 && o.group_mma != 3)
-    return plan_spmm_rowstack(p, row_ptr, col_idx, sm_count, max_smem, opts);
+  // DDA: group_mma 4 forces the single-CTA row-stacked kernel, 5 the CTA-pair
+  // kernel (2-SM MMA).  By default both schedules are built and the one with
+  // the shorter estimated critical path wins: a pair stage moves twice the
+  // rows for ~0.8x the time of a single-CTA stage (measured on B200), but
+  // pairing 8 block-rows instead of 4 widens each unit's column union, which
+  // costs more than it saves below ~30% block density.
+  if (p->strategy == BSP_DDA && o.group_mma != 2 && o.group_mma != 3) {
+    if (o.group_mma == 4 || sm_count < 2) return plan_spmm_rowstack(p, row_ptr, col_idx, sm_count, max_smem, opts);
+    if (o.group_mma == 5) return plan_spmm_pair(p, row_ptr, col_idx, sm_count, max_smem, opts);
+    bsp_status st1 = plan_spmm_rowstack(p, row_ptr, col_idx, sm_count, max_smem, opts);
+    if (st1 != BSP_OK) return plan_spmm_pair(p, row_ptr, col_idx, sm_count, max_smem, opts);
+    auto longest = [](const bsp_spmm_plan* q, int step) {
+      int64_t m = 0;
+      for (size_t c = 0; c + step < q->h_cta_stage_begin.size(); c += step)
+        m = std::max<int64_t>(m, q->h_cta_stage_begin[c + 1] - q->h_cta_stage_begin[c]);
+      return m;
+    };
+    const int64_t s1 = longest(p, 1);
+    bsp_spmm_plan pair;
+    pair.M = p->M;
+    pair.K = p->K;
+    pair.N = p->N;
+    pair.R = p->R;
+    pair.C = p->C;
+    pair.nnzb = p->nnzb;
+    pair.c_type = p->c_type;
+    pair.strategy = p->strategy;
+    if (plan_spmm_pair(&pair, row_ptr, col_idx, sm_count, max_smem, opts) != BSP_OK) return BSP_OK;
+    const int64_t s2 = longest(&pair, 2);  // per pair: the leader's list (both lists are equal length)
+    if (4 * s2 < 5 * s1)  // pair time ~ 0.8 x its stages vs single-CTA stages
+      return plan_spmm_pair(p, row_ptr, col_idx, sm_count, max_smem, opts);
+    return BSP_OK;
+  }
   p->variant = 0;
 
   const int Rs = slab_height(R);
@@ -479,6 +510,202 @@ bsp_status plan_spmm_rowstack(bsp_spmm_plan* p, const int32_t* row_ptr, const in
       return set_error(BSP_ERR_UNSUPPORTED, "schedule too long");
     p->h_cta_stage_begin.push_back(static_cast<int32_t>(p->h_stage_list.size() / W));
   }
+  return BSP_OK;
+}
+
+// Row-stacked schedule for CTA pairs (2-SM MMA, spmm_pair.cu).  A pair unit
+// is 2G entries (256 output rows) x 256 columns; CTA rank r of the pair holds
+// entries r*G .. r*G+G-1 (its 128 TMEM lanes) and loads B columns
+// n0 + 128 r .. +127.  Every entry slot is loaded at every step: an absent
+// block comes from a TMA box entirely above the A tensor (y = -Rs), which
+// the TMA fills with zeros, so each stage moves a fixed number of bytes and
+// no slot ever needs clearing.  Units and stage lists are per CTA (the two
+// CTAs of a pair walk the same stage sequence with their own coordinates).
+bsp_status plan_spmm_pair(bsp_spmm_plan* p, const int32_t* row_ptr, const int32_t* col_idx,
+                          int sm_count, int max_smem, const bsp_spmm_opts* opts) {
+  bsp_spmm_opts o;
+  memset(&o, 0, sizeof(o));
+  if (opts) o = *opts;
+  const int R = p->R, C = p->C;
+  const int64_t nbr = p->M / R;
+  const int Rs = (R % 128 == 0) ? 128 : (R % 64 == 0) ? 64 : 32;
+  const int slabs = R / Rs;
+  const int G = 128 / Rs;  // entries per CTA
+  const int G2 = 2 * G;    // entries per pair unit
+  const int kc = (C % 64 == 0) ? 64 : 32;
+  const int nkc = C / kc;
+  const int64_t n_entries = nbr * slabs;
+  const int ntiles = static_cast<int>((p->N + 255) / 256);
+  if (n_entries >= (int64_t(1) << 31)) return set_error(BSP_ERR_UNSUPPORTED, "too many block-rows");
+  p->variant = 2;
+  p->Rs = Rs;
+  p->kc = kc;
+  p->G = G;
+  p->NT = 2;
+  p->stacked = 1;
+  const int stride = 1 + G2;
+  p->step_stride = stride;
+  std::vector<int32_t>& steps = p->h_steps;
+  steps.clear();
+  struct PairUnit {
+    int64_t e0;
+    int nent;
+    int32_t s_begin, s_end, n0;
+    int32_t mask;  // present entries (bit g of the 2G)
+  };
+  std::vector<PairUnit> units;
+  std::vector<int64_t> weight;
+  const int esz = p->c_type == BSP_F32 ? 4 : 2;
+  std::vector<std::pair<int32_t, int32_t>> items;
+  std::vector<int8_t> item_g;
+  for (int64_t e0 = 0; e0 < n_entries; e0 += G2) {
+    const int nent = static_cast<int>(std::min<int64_t>(G2, n_entries - e0));
+    const int32_t s_begin = static_cast<int32_t>(steps.size() / stride);
+    int32_t mask = 0;
+    items.clear();
+    item_g.clear();
+    for (int g = 0; g < nent; ++g) {
+      const int64_t i = (e0 + g) / slabs;
+      if (row_ptr[i + 1] > row_ptr[i]) mask |= 1 << g;
+      for (int32_t b = row_ptr[i]; b < row_ptr[i + 1]; ++b) {
+        items.push_back({col_idx[b], b});
+        item_g.push_back(static_cast<int8_t>(g));
+      }
+    }
+    std::vector<int32_t> order(items.size());
+    std::iota(order.begin(), order.end(), 0);
+    std::stable_sort(order.begin(), order.end(),
+                     [&](int32_t a, int32_t b) { return items[a].first < items[b].first; });
+    int64_t cur = -1;
+    for (int32_t k : order) {
+      const int g = item_g[k];
+      const bool open = cur >= 0 && steps[cur * stride] == items[k].first && steps[cur * stride + 1 + g] < 0;
+      if (!open) {
+        cur = static_cast<int64_t>(steps.size() / stride);
+        steps.push_back(items[k].first);
+        for (int q = 0; q < G2; ++q) steps.push_back(-1);
+      }
+      steps[cur * stride + 1 + g] = items[k].second;
+    }
+    const int32_t s_end = static_cast<int32_t>(steps.size() / stride);
+    for (int t = 0; t < ntiles; ++t) {
+      units.push_back({e0, nent, s_begin, s_end, t * 256, mask});
+      // bytes staged per CTA: B half + all entry slots per step, plus its C rows
+      weight.push_back(int64_t(s_end - s_begin) * nkc * (int64_t(kc) * 128 * 2 + int64_t(G) * Rs * kc * 2) +
+                       int64_t(G) * Rs * 256 * esz + 4096);
+    }
+  }
+  p->n_steps = static_cast<int64_t>(steps.size() / stride);
+  int npairs = (o.max_ctas > 0 ? std::min(o.max_ctas, sm_count) : sm_count) / 2;
+  npairs = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(npairs, units.size())));
+  std::vector<std::vector<int32_t>> per;
+  if (o.no_load_balance)
+    contiguous_split(static_cast<int64_t>(units.size()), npairs, &per);
+  else
+    serpentine_order(weight, npairs, &per);
+
+  // stages: nsub consecutive (step, k-chunk) items per stage, as in the
+  // single-CTA kernel (two 32-wide block-columns = 4 MMAs per hand-off)
+  int nsub = 1;
+  if (kc == 32 && nkc == 1 && o.steps_per_stage != 1) nsub = 2;
+  const int b_half = 2 * kc * 128;               // two 64-column boxes
+  const int sub_bytes = b_half + G * Rs * kc * 2;
+  p->sub_bytes = sub_bytes;
+  p->nsub = nsub;
+  int stage_bytes = nsub * sub_bytes;
+  stage_bytes = (stage_bytes + 1023) / 1024 * 1024;
+  const int max_stages = std::min(rowstack_max_stages(), (max_smem - 2048 - 16384) / stage_bytes);
+  if (max_stages < 2) return set_error(BSP_ERR_UNSUPPORTED, "block too large for the pipeline");
+  int nprod = 1, stages = max_stages;
+  if (o.producers > 0) {
+    nprod = std::min({o.producers, rowstack_max_producers(), max_stages});
+    stages = max_stages / nprod * nprod;
+  } else {
+    for (int q = 2; q <= std::min(rowstack_max_producers(), max_stages); ++q) {
+      const int sq = max_stages / q * q;
+      if (sq >= stages - (stages > 6 ? 1 : 0)) {
+        nprod = q;
+        stages = sq;
+      }
+    }
+  }
+  p->nprod = nprod;
+  p->stage_bytes = stage_bytes;
+  p->stages = stages;
+  p->xfer_off = 1024 + stages * stage_bytes;  // staging for replicated launches
+  p->smem_bytes = 2048 + stages * stage_bytes + 16384;
+  p->tmem_cols = 512;
+  p->timeout_ns = static_cast<uint64_t>(o.timeout_ms > 0 ? o.timeout_ms : 2000) * 1000000ull;
+  p->grid = 2 * npairs;
+
+  // per-CTA units and stage lists (CTA 2c + r = rank r of pair c)
+  const bool b3d = (p->N % 64 == 0);
+  const int W = kRsStageWords;
+  p->h_units.clear();
+  p->h_cta_begin.assign(1, 0);
+  p->h_stage_list.clear();
+  p->h_cta_stage_begin.assign(1, 0);
+  for (int c = 0; c < npairs; ++c) {
+    for (int r = 0; r < 2; ++r) {
+      for (int32_t idx : per[c]) {
+        const PairUnit& pu = units[idx];
+        SpmmUnit u;
+        u.row0 = static_cast<int32_t>(pu.e0 + r * G);
+        u.nrows = std::max(0, std::min(G, pu.nent - r * G));
+        u.r_off = 0;
+        u.n0 = pu.n0;
+        u.nt = 1;
+        u.step_begin = pu.s_begin;
+        u.step_end = pu.s_end;
+        u.row_mask = (pu.mask >> (r * G)) & ((1 << G) - 1);
+        p->h_units.push_back(u);
+        const int nsteps = pu.s_end - pu.s_begin;
+        if (nsteps == 0) {
+          int32_t e[kRsStageWords] = {RS_F_FIRST | RS_F_LAST | RS_F_EMPTY};
+          p->h_stage_list.insert(p->h_stage_list.end(), e, e + W);
+          continue;
+        }
+        int slab_off[4] = {0, 0, 0, 0};
+        for (int g = 0; g < G; ++g) slab_off[g] = static_cast<int>((u.row0 + g) % slabs) * Rs;
+        const int nitems = nsteps * nkc;
+        for (int s0 = 0; s0 < nitems; s0 += nsub) {
+          const int nin = std::min(nsub, nitems - s0);
+          int32_t e[kRsStageWords];
+          for (int q = 0; q < W; ++q) e[q] = 0;
+          uint32_t flags = 0;
+          for (int sub = 0; sub < nsub; ++sub) {
+            for (int g = 0; g < 4; ++g) e[5 + 4 * sub + g] = -Rs;  // absent: a box above the tensor
+            if (sub >= nin) continue;
+            const int s_ = s0 + sub;
+            const int j = s_ / nkc, kci = s_ % nkc;
+            const int32_t* st = &steps[static_cast<size_t>(pu.s_begin + j) * stride];
+            for (int g = 0; g < G; ++g) {
+              const int gg = r * G + g;
+              if (g < u.nrows && st[1 + gg] >= 0) e[5 + 4 * sub + g] = st[1 + gg] * R + slab_off[g];
+            }
+            e[3 + sub] = st[0] * C + kci * kc;
+            e[2] = kci * kc;
+          }
+          if (s0 == 0) flags |= RS_F_FIRST;
+          if (s0 + nin >= nitems) flags |= RS_F_LAST;
+          if (nin == 2) flags |= RS_F_TWO;
+          e[0] = static_cast<int32_t>(flags);
+          e[1] = b3d ? pu.n0 / 64 + 2 * r : pu.n0 + 128 * r;
+          p->h_stage_list.insert(p->h_stage_list.end(), e, e + W);
+        }
+      }
+      p->h_cta_begin.push_back(static_cast<int32_t>(p->h_units.size()));
+      if (p->h_stage_list.size() / W >= (size_t(1) << 31))
+        return set_error(BSP_ERR_UNSUPPORTED, "schedule too long");
+      p->h_cta_stage_begin.push_back(static_cast<int32_t>(p->h_stage_list.size() / W));
+    }
+  }
+  if (steps.empty()) {
+    steps.push_back(0);
+    for (int q = 0; q < G2; ++q) steps.push_back(-1);
+  }
+  // one unit record per CTA of each pair unit
+  p->n_units = static_cast<int64_t>(p->h_units.size());
   return BSP_OK;
 }
 

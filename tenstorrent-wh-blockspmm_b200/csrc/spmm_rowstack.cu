@@ -32,50 +32,13 @@
 
 #include <type_traits>
 
-#include "bsp_internal.h"
-#include "bsp_ptx.cuh"
+#include "rowstack_common.cuh"
 
 namespace bsp {
 using namespace dev;
+using namespace rs;
 
 namespace {
-
-constexpr int kRsMmaWarp = 0;
-constexpr int kRsProd0 = 1;
-constexpr int kRsMaxProducers = 3;
-constexpr int kRsEpi0 = 4;
-constexpr int kRsThreads = 8 * 32;
-constexpr int kRsMaxStages = 30;
-constexpr int kRsN = 256;       // MMA N: dense columns per unit
-constexpr int kRsMaxG = 4;      // entries per stack (128 / 32)
-
-struct RsSmemHeader {
-  uint64_t full[kRsMaxStages];
-  uint64_t empty[kRsMaxStages];
-  uint64_t acc_full[2];
-  uint64_t acc_empty[2];
-  uint64_t drain;
-  uint32_t info[kRsMaxStages];
-  uint32_t tmem_base;
-  int abort_flag;
-};
-static_assert(sizeof(RsSmemHeader) <= 1024, "header must fit its 1 KiB slot");
-
-enum : uint32_t {
-  RS_FIRST = static_cast<uint32_t>(RS_F_FIRST),
-  RS_LAST = static_cast<uint32_t>(RS_F_LAST),
-  RS_EMPTY = static_cast<uint32_t>(RS_F_EMPTY),
-  RS_TWO = static_cast<uint32_t>(RS_F_TWO),
-};
-
-__device__ __forceinline__ uint32_t baddr(const uint64_t* b) { return smem_u32(b); }
-
-__device__ __noinline__ bool rs_drain_wait(uint32_t bar, uint32_t parity, const WaitCtl& ctl) {
-  int zero = 0;
-  WaitCtl c2{&zero, ctl.status, ctl.timeout_ns};
-  return mbar_wait_bounded(bar, parity, c2, ST_TIMEOUT_DRAIN);
-}
-
 // Producer warp pw (0-based among producers): issues the CTA's pipeline
 // stages pw, pw + nprod, pw + 2*nprod, ... from the precomputed stage list.
 // 32 of its stages are fetched at once (lane l holds the l-th, 64 bytes) and
@@ -260,124 +223,6 @@ __device__ __forceinline__ void rs_mma(const SpmmKernelParams& p, RsSmemHeader* 
     rs_drain_wait(baddr(&hdr->drain), 0, ctl);
   }
   __syncwarp();
-}
-
-// Epilogue warp with TMEM lane quarter q: lanes 32q..32q+31 are output rows of
-// entry g = 32q / Rs; each thread writes its row, 32 columns per TMEM load.
-template <bool kF32>
-__device__ __forceinline__ void rs_epilogue(const SpmmKernelParams& p, RsSmemHeader* hdr,
-                                           uint32_t tmem_base, int u_begin, int u_end,
-                                           const WaitCtl& ctl, int warp, int lane) {
-  const int q = warp & 3;
-  const int g = (32 * q) / p.Rs;
-  const int rrow = (32 * q) % p.Rs + lane;
-  const int slabs = p.R / p.Rs;
-  int acc = 0;
-  uint32_t acc_phase = 0;
-  // Peer copies of C leave as whole 128-byte row segments: the warp's 32 rows
-  // x 128 bytes are staged in shared memory (16-byte pieces XOR-swizzled by
-  // row), then each store instruction writes 4 rows x 128 contiguous bytes.
-  constexpr int kEsz = kF32 ? 4 : 2;
-  constexpr int kChunksPerFlush = 128 / (32 * kEsz);  // 32-column chunks per 128-byte segment
-  const bool staged = p.n_peers > 0 && p.xfer_off > 0;
-  uint4* xf = reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(hdr) + p.xfer_off) + q * (32 * 8);
-  SpmmUnit nxt;
-  if (u_begin < u_end) nxt = p.units[u_begin];
-#pragma unroll 1
-  for (int u = u_begin; u < u_end; ++u) {
-    const SpmmUnit un = nxt;
-    if (u + 1 < u_end) nxt = p.units[u + 1];
-    if (!mbar_wait_bounded(baddr(&hdr->acc_full[acc]), acc_phase, ctl, ST_TIMEOUT_EPILOGUE)) break;
-    tc_fence_after();
-    if (g < un.nrows) {
-      const int e = un.row0 + g;
-      const int64_t row = static_cast<int64_t>(e / slabs) * p.R + (e % slabs) * p.Rs + rrow;
-      const bool present = (un.row_mask >> g) & 1;
-#pragma unroll 1
-      for (int c = 0; c < kRsN / 32; ++c) {
-        const int n = un.n0 + c * 32;
-        if (n >= p.N) break;
-        uint32_t v[32];
-        if (present) {
-          tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
-                                 static_cast<uint32_t>(acc * kRsN + c * 32),
-                             v);
-          tmem_ld_wait();
-        } else {
-#pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] = 0u;
-        }
-        const int64_t eo = row * p.ldc + n;  // element offset, the same in every peer's C
-        const int piece0 = (c % kChunksPerFlush) * (32 * kEsz / 16);  // first 16-byte piece of this chunk
-        if constexpr (kF32) {
-          float* dst = static_cast<float*>(p.c_ptr) + eo;
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const uint4 val = make_uint4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
-            if (n + 4 * i < p.N) {
-              reinterpret_cast<uint4*>(dst)[i] = val;
-              if (!staged) {
-#pragma unroll 1
-                for (int pp = 0; pp < p.n_peers; ++pp)
-                  reinterpret_cast<uint4*>(static_cast<float*>(p.peer_c[pp]) + eo)[i] = val;
-              }
-            }
-            if (staged) xf[lane * 8 + ((piece0 + i) ^ (lane & 7))] = val;
-          }
-        } else {
-          __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(p.c_ptr) + eo;
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            uint32_t w[4];
-#pragma unroll
-            for (int h = 0; h < 4; ++h) {
-              const __nv_bfloat162 b2 = __floats2bfloat162_rn(__uint_as_float(v[8 * i + 2 * h]),
-                                                              __uint_as_float(v[8 * i + 2 * h + 1]));
-              w[h] = *reinterpret_cast<const uint32_t*>(&b2);
-            }
-            const uint4 val = make_uint4(w[0], w[1], w[2], w[3]);
-            if (n + 8 * i < p.N) {
-              reinterpret_cast<uint4*>(dst)[i] = val;
-              if (!staged) {
-#pragma unroll 1
-                for (int pp = 0; pp < p.n_peers; ++pp)
-                  reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.peer_c[pp]) + eo)[i] = val;
-              }
-            }
-            if (staged) xf[lane * 8 + ((piece0 + i) ^ (lane & 7))] = val;
-          }
-        }
-        // flush the staged 128-byte segments after the segment's last chunk
-        if (staged && (c % kChunksPerFlush == kChunksPerFlush - 1 || n + 32 >= p.N ||
-                       c == kRsN / 32 - 1)) {
-          __syncwarp();
-          const int nseg0 = un.n0 + (c - c % kChunksPerFlush) * 32;  // first column of the segment
-          const int64_t row_w = row - lane;                             // the warp's first row
-          const int pc = lane & 7;
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const int r = 4 * i + (lane >> 3);
-            const int col = nseg0 + pc * (16 / kEsz);
-            if (col < p.N && pc < (c % kChunksPerFlush + 1) * (32 * kEsz / 16)) {
-              const uint4 val = xf[r * 8 + (pc ^ (r & 7))];
-              const int64_t off = (row_w + r) * p.ldc + col;
-#pragma unroll 1
-              for (int pp = 0; pp < p.n_peers; ++pp)
-                *reinterpret_cast<uint4*>(static_cast<uint8_t*>(p.peer_c[pp]) + off * kEsz) = val;
-            }
-          }
-          __syncwarp();
-        }
-      }
-    }
-    tc_fence_before();
-    __syncwarp();
-    if (lane == 0) mbar_arrive(baddr(&hdr->acc_empty[acc]));
-    acc ^= 1;
-    if (acc == 0) acc_phase ^= 1u;
-  }
-  // peer stores are visible system-wide before this CTA retires
-  if (p.n_peers > 0) __threadfence_system();
 }
 
 template <bool kF32>

@@ -9,9 +9,11 @@ import pytest
 import bsp
 from helpers import rand_bsr
 
-STRATS = [("naive", {}), ("snf", {}), ("dda", {}), ("dda", dict(steps_per_stage=2)),
+# DDA picks the single-CTA row-stacked kernel (variant 1) or the CTA-pair
+# kernel (variant 2) by estimated cost; group_mma=4 / 5 force one of them.
+STRATS = [("naive", {}), ("snf", {}), ("dda", dict(group_mma=4)), ("dda", dict(group_mma=4, steps_per_stage=1)),
           ("dda", dict(group_mma=2)), ("dda", dict(group_mma=3)), ("snf", dict(no_load_balance=1)),
-          ("dda", dict(no_load_balance=1, producers=2))]
+          ("dda", dict(group_mma=4, no_load_balance=1, producers=2))]
 
 SHAPES = [(1024, 1024, 256, 32, 32, 0.1), (512, 768, 200, 32, 32, 0.3), (512, 512, 384, 64, 64, 0.4),
           (768, 512, 128, 96, 32, 0.5), (1024, 512, 64, 512, 64, 0.5), (256, 256, 8, 32, 32, 0.0),
@@ -211,3 +213,79 @@ def test_planner_rejects_bad_shapes():
     bad = np.array([0, 2, 1, 1, 1, 1, 1, 1, 1], np.int32)  # decreasing row_ptr
     with pytest.raises(bsp.BspError):
         bsp.inspect_spmm_plan(256, 256, 32, 32, bad, [0, 1], 128)
+
+
+PAIR_OPTS = [dict(group_mma=5), dict(group_mma=5, steps_per_stage=1),
+             dict(group_mma=5, no_load_balance=1, producers=2), dict(group_mma=5, max_ctas=20)]
+
+
+@pytest.mark.parametrize("shape", SHAPES, ids=[f"{s[0]}x{s[1]}x{s[2]}R{s[3]}C{s[4]}p{s[5]}" for s in SHAPES])
+@pytest.mark.parametrize("opts", PAIR_OPTS, ids=[str(o) for o in PAIR_OPTS])
+def test_pair_schedule_covers_work_exactly_once(shape, opts):
+    """CTA-pair plans: CTA 2c+r of pair c holds entries r*G.. of each pair
+    unit; both CTAs walk stage lists of equal length; every entry's blocks
+    appear once per 256-column chunk, each at the TMA row of its block, and
+    every absent slot points at a box above the A tensor (zero fill)."""
+    M, K, N, R, C, p = shape
+    rng = np.random.default_rng(int(M + K + N + R + 1000 * p))
+    rp, ci, _ = rand_bsr(rng, M, K, R, C, p)
+    plan = bsp.inspect_spmm_plan(M, K, R, C, rp, ci, N, bsp.DDA, opts=bsp.make_opts(**opts))
+    assert plan["variant"] == 2 and plan["ctas"] % 2 == 0 and plan["ctas"] <= 148
+    units, cta, steps = plan["unit_table"], plan["cta_begin"], plan["step_table"]
+    st, cst = plan["stage_table"], plan["cta_stage_begin"]
+    G, Rs, kc, nsub = plan["group_rows"], plan["slab"], plan["kc"], plan["nsub"]
+    slabs, nkc = R // Rs, C // kc
+    assert G * Rs == 128 and plan["step_stride"] == 1 + 2 * G
+    FIRST, LAST, EMPTY, TWO = 1 << 24, 1 << 25, 1 << 26, 1 << 27
+    seen = {}
+    for pc in range(plan["ctas"] // 2):
+        lead = range(cta[2 * pc], cta[2 * pc + 1])
+        peer = range(cta[2 * pc + 1], cta[2 * pc + 2])
+        assert len(lead) == len(peer)
+        assert cst[2 * pc + 1] - cst[2 * pc] == cst[2 * pc + 2] - cst[2 * pc + 1]
+        for r, rng_u in enumerate((lead, peer)):
+            rows = st[cst[2 * pc + r]:cst[2 * pc + r + 1]]
+            k = 0
+            for ui in rng_u:
+                row0, nent, _, n0, _, sb, se, mask = (int(x) for x in units[ui])
+                assert n0 % 256 == 0 and 0 <= nent <= G
+                items = [(j, kci) for j in range(sb, se) for kci in range(nkc)]
+                if not items:
+                    assert rows[k, 0] & (FIRST | LAST | EMPTY) == FIRST | LAST | EMPTY
+                    k += 1
+                    continue
+                i = 0
+                while i < len(items):
+                    f = int(rows[k, 0])
+                    n_in = 2 if f & TWO else 1
+                    assert n_in <= nsub and bool(f & FIRST) == (i == 0) and not f & EMPTY
+                    assert rows[k, 1] == (n0 // 64 + 2 * r if N % 64 == 0 else n0 + 128 * r)
+                    for q in range(n_in):
+                        j, kci = items[i + q]
+                        assert rows[k, 3 + q] == steps[j, 0] * C + kci * kc
+                        for g in range(4):
+                            ay = int(rows[k, 5 + 4 * q + g])
+                            b = int(steps[j, 1 + r * G + g]) if g < G else -1
+                            if g < nent and b >= 0:
+                                assert ci[b] == steps[j, 0] and rp[(row0 + g) // slabs] <= b < rp[(row0 + g) // slabs + 1]
+                                assert ay == b * R + ((row0 + g) % slabs) * Rs
+                                key = (b, (row0 + g) % slabs, kci, n0)
+                                seen[key] = seen.get(key, 0) + 1
+                            else:
+                                assert ay == -Rs
+                    i += n_in
+                    assert bool(f & LAST) == (i >= len(items))
+                    k += 1
+            assert k == len(rows)
+    assert len(seen) == int(rp[-1]) * slabs * nkc * ((N + 255) // 256)
+    assert all(v == 1 for v in seen.values())
+
+
+def test_dda_picks_pair_kernel_only_where_it_pays():
+    """Dense-enough patterns go to the CTA-pair kernel, sparse ones stay on
+    the single-CTA kernel (the pair's wider column unions cost more there)."""
+    for p, want in [(0.05, 1), (0.5, 2)]:
+        rng = np.random.default_rng(77)
+        rp, ci, _ = rand_bsr(rng, 4096, 4096, 32, 32, p)
+        plan = bsp.inspect_spmm_plan(4096, 4096, 32, 32, rp, ci, 4096, bsp.DDA)
+        assert plan["variant"] == want, (p, plan["variant"])

@@ -22,7 +22,17 @@ def _bsp():
     return bsp
 
 
-STRATS = ["naive", "snf", "dda"]
+# strategy names of the reference plus the two DDA kernels forced explicitly
+# (plain "dda" picks between them by estimated cost)
+VARIANTS = {"naive": ("naive", {}), "snf": ("snf", {}), "dda": ("dda", {}),
+            "dda_1cta": ("dda", {"group_mma": 4}), "dda_pair": ("dda", {"group_mma": 5})}
+STRATS = list(VARIANTS)
+
+
+def _sv(bsp, name, **extra):
+    """(strategy id, Opts) of a VARIANTS name, with extra option fields."""
+    s, o = VARIANTS[name]
+    return bsp.STRATEGIES[s], bsp.make_opts(**{**o, **extra})
 
 # (M, K, N, R, C, density)
 CASES = [
@@ -46,7 +56,8 @@ def _run(bsp, M, K, N, R, C, rp, ci, vals, B, strategy, c_type=0, opts=None):
 
     A = bsp.DeviceBSR.from_host(M, K, R, C, rp, ci, vals)
     Bd = bsp.to_device_bf16(B)
-    out = bsp.spmm(A, Bd, strategy=bsp.STRATEGIES[strategy], c_type=c_type, opts=opts)
+    sid, vopts = _sv(bsp, strategy)
+    out = bsp.spmm(A, Bd, strategy=sid, c_type=c_type, opts=opts if opts is not None else vopts)
     if c_type == bsp.F32:
         return out.cpu().numpy()
     return bsp.to_host_bits(out)
@@ -110,7 +121,8 @@ def test_spmm_empty_matrix_writes_zeros(strategy):
     A = bsp.DeviceBSR.from_host(M, K, R, C, rp, ci, np.zeros(0, np.uint16))
     B = bsp.to_device_bf16(rand_dense(np.random.default_rng(0), K, N))
     C_ = torch.full((M, N), 7.0, dtype=torch.bfloat16, device="cuda")
-    plan = bsp.SpmmPlan(bsp.device(), A, N, bsp.STRATEGIES[strategy])
+    sid, vopts = _sv(bsp, strategy)
+    plan = bsp.SpmmPlan(bsp.device(), A, N, sid, opts=vopts)
     plan.execute(A, B, C_)
     bsp.device().synchronize()
     assert torch.count_nonzero(C_).item() == 0
@@ -129,7 +141,8 @@ def test_spmm_overwrites_stale_output(strategy):
     gold = oracle.spmm_bf16(rp, ci, vals, M, K, R, C, B, N)
     A = bsp.DeviceBSR.from_host(M, K, R, C, rp, ci, vals)
     C_ = torch.full((M, N), float("nan"), dtype=torch.bfloat16, device="cuda")
-    plan = bsp.SpmmPlan(bsp.device(), A, N, bsp.STRATEGIES[strategy])
+    sid, vopts = _sv(bsp, strategy)
+    plan = bsp.SpmmPlan(bsp.device(), A, N, sid, opts=vopts)
     plan.execute(A, bsp.to_device_bf16(B), C_)
     bsp.device().synchronize()
     assert_bf16_close(bsp.to_host_bits(C_), gold)
@@ -146,7 +159,7 @@ def test_spmm_duplicate_and_unsorted_columns():
     B = rand_dense(rng, K, N)
     gold = oracle.spmm_bf16(rp, ci, vals, M, K, R, C, B, N)
     for s in STRATS:
-        out = _run(bsp, M, K, N, R, C, rp, ci, vals, B, s, opts=bsp.make_opts(group_rows=4) if s == "dda" else None)
+        out = _run(bsp, M, K, N, R, C, rp, ci, vals, B, s)
         assert_bf16_close(out, gold, what=s)
 
 
@@ -193,7 +206,8 @@ def test_spmm_host_buffer_api(strategy):
     rp, ci, vals = rand_bsr(rng, M, K, R, C, 0.10)
     B = rand_dense(rng, K, N)
     gold = oracle.spmm_bf16(rp, ci, vals, M, K, R, C, B, N)
-    out = bsp.spmm_host(M, K, R, C, rp, ci, vals, B, N, strategy=bsp.STRATEGIES[strategy])
+    sid, vopts = _sv(bsp, strategy)
+    out = bsp.spmm_host(M, K, R, C, rp, ci, vals, B, N, strategy=sid, opts=vopts)
     assert_bf16_close(out, gold)
 
 

@@ -259,6 +259,54 @@ bsp_status bsp_sddmm_host_profile(bsp_device* dev, int64_t M, int64_t N, int32_t
                                   bsp_strategy strategy, const bsp_sddmm_opts* opts, int32_t iters,
                                   double* ms_per_launch);
 
+/* ---- SpGEMM: C_bsr = A_bsr[M x K] * B_bsr[K x N] -------------------------
+ * Device form of bsr_matrix<T>::spgemm (sparse_common/bsr_matrix.hpp:741-810),
+ * which the reference has only as a CPU golden: A has Ra x Ca blocks, B has
+ * Ca x Cb blocks (the reference asserts W_A == H_B and C_A == R_B, 743-744),
+ * C has Ra x Cb blocks.  C's pattern is every (i, j) with some A[i, k] and
+ * B[k, j] stored, columns ascending per block-row (the reference's row-major
+ * walk of its present[] map, 786-802); each block is accumulated in fp32 and
+ * rounded to bf16 once.  Repeated column indices inside a row of A or B
+ * contribute every stored block, as in the reference's loops.
+ * Block sizes: Ra, Ca, Cb each 32, 64 or 128.
+ *
+ * The plan holds C's pattern (computed on the host from A's and B's
+ * patterns); read it with bsp_spgemm_pattern, allocate nnzb * Ra * Cb bf16
+ * values, then execute. */
+typedef struct bsp_spgemm_plan bsp_spgemm_plan;
+
+bsp_status bsp_spgemm_plan_create(bsp_device* dev, const bsp_bsr_desc* A,
+                                  const int32_t* a_host_row_ptr, const int32_t* a_host_col_idx,
+                                  const bsp_bsr_desc* B, const int32_t* b_host_row_ptr,
+                                  const int32_t* b_host_col_idx, const bsp_spmm_opts* opts,
+                                  bsp_spgemm_plan** out);
+/* C's pattern: *nnzb_out always; row_ptr_out[M/Ra + 1] and col_idx_out[nnzb]
+ * (host arrays) when not NULL. */
+bsp_status bsp_spgemm_pattern(const bsp_spgemm_plan* plan, int64_t* nnzb_out, int32_t* row_ptr_out,
+                              int32_t* col_idx_out);
+/* A->values, B->values: device bf16 blocks; out_values: device, nnzb*Ra*Cb. */
+bsp_status bsp_spgemm_execute(const bsp_spgemm_plan* plan, const bsp_bsr_desc* A,
+                              const bsp_bsr_desc* B, void* out_values, void* stream);
+bsp_status bsp_spgemm_plan_destroy(bsp_spgemm_plan* plan);
+/* info[0] units, [1] grid, [2] steps, [3] block products (A[i,k]*B[k,j] pairs),
+ * [4] output blocks, [5] kc, [6] stages, [7] sub-steps per stage,
+ * [8] table bytes, [9] shared memory, [10] TMEM columns, [11] segments per
+ * unit, [12] producer warps. */
+bsp_status bsp_spgemm_plan_info(const bsp_spgemm_plan* plan, int64_t info[16]);
+
+/* Host-buffer SpGEMM (bsr_matrix<T>::spgemm semantics: host BSR in, host BSR
+ * out).  With out_values == NULL only *out_nnzb is written (size query);
+ * otherwise out_row_ptr[M/Ra + 1], out_col_idx[out_cap], out_values[out_cap *
+ * Ra * Cb] receive C and out_cap must be >= its block count.  iters > 0 also
+ * times that many device launches (*ms_per_launch, may be NULL otherwise). */
+bsp_status bsp_spgemm_host(bsp_device* dev, int64_t M, int64_t K, int64_t N, int32_t Ra, int32_t Ca,
+                           int32_t Cb, int64_t a_nnzb, const int32_t* a_row_ptr,
+                           const int32_t* a_col_idx, const uint16_t* a_values, int64_t b_nnzb,
+                           const int32_t* b_row_ptr, const int32_t* b_col_idx,
+                           const uint16_t* b_values, int64_t out_cap, int64_t* out_nnzb,
+                           int32_t* out_row_ptr, int32_t* out_col_idx, uint16_t* out_values,
+                           const bsp_spmm_opts* opts, int32_t iters, double* ms_per_launch);
+
 /* ---- multi-GPU helpers (host logic; the exchange itself is NCCL) --------
  * Contiguous block-row ranges for `parts` GPUs balanced by nonzero-block
  * count (a generalisation of the reference's serpentine balancer,

@@ -39,6 +39,21 @@ bsp_status bsp_sddmm_plan_inspect(int64_t M, int64_t N, int32_t R, int32_t C, in
                                   int32_t sm_count, int32_t max_smem, int64_t info[16],
                                   int32_t* units_out, int32_t* cta_begin_out);
 
+/* SpGEMM planner (A: M x K with Ra x Ca blocks, B: K x N with Ca x Cb).
+ * info[16] as bsp_spgemm_plan_info.  With null output buffers only `info` is
+ * filled: out_row_ptr[M/Ra + 1], out_col_idx[info[4]] (C's pattern),
+ * units_out[info[0] * 48] (step_begin, n_steps, n_ent, nseg, seg_x[8],
+ * ent_r[4], out_blk[4][8] per unit, in CTA order), steps_out[info[2] * 12]
+ * (a_y[4], b_y[8]: TMA row of each entry's A slab / segment's B block, -1
+ * absent), cta_begin_out[info[1] + 1]. */
+bsp_status bsp_spgemm_plan_inspect(int64_t M, int64_t K, int64_t N, int32_t Ra, int32_t Ca,
+                                   int32_t Cb, int64_t a_nnzb, const int32_t* a_row_ptr,
+                                   const int32_t* a_col_idx, int64_t b_nnzb,
+                                   const int32_t* b_row_ptr, const int32_t* b_col_idx,
+                                   const bsp_spmm_opts* opts, int32_t sm_count, int32_t max_smem,
+                                   int64_t info[16], int32_t* out_row_ptr, int32_t* out_col_idx,
+                                   int32_t* units_out, int32_t* steps_out, int32_t* cta_begin_out);
+
 #ifdef __cplusplus
 }
 #endif

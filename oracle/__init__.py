@@ -54,6 +54,9 @@ def lib():
         _lib.bsp_oracle_sddmm_bf16_mt.argtypes = [I, I, I, I, P, P, P, I, P, P, P, I, I, _i32]
         _lib.bsp_oracle_sddmm_f32.argtypes = [I, I, I, I, P, P, P, I, P, P, P, I, I]
         _lib.bsp_oracle_serpentine.argtypes = [I, I, P, P]
+        _lib.bsp_oracle_spgemm_symbolic.argtypes = [I, I, P, P, P, P, P, P]
+        _lib.bsp_oracle_spgemm_symbolic.restype = _i64
+        _lib.bsp_oracle_spgemm_bf16.argtypes = [I, I, I, I, P, P, P, P, P, P, P, P, P]
     return _lib
 
 
@@ -81,6 +84,8 @@ def ref():
         _ref.ref_spmm_bf16_timed.restype = ctypes.c_double
         _ref.ref_sddmm_bf16_timed.argtypes = [I, I, I, I, P, P, P, I, P, P, I, I, _i32, _i32]
         _ref.ref_sddmm_bf16_timed.restype = ctypes.c_double
+        _ref.ref_spgemm_bf16.argtypes = [I, I, I, I, I, P, P, P, I, I, I, P, P, P, I, P, P, P]
+        _ref.ref_spgemm_bf16.restype = _i64
     return _ref
 
 
@@ -160,6 +165,33 @@ def serpentine(n: int, parts: int):
     slot = np.zeros(n, dtype=np.int32)
     lib().bsp_oracle_serpentine(n, parts, _ptr(owner), _ptr(slot))
     return owner, slot
+
+
+def spgemm_pattern(a_rp, a_ci, b_rp, b_ci, nbc_b):
+    """Block pattern (row_ptr, col_idx) of A_bsr @ B_bsr (bsp_oracle_spgemm_symbolic)."""
+    a_rp, a_ci = _c(a_rp, np.int32), _c(a_ci, np.int32)
+    b_rp, b_ci = _c(b_rp, np.int32), _c(b_ci, np.int32)
+    nbr = a_rp.size - 1
+    out_rp = np.zeros(nbr + 1, dtype=np.int32)
+    n = int(lib().bsp_oracle_spgemm_symbolic(nbr, nbc_b, _ptr(a_rp), _ptr(a_ci), _ptr(b_rp),
+                                             _ptr(b_ci), _ptr(out_rp), None))
+    out_ci = np.zeros(max(n, 1), dtype=np.int32)
+    lib().bsp_oracle_spgemm_symbolic(nbr, nbc_b, _ptr(a_rp), _ptr(a_ci), _ptr(b_rp), _ptr(b_ci),
+                                     _ptr(out_rp), _ptr(out_ci))
+    return out_rp, out_ci[:n]
+
+
+def spgemm_bf16(a_rp, a_ci, a_vals, Ra, Ca, b_rp, b_ci, b_vals, Cb, nbc_b):
+    """A_bsr (Ra x Ca blocks) @ B_bsr (Ca x Cb blocks) -> (row_ptr, col_idx, values) in BSR,
+    bf16 bits (bsp_oracle_spgemm_bf16)."""
+    out_rp, out_ci = spgemm_pattern(a_rp, a_ci, b_rp, b_ci, nbc_b)
+    a_rp, a_ci, a_vals = _c(a_rp, np.int32), _c(a_ci, np.int32), _c(a_vals, np.uint16)
+    b_rp, b_ci, b_vals = _c(b_rp, np.int32), _c(b_ci, np.int32), _c(b_vals, np.uint16)
+    out = np.zeros(max(out_ci.size * Ra * Cb, 1), dtype=np.uint16)
+    lib().bsp_oracle_spgemm_bf16(a_rp.size - 1, Ra, Ca, Cb, _ptr(a_rp), _ptr(a_ci), _ptr(a_vals),
+                                 _ptr(b_rp), _ptr(b_ci), _ptr(b_vals), _ptr(out_rp), _ptr(out_ci),
+                                 _ptr(out))
+    return out_rp, out_ci, out[: out_ci.size * Ra * Cb]
 
 
 # ---- the reference golden (oracle/_ref) -----------------------------------
@@ -258,3 +290,18 @@ def ref_sddmm_timed(indptr, indices, mask_data, H, W, R, C, A, B, K, rows, threa
     return float(ref().ref_sddmm_bf16_timed(H, W, R, C, _ptr(indptr), _ptr(indices),
                                             _ptr(mask_data), K, _ptr(A), _ptr(B), rows[0],
                                             rows[1], threads, reps))
+
+
+def ref_spgemm_bf16(a_rp, a_ci, a_vals, Ha, Wa, Ra, Ca, b_rp, b_ci, b_vals, Wb, Cb):
+    """(row_ptr, col_idx, values) of A @ B from the reference's bsr_matrix::spgemm."""
+    r = ref()
+    a_rp, a_ci, a_vals = _c(a_rp, np.int32), _c(a_ci, np.int32), _c(a_vals, np.uint16)
+    b_rp, b_ci, b_vals = _c(b_rp, np.int32), _c(b_ci, np.int32), _c(b_vals, np.uint16)
+    args = (Ha, Wa, Ra, Ca, int(a_rp[-1]), _ptr(a_rp), _ptr(a_ci), _ptr(a_vals), Wb, Cb,
+            int(b_rp[-1]), _ptr(b_rp), _ptr(b_ci), _ptr(b_vals))
+    n = int(r.ref_spgemm_bf16(*args, 0, None, None, None))
+    out_rp = np.zeros(Ha // Ra + 1, dtype=np.int32)
+    out_ci = np.zeros(max(n, 1), dtype=np.int32)
+    out = np.zeros(max(n * Ra * Cb, 1), dtype=np.uint16)
+    r.ref_spgemm_bf16(*args, n, _ptr(out_rp), _ptr(out_ci), _ptr(out))
+    return out_rp, out_ci[:n], out[: n * Ra * Cb]

@@ -168,6 +168,80 @@ void bsp_oracle_sddmm_f32(int64_t H, int64_t W, int64_t R, int64_t C, const int3
   free(dot);
 }
 
+/* bsr_matrix.hpp:741-810, pattern part: block (i, j) of A*B exists when some
+ * A[i, k] and B[k, j] both exist; each output row lists its columns in
+ * ascending order (the reference walks a dense present[] map row-major). */
+int64_t bsp_oracle_spgemm_symbolic(int64_t nbr_a, int64_t nbc_b, const int32_t* a_rp,
+                                   const int32_t* a_ci, const int32_t* b_rp, const int32_t* b_ci,
+                                   int32_t* out_rp, int32_t* out_ci) {
+  uint8_t* seen = (uint8_t*)calloc((size_t)(nbc_b > 0 ? nbc_b : 1), 1);
+  int64_t total = 0;
+  out_rp[0] = 0;
+  for (int64_t i = 0; i < nbr_a; ++i) {
+    for (int32_t a = a_rp[i]; a < a_rp[i + 1]; ++a) {
+      const int32_t k = a_ci[a];
+      for (int32_t b = b_rp[k]; b < b_rp[k + 1]; ++b) seen[b_ci[b]] = 1;
+    }
+    for (int64_t j = 0; j < nbc_b; ++j) {
+      if (!seen[j]) continue;
+      if (out_ci) out_ci[total] = (int32_t)j;
+      ++total;
+      seen[j] = 0;
+    }
+    out_rp[i + 1] = (int32_t)total;
+  }
+  free(seen);
+  return total;
+}
+
+/* bsr_matrix.hpp:741-810, values: for every pair (A[i, k], B[k, j]) in A's
+ * storage order and then B's, each element (r, p) of the product block is an
+ * fp32 sum over c from zero in column order, added to the fp32 accumulator of
+ * output block (i, j) (started at zero); every block is rounded to bf16 once.
+ * Ra x Ca blocks of A, Ca x Cb blocks of B, Ra x Cb blocks out. */
+void bsp_oracle_spgemm_bf16(int64_t nbr_a, int64_t Ra, int64_t Ca, int64_t Cb, const int32_t* a_rp,
+                            const int32_t* a_ci, const uint16_t* a_vals, const int32_t* b_rp,
+                            const int32_t* b_ci, const uint16_t* b_vals, const int32_t* out_rp,
+                            const int32_t* out_ci, uint16_t* out_vals) {
+  const int64_t ob = Ra * Cb;
+  float* acc = NULL;
+  int64_t acc_cap = 0;
+  for (int64_t i = 0; i < nbr_a; ++i) {
+    const int32_t o0 = out_rp[i], no = out_rp[i + 1] - out_rp[i];
+    if (no == 0) continue;
+    if ((int64_t)no * ob > acc_cap) {
+      acc_cap = (int64_t)no * ob;
+      acc = (float*)realloc(acc, (size_t)acc_cap * sizeof(float));
+    }
+    memset(acc, 0, (size_t)no * ob * sizeof(float));
+    for (int32_t a = a_rp[i]; a < a_rp[i + 1]; ++a) {
+      const int32_t k = a_ci[a];
+      const uint16_t* ab = a_vals + (int64_t)a * Ra * Ca;
+      for (int32_t b = b_rp[k]; b < b_rp[k + 1]; ++b) {
+        const int32_t j = b_ci[b];
+        int32_t lo = 0, hi = no; /* slot of column j in output row i */
+        while (lo < hi) {
+          const int32_t mid = (lo + hi) / 2;
+          if (out_ci[o0 + mid] < j) lo = mid + 1;
+          else hi = mid;
+        }
+        float* dst = acc + (int64_t)lo * ob;
+        const uint16_t* bb = b_vals + (int64_t)b * Ca * Cb;
+        for (int64_t r = 0; r < Ra; ++r)
+          for (int64_t p2 = 0; p2 < Cb; ++p2) {
+            float sum = 0.0f;
+            for (int64_t c = 0; c < Ca; ++c)
+              sum += bsp_oracle_bf16_to_f32(ab[r * Ca + c]) * bsp_oracle_bf16_to_f32(bb[c * Cb + p2]);
+            dst[r * Cb + p2] += sum;
+          }
+      }
+    }
+    for (int64_t e = 0; e < (int64_t)no * ob; ++e)
+      out_vals[(int64_t)o0 * ob + e] = bsp_oracle_f32_to_bf16(acc[e]);
+  }
+  free(acc);
+}
+
 /* bsr_spmm_multicore_load_balanced_new_DM.cpp:371-393.  Pass `it` (from 1)
  * hands the next `parts` heaviest rows, front of `perm`, to workers 0..parts-1
  * in order, then the `parts` rows counted back from the end of `perm` to

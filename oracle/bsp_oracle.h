@@ -55,6 +55,16 @@ void bsp_oracle_sddmm_f32(int64_t H, int64_t W, int64_t R, int64_t C, const int3
  * Follows block_spmm/inc/host_code/bsr_spmm_multicore_load_balanced_new_DM.cpp:346-393. */
 void bsp_oracle_serpentine(int64_t n, int64_t parts, int32_t* owner_of_pos, int32_t* slot_of_pos);
 
+/* SpGEMM (bsr_matrix.hpp:741-810): symbolic pattern of A*B (returns the block
+ * count, fills out_rp[nbr_a+1] and, when non-null, out_ci), then the values. */
+int64_t bsp_oracle_spgemm_symbolic(int64_t nbr_a, int64_t nbc_b, const int32_t* a_rp,
+                                   const int32_t* a_ci, const int32_t* b_rp, const int32_t* b_ci,
+                                   int32_t* out_rp, int32_t* out_ci);
+void bsp_oracle_spgemm_bf16(int64_t nbr_a, int64_t Ra, int64_t Ca, int64_t Cb, const int32_t* a_rp,
+                            const int32_t* a_ci, const uint16_t* a_vals, const int32_t* b_rp,
+                            const int32_t* b_ci, const uint16_t* b_vals, const int32_t* out_rp,
+                            const int32_t* out_ci, uint16_t* out_vals);
+
 /* Threaded driver: runs bsp_oracle_spmm_bf16 / _sddmm_bf16 on `nthreads`
  * disjoint block-row ranges split by equal block counts. */
 void bsp_oracle_spmm_bf16_mt(int64_t H, int64_t W, int64_t R, int64_t C, const int32_t* indptr,

@@ -9,7 +9,7 @@
 //   bsr_matrix<bfloat16>::omp_spmm_bf16   sparse_common/bsr_matrix.hpp:909-955
 //   bsr_matrix<float>::spmm               sparse_common/bsr_matrix.hpp:859-881
 //   bsr_matrix<T>::sddmm                  sparse_common/bsr_matrix.hpp:816-857
-//   bsr_matrix<float>::spgemm             sparse_common/bsr_matrix.hpp:741-810
+//   bsr_matrix<T>::spgemm                 sparse_common/bsr_matrix.hpp:741-810
 //   bsr_matrix<T>(H,W,R,C,n,fill,content) sparse_common/bsr_matrix.hpp:244-408
 //   dense_matrix<T>(H,W,content)          sparse_common/bsr_matrix.hpp:50-75
 //   check_bfloat16_vector_pcc             sparse_common/bmm_op.hpp:79-113
@@ -117,6 +117,27 @@ int ref_sddmm_f32(int64_t H, int64_t W, int64_t R, int64_t C, int64_t nnzb, cons
   bsr_matrix<float> o = m.sddmm(a, b);
   std::memcpy(out, o.data.data(), o.data.size() * sizeof(float));
   return (int)o.nblocks;
+}
+
+// A (Ha x Wa, Ra x Ca blocks) times B (Wa x Wb, Ca x Cb blocks) through the
+// reference's spgemm.  Returns the output block count; the outputs are copied
+// only when it is <= cap (call with cap = 0 first to learn it).
+int64_t ref_spgemm_bf16(int64_t Ha, int64_t Wa, int64_t Ra, int64_t Ca, int64_t nnzb_a,
+                        const int32_t* a_rp, const int32_t* a_ci, const uint16_t* a_vals, int64_t Wb,
+                        int64_t Cb, int64_t nnzb_b, const int32_t* b_rp, const int32_t* b_ci,
+                        const uint16_t* b_vals, int64_t cap, int32_t* out_rp, int32_t* out_ci,
+                        uint16_t* out_vals) {
+  auto a = make_bsr_bf16(Ha, Wa, Ra, Ca, nnzb_a, a_rp, a_ci, a_vals);
+  auto b = make_bsr_bf16(Wa, Wb, Ca, Cb, nnzb_b, b_rp, b_ci, b_vals);
+  bsr_matrix<bfloat16> o = a.spgemm(b);
+  const int64_t n = (int64_t)o.nblocks;
+  if (n <= cap) {
+    if (out_rp) std::memcpy(out_rp, o.indptr.data(), o.indptr.size() * sizeof(int));
+    if (out_ci) std::memcpy(out_ci, o.indices.data(), o.indices.size() * sizeof(int));
+    if (out_vals)
+      for (size_t i = 0; i < o.data.size(); ++i) out_vals[i] = o.data[i].to_uint16();
+  }
+  return n;
 }
 
 float ref_pcc_bf16(const uint16_t* a, const uint16_t* b, int64_t n) {

@@ -32,7 +32,8 @@ EXPORTS = [
     "bsp_partition_rows", "bsp_serpentine_assign", "bsp_spmm_host_profile",
     "bsp_sddmm_host_profile", "bsp_spmm_plan_inspect", "bsp_sddmm_plan_inspect",
     "bsp_spmm_noalloc", "bsp_spmm_execute_replicated", "bsp_ipc_export", "bsp_ipc_import",
-    "bsp_ipc_close",
+    "bsp_ipc_close", "bsp_spgemm_plan_create", "bsp_spgemm_pattern", "bsp_spgemm_execute",
+    "bsp_spgemm_plan_destroy", "bsp_spgemm_plan_info", "bsp_spgemm_host", "bsp_spgemm_plan_inspect",
 ]
 IPC_HANDLE_BYTES = 64
 
@@ -116,6 +117,17 @@ def lib():
         "bsp_ipc_close": (S, [P, P]),
         "bsp_sddmm_plan_inspect": (S, [I64, I64, I32, I32, I64, P, P, I64, S, ctypes.POINTER(Opts),
                                        I32, I32, P, P, P]),
+        "bsp_spgemm_plan_create": (S, [P, ctypes.POINTER(BsrDesc), P, P, ctypes.POINTER(BsrDesc),
+                                       P, P, ctypes.POINTER(Opts), ctypes.POINTER(P)]),
+        "bsp_spgemm_pattern": (S, [P, ctypes.POINTER(I64), P, P]),
+        "bsp_spgemm_execute": (S, [P, ctypes.POINTER(BsrDesc), ctypes.POINTER(BsrDesc), P, P]),
+        "bsp_spgemm_plan_destroy": (S, [P]),
+        "bsp_spgemm_plan_info": (S, [P, ctypes.POINTER(I64)]),
+        "bsp_spgemm_host": (S, [P, I64, I64, I64, I32, I32, I32, I64, P, P, P, I64, P, P, P, I64,
+                                ctypes.POINTER(I64), P, P, P, ctypes.POINTER(Opts), I32,
+                                ctypes.POINTER(ctypes.c_double)]),
+        "bsp_spgemm_plan_inspect": (S, [I64, I64, I64, I32, I32, I32, I64, P, P, I64, P, P,
+                                        ctypes.POINTER(Opts), I32, I32, P, P, P, P, P, P]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -385,6 +397,129 @@ def sddmm_host(M, N, R, C, row_ptr, col_idx, mask_values, A, B, K, strategy=NAIV
     _check(lib().bsp_sddmm_host(dev.handle, M, N, R, C, nnzb, _ptr(rp), _ptr(ci), _ptr(mv),
                                 _ptr(a), _ptr(b), K, _ptr(o), strategy, ctypes.byref(opt)))
     return o
+
+
+# ------------------------------------------------------------------ SpGEMM --
+SPGEMM_INFO_KEYS = ["units", "ctas", "steps", "pairs", "out_nnzb", "kc", "stages",
+                    "steps_per_stage", "plan_bytes", "smem_bytes", "tmem_cols", "nseg_max",
+                    "producers"]
+
+
+class SpgemmPlan:
+    """C = A @ B for two BSR matrices (bsr_matrix<T>::spgemm,
+    sparse_common/bsr_matrix.hpp:741-810); the plan holds C's pattern."""
+
+    def __init__(self, dev: Device, A: DeviceBSR, B: DeviceBSR, opts=None):
+        self.dev = dev
+        self.M, self.N, self.Ra, self.Cb = A.rows, B.cols, A.R, B.C
+        da, db = A.desc(), B.desc()
+        h = ctypes.c_void_p()
+        o = opts if opts is not None else Opts()
+        _check(lib().bsp_spgemm_plan_create(dev.handle, ctypes.byref(da), _ptr(A.h_row_ptr),
+                                            _ptr(A.h_col_idx), ctypes.byref(db), _ptr(B.h_row_ptr),
+                                            _ptr(B.h_col_idx), ctypes.byref(o), ctypes.byref(h)))
+        self.handle = h
+        n = ctypes.c_int64()
+        _check(lib().bsp_spgemm_pattern(h, ctypes.byref(n), None, None))
+        self.nnzb = int(n.value)
+        self.row_ptr = np.zeros(self.M // self.Ra + 1, np.int32)
+        self.col_idx = np.zeros(max(self.nnzb, 1), np.int32)
+        _check(lib().bsp_spgemm_pattern(h, ctypes.byref(n), _ptr(self.row_ptr), _ptr(self.col_idx)))
+        self.col_idx = self.col_idx[: self.nnzb]
+
+    def info(self) -> dict:
+        arr = (ctypes.c_int64 * 16)()
+        _check(lib().bsp_spgemm_plan_info(self.handle, arr))
+        return {k: int(arr[i]) for i, k in enumerate(SPGEMM_INFO_KEYS)}
+
+    def execute(self, A: DeviceBSR, B: DeviceBSR, out, stream=None):
+        """out: device bf16, at least nnzb * Ra * Cb elements."""
+        da, db = A.desc(), B.desc()
+        _check(lib().bsp_spgemm_execute(self.handle, ctypes.byref(da), ctypes.byref(db), _ptr(out),
+                                        _stream_ptr(stream)))
+
+    def close(self):
+        if self.handle:
+            lib().bsp_spgemm_plan_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def spgemm(A: DeviceBSR, B: DeviceBSR, opts=None, dev: Device = None) -> DeviceBSR:
+    """One-shot C = A @ B (both BSR on the GPU); returns C as a DeviceBSR."""
+    import torch
+    dev = dev or device(A.values.device.index or 0)
+    plan = SpgemmPlan(dev, A, B, opts)
+    out = torch.empty(max(plan.nnzb * A.R * B.C, 8), dtype=torch.bfloat16, device=A.values.device)
+    plan.execute(A, B, out)
+    dev.synchronize()
+    C = DeviceBSR(A.rows, B.cols, A.R, B.C,
+                  torch.from_numpy(plan.row_ptr.copy()).to(out.device),
+                  torch.from_numpy(plan.col_idx.copy() if plan.nnzb else np.zeros(1, np.int32)).to(out.device),
+                  out, plan.row_ptr.copy(), plan.col_idx.copy())
+    plan.close()
+    return C
+
+
+def spgemm_host(M, K, N, Ra, Ca, Cb, a_row_ptr, a_col_idx, a_values, b_row_ptr, b_col_idx,
+                b_values, opts=None, dev: Device = None, iters=0):
+    """Host BSR in, host BSR out: (row_ptr, col_idx, values bf16 bits) of A @ B,
+    plus the mean launch time in ms when iters > 0."""
+    dev = dev or device(0)
+    arp = np.ascontiguousarray(a_row_ptr, dtype=np.int32)
+    aci = np.ascontiguousarray(a_col_idx, dtype=np.int32)
+    av = np.ascontiguousarray(a_values, dtype=np.uint16)
+    brp = np.ascontiguousarray(b_row_ptr, dtype=np.int32)
+    bci = np.ascontiguousarray(b_col_idx, dtype=np.int32)
+    bv = np.ascontiguousarray(b_values, dtype=np.uint16)
+    opt = opts if opts is not None else Opts()
+    n = ctypes.c_int64()
+    ms = ctypes.c_double(0.0)
+    common = (dev.handle, M, K, N, Ra, Ca, Cb, int(arp[-1]), _ptr(arp), _ptr(aci), _ptr(av),
+              int(brp[-1]), _ptr(brp), _ptr(bci), _ptr(bv))
+    _check(lib().bsp_spgemm_host(*common, 0, ctypes.byref(n), None, None, None, ctypes.byref(opt),
+                                 0, None))
+    cap = int(n.value)
+    orp = np.zeros(M // Ra + 1, np.int32)
+    oci = np.zeros(max(cap, 1), np.int32)
+    ov = np.zeros(max(cap * Ra * Cb, 8), np.uint16)
+    _check(lib().bsp_spgemm_host(*common, cap, ctypes.byref(n), _ptr(orp), _ptr(oci), _ptr(ov),
+                                 ctypes.byref(opt), iters, ctypes.byref(ms)))
+    res = (orp, oci[:cap], ov[: cap * Ra * Cb])
+    return res + (ms.value,) if iters > 0 else res
+
+
+def inspect_spgemm_plan(M, K, N, Ra, Ca, Cb, a_row_ptr, a_col_idx, b_row_ptr, b_col_idx, opts=None,
+                        sm_count=148, max_smem=232448):
+    """Run the SpGEMM planner on the host only (no GPU) and return its schedule."""
+    arp = np.ascontiguousarray(a_row_ptr, dtype=np.int32)
+    aci = np.ascontiguousarray(a_col_idx, dtype=np.int32)
+    brp = np.ascontiguousarray(b_row_ptr, dtype=np.int32)
+    bci = np.ascontiguousarray(b_col_idx, dtype=np.int32)
+    aci = aci if aci.size else np.zeros(1, np.int32)
+    bci = bci if bci.size else np.zeros(1, np.int32)
+    info = np.zeros(16, np.int64)
+    o = opts if opts is not None else Opts()
+    args = (M, K, N, Ra, Ca, Cb, int(arp[-1]), _ptr(arp), _ptr(aci), int(brp[-1]), _ptr(brp),
+            _ptr(bci), ctypes.byref(o), sm_count, max_smem, _ptr(info))
+    _check(lib().bsp_spgemm_plan_inspect(*args, None, None, None, None, None))
+    nu, ns, nb, nc = int(info[0]), int(info[2]), int(info[4]), int(info[1])
+    orp = np.zeros(M // Ra + 1, np.int32)
+    oci = np.zeros(max(nb, 1), np.int32)
+    units = np.zeros((max(nu, 1), 48), np.int32)
+    steps = np.zeros((max(ns, 1), 12), np.int32)
+    cta = np.zeros(nc + 1, np.int32)
+    _check(lib().bsp_spgemm_plan_inspect(*args, _ptr(orp), _ptr(oci), _ptr(units), _ptr(steps),
+                                         _ptr(cta)))
+    d = {k: int(info[i]) for i, k in enumerate(SPGEMM_INFO_KEYS)}
+    d.update(out_row_ptr=orp, out_col_idx=oci[:nb], unit_table=units[:nu], step_table=steps[:ns],
+             cta_begin=cta)
+    return d
 
 
 # ----------------------------------------------------------------- helpers --

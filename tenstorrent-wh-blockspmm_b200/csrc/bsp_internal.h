@@ -138,6 +138,53 @@ struct SddmmKernelParams {
   int32_t M, nseg_max, nprod, seg_bytes;
 };
 
+// ---- SpGEMM schedule ------------------------------------------------------------
+// C_bsr = A_bsr (Ra x Ca blocks) * B_bsr (Ca x Cb blocks).  A work unit is four
+// "entries" (32-row slabs of output block-rows: MMA M = 128) against up to
+// eight gathered 32-column "segments" of output block-columns (MMA N = 256).
+// Its steps walk the shared block index k: each step stacks, per entry, the
+// slab of A[i_e, k] (or a zero box) and gathers, per segment, the 32 columns
+// of B[k, j_s] (or a zero box).  The product accumulates in TMEM over the
+// unit's steps; the epilogue writes the (entry, segment) tiles whose output
+// block exists.
+constexpr int kSpgemmEnt = 4;
+constexpr int kSpgemmMaxSeg = 8;
+struct SpgemmUnit {
+  int32_t step_begin;                 // first record in the step table
+  int32_t n_steps;                    // >= 1
+  int32_t n_ent;                      // entries in use (1..4)
+  int32_t nseg;                       // segments in use (1..8)
+  int32_t seg_x[kSpgemmMaxSeg];       // column of segment s inside its block (t*32); 0 unused
+  int32_t ent_r[kSpgemmEnt];          // row of entry e's slab inside its block (slab*32)
+  int32_t out_blk[kSpgemmEnt][kSpgemmMaxSeg];  // output block of tile (e, s), -1 none
+};
+static_assert(sizeof(SpgemmUnit) == 192, "unit layout");
+
+// One step: TMA row coordinates of the operands, -1 = absent (zero box).
+//   a_y[e] = (A block index) * Ra + slab * 32, rows of A viewed as [nnzb_a*Ra, Ca]
+//   b_y[s] = (B block index) * Ca,             rows of B viewed as [nnzb_b*Ca, Cb]
+struct SpgemmStep {
+  int32_t a_y[kSpgemmEnt];
+  int32_t b_y[kSpgemmMaxSeg];
+};
+static_assert(sizeof(SpgemmStep) == 48, "step layout");
+
+struct SpgemmKernelParams {
+  CUtensorMap tm_a;  // A values [nnzb_a*Ra rows, Ca cols], box {kc, 32}
+  CUtensorMap tm_b;  // B values [nnzb_b*Ca rows, Cb cols], box {32, kc}, 64B swizzle
+  const SpgemmUnit* units;   // in CTA order
+  const SpgemmStep* steps;
+  const int32_t* cta_begin;  // [grid + 1]
+  uint16_t* out_vals;
+  unsigned int* status;
+  uint64_t timeout_ns;
+  int32_t Ra, Cb, kc, nkc;
+  int32_t sps;               // sub-steps (step, k-chunk) per pipeline stage
+  int32_t stages, stage_bytes, sub_bytes, a_slot, seg_bytes;
+  int32_t a_swizzle_mode;    // 2 = 128B (kc 64), 4 = 64B (kc 32)
+  int32_t tmem_cols, nseg_max, nprod;
+};
+
 // ---- host objects -------------------------------------------------------------
 typedef CUresult (*PFN_encodeTiled)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
                                     const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
@@ -157,6 +204,27 @@ struct bsp_device {
   size_t ws_bytes = 0;
   void* pinned = nullptr;
   size_t pinned_bytes = 0;
+};
+
+struct bsp_spgemm_plan {
+  bsp_device* dev = nullptr;
+  int64_t M = 0, K = 0, N = 0, nnzb_a = 0, nnzb_b = 0;
+  int32_t Ra = 0, Ca = 0, Cb = 0, kc = 0, nkc = 1, sps = 1;
+  int32_t grid = 0, stages = 0, stage_bytes = 0, sub_bytes = 0, smem_bytes = 0, tmem_cols = 0;
+  int32_t nseg_max = 8, nprod = 1;
+  int64_t n_units = 0, n_steps = 0;
+  int64_t pairs = 0;         // block products A[i,k] * B[k,j] (useful work)
+  uint64_t timeout_ns = 0;
+  void* d_blob = nullptr;    // units | steps | cta_begin
+  size_t blob_bytes = 0;
+  bsp::SpgemmUnit* d_units = nullptr;
+  bsp::SpgemmStep* d_steps = nullptr;
+  int32_t* d_cta_begin = nullptr;
+  // output pattern (host), sorted columns per block-row
+  std::vector<int32_t> out_row_ptr, out_col_idx;
+  std::vector<bsp::SpgemmUnit> h_units;
+  std::vector<bsp::SpgemmStep> h_steps;
+  std::vector<int32_t> h_cta_begin;
 };
 
 struct bsp_spmm_plan {
@@ -259,6 +327,13 @@ bsp_status plan_spmm_pair(bsp_spmm_plan* p, const int32_t* row_ptr, const int32_
 bsp_status launch_spmm_pair(const bsp_spmm_plan* p, const bsp_bsr_desc* A, const void* B, int64_t ldb,
                             void* C, int64_t ldc, cudaStream_t stream, void* const* peer_c = nullptr,
                             int n_peers = 0);
+bsp_status plan_spgemm_host(bsp_spgemm_plan* p, const int32_t* a_rp, const int32_t* a_ci,
+                            const int32_t* b_rp, const int32_t* b_ci, int sm_count, int max_smem,
+                            const bsp_spmm_opts* opts);
+bsp_status launch_spgemm(const bsp_spgemm_plan* p, const void* a_vals, const void* b_vals,
+                         void* out_vals, cudaStream_t stream);
+int spgemm_max_stages();
+int spgemm_max_producers();
 bsp_status plan_spmm_rowstack(bsp_spmm_plan* p, const int32_t* row_ptr, const int32_t* col_idx,
                               int sm_count, int max_smem, const bsp_spmm_opts* opts);
 }  // namespace bsp

@@ -707,6 +707,214 @@ bsp_status bsp_sddmm_host_profile(bsp_device* dev, int64_t M, int64_t N, int32_t
                          out_values, strategy, opts, iters, ms_per_launch);
 }
 
+// -------------------------------------------------------------- SpGEMM ----
+static bsp_status spgemm_check_pair(const bsp_bsr_desc* A, const bsp_bsr_desc* B) {
+  if (A->cols != B->rows || A->C != B->R)
+    return set_error(BSP_ERR_INVALID_ARG, "A's columns (and block width) must match B's rows");
+  return BSP_OK;
+}
+
+bsp_status bsp_spgemm_plan_create(bsp_device* dev, const bsp_bsr_desc* A,
+                                  const int32_t* a_host_row_ptr, const int32_t* a_host_col_idx,
+                                  const bsp_bsr_desc* B, const int32_t* b_host_row_ptr,
+                                  const int32_t* b_host_col_idx, const bsp_spmm_opts* opts,
+                                  bsp_spgemm_plan** out) {
+  if (!dev || !out) return set_error(BSP_ERR_INVALID_ARG, "null argument");
+  *out = nullptr;
+  bsp_status s = check_desc(A, false);
+  if (s == BSP_OK) s = check_desc(B, false);
+  if (s == BSP_OK) s = spgemm_check_pair(A, B);
+  if (s != BSP_OK) return s;
+  std::vector<int32_t> arp, aci, brp, bci;
+  const int32_t *parp = nullptr, *paci = nullptr, *pbrp = nullptr, *pbci = nullptr;
+  s = host_pattern(A, a_host_row_ptr, a_host_col_idx, &arp, &aci, &parp, &paci);
+  if (s == BSP_OK) s = host_pattern(B, b_host_row_ptr, b_host_col_idx, &brp, &bci, &pbrp, &pbci);
+  if (s != BSP_OK) return s;
+  bsp_spgemm_plan* p = new (std::nothrow) bsp_spgemm_plan();
+  if (!p) return set_error(BSP_ERR_ALLOC, "host allocation failed");
+  p->dev = dev;
+  p->M = A->rows;
+  p->K = A->cols;
+  p->N = B->cols;
+  p->Ra = A->R;
+  p->Ca = A->C;
+  p->Cb = B->C;
+  p->nnzb_a = A->nnzb;
+  p->nnzb_b = B->nnzb;
+  s = plan_spgemm_host(p, parp, paci, pbrp, pbci, dev->sm_count, dev->max_smem_optin, opts);
+  if (s != BSP_OK) {
+    delete p;
+    return s;
+  }
+  std::vector<void*> ptrs;
+  s = upload_blob({{p->h_units.data(), p->h_units.size() * sizeof(SpgemmUnit)},
+                   {p->h_steps.data(), p->h_steps.size() * sizeof(SpgemmStep)},
+                   {p->h_cta_begin.data(), p->h_cta_begin.size() * sizeof(int32_t)}},
+                  &p->d_blob, &p->blob_bytes, &ptrs);
+  if (s != BSP_OK) {
+    delete p;
+    return s;
+  }
+  p->d_units = static_cast<SpgemmUnit*>(ptrs[0]);
+  p->d_steps = static_cast<SpgemmStep*>(ptrs[1]);
+  p->d_cta_begin = static_cast<int32_t*>(ptrs[2]);
+  *out = p;
+  return BSP_OK;
+}
+
+bsp_status bsp_spgemm_pattern(const bsp_spgemm_plan* p, int64_t* nnzb_out, int32_t* row_ptr_out,
+                              int32_t* col_idx_out) {
+  if (!p || !nnzb_out) return set_error(BSP_ERR_INVALID_ARG, "null argument");
+  *nnzb_out = static_cast<int64_t>(p->out_col_idx.size());
+  if (row_ptr_out) memcpy(row_ptr_out, p->out_row_ptr.data(), p->out_row_ptr.size() * sizeof(int32_t));
+  if (col_idx_out && !p->out_col_idx.empty())
+    memcpy(col_idx_out, p->out_col_idx.data(), p->out_col_idx.size() * sizeof(int32_t));
+  return BSP_OK;
+}
+
+bsp_status bsp_spgemm_execute(const bsp_spgemm_plan* plan, const bsp_bsr_desc* A,
+                              const bsp_bsr_desc* B, void* out_values, void* stream) {
+  if (!plan) return set_error(BSP_ERR_INVALID_ARG, "null plan");
+  bsp_status s = check_desc(A, true);
+  if (s == BSP_OK) s = check_desc(B, true);
+  if (s == BSP_OK) s = spgemm_check_pair(A, B);
+  if (s != BSP_OK) return s;
+  if (A->rows != plan->M || A->cols != plan->K || B->cols != plan->N || A->R != plan->Ra ||
+      A->C != plan->Ca || B->C != plan->Cb || A->nnzb != plan->nnzb_a || B->nnzb != plan->nnzb_b)
+    return set_error(BSP_ERR_INVALID_ARG, "A or B does not match the plan's patterns");
+  if (!plan->out_col_idx.empty() && !out_values)
+    return set_error(BSP_ERR_INVALID_ARG, "out_values missing");
+  return launch_spgemm(plan, A->values, B->values, out_values, static_cast<cudaStream_t>(stream));
+}
+
+bsp_status bsp_spgemm_plan_destroy(bsp_spgemm_plan* plan) {
+  if (!plan) return BSP_OK;
+  if (plan->d_blob) cudaFree(plan->d_blob);
+  delete plan;
+  return BSP_OK;
+}
+
+bsp_status bsp_spgemm_plan_info(const bsp_spgemm_plan* p, int64_t info[16]) {
+  if (!p || !info) return set_error(BSP_ERR_INVALID_ARG, "null argument");
+  memset(info, 0, sizeof(int64_t) * 16);
+  info[0] = p->n_units;
+  info[1] = p->grid;
+  info[2] = p->n_steps;
+  info[3] = p->pairs;
+  info[4] = static_cast<int64_t>(p->out_col_idx.size());
+  info[5] = p->kc;
+  info[6] = p->stages;
+  info[7] = p->sps;
+  info[8] = static_cast<int64_t>(p->blob_bytes);
+  info[9] = p->smem_bytes;
+  info[10] = p->tmem_cols;
+  info[11] = p->nseg_max;
+  info[12] = p->nprod;
+  return BSP_OK;
+}
+
+struct SpgemmLaunchCtx {
+  const bsp_spgemm_plan* p;
+  const bsp_bsr_desc* A;
+  const bsp_bsr_desc* B;
+  void* out;
+};
+static bsp_status spgemm_launch_ctx(const void* v) {
+  const SpgemmLaunchCtx* c = static_cast<const SpgemmLaunchCtx*>(v);
+  return bsp_spgemm_execute(c->p, c->A, c->B, c->out, nullptr);
+}
+
+bsp_status bsp_spgemm_host(bsp_device* dev, int64_t M, int64_t K, int64_t N, int32_t Ra, int32_t Ca,
+                           int32_t Cb, int64_t a_nnzb, const int32_t* a_row_ptr,
+                           const int32_t* a_col_idx, const uint16_t* a_values, int64_t b_nnzb,
+                           const int32_t* b_row_ptr, const int32_t* b_col_idx,
+                           const uint16_t* b_values, int64_t out_cap, int64_t* out_nnzb,
+                           int32_t* out_row_ptr, int32_t* out_col_idx, uint16_t* out_values,
+                           const bsp_spmm_opts* opts, int32_t iters, double* ms_per_launch) {
+  if (!dev || !a_row_ptr || !b_row_ptr || !out_nnzb || (a_nnzb > 0 && (!a_col_idx || !a_values)) ||
+      (b_nnzb > 0 && (!b_col_idx || !b_values)) || (iters > 0 && !ms_per_launch) || iters < 0)
+    return set_error(BSP_ERR_INVALID_ARG, "null argument");
+  if (Ra <= 0 || Ca <= 0 || Cb <= 0 || M <= 0 || K <= 0 || N <= 0 || M % Ra || K % Ca || N % Cb)
+    return set_error(BSP_ERR_INVALID_ARG, "bad dimensions");
+  const int64_t nbr = M / Ra, nbk = K / Ca;
+  // planning needs only the patterns; the device copies come after the size query
+  bsp_spgemm_plan probe;
+  probe.dev = dev;
+  probe.M = M;
+  probe.K = K;
+  probe.N = N;
+  probe.Ra = Ra;
+  probe.Ca = Ca;
+  probe.Cb = Cb;
+  probe.nnzb_a = a_nnzb;
+  probe.nnzb_b = b_nnzb;
+  const bool query = out_values == nullptr;
+  bsp_status s = BSP_OK;
+  bsp_spgemm_plan* p = nullptr;
+  if (query) {
+    s = plan_spgemm_host(&probe, a_row_ptr, a_col_idx, b_row_ptr, b_col_idx, dev->sm_count,
+                         dev->max_smem_optin, opts);
+    if (s == BSP_OK) *out_nnzb = static_cast<int64_t>(probe.out_col_idx.size());
+    return s;
+  }
+  if (!out_row_ptr || (out_cap > 0 && !out_col_idx))
+    return set_error(BSP_ERR_INVALID_ARG, "output arrays missing");
+  const size_t a_blk = sizeof(uint16_t) * a_nnzb * Ra * Ca;
+  const size_t b_blk = sizeof(uint16_t) * b_nnzb * Ca * Cb;
+  const size_t o_cap = sizeof(uint16_t) * std::max<int64_t>(out_cap, 0) * Ra * Cb;
+  const size_t b_av = align256(std::max<size_t>(a_blk, 16)), b_bv = align256(std::max<size_t>(b_blk, 16));
+  const size_t b_ov = align256(std::max<size_t>(o_cap, 16));
+  const size_t b_arp = align256(sizeof(int32_t) * (nbr + 1)), b_aci = align256(sizeof(int32_t) * std::max<int64_t>(a_nnzb, 1));
+  const size_t b_brp = align256(sizeof(int32_t) * (nbk + 1)), b_bci = align256(sizeof(int32_t) * std::max<int64_t>(b_nnzb, 1));
+  s = ws_reserve(dev, b_av + b_bv + b_ov + b_arp + b_aci + b_brp + b_bci);
+  if (s != BSP_OK) return s;
+  uint8_t* w = static_cast<uint8_t*>(dev->ws);
+  void* d_av = w;
+  void* d_bv = w + b_av;
+  void* d_ov = w + b_av + b_bv;
+  int32_t* d_arp = reinterpret_cast<int32_t*>(w + b_av + b_bv + b_ov);
+  int32_t* d_aci = reinterpret_cast<int32_t*>(w + b_av + b_bv + b_ov + b_arp);
+  int32_t* d_brp = reinterpret_cast<int32_t*>(w + b_av + b_bv + b_ov + b_arp + b_aci);
+  int32_t* d_bci = reinterpret_cast<int32_t*>(w + b_av + b_bv + b_ov + b_arp + b_aci + b_brp);
+  cudaStream_t stream = nullptr;
+  struct Cp { void* d; const void* h; size_t n; const char* what; };
+  const Cp cps[] = {{d_av, a_values, a_blk, "H2D A values"}, {d_bv, b_values, b_blk, "H2D B values"},
+                    {d_arp, a_row_ptr, sizeof(int32_t) * (nbr + 1), "H2D A row_ptr"},
+                    {d_aci, a_col_idx, sizeof(int32_t) * a_nnzb, "H2D A col_idx"},
+                    {d_brp, b_row_ptr, sizeof(int32_t) * (nbk + 1), "H2D B row_ptr"},
+                    {d_bci, b_col_idx, sizeof(int32_t) * b_nnzb, "H2D B col_idx"}};
+  for (const Cp& c : cps)
+    if (c.n > 0 && (s = cuda_check(cudaMemcpyAsync(c.d, c.h, c.n, cudaMemcpyHostToDevice, stream), c.what)) != BSP_OK)
+      return s;
+  const bsp_bsr_desc A{M, K, Ra, Ca, a_nnzb, d_arp, d_aci, d_av};
+  const bsp_bsr_desc B{K, N, Ca, Cb, b_nnzb, d_brp, d_bci, d_bv};
+  s = bsp_spgemm_plan_create(dev, &A, a_row_ptr, a_col_idx, &B, b_row_ptr, b_col_idx, opts, &p);
+  if (s != BSP_OK) return s;
+  const int64_t n_out = static_cast<int64_t>(p->out_col_idx.size());
+  *out_nnzb = n_out;
+  if (n_out > out_cap) {
+    bsp_spgemm_plan_destroy(p);
+    return set_error(BSP_ERR_INVALID_ARG, "out_cap is smaller than the product's block count");
+  }
+  s = bsp_spgemm_execute(p, &A, &B, d_ov, stream);
+  if (s == BSP_OK && iters > 0) {
+    const SpgemmLaunchCtx ctx{p, &A, &B, d_ov};
+    s = time_launches(iters, ms_per_launch, stream, spgemm_launch_ctx, &ctx);
+  }
+  if (s == BSP_OK && n_out > 0)
+    s = cuda_check(cudaMemcpyAsync(out_values, d_ov, sizeof(uint16_t) * n_out * Ra * Cb,
+                                   cudaMemcpyDeviceToHost, stream),
+                   "D2H C values");
+  if (s == BSP_OK) s = cuda_check(cudaStreamSynchronize(stream), "sync");
+  if (s == BSP_OK) {
+    memcpy(out_row_ptr, p->out_row_ptr.data(), p->out_row_ptr.size() * sizeof(int32_t));
+    if (n_out > 0) memcpy(out_col_idx, p->out_col_idx.data(), n_out * sizeof(int32_t));
+  }
+  bsp_spgemm_plan_destroy(p);
+  if (s == BSP_OK) s = bsp_device_synchronize(dev);
+  return s;
+}
+
 // ----------------------------------------------------------- helpers ----
 bsp_status bsp_partition_rows(const int32_t* row_ptr, int64_t n_block_rows, int32_t parts,
                               int64_t* bounds) {
@@ -807,6 +1015,36 @@ bsp_status bsp_sddmm_plan_inspect(int64_t M, int64_t N, int32_t R, int32_t C, in
   }
   if (cta_begin_out)
     memcpy(cta_begin_out, p.h_cta_begin.data(), p.h_cta_begin.size() * sizeof(int32_t));
+  return BSP_OK;
+}
+
+bsp_status bsp_spgemm_plan_inspect(int64_t M, int64_t K, int64_t N, int32_t Ra, int32_t Ca,
+                                   int32_t Cb, int64_t a_nnzb, const int32_t* a_row_ptr,
+                                   const int32_t* a_col_idx, int64_t b_nnzb,
+                                   const int32_t* b_row_ptr, const int32_t* b_col_idx,
+                                   const bsp_spmm_opts* opts, int32_t sm_count, int32_t max_smem,
+                                   int64_t info[16], int32_t* out_row_ptr, int32_t* out_col_idx,
+                                   int32_t* units_out, int32_t* steps_out, int32_t* cta_begin_out) {
+  if (!a_row_ptr || !b_row_ptr || !info || (a_nnzb > 0 && !a_col_idx) || (b_nnzb > 0 && !b_col_idx))
+    return set_error(BSP_ERR_INVALID_ARG, "bad arguments");
+  bsp_spgemm_plan p;
+  p.M = M;
+  p.K = K;
+  p.N = N;
+  p.Ra = Ra;
+  p.Ca = Ca;
+  p.Cb = Cb;
+  p.nnzb_a = a_nnzb;
+  p.nnzb_b = b_nnzb;
+  bsp_status s = plan_spgemm_host(&p, a_row_ptr, a_col_idx, b_row_ptr, b_col_idx, sm_count, max_smem, opts);
+  if (s != BSP_OK) return s;
+  bsp_spgemm_plan_info(&p, info);
+  if (out_row_ptr) memcpy(out_row_ptr, p.out_row_ptr.data(), p.out_row_ptr.size() * sizeof(int32_t));
+  if (out_col_idx && !p.out_col_idx.empty())
+    memcpy(out_col_idx, p.out_col_idx.data(), p.out_col_idx.size() * sizeof(int32_t));
+  if (units_out && !p.h_units.empty()) memcpy(units_out, p.h_units.data(), p.h_units.size() * sizeof(SpgemmUnit));
+  if (steps_out && !p.h_steps.empty()) memcpy(steps_out, p.h_steps.data(), p.h_steps.size() * sizeof(SpgemmStep));
+  if (cta_begin_out) memcpy(cta_begin_out, p.h_cta_begin.data(), p.h_cta_begin.size() * sizeof(int32_t));
   return BSP_OK;
 }
 

@@ -960,4 +960,258 @@ bsp_status plan_sddmm_rowstack(bsp_sddmm_plan* p, const int32_t* row_ptr, const 
   return BSP_OK;
 }
 
+// SpGEMM schedule (C_bsr = A_bsr * B_bsr).  The output pattern is computed
+// first (bsr_matrix.hpp:741-810: block (i, j) exists when some A[i, k] and
+// B[k, j] are stored; columns ascending).  Output rows are then cut into
+// 32-row slabs ("entries"), four per group (MMA M = 128); the union of the
+// group's output block-columns is cut into 32-column segments, nseg_max per
+// unit (MMA N).  A unit's steps are the block indices k for which one of its
+// entries' rows stores A[i, k] and one of its columns stores B[k, j], in
+// ascending order.  A k repeated inside a row of A (or a column repeated in
+// row k of B) gives layered steps, one per pair of repeats, so every stored
+// block product is taken exactly once.
+bsp_status plan_spgemm_host(bsp_spgemm_plan* p, const int32_t* a_rp, const int32_t* a_ci,
+                            const int32_t* b_rp, const int32_t* b_ci, int sm_count, int max_smem,
+                            const bsp_spmm_opts* opts) {
+  bsp_spmm_opts o;
+  memset(&o, 0, sizeof(o));
+  if (opts) o = *opts;
+  const int64_t M = p->M, K = p->K, N = p->N;
+  const int Ra = p->Ra, Ca = p->Ca, Cb = p->Cb;
+  auto ok_blk = [](int x) { return x == 32 || x == 64 || x == 128; };
+  if (!ok_blk(Ra) || !ok_blk(Ca) || !ok_blk(Cb))
+    return set_error(BSP_ERR_UNSUPPORTED, "SpGEMM block sizes must be 32, 64 or 128");
+  if (M <= 0 || K <= 0 || N <= 0 || M % Ra || K % Ca || N % Cb)
+    return set_error(BSP_ERR_INVALID_ARG, "M % Ra, K % Ca and N % Cb must be 0");
+  if (p->nnzb_a < 0 || p->nnzb_b < 0 || p->nnzb_a * Ra >= (int64_t(1) << 31) ||
+      p->nnzb_b * Ca >= (int64_t(1) << 31) || M >= (int64_t(1) << 31) || N >= (int64_t(1) << 31))
+    return set_error(BSP_ERR_UNSUPPORTED, "matrix too large for 32-bit TMA coordinates");
+  const int64_t nbr = M / Ra, nbk = K / Ca, nbc = N / Cb;
+  bsp_status st = check_pattern(a_rp, a_ci, nbr, nbk, p->nnzb_a);
+  if (st != BSP_OK) return st;
+  st = check_pattern(b_rp, b_ci, nbk, nbc, p->nnzb_b);
+  if (st != BSP_OK) return st;
+
+  // ---- output pattern (symbolic product) ----
+  p->out_row_ptr.assign(static_cast<size_t>(nbr + 1), 0);
+  p->out_col_idx.clear();
+  std::vector<int64_t> stamp(static_cast<size_t>(nbc), -1);
+  int64_t pairs = 0;
+  for (int64_t i = 0; i < nbr; ++i) {
+    const size_t start = p->out_col_idx.size();
+    for (int32_t a = a_rp[i]; a < a_rp[i + 1]; ++a) {
+      const int32_t k = a_ci[a];
+      pairs += b_rp[k + 1] - b_rp[k];
+      for (int32_t b = b_rp[k]; b < b_rp[k + 1]; ++b) {
+        const int32_t j = b_ci[b];
+        if (stamp[j] != i) {
+          stamp[j] = i;
+          p->out_col_idx.push_back(j);
+        }
+      }
+    }
+    std::sort(p->out_col_idx.begin() + static_cast<std::ptrdiff_t>(start), p->out_col_idx.end());
+    if (p->out_col_idx.size() >= (size_t(1) << 31))
+      return set_error(BSP_ERR_UNSUPPORTED, "output has too many blocks");
+    p->out_row_ptr[i + 1] = static_cast<int32_t>(p->out_col_idx.size());
+  }
+  p->pairs = pairs;
+  const int64_t out_nnzb = static_cast<int64_t>(p->out_col_idx.size());
+  if (out_nnzb * Ra * Cb >= (int64_t(1) << 40))
+    return set_error(BSP_ERR_UNSUPPORTED, "output too large");
+
+  // ---- stage geometry ----
+  const int kc = Ca == 32 ? 32 : 64;
+  const int nkc = Ca / kc;
+  int nseg_max = (o.n_tiles == 1) ? 4 : 8;
+  p->kc = kc;
+  p->nkc = nkc;
+  p->nseg_max = nseg_max;
+  const int spr = Ra / 32;                      // slabs (entries) per output block-row
+  const int segs_per_col = Cb / 32;             // segments per output block-column
+  const int cpu = std::max(1, nseg_max / segs_per_col);  // block-columns per unit
+  const int64_t n_ent = nbr * spr;
+  const int64_t ngroups = (n_ent + kSpgemmEnt - 1) / kSpgemmEnt;
+
+  std::vector<SpgemmUnit> units;
+  std::vector<int64_t> weight;
+  p->h_steps.clear();
+  std::vector<int64_t> colpos(static_cast<size_t>(nbc), -1), colstamp(static_cast<size_t>(nbc), -1);
+  std::vector<int64_t> kstamp(static_cast<size_t>(nbk), -1);
+  std::vector<int32_t> cols, ks;
+  std::vector<std::vector<int32_t>> chunk_k;
+  std::vector<int32_t> lastk;
+  std::vector<std::vector<int32_t>> bl(kSpgemmMaxSeg);  // B blocks of row k per unit column
+  // (k, A block) of each distinct block-row of the group, sorted by k (stable)
+  std::vector<std::vector<std::pair<int32_t, int32_t>>> rowpairs;
+  for (int64_t g = 0; g < ngroups; ++g) {
+    const int64_t e0 = g * kSpgemmEnt, e1 = std::min<int64_t>(n_ent, e0 + kSpgemmEnt);
+    const int64_t r0 = e0 / spr, r1 = (e1 - 1) / spr + 1;  // block-rows [r0, r1)
+    cols.clear();
+    for (int64_t i = r0; i < r1; ++i)
+      for (int32_t q = p->out_row_ptr[i]; q < p->out_row_ptr[i + 1]; ++q) {
+        const int32_t j = p->out_col_idx[q];
+        if (colstamp[j] != g) {
+          colstamp[j] = g;
+          cols.push_back(j);
+        }
+      }
+    if (cols.empty()) continue;
+    std::sort(cols.begin(), cols.end());
+    for (size_t c = 0; c < cols.size(); ++c) colpos[cols[c]] = static_cast<int64_t>(c);
+    const int64_t nchunks = (static_cast<int64_t>(cols.size()) + cpu - 1) / cpu;
+    rowpairs.assign(static_cast<size_t>(r1 - r0), {});
+    ks.clear();
+    for (int64_t i = r0; i < r1; ++i) {
+      auto& v = rowpairs[static_cast<size_t>(i - r0)];
+      for (int32_t a = a_rp[i]; a < a_rp[i + 1]; ++a) {
+        v.push_back({a_ci[a], a});
+        if (kstamp[a_ci[a]] != g) {
+          kstamp[a_ci[a]] = g;
+          ks.push_back(a_ci[a]);
+        }
+      }
+      std::stable_sort(v.begin(), v.end(),
+                       [](const std::pair<int32_t, int32_t>& x, const std::pair<int32_t, int32_t>& y) {
+                         return x.first < y.first;
+                       });
+    }
+    std::sort(ks.begin(), ks.end());
+    chunk_k.assign(static_cast<size_t>(nchunks), {});
+    lastk.assign(static_cast<size_t>(nchunks), -1);
+    for (int32_t k : ks)
+      for (int32_t b = b_rp[k]; b < b_rp[k + 1]; ++b) {
+        const int64_t c = colpos[b_ci[b]] / cpu;
+        if (lastk[c] != k) {
+          lastk[c] = k;
+          chunk_k[c].push_back(k);
+        }
+      }
+    for (int64_t c = 0; c < nchunks; ++c) {
+      SpgemmUnit u;
+      memset(&u, 0, sizeof(u));
+      const int64_t j0 = c * cpu;
+      const int ncols = static_cast<int>(std::min<int64_t>(cpu, static_cast<int64_t>(cols.size()) - j0));
+      u.n_ent = static_cast<int32_t>(e1 - e0);
+      u.nseg = std::min(nseg_max, ncols * segs_per_col);
+      for (int s_ = 0; s_ < kSpgemmMaxSeg; ++s_) u.seg_x[s_] = s_ < u.nseg ? (s_ % segs_per_col) * 32 : 0;
+      for (int e = 0; e < kSpgemmEnt; ++e) {
+        const int64_t E = e0 + e;
+        u.ent_r[e] = E < e1 ? static_cast<int32_t>(E % spr) * 32 : 0;
+        for (int s_ = 0; s_ < kSpgemmMaxSeg; ++s_) {
+          u.out_blk[e][s_] = -1;
+          if (E >= e1 || s_ >= u.nseg) continue;
+          const int64_t i = E / spr;
+          const int32_t j = cols[static_cast<size_t>(j0 + s_ / segs_per_col)];
+          const int32_t* lo = p->out_col_idx.data() + p->out_row_ptr[i];
+          const int32_t* hi = p->out_col_idx.data() + p->out_row_ptr[i + 1];
+          const int32_t* it = std::lower_bound(lo, hi, j);
+          if (it != hi && *it == j) u.out_blk[e][s_] = static_cast<int32_t>(it - p->out_col_idx.data());
+        }
+      }
+      u.step_begin = static_cast<int32_t>(p->h_steps.size());
+      if (p->h_steps.size() >= (size_t(1) << 31) - 4096)
+        return set_error(BSP_ERR_UNSUPPORTED, "SpGEMM schedule too large");
+      for (int32_t k : chunk_k[c]) {
+        // A blocks of column k per entry, B blocks of row k per unit column
+        int32_t a_first[kSpgemmEnt], a_cnt[kSpgemmEnt];
+        int la_max = 0;
+        for (int e = 0; e < kSpgemmEnt; ++e) {
+          a_first[e] = 0;
+          a_cnt[e] = 0;
+          const int64_t E = e0 + e;
+          if (E >= e1) continue;
+          const auto& v = rowpairs[static_cast<size_t>(E / spr - r0)];
+          auto it = std::lower_bound(v.begin(), v.end(), std::make_pair(k, INT32_MIN));
+          a_first[e] = static_cast<int32_t>(it - v.begin());
+          while (it != v.end() && it->first == k) {
+            ++a_cnt[e];
+            ++it;
+          }
+          la_max = std::max(la_max, static_cast<int>(a_cnt[e]));
+        }
+        for (auto& l : bl) l.clear();
+        int lb_max = 0;
+        for (int32_t b = b_rp[k]; b < b_rp[k + 1]; ++b) {
+          const int64_t pos = colpos[b_ci[b]];
+          if (pos / cpu != c) continue;
+          auto& l = bl[static_cast<size_t>(pos - j0)];
+          l.push_back(b);
+          lb_max = std::max(lb_max, static_cast<int>(l.size()));
+        }
+        for (int la = 0; la < la_max; ++la)
+          for (int lb = 0; lb < lb_max; ++lb) {
+            SpgemmStep sp;
+            for (int e = 0; e < kSpgemmEnt; ++e) {
+              sp.a_y[e] = -1;
+              if (la < a_cnt[e]) {
+                const auto& v = rowpairs[static_cast<size_t>((e0 + e) / spr - r0)];
+                sp.a_y[e] = v[static_cast<size_t>(a_first[e] + la)].second * Ra + u.ent_r[e];
+              }
+            }
+            for (int s_ = 0; s_ < kSpgemmMaxSeg; ++s_) {
+              sp.b_y[s_] = -1;
+              if (s_ >= u.nseg) continue;
+              const auto& l = bl[static_cast<size_t>(s_ / segs_per_col)];
+              if (lb < static_cast<int>(l.size())) sp.b_y[s_] = l[static_cast<size_t>(lb)] * Ca;
+            }
+            p->h_steps.push_back(sp);
+          }
+      }
+      u.n_steps = static_cast<int32_t>(p->h_steps.size()) - u.step_begin;
+      if (u.n_steps == 0) continue;  // cannot happen: every unit column has a product
+      units.push_back(u);
+      weight.push_back(static_cast<int64_t>(u.n_steps) * nkc + 2);
+    }
+  }
+  p->n_steps = static_cast<int64_t>(p->h_steps.size());
+
+  int grid = o.max_ctas > 0 ? std::min(o.max_ctas, sm_count) : sm_count;
+  grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(grid, units.size())));
+  std::vector<std::vector<int32_t>> per;
+  if (o.no_load_balance) contiguous_split(static_cast<int64_t>(units.size()), grid, &per);
+  else serpentine_order(weight, grid, &per);
+  p->h_units.clear();
+  p->h_cta_begin.assign(1, 0);
+  for (int cta = 0; cta < grid; ++cta) {
+    for (int32_t idx : per[cta]) p->h_units.push_back(units[idx]);
+    p->h_cta_begin.push_back(static_cast<int32_t>(p->h_units.size()));
+  }
+  p->n_units = static_cast<int64_t>(units.size());
+  p->grid = units.empty() ? 0 : grid;
+
+  const int a_slot = 32 * kc * 2;
+  const int sub_bytes = kSpgemmEnt * a_slot + nseg_max * kc * 64;
+  int sps = o.steps_per_stage > 0 ? std::min(4, o.steps_per_stage) : (kc == 32 ? 2 : 1);
+  int max_stages = 0;
+  for (;; sps = std::max(1, sps / 2)) {
+    max_stages = std::min(spgemm_max_stages(), (max_smem - 2048) / (sps * sub_bytes));
+    if (max_stages >= 2 || sps == 1) break;
+  }
+  if (max_stages < 2) return set_error(BSP_ERR_UNSUPPORTED, "stage too large for the pipeline");
+  const int stage_bytes = sps * sub_bytes;
+  int nprod = 1, stages = max_stages;
+  if (o.producers > 0) {
+    nprod = std::min({o.producers, spgemm_max_producers(), max_stages});
+    stages = max_stages / nprod * nprod;
+  } else {
+    for (int q = 2; q <= std::min(spgemm_max_producers(), max_stages); ++q) {
+      const int sq = max_stages / q * q;
+      if (sq >= stages - (stages > 6 ? 1 : 0)) {
+        nprod = q;
+        stages = sq;
+      }
+    }
+  }
+  p->sps = sps;
+  p->sub_bytes = sub_bytes;
+  p->nprod = nprod;
+  p->stage_bytes = stage_bytes;
+  p->stages = stages;
+  p->smem_bytes = 2048 + stages * stage_bytes;
+  p->tmem_cols = pow2_at_least(2 * 32 * nseg_max);
+  p->timeout_ns = static_cast<uint64_t>(o.timeout_ms > 0 ? o.timeout_ms : 2000) * 1000000ull;
+  return BSP_OK;
+}
+
 }  // namespace bsp

@@ -16,8 +16,13 @@ Cases:
     uniform[-1,1], numpy seed 1234);
   * the reference's SDDMM registry shapes (block_sddmm/inc/test_suite.hpp:
     single_block, diagonal_mask, full_mask, identity_mask, nonsquare,
-    diagonal_mask_short_k) for R = C = 32 and 64, plus a seeded random mask.
+    diagonal_mask_short_k) for R = C = 32 and 64, plus a seeded random mask;
+  * SpGEMM (bsr_matrix<T>::spgemm, sparse_common/bsr_matrix.hpp:741-810):
+    seeded random patterns for each block-size combination, the reference's
+    FILL_DIAG / FILL_TRIL generators, empty block-rows, and rows with
+    repeated and unsorted column indices.
 Every fixture stores inputs and golden outputs as raw bf16 bit patterns.
+`python tests/golden/make_golden.py spgemm` regenerates only the SpGEMM ones.
 """
 import os
 import sys
@@ -59,9 +64,59 @@ def sddmm_case(name, H, W, R, C, K, ip, ix, mask_f32, A_f32, B_f32):
          out=out, out_f32=out_f32)
 
 
+def spgemm_case(name, Ha, Wa, Wb, Ra, Ca, Cb, arp, aci, av_f32, brp, bci, bv_f32):
+    av, bv = F.f32_to_bf16(av_f32), F.f32_to_bf16(bv_f32)
+    orp, oci, out = F.ref_spgemm_bf16(arp, aci, av, Ha, Wa, Ra, Ca, brp, bci, bv, Wb, Cb)
+    save(name, kind="spgemm", Ha=Ha, Wa=Wa, Wb=Wb, Ra=Ra, Ca=Ca, Cb=Cb, a_indptr=arp, a_indices=aci,
+         a_values=av, b_indptr=brp, b_indices=bci, b_values=bv, out_indptr=orp, out_indices=oci,
+         out=out)
+
+
+def rand_pattern(rng, nbr, nbc, p, empty_rows=()):
+    occ = rng.random((nbr, nbc)) < p
+    for r in empty_rows:
+        occ[r, :] = False
+    ip = np.concatenate([[0], np.cumsum(occ.sum(1))]).astype(np.int32)
+    return ip, np.nonzero(occ)[1].astype(np.int32)
+
+
+def spgemm_cases():
+    rng = np.random.default_rng(741)
+    # seeded random patterns, every block-size family the device path takes
+    for name, Ha, Wa, Wb, Ra, Ca, Cb, pa, pb in [
+            ("spgemm_rand_32", 512, 384, 448, 32, 32, 32, 0.2, 0.2),
+            ("spgemm_rand_64_32_64", 384, 256, 384, 64, 32, 64, 0.3, 0.25),
+            ("spgemm_rand_32_64_32", 288, 512, 256, 32, 64, 32, 0.25, 0.3),
+            ("spgemm_rand_128_128_32", 384, 512, 192, 128, 128, 32, 0.5, 0.4),
+            ("spgemm_rand_32_128_128", 160, 384, 512, 32, 128, 128, 0.4, 0.4)]:
+        arp, aci = rand_pattern(rng, Ha // Ra, Wa // Ca, pa, empty_rows=(1,))
+        brp, bci = rand_pattern(rng, Wa // Ca, Wb // Cb, pb, empty_rows=(0,))
+        spgemm_case(name, Ha, Wa, Wb, Ra, Ca, Cb, arp, aci,
+                    rng.uniform(-1, 1, aci.size * Ra * Ca).astype(np.float32), brp, bci,
+                    rng.uniform(-1, 1, bci.size * Ca * Cb).astype(np.float32))
+    # the reference's own generators (RAND content after srand)
+    for name, fa, fb, nb in [("spgemm_fill_diag", F.FILL_DIAG, F.FILL_DIAG, 16),
+                             ("spgemm_fill_tril_diag", F.FILL_TRIL, F.FILL_DIAG, 0)]:
+        arp, aci, ad = F.ref_generate_bsr(512, 512, 32, 32, nb, fa, F.RAND, seed=42)
+        brp, bci, bd = F.ref_generate_bsr(512, 256, 32, 32, 8 if fb == F.FILL_DIAG else nb, fb,
+                                          F.RAND, seed=43)
+        spgemm_case(name, 512, 512, 256, 32, 32, 32, arp, aci, ad, brp, bci, bd)
+    # repeated and unsorted column indices in rows of A and of B
+    arp = np.array([0, 3, 3, 7, 9], np.int32)
+    aci = np.array([2, 0, 2, 1, 3, 1, 1, 0, 3], np.int32)
+    brp = np.array([0, 2, 4, 7, 9], np.int32)
+    bci = np.array([1, 1, 2, 0, 4, 3, 4, 0, 2], np.int32)
+    spgemm_case("spgemm_repeats", 128, 128, 160, 32, 32, 32, arp, aci,
+                rng.uniform(-1, 1, aci.size * 1024).astype(np.float32), brp, bci,
+                rng.uniform(-1, 1, bci.size * 1024).astype(np.float32))
+
+
 def main():
     if not F.ref_available():
         sys.exit("oracle/_ref/libref_golden.so is missing: run `make -C oracle` with the reference sources")
+    if sys.argv[1:] == ["spgemm"]:
+        spgemm_cases()
+        return
     # ---- SpMM known-answer cases (test_suite.hpp:1841-1921) ----
     for name, acontent, bcontent in [("spmm_1_block_id", F.ID, F.ID),
                                      ("spmm_1_block_arange", F.ARANGE, F.UNIFORM),
@@ -110,6 +165,7 @@ def main():
     A = (rng.normal(0, 1, (512, 256)) / 16).astype(np.float32)
     Bd = (rng.normal(0, 1, (256, 512)) / 16).astype(np.float32)
     sddmm_case("sddmm_random_p15", 512, 512, 32, 32, 256, ip, ix, m, A, Bd)
+    spgemm_cases()
 
 
 if __name__ == "__main__":

@@ -18,12 +18,20 @@ FIXTURES = sorted(glob.glob(os.path.join(GOLDEN, "*.npz")))
 def test_fixtures_present():
     names = {os.path.basename(f)[:-4] for f in FIXTURES}
     assert {"spmm_config1", "spmm_1_block_id", "sddmm_identity_mask_R32", "sddmm_random_p15"} <= names
-    assert len(FIXTURES) >= 20
+    assert {"spgemm_rand_32", "spgemm_repeats", "spgemm_fill_diag"} <= names
+    assert len(FIXTURES) >= 30
 
 
 @pytest.mark.parametrize("path", FIXTURES, ids=[os.path.basename(f)[:-4] for f in FIXTURES])
 def test_oracle_reproduces_reference_fixture(path):
     z = np.load(path)
+    if str(z["kind"]) == "spgemm":
+        Ra, Ca, Cb, Wb = (int(z[k]) for k in ("Ra", "Ca", "Cb", "Wb"))
+        orp, oci, out = oracle.spgemm_bf16(z["a_indptr"], z["a_indices"], z["a_values"], Ra, Ca,
+                                           z["b_indptr"], z["b_indices"], z["b_values"], Cb, Wb // Cb)
+        assert np.array_equal(orp, z["out_indptr"]) and np.array_equal(oci, z["out_indices"])
+        assert np.array_equal(out, z["out"])
+        return
     H, W, R, C = (int(z[k]) for k in ("H", "W", "R", "C"))
     ip, ix = z["indptr"], z["indices"]
     if str(z["kind"]) == "spmm":
@@ -82,6 +90,41 @@ def test_oracle_matches_reference_golden_live(R, C, N, p):
     g, oip, oix = oracle.ref_sddmm_bf16(ip, ix, vals, H, W, R, C, A, Bs, K)
     assert np.array_equal(oracle.sddmm_bf16(ip, ix, vals, H, W, R, C, A, Bs, K), g)
     assert np.array_equal(oip, ip) and np.array_equal(oix, ix)
+
+
+@pytest.mark.skipif(not oracle.ref_available(), reason="reference golden not built here")
+@pytest.mark.parametrize("Ra,Ca,Cb,pa,pb", [(32, 32, 32, 0.3, 0.3), (64, 32, 32, 0.5, 0.2),
+                                            (32, 64, 128, 0.2, 0.6), (128, 32, 64, 0.4, 0.4)])
+def test_spgemm_oracle_matches_reference_golden_live(Ra, Ca, Cb, pa, pb):
+    rng = np.random.default_rng(Ra + 7 * Ca + 13 * Cb)
+    nbr, nbk, nbc = 6, 5, 7
+    occ_a = rng.random((nbr, nbk)) < pa
+    occ_b = rng.random((nbk, nbc)) < pb
+    arp = np.concatenate([[0], np.cumsum(occ_a.sum(1))]).astype(np.int32)
+    aci = np.nonzero(occ_a)[1].astype(np.int32)
+    brp = np.concatenate([[0], np.cumsum(occ_b.sum(1))]).astype(np.int32)
+    bci = np.nonzero(occ_b)[1].astype(np.int32)
+    av = oracle.f32_to_bf16(rng.uniform(-1, 1, aci.size * Ra * Ca).astype(np.float32))
+    bv = oracle.f32_to_bf16(rng.uniform(-1, 1, bci.size * Ca * Cb).astype(np.float32))
+    got = oracle.spgemm_bf16(arp, aci, av, Ra, Ca, brp, bci, bv, Cb, nbc)
+    ref = oracle.ref_spgemm_bf16(arp, aci, av, nbr * Ra, nbk * Ca, Ra, Ca, brp, bci, bv, nbc * Cb, Cb)
+    for g, r in zip(got, ref):
+        assert np.array_equal(g, r)
+
+
+def test_spgemm_oracle_closed_form():
+    """Block-diagonal identity A times B returns B's blocks on B's pattern."""
+    rng = np.random.default_rng(3)
+    n = 4
+    arp = np.arange(n + 1, dtype=np.int32)
+    aci = np.arange(n, dtype=np.int32)
+    av = oracle.f32_to_bf16(np.tile(np.eye(32, dtype=np.float32).ravel(), n))
+    occ = rng.random((n, 5)) < 0.5
+    brp = np.concatenate([[0], np.cumsum(occ.sum(1))]).astype(np.int32)
+    bci = np.nonzero(occ)[1].astype(np.int32)
+    bv = oracle.f32_to_bf16(rng.uniform(-1, 1, bci.size * 32 * 32).astype(np.float32))
+    orp, oci, out = oracle.spgemm_bf16(arp, aci, av, 32, 32, brp, bci, bv, 32, 5)
+    assert np.array_equal(orp, brp) and np.array_equal(oci, bci) and np.array_equal(out, bv)
 
 
 def test_bf16_rounding_is_nearest_even():

@@ -61,6 +61,8 @@ METRICS = {
     "cfg3": "effective TFLOP/s (nnz blocks only), BSR SDDMM",
     "cfg4": "effective TFLOP/s (nnz blocks only), BSR SDDMM + SpMM attention pair",
     "cfg5": "effective TFLOP/s (nnz blocks only), multi-GPU BSR SpMM with C all-gather",
+    "spgemm": "effective TFLOP/s (stored block products only), BSR x BSR -> BSR SpGEMM",
+    "spgemm_rand": "effective TFLOP/s (stored block products only), BSR x BSR -> BSR SpGEMM",
 }
 WORKLOAD_DESC = {
     "sweep": "BASELINE config 2: BSR SpMM 4096x4096x4096, 32x32 blocks, p in {0.01,0.05,0.10,0.25,0.50}",
@@ -69,6 +71,10 @@ WORKLOAD_DESC = {
     "cfg4": "BASELINE config 4: SDDMM Q K^T + SpMM P V, seq 16384, head 128, 32x32 blocks, band+global+Zipf mask",
     "cfg5": "BASELINE config 5: BSR SpMM 65536x65536 (64x64 blocks, Zipf(1.1) rows, 1% mean) x 65536x8192, "
             "row panels sharded by nnz blocks + NCCL exchange of C",
+    "spgemm": "SpGEMM (bsr_matrix::spgemm): banded 16384x16384 BSR (32x32 blocks, half-width 32 blocks) "
+              "times a second matrix of the same pattern",
+    "spgemm_rand": "SpGEMM (bsr_matrix::spgemm): 16384x16384 BSR (32x32 blocks, uniform p=0.05) "
+                   "times an independent matrix of the same shape and density",
 }
 DENSITIES = [0.01, 0.05, 0.10, 0.25, 0.50]
 L2_FLUSH_BYTES = 256 << 20
@@ -221,6 +227,29 @@ def gen_cfg5(seed, M=65536, K=65536, N=8192, R=64, C=64, density=0.01, s=1.1):
                 vals=vals, B=B)
 
 
+def gen_spgemm_case(arp, aci, brp, bci, R, seed, name):
+    """C = A @ B, both n x n blocks of R x R (uniform[-1, 1] values)."""
+    rng = np.random.default_rng(seed)
+    av = uniform_bf16(rng, (aci.size * R, R))
+    bv = uniform_bf16(rng, (bci.size * R, R))
+    nb = arp.size - 1
+    pairs = int(np.diff(brp)[aci].sum())
+    return dict(kind="spgemm", name=name, M=nb * R, K=nb * R, N=nb * R, R=R, C=R, Ra=R, Ca=R, Cb=R,
+                rp=arp, ci=aci, vals=av, brp=brp, bci=bci, bvals=bv, pairs=pairs)
+
+
+def gen_spgemm_band(seed, n=512, hw=32, R=32):
+    rp, ci = _pattern_from_sets([np.arange(max(0, i - hw), min(n, i + hw + 1)) for i in range(n)])
+    return gen_spgemm_case(rp, ci, rp, ci, R, seed, f"band hw{hw}")
+
+
+def gen_spgemm_rand(seed, n=512, p=0.05, R=32):
+    rng = np.random.default_rng(seed)
+    arp, aci = _pattern_from_occupancy(rng.random((n, n)) < p)
+    brp, bci = _pattern_from_occupancy(rng.random((n, n)) < p)
+    return gen_spgemm_case(arp, aci, brp, bci, R, seed + 1, f"random p={p}")
+
+
 def workload_ops(workload, rank):
     """Host-side ops of one step of `workload` (rank picks the seed of the
     independent per-rank copies)."""
@@ -235,6 +264,10 @@ def workload_ops(workload, rank):
         return gen_cfg4(base)
     if workload == "cfg5":
         return [gen_cfg5(1234)]   # one problem shared by all ranks
+    if workload == "spgemm":
+        return [gen_spgemm_band(base)]
+    if workload == "spgemm_rand":
+        return [gen_spgemm_rand(base)]
     raise ValueError(workload)
 
 
@@ -242,9 +275,22 @@ def op_flops(op):
     """Effective FLOPs (reference formulas, GEMM_profiling/read_spmm_profiler.py:73
     and read_sddmm_profiler.py:75)."""
     nnzb = int(op["rp"][-1])
+    if op["kind"] == "spgemm":
+        return 2.0 * op["pairs"] * op["Ra"] * op["Ca"] * op["Cb"]
     if op["kind"] == "spmm":
         return 2.0 * nnzb * op["R"] * op["C"] * op["N"]
     return 2.0 * nnzb * op["R"] * op["C"] * op["K"] + nnzb * op["R"] * op["C"]
+
+
+def spgemm_out_nnzb(op):
+    """Block count of C (symbolic product of the patterns)."""
+    nb = op["rp"].size - 1
+    n = 0
+    for i in range(nb):
+        ks = op["ci"][op["rp"][i]:op["rp"][i + 1]]
+        if ks.size:
+            n += np.unique(np.concatenate([op["bci"][op["brp"][k]:op["brp"][k + 1]] for k in ks])).size
+    return n
 
 
 def op_bytes(op):
@@ -252,6 +298,12 @@ def op_bytes(op):
     once, plus the output written once."""
     nnzb = int(op["rp"][-1])
     R, C = op["R"], op["C"]
+    if op["kind"] == "spgemm":
+        if "out_nnzb" not in op:
+            op["out_nnzb"] = spgemm_out_nnzb(op)
+        nb_b = int(op["brp"][-1])
+        return (2 * nnzb * op["Ra"] * op["Ca"] + 2 * nb_b * op["Ca"] * op["Cb"]
+                + 2 * op["out_nnzb"] * op["Ra"] * op["Cb"] + 4 * (nnzb + nb_b + op["out_nnzb"]))
     ncols = np.unique(op["ci"]).size
     idx = 4 * (nnzb + op["M"] // R + 1)
     if op["kind"] == "spmm":
@@ -405,6 +457,19 @@ def _cpu_time(op, rows, threads, kind):
     block-rows [0, rows) of `op`."""
     import oracle
 
+    if op["kind"] == "spgemm":
+        # A's first `rows` block-rows times all of B (the reference's spgemm is one thread)
+        arp = op["rp"][: rows + 1]
+        n = int(arp[-1])
+        aci, av = op["ci"][:n], op["vals"][: n * op["Ra"]]
+        t0 = time.perf_counter()
+        if kind == "reference":
+            oracle.ref_spgemm_bf16(arp, aci, av, rows * op["Ra"], op["K"], op["Ra"], op["Ca"], op["brp"],
+                                   op["bci"], op["bvals"], op["N"], op["Cb"])
+        else:
+            oracle.spgemm_bf16(arp, aci, av, op["Ra"], op["Ca"], op["brp"], op["bci"], op["bvals"],
+                               op["Cb"], op["N"] // op["Cb"])
+        return time.perf_counter() - t0
     if op["kind"] == "spmm":
         args = (op["rp"], op["ci"], op["vals"], op["M"], op["K"], op["R"], op["C"], op["B"], op["N"])
         if kind == "reference":
@@ -423,6 +488,8 @@ def _cpu_time(op, rows, threads, kind):
 
 def _sample_flops(op, rows):
     nnzb = int(op["rp"][rows])
+    if op["kind"] == "spgemm":
+        return 2.0 * float(np.diff(op["brp"])[op["ci"][:nnzb]].sum()) * op["Ra"] * op["Ca"] * op["Cb"]
     if op["kind"] == "spmm":
         return 2.0 * nnzb * op["R"] * op["C"] * op["N"]
     return 2.0 * nnzb * op["R"] * op["C"] * op["K"] + nnzb * op["R"] * op["C"]
@@ -449,6 +516,21 @@ def cpu_calibrate(ops, budget_s=12.0, threads=None):
     return out, kind
 
 
+def cpu_threads_used(ops, threads=None):
+    """The reference's spgemm golden is a single-threaded loop; its SpMM and
+    SDDMM goldens run on every host thread here."""
+    if all(op["kind"] == "spgemm" for op in ops):
+        return 1
+    return threads or os.cpu_count() or 1
+
+
+def golden_name(ops):
+    kinds = {op["kind"] for op in ops}
+    names = {"spmm": "bsr_matrix::spmm_bfloat16", "sddmm": "bsr_matrix::sddmm",
+             "spgemm": "bsr_matrix::spgemm"}
+    return " / ".join(names[k] for k in sorted(kinds))
+
+
 def cpu_sample_time(ops, rows, kind, threads=None):
     threads = threads or os.cpu_count() or 1
     f = t = 0.0
@@ -471,7 +553,16 @@ class DevOp:
 
         self.op = op
         self.kind = op["kind"]
-        if self.kind == "spmm":
+        if self.kind == "spgemm":
+            self.A = bsp.DeviceBSR.from_host(op["M"], op["K"], op["Ra"], op["Ca"], op["rp"], op["ci"],
+                                             op["vals"], local)
+            self.Bm = bsp.DeviceBSR.from_host(op["K"], op["N"], op["Ca"], op["Cb"], op["brp"], op["bci"],
+                                              op["bvals"], local)
+            self.plan = bsp.SpgemmPlan(dev, self.A, self.Bm)
+            op["out_nnzb"] = self.plan.nnzb
+            self.out = torch.empty(max(self.plan.nnzb * op["Ra"] * op["Cb"], 8), dtype=torch.bfloat16,
+                                   device="cuda")
+        elif self.kind == "spmm":
             self.A = bsp.DeviceBSR.from_host(op["M"], op["K"], op["R"], op["C"], op["rp"], op["ci"],
                                              op["vals"], local)
             self.B = bsp.to_device_bf16(op["B"], local)
@@ -487,12 +578,16 @@ class DevOp:
             self.plan = bsp.SddmmPlan(dev, self.mask, op["K"], strategy)
 
     def run(self, stream):
-        if self.kind == "spmm":
+        if self.kind == "spgemm":
+            self.plan.execute(self.A, self.Bm, self.out, stream)
+        elif self.kind == "spmm":
             self.plan.execute(self.A, self.B, self.out, stream)
         else:
             self.plan.execute(self.mask, self.Ad, self.Bd, self.out, stream)
 
     def kernel(self):
+        if self.kind == "spgemm":
+            return "spgemm_tcgen05"
         if self.kind == "sddmm":
             return "sddmm_bsr_tcgen05"
         return {1: "spmm_rowstack_tcgen05", 2: "spmm_pair_tcgen05"}.get(self.plan.info().get("variant", 0),
@@ -625,8 +720,9 @@ def run_bsp(args):
         host_ops = [r["op"] for r in runs]
         rows, kind = cpu_calibrate(host_ops, budget_s=args.cpu_budget)
         f, t, sample = cpu_sample_time(host_ops, rows, kind)
-        cpu = {"value": f / t / 1e12, "unit": "TFLOP/s", "cores": os.cpu_count() or 1, "kind": kind,
-               "sample": sample + ("; reference golden bsr_matrix::spmm_bfloat16 / sddmm"
+        cpu = {"value": f / t / 1e12, "unit": "TFLOP/s", "cores": cpu_threads_used(host_ops),
+               "kind": kind,
+               "sample": sample + ("; reference golden " + golden_name(host_ops)
                                    if kind == "reference" else "; oracle restatement")}
 
     out = {
@@ -696,7 +792,12 @@ def run_e2e(args, runs, dev, dist, shard):
         host = []
         for r in runs:
             op = r["op"]
-            if op["kind"] == "spmm":
+            if op["kind"] == "spgemm":
+                hc = dict(rp=_pinned(op["rp"]), ci=_pinned(op["ci"]), v=_pinned(op["vals"]),
+                          brp=_pinned(op["brp"]), bci=_pinned(op["bci"]), bv=_pinned(op["bvals"]))
+                h2d += sum(hc[k].nbytes for k in hc)
+                d2h += 4 * (op["M"] // op["Ra"] + 1) + op["out_nnzb"] * (4 + 2 * op["Ra"] * op["Cb"])
+            elif op["kind"] == "spmm":
                 hc = dict(rp=_pinned(op["rp"]), ci=_pinned(op["ci"]), v=_pinned(op["vals"]),
                           B=_pinned(op["B"]),
                           out=torch.empty((op["M"], op["N"]), dtype=torch.int16).pin_memory()
@@ -708,12 +809,16 @@ def run_e2e(args, runs, dev, dist, shard):
                           out=torch.empty(max(nv, 1), dtype=torch.int16).pin_memory()
                           .numpy().view(np.uint16)[:nv])
                 h2d += hc["rp"].nbytes + hc["ci"].nbytes + hc["A"].nbytes + hc["B"].nbytes
-            d2h += hc["out"].nbytes
+            if "out" in hc:
+                d2h += hc["out"].nbytes
             host.append((op, hc, strategy_for(op, args.strategy)))
 
         def one():
             for op, hc, strat in host:
-                if op["kind"] == "spmm":
+                if op["kind"] == "spgemm":
+                    bsp.spgemm_host(op["M"], op["K"], op["N"], op["Ra"], op["Ca"], op["Cb"], hc["rp"],
+                                    hc["ci"], hc["v"], hc["brp"], hc["bci"], hc["bv"], dev=dev)
+                elif op["kind"] == "spmm":
                     bsp.spmm_host(op["M"], op["K"], op["R"], op["C"], hc["rp"], hc["ci"], hc["v"], hc["B"],
                                   op["N"], strategy=strat, dev=dev, out=hc["out"])
                 else:
@@ -730,7 +835,9 @@ def run_e2e(args, runs, dev, dist, shard):
     return {"value": f / t / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": int(h2d),
             "d2h_bytes_per_step": int(d2h), "steps": steps,
             "path": ("bsp_dist.ShardedSpmm (host B and A values in, NCCL exchange, full C out)"
-                     if shard is not None else "bsp_spmm_host / bsp_sddmm_host (C ABI, host buffers)")}
+                     if shard is not None else
+                     "bsp_spmm_host / bsp_sddmm_host / bsp_spgemm_host (C ABI, host buffers; SpGEMM "
+                     "plans C's pattern on the host every call, as bsr_matrix::spgemm does)")}
 
 
 def traffic_for(workload, name):
@@ -774,7 +881,8 @@ def run_reference(args):
            "dtype": "bf16", "data": "synthetic",
            "config": {"workload": WORKLOAD_DESC[args.workload], "name": args.workload,
                       "strategy": "cpu golden"},
-           "cpu_baseline": {"value": v, "unit": "TFLOP/s", "cores": threads, "kind": kind,
+           "cpu_baseline": {"value": v, "unit": "TFLOP/s", "cores": cpu_threads_used(ops, threads),
+                            "kind": kind,
                             "sample": sample + ", every step"},
            "e2e": {"value": v, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(out), flush=True)

@@ -269,6 +269,12 @@ bsp_status bsp_sddmm_host_profile(bsp_device* dev, int64_t M, int64_t N, int32_t
  * rounded to bf16 once.  Repeated column indices inside a row of A or B
  * contribute every stored block, as in the reference's loops.
  * Block sizes: Ra, Ca, Cb each 32, 64 or 128.
+ * Options (bsp_spmm_opts): n_tiles 1 = 4 segments per unit (MMA N = 128),
+ * 2 = 8 (N = 256), 0 = 8 unless 4 moves fewer operand bytes (sparse
+ * products); steps_per_stage 1..4; producers; max_ctas; timeout_ms;
+ * no_load_balance 0 = units dealt in order to the least-loaded CTA (default,
+ * keeps neighbouring units concurrent for L2 reuse), 1 = contiguous split,
+ * 2 = serpentine over units sorted by work.
  *
  * The plan holds C's pattern (computed on the host from A's and B's
  * patterns); read it with bsp_spgemm_pattern, allocate nnzb * Ra * Cb bf16
@@ -291,7 +297,7 @@ bsp_status bsp_spgemm_plan_destroy(bsp_spgemm_plan* plan);
 /* info[0] units, [1] grid, [2] steps, [3] block products (A[i,k]*B[k,j] pairs),
  * [4] output blocks, [5] kc, [6] stages, [7] sub-steps per stage,
  * [8] table bytes, [9] shared memory, [10] TMEM columns, [11] segments per
- * unit, [12] producer warps. */
+ * unit, [12] producer warps, [13] TMA boxes over all steps (per k-chunk). */
 bsp_status bsp_spgemm_plan_info(const bsp_spgemm_plan* plan, int64_t info[16]);
 
 /* Host-buffer SpGEMM (bsr_matrix<T>::spgemm semantics: host BSR in, host BSR

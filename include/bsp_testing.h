@@ -43,9 +43,12 @@ bsp_status bsp_sddmm_plan_inspect(int64_t M, int64_t N, int32_t R, int32_t C, in
  * info[16] as bsp_spgemm_plan_info.  With null output buffers only `info` is
  * filled: out_row_ptr[M/Ra + 1], out_col_idx[info[4]] (C's pattern),
  * units_out[info[0] * 48] (step_begin, n_steps, n_ent, nseg, seg_x[8],
- * ent_r[4], out_blk[4][8] per unit, in CTA order), steps_out[info[2] * 12]
- * (a_y[4], b_y[8]: TMA row of each entry's A slab / segment's B block, -1
- * absent), cta_begin_out[info[1] + 1]. */
+ * ent_r[4], out_blk[4][8] per unit, in CTA order), steps_out[info[2] * 16]
+ * (per step: a_y[4] first A row of each entry box or -32*L for L zero slabs,
+ * b_z[8] first B block of each segment box or -L for L zero segments, then
+ * the meta bytes a_meta[4], b_meta[8], 4 pad bytes: bit 7 box present, bits
+ * 0-2 first slot, bits 3-4 log2 slots, bits 5-6 32-column slice of B),
+ * cta_begin_out[info[1] + 1]. */
 bsp_status bsp_spgemm_plan_inspect(int64_t M, int64_t K, int64_t N, int32_t Ra, int32_t Ca,
                                    int32_t Cb, int64_t a_nnzb, const int32_t* a_row_ptr,
                                    const int32_t* a_col_idx, int64_t b_nnzb,

@@ -402,7 +402,7 @@ def sddmm_host(M, N, R, C, row_ptr, col_idx, mask_values, A, B, K, strategy=NAIV
 # ------------------------------------------------------------------ SpGEMM --
 SPGEMM_INFO_KEYS = ["units", "ctas", "steps", "pairs", "out_nnzb", "kc", "stages",
                     "steps_per_stage", "plan_bytes", "smem_bytes", "tmem_cols", "nseg_max",
-                    "producers"]
+                    "producers", "boxes"]
 
 
 class SpgemmPlan:
@@ -468,8 +468,38 @@ def spgemm(A: DeviceBSR, B: DeviceBSR, opts=None, dev: Device = None) -> DeviceB
 
 def spgemm_host(M, K, N, Ra, Ca, Cb, a_row_ptr, a_col_idx, a_values, b_row_ptr, b_col_idx,
                 b_values, opts=None, dev: Device = None, iters=0):
-    """Host BSR in, host BSR out: (row_ptr, col_idx, values bf16 bits) of A @ B,
-    plus the mean launch time in ms when iters > 0."""
+    """Host BSR in, host BSR out: (row_ptr, col_idx, values bf16 bits) of A @ B
+    (bsr_matrix<T>::spgemm semantics), plus the mean launch time in ms when
+    iters > 0.  Uploads, plans once (C's pattern on the host), runs, downloads."""
+    import torch
+
+    dev = dev or device(0)
+    A = DeviceBSR.from_host(M, K, Ra, Ca, a_row_ptr, a_col_idx, a_values, dev.ordinal)
+    B = DeviceBSR.from_host(K, N, Ca, Cb, b_row_ptr, b_col_idx, b_values, dev.ordinal)
+    plan = SpgemmPlan(dev, A, B, opts)
+    n = plan.nnzb * Ra * Cb
+    out = torch.empty(max(n, 8), dtype=torch.bfloat16, device=A.row_ptr.device)
+    plan.execute(A, B, out)
+    ms = 0.0
+    if iters > 0:
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(iters):
+            plan.execute(A, B, out)
+        e1.record()
+        e1.synchronize()
+        ms = e0.elapsed_time(e1) / iters
+    dev.synchronize()
+    res = (plan.row_ptr.copy(), plan.col_idx.copy(), to_host_bits(out)[:n])
+    plan.close()
+    return res + (ms,) if iters > 0 else res
+
+
+def spgemm_host_c(M, K, N, Ra, Ca, Cb, a_row_ptr, a_col_idx, a_values, b_row_ptr, b_col_idx,
+                  b_values, opts=None, dev: Device = None, iters=0):
+    """The same through the C ABI's host-buffer entry point bsp_spgemm_host
+    (a size query, then the product: C's pattern is planned twice)."""
     dev = dev or device(0)
     arp = np.ascontiguousarray(a_row_ptr, dtype=np.int32)
     aci = np.ascontiguousarray(a_col_idx, dtype=np.int32)
@@ -512,7 +542,7 @@ def inspect_spgemm_plan(M, K, N, Ra, Ca, Cb, a_row_ptr, a_col_idx, b_row_ptr, b_
     orp = np.zeros(M // Ra + 1, np.int32)
     oci = np.zeros(max(nb, 1), np.int32)
     units = np.zeros((max(nu, 1), 48), np.int32)
-    steps = np.zeros((max(ns, 1), 12), np.int32)
+    steps = np.zeros((max(ns, 1), 16), np.int32)
     cta = np.zeros(nc + 1, np.int32)
     _check(lib().bsp_spgemm_plan_inspect(*args, _ptr(orp), _ptr(oci), _ptr(units), _ptr(steps),
                                          _ptr(cta)))

@@ -160,18 +160,29 @@ struct SpgemmUnit {
 };
 static_assert(sizeof(SpgemmUnit) == 192, "unit layout");
 
-// One step: TMA row coordinates of the operands, -1 = absent (zero box).
-//   a_y[e] = (A block index) * Ra + slab * 32, rows of A viewed as [nnzb_a*Ra, Ca]
-//   b_y[s] = (B block index) * Ca,             rows of B viewed as [nnzb_b*Ca, Cb]
+// One step = the TMA boxes that fill its operand slots.  Consecutive slots
+// whose data is contiguous in memory (or which are all absent, i.e. zero)
+// share one box of 1, 2, 4 (entries) or 1, 2, 4, 8 (segments) slots.
+//   a_y[i]    box i of the entries: first row of A viewed as [nnzb_a*Ra, Ca]
+//             (block * Ra + slab * 32), or -32*L for L zero slabs
+//   b_z[i]    box i of the segments: first block of B viewed as
+//             [nnzb_b][Ca][Cb], or -L for L zero segments
+//   a_meta[i], b_meta[i]: bit 7 box present, bits 0-2 first slot,
+//             bits 3-4 log2 of the slot count, bits 5-6 (segments) the
+//             32-column slice t inside the block (x = 32 t)
 struct SpgemmStep {
   int32_t a_y[kSpgemmEnt];
-  int32_t b_y[kSpgemmMaxSeg];
+  int32_t b_z[kSpgemmMaxSeg];
+  uint8_t a_meta[kSpgemmEnt];
+  uint8_t b_meta[kSpgemmMaxSeg];
+  uint8_t pad[4];
 };
-static_assert(sizeof(SpgemmStep) == 48, "step layout");
+static_assert(sizeof(SpgemmStep) == 64, "step layout");
+constexpr int kSpgemmBoxValid = 0x80;
 
 struct SpgemmKernelParams {
-  CUtensorMap tm_a;  // A values [nnzb_a*Ra rows, Ca cols], box {kc, 32}
-  CUtensorMap tm_b;  // B values [nnzb_b*Ca rows, Cb cols], box {32, kc}, 64B swizzle
+  CUtensorMap tm_a[3];  // A values [nnzb_a*Ra rows, Ca cols], box {kc, 32 << l}
+  CUtensorMap tm_b[4];  // B values [nnzb_b][Ca][Cb], box {32, kc, 1 << l}, 64B swizzle
   const SpgemmUnit* units;   // in CTA order
   const SpgemmStep* steps;
   const int32_t* cta_begin;  // [grid + 1]
@@ -212,7 +223,9 @@ struct bsp_spgemm_plan {
   int32_t Ra = 0, Ca = 0, Cb = 0, kc = 0, nkc = 1, sps = 1;
   int32_t grid = 0, stages = 0, stage_bytes = 0, sub_bytes = 0, smem_bytes = 0, tmem_cols = 0;
   int32_t nseg_max = 8, nprod = 1;
+  int32_t la_log2 = 0, lb_log2 = 0;  // largest box (log2 slots) of the entries / segments
   int64_t n_units = 0, n_steps = 0;
+  int64_t n_boxes = 0;       // TMA boxes over all steps (one k-chunk)
   int64_t pairs = 0;         // block products A[i,k] * B[k,j] (useful work)
   uint64_t timeout_ns = 0;
   void* d_blob = nullptr;    // units | steps | cta_begin

@@ -810,6 +810,7 @@ bsp_status bsp_spgemm_plan_info(const bsp_spgemm_plan* p, int64_t info[16]) {
   info[10] = p->tmem_cols;
   info[11] = p->nseg_max;
   info[12] = p->nprod;
+  info[13] = p->n_boxes;
   return BSP_OK;
 }
 

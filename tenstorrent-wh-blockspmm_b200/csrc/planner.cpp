@@ -73,6 +73,29 @@ void serpentine_order(const std::vector<int64_t>& weight, int parts,
   }
 }
 
+// Items in their given order, each to the part with the least weight so far
+// (ties: lowest part).  Parts then run their lists in that order, so items
+// that are close in the given order run at about the same time (shared
+// operands stay in L2) while the parts' totals stay balanced.
+static void ordered_greedy(const std::vector<int64_t>& weight, int parts,
+                           std::vector<std::vector<int32_t>>* per_part) {
+  per_part->assign(parts, {});
+  std::vector<std::pair<int64_t, int32_t>> heap;
+  heap.reserve(parts);
+  for (int p = 0; p < parts; ++p) heap.push_back({0, p});
+  auto cmp = [](const std::pair<int64_t, int32_t>& a, const std::pair<int64_t, int32_t>& b) {
+    return a.first != b.first ? a.first > b.first : a.second > b.second;
+  };
+  std::make_heap(heap.begin(), heap.end(), cmp);
+  for (size_t i = 0; i < weight.size(); ++i) {
+    std::pop_heap(heap.begin(), heap.end(), cmp);
+    auto& top = heap.back();
+    (*per_part)[top.second].push_back(static_cast<int32_t>(i));
+    top.first += weight[i];
+    std::push_heap(heap.begin(), heap.end(), cmp);
+  }
+}
+
 static void contiguous_split(int64_t n, int parts, std::vector<std::vector<int32_t>>* per_part) {
   per_part->assign(parts, {});
   for (int p = 0; p < parts; ++p) {
@@ -970,6 +993,66 @@ bsp_status plan_sddmm_rowstack(bsp_sddmm_plan* p, const int32_t* row_ptr, const 
 // ascending order.  A k repeated inside a row of A (or a column repeated in
 // row k of B) gives layered steps, one per pair of repeats, so every stored
 // block product is taken exactly once.
+// Cut one step's slots into TMA boxes.  ay[e]: first A row of entry e's slab
+// (-1 absent); bb[s] / bt[s]: block of B and 32-column slice of segment s
+// (block -1 absent).  A run of slots that are all absent, or whose data is
+// contiguous (A slabs 32 rows apart; B segments of one slice in consecutive
+// blocks), is covered by power-of-two boxes of at most 1 << la_log2 /
+// 1 << lb_log2 slots, largest first.
+static SpgemmStep spgemm_boxes(const int32_t* ay, const int32_t* bb, const int32_t* bt, int nseg,
+                               int la_log2, int lb_log2) {
+  SpgemmStep st;
+  memset(&st, 0, sizeof(st));
+  int nbox = 0;
+  auto emit_a = [&](int e0, int len) {
+    while (len > 0) {
+      int l = la_log2;
+      while ((1 << l) > len) --l;
+      const int L = 1 << l;
+      st.a_y[nbox] = ay[e0] >= 0 ? ay[e0] : -32 * L;
+      st.a_meta[nbox] = static_cast<uint8_t>(kSpgemmBoxValid | e0 | (l << 3));
+      ++nbox;
+      e0 += L;
+      len -= L;
+    }
+  };
+  for (int e = 0; e < kSpgemmEnt;) {
+    int r = e + 1;
+    while (r < kSpgemmEnt && ((ay[e] < 0 && ay[r] < 0) || (ay[e] >= 0 && ay[r] == ay[r - 1] + 32))) ++r;
+    emit_a(e, r - e);
+    e = r;
+  }
+  nbox = 0;
+  auto emit_b = [&](int s0, int len) {
+    while (len > 0) {
+      int l = lb_log2;
+      while ((1 << l) > len) --l;
+      const int L = 1 << l;
+      st.b_z[nbox] = bb[s0] >= 0 ? bb[s0] : -L;
+      st.b_meta[nbox] = static_cast<uint8_t>(kSpgemmBoxValid | s0 | (l << 3) | ((bt[s0] & 3) << 5));
+      ++nbox;
+      s0 += L;
+      len -= L;
+    }
+  };
+  for (int s_ = 0; s_ < nseg;) {
+    int r = s_ + 1;
+    while (r < nseg && ((bb[s_] < 0 && bb[r] < 0) ||
+                        (bb[s_] >= 0 && bb[r] == bb[r - 1] + 1 && bt[r] == bt[s_])))
+      ++r;
+    emit_b(s_, r - s_);
+    s_ = r;
+  }
+  return st;
+}
+
+static int spgemm_box_count(const SpgemmStep& st) {
+  int n = 0;
+  for (int i = 0; i < kSpgemmEnt; ++i) n += (st.a_meta[i] & kSpgemmBoxValid) ? 1 : 0;
+  for (int i = 0; i < kSpgemmMaxSeg; ++i) n += (st.b_meta[i] & kSpgemmBoxValid) ? 1 : 0;
+  return n;
+}
+
 bsp_status plan_spgemm_host(bsp_spgemm_plan* p, const int32_t* a_rp, const int32_t* a_ci,
                             const int32_t* b_rp, const int32_t* b_ci, int sm_count, int max_smem,
                             const bsp_spmm_opts* opts) {
@@ -1023,154 +1106,197 @@ bsp_status plan_spgemm_host(bsp_spgemm_plan* p, const int32_t* a_rp, const int32
   // ---- stage geometry ----
   const int kc = Ca == 32 ? 32 : 64;
   const int nkc = Ca / kc;
-  int nseg_max = (o.n_tiles == 1) ? 4 : 8;
   p->kc = kc;
   p->nkc = nkc;
-  p->nseg_max = nseg_max;
   const int spr = Ra / 32;                      // slabs (entries) per output block-row
   const int segs_per_col = Cb / 32;             // segments per output block-column
-  const int cpu = std::max(1, nseg_max / segs_per_col);  // block-columns per unit
   const int64_t n_ent = nbr * spr;
   const int64_t ngroups = (n_ent + kSpgemmEnt - 1) / kSpgemmEnt;
 
+  // largest boxes the tensors can hold (a box may not exceed its tensor)
+  p->la_log2 = 0;
+  while (p->la_log2 < 2 && (int64_t(32) << (p->la_log2 + 1)) <= p->nnzb_a * Ra) ++p->la_log2;
+  p->lb_log2 = 0;
+  while (p->lb_log2 < 3 && (int64_t(1) << (p->lb_log2 + 1)) <= p->nnzb_b) ++p->lb_log2;
+  // The unit list and step table for nseg_max segments per unit.
+  auto build = [&](int nseg_max, std::vector<SpgemmUnit>& units, std::vector<int64_t>& weight,
+                   std::vector<SpgemmStep>& steps, int64_t& n_boxes) -> bsp_status {
+    n_boxes = 0;
+    units.clear();
+    weight.clear();
+    steps.clear();
+    const int cpu = std::max(1, nseg_max / segs_per_col);  // block-columns per unit
+    std::vector<int64_t> colpos(static_cast<size_t>(nbc), -1), colstamp(static_cast<size_t>(nbc), -1);
+    std::vector<int64_t> kstamp(static_cast<size_t>(nbk), -1);
+    std::vector<int32_t> cols, ks;
+    std::vector<std::vector<int32_t>> chunk_k;
+    std::vector<int32_t> lastk;
+    std::vector<std::vector<int32_t>> bl(kSpgemmMaxSeg);  // B blocks of row k per unit column
+    // (k, A block) of each distinct block-row of the group, sorted by k (stable)
+    std::vector<std::vector<std::pair<int32_t, int32_t>>> rowpairs;
+    for (int64_t g = 0; g < ngroups; ++g) {
+      const int64_t e0 = g * kSpgemmEnt, e1 = std::min<int64_t>(n_ent, e0 + kSpgemmEnt);
+      const int64_t r0 = e0 / spr, r1 = (e1 - 1) / spr + 1;  // block-rows [r0, r1)
+      cols.clear();
+      for (int64_t i = r0; i < r1; ++i)
+        for (int32_t q = p->out_row_ptr[i]; q < p->out_row_ptr[i + 1]; ++q) {
+          const int32_t j = p->out_col_idx[q];
+          if (colstamp[j] != g) {
+            colstamp[j] = g;
+            cols.push_back(j);
+          }
+        }
+      if (cols.empty()) continue;
+      std::sort(cols.begin(), cols.end());
+      for (size_t c = 0; c < cols.size(); ++c) colpos[cols[c]] = static_cast<int64_t>(c);
+      const int64_t nchunks = (static_cast<int64_t>(cols.size()) + cpu - 1) / cpu;
+      rowpairs.assign(static_cast<size_t>(r1 - r0), {});
+      ks.clear();
+      for (int64_t i = r0; i < r1; ++i) {
+        auto& v = rowpairs[static_cast<size_t>(i - r0)];
+        for (int32_t a = a_rp[i]; a < a_rp[i + 1]; ++a) {
+          v.push_back({a_ci[a], a});
+          if (kstamp[a_ci[a]] != g) {
+            kstamp[a_ci[a]] = g;
+            ks.push_back(a_ci[a]);
+          }
+        }
+        std::stable_sort(v.begin(), v.end(),
+                         [](const std::pair<int32_t, int32_t>& x, const std::pair<int32_t, int32_t>& y) {
+                           return x.first < y.first;
+                         });
+      }
+      std::sort(ks.begin(), ks.end());
+      chunk_k.assign(static_cast<size_t>(nchunks), {});
+      lastk.assign(static_cast<size_t>(nchunks), -1);
+      for (int32_t k : ks)
+        for (int32_t b = b_rp[k]; b < b_rp[k + 1]; ++b) {
+          const int64_t c = colpos[b_ci[b]] / cpu;
+          if (lastk[c] != k) {
+            lastk[c] = k;
+            chunk_k[c].push_back(k);
+          }
+        }
+      for (int64_t c = 0; c < nchunks; ++c) {
+        SpgemmUnit u;
+        memset(&u, 0, sizeof(u));
+        const int64_t j0 = c * cpu;
+        const int ncols = static_cast<int>(std::min<int64_t>(cpu, static_cast<int64_t>(cols.size()) - j0));
+        u.n_ent = static_cast<int32_t>(e1 - e0);
+        u.nseg = std::min(nseg_max, ncols * segs_per_col);
+        // segments slice-major: segment s is 32-column slice s / ncols of
+        // column s % ncols, so that a slice of consecutive stored blocks of a
+        // row of B lands in consecutive segments (one TMA box)
+        for (int s_ = 0; s_ < kSpgemmMaxSeg; ++s_) u.seg_x[s_] = s_ < u.nseg ? (s_ / ncols) * 32 : 0;
+        for (int e = 0; e < kSpgemmEnt; ++e) {
+          const int64_t E = e0 + e;
+          u.ent_r[e] = E < e1 ? static_cast<int32_t>(E % spr) * 32 : 0;
+          for (int s_ = 0; s_ < kSpgemmMaxSeg; ++s_) {
+            u.out_blk[e][s_] = -1;
+            if (E >= e1 || s_ >= u.nseg) continue;
+            const int64_t i = E / spr;
+            const int32_t j = cols[static_cast<size_t>(j0 + s_ % ncols)];
+            const int32_t* lo = p->out_col_idx.data() + p->out_row_ptr[i];
+            const int32_t* hi = p->out_col_idx.data() + p->out_row_ptr[i + 1];
+            const int32_t* it = std::lower_bound(lo, hi, j);
+            if (it != hi && *it == j) u.out_blk[e][s_] = static_cast<int32_t>(it - p->out_col_idx.data());
+          }
+        }
+        u.step_begin = static_cast<int32_t>(steps.size());
+        if (steps.size() >= (size_t(1) << 31) - 4096)
+          return set_error(BSP_ERR_UNSUPPORTED, "SpGEMM schedule too large");
+        for (int32_t k : chunk_k[c]) {
+          // A blocks of column k per entry, B blocks of row k per unit column
+          int32_t a_first[kSpgemmEnt], a_cnt[kSpgemmEnt];
+          int la_max = 0;
+          for (int e = 0; e < kSpgemmEnt; ++e) {
+            a_first[e] = 0;
+            a_cnt[e] = 0;
+            const int64_t E = e0 + e;
+            if (E >= e1) continue;
+            const auto& v = rowpairs[static_cast<size_t>(E / spr - r0)];
+            auto it = std::lower_bound(v.begin(), v.end(), std::make_pair(k, INT32_MIN));
+            a_first[e] = static_cast<int32_t>(it - v.begin());
+            while (it != v.end() && it->first == k) {
+              ++a_cnt[e];
+              ++it;
+            }
+            la_max = std::max(la_max, static_cast<int>(a_cnt[e]));
+          }
+          for (auto& l : bl) l.clear();
+          int lb_max = 0;
+          for (int32_t b = b_rp[k]; b < b_rp[k + 1]; ++b) {
+            const int64_t pos = colpos[b_ci[b]];
+            if (pos / cpu != c) continue;
+            auto& l = bl[static_cast<size_t>(pos - j0)];
+            l.push_back(b);
+            lb_max = std::max(lb_max, static_cast<int>(l.size()));
+          }
+          for (int la = 0; la < la_max; ++la)
+            for (int lb = 0; lb < lb_max; ++lb) {
+              int32_t ay[kSpgemmEnt], bb[kSpgemmMaxSeg], bt[kSpgemmMaxSeg];
+              for (int e = 0; e < kSpgemmEnt; ++e) {
+                ay[e] = -1;
+                if (la < a_cnt[e]) {
+                  const auto& v = rowpairs[static_cast<size_t>((e0 + e) / spr - r0)];
+                  ay[e] = v[static_cast<size_t>(a_first[e] + la)].second * Ra + u.ent_r[e];
+                }
+              }
+              for (int s_ = 0; s_ < u.nseg; ++s_) {
+                const auto& l = bl[static_cast<size_t>(s_ % ncols)];
+                bb[s_] = lb < static_cast<int>(l.size()) ? l[static_cast<size_t>(lb)] : -1;
+                bt[s_] = s_ / ncols;
+              }
+              steps.push_back(spgemm_boxes(ay, bb, bt, u.nseg, p->la_log2, p->lb_log2));
+              n_boxes += spgemm_box_count(steps.back());
+            }
+        }
+        u.n_steps = static_cast<int32_t>(steps.size()) - u.step_begin;
+        if (u.n_steps == 0) continue;  // cannot happen: every unit column has a product
+        units.push_back(u);
+        weight.push_back(static_cast<int64_t>(u.n_steps) * nkc + 2);
+      }
+    }
+    return BSP_OK;
+  };
+  // MMA N = 256 (8 segments) unless the caller asks for 128; when 256-wide
+  // tiles would be mostly empty, N = 128 is taken if its schedule moves fewer
+  // operand bytes (a step costs about its bytes: the smem fill rate bounds it).
   std::vector<SpgemmUnit> units;
   std::vector<int64_t> weight;
-  p->h_steps.clear();
-  std::vector<int64_t> colpos(static_cast<size_t>(nbc), -1), colstamp(static_cast<size_t>(nbc), -1);
-  std::vector<int64_t> kstamp(static_cast<size_t>(nbk), -1);
-  std::vector<int32_t> cols, ks;
-  std::vector<std::vector<int32_t>> chunk_k;
-  std::vector<int32_t> lastk;
-  std::vector<std::vector<int32_t>> bl(kSpgemmMaxSeg);  // B blocks of row k per unit column
-  // (k, A block) of each distinct block-row of the group, sorted by k (stable)
-  std::vector<std::vector<std::pair<int32_t, int32_t>>> rowpairs;
-  for (int64_t g = 0; g < ngroups; ++g) {
-    const int64_t e0 = g * kSpgemmEnt, e1 = std::min<int64_t>(n_ent, e0 + kSpgemmEnt);
-    const int64_t r0 = e0 / spr, r1 = (e1 - 1) / spr + 1;  // block-rows [r0, r1)
-    cols.clear();
-    for (int64_t i = r0; i < r1; ++i)
-      for (int32_t q = p->out_row_ptr[i]; q < p->out_row_ptr[i + 1]; ++q) {
-        const int32_t j = p->out_col_idx[q];
-        if (colstamp[j] != g) {
-          colstamp[j] = g;
-          cols.push_back(j);
-        }
+  int nseg_max = (o.n_tiles == 1) ? 4 : 8;
+  st = build(nseg_max, units, weight, p->h_steps, p->n_boxes);
+  if (st != BSP_OK) return st;
+  if (o.n_tiles == 0 && !p->h_steps.empty()) {
+    const double fill = static_cast<double>(pairs) * spr * segs_per_col /
+                        (static_cast<double>(p->h_steps.size()) * kSpgemmEnt * 8);
+    if (fill < 0.5) {
+      std::vector<SpgemmUnit> u4;
+      std::vector<int64_t> w4;
+      std::vector<SpgemmStep> s4;
+      int64_t b4 = 0;
+      st = build(4, u4, w4, s4, b4);
+      if (st != BSP_OK) return st;
+      auto sub = [&](int n) { return static_cast<double>(kSpgemmEnt * 32 * kc * 2 + n * kc * 64); };
+      if (static_cast<double>(s4.size()) * sub(4) < static_cast<double>(p->h_steps.size()) * sub(8)) {
+        units.swap(u4);
+        weight.swap(w4);
+        p->h_steps.swap(s4);
+        p->n_boxes = b4;
+        nseg_max = 4;
       }
-    if (cols.empty()) continue;
-    std::sort(cols.begin(), cols.end());
-    for (size_t c = 0; c < cols.size(); ++c) colpos[cols[c]] = static_cast<int64_t>(c);
-    const int64_t nchunks = (static_cast<int64_t>(cols.size()) + cpu - 1) / cpu;
-    rowpairs.assign(static_cast<size_t>(r1 - r0), {});
-    ks.clear();
-    for (int64_t i = r0; i < r1; ++i) {
-      auto& v = rowpairs[static_cast<size_t>(i - r0)];
-      for (int32_t a = a_rp[i]; a < a_rp[i + 1]; ++a) {
-        v.push_back({a_ci[a], a});
-        if (kstamp[a_ci[a]] != g) {
-          kstamp[a_ci[a]] = g;
-          ks.push_back(a_ci[a]);
-        }
-      }
-      std::stable_sort(v.begin(), v.end(),
-                       [](const std::pair<int32_t, int32_t>& x, const std::pair<int32_t, int32_t>& y) {
-                         return x.first < y.first;
-                       });
-    }
-    std::sort(ks.begin(), ks.end());
-    chunk_k.assign(static_cast<size_t>(nchunks), {});
-    lastk.assign(static_cast<size_t>(nchunks), -1);
-    for (int32_t k : ks)
-      for (int32_t b = b_rp[k]; b < b_rp[k + 1]; ++b) {
-        const int64_t c = colpos[b_ci[b]] / cpu;
-        if (lastk[c] != k) {
-          lastk[c] = k;
-          chunk_k[c].push_back(k);
-        }
-      }
-    for (int64_t c = 0; c < nchunks; ++c) {
-      SpgemmUnit u;
-      memset(&u, 0, sizeof(u));
-      const int64_t j0 = c * cpu;
-      const int ncols = static_cast<int>(std::min<int64_t>(cpu, static_cast<int64_t>(cols.size()) - j0));
-      u.n_ent = static_cast<int32_t>(e1 - e0);
-      u.nseg = std::min(nseg_max, ncols * segs_per_col);
-      for (int s_ = 0; s_ < kSpgemmMaxSeg; ++s_) u.seg_x[s_] = s_ < u.nseg ? (s_ % segs_per_col) * 32 : 0;
-      for (int e = 0; e < kSpgemmEnt; ++e) {
-        const int64_t E = e0 + e;
-        u.ent_r[e] = E < e1 ? static_cast<int32_t>(E % spr) * 32 : 0;
-        for (int s_ = 0; s_ < kSpgemmMaxSeg; ++s_) {
-          u.out_blk[e][s_] = -1;
-          if (E >= e1 || s_ >= u.nseg) continue;
-          const int64_t i = E / spr;
-          const int32_t j = cols[static_cast<size_t>(j0 + s_ / segs_per_col)];
-          const int32_t* lo = p->out_col_idx.data() + p->out_row_ptr[i];
-          const int32_t* hi = p->out_col_idx.data() + p->out_row_ptr[i + 1];
-          const int32_t* it = std::lower_bound(lo, hi, j);
-          if (it != hi && *it == j) u.out_blk[e][s_] = static_cast<int32_t>(it - p->out_col_idx.data());
-        }
-      }
-      u.step_begin = static_cast<int32_t>(p->h_steps.size());
-      if (p->h_steps.size() >= (size_t(1) << 31) - 4096)
-        return set_error(BSP_ERR_UNSUPPORTED, "SpGEMM schedule too large");
-      for (int32_t k : chunk_k[c]) {
-        // A blocks of column k per entry, B blocks of row k per unit column
-        int32_t a_first[kSpgemmEnt], a_cnt[kSpgemmEnt];
-        int la_max = 0;
-        for (int e = 0; e < kSpgemmEnt; ++e) {
-          a_first[e] = 0;
-          a_cnt[e] = 0;
-          const int64_t E = e0 + e;
-          if (E >= e1) continue;
-          const auto& v = rowpairs[static_cast<size_t>(E / spr - r0)];
-          auto it = std::lower_bound(v.begin(), v.end(), std::make_pair(k, INT32_MIN));
-          a_first[e] = static_cast<int32_t>(it - v.begin());
-          while (it != v.end() && it->first == k) {
-            ++a_cnt[e];
-            ++it;
-          }
-          la_max = std::max(la_max, static_cast<int>(a_cnt[e]));
-        }
-        for (auto& l : bl) l.clear();
-        int lb_max = 0;
-        for (int32_t b = b_rp[k]; b < b_rp[k + 1]; ++b) {
-          const int64_t pos = colpos[b_ci[b]];
-          if (pos / cpu != c) continue;
-          auto& l = bl[static_cast<size_t>(pos - j0)];
-          l.push_back(b);
-          lb_max = std::max(lb_max, static_cast<int>(l.size()));
-        }
-        for (int la = 0; la < la_max; ++la)
-          for (int lb = 0; lb < lb_max; ++lb) {
-            SpgemmStep sp;
-            for (int e = 0; e < kSpgemmEnt; ++e) {
-              sp.a_y[e] = -1;
-              if (la < a_cnt[e]) {
-                const auto& v = rowpairs[static_cast<size_t>((e0 + e) / spr - r0)];
-                sp.a_y[e] = v[static_cast<size_t>(a_first[e] + la)].second * Ra + u.ent_r[e];
-              }
-            }
-            for (int s_ = 0; s_ < kSpgemmMaxSeg; ++s_) {
-              sp.b_y[s_] = -1;
-              if (s_ >= u.nseg) continue;
-              const auto& l = bl[static_cast<size_t>(s_ / segs_per_col)];
-              if (lb < static_cast<int>(l.size())) sp.b_y[s_] = l[static_cast<size_t>(lb)] * Ca;
-            }
-            p->h_steps.push_back(sp);
-          }
-      }
-      u.n_steps = static_cast<int32_t>(p->h_steps.size()) - u.step_begin;
-      if (u.n_steps == 0) continue;  // cannot happen: every unit column has a product
-      units.push_back(u);
-      weight.push_back(static_cast<int64_t>(u.n_steps) * nkc + 2);
     }
   }
+  p->nseg_max = nseg_max;
   p->n_steps = static_cast<int64_t>(p->h_steps.size());
 
   int grid = o.max_ctas > 0 ? std::min(o.max_ctas, sm_count) : sm_count;
   grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(grid, units.size())));
   std::vector<std::vector<int32_t>> per;
-  if (o.no_load_balance) contiguous_split(static_cast<int64_t>(units.size()), grid, &per);
-  else serpentine_order(weight, grid, &per);
+  // no_load_balance: 0 ordered greedy (default), 1 contiguous split, 2 serpentine
+  if (o.no_load_balance == 1) contiguous_split(static_cast<int64_t>(units.size()), grid, &per);
+  else if (o.no_load_balance == 2) serpentine_order(weight, grid, &per);
+  else ordered_greedy(weight, grid, &per);
   p->h_units.clear();
   p->h_cta_begin.assign(1, 0);
   for (int cta = 0; cta < grid; ++cta) {
@@ -1190,19 +1316,11 @@ bsp_status plan_spgemm_host(bsp_spgemm_plan* p, const int32_t* a_rp, const int32
   }
   if (max_stages < 2) return set_error(BSP_ERR_UNSUPPORTED, "stage too large for the pipeline");
   const int stage_bytes = sps * sub_bytes;
-  int nprod = 1, stages = max_stages;
-  if (o.producers > 0) {
-    nprod = std::min({o.producers, spgemm_max_producers(), max_stages});
-    stages = max_stages / nprod * nprod;
-  } else {
-    for (int q = 2; q <= std::min(spgemm_max_producers(), max_stages); ++q) {
-      const int sq = max_stages / q * q;
-      if (sq >= stages - (stages > 6 ? 1 : 0)) {
-        nprod = q;
-        stages = sq;
-      }
-    }
-  }
+  // Issuing the many small boxes of a stage is the producers' bottleneck, so
+  // as many producer warps as can own stages, even at the cost of a ring slot.
+  const int nprod = std::min({o.producers > 0 ? o.producers : spgemm_max_producers(),
+                              spgemm_max_producers(), max_stages});
+  const int stages = max_stages / nprod * nprod;
   p->sps = sps;
   p->sub_bytes = sub_bytes;
   p->nprod = nprod;

@@ -27,6 +27,8 @@
 // Every wait is bounded (bsp_ptx.cuh).
 #include <cuda_bf16.h>
 
+#include <cstddef>
+
 #include "bsp_internal.h"
 #include "bsp_ptx.cuh"
 
@@ -64,18 +66,48 @@ __device__ __noinline__ bool sg_drain_wait(uint32_t bar, uint32_t parity, const 
 }
 
 // Lane roles inside one issue round (two sub-steps): lanes 0..7 entry boxes
-// (sub-step lane>>2, entry lane&3), lanes 8..23 segment boxes (sub-step
-// (lane-8)>>3, segment (lane-8)&7).
+// (sub-step lane>>2, box lane&3), lanes 8..23 segment boxes (sub-step
+// (lane-8)>>3, box (lane-8)&7).
 __device__ __forceinline__ int lane_sub(int lane) { return lane < 8 ? (lane >> 2) : ((lane - 8) >> 3); }
 __device__ __forceinline__ int lane_idx(int lane) { return lane < 8 ? (lane & 3) : ((lane - 8) & 7); }
 
 // Producer warp pw of P: the CTA's stage sequence is unit-major (unit u has
 // ceil(n_steps * nkc / sps) stages); this warp issues every P-th of them.
+// The step words of the next owned stage are fetched while the current one
+// waits for its slot and issues, so their latency stays off the critical path.
+struct SgCursor {
+  int u;            // unit (u_end: done)
+  int ls;           // stage inside the unit
+  int64_t seq;      // CTA stages before the unit
+  int ns, total_sub, step_begin, nseg;
+};
+
+__device__ __forceinline__ void sg_load_unit(const SpgemmKernelParams& p, SgCursor* c, int my_idx) {
+  const SpgemmUnit* un = p.units + c->u;
+  const int n_steps = __ldg(&un->n_steps);
+  c->step_begin = __ldg(&un->step_begin);
+  c->nseg = __ldg(&un->nseg);
+  c->total_sub = n_steps * p.nkc;
+  c->ns = (c->total_sub + p.sps - 1) / p.sps;
+}
+
+// Move to the next stage this producer owns (P stages further on).
+__device__ __forceinline__ void sg_advance(const SpgemmKernelParams& p, SgCursor* c, int u_end, int P,
+                                           int my_idx) {
+  c->ls += P;
+  while (c->ls >= c->ns) {
+    c->ls -= c->ns;
+    c->seq += c->ns;
+    if (++c->u >= u_end) return;
+    sg_load_unit(p, c, my_idx);
+  }
+}
+
 __device__ __forceinline__ void sg_producer(const SpgemmKernelParams& p, SgSmemHeader* hdr,
                                            uint32_t stage0, int u_begin, int u_end,
                                            const WaitCtl& ctl, int pw, int lane) {
   const int P = p.nprod;
-  const int nkc = p.nkc, sps = p.sps, kc = p.kc;
+  const int sps = p.sps, kc = p.kc;
   const uint32_t a_slot = static_cast<uint32_t>(p.a_slot);
   const uint32_t seg_bytes = static_cast<uint32_t>(p.seg_bytes);
   const uint32_t a_all = kSpgemmEnt * a_slot;
@@ -84,61 +116,75 @@ __device__ __forceinline__ void sg_producer(const SpgemmKernelParams& p, SgSmemH
   const int my_sub = lane_sub(lane);
   const int my_idx = lane_idx(lane);
   const int my_word = is_a ? my_idx : kSpgemmEnt + my_idx;
-  const uint32_t my_off = is_a ? static_cast<uint32_t>(my_idx) * a_slot
-                               : a_all + static_cast<uint32_t>(my_idx) * seg_bytes;
-  int64_t seq = 0;  // stages of the CTA before the current unit
+  const int my_meta = is_a ? offsetof(SpgemmStep, a_meta) + my_idx : offsetof(SpgemmStep, b_meta) + my_idx;
   uint32_t armed = 0, armed_parity = 0;
-  bool ok = true;
-#pragma unroll 1
-  for (int u = u_begin; u < u_end && ok; ++u) {
-    const SpgemmUnit* un = p.units + u;
-    const int n_steps = __ldg(&un->n_steps);
-    const int step_begin = __ldg(&un->step_begin);
-    const int nseg = __ldg(&un->nseg);
-    const int32_t seg_x = __ldg(&un->seg_x[my_idx & 7]);
-    const int total_sub = n_steps * nkc;
-    const int ns = (total_sub + sps - 1) / sps;
-    int ls = static_cast<int>(((pw - seq) % P + P) % P);
-#pragma unroll 1
-    for (; ls < ns; ls += P) {
-      const int64_t gs = seq + ls;
-      const int slot = static_cast<int>(gs % p.stages);
-      const uint32_t phase = static_cast<uint32_t>((gs / p.stages) & 1);
-      const int n_sub = min(sps, total_sub - ls * sps);
-      // this lane's step words for the (up to two) issue rounds, fetched
-      // before the wait so that their latency hides behind it
-      int32_t w[kSgMaxSps / 2];
-      int kci[kSgMaxSps / 2];
-      bool valid[kSgMaxSps / 2];
+
+  // this lane's box of a stage (up to two issue rounds of two sub-steps):
+  // its coordinate word and its meta byte
+  struct Words {
+    int32_t w[kSgMaxSps / 2];
+    uint32_t meta[kSgMaxSps / 2];
+    int kci[kSgMaxSps / 2];
+    int n_sub;
+  };
+  auto fetch = [&](const SgCursor& c, Words* W) {
+    W->n_sub = min(sps, c.total_sub - c.ls * sps);
 #pragma unroll
-      for (int r = 0; r < kSgMaxSps / 2; ++r) {
-        const int sub = 2 * r + my_sub;
-        valid[r] = lane < 24 && sub < n_sub && (is_a || my_idx < nseg);
-        const int fs = ls * sps + sub;
-        const int step = fs / nkc;
-        kci[r] = fs - step * nkc;
-        w[r] = valid[r] ? __ldg(step_words + static_cast<int64_t>(step_begin + step) * kStepWords + my_word) : -1;
-      }
-      ok = __all_sync(0xffffffffu, mbar_wait_bounded(baddr(&hdr->empty[slot]), phase ^ 1u, ctl,
-                                                     ST_TIMEOUT_PRODUCER));
-      if (!ok) break;
-      const uint32_t sb = stage0 + static_cast<uint32_t>(slot) * p.stage_bytes;
-      const uint32_t full = baddr(&hdr->full[slot]);
-      mbar_arrive_expect_tx_pred(full, static_cast<uint32_t>(n_sub) * (a_all + nseg * seg_bytes), lane == 0);
-#pragma unroll
-      for (int r = 0; r < kSgMaxSps / 2; ++r) {
-        if (2 * r >= n_sub) break;  // warp-uniform
-        const uint32_t dst = sb + static_cast<uint32_t>(2 * r + my_sub) * p.sub_bytes + my_off;
-        // entries: A rows (slab of block a) at k-offset kci*kc; absent -> rows -32..-1
-        tma_load_2d_pred(dst, &p.tm_a, kci[r] * kc, w[r] >= 0 ? w[r] : -32, full, valid[r] && is_a);
-        // segments: B rows of block b at k-offset kci*kc, columns seg_x..+31
-        tma_load_2d_pred(dst, &p.tm_b, seg_x, w[r] >= 0 ? w[r] + kci[r] * kc : -kc, full,
-                         valid[r] && !is_a);
-      }
-      armed |= 1u << slot;
-      armed_parity = (armed_parity & ~(1u << slot)) | (phase << slot);
+    for (int r = 0; r < kSgMaxSps / 2; ++r) {
+      const int sub = 2 * r + my_sub;
+      const bool in = lane < 24 && sub < W->n_sub;
+      const int fs = c.ls * sps + sub;
+      const int step = fs / p.nkc;
+      W->kci[r] = fs - step * p.nkc;
+      const int64_t rec = static_cast<int64_t>(c.step_begin + step) * kStepWords;
+      W->w[r] = in ? __ldg(step_words + rec + my_word) : 0;
+      W->meta[r] = in ? __ldg(reinterpret_cast<const uint8_t*>(step_words + rec) + my_meta) : 0u;
     }
-    seq += ns;
+  };
+
+  SgCursor cur{u_begin, 0, 0, 0, 0, 0, 0};
+  if (cur.u < u_end) {
+    sg_load_unit(p, &cur, my_idx);
+    // first owned stage: pw (stages are numbered from 0 across the CTA's units)
+    cur.ls = pw - P;
+    sg_advance(p, &cur, u_end, P, my_idx);
+  }
+  Words wc;
+  if (cur.u < u_end) fetch(cur, &wc);
+#pragma unroll 1
+  while (cur.u < u_end) {
+    SgCursor nxt = cur;
+    sg_advance(p, &nxt, u_end, P, my_idx);
+    Words wn;
+    if (nxt.u < u_end) fetch(nxt, &wn);
+    const int64_t gs = cur.seq + cur.ls;
+    const int slot = static_cast<int>(gs % p.stages);
+    const uint32_t phase = static_cast<uint32_t>((gs / p.stages) & 1);
+    const bool ok = __all_sync(0xffffffffu, mbar_wait_bounded(baddr(&hdr->empty[slot]), phase ^ 1u, ctl,
+                                                              ST_TIMEOUT_PRODUCER));
+    if (!ok) break;
+    const uint32_t sb = stage0 + static_cast<uint32_t>(slot) * p.stage_bytes;
+    const uint32_t full = baddr(&hdr->full[slot]);
+    mbar_arrive_expect_tx_pred(full, static_cast<uint32_t>(wc.n_sub) * (a_all + cur.nseg * seg_bytes),
+                               lane == 0);
+#pragma unroll
+    for (int r = 0; r < kSgMaxSps / 2; ++r) {
+      if (2 * r >= wc.n_sub) break;  // warp-uniform
+      const uint32_t m = wc.meta[r];
+      const bool valid = (m & kSpgemmBoxValid) != 0;
+      const uint32_t first = m & 7u, lg = (m >> 3) & 3u;
+      const uint32_t sub_base = sb + static_cast<uint32_t>(2 * r + my_sub) * p.sub_bytes;
+      // entries: rows of A (slabs of blocks) at k-offset kci*kc, 32 << lg rows
+      tma_load_2d_pred(sub_base + first * a_slot, &p.tm_a[min(lg, 2u)], wc.kci[r] * kc,
+                       wc.w[r], full, valid && is_a);
+      // segments: slice t of 1 << lg consecutive blocks of B at k-offset kci*kc
+      tma_load_3d_pred(sub_base + a_all + first * seg_bytes, &p.tm_b[lg], static_cast<int32_t>((m >> 5) & 3u) * 32,
+                       wc.kci[r] * kc, wc.w[r], full, valid && !is_a);
+    }
+    armed |= 1u << slot;
+    armed_parity = (armed_parity & ~(1u << slot)) | (phase << slot);
+    cur = nxt;
+    wc = wn;
   }
   if (lane == 0) {
 #pragma unroll 1
@@ -299,8 +345,8 @@ __global__ void __launch_bounds__(kSgThreads, 1) spgemm_tcgen05(const __grid_con
     mbar_init(baddr(&hdr->drain), 1);
     hdr->abort_flag = 0;
     fence_mbar_init();
-    tma_prefetch_desc(&p.tm_a);
-    tma_prefetch_desc(&p.tm_b);
+    tma_prefetch_desc(&p.tm_a[0]);
+    tma_prefetch_desc(&p.tm_b[0]);
   }
   if (warp == kSgMmaWarp) {
     tmem_alloc(smem_u32(&hdr->tmem_base), static_cast<uint32_t>(p.tmem_cols));
@@ -346,12 +392,21 @@ bsp_status launch_spgemm(const bsp_spgemm_plan* p, const void* a_vals, const voi
   SpgemmKernelParams kp;
   memset(&kp, 0, sizeof(kp));
   const CUtensorMapSwizzle a_swz = p->kc == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
-  bsp_status st = encode_2d(dev, &kp.tm_a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a_vals, p->Ca,
-                            static_cast<uint64_t>(p->nnzb_a) * p->Ra, p->Ca, p->kc, 32, a_swz);
-  if (st != BSP_OK) return st;
-  st = encode_2d(dev, &kp.tm_b, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, b_vals, p->Cb,
-                 static_cast<uint64_t>(p->nnzb_b) * p->Ca, p->Cb, 32, p->kc, CU_TENSOR_MAP_SWIZZLE_64B);
-  if (st != BSP_OK) return st;
+  // one map per box size; sizes larger than the tensor are never used
+  for (int l = 0; l <= p->la_log2; ++l) {
+    bsp_status st = encode_2d(dev, &kp.tm_a[l], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a_vals, p->Ca,
+                              static_cast<uint64_t>(p->nnzb_a) * p->Ra, p->Ca, p->kc, 32u << l, a_swz);
+    if (st != BSP_OK) return st;
+  }
+  for (int l = 0; l <= p->lb_log2; ++l) {
+    const uint64_t dims[3] = {static_cast<uint64_t>(p->Cb), static_cast<uint64_t>(p->Ca),
+                              static_cast<uint64_t>(p->nnzb_b)};
+    const uint64_t strides[2] = {static_cast<uint64_t>(p->Cb) * 2, static_cast<uint64_t>(p->Ca) * p->Cb * 2};
+    const uint32_t box[3] = {32, static_cast<uint32_t>(p->kc), 1u << l};
+    bsp_status st = encode_nd(dev, &kp.tm_b[l], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, b_vals, dims, strides, box,
+                              CU_TENSOR_MAP_SWIZZLE_64B);
+    if (st != BSP_OK) return st;
+  }
   kp.units = p->d_units;
   kp.steps = p->d_steps;
   kp.cta_begin = p->d_cta_begin;

@@ -39,31 +39,67 @@ def dense(rp, ci, vals, R, C, H, W):
 
 
 def emulate(plan, Ra, Ca, Cb, av, bv, nnzb_out):
-    """Run the schedule the way the kernel does (float64)."""
+    """Run the schedule the way the kernel does (float64): every step's TMA
+    boxes fill the entry and segment slots (zero boxes for absent data), the
+    MMA accumulates, the epilogue writes the tiles of existing blocks."""
     a2 = av.reshape(-1, Ca)
-    b2 = bv.reshape(-1, Cb)
+    b3 = bv.reshape(-1, Ca, Cb)
     nseg_max = plan["nseg_max"]
     out = np.full((nnzb_out, Ra, Cb), np.nan)
     written = np.zeros((nnzb_out, Ra, Cb), np.int32)
     steps = plan["step_table"]
     cta = plan["cta_begin"]
     assert cta[0] == 0 and cta[-1] == plan["units"] and np.all(np.diff(cta) >= 0)
+    n_boxes = 0
     for u in plan["unit_table"]:
         sb, ns, n_ent, nseg = u[:4]
         seg_x, ent_r, out_blk = u[4:12], u[12:16], u[16:48].reshape(4, 8)
         assert ns >= 1 and 1 <= n_ent <= 4 and 1 <= nseg <= nseg_max
         D = np.zeros((128, 32 * nseg_max))
         for st in steps[sb:sb + ns]:
-            A = np.zeros((128, Ca))
-            B = np.zeros((Ca, 32 * nseg_max))
-            for e in range(4):
-                if st[e] >= 0:
-                    assert e < n_ent
-                    A[32 * e:32 * e + 32] = a2[st[e]:st[e] + 32]
-            for s in range(8):
-                if st[4 + s] >= 0:
-                    assert s < nseg
-                    B[:, 32 * s:32 * s + 32] = b2[st[4 + s]:st[4 + s] + Ca, seg_x[s]:seg_x[s] + 32]
+            meta = st[12:16].copy().view(np.uint8)
+            a_meta, b_meta = meta[0:4], meta[4:12]
+            A = np.full((128, Ca), np.nan)
+            B = np.full((Ca, 32 * nseg_max), np.nan)
+            cover_a = np.zeros(4, np.int32)
+            cover_b = np.zeros(8, np.int32)
+            for i in range(4):
+                m = int(a_meta[i])
+                if not m & 0x80:
+                    continue
+                n_boxes += 1
+                e0, L = m & 7, 1 << ((m >> 3) & 3)
+                y = st[i]
+                assert e0 + L <= 4 and L <= 4
+                cover_a[e0:e0 + L] += 1
+                if y >= 0:
+                    assert y + 32 * L <= a2.shape[0]
+                    A[32 * e0:32 * (e0 + L)] = a2[y:y + 32 * L]
+                else:
+                    assert y == -32 * L
+                    A[32 * e0:32 * (e0 + L)] = 0
+            for i in range(8):
+                m = int(b_meta[i])
+                if not m & 0x80:
+                    continue
+                n_boxes += 1
+                s0, L, t = m & 7, 1 << ((m >> 3) & 3), (m >> 5) & 3
+                z = st[4 + i]
+                assert s0 + L <= nseg
+                cover_b[s0:s0 + L] += 1
+                for q in range(L):
+                    if z >= 0:
+                        assert z + L <= b3.shape[0]
+                        assert seg_x[s0 + q] == 32 * t
+                        B[:, 32 * (s0 + q):32 * (s0 + q + 1)] = b3[z + q, :, 32 * t:32 * t + 32]
+                    else:
+                        assert z == -L
+                        B[:, 32 * (s0 + q):32 * (s0 + q + 1)] = 0
+            assert np.all(cover_a == 1), "every entry slot filled by exactly one box"
+            assert np.all(cover_b[:nseg] == 1) and np.all(cover_b[nseg:] == 0)
+            # rows of inactive entries / columns of unused segments stay out of the result
+            A[np.isnan(A)] = 0
+            B[:, 32 * nseg:] = 0
             D += A @ B
         for e in range(4):
             for s in range(8):
@@ -74,6 +110,7 @@ def emulate(plan, Ra, Ca, Cb, av, bv, nnzb_out):
                 out[blk, ent_r[e]:ent_r[e] + 32, seg_x[s]:seg_x[s] + 32] = D[32 * e:32 * e + 32, 32 * s:32 * s + 32]
                 written[blk, ent_r[e]:ent_r[e] + 32, seg_x[s]:seg_x[s] + 32] += 1
     assert np.all(written == 1), "every output element written exactly once"
+    assert n_boxes == plan["boxes"]
     return out
 
 
@@ -106,15 +143,16 @@ def test_schedule_emulates_product(Ra, Ca, Cb):
     assert plan["kc"] == (32 if Ca == 32 else 64)
 
 
-@pytest.mark.parametrize("opts", [dict(n_tiles=1), dict(steps_per_stage=1), dict(steps_per_stage=4),
-                                  dict(no_load_balance=1), dict(max_ctas=3), dict(producers=1)])
+@pytest.mark.parametrize("opts", [dict(n_tiles=1), dict(n_tiles=2), dict(steps_per_stage=1),
+                                  dict(steps_per_stage=4), dict(no_load_balance=1),
+                                  dict(no_load_balance=2), dict(max_ctas=3), dict(producers=1)])
 def test_schedule_options(opts):
     rng = np.random.default_rng(11)
     arp, aci = rand_pattern(rng, 14, 10, 0.35)
     brp, bci = rand_pattern(rng, 10, 12, 0.35)
     plan = check_case(rng, 14 * 32, 10 * 32, 12 * 32, 32, 32, 32, arp, aci, brp, bci, **opts)
     if "n_tiles" in opts:
-        assert plan["nseg_max"] == 4
+        assert plan["nseg_max"] == 4 * opts["n_tiles"]
     if "max_ctas" in opts:
         assert plan["ctas"] <= 3
     assert plan["stages"] % plan["producers"] == 0
@@ -160,7 +198,9 @@ def test_unit_shape_banded():
     rows = [[c for c in range(max(0, i - 2), min(n, i + 3))] for i in range(n)]
     rp = np.concatenate([[0], np.cumsum([len(r) for r in rows])]).astype(np.int32)
     ci = np.array([c for r in rows for c in r], np.int32)
-    plan = bsp.inspect_spgemm_plan(n * 32, n * 32, n * 32, 32, 32, 32, rp, ci, rp, ci)
+    plan = bsp.inspect_spgemm_plan(n * 32, n * 32, n * 32, 32, 32, 32, rp, ci, rp, ci,
+                                   opts=bsp.make_opts(n_tiles=2))
+    assert plan["nseg_max"] == 8
     u = plan["unit_table"]
     assert np.all(u[:, 2] == 4)
     # an interior group of 4 rows covers 12 output columns (one unit of 8 and
@@ -168,6 +208,8 @@ def test_unit_shape_banded():
     assert plan["units"] == 2 * (n // 4) - 2
     # each unit's steps: k in the union of its rows' bands that reach its columns
     assert plan["steps"] <= plan["units"] * 8
+    # consecutive stored blocks of a row of B merge: far fewer than 12 boxes a step
+    assert plan["boxes"] < 7 * plan["steps"]
 
 
 def test_bad_arguments():
@@ -179,3 +221,19 @@ def test_bad_arguments():
         bsp.inspect_spgemm_plan(32, 32, 40, 32, 32, 32, rp, ci, rp, ci)  # N % Cb
     with pytest.raises(bsp.BspError):
         bsp.inspect_spgemm_plan(32, 32, 32, 32, 32, 32, rp, np.array([3], np.int32), rp, ci)
+
+
+def test_unit_width_choice():
+    """Sparse random products get 4-segment units (N = 128) when those move
+    fewer operand bytes; wide bands keep 8 (N = 256)."""
+    rng = np.random.default_rng(21)
+    arp, aci = rand_pattern(rng, 256, 256, 0.03)
+    brp, bci = rand_pattern(rng, 256, 256, 0.03)
+    p = bsp.inspect_spgemm_plan(256 * 32, 256 * 32, 256 * 32, 32, 32, 32, arp, aci, brp, bci)
+    assert p["nseg_max"] == 4
+    n = 128
+    rows = [list(range(max(0, i - 16), min(n, i + 17))) for i in range(n)]
+    rp = np.concatenate([[0], np.cumsum([len(r) for r in rows])]).astype(np.int32)
+    ci = np.array([c for r in rows for c in r], np.int32)
+    p = bsp.inspect_spgemm_plan(n * 32, n * 32, n * 32, 32, 32, 32, rp, ci, rp, ci)
+    assert p["nseg_max"] == 8

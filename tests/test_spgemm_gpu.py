@@ -73,8 +73,9 @@ def test_spgemm_block_sizes(Ra, Ca, Cb):
                   rand_vals(rng, aci.size * Ra * Ca), brp, bci, rand_vals(rng, bci.size * Ca * Cb))
 
 
-@pytest.mark.parametrize("opts", [dict(n_tiles=1), dict(steps_per_stage=1), dict(steps_per_stage=4),
-                                  dict(producers=1), dict(max_ctas=5), dict(no_load_balance=1)])
+@pytest.mark.parametrize("opts", [dict(n_tiles=1), dict(n_tiles=2), dict(steps_per_stage=1),
+                                  dict(steps_per_stage=4), dict(producers=1), dict(max_ctas=5),
+                                  dict(no_load_balance=1), dict(no_load_balance=2)])
 def test_spgemm_options(opts):
     import bsp
 
@@ -218,3 +219,19 @@ def test_spgemm_banded_full_size_properties():
     g = oracle.spgemm_bf16(sub_rp, sub_ci, sub_av, 32, 32, rp, ci, bv, 32, n)
     assert np.array_equal(oci[orp[r0]:orp[r1]], g[1])
     assert_bf16_close(out[orp[r0] * 1024:orp[r1] * 1024], g[2], what="banded slab")
+
+
+def test_spgemm_c_abi_host_entry():
+    """bsp_spgemm_host (size query, then the product, with launch timing)."""
+    import bsp
+
+    rng = np.random.default_rng(31)
+    arp, aci = rand_pattern(rng, 30, 20, 0.2)
+    brp, bci = rand_pattern(rng, 20, 25, 0.2)
+    av, bv = rand_vals(rng, aci.size * 2048), rand_vals(rng, bci.size * 2048)
+    orp, oci, out, ms = bsp.spgemm_host_c(30 * 64, 20 * 32, 25 * 64, 64, 32, 64, arp, aci, av, brp, bci,
+                                          bv, iters=3)
+    gold = oracle.spgemm_bf16(arp, aci, av, 64, 32, brp, bci, bv, 64, 25)
+    assert np.array_equal(orp, gold[0]) and np.array_equal(oci, gold[1])
+    assert_bf16_close(out, gold[2], what="C ABI host entry")
+    assert ms > 0

@@ -313,6 +313,38 @@ bsp_status bsp_spgemm_host(bsp_device* dev, int64_t M, int64_t K, int64_t N, int
                            int32_t* out_row_ptr, int32_t* out_col_idx, uint16_t* out_values,
                            const bsp_spmm_opts* opts, int32_t iters, double* ms_per_launch);
 
+/* ---- fused block-sparse attention step (one head) ------------------------
+ * O = softmax_rows(scale * Q K^T on the mask's blocks) V: the chain of the
+ * reference's SDDMM (block_sddmm/inc/host_code.hpp:104-115, golden
+ * bsr_matrix::sddmm, sparse_common/bsr_matrix.hpp:816-857), a row softmax over
+ * each row's stored positions, and its SpMM (block_spmm/inc/host_code.hpp:
+ * 165-177, golden spmm_bfloat16, bsr_matrix.hpp:692-736), fused so that the
+ * probabilities never reach DRAM.  The reference has no fused form (config 4
+ * of its benchmark runs the two programs back to back).
+ * mask: S x S pattern with 32 x 32 blocks (values ignored; a column repeated
+ * in a row counts once).  Q, K, V: [S, d] row-major bf16 with leading
+ * dimensions ldq, ldk, ldv (K is not transposed), d = 64 or 128.  O: [S, d]
+ * bf16, ldo; rows of block-rows without mask blocks are written as 0.
+ * Softmax in fp32 with exp2 of scale * log2(e) * S; P is rounded to bf16 for
+ * the P V product; O is accumulated in fp32 and rounded once. */
+typedef struct bsp_attn_plan bsp_attn_plan;
+
+bsp_status bsp_attn_plan_create(bsp_device* dev, const bsp_bsr_desc* mask, const int32_t* host_row_ptr,
+                                const int32_t* host_col_idx, int64_t d, const bsp_spmm_opts* opts,
+                                bsp_attn_plan** out);
+bsp_status bsp_attn_execute(const bsp_attn_plan* plan, const void* Q, int64_t ldq, const void* K,
+                            int64_t ldk, const void* V, int64_t ldv, float scale, void* O,
+                            int64_t ldo, void* stream);
+bsp_status bsp_attn_plan_destroy(bsp_attn_plan* plan);
+/* info[0] units, [1] grid, [2] chunks, [3] mask blocks (distinct), [4] S,
+ * [5] d, [8] table bytes, [9] shared memory, [10] TMEM columns. */
+bsp_status bsp_attn_plan_info(const bsp_attn_plan* plan, int64_t info[16]);
+
+/* Host-buffer form: mask pattern, Q, K, V, O all host arrays ([S, d] dense). */
+bsp_status bsp_attn_host(bsp_device* dev, int64_t S, int64_t d, int64_t nnzb, const int32_t* row_ptr,
+                         const int32_t* col_idx, const uint16_t* Q, const uint16_t* K,
+                         const uint16_t* V, float scale, uint16_t* O, const bsp_spmm_opts* opts);
+
 /* ---- multi-GPU helpers (host logic; the exchange itself is NCCL) --------
  * Contiguous block-row ranges for `parts` GPUs balanced by nonzero-block
  * count (a generalisation of the reference's serpentine balancer,

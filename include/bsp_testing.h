@@ -57,6 +57,16 @@ bsp_status bsp_spgemm_plan_inspect(int64_t M, int64_t K, int64_t N, int32_t Ra, 
                                    int64_t info[16], int32_t* out_row_ptr, int32_t* out_col_idx,
                                    int32_t* units_out, int32_t* steps_out, int32_t* cta_begin_out);
 
+/* Attention planner (S x S mask with 32 x 32 blocks, head size d).
+ * info[16] as bsp_attn_plan_info; units_out[info[0] * 4] (row0, chunk_begin,
+ * n_chunks, pad per unit, in CTA order), chunks_out[info[2] * 8] (kb[4]:
+ * key block of each slot or -1, bits: bit 4 q + s set when block-row q of the
+ * unit holds slot s, pad[3]), cta_begin_out[info[1] + 1]. */
+bsp_status bsp_attn_plan_inspect(int64_t S, int64_t d, int64_t nnzb, const int32_t* row_ptr,
+                                 const int32_t* col_idx, const bsp_spmm_opts* opts, int32_t sm_count,
+                                 int32_t max_smem, int64_t info[16], int32_t* units_out,
+                                 int32_t* chunks_out, int32_t* cta_begin_out);
+
 #ifdef __cplusplus
 }
 #endif

@@ -159,6 +159,47 @@ def sddmm_f32(indptr, indices, mask_data, H, W, R, C, A, B, K):
     return out
 
 
+def attention_bf16(indptr, indices, S, d, Q, K, V, scale, rows=None):
+    """Block-sparse attention step, the reference chain with a row softmax
+    between its two goldens: Sc = sddmm(mask, Q, K^T) with T = float
+    (bsr_matrix.hpp:816-857), P = softmax over each row's stored positions of
+    scale * Sc (float64, then rounded once to bf16), O = spmm_bfloat16(P, V)
+    (bsr_matrix.hpp:692-736).  The mask (S x S, 32 x 32 blocks) is a pattern:
+    a column repeated in a row counts once.  Q, K, V: [S, d] bf16 bits.
+    Returns O [S, d] bf16 bits (rows of block-rows without blocks are 0).
+    ``rows`` = (r0, r1) restricts the work to those block-rows (others 0)."""
+    R = 32
+    rp = _c(indptr, np.int32)
+    ci = _c(indices, np.int32)
+    nbr = S // R
+    r0, r1 = rows if rows is not None else (0, nbr)
+    # the pattern as sets, rows outside [r0, r1) emptied
+    sets = [np.unique(ci[rp[i]:rp[i + 1]]) if r0 <= i < r1 else np.zeros(0, np.int32)
+            for i in range(nbr)]
+    urp = np.concatenate([[0], np.cumsum([len(x) for x in sets])]).astype(np.int32)
+    uci = (np.concatenate(sets) if urp[-1] else np.zeros(0, np.int32)).astype(np.int32)
+    nnzb = int(urp[-1])
+    O = np.zeros((S, d), dtype=np.uint16)
+    if nnzb == 0:
+        return O
+    Qf = bf16_to_f32(_c(Q, np.uint16)).reshape(S, d)
+    Kt = np.ascontiguousarray(bf16_to_f32(_c(K, np.uint16)).reshape(S, d).T)
+    ones = np.ones(nnzb * R * R, np.float32)
+    Sc = sddmm_f32(urp, uci, ones, S, S, R, R, Qf, Kt, d).reshape(nnzb, R, R)
+    P = np.zeros_like(Sc)
+    for i in range(r0, r1):
+        b0, b1 = urp[i], urp[i + 1]
+        if b0 == b1:
+            continue
+        x = Sc[b0:b1].transpose(1, 0, 2).reshape(R, -1).astype(np.float64) * scale
+        x -= x.max(axis=1, keepdims=True)
+        e = np.exp(x)
+        e /= e.sum(axis=1, keepdims=True)
+        P[b0:b1] = e.reshape(R, b1 - b0, R).transpose(1, 0, 2)
+    Pb = f32_to_bf16(P.astype(np.float32).ravel())
+    return spmm_bf16(urp, uci, Pb, S, S, R, R, _c(V, np.uint16).reshape(S, d), d)
+
+
 def serpentine(n: int, parts: int):
     """(owner, slot) per position of the heaviest-first permutation."""
     owner = np.zeros(n, dtype=np.int32)

@@ -34,6 +34,8 @@ EXPORTS = [
     "bsp_spmm_noalloc", "bsp_spmm_execute_replicated", "bsp_ipc_export", "bsp_ipc_import",
     "bsp_ipc_close", "bsp_spgemm_plan_create", "bsp_spgemm_pattern", "bsp_spgemm_execute",
     "bsp_spgemm_plan_destroy", "bsp_spgemm_plan_info", "bsp_spgemm_host", "bsp_spgemm_plan_inspect",
+    "bsp_attn_plan_create", "bsp_attn_execute", "bsp_attn_plan_destroy", "bsp_attn_plan_info",
+    "bsp_attn_host", "bsp_attn_plan_inspect",
 ]
 IPC_HANDLE_BYTES = 64
 
@@ -128,6 +130,13 @@ def lib():
                                 ctypes.POINTER(ctypes.c_double)]),
         "bsp_spgemm_plan_inspect": (S, [I64, I64, I64, I32, I32, I32, I64, P, P, I64, P, P,
                                         ctypes.POINTER(Opts), I32, I32, P, P, P, P, P, P]),
+        "bsp_attn_plan_create": (S, [P, ctypes.POINTER(BsrDesc), P, P, I64, ctypes.POINTER(Opts),
+                                     ctypes.POINTER(P)]),
+        "bsp_attn_execute": (S, [P, P, I64, P, I64, P, I64, ctypes.c_float, P, I64, P]),
+        "bsp_attn_plan_destroy": (S, [P]),
+        "bsp_attn_plan_info": (S, [P, ctypes.POINTER(I64)]),
+        "bsp_attn_host": (S, [P, I64, I64, I64, P, P, P, P, P, ctypes.c_float, P, ctypes.POINTER(Opts)]),
+        "bsp_attn_plan_inspect": (S, [I64, I64, I64, P, P, ctypes.POINTER(Opts), I32, I32, P, P, P, P]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -550,6 +559,95 @@ def inspect_spgemm_plan(M, K, N, Ra, Ca, Cb, a_row_ptr, a_col_idx, b_row_ptr, b_
     d.update(out_row_ptr=orp, out_col_idx=oci[:nb], unit_table=units[:nu], step_table=steps[:ns],
              cta_begin=cta)
     return d
+
+
+# --------------------------------------------------------------- attention --
+ATTN_INFO_KEYS = ["units", "ctas", "chunks", "mask_blocks", "S", "d", "_6", "_7", "plan_bytes",
+                  "smem_bytes", "tmem_cols"]
+
+
+class AttnPlan:
+    """Fused block-sparse attention step for one mask pattern and head size:
+    O = softmax_rows(scale * Q K^T on the mask's blocks) V (the reference's
+    SDDMM -> softmax -> SpMM chain in one kernel)."""
+
+    def __init__(self, dev: Device, mask: DeviceBSR, d: int, opts=None):
+        self.dev, self.d, self.S = dev, d, mask.rows
+        self._desc = mask.desc()
+        h = ctypes.c_void_p()
+        o = opts if opts is not None else Opts()
+        _check(lib().bsp_attn_plan_create(dev.handle, ctypes.byref(self._desc), _ptr(mask.h_row_ptr),
+                                          _ptr(mask.h_col_idx), d, ctypes.byref(o), ctypes.byref(h)))
+        self.handle = h
+
+    def info(self) -> dict:
+        arr = (ctypes.c_int64 * 16)()
+        _check(lib().bsp_attn_plan_info(self.handle, arr))
+        return {k: int(arr[i]) for i, k in enumerate(ATTN_INFO_KEYS) if not k.startswith("_")}
+
+    def execute(self, Q, K, V, O, scale=None, stream=None):
+        """Q, K, V, O: torch bf16 cuda [S, d] (row strides may exceed d)."""
+        sc = float(scale) if scale is not None else 1.0 / float(np.sqrt(self.d))
+        _check(lib().bsp_attn_execute(self.handle, _ptr(Q), Q.stride(0), _ptr(K), K.stride(0), _ptr(V),
+                                      V.stride(0), sc, _ptr(O), O.stride(0), _stream_ptr(stream)))
+
+    def close(self):
+        if self.handle:
+            lib().bsp_attn_plan_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def attention(mask: DeviceBSR, Q, K, V, scale=None, opts=None, dev: Device = None):
+    """One-shot fused attention step on device tensors; returns O."""
+    import torch
+
+    dev = dev or device(Q.device.index or 0)
+    O = torch.empty_like(Q)
+    plan = AttnPlan(dev, mask, Q.shape[1], opts)
+    plan.execute(Q, K, V, O, scale)
+    dev.synchronize()
+    plan.close()
+    return O
+
+
+def attn_host(S, d, row_ptr, col_idx, Q, K, V, scale=None, opts=None, dev: Device = None):
+    """Host arrays in (pattern, Q, K, V bf16 bits), host O out (bsp_attn_host)."""
+    dev = dev or device(0)
+    rp = np.ascontiguousarray(row_ptr, dtype=np.int32)
+    ci = np.ascontiguousarray(col_idx, dtype=np.int32)
+    q = np.ascontiguousarray(Q, dtype=np.uint16)
+    k = np.ascontiguousarray(K, dtype=np.uint16)
+    v = np.ascontiguousarray(V, dtype=np.uint16)
+    o = np.empty((S, d), dtype=np.uint16)
+    sc = float(scale) if scale is not None else 1.0 / float(np.sqrt(d))
+    opt = opts if opts is not None else Opts()
+    _check(lib().bsp_attn_host(dev.handle, S, d, int(rp[-1]), _ptr(rp), _ptr(ci), _ptr(q), _ptr(k), _ptr(v),
+                               sc, _ptr(o), ctypes.byref(opt)))
+    return o
+
+
+def inspect_attn_plan(S, d, row_ptr, col_idx, opts=None, sm_count=148, max_smem=232448):
+    """Run the attention planner on the host only (no GPU)."""
+    rp = np.ascontiguousarray(row_ptr, dtype=np.int32)
+    ci = np.ascontiguousarray(col_idx, dtype=np.int32)
+    ci = ci if ci.size else np.zeros(1, np.int32)
+    info = np.zeros(16, np.int64)
+    o = opts if opts is not None else Opts()
+    args = (S, d, int(rp[-1]), _ptr(rp), _ptr(ci), ctypes.byref(o), sm_count, max_smem, _ptr(info))
+    _check(lib().bsp_attn_plan_inspect(*args, None, None, None))
+    units = np.zeros((max(int(info[0]), 1), 4), np.int32)
+    chunks = np.zeros((max(int(info[2]), 1), 8), np.int32)
+    cta = np.zeros(int(info[1]) + 1, np.int32)
+    _check(lib().bsp_attn_plan_inspect(*args, _ptr(units), _ptr(chunks), _ptr(cta)))
+    dd = {k: int(info[i]) for i, k in enumerate(ATTN_INFO_KEYS) if not k.startswith("_")}
+    dd.update(unit_table=units[: int(info[0])], chunk_table=chunks[: int(info[2])], cta_begin=cta)
+    return dd
 
 
 # ----------------------------------------------------------------- helpers --

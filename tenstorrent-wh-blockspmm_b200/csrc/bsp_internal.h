@@ -196,6 +196,44 @@ struct SpgemmKernelParams {
   int32_t tmem_cols, nseg_max, nprod;
 };
 
+// ---- fused attention step schedule -------------------------------------------
+// O = softmax_rows(scale * Q K^T on the mask's blocks) V for one head.  A work
+// unit is 128 query rows (four 32-row block-rows: MMA M); its key blocks are
+// the union of those block-rows' mask columns, taken four at a time
+// ("chunks": 128 keys = MMA N of S = Q K^T and MMA K of O += P V).  bits says
+// which (block-row, key block) pairs of the chunk the mask holds; the others
+// are masked to -inf before the softmax.
+constexpr int kAttnSlots = 4;
+struct AttnUnit {
+  int32_t row0;          // first query row (multiple of 128)
+  int32_t chunk_begin;   // first chunk record
+  int32_t n_chunks;      // 0: no block-row of the unit holds a mask block (O rows = 0)
+  int32_t pad;
+};
+static_assert(sizeof(AttnUnit) == 16, "unit layout");
+struct AttnChunk {
+  int32_t kb[kAttnSlots];  // key block of each slot, -1 none (zero box)
+  uint32_t bits;           // bit 4 q + s: block-row q of the unit holds key block kb[s]
+  int32_t pad[3];
+};
+static_assert(sizeof(AttnChunk) == 32, "chunk layout");
+
+struct AttnKernelParams {
+  CUtensorMap tm_q;  // Q [S, d], box {64, 128}, 128B swizzle
+  CUtensorMap tm_k;  // K [S, d], box {64, 32}
+  CUtensorMap tm_v;  // V [S, d], box {64, 32}
+  const AttnUnit* units;
+  const AttnChunk* chunks;
+  const int32_t* cta_begin;
+  uint16_t* o;
+  int64_t ldo;
+  unsigned int* status;
+  uint64_t timeout_ns;
+  int32_t S, d;
+  float scale_log2;      // softmax scale * log2(e)
+  int32_t tmem_cols;
+};
+
 // ---- host objects -------------------------------------------------------------
 typedef CUresult (*PFN_encodeTiled)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
                                     const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
@@ -237,6 +275,23 @@ struct bsp_spgemm_plan {
   std::vector<int32_t> out_row_ptr, out_col_idx;
   std::vector<bsp::SpgemmUnit> h_units;
   std::vector<bsp::SpgemmStep> h_steps;
+  std::vector<int32_t> h_cta_begin;
+};
+
+struct bsp_attn_plan {
+  bsp_device* dev = nullptr;
+  int64_t S = 0, d = 0, nnzb = 0;
+  int64_t mask_blocks = 0;   // distinct (block-row, key block) pairs (useful work)
+  int32_t grid = 0, smem_bytes = 0, tmem_cols = 0;
+  int64_t n_units = 0, n_chunks = 0;
+  uint64_t timeout_ns = 0;
+  void* d_blob = nullptr;
+  size_t blob_bytes = 0;
+  bsp::AttnUnit* d_units = nullptr;
+  bsp::AttnChunk* d_chunks = nullptr;
+  int32_t* d_cta_begin = nullptr;
+  std::vector<bsp::AttnUnit> h_units;
+  std::vector<bsp::AttnChunk> h_chunks;
   std::vector<int32_t> h_cta_begin;
 };
 
@@ -347,6 +402,12 @@ bsp_status launch_spgemm(const bsp_spgemm_plan* p, const void* a_vals, const voi
                          void* out_vals, cudaStream_t stream);
 int spgemm_max_stages();
 int spgemm_max_producers();
+bsp_status plan_attn_host(bsp_attn_plan* p, const int32_t* row_ptr, const int32_t* col_idx,
+                          int sm_count, int max_smem, const bsp_spmm_opts* opts);
+bsp_status launch_attn(const bsp_attn_plan* p, const void* Q, int64_t ldq, const void* K, int64_t ldk,
+                       const void* V, int64_t ldv, float scale, void* O, int64_t ldo,
+                       cudaStream_t stream);
+int attn_smem_bytes(int d);
 bsp_status plan_spmm_rowstack(bsp_spmm_plan* p, const int32_t* row_ptr, const int32_t* col_idx,
                               int sm_count, int max_smem, const bsp_spmm_opts* opts);
 }  // namespace bsp

@@ -916,6 +916,115 @@ bsp_status bsp_spgemm_host(bsp_device* dev, int64_t M, int64_t K, int64_t N, int
   return s;
 }
 
+// ----------------------------------------------------------- attention ----
+bsp_status bsp_attn_plan_create(bsp_device* dev, const bsp_bsr_desc* mask, const int32_t* host_row_ptr,
+                                const int32_t* host_col_idx, int64_t d, const bsp_spmm_opts* opts,
+                                bsp_attn_plan** out) {
+  if (!dev || !out) return set_error(BSP_ERR_INVALID_ARG, "null argument");
+  *out = nullptr;
+  bsp_status s = check_desc(mask, false);
+  if (s != BSP_OK) return s;
+  if (mask->R != 32 || mask->C != 32 || mask->rows != mask->cols)
+    return set_error(BSP_ERR_INVALID_ARG, "attention mask must be square with 32 x 32 blocks");
+  std::vector<int32_t> rp, ci;
+  const int32_t *prp = nullptr, *pci = nullptr;
+  s = host_pattern(mask, host_row_ptr, host_col_idx, &rp, &ci, &prp, &pci);
+  if (s != BSP_OK) return s;
+  bsp_attn_plan* p = new (std::nothrow) bsp_attn_plan();
+  if (!p) return set_error(BSP_ERR_ALLOC, "host allocation failed");
+  p->dev = dev;
+  p->S = mask->rows;
+  p->d = d;
+  p->nnzb = mask->nnzb;
+  s = plan_attn_host(p, prp, pci, dev->sm_count, dev->max_smem_optin, opts);
+  if (s != BSP_OK) {
+    delete p;
+    return s;
+  }
+  std::vector<void*> ptrs;
+  s = upload_blob({{p->h_units.data(), p->h_units.size() * sizeof(AttnUnit)},
+                   {p->h_chunks.data(), p->h_chunks.size() * sizeof(AttnChunk)},
+                   {p->h_cta_begin.data(), p->h_cta_begin.size() * sizeof(int32_t)}},
+                  &p->d_blob, &p->blob_bytes, &ptrs);
+  if (s != BSP_OK) {
+    delete p;
+    return s;
+  }
+  p->d_units = static_cast<AttnUnit*>(ptrs[0]);
+  p->d_chunks = static_cast<AttnChunk*>(ptrs[1]);
+  p->d_cta_begin = static_cast<int32_t*>(ptrs[2]);
+  *out = p;
+  return BSP_OK;
+}
+
+bsp_status bsp_attn_execute(const bsp_attn_plan* plan, const void* Q, int64_t ldq, const void* K,
+                            int64_t ldk, const void* V, int64_t ldv, float scale, void* O,
+                            int64_t ldo, void* stream) {
+  if (!plan || !Q || !K || !V || !O) return set_error(BSP_ERR_INVALID_ARG, "null argument");
+  if (ldq < plan->d || ldk < plan->d || ldv < plan->d || ldo < plan->d)
+    return set_error(BSP_ERR_INVALID_ARG, "leading dimensions must be >= d");
+  return launch_attn(plan, Q, ldq, K, ldk, V, ldv, scale, O, ldo, static_cast<cudaStream_t>(stream));
+}
+
+bsp_status bsp_attn_plan_destroy(bsp_attn_plan* plan) {
+  if (!plan) return BSP_OK;
+  if (plan->d_blob) cudaFree(plan->d_blob);
+  delete plan;
+  return BSP_OK;
+}
+
+bsp_status bsp_attn_plan_info(const bsp_attn_plan* p, int64_t info[16]) {
+  if (!p || !info) return set_error(BSP_ERR_INVALID_ARG, "null argument");
+  memset(info, 0, sizeof(int64_t) * 16);
+  info[0] = p->n_units;
+  info[1] = p->grid;
+  info[2] = p->n_chunks;
+  info[3] = p->mask_blocks;
+  info[4] = p->S;
+  info[5] = p->d;
+  info[8] = static_cast<int64_t>(p->blob_bytes);
+  info[9] = p->smem_bytes;
+  info[10] = p->tmem_cols;
+  return BSP_OK;
+}
+
+bsp_status bsp_attn_host(bsp_device* dev, int64_t S, int64_t d, int64_t nnzb, const int32_t* row_ptr,
+                         const int32_t* col_idx, const uint16_t* Q, const uint16_t* K,
+                         const uint16_t* V, float scale, uint16_t* O, const bsp_spmm_opts* opts) {
+  if (!dev || !row_ptr || !Q || !K || !V || !O || (nnzb > 0 && !col_idx))
+    return set_error(BSP_ERR_INVALID_ARG, "null argument");
+  if (S <= 0 || S % 32 || d <= 0) return set_error(BSP_ERR_INVALID_ARG, "bad dimensions");
+  const int64_t nbr = S / 32;
+  const size_t mat = sizeof(uint16_t) * S * d;
+  const size_t b_m = align256(mat);
+  const size_t b_rp = align256(sizeof(int32_t) * (nbr + 1));
+  const size_t b_ci = align256(sizeof(int32_t) * std::max<int64_t>(nnzb, 1));
+  bsp_status s = ws_reserve(dev, 4 * b_m + b_rp + b_ci);
+  if (s != BSP_OK) return s;
+  uint8_t* w = static_cast<uint8_t*>(dev->ws);
+  void *dQ = w, *dK = w + b_m, *dV = w + 2 * b_m, *dO = w + 3 * b_m;
+  int32_t* d_rp = reinterpret_cast<int32_t*>(w + 4 * b_m);
+  int32_t* d_ci = reinterpret_cast<int32_t*>(w + 4 * b_m + b_rp);
+  cudaStream_t stream = nullptr;
+  struct Cp { void* d; const void* h; size_t n; const char* what; };
+  const Cp cps[] = {{dQ, Q, mat, "H2D Q"}, {dK, K, mat, "H2D K"}, {dV, V, mat, "H2D V"},
+                    {d_rp, row_ptr, sizeof(int32_t) * (nbr + 1), "H2D row_ptr"},
+                    {d_ci, col_idx, sizeof(int32_t) * nnzb, "H2D col_idx"}};
+  for (const Cp& c : cps)
+    if (c.n > 0 && (s = cuda_check(cudaMemcpyAsync(c.d, c.h, c.n, cudaMemcpyHostToDevice, stream), c.what)) != BSP_OK)
+      return s;
+  const bsp_bsr_desc mask{S, S, 32, 32, nnzb, d_rp, d_ci, nullptr};
+  bsp_attn_plan* p = nullptr;
+  s = bsp_attn_plan_create(dev, &mask, row_ptr, col_idx, d, opts, &p);
+  if (s != BSP_OK) return s;
+  s = bsp_attn_execute(p, dQ, d, dK, d, dV, d, scale, dO, d, stream);
+  if (s == BSP_OK) s = cuda_check(cudaMemcpyAsync(O, dO, mat, cudaMemcpyDeviceToHost, stream), "D2H O");
+  if (s == BSP_OK) s = cuda_check(cudaStreamSynchronize(stream), "sync");
+  bsp_attn_plan_destroy(p);
+  if (s == BSP_OK) s = bsp_device_synchronize(dev);
+  return s;
+}
+
 // ----------------------------------------------------------- helpers ----
 bsp_status bsp_partition_rows(const int32_t* row_ptr, int64_t n_block_rows, int32_t parts,
                               int64_t* bounds) {
@@ -1045,6 +1154,25 @@ bsp_status bsp_spgemm_plan_inspect(int64_t M, int64_t K, int64_t N, int32_t Ra, 
     memcpy(out_col_idx, p.out_col_idx.data(), p.out_col_idx.size() * sizeof(int32_t));
   if (units_out && !p.h_units.empty()) memcpy(units_out, p.h_units.data(), p.h_units.size() * sizeof(SpgemmUnit));
   if (steps_out && !p.h_steps.empty()) memcpy(steps_out, p.h_steps.data(), p.h_steps.size() * sizeof(SpgemmStep));
+  if (cta_begin_out) memcpy(cta_begin_out, p.h_cta_begin.data(), p.h_cta_begin.size() * sizeof(int32_t));
+  return BSP_OK;
+}
+
+bsp_status bsp_attn_plan_inspect(int64_t S, int64_t d, int64_t nnzb, const int32_t* row_ptr,
+                                 const int32_t* col_idx, const bsp_spmm_opts* opts, int32_t sm_count,
+                                 int32_t max_smem, int64_t info[16], int32_t* units_out,
+                                 int32_t* chunks_out, int32_t* cta_begin_out) {
+  if (!row_ptr || !info || (nnzb > 0 && !col_idx)) return set_error(BSP_ERR_INVALID_ARG, "bad arguments");
+  bsp_attn_plan p;
+  p.S = S;
+  p.d = d;
+  p.nnzb = nnzb;
+  bsp_status s = plan_attn_host(&p, row_ptr, col_idx, sm_count, max_smem, opts);
+  if (s != BSP_OK) return s;
+  bsp_attn_plan_info(&p, info);
+  if (units_out && !p.h_units.empty()) memcpy(units_out, p.h_units.data(), p.h_units.size() * sizeof(AttnUnit));
+  if (chunks_out && !p.h_chunks.empty())
+    memcpy(chunks_out, p.h_chunks.data(), p.h_chunks.size() * sizeof(AttnChunk));
   if (cta_begin_out) memcpy(cta_begin_out, p.h_cta_begin.data(), p.h_cta_begin.size() * sizeof(int32_t));
   return BSP_OK;
 }

@@ -1332,4 +1332,90 @@ bsp_status plan_spgemm_host(bsp_spgemm_plan* p, const int32_t* a_rp, const int32
   return BSP_OK;
 }
 
+// Fused attention schedule: query rows in units of 128 (four block-rows of
+// the 32 x 32 mask); per unit the sorted union of its block-rows' mask
+// columns (a column repeated within a row counts once) cut into chunks of four
+// key blocks, each with the bits of the (block-row, key block) pairs the mask
+// holds.  Units are dealt in order to the least-loaded CTA.
+bsp_status plan_attn_host(bsp_attn_plan* p, const int32_t* row_ptr, const int32_t* col_idx,
+                          int sm_count, int max_smem, const bsp_spmm_opts* opts) {
+  bsp_spmm_opts o;
+  memset(&o, 0, sizeof(o));
+  if (opts) o = *opts;
+  const int64_t S = p->S;
+  if (p->d != 64 && p->d != 128) return set_error(BSP_ERR_UNSUPPORTED, "attention head size must be 64 or 128");
+  if (S <= 0 || S % 32 || S >= (int64_t(1) << 31))
+    return set_error(BSP_ERR_INVALID_ARG, "sequence length must be a positive multiple of 32");
+  const int64_t nbr = S / 32;
+  bsp_status st = check_pattern(row_ptr, col_idx, nbr, nbr, p->nnzb);
+  if (st != BSP_OK) return st;
+  if (attn_smem_bytes(static_cast<int>(p->d)) > max_smem)
+    return set_error(BSP_ERR_UNSUPPORTED, "not enough shared memory for the attention pipeline");
+  const int64_t ngroups = (nbr + 3) / 4;
+  p->h_units.clear();
+  p->h_chunks.clear();
+  p->mask_blocks = 0;
+  std::vector<int64_t> weight;
+  std::vector<int64_t> stamp(static_cast<size_t>(nbr), -1);
+  std::vector<int32_t> cols;
+  std::vector<std::vector<int32_t>> rowcols(4);
+  for (int64_t g = 0; g < ngroups; ++g) {
+    AttnUnit u;
+    memset(&u, 0, sizeof(u));
+    u.row0 = static_cast<int32_t>(g * 128);
+    u.chunk_begin = static_cast<int32_t>(p->h_chunks.size());
+    cols.clear();
+    for (int q = 0; q < 4; ++q) {
+      rowcols[q].clear();
+      const int64_t i = g * 4 + q;
+      if (i >= nbr) continue;
+      for (int32_t b = row_ptr[i]; b < row_ptr[i + 1]; ++b) rowcols[q].push_back(col_idx[b]);
+      std::sort(rowcols[q].begin(), rowcols[q].end());
+      rowcols[q].erase(std::unique(rowcols[q].begin(), rowcols[q].end()), rowcols[q].end());
+      p->mask_blocks += static_cast<int64_t>(rowcols[q].size());
+      for (int32_t c : rowcols[q])
+        if (stamp[c] != g) {
+          stamp[c] = g;
+          cols.push_back(c);
+        }
+    }
+    std::sort(cols.begin(), cols.end());
+    for (size_t c0 = 0; c0 < cols.size(); c0 += kAttnSlots) {
+      AttnChunk ch;
+      memset(&ch, 0, sizeof(ch));
+      for (int s_ = 0; s_ < kAttnSlots; ++s_) {
+        ch.kb[s_] = -1;
+        if (c0 + s_ >= cols.size()) continue;
+        const int32_t c = cols[c0 + s_];
+        ch.kb[s_] = c;
+        for (int q = 0; q < 4; ++q)
+          if (std::binary_search(rowcols[q].begin(), rowcols[q].end(), c)) ch.bits |= 1u << (4 * q + s_);
+      }
+      p->h_chunks.push_back(ch);
+    }
+    u.n_chunks = static_cast<int32_t>(p->h_chunks.size()) - u.chunk_begin;
+    p->h_units.push_back(u);
+    weight.push_back(static_cast<int64_t>(u.n_chunks) * 4 + 1);
+  }
+  p->n_units = static_cast<int64_t>(p->h_units.size());
+  p->n_chunks = static_cast<int64_t>(p->h_chunks.size());
+  int grid = o.max_ctas > 0 ? std::min(o.max_ctas, sm_count) : sm_count;
+  grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(grid, p->n_units)));
+  std::vector<std::vector<int32_t>> per;
+  if (o.no_load_balance == 1) contiguous_split(p->n_units, grid, &per);
+  else ordered_greedy(weight, grid, &per);
+  std::vector<AttnUnit> ordered;
+  p->h_cta_begin.assign(1, 0);
+  for (int c = 0; c < grid; ++c) {
+    for (int32_t idx : per[c]) ordered.push_back(p->h_units[idx]);
+    p->h_cta_begin.push_back(static_cast<int32_t>(ordered.size()));
+  }
+  p->h_units.swap(ordered);
+  p->grid = grid;
+  p->smem_bytes = attn_smem_bytes(static_cast<int>(p->d));
+  p->tmem_cols = 512;
+  p->timeout_ns = static_cast<uint64_t>(o.timeout_ms > 0 ? o.timeout_ms : 2000) * 1000000ull;
+  return BSP_OK;
+}
+
 }  // namespace bsp

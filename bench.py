@@ -61,6 +61,7 @@ METRICS = {
     "cfg3": "effective TFLOP/s (nnz blocks only), BSR SDDMM",
     "cfg4": "effective TFLOP/s (nnz blocks only), BSR SDDMM + SpMM attention pair",
     "cfg5": "effective TFLOP/s (nnz blocks only), multi-GPU BSR SpMM with C all-gather",
+    "attn": "effective TFLOP/s (nnz blocks only), fused SDDMM -> row softmax -> SpMM attention step",
     "spgemm": "effective TFLOP/s (stored block products only), BSR x BSR -> BSR SpGEMM",
     "spgemm_rand": "effective TFLOP/s (stored block products only), BSR x BSR -> BSR SpGEMM",
 }
@@ -71,6 +72,8 @@ WORKLOAD_DESC = {
     "cfg4": "BASELINE config 4: SDDMM Q K^T + SpMM P V, seq 16384, head 128, 32x32 blocks, band+global+Zipf mask",
     "cfg5": "BASELINE config 5: BSR SpMM 65536x65536 (64x64 blocks, Zipf(1.1) rows, 1% mean) x 65536x8192, "
             "row panels sharded by nnz blocks + NCCL exchange of C",
+    "attn": "BASELINE config 4 shapes, fused: O = softmax(Q K^T / sqrt(128) on the band+global+Zipf mask) V, "
+            "seq 16384, head 128, 32x32 blocks, Q/K/V ~ N(0,1)",
     "spgemm": "SpGEMM (bsr_matrix::spgemm): banded 16384x16384 BSR (32x32 blocks, half-width 32 blocks) "
               "times a second matrix of the same pattern",
     "spgemm_rand": "SpGEMM (bsr_matrix::spgemm): 16384x16384 BSR (32x32 blocks, uniform p=0.05) "
@@ -250,6 +253,15 @@ def gen_spgemm_rand(seed, n=512, p=0.05, R=32):
     return gen_spgemm_case(arp, aci, brp, bci, R, seed + 1, f"random p={p}")
 
 
+def gen_attn(seed, S=16384, D=128, R=32):
+    """Config 4's mask and shapes for the fused attention step."""
+    rng = np.random.default_rng(seed)
+    rp, ci = gen_attention_mask(S // R, rng)
+    Q, K, V = (f32_to_bf16(rng.standard_normal((S, D)).astype(np.float32)) for _ in range(3))
+    return dict(kind="attn", name="attention step", M=S, S=S, d=D, R=R, C=R, p=None, rp=rp, ci=ci,
+                Q=Q, K=K, V=V, scale=1.0 / np.sqrt(D))
+
+
 def workload_ops(workload, rank):
     """Host-side ops of one step of `workload` (rank picks the seed of the
     independent per-rank copies)."""
@@ -264,6 +276,8 @@ def workload_ops(workload, rank):
         return gen_cfg4(base)
     if workload == "cfg5":
         return [gen_cfg5(1234)]   # one problem shared by all ranks
+    if workload == "attn":
+        return [gen_attn(base)]
     if workload == "spgemm":
         return [gen_spgemm_band(base)]
     if workload == "spgemm_rand":
@@ -275,6 +289,9 @@ def op_flops(op):
     """Effective FLOPs (reference formulas, GEMM_profiling/read_spmm_profiler.py:73
     and read_sddmm_profiler.py:75)."""
     nnzb = int(op["rp"][-1])
+    if op["kind"] == "attn":
+        # S = Q K^T on the mask's blocks and O = P V (the softmax is not counted)
+        return 4.0 * nnzb * op["R"] * op["C"] * op["d"]
     if op["kind"] == "spgemm":
         return 2.0 * op["pairs"] * op["Ra"] * op["Ca"] * op["Cb"]
     if op["kind"] == "spmm":
@@ -298,6 +315,8 @@ def op_bytes(op):
     once, plus the output written once."""
     nnzb = int(op["rp"][-1])
     R, C = op["R"], op["C"]
+    if op["kind"] == "attn":
+        return 4 * 2 * op["S"] * op["d"] + 4 * (nnzb + op["S"] // R + 1)
     if op["kind"] == "spgemm":
         if "out_nnzb" not in op:
             op["out_nnzb"] = spgemm_out_nnzb(op)
@@ -457,6 +476,11 @@ def _cpu_time(op, rows, threads, kind):
     block-rows [0, rows) of `op`."""
     import oracle
 
+    if op["kind"] == "attn":
+        t0 = time.perf_counter()
+        oracle.attention_bf16(op["rp"], op["ci"], op["S"], op["d"], op["Q"], op["K"], op["V"], op["scale"],
+                              rows=(0, rows), use_ref=kind == "reference")
+        return time.perf_counter() - t0
     if op["kind"] == "spgemm":
         # A's first `rows` block-rows times all of B (the reference's spgemm is one thread)
         arp = op["rp"][: rows + 1]
@@ -488,6 +512,8 @@ def _cpu_time(op, rows, threads, kind):
 
 def _sample_flops(op, rows):
     nnzb = int(op["rp"][rows])
+    if op["kind"] == "attn":
+        return 4.0 * nnzb * op["R"] * op["C"] * op["d"]
     if op["kind"] == "spgemm":
         return 2.0 * float(np.diff(op["brp"])[op["ci"][:nnzb]].sum()) * op["Ra"] * op["Ca"] * op["Cb"]
     if op["kind"] == "spmm":
@@ -519,7 +545,7 @@ def cpu_calibrate(ops, budget_s=12.0, threads=None):
 def cpu_threads_used(ops, threads=None):
     """The reference's spgemm golden is a single-threaded loop; its SpMM and
     SDDMM goldens run on every host thread here."""
-    if all(op["kind"] == "spgemm" for op in ops):
+    if all(op["kind"] in ("spgemm", "attn") for op in ops):
         return 1
     return threads or os.cpu_count() or 1
 
@@ -527,7 +553,8 @@ def cpu_threads_used(ops, threads=None):
 def golden_name(ops):
     kinds = {op["kind"] for op in ops}
     names = {"spmm": "bsr_matrix::spmm_bfloat16", "sddmm": "bsr_matrix::sddmm",
-             "spgemm": "bsr_matrix::spgemm"}
+             "spgemm": "bsr_matrix::spgemm",
+             "attn": "bsr_matrix::sddmm (float) -> softmax (numpy) -> bsr_matrix::spmm_bfloat16"}
     return " / ".join(names[k] for k in sorted(kinds))
 
 
@@ -553,7 +580,13 @@ class DevOp:
 
         self.op = op
         self.kind = op["kind"]
-        if self.kind == "spgemm":
+        if self.kind == "attn":
+            S, d = op["S"], op["d"]
+            self.mask = bsp.DeviceBSR.from_host(S, S, 32, 32, op["rp"], op["ci"], None, local)
+            self.Q, self.K, self.V = (bsp.to_device_bf16(op[k], local).view(S, d) for k in ("Q", "K", "V"))
+            self.out = torch.empty((S, d), dtype=torch.bfloat16, device="cuda")
+            self.plan = bsp.AttnPlan(dev, self.mask, d)
+        elif self.kind == "spgemm":
             self.A = bsp.DeviceBSR.from_host(op["M"], op["K"], op["Ra"], op["Ca"], op["rp"], op["ci"],
                                              op["vals"], local)
             self.Bm = bsp.DeviceBSR.from_host(op["K"], op["N"], op["Ca"], op["Cb"], op["brp"], op["bci"],
@@ -578,7 +611,9 @@ class DevOp:
             self.plan = bsp.SddmmPlan(dev, self.mask, op["K"], strategy)
 
     def run(self, stream):
-        if self.kind == "spgemm":
+        if self.kind == "attn":
+            self.plan.execute(self.Q, self.K, self.V, self.out, self.op["scale"], stream)
+        elif self.kind == "spgemm":
             self.plan.execute(self.A, self.Bm, self.out, stream)
         elif self.kind == "spmm":
             self.plan.execute(self.A, self.B, self.out, stream)
@@ -586,6 +621,8 @@ class DevOp:
             self.plan.execute(self.mask, self.Ad, self.Bd, self.out, stream)
 
     def kernel(self):
+        if self.kind == "attn":
+            return "attn_tcgen05"
         if self.kind == "spgemm":
             return "spgemm_tcgen05"
         if self.kind == "sddmm":
@@ -604,7 +641,7 @@ def strategy_for(op, name):
 
     if name != "auto":
         return bsp.STRATEGIES[name]
-    if op["kind"] == "sddmm":
+    if op["kind"] in ("sddmm", "attn", "spgemm"):
         return bsp.DDA
     return bsp.DDA if op["N"] >= 256 else bsp.SNF
 
@@ -792,7 +829,12 @@ def run_e2e(args, runs, dev, dist, shard):
         host = []
         for r in runs:
             op = r["op"]
-            if op["kind"] == "spgemm":
+            if op["kind"] == "attn":
+                hc = dict(rp=_pinned(op["rp"]), ci=_pinned(op["ci"]), Q=_pinned(op["Q"]), K=_pinned(op["K"]),
+                          V=_pinned(op["V"]))
+                h2d += sum(hc[k].nbytes for k in hc)
+                d2h += 2 * op["S"] * op["d"]
+            elif op["kind"] == "spgemm":
                 hc = dict(rp=_pinned(op["rp"]), ci=_pinned(op["ci"]), v=_pinned(op["vals"]),
                           brp=_pinned(op["brp"]), bci=_pinned(op["bci"]), bv=_pinned(op["bvals"]))
                 h2d += sum(hc[k].nbytes for k in hc)
@@ -815,7 +857,10 @@ def run_e2e(args, runs, dev, dist, shard):
 
         def one():
             for op, hc, strat in host:
-                if op["kind"] == "spgemm":
+                if op["kind"] == "attn":
+                    bsp.attn_host(op["S"], op["d"], hc["rp"], hc["ci"], hc["Q"], hc["K"], hc["V"], op["scale"],
+                                  dev=dev)
+                elif op["kind"] == "spgemm":
                     bsp.spgemm_host(op["M"], op["K"], op["N"], op["Ra"], op["Ca"], op["Cb"], hc["rp"],
                                     hc["ci"], hc["v"], hc["brp"], hc["bci"], hc["bv"], dev=dev)
                 elif op["kind"] == "spmm":
@@ -836,7 +881,7 @@ def run_e2e(args, runs, dev, dist, shard):
             "d2h_bytes_per_step": int(d2h), "steps": steps,
             "path": ("bsp_dist.ShardedSpmm (host B and A values in, NCCL exchange, full C out)"
                      if shard is not None else
-                     "bsp_spmm_host / bsp_sddmm_host / bsp_spgemm_host (C ABI, host buffers; SpGEMM "
+                     "bsp_spmm_host / bsp_sddmm_host / bsp_attn_host / bsp_spgemm_host (C ABI, host buffers; SpGEMM "
                      "plans C's pattern on the host every call, as bsr_matrix::spgemm does)")}
 
 
@@ -888,6 +933,105 @@ def run_reference(args):
     print(json.dumps(out), flush=True)
 
 
+# ---------------------------------------------------------------- ablation --
+def table1_patterns():
+    """The six cases of the reference's Table 1 (block_spmm/scripts/
+    experiments_dram_reads_table.tex; M = N = K = 8192): Row R=C=256 d=25%,
+    multi-diagonal R=C=256 d=50%, Row R=C=64 d=0.6%, multi-diagonal R=C=64
+    d=0.6%, lower- and upper-triangular R=C=256.  Row fills the block grid in
+    row-major order; multi-diagonal takes diagonals 0, +1, -1, +2, ... of the
+    block grid (the reference generators' FILL_ROW / FILL_MULTI_DIAG /
+    FILL_TRIL / FILL_TRIU)."""
+    S = 8192
+
+    def row_fill(nb, n):
+        occ = np.zeros((nb, nb), bool)
+        occ.flat[:n] = True
+        return occ
+
+    def multi_diag(nb, n):
+        occ = np.zeros((nb, nb), bool)
+        placed, d = 0, 0
+        while placed < n:
+            for t in range(nb):
+                i, j = (t, t + d) if d >= 0 else (t - d, t)
+                if i < nb and j < nb and placed < n:
+                    occ[i, j] = True
+                    placed += 1
+            d = -d + 1 if d <= 0 else -d
+        return occ
+
+    out = []
+    for name, R, occ in [("Row_R256_d25", 256, row_fill(32, 256)),
+                         ("MultiDiag_R256_d50", 256, multi_diag(32, 512)),
+                         ("Row_R64_d0.6", 64, row_fill(128, 98)),
+                         ("MultiDiag_R64_d0.6", 64, multi_diag(128, 98)),
+                         ("LowerTri_R256", 256, np.tril(np.ones((32, 32), bool))),
+                         ("UpperTri_R256", 256, np.triu(np.ones((32, 32), bool)))]:
+        rp, ci = _pattern_from_occupancy(occ)
+        out.append((name, R, rp, ci, S))
+    return out
+
+
+def run_ablation(args):
+    """Per-strategy operand traffic and throughput on the Table 1 cases: the
+    counterpart of the reference's count_dram_reads.py (in0 = A, in1 = B reads
+    per core) and its *_no_lb variants.  One JSON line per (case, strategy):
+    the bytes each plan moves with TMA (A, B, as multiples of reading each
+    operand once), device time and effective TFLOP/s."""
+    import torch
+
+    import bsp
+
+    dev = bsp.device(0)
+    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device="cuda")
+    strategies = [("Naive", bsp.NAIVE, {}), ("SnF", bsp.SNF, {}), ("DDA", bsp.DDA, {}),
+                  ("Naive_no_lb", bsp.NAIVE, dict(no_load_balance=1)), ("SnF_no_lb", bsp.SNF, dict(no_load_balance=1)),
+                  ("DDA_no_lb", bsp.DDA, dict(no_load_balance=1))]
+    rng = np.random.default_rng(1234)
+    for name, R, rp, ci, S in table1_patterns():
+        if args.cases and name not in args.cases.split(","):
+            continue
+        vals = uniform_bf16(rng, (ci.size * R, R))
+        B = uniform_bf16(rng, (S, S))
+        A = bsp.DeviceBSR.from_host(S, S, R, R, rp, ci, vals)
+        Bd = bsp.to_device_bf16(B)
+        C = torch.empty((S, S), dtype=torch.bfloat16, device="cuda")
+        flops = 2.0 * ci.size * R * R * S
+        a_once = 2 * ci.size * R * R
+        b_once = 2 * np.unique(ci).size * R * S
+        for sname, strat, o in strategies:
+            opts = bsp.make_opts(**o)
+            tr = bsp.spmm_plan_traffic(S, S, R, R, rp, ci, S, strat, opts=opts, sm_count=dev.sm_count)
+            plan = bsp.SpmmPlan(dev, A, S, strat, bsp.BF16, opts)
+            ts = []
+            try:
+                for it in range(args.warmup + args.steps):
+                    flush.zero_()
+                    e0 = torch.cuda.Event(enable_timing=True)
+                    e1 = torch.cuda.Event(enable_timing=True)
+                    e0.record()
+                    plan.execute(A, Bd, C)
+                    e1.record()
+                    torch.cuda.synchronize()
+                    if it >= args.warmup:
+                        ts.append(e0.elapsed_time(e1))
+                dev.synchronize()
+            except bsp.BspError as err:
+                print(json.dumps({"case": name, "strategy": sname, "variant": tr["variant"], "error": str(err)}),
+                      flush=True)
+                plan.close()
+                continue
+            ms = float(np.median(ts))
+            print(json.dumps({"case": name, "strategy": sname, "R": R, "nnzb": int(ci.size),
+                              "variant": tr["variant"], "units": tr["units"],
+                              "a_bytes": tr["a_bytes"], "b_bytes": tr["b_bytes"],
+                              "a_boxes": tr["a_boxes"], "b_boxes": tr["b_boxes"],
+                              "a_reads_x": tr["a_bytes"] / a_once, "b_reads_x": tr["b_bytes"] / b_once,
+                              "ms": ms, "tflops": flops / (ms * 1e-3) / 1e12}), flush=True)
+            plan.close()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -901,10 +1045,15 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--nccl-exchange", action="store_true",
                     help="cfg5 with N > 1: exchange C panels by NCCL send/recv instead of the fused kernel")
+    ap.add_argument("--ablation", action="store_true",
+                    help="per-strategy operand traffic and TFLOP/s on the reference's Table 1 cases")
+    ap.add_argument("--cases", default="", help="--ablation: comma-separated case names")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    if args.impl == "reference":
+    if args.ablation:
+        run_ablation(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_bsp(args)

@@ -336,8 +336,16 @@ bsp_status bsp_attn_execute(const bsp_attn_plan* plan, const void* Q, int64_t ld
                             int64_t ldk, const void* V, int64_t ldv, float scale, void* O,
                             int64_t ldo, void* stream);
 bsp_status bsp_attn_plan_destroy(bsp_attn_plan* plan);
-/* info[0] units, [1] grid, [2] chunks, [3] mask blocks (distinct), [4] S,
- * [5] d, [8] table bytes, [9] shared memory, [10] TMEM columns. */
+/* info[0] work units (parts of split units counted), [1] grid, [2] chunks,
+ * [3] mask blocks (distinct), [4] S, [5] d, [6] parts of split units,
+ * [7] split units, [8] table bytes, [9] shared memory, [10] TMEM columns.
+ * Work units are 128 query rows.  When there are fewer units than CTAs, the
+ * longest units are split into parts (consecutive key chunks, up to 16 per
+ * unit) that run on the otherwise idle CTAs and are merged by the part that
+ * finishes last; a plan therefore executes on one stream at a time.
+ * Options: max_ctas; timeout_ms; n_tiles > 0 = instead cut every unit longer
+ * than 5/4 n_tiles chunks into parts of about n_tiles chunks; group_rows = -1
+ * never splits. */
 bsp_status bsp_attn_plan_info(const bsp_attn_plan* plan, int64_t info[16]);
 
 /* Host-buffer form: mask pattern, Q, K, V, O all host arrays ([S, d] dense). */

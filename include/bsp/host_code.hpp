@@ -129,6 +129,56 @@ void sddmm(bsr_matrix<bfloat16>& mask, dense_matrix<bfloat16>& c, dense_matrix<b
 }
 
 }  // namespace detail
+
+// C = a * b for two BSR matrices on the GPU: the device form of the
+// reference's bsr_matrix<T>::spgemm (sparse_common/bsr_matrix.hpp:741-810),
+// same result pattern (columns ascending per block-row) and one bf16 rounding
+// per block.  Block sizes 32, 64 or 128; a.W == b.H and a.C == b.R.
+inline bsr_matrix<bfloat16> spgemm(bsr_matrix<bfloat16>& a, bsr_matrix<bfloat16>& b, IDevice* device,
+                                   const bsp_spmm_opts* opts = nullptr) {
+  if (a.W != b.H || a.C != b.R) throw std::runtime_error("bsp: spgemm operands do not chain");
+  const std::vector<uint16_t> av = detail::bits(a.data), bv = detail::bits(b.data);
+  int64_t nnzb = 0;
+  check(bsp_spgemm_host(device->handle(), a.H, a.W, b.W, static_cast<int32_t>(a.R), static_cast<int32_t>(a.C),
+                        static_cast<int32_t>(b.C), static_cast<int64_t>(a.nblocks), a.indptr.data(),
+                        a.indices.data(), av.data(), static_cast<int64_t>(b.nblocks), b.indptr.data(),
+                        b.indices.data(), bv.data(), 0, &nnzb, nullptr, nullptr, nullptr, opts, 0, nullptr),
+        "bsp_spgemm_host (size)");
+  std::vector<int> rp(a.H / a.R + 1), ci(static_cast<size_t>(nnzb));
+  std::vector<uint16_t> out(static_cast<size_t>(nnzb) * a.R * b.C);
+  check(bsp_spgemm_host(device->handle(), a.H, a.W, b.W, static_cast<int32_t>(a.R), static_cast<int32_t>(a.C),
+                        static_cast<int32_t>(b.C), static_cast<int64_t>(a.nblocks), a.indptr.data(),
+                        a.indices.data(), av.data(), static_cast<int64_t>(b.nblocks), b.indptr.data(),
+                        b.indices.data(), bv.data(), nnzb, &nnzb, rp.data(), ci.data(), out.data(), opts, 0,
+                        nullptr),
+        "bsp_spgemm_host");
+  std::vector<bfloat16> vals(out.size());
+  for (size_t i = 0; i < out.size(); ++i) vals[i] = bfloat16::from_bits(out[i]);
+  return bsr_matrix<bfloat16>(std::move(vals), std::move(rp), std::move(ci), a.H, b.W, a.R, b.C,
+                              static_cast<size_t>(nnzb));
+}
+
+// O = softmax_rows(scale * Q K^T on the mask's blocks) V, one head: the
+// reference's SDDMM -> row softmax -> SpMM chain fused on the GPU.  mask: S x S
+// with 32 x 32 blocks (values ignored); Q, K, V: S x d (d = 64 or 128).
+inline dense_matrix<bfloat16> attention_step(bsr_matrix<bfloat16>& mask, dense_matrix<bfloat16>& q,
+                                             dense_matrix<bfloat16>& k, dense_matrix<bfloat16>& v, float scale,
+                                             IDevice* device) {
+  if (mask.H != mask.W || mask.R != 32 || mask.C != 32 || q.H != mask.H || k.H != q.H || v.H != q.H ||
+      k.W != q.W || v.W != q.W)
+    throw std::runtime_error("bsp: attention_step operands do not match");
+  const std::vector<uint16_t> qv = detail::bits(q.data), kv = detail::bits(k.data), vv = detail::bits(v.data);
+  std::vector<uint16_t> o(qv.size());
+  check(bsp_attn_host(device->handle(), static_cast<int64_t>(mask.H), static_cast<int64_t>(q.W),
+                      static_cast<int64_t>(mask.nblocks),
+                      mask.indptr.data(), mask.indices.data(), qv.data(), kv.data(), vv.data(), scale, o.data(),
+                      nullptr),
+        "bsp_attn_host");
+  dense_matrix<bfloat16> out(static_cast<int>(q.H), static_cast<int>(q.W));
+  for (size_t i = 0; i < o.size(); ++i) out.data[i] = bfloat16::from_bits(o[i]);
+  return out;
+}
+
 }  // namespace bsp
 
 namespace bsr_host_code {

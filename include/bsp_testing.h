@@ -30,6 +30,16 @@ bsp_status bsp_spmm_plan_inspect(int64_t M, int64_t K, int32_t R, int32_t C, int
                                  int32_t* steps_out, int32_t* stage_list_out,
                                  int32_t* cta_stage_begin_out);
 
+/* The SpMM planner's operand traffic (host only): traffic[0] A bytes and
+ * traffic[2] A boxes, traffic[1] B bytes and traffic[3] B boxes that the
+ * plan's kernel moves with TMA into shared memory (absent blocks excluded).
+ * The counterpart of the reference's per-core in0 / in1 DRAM read counts
+ * (block_spmm/scripts/count_dram_reads.py); info as bsp_spmm_plan_info. */
+bsp_status bsp_spmm_plan_traffic(int64_t M, int64_t K, int32_t R, int32_t C, int64_t nnzb,
+                                 const int32_t* row_ptr, const int32_t* col_idx, int64_t N,
+                                 bsp_strategy strategy, const bsp_spmm_opts* opts, int32_t sm_count,
+                                 int32_t max_smem, int64_t info[16], int64_t traffic[4]);
+
 /* units_out[info[0] * info[12]]: info[11] == 0 (swap-AB kernel): 12 words per
  * unit (row, r_off, nseg, pad, blk[4], col[4]); info[11] == 1 (row-stacked
  * kernel): 44 words per unit (row0, nseg, pad[2], seg_col[8], blk[4][8]). */
@@ -58,8 +68,9 @@ bsp_status bsp_spgemm_plan_inspect(int64_t M, int64_t K, int64_t N, int32_t Ra, 
                                    int32_t* units_out, int32_t* steps_out, int32_t* cta_begin_out);
 
 /* Attention planner (S x S mask with 32 x 32 blocks, head size d).
- * info[16] as bsp_attn_plan_info; units_out[info[0] * 4] (row0, chunk_begin,
- * n_chunks, pad per unit, in CTA order), chunks_out[info[2] * 8] (kb[4]:
+ * info[16] as bsp_attn_plan_info; units_out[info[0] * 8] (row0, chunk_begin,
+ * n_chunks, n_parts, part, slot0, counter, pad per unit or part, in CTA
+ * order), chunks_out[info[2] * 8] (kb[4]:
  * key block of each slot or -1, bits: bit 4 q + s set when block-row q of the
  * unit holds slot s, pad[3]), cta_begin_out[info[1] + 1]. */
 bsp_status bsp_attn_plan_inspect(int64_t S, int64_t d, int64_t nnzb, const int32_t* row_ptr,

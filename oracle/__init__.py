@@ -159,7 +159,7 @@ def sddmm_f32(indptr, indices, mask_data, H, W, R, C, A, B, K):
     return out
 
 
-def attention_bf16(indptr, indices, S, d, Q, K, V, scale, rows=None):
+def attention_bf16(indptr, indices, S, d, Q, K, V, scale, rows=None, use_ref=False):
     """Block-sparse attention step, the reference chain with a row softmax
     between its two goldens: Sc = sddmm(mask, Q, K^T) with T = float
     (bsr_matrix.hpp:816-857), P = softmax over each row's stored positions of
@@ -167,7 +167,9 @@ def attention_bf16(indptr, indices, S, d, Q, K, V, scale, rows=None):
     (bsr_matrix.hpp:692-736).  The mask (S x S, 32 x 32 blocks) is a pattern:
     a column repeated in a row counts once.  Q, K, V: [S, d] bf16 bits.
     Returns O [S, d] bf16 bits (rows of block-rows without blocks are 0).
-    ``rows`` = (r0, r1) restricts the work to those block-rows (others 0)."""
+    ``rows`` = (r0, r1) restricts the work to those block-rows (others 0).
+    ``use_ref`` runs the two products through the reference's own compiled
+    goldens (oracle/_ref) instead of the restatement."""
     R = 32
     rp = _c(indptr, np.int32)
     ci = _c(indices, np.int32)
@@ -185,7 +187,8 @@ def attention_bf16(indptr, indices, S, d, Q, K, V, scale, rows=None):
     Qf = bf16_to_f32(_c(Q, np.uint16)).reshape(S, d)
     Kt = np.ascontiguousarray(bf16_to_f32(_c(K, np.uint16)).reshape(S, d).T)
     ones = np.ones(nnzb * R * R, np.float32)
-    Sc = sddmm_f32(urp, uci, ones, S, S, R, R, Qf, Kt, d).reshape(nnzb, R, R)
+    sd = ref_sddmm_f32 if use_ref else sddmm_f32
+    Sc = sd(urp, uci, ones, S, S, R, R, Qf, Kt, d).reshape(nnzb, R, R)
     P = np.zeros_like(Sc)
     for i in range(r0, r1):
         b0, b1 = urp[i], urp[i + 1]
@@ -197,6 +200,8 @@ def attention_bf16(indptr, indices, S, d, Q, K, V, scale, rows=None):
         e /= e.sum(axis=1, keepdims=True)
         P[b0:b1] = e.reshape(R, b1 - b0, R).transpose(1, 0, 2)
     Pb = f32_to_bf16(P.astype(np.float32).ravel())
+    if use_ref:
+        return ref_spmm_bf16(urp, uci, Pb, S, S, R, R, _c(V, np.uint16).reshape(S, d), d)
     return spmm_bf16(urp, uci, Pb, S, S, R, R, _c(V, np.uint16).reshape(S, d), d)
 
 

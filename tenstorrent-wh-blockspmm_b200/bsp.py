@@ -35,7 +35,7 @@ EXPORTS = [
     "bsp_ipc_close", "bsp_spgemm_plan_create", "bsp_spgemm_pattern", "bsp_spgemm_execute",
     "bsp_spgemm_plan_destroy", "bsp_spgemm_plan_info", "bsp_spgemm_host", "bsp_spgemm_plan_inspect",
     "bsp_attn_plan_create", "bsp_attn_execute", "bsp_attn_plan_destroy", "bsp_attn_plan_info",
-    "bsp_attn_host", "bsp_attn_plan_inspect",
+    "bsp_attn_host", "bsp_attn_plan_inspect", "bsp_spmm_plan_traffic",
 ]
 IPC_HANDLE_BYTES = 64
 
@@ -137,6 +137,8 @@ def lib():
         "bsp_attn_plan_info": (S, [P, ctypes.POINTER(I64)]),
         "bsp_attn_host": (S, [P, I64, I64, I64, P, P, P, P, P, ctypes.c_float, P, ctypes.POINTER(Opts)]),
         "bsp_attn_plan_inspect": (S, [I64, I64, I64, P, P, ctypes.POINTER(Opts), I32, I32, P, P, P, P]),
+        "bsp_spmm_plan_traffic": (S, [I64, I64, I32, I32, I64, P, P, I64, S, ctypes.POINTER(Opts), I32, I32,
+                                      P, P]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -562,8 +564,8 @@ def inspect_spgemm_plan(M, K, N, Ra, Ca, Cb, a_row_ptr, a_col_idx, b_row_ptr, b_
 
 
 # --------------------------------------------------------------- attention --
-ATTN_INFO_KEYS = ["units", "ctas", "chunks", "mask_blocks", "S", "d", "_6", "_7", "plan_bytes",
-                  "smem_bytes", "tmem_cols"]
+ATTN_INFO_KEYS = ["units", "ctas", "chunks", "mask_blocks", "S", "d", "parts", "split_units",
+                  "plan_bytes", "smem_bytes", "tmem_cols"]
 
 
 class AttnPlan:
@@ -641,7 +643,7 @@ def inspect_attn_plan(S, d, row_ptr, col_idx, opts=None, sm_count=148, max_smem=
     o = opts if opts is not None else Opts()
     args = (S, d, int(rp[-1]), _ptr(rp), _ptr(ci), ctypes.byref(o), sm_count, max_smem, _ptr(info))
     _check(lib().bsp_attn_plan_inspect(*args, None, None, None))
-    units = np.zeros((max(int(info[0]), 1), 4), np.int32)
+    units = np.zeros((max(int(info[0]), 1), 8), np.int32)
     chunks = np.zeros((max(int(info[2]), 1), 8), np.int32)
     cta = np.zeros(int(info[1]) + 1, np.int32)
     _check(lib().bsp_attn_plan_inspect(*args, _ptr(units), _ptr(chunks), _ptr(cta)))
@@ -677,6 +679,22 @@ def inspect_spmm_plan(M, K, R, C, row_ptr, col_idx, N, strategy=NAIVE, c_type=BF
     d.update(unit_table=units, cta_begin=cta, step_table=steps[: int(info[7])],
              stage_table=stages[: int(info[13])], cta_stage_begin=cta_st)
     return d
+
+
+def spmm_plan_traffic(M, K, R, C, row_ptr, col_idx, N, strategy=NAIVE, opts=None, sm_count=148,
+                      max_smem=232448):
+    """Operand bytes / boxes the SpMM plan moves into shared memory (host only):
+    dict(a_bytes, b_bytes, a_boxes, b_boxes, variant)."""
+    rp = np.ascontiguousarray(row_ptr, dtype=np.int32)
+    ci = np.ascontiguousarray(col_idx, dtype=np.int32)
+    ci = ci if ci.size else np.zeros(1, np.int32)
+    info = np.zeros(16, np.int64)
+    tr = np.zeros(4, np.int64)
+    o = opts if opts is not None else Opts()
+    _check(lib().bsp_spmm_plan_traffic(M, K, R, C, int(rp[-1]), _ptr(rp), _ptr(ci), N, strategy,
+                                       ctypes.byref(o), sm_count, max_smem, _ptr(info), _ptr(tr)))
+    return dict(a_bytes=int(tr[0]), b_bytes=int(tr[1]), a_boxes=int(tr[2]), b_boxes=int(tr[3]),
+                variant=int(info[11]), units=int(info[0]))
 
 
 def inspect_sddmm_plan(M, N, R, C, row_ptr, col_idx, K, strategy=NAIVE, opts=None, sm_count=148,

@@ -16,9 +16,11 @@
 //   P   = exp2(S * scale * log2 e - m)   softmax warps, one thread per query
 //         row: slots the row's block-row does not hold are masked out, the
 //         running maximum m moves only when it grows by more than 2^8 (then
-//         the O row and the row sum are rescaled), P is written to shared
-//         memory as the K-major bf16 operand
-//   O  += P V_c            MMA 128 x d x 128 into TMEM
+//         the O row and the row sum are rescaled), P is stored to TMEM as
+//         bf16 pairs (row m in lane m)
+//   O  += P V_c            MMA 128 x d x 128 into TMEM, A = P read from TMEM
+//                          (only V crosses shared memory, so this MMA is not
+//                          held back by shared-memory bandwidth)
 // and at the end of the unit O / l is rounded to bf16 and stored.  The MMA
 // warp issues S of chunk j + 1 before P V of chunk j, so the tensor pipe works
 // while the softmax warps do.  K and V have separate two-slot rings (K of
@@ -46,28 +48,35 @@ constexpr int kAtMmaWarp = 0;
 constexpr int kAtKWarp = 1;
 constexpr int kAtVWarp = 2;
 constexpr int kAtSoft0 = 4;
-constexpr uint32_t kAtPBytes = 128 * 128 * 2;  // one P tile
 constexpr uint32_t kAtAtom = 128 * 128;        // 128 rows x 128 B (64 bf16 columns)
 constexpr float kAtRescale = 8.0f;             // log2 of the growth that forces a rescale
+constexpr int kAtSoftWarps = 4;                // one per TMEM lane quarter
+// TMEM columns: S buffers 0..255 (two of 128 fp32), P buffers 256..383 (two
+// of 64: 128 bf16 keys packed in pairs), O 384 .. 384 + d.
+constexpr int kAtSBuf = 2;
+constexpr uint32_t kAtPCol = 256;
+constexpr uint32_t kAtOCol = 384;
 
 struct AtSmemHeader {
   uint64_t q_full, q_empty;
   uint64_t k_full[2], k_empty[2];
   uint64_t v_full[2], v_empty[2];
-  uint64_t s_full[2], s_empty[2];
+  uint64_t s_full[kAtSBuf], s_empty[kAtSBuf];
   uint64_t p_full[2], p_empty[2];
   uint64_t o_full, o_empty;
+  uint64_t merge_bar;  // the softmax warps, split-unit merge
   uint64_t drain;
   uint32_t tmem_base;
   int abort_flag;
+  int merge_flag;
 };
 static_assert(sizeof(AtSmemHeader) <= 1024, "header must fit its 1 KiB slot");
 
 __host__ __device__ constexpr uint32_t at_tile(int d) { return 128u * static_cast<uint32_t>(d) * 2u; }
 
-// Shared memory (from the 1 KiB-aligned base): header, Q, K[2], V[2], P[2].
+// Shared memory (from the 1 KiB-aligned base): header, Q, K[2], V[2].
 struct AtLayout {
-  uint32_t q, k[2], v[2], p[2];
+  uint32_t q, k[2], v[2];
   __device__ AtLayout(uint32_t base, int d) {
     const uint32_t t = at_tile(d);
     q = base + 1024u;
@@ -75,8 +84,6 @@ struct AtLayout {
     k[1] = k[0] + t;
     v[0] = k[1] + t;
     v[1] = v[0] + t;
-    p[0] = v[1] + t;
-    p[1] = p[0] + kAtPBytes;
   }
 };
 
@@ -158,15 +165,14 @@ __device__ __forceinline__ void at_mma(const AttnKernelParams& p, AtSmemHeader* 
   const int ks_d = p.d / 16;  // k-steps of S = Q K^T
   const uint32_t atom16 = kAtAtom >> 4;
   const uint64_t qdesc = smem_desc(L.q, 16u, 1024u, 2u);
-  uint64_t kdesc[2], vdesc[2], pdesc[2];
+  uint64_t kdesc[2], vdesc[2];
   for (int s = 0; s < 2; ++s) {
     kdesc[s] = smem_desc(L.k[s], 16u, 1024u, 2u);
     vdesc[s] = smem_desc(L.v[s], kAtAtom, 1024u, 2u);  // MN-major: LBO = next 64 columns of d
-    pdesc[s] = smem_desc(L.p[s], 16u, 1024u, 2u);
   }
   const uint32_t idesc_s = idesc_bf16_f32(128, 128, 0, 0);
   const uint32_t idesc_pv = idesc_bf16_f32(128, p.d, 0, 1);
-  const uint32_t t_o = tmem_base + 256u;
+  const uint32_t t_o = tmem_base + kAtOCol;
   int64_t kn = 0;
   int qn = 0, on = 0;
   bool ok = true;
@@ -181,14 +187,18 @@ __device__ __forceinline__ void at_mma(const AttnKernelParams& p, AtSmemHeader* 
     if (!wait_all(baddr(&hdr->v_full[st]), ph, ctl, ST_TIMEOUT_MMA)) return false;
     if (!wait_all(baddr(&hdr->p_full[st]), ph, ctl, ST_TIMEOUT_MMA)) return false;
     tc_fence_after();
+    // A = P from TMEM: 16 keys (8 packed columns) per MMA
+    const uint32_t t_p = tmem_base + kAtPCol + 64u * static_cast<uint32_t>(st);
 #pragma unroll
     for (int k = 0; k < 8; ++k)
-      mma_bf16_pred(t_o, pdesc[st] + (k >> 2) * atom16 + (k & 3) * 2u, vdesc[st] + k * 128u, idesc_pv,
-                    acc || k > 0, is0);
+      mma_bf16_ts_pred(t_o, t_p + 8u * k, vdesc[st] + k * 128u, idesc_pv, acc || k > 0, is0);
     mma_commit_pred(baddr(&hdr->v_empty[st]), is0);
     mma_commit_pred(baddr(&hdr->p_empty[st]), is0);
     return true;
   };
+  // S of chunk j + 2 is issued before P V of chunk j (kAtSBuf S buffers), so
+  // the softmax of a chunk has two MMA groups' time before its P V is due.
+  constexpr int kLead = kAtSBuf - 1;
 #pragma unroll 1
   for (int u = u_begin; u < u_end && ok; ++u) {
     const int n = __ldg(&p.units[u].n_chunks);
@@ -201,22 +211,23 @@ __device__ __forceinline__ void at_mma(const AttnKernelParams& p, AtSmemHeader* 
       const int64_t g = kn + j;
       const int st = static_cast<int>(g & 1);
       const uint32_t ph = static_cast<uint32_t>((g >> 1) & 1);
+      const int sb = static_cast<int>(g % kAtSBuf);
+      const uint32_t sph = static_cast<uint32_t>((g / kAtSBuf) & 1);
       ok = wait_all(baddr(&hdr->k_full[st]), ph, ctl, ST_TIMEOUT_MMA) &&
-           wait_all(baddr(&hdr->s_empty[st]), ph ^ 1u, ctl, ST_TIMEOUT_MMA);
+           wait_all(baddr(&hdr->s_empty[sb]), sph ^ 1u, ctl, ST_TIMEOUT_MMA);
       if (!ok) break;
       tc_fence_after();
-      const uint32_t t_s = tmem_base + static_cast<uint32_t>(st) * 128u;
+      const uint32_t t_s = tmem_base + static_cast<uint32_t>(sb) * 128u;
 #pragma unroll 1
       for (int k = 0; k < ks_d; ++k)
         mma_bf16_pred(t_s, qdesc + (k >> 2) * atom16 + (k & 3) * 2u, kdesc[st] + (k >> 2) * atom16 + (k & 3) * 2u,
                       idesc_s, k > 0, is0);
-      mma_commit_pred(baddr(&hdr->s_full[st]), is0);
+      mma_commit_pred(baddr(&hdr->s_full[sb]), is0);
       mma_commit_pred(baddr(&hdr->k_empty[st]), is0);
       if (j == n - 1) mma_commit_pred(baddr(&hdr->q_empty), is0);
-      if (j >= 1) ok = pv(g - 1, j > 1);
+      if (j >= kLead) ok = pv(g - kLead, j > kLead);
     }
-    if (!ok) break;
-    ok = pv(kn + n - 1, n > 1);
+    for (int j = n > kLead ? n - kLead : 0; j < n && ok; ++j) ok = pv(kn + j, j > 0);
     if (!ok) break;
     mma_commit_pred(baddr(&hdr->o_full), is0);
     kn += n;
@@ -233,19 +244,28 @@ __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
   return *reinterpret_cast<const uint32_t*>(&h);
 }
 
-// Softmax / rescale / epilogue warp of lane quarter q: thread = query row
-// 32 q + lane of the unit.
+__device__ __forceinline__ void store_row_bf16(uint4* dst, const float* v, float scale) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    dst[i] = make_uint4(pack_bf16(v[8 * i] * scale, v[8 * i + 1] * scale), pack_bf16(v[8 * i + 2] * scale, v[8 * i + 3] * scale),
+                        pack_bf16(v[8 * i + 4] * scale, v[8 * i + 5] * scale),
+                        pack_bf16(v[8 * i + 6] * scale, v[8 * i + 7] * scale));
+}
+
+// Softmax / rescale / epilogue warp of TMEM lane quarter q = warp - 4:
+// thread = query row 32 q + lane of the unit; the chunk's S row is read from
+// TMEM once into registers.
 __device__ __forceinline__ void at_softmax(const AttnKernelParams& p, AtSmemHeader* hdr, const AtLayout& L,
                                           uint8_t* gbase, uint32_t base, uint32_t tmem_base, int u_begin,
                                           int u_end, const WaitCtl& ctl, int warp, int lane) {
   const int q = warp - kAtSoft0;
   const int r = 32 * q + lane;  // row inside the unit
   const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(32 * q) << 16);
-  const uint32_t t_o = lane_base + 256u;
-  const int dc = p.d / 32;       // 32-column groups of a head row
+  const uint32_t t_o = lane_base + kAtOCol;
+  const int gd = p.d / 32;      // 32-column groups of O
   const float sl2 = p.scale_log2;
   int64_t kn = 0;
-  int on = 0;
+  int on = 0, mp = 0;
   bool ok = true;
 #pragma unroll 1
   for (int u = u_begin; u < u_end && ok; ++u) {
@@ -263,29 +283,37 @@ __device__ __forceinline__ void at_softmax(const AttnKernelParams& p, AtSmemHead
 #pragma unroll 1
     for (int j = 0; j < n; ++j) {
       const int64_t g = kn + j;
+      const int sb = static_cast<int>(g % kAtSBuf);
+      const uint32_t sph = static_cast<uint32_t>((g / kAtSBuf) & 1);
       const int st = static_cast<int>(g & 1);
       const uint32_t ph = static_cast<uint32_t>((g >> 1) & 1);
-      const uint32_t bits = bits_next;
+      const uint32_t bits = bits_next;  // bit s: slot s held by this block-row
       if (j + 1 < n) bits_next = (__ldg(&p.chunks[cb + j + 1].bits) >> (4 * q)) & 0xFu;
-      ok = mbar_wait_bounded(baddr(&hdr->s_full[st]), ph, ctl, ST_TIMEOUT_EPILOGUE);
-      if (!__all_sync(0xffffffffu, ok)) {
+      if (!__all_sync(0xffffffffu, mbar_wait_bounded(baddr(&hdr->s_full[sb]), sph, ctl, ST_TIMEOUT_EPILOGUE))) {
         ok = false;
         break;
       }
       tc_fence_after();
-      const uint32_t t_s = lane_base + static_cast<uint32_t>(st) * 128u;
-      // pass 1: the row maximum over the slots this block-row holds
-      float mx = -INFINITY;
-#pragma unroll 1
-      for (int s = 0; s < kAttnSlots; ++s) {
-        if (!((bits >> s) & 1u)) continue;  // warp-uniform
-        uint32_t v[32];
-        tmem_ld_32x32b_x32(t_s + 32u * s, v);
-        tmem_ld_wait();
+      const uint32_t t_s = lane_base + static_cast<uint32_t>(sb) * 128u;
+      uint32_t v[kAttnSlots][32];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) mx = fmaxf(mx, __uint_as_float(v[i]));
-      }
-      mx *= sl2;
+      for (int s_ = 0; s_ < kAttnSlots; ++s_)
+        if ((bits >> s_) & 1u) tmem_ld_32x32b_x32(t_s + 32u * s_, v[s_]);
+      tmem_ld_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(baddr(&hdr->s_empty[sb]));  // S is in registers now
+      float mx = -INFINITY;
+#pragma unroll
+      for (int s_ = 0; s_ < kAttnSlots; ++s_)
+        if ((bits >> s_) & 1u) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) mx = fmaxf(mx, __uint_as_float(v[s_][i]));
+        }
+      // The scaled scores below are rounded exactly like this maximum (no
+      // fused multiply-add), so every exponent S * sl2 - m stays <= 8 even
+      // when the scores are so large that one fp32 ulp exceeds 2^8.
+      mx = __fmul_rn(mx, sl2);
       const bool need = mx > m_used + kAtRescale;
       if (__any_sync(0xffffffffu, need)) {
         const float new_m = need ? mx : m_used;
@@ -293,87 +321,156 @@ __device__ __forceinline__ void at_softmax(const AttnKernelParams& p, AtSmemHead
         if (j >= 1) {
           // O holds the unit's chunks 0..j-1: wait for the last of those P V
           const int64_t gp = g - 1;
-          ok = mbar_wait_bounded(baddr(&hdr->p_empty[gp & 1]), static_cast<uint32_t>((gp >> 1) & 1), ctl,
-                                 ST_TIMEOUT_EPILOGUE);
-          if (!__all_sync(0xffffffffu, ok)) {
+          if (!__all_sync(0xffffffffu, mbar_wait_bounded(baddr(&hdr->p_empty[gp & 1]),
+                                                         static_cast<uint32_t>((gp >> 1) & 1), ctl,
+                                                         ST_TIMEOUT_EPILOGUE))) {
             ok = false;
             break;
           }
           tc_fence_after();
 #pragma unroll 1
-          for (int c = 0; c < dc; ++c) {
-            uint32_t v[32];
-            tmem_ld_32x32b_x32(t_o + 32u * c, v);
+          for (int c = 0; c < gd; ++c) {
+            uint32_t o[32];
+            tmem_ld_32x32b_x32(t_o + 32u * c, o);
             tmem_ld_wait();
 #pragma unroll
-            for (int i = 0; i < 32; ++i) v[i] = __float_as_uint(__uint_as_float(v[i]) * alpha);
-            tmem_st_32x32b_x32(t_o + 32u * c, v);
+            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+            tmem_st_32x32b_x32(t_o + 32u * c, o);
           }
           tmem_st_wait();
         }
         l *= alpha;
         m_used = new_m;
       }
-      // pass 2: P = exp2(S * sl2 - m) into this chunk's P buffer
-      ok = mbar_wait_bounded(baddr(&hdr->p_empty[st]), ph ^ 1u, ctl, ST_TIMEOUT_EPILOGUE);
-      if (!__all_sync(0xffffffffu, ok)) {
+      // P = exp2(S * sl2 - m) into this chunk's P buffer
+      if (!__all_sync(0xffffffffu, mbar_wait_bounded(baddr(&hdr->p_empty[st]), ph ^ 1u, ctl, ST_TIMEOUT_EPILOGUE))) {
         ok = false;
         break;
       }
-      uint8_t* prow = gbase + (L.p[st] - base) + static_cast<uint32_t>(r) * 128u;
-#pragma unroll 1
-      for (int s = 0; s < kAttnSlots; ++s) {
-        uint32_t w[16];
-        if ((bits >> s) & 1u) {
-          uint32_t v[32];
-          tmem_ld_32x32b_x32(t_s + 32u * s, v);
-          tmem_ld_wait();
+      uint32_t w[kAttnSlots * 16];  // this row's 128 keys as bf16 pairs
+#pragma unroll
+      for (int s_ = 0; s_ < kAttnSlots; ++s_) {
+        if ((bits >> s_) & 1u) {
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
-            const float a = exp2f(__uint_as_float(v[2 * i]) * sl2 - m_used);
-            const float b = exp2f(__uint_as_float(v[2 * i + 1]) * sl2 - m_used);
-            w[i] = pack_bf16(a, b);
-            l += __uint_as_float(w[i] << 16) + __uint_as_float(w[i] & 0xFFFF0000u);
+            const uint32_t x =
+                pack_bf16(exp2f(__fsub_rn(__fmul_rn(__uint_as_float(v[s_][2 * i]), sl2), m_used)),
+                          exp2f(__fsub_rn(__fmul_rn(__uint_as_float(v[s_][2 * i + 1]), sl2), m_used)));
+            w[16 * s_ + i] = x;
+            l += __uint_as_float(x << 16) + __uint_as_float(x & 0xFFFF0000u);
           }
         } else {
 #pragma unroll
-          for (int i = 0; i < 16; ++i) w[i] = 0u;
-        }
-        // keys 32 s .. 32 s + 31: atom s / 2, 16-byte chunks 4 (s & 1) .. + 3, XOR-swizzled by row
-        uint8_t* atom = prow + static_cast<uint32_t>(s >> 1) * kAtAtom;
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          const uint32_t chunk = static_cast<uint32_t>(4 * (s & 1) + c) ^ static_cast<uint32_t>(r & 7);
-          *reinterpret_cast<uint4*>(atom + chunk * 16u) = make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
+          for (int i = 0; i < 16; ++i) w[16 * s_ + i] = 0u;
         }
       }
+      const uint32_t t_p = lane_base + kAtPCol + 64u * static_cast<uint32_t>(st);
+      tmem_st_32x32b_x32(t_p, *reinterpret_cast<const uint32_t(*)[32]>(w));
+      tmem_st_32x32b_x32(t_p + 32u, *reinterpret_cast<const uint32_t(*)[32]>(w + 32));
+      tmem_st_wait();
       tc_fence_before();
-      fence_proxy_async_smem();
       __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(baddr(&hdr->s_empty[st]));
-        mbar_arrive(baddr(&hdr->p_full[st]));
-      }
+      if (lane == 0) mbar_arrive(baddr(&hdr->p_full[st]));
     }
     if (!ok) break;
-    // epilogue: O / l, rounded once to bf16
-    ok = mbar_wait_bounded(baddr(&hdr->o_full), static_cast<uint32_t>(on & 1), ctl, ST_TIMEOUT_EPILOGUE);
-    if (!__all_sync(0xffffffffu, ok)) break;
+    if (!__all_sync(0xffffffffu, mbar_wait_bounded(baddr(&hdr->o_full), static_cast<uint32_t>(on & 1), ctl,
+                                                   ST_TIMEOUT_EPILOGUE)))
+      break;
     ++on;
     tc_fence_after();
-    const float inv = l > 0.f ? 1.f / l : 0.f;
+    const int n_parts = __ldg(&p.units[u].n_parts);
+    if (n_parts == 1) {
+      // epilogue: O / l, rounded once to bf16
+      const float inv = l > 0.f ? 1.f / l : 0.f;
 #pragma unroll 1
-    for (int c = 0; c < dc; ++c) {
-      uint32_t v[32];
-      tmem_ld_32x32b_x32(t_o + 32u * c, v);
-      tmem_ld_wait();
-      if (row < p.S) {
+      for (int c = 0; c < gd; ++c) {
+        uint32_t o[32];
+        tmem_ld_32x32b_x32(t_o + 32u * c, o);
+        tmem_ld_wait();
+        if (row < p.S) store_row_bf16(orow + 4 * c, reinterpret_cast<const float*>(o), inv);
+      }
+    } else {
+      // A part of a split unit: its unnormalised O row, running maximum and
+      // row sum go to this part's workspace slot; the part that finishes last
+      // merges O = sum_p 2^(m_p - M) O_p / sum_p 2^(m_p - M) l_p, its own O
+      // still in TMEM.
+      const int slot0 = __ldg(&p.units[u].slot0);
+      const int part = __ldg(&p.units[u].part);
+      const int cnt = __ldg(&p.units[u].counter);
+      const int64_t slot_floats = 128 * static_cast<int64_t>(p.d + 2);
+      const float* base0 = p.work + slot0 * slot_floats;
+      float* ws = p.work + (slot0 + part) * slot_floats;
+      float4* wrow = reinterpret_cast<float4*>(ws + static_cast<int64_t>(r) * p.d);
+#pragma unroll 1
+      for (int c = 0; c < gd; ++c) {
+        uint32_t o[32];
+        tmem_ld_32x32b_x32(t_o + 32u * c, o);
+        tmem_ld_wait();
 #pragma unroll
-        for (int i = 0; i < 4; ++i)
-          orow[4 * c + i] = make_uint4(pack_bf16(__uint_as_float(v[8 * i]) * inv, __uint_as_float(v[8 * i + 1]) * inv),
-                                       pack_bf16(__uint_as_float(v[8 * i + 2]) * inv, __uint_as_float(v[8 * i + 3]) * inv),
-                                       pack_bf16(__uint_as_float(v[8 * i + 4]) * inv, __uint_as_float(v[8 * i + 5]) * inv),
-                                       pack_bf16(__uint_as_float(v[8 * i + 6]) * inv, __uint_as_float(v[8 * i + 7]) * inv));
+        for (int i = 0; i < 8; ++i)
+          __stcg(wrow + 8 * c + i, make_float4(__uint_as_float(o[4 * i]), __uint_as_float(o[4 * i + 1]),
+                                               __uint_as_float(o[4 * i + 2]), __uint_as_float(o[4 * i + 3])));
+      }
+      __stcg(ws + 128 * p.d + r, m_used);
+      __stcg(ws + 128 * p.d + 128 + r, l);
+      // two rounds of the softmax warps' merge barrier (bounded waits): all
+      // partial rows written and fenced, then the counter result published
+      __threadfence();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(baddr(&hdr->merge_bar));
+      ok = mbar_wait_bounded(baddr(&hdr->merge_bar), static_cast<uint32_t>(mp & 1), ctl, ST_TIMEOUT_EPILOGUE);
+      ++mp;
+      if (!__all_sync(0xffffffffu, ok)) break;
+      if (r == 0) hdr->merge_flag = atomicAdd(p.counters + cnt, 1) == n_parts - 1 ? 1 : 0;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(baddr(&hdr->merge_bar));
+      ok = mbar_wait_bounded(baddr(&hdr->merge_bar), static_cast<uint32_t>(mp & 1), ctl, ST_TIMEOUT_EPILOGUE);
+      ++mp;
+      if (!__all_sync(0xffffffffu, ok)) break;
+      if (*reinterpret_cast<volatile int*>(&hdr->merge_flag)) {
+        __threadfence();
+        float mk[kAttnMaxParts], wk[kAttnMaxParts];
+#pragma unroll
+        for (int k = 0; k < kAttnMaxParts; ++k)
+          mk[k] = (k < n_parts && k != part) ? __ldcg(base0 + k * slot_floats + 128 * p.d + r) : -INFINITY;
+        float M = m_used;
+#pragma unroll
+        for (int k = 0; k < kAttnMaxParts; ++k) M = fmaxf(M, mk[k]);
+        const float w_self = (M == -INFINITY || m_used == -INFINITY) ? 0.f : exp2f(m_used - M);
+        float Lt = w_self * l;
+#pragma unroll
+        for (int k = 0; k < kAttnMaxParts; ++k) {
+          wk[k] = (M == -INFINITY || mk[k] == -INFINITY) ? 0.f : exp2f(mk[k] - M);
+          if (wk[k] != 0.f) Lt += wk[k] * __ldcg(base0 + k * slot_floats + 128 * p.d + 128 + r);
+        }
+        const float inv = Lt > 0.f ? 1.f / Lt : 0.f;
+#pragma unroll 1
+        for (int c = 0; c < gd; ++c) {
+          uint32_t o[32];
+          tmem_ld_32x32b_x32(t_o + 32u * c, o);
+          tmem_ld_wait();
+          float acc[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) acc[i] = w_self * __uint_as_float(o[i]);
+#pragma unroll 1
+          for (int k = 0; k < n_parts; ++k) {
+            if (wk[k] == 0.f) continue;
+            const float4* src =
+                reinterpret_cast<const float4*>(base0 + k * slot_floats + static_cast<int64_t>(r) * p.d) + 8 * c;
+            float4 t[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) t[i] = __ldcg(src + i);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              acc[4 * i] += wk[k] * t[i].x;
+              acc[4 * i + 1] += wk[k] * t[i].y;
+              acc[4 * i + 2] += wk[k] * t[i].z;
+              acc[4 * i + 3] += wk[k] * t[i].w;
+            }
+          }
+          if (row < p.S) store_row_bf16(orow + 4 * c, acc, inv);
+        }
+        if (r == 0) p.counters[cnt] = 0;  // ready for the next launch
       }
     }
     tc_fence_before();
@@ -403,13 +500,16 @@ __global__ void __launch_bounds__(kAtThreads, 1) attn_tcgen05(const __grid_const
       mbar_init(baddr(&hdr->k_empty[s]), 1);
       mbar_init(baddr(&hdr->v_full[s]), 1);
       mbar_init(baddr(&hdr->v_empty[s]), 1);
-      mbar_init(baddr(&hdr->s_full[s]), 1);
-      mbar_init(baddr(&hdr->s_empty[s]), 4);
-      mbar_init(baddr(&hdr->p_full[s]), 4);
+      mbar_init(baddr(&hdr->p_full[s]), kAtSoftWarps);
       mbar_init(baddr(&hdr->p_empty[s]), 1);
     }
     mbar_init(baddr(&hdr->o_full), 1);
-    mbar_init(baddr(&hdr->o_empty), 4);
+    mbar_init(baddr(&hdr->o_empty), kAtSoftWarps);
+    mbar_init(baddr(&hdr->merge_bar), kAtSoftWarps);
+    for (int b = 0; b < kAtSBuf; ++b) {
+      mbar_init(baddr(&hdr->s_full[b]), 1);
+      mbar_init(baddr(&hdr->s_empty[b]), kAtSoftWarps);
+    }
     mbar_init(baddr(&hdr->drain), 1);
     hdr->abort_flag = 0;
     fence_mbar_init();
@@ -446,7 +546,7 @@ __global__ void __launch_bounds__(kAtThreads, 1) attn_tcgen05(const __grid_const
 
 }  // namespace
 
-int attn_smem_bytes(int d) { return static_cast<int>(2048u + 5u * at_tile(d) + 2u * kAtPBytes); }
+int attn_smem_bytes(int d) { return static_cast<int>(2048u + 5u * at_tile(d)); }
 
 bsp_status launch_attn(const bsp_attn_plan* p, const void* Q, int64_t ldq, const void* K, int64_t ldk,
                        const void* V, int64_t ldv, float scale, void* O, int64_t ldo, cudaStream_t stream) {
@@ -468,6 +568,8 @@ bsp_status launch_attn(const bsp_attn_plan* p, const void* Q, int64_t ldq, const
   kp.units = p->d_units;
   kp.chunks = p->d_chunks;
   kp.cta_begin = p->d_cta_begin;
+  kp.work = p->d_work;
+  kp.counters = p->d_counters;
   kp.o = static_cast<uint16_t*>(O);
   kp.ldo = ldo;
   kp.status = dev->d_status;

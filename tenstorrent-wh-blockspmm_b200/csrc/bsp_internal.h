@@ -204,13 +204,22 @@ struct SpgemmKernelParams {
 // which (block-row, key block) pairs of the chunk the mask holds; the others
 // are masked to -inf before the softmax.
 constexpr int kAttnSlots = 4;
+constexpr int kAttnMaxParts = 16;
+// A unit whose chunk list is much longer than the average CTA's share is cut
+// into parts (consecutive chunk ranges) that run on different CTAs; each part
+// writes its unnormalised O rows, running maxima and row sums to a workspace
+// slot, and the part that finishes last (a counter per unit) merges them.
 struct AttnUnit {
   int32_t row0;          // first query row (multiple of 128)
-  int32_t chunk_begin;   // first chunk record
+  int32_t chunk_begin;   // first chunk record of this part
   int32_t n_chunks;      // 0: no block-row of the unit holds a mask block (O rows = 0)
+  int32_t n_parts;       // parts of the unit (1: not split)
+  int32_t part;          // this part's index
+  int32_t slot0;         // workspace slot of part 0 (parts use slot0 .. slot0 + n_parts - 1)
+  int32_t counter;       // index of the unit's completion counter
   int32_t pad;
 };
-static_assert(sizeof(AttnUnit) == 16, "unit layout");
+static_assert(sizeof(AttnUnit) == 32, "unit layout");
 struct AttnChunk {
   int32_t kb[kAttnSlots];  // key block of each slot, -1 none (zero box)
   uint32_t bits;           // bit 4 q + s: block-row q of the unit holds key block kb[s]
@@ -229,6 +238,8 @@ struct AttnKernelParams {
   int64_t ldo;
   unsigned int* status;
   uint64_t timeout_ns;
+  float* work;           // split units: per slot 128 x d partial O, then 128 maxima, 128 sums
+  int32_t* counters;     // split units: parts finished (the merging part resets it to 0)
   int32_t S, d;
   float scale_log2;      // softmax scale * log2(e)
   int32_t tmem_cols;
@@ -284,12 +295,15 @@ struct bsp_attn_plan {
   int64_t mask_blocks = 0;   // distinct (block-row, key block) pairs (useful work)
   int32_t grid = 0, smem_bytes = 0, tmem_cols = 0;
   int64_t n_units = 0, n_chunks = 0;
+  int64_t n_slots = 0, n_counters = 0;  // workspace slots and counters of split units
   uint64_t timeout_ns = 0;
-  void* d_blob = nullptr;
+  void* d_blob = nullptr;    // units | chunks | cta_begin | counters (zeroed)
   size_t blob_bytes = 0;
+  float* d_work = nullptr;
   bsp::AttnUnit* d_units = nullptr;
   bsp::AttnChunk* d_chunks = nullptr;
   int32_t* d_cta_begin = nullptr;
+  int32_t* d_counters = nullptr;
   std::vector<bsp::AttnUnit> h_units;
   std::vector<bsp::AttnChunk> h_chunks;
   std::vector<int32_t> h_cta_begin;
@@ -402,6 +416,7 @@ bsp_status launch_spgemm(const bsp_spgemm_plan* p, const void* a_vals, const voi
                          void* out_vals, cudaStream_t stream);
 int spgemm_max_stages();
 int spgemm_max_producers();
+void spmm_plan_traffic(const bsp_spmm_plan& p, int64_t out[4]);
 bsp_status plan_attn_host(bsp_attn_plan* p, const int32_t* row_ptr, const int32_t* col_idx,
                           int sm_count, int max_smem, const bsp_spmm_opts* opts);
 bsp_status launch_attn(const bsp_attn_plan* p, const void* Q, int64_t ldq, const void* K, int64_t ldk,

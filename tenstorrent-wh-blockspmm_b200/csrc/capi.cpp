@@ -942,9 +942,11 @@ bsp_status bsp_attn_plan_create(bsp_device* dev, const bsp_bsr_desc* mask, const
     return s;
   }
   std::vector<void*> ptrs;
+  const std::vector<int32_t> zeros(static_cast<size_t>(p->n_counters), 0);
   s = upload_blob({{p->h_units.data(), p->h_units.size() * sizeof(AttnUnit)},
                    {p->h_chunks.data(), p->h_chunks.size() * sizeof(AttnChunk)},
-                   {p->h_cta_begin.data(), p->h_cta_begin.size() * sizeof(int32_t)}},
+                   {p->h_cta_begin.data(), p->h_cta_begin.size() * sizeof(int32_t)},
+                   {zeros.data(), zeros.size() * sizeof(int32_t)}},
                   &p->d_blob, &p->blob_bytes, &ptrs);
   if (s != BSP_OK) {
     delete p;
@@ -953,6 +955,12 @@ bsp_status bsp_attn_plan_create(bsp_device* dev, const bsp_bsr_desc* mask, const
   p->d_units = static_cast<AttnUnit*>(ptrs[0]);
   p->d_chunks = static_cast<AttnChunk*>(ptrs[1]);
   p->d_cta_begin = static_cast<int32_t*>(ptrs[2]);
+  p->d_counters = static_cast<int32_t*>(ptrs[3]);
+  if (p->n_slots > 0 &&
+      cudaMalloc(&p->d_work, sizeof(float) * 128 * (p->d + 2) * p->n_slots) != cudaSuccess) {
+    bsp_attn_plan_destroy(p);
+    return set_error(BSP_ERR_ALLOC, "cudaMalloc of the attention merge workspace failed");
+  }
   *out = p;
   return BSP_OK;
 }
@@ -969,6 +977,7 @@ bsp_status bsp_attn_execute(const bsp_attn_plan* plan, const void* Q, int64_t ld
 bsp_status bsp_attn_plan_destroy(bsp_attn_plan* plan) {
   if (!plan) return BSP_OK;
   if (plan->d_blob) cudaFree(plan->d_blob);
+  if (plan->d_work) cudaFree(plan->d_work);
   delete plan;
   return BSP_OK;
 }
@@ -982,6 +991,8 @@ bsp_status bsp_attn_plan_info(const bsp_attn_plan* p, int64_t info[16]) {
   info[3] = p->mask_blocks;
   info[4] = p->S;
   info[5] = p->d;
+  info[6] = p->n_slots;
+  info[7] = p->n_counters;
   info[8] = static_cast<int64_t>(p->blob_bytes);
   info[9] = p->smem_bytes;
   info[10] = p->tmem_cols;
@@ -1098,6 +1109,27 @@ bsp_status bsp_spmm_plan_inspect(int64_t M, int64_t K, int32_t R, int32_t C, int
     memcpy(stage_list_out, p.h_stage_list.data(), p.h_stage_list.size() * sizeof(int32_t));
   if (cta_stage_begin_out && !p.h_cta_stage_begin.empty())
     memcpy(cta_stage_begin_out, p.h_cta_stage_begin.data(), p.h_cta_stage_begin.size() * sizeof(int32_t));
+  return BSP_OK;
+}
+
+bsp_status bsp_spmm_plan_traffic(int64_t M, int64_t K, int32_t R, int32_t C, int64_t nnzb,
+                                 const int32_t* row_ptr, const int32_t* col_idx, int64_t N,
+                                 bsp_strategy strategy, const bsp_spmm_opts* opts, int32_t sm_count,
+                                 int32_t max_smem, int64_t info[16], int64_t traffic[4]) {
+  if (!row_ptr || !info || !traffic || (nnzb > 0 && !col_idx) || R <= 0 || C <= 0)
+    return set_error(BSP_ERR_INVALID_ARG, "bad arguments");
+  bsp_spmm_plan p;
+  p.M = M;
+  p.K = K;
+  p.N = N;
+  p.R = R;
+  p.C = C;
+  p.nnzb = nnzb;
+  p.strategy = strategy;
+  bsp_status s = plan_spmm_host(&p, row_ptr, col_idx, sm_count, max_smem, opts);
+  if (s != BSP_OK) return s;
+  bsp_spmm_plan_info(&p, info);
+  spmm_plan_traffic(p, traffic);
   return BSP_OK;
 }
 

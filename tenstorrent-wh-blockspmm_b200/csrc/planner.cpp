@@ -96,6 +96,23 @@ static void ordered_greedy(const std::vector<int64_t>& weight, int parts,
   }
 }
 
+// Longest processing time first: items by weight (heaviest first, ties by
+// index), each to the part with the least weight so far; each part's list is
+// then put back in index order.
+static void lpt_order(const std::vector<int64_t>& weight, int parts,
+                      std::vector<std::vector<int32_t>>* per_part) {
+  std::vector<int32_t> order(weight.size());
+  std::iota(order.begin(), order.end(), 0);
+  std::stable_sort(order.begin(), order.end(), [&](int32_t a, int32_t b) { return weight[a] > weight[b]; });
+  std::vector<int64_t> sorted_w(order.size());
+  for (size_t i = 0; i < order.size(); ++i) sorted_w[i] = weight[order[i]];
+  ordered_greedy(sorted_w, parts, per_part);
+  for (auto& v : *per_part) {
+    for (auto& x : v) x = order[x];
+    std::sort(v.begin(), v.end());
+  }
+}
+
 static void contiguous_split(int64_t n, int parts, std::vector<std::vector<int32_t>>* per_part) {
   per_part->assign(parts, {});
   for (int p = 0; p < parts; ++p) {
@@ -1336,7 +1353,7 @@ bsp_status plan_spgemm_host(bsp_spgemm_plan* p, const int32_t* a_rp, const int32
 // the 32 x 32 mask); per unit the sorted union of its block-rows' mask
 // columns (a column repeated within a row counts once) cut into chunks of four
 // key blocks, each with the bits of the (block-row, key block) pairs the mask
-// holds.  Units are dealt in order to the least-loaded CTA.
+// holds.  Units (and parts) are dealt longest first to the least-loaded CTA.
 bsp_status plan_attn_host(bsp_attn_plan* p, const int32_t* row_ptr, const int32_t* col_idx,
                           int sm_count, int max_smem, const bsp_spmm_opts* opts) {
   bsp_spmm_opts o;
@@ -1394,16 +1411,73 @@ bsp_status plan_attn_host(bsp_attn_plan* p, const int32_t* row_ptr, const int32_
       p->h_chunks.push_back(ch);
     }
     u.n_chunks = static_cast<int32_t>(p->h_chunks.size()) - u.chunk_begin;
+    u.n_parts = 1;
+    u.counter = -1;
     p->h_units.push_back(u);
-    weight.push_back(static_cast<int64_t>(u.n_chunks) * 4 + 1);
   }
-  p->n_units = static_cast<int64_t>(p->h_units.size());
   p->n_chunks = static_cast<int64_t>(p->h_chunks.size());
   int grid = o.max_ctas > 0 ? std::min(o.max_ctas, sm_count) : sm_count;
+  // Split units: by default only into CTAs that would otherwise stay idle --
+  // while there are fewer work items than CTAs, the item with the most
+  // chunks is cut into one more part (at most 16), so every CTA runs one
+  // item.  n_tiles > 0 instead cuts every unit into parts of about that many
+  // chunks; group_rows = -1 never splits.
+  std::vector<int64_t> np_of(p->h_units.size(), 1);
+  if (o.group_rows >= 0 && o.n_tiles > 0) {
+    for (size_t i = 0; i < p->h_units.size(); ++i) {
+      const int64_t n = p->h_units[i].n_chunks;
+      if (n > o.n_tiles + o.n_tiles / 4)
+        np_of[i] = std::min<int64_t>(kAttnMaxParts, (n + o.n_tiles - 1) / o.n_tiles);
+    }
+  } else if (o.group_rows >= 0) {
+    int64_t items = static_cast<int64_t>(p->h_units.size());
+    std::vector<std::pair<double, size_t>> heap;  // (chunks per part, unit)
+    for (size_t i = 0; i < p->h_units.size(); ++i) heap.push_back({double(p->h_units[i].n_chunks), i});
+    std::make_heap(heap.begin(), heap.end());
+    while (items < grid && !heap.empty()) {
+      std::pop_heap(heap.begin(), heap.end());
+      auto top = heap.back();
+      heap.pop_back();
+      const size_t i = top.second;
+      const int64_t n = p->h_units[i].n_chunks;
+      if (np_of[i] >= kAttnMaxParts || n < 2 * (np_of[i] + 1) || top.first < 4.0) break;
+      ++np_of[i];
+      ++items;
+      heap.push_back({double(n) / double(np_of[i]), i});
+      std::push_heap(heap.begin(), heap.end());
+    }
+  }
+  std::vector<AttnUnit> parts;
+  p->n_slots = 0;
+  p->n_counters = 0;
+  for (size_t i = 0; i < p->h_units.size(); ++i) {
+    const AttnUnit& u = p->h_units[i];
+    const int64_t np = np_of[i];
+    if (np == 1) {
+      parts.push_back(u);
+      continue;
+    }
+    for (int64_t k = 0; k < np; ++k) {
+      AttnUnit v = u;
+      const int64_t b = u.n_chunks * k / np, e = u.n_chunks * (k + 1) / np;
+      v.chunk_begin = u.chunk_begin + static_cast<int32_t>(b);
+      v.n_chunks = static_cast<int32_t>(e - b);
+      v.n_parts = static_cast<int32_t>(np);
+      v.part = static_cast<int32_t>(k);
+      v.slot0 = static_cast<int32_t>(p->n_slots);
+      v.counter = static_cast<int32_t>(p->n_counters);
+      parts.push_back(v);
+    }
+    p->n_slots += np;
+    ++p->n_counters;
+  }
+  p->h_units.swap(parts);
+  for (const AttnUnit& u : p->h_units) weight.push_back(static_cast<int64_t>(u.n_chunks) * 4 + 1);
+  p->n_units = static_cast<int64_t>(p->h_units.size());
   grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(grid, p->n_units)));
   std::vector<std::vector<int32_t>> per;
   if (o.no_load_balance == 1) contiguous_split(p->n_units, grid, &per);
-  else ordered_greedy(weight, grid, &per);
+  else lpt_order(weight, grid, &per);
   std::vector<AttnUnit> ordered;
   p->h_cta_begin.assign(1, 0);
   for (int c = 0; c < grid; ++c) {
@@ -1416,6 +1490,45 @@ bsp_status plan_attn_host(bsp_attn_plan* p, const int32_t* row_ptr, const int32_
   p->tmem_cols = 512;
   p->timeout_ns = static_cast<uint64_t>(o.timeout_ms > 0 ? o.timeout_ms : 2000) * 1000000ull;
   return BSP_OK;
+}
+
+// Operand bytes a SpMM plan moves with TMA into shared memory (the B200
+// counterpart of the reference's per-core DRAM read counts of in0 = A and
+// in1 = B, block_spmm/scripts/count_dram_reads.py): out[0] A bytes, out[1] B
+// bytes, out[2] A boxes, out[3] B boxes.  Zero boxes for absent blocks read
+// nothing and are not counted.
+void spmm_plan_traffic(const bsp_spmm_plan& p, int64_t out[4]) {
+  out[0] = out[1] = out[2] = out[3] = 0;
+  const int64_t kc = p.kc, Rs = p.Rs;
+  if (p.variant == 0) {
+    const int stride = p.step_stride;
+    const int64_t nkc = p.C / p.kc;
+    for (const SpmmUnit& u : p.h_units)
+      for (int32_t s = u.step_begin; s < u.step_end; ++s) {
+        int64_t present = 0;
+        for (int g = 0; g < p.G; ++g) present += p.h_steps[static_cast<size_t>(s) * stride + 1 + g] >= 0;
+        out[0] += nkc * present * Rs * kc * 2;
+        out[2] += nkc * present;
+        out[1] += nkc * int64_t(u.nt) * kc * kTileN * 2;
+        out[3] += nkc * int64_t(u.nt) * 2;  // two 64-column boxes per 128-column tile
+      }
+    return;
+  }
+  const size_t W = kRsStageWords;
+  const int64_t b_cols = p.variant == 2 ? 128 : 256;  // a pair CTA loads half of the 256 columns
+  for (size_t k = 0; k + W <= p.h_stage_list.size(); k += W) {
+    const uint32_t flags = static_cast<uint32_t>(p.h_stage_list[k]);
+    if (flags & RS_F_EMPTY) continue;
+    const int nsub = (flags & RS_F_TWO) ? 2 : 1;
+    out[1] += nsub * kc * b_cols * 2;
+    out[3] += nsub * (b_cols / 64);
+    for (int sub = 0; sub < nsub; ++sub)
+      for (int g = 0; g < 4; ++g)
+        if (p.h_stage_list[k + 5 + 4 * sub + g] >= 0) {
+          out[0] += Rs * kc * 2;
+          out[2] += 1;
+        }
+  }
 }
 
 }  // namespace bsp

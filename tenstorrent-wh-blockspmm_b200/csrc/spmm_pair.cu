@@ -132,6 +132,16 @@ __device__ __forceinline__ void pr_producer(const SpmmKernelParams& p, RsSmemHea
     for (int s = 0; s < p.stages; ++s)
       if (armed & (1u << s)) rs_drain_wait(baddr(&hdr->full[s]), (armed_parity >> s) & 1u, ctl);
   }
+  // Every slot this warp filled is released by the leader's MMA warp with a
+  // multicast arrive on this CTA's empty barrier; wait for the last of those
+  // arrives, so that none is still in flight towards this CTA's shared
+  // memory when the CTA exits (it would land in the next launch's CTA on
+  // this SM).
+  if (lane == 0) {
+#pragma unroll 1
+    for (int s = 0; s < p.stages; ++s)
+      if (armed & (1u << s)) rs_drain_wait(baddr(&hdr->empty[s]), (armed_parity >> s) & 1u, ctl);
+  }
   __syncwarp();
 }
 
@@ -183,10 +193,25 @@ __device__ __forceinline__ void pr_mma(const SpmmKernelParams& p, RsSmemHeader* 
         for (int k = 0; k < kKS; ++k)
           mma_bf16_pair_pred(d0, ad + sub16 + k * 2u, bd + sub16 + k * 128u, idesc, 1u, is0);
       }
+      mma_commit_pair_both_pred(empty0 + stage * 8, is0);
+      if (info & RS_LAST) mma_commit_pair_both_pred(baddr(&hdr->acc_full[acc]), is0);
+    } else if (lane == 0) {
+      // A stage (and unit) without blocks has nothing in shared memory and
+      // nothing in TMEM to wait for: release it with plain arrives on both
+      // CTAs' barriers.  A 2-SM commit is not used here -- with no pair MMA
+      // issued before it (a pair whose first units are empty) its multicast
+      // arrive was not reliably delivered on B200.
+      const uint32_t e_local = empty0 + stage * 8;
+      mbar_arrive(e_local);
+      mbar_remote_arrive(mapa_shared(e_local, 1));
+      if (info & RS_LAST) {
+        const uint32_t f_local = baddr(&hdr->acc_full[acc]);
+        mbar_arrive(f_local);
+        mbar_remote_arrive(mapa_shared(f_local, 1));
+      }
     }
-    mma_commit_pair_both_pred(empty0 + stage * 8, is0);
+    __syncwarp();
     if (info & RS_LAST) {
-      mma_commit_pair_both_pred(baddr(&hdr->acc_full[acc]), is0);
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1u;
       --units_left;

@@ -6,6 +6,7 @@
 // error <= 1e-2 bar of this library.
 //
 // Usage: test_host_code [device]   (exit code = number of failed cases)
+#include <algorithm>
 #include <cmath>
 #include <cstdio>
 #include <string>
@@ -134,6 +135,84 @@ int main(int argc, char** argv) {
       }
     }
   }
+  // SpGEMM (bsr_matrix::spgemm on the GPU) against the oracle's restatement
+  {
+    struct G { size_t Ha, Wa, Wb, Ra, Ca, Cb, na, nb; int fa, fb; const char* name; };
+    const G gs[] = {{512, 512, 512, 32, 32, 32, 40, 40, FILL_MULTI_DIAG, FILL_MULTI_DIAG, "multi_diag x multi_diag"},
+                    {256, 512, 384, 64, 32, 64, 20, 30, FILL_ROW, FILL_COL, "row x col"},
+                    {512, 512, 256, 32, 32, 32, 16, 8, FILL_DIAG, FILL_DIAG, "diag x diag"}};
+    for (const auto& g : gs) {
+      srand(21);
+      bsr_matrix<float> af(g.Ha, g.Wa, g.Ra, g.Ca, g.na, g.fa, RAND);
+      bsr_matrix<float> bf(g.Wa, g.Wb, g.Ca, g.Cb, g.nb, g.fb, RAND);
+      auto a = af.bfloat16_cast();
+      auto b = bf.bfloat16_cast();
+      bsr_matrix<bfloat16> c = bsp::spgemm(a, b, device);
+      std::vector<int32_t> rp(g.Ha / g.Ra + 1);
+      const int64_t n = bsp_oracle_spgemm_symbolic(g.Ha / g.Ra, g.Wb / g.Cb, a.indptr.data(), a.indices.data(),
+                                                   b.indptr.data(), b.indices.data(), rp.data(), nullptr);
+      std::vector<int32_t> ci(static_cast<size_t>(n));
+      bsp_oracle_spgemm_symbolic(g.Ha / g.Ra, g.Wb / g.Cb, a.indptr.data(), a.indices.data(), b.indptr.data(),
+                                 b.indices.data(), rp.data(), ci.data());
+      std::vector<uint16_t> gold(static_cast<size_t>(n) * g.Ra * g.Cb);
+      const auto av = bits(a.data), bv = bits(b.data);
+      bsp_oracle_spgemm_bf16(g.Ha / g.Ra, g.Ra, g.Ca, g.Cb, a.indptr.data(), a.indices.data(), av.data(),
+                             b.indptr.data(), b.indices.data(), bv.data(), rp.data(), ci.data(), gold.data());
+      const bool pattern = c.nblocks == static_cast<size_t>(n) &&
+                           std::equal(rp.begin(), rp.end(), c.indptr.begin()) &&
+                           std::equal(ci.begin(), ci.end(), c.indices.begin());
+      const Scores s = gold.empty() ? Scores{1.0, 0.0} : compare(c.data, gold);
+      const bool ok = pattern && s.pcc >= 0.99 && s.max_rel <= 1e-2;
+      failures += !ok;
+      std::printf("%s %-48s %-24s pcc=%.6f max_rel=%.3e blocks=%lld\n", ok ? "PASS" : "FAIL", "bsp::spgemm", g.name,
+                  s.pcc, s.max_rel, static_cast<long long>(n));
+    }
+  }
+
+  // Fused attention step against a float reference computed here
+  {
+    const int S = 256, d = 64;
+    srand(5);
+    bsr_matrix<float> mf(S, S, 32, 32, 20, FILL_MULTI_DIAG, UNIFORM);
+    dense_matrix<float> qf(S, d, RAND), kf(S, d, RAND), vf(S, d, RAND);
+    auto mask = mf.bfloat16_cast();
+    auto q = qf.bfloat16_cast();
+    auto k = kf.bfloat16_cast();
+    auto v = vf.bfloat16_cast();
+    const float scale = 0.125f;
+    dense_matrix<bfloat16> o = bsp::attention_step(mask, q, k, v, scale, device);
+    double err = 0, ref = 0;
+    for (int i = 0; i < S; ++i) {
+      const int bi = i / 32;
+      std::vector<double> sc;
+      std::vector<int> keys;
+      for (int b = mask.indptr[bi]; b < mask.indptr[bi + 1]; ++b)
+        for (int t = 0; t < 32; ++t) {
+          const int key = mask.indices[b] * 32 + t;
+          double dot = 0;
+          for (int c = 0; c < d; ++c) dot += double(q.data[i * d + c].to_float()) * k.data[key * d + c].to_float();
+          sc.push_back(dot * scale);
+          keys.push_back(key);
+        }
+      double mx = -1e300, sum = 0;
+      for (double x : sc) mx = std::max(mx, x);
+      for (double& x : sc) sum += (x = std::exp(x - mx));
+      for (int c = 0; c < d; ++c) {
+        double acc = 0;
+        for (size_t t = 0; t < keys.size(); ++t) acc += sc[t] / sum * v.data[keys[t] * d + c].to_float();
+        if (keys.empty()) acc = 0;
+        const double got = o.data[i * d + c].to_float();
+        err += (got - acc) * (got - acc);
+        ref += acc * acc;
+      }
+    }
+    const double rel = ref > 0 ? std::sqrt(err / ref) : std::sqrt(err);
+    const bool ok = rel <= 1e-2;
+    failures += !ok;
+    std::printf("%s %-48s %-24s normwise=%.3e\n", ok ? "PASS" : "FAIL", "bsp::attention_step", "multi_diag S=256",
+                rel);
+  }
+
   bsp::CloseDevice(device);
   std::printf("%d failure(s)\n", failures);
   return failures;

@@ -30,17 +30,19 @@ def bf16_round(x):
 
 
 def emulate(plan, S, d, Q, K, V, scale):
+    """The kernel's algorithm over the planned schedule (float64): per unit or
+    part, S per chunk, masking by the chunk bits, the lazily moved running
+    maximum, bf16 P, O += P V; unsplit units normalise, split units merge
+    their parts' (O, m, l) the way the last part does."""
     Qf = oracle.bf16_to_f32(Q).reshape(S, d).astype(np.float64)
     Kf = oracle.bf16_to_f32(K).reshape(S, d).astype(np.float64)
     Vf = oracle.bf16_to_f32(V).reshape(S, d).astype(np.float64)
     O = np.zeros((S, d))
     written = np.zeros(S, np.int32)
     sl2 = scale * np.log2(np.e)
-    for row0, cb, n, _ in plan["unit_table"]:
+    partials = {}
+    for row0, cb, n, n_parts, part, slot0, counter, _ in plan["unit_table"]:
         rows = np.arange(row0, min(row0 + 128, S))
-        written[rows] += 1
-        if n == 0:
-            continue
         m = np.full(rows.size, -np.inf)
         lsum = np.zeros(rows.size)
         acc = np.zeros((rows.size, d))
@@ -71,8 +73,24 @@ def emulate(plan, S, d, Q, K, V, scale):
             p = bf16_round(p).astype(np.float64)
             lsum += p.sum(axis=1)
             acc += p @ Vc
-        inv = np.where(lsum > 0, 1.0 / np.where(lsum > 0, lsum, 1), 0.0)
-        O[rows] = acc * inv[:, None]
+        if n_parts == 1:
+            inv = np.where(lsum > 0, 1.0 / np.where(lsum > 0, lsum, 1), 0.0)
+            O[rows] = acc * inv[:, None]
+            written[rows] += 1
+            continue
+        partials.setdefault(counter, []).append((part, rows, acc, m, lsum))
+        if len(partials[counter]) == n_parts:
+            parts = sorted(partials.pop(counter), key=lambda t: t[0])
+            assert [t[0] for t in parts] == list(range(n_parts))
+            M = np.max([t[3] for t in parts], axis=0)
+            with np.errstate(invalid="ignore"):
+                w = [np.where(np.isneginf(M) | np.isneginf(t[3]), 0.0, np.exp2(t[3] - M)) for t in parts]
+            L = sum(wk * t[4] for wk, t in zip(w, parts))
+            acc = sum(wk[:, None] * t[2] for wk, t in zip(w, parts))
+            inv = np.where(L > 0, 1.0 / np.where(L > 0, L, 1), 0.0)
+            O[rows] = acc * inv[:, None]
+            written[rows] += 1
+    assert not partials
     assert np.all(written == 1)
     return O
 
@@ -80,7 +98,17 @@ def emulate(plan, S, d, Q, K, V, scale):
 def check_schedule(plan, S, rp, ci):
     nbr = S // 32
     seen = set()
-    for row0, cb, n, _ in plan["unit_table"]:
+    units = {}
+    for row0, cb, n, n_parts, part, slot0, counter, _ in plan["unit_table"]:
+        units.setdefault(row0, []).append((part, cb, n, n_parts))
+    assert len(units) == (nbr + 3) // 4
+    for row0, pieces in units.items():
+        pieces.sort()
+        assert [p_[0] for p_ in pieces] == list(range(len(pieces)))
+        assert all(p_[3] == len(pieces) for p_ in pieces) and len(pieces) <= 16
+        for a, b in zip(pieces, pieces[1:]):
+            assert a[1] + a[2] == b[1]            # consecutive chunk ranges
+        cb, n = pieces[0][1], sum(p_[2] for p_ in pieces)
         union = sorted({int(c) for i in range(row0 // 32, min(row0 // 32 + 4, nbr))
                         for c in ci[rp[i]:rp[i + 1]]})
         kbs = [int(k) for ch in plan["chunk_table"][cb:cb + n] for k in ch[:4] if k >= 0]
@@ -133,6 +161,37 @@ def test_rescale_path_matches():
     plan = bsp.inspect_attn_plan(S, d, rp, ci)
     got = emulate(plan, S, d, Q, K, V, 1.0)
     gold = oracle.bf16_to_f32(oracle.attention_bf16(rp, ci, S, d, Q, K, V, 1.0)).reshape(S, d)
+    assert np.linalg.norm(got - gold) / np.linalg.norm(gold) < 1e-2
+
+
+def heavy_mask(rng, nbr):
+    """Block-rows 0..3 hold every column; the others a sparse band."""
+    rows = [list(range(nbr)) if i < 4 else sorted({max(0, i - 1), i, min(nbr - 1, i + 1)}
+                                                  | set(rng.integers(0, nbr, 2).tolist()))
+            for i in range(nbr)]
+    rp = np.concatenate([[0], np.cumsum([len(r) for r in rows])]).astype(np.int32)
+    return rp, np.array([c for r in rows for c in r], np.int32)
+
+
+@pytest.mark.parametrize("opts,split", [(dict(), True), (dict(n_tiles=1), True), (dict(n_tiles=3), True),
+                                        (dict(group_rows=-1), False)])
+def test_split_units_schedule_and_merge(opts, split):
+    """A heavy unit (or a short part length) is cut into parts; the emulated
+    parts merged the way the kernel merges them match the oracle."""
+    rng = np.random.default_rng(9)
+    S, d = 2048, 64
+    rp, ci = heavy_mask(rng, S // 32)
+    plan = bsp.inspect_attn_plan(S, d, rp, ci, opts=bsp.make_opts(**opts))
+    check_schedule(plan, S, rp, ci)
+    assert (plan["parts"] > 0 and plan["split_units"] > 0) == split
+    if split and not opts:
+        heavy = [u for u in plan["unit_table"] if u[0] == 0]
+        assert len(heavy) > 1                      # the 16-chunk unit runs as parts
+    Q = oracle.f32_to_bf16(rng.normal(0, 1, (S, d)).astype(np.float32))
+    K = oracle.f32_to_bf16(rng.normal(0, 1, (S, d)).astype(np.float32))
+    V = oracle.f32_to_bf16(rng.normal(0, 1, (S, d)).astype(np.float32))
+    got = emulate(plan, S, d, Q, K, V, 0.125)
+    gold = oracle.bf16_to_f32(oracle.attention_bf16(rp, ci, S, d, Q, K, V, 0.125)).reshape(S, d)
     assert np.linalg.norm(got - gold) / np.linalg.norm(gold) < 1e-2
 
 

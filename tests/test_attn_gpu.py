@@ -96,7 +96,7 @@ def test_attention_repeated_columns_and_device_api():
     dev = bsp.device(0)
     plan = bsp.AttnPlan(dev, mask, d)
     info = plan.info()
-    assert info["units"] == S // 128 and info["chunks"] > 0
+    assert info["units"] >= S // 128 and info["chunks"] > 0
     # strided Q (leading dimension 2 d) exercises the tensor-map pitch
     Qw = torch.zeros((S, 2 * d), dtype=torch.bfloat16, device="cuda")
     Qw[:, :d] = bsp.to_device_bf16(Q).view(S, d)
@@ -129,3 +129,53 @@ def test_attention_config4_shape_slab():
         o = out.reshape(S, d)[32 * r0:32 * r1]
         g = gold.reshape(S, d)[32 * r0:32 * r1]
         check(o, g, 32 * (r1 - r0), d, f"config 4 rows {r0}..{r1}")
+
+
+def heavy_mask(rng, nbr):
+    rows = [list(range(nbr)) if i < 4 else sorted({max(0, i - 1), i, min(nbr - 1, i + 1)}
+                                                  | set(rng.integers(0, nbr, 2).tolist()))
+            for i in range(nbr)]
+    rp = np.concatenate([[0], np.cumsum([len(r) for r in rows])]).astype(np.int32)
+    return rp, np.array([c for r in rows for c in r], np.int32)
+
+
+@pytest.mark.parametrize("opts", [dict(), dict(n_tiles=1), dict(n_tiles=3, max_ctas=7), dict(group_rows=-1)])
+def test_attention_split_units(opts):
+    """Heavy units run as parts on several CTAs and are merged by the last
+    part; the same plan launched three times (the merge counters reset)."""
+    import bsp
+    import torch
+
+    rng = np.random.default_rng(17)
+    S, d = 4096, 128
+    rp, ci = heavy_mask(rng, S // 32)
+    Q, K, V = qkv(rng, S, d)
+    mask = bsp.DeviceBSR.from_host(S, S, 32, 32, rp, ci, None)
+    dev = bsp.device(0)
+    plan = bsp.AttnPlan(dev, mask, d, bsp.make_opts(**opts))
+    info = plan.info()
+    assert (info["parts"] > 0) == (opts.get("group_rows") != -1)
+    Qd, Kd, Vd = (bsp.to_device_bf16(x).view(S, d) for x in (Q, K, V))
+    gold = oracle.attention_bf16(rp, ci, S, d, Q, K, V, 1 / np.sqrt(d))
+    for it in range(3):
+        O = torch.full((S, d), float("nan"), dtype=torch.bfloat16, device="cuda")
+        plan.execute(Qd, Kd, Vd, O)
+        dev.synchronize()
+        check(bsp.to_host_bits(O), gold, S, d, f"split {opts} launch {it}")
+    plan.close()
+
+
+def test_attention_huge_scores_stay_finite():
+    """Scores near 1e13 (one fp32 ulp far above 2^8): the kernel's exponents
+    are rounded like its running maximum, so nothing overflows."""
+    import bsp
+
+    rng = np.random.default_rng(23)
+    S, d = 256, 64
+    rp, ci = rand_mask(rng, S // 32, 0.4)
+    Q, K, V = (oracle.f32_to_bf16(rng.uniform(-5e5, 5e5, (S, d)).astype(np.float32)) for _ in range(3))
+    out = bsp.attn_host(S, d, rp, ci, Q, K, V, 0.125)
+    gold = oracle.attention_bf16(rp, ci, S, d, Q, K, V, 0.125)
+    o = oracle.bf16_to_f32(out)
+    assert np.all(np.isfinite(o))
+    check(out, gold, S, d, "huge scores")

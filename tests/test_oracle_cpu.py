@@ -127,6 +127,21 @@ def test_spgemm_oracle_closed_form():
     assert np.array_equal(orp, brp) and np.array_equal(oci, bci) and np.array_equal(out, bv)
 
 
+@pytest.mark.skipif(not oracle.ref_available(), reason="reference golden not built here")
+def test_attention_chain_restatement_matches_reference_goldens():
+    """The attention chain through the restated goldens equals the chain
+    through the reference's own compiled goldens, bit for bit."""
+    rng = np.random.default_rng(12)
+    S, d = 256, 64
+    occ = rng.random((S // 32, S // 32)) < 0.4
+    rp = np.concatenate([[0], np.cumsum(occ.sum(1))]).astype(np.int32)
+    ci = np.nonzero(occ)[1].astype(np.int32)
+    Q, K, V = (oracle.f32_to_bf16(rng.normal(0, 1, (S, d)).astype(np.float32)) for _ in range(3))
+    a = oracle.attention_bf16(rp, ci, S, d, Q, K, V, 0.125)
+    b = oracle.attention_bf16(rp, ci, S, d, Q, K, V, 0.125, use_ref=True)
+    assert np.array_equal(a, b)
+
+
 def test_bf16_rounding_is_nearest_even():
     x = np.array([1.0, 1.0 + 2 ** -8, 1.0 + 3 * 2 ** -8, -2.5, np.inf, 3.0e38], np.float32)
     b = oracle.f32_to_bf16(x)

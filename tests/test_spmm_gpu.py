@@ -225,3 +225,36 @@ def test_spmm_rejects_bad_arguments():
     A2 = bsp.DeviceBSR.from_host(M, K, R, C, rp2, np.array([99], np.int32), np.zeros(R * C, np.uint16))
     with pytest.raises(bsp.BspError):
         bsp.SpmmPlan(bsp.device(), A2, 128, bsp.NAIVE)  # column index out of range
+
+
+@pytest.mark.parametrize("R,nonempty_rows,no_lb", [(64, 1, 0), (64, 1, 1), (256, 2, 1), (32, 3, 0)])
+def test_pair_kernel_empty_first_units(R, nonempty_rows, no_lb):
+    """CTA pairs whose lists start with (or are only) units without blocks:
+    their stages are released by plain arrives, not by a 2-SM commit with no
+    MMA before it; twenty launches each must finish and match the oracle."""
+    import bsp
+    import torch
+
+    rng = np.random.default_rng(R + nonempty_rows)
+    M = K = 2048
+    N = 512
+    nb = M // R
+    occ = np.zeros((nb, K // R), bool)
+    occ[:nonempty_rows] = rng.random((nonempty_rows, K // R)) < 0.8
+    rp = np.concatenate([[0], np.cumsum(occ.sum(1))]).astype(np.int32)
+    ci = np.nonzero(occ)[1].astype(np.int32)
+    vals = rand_dense(rng, ci.size * R, R).ravel()
+    B = rand_dense(rng, K, N)
+    gold = oracle.spmm_bf16(rp, ci, vals, M, K, R, R, B, N)
+    A = bsp.DeviceBSR.from_host(M, K, R, R, rp, ci, vals)
+    Bd = bsp.to_device_bf16(B)
+    C = torch.empty((M, N), dtype=torch.bfloat16, device="cuda")
+    dev = bsp.device(0)
+    plan = bsp.SpmmPlan(dev, A, N, bsp.DDA, bsp.BF16, bsp.make_opts(group_mma=5, no_load_balance=no_lb, timeout_ms=500))
+    assert plan.info()["variant"] == 2
+    for _ in range(20):
+        C.fill_(float("nan"))
+        plan.execute(A, Bd, C)
+        dev.synchronize()
+        assert_bf16_close(bsp.to_host_bits(C), gold, what=f"pair R={R}")
+    plan.close()

@@ -13,7 +13,9 @@ from helpers import assert_bf16_close, normwise
 pytestmark = pytest.mark.gpu
 
 GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
-FIXTURES = sorted(glob.glob(os.path.join(GOLDEN, "*.npz")))
+# SpMM and SDDMM fixtures (the SpGEMM ones are checked by test_spgemm_gpu.py)
+FIXTURES = sorted(f for f in glob.glob(os.path.join(GOLDEN, "*.npz"))
+                  if os.path.basename(f).startswith(("spmm_", "sddmm_")))
 
 
 @pytest.mark.parametrize("path", FIXTURES, ids=[os.path.basename(f)[:-4] for f in FIXTURES])

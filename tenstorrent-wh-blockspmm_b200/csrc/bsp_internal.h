@@ -264,6 +264,14 @@ struct bsp_device {
   size_t ws_bytes = 0;
   void* pinned = nullptr;
   size_t pinned_bytes = 0;
+  // host-buffer entry points: plan tables of their temporary plans (device
+  // area + pinned staging, grow-only) and copy / compute streams
+  void* plan_ws = nullptr;
+  size_t plan_ws_bytes = 0;
+  void* aux_ws = nullptr;   // attention merge workspace of host-buffer plans
+  size_t aux_ws_bytes = 0;
+  cudaStream_t s_h2d = nullptr, s_comp = nullptr, s_d2h = nullptr;
+  std::vector<cudaEvent_t> ev_in, ev_out;
 };
 
 struct bsp_spgemm_plan {
@@ -279,6 +287,7 @@ struct bsp_spgemm_plan {
   uint64_t timeout_ns = 0;
   void* d_blob = nullptr;    // units | steps | cta_begin
   size_t blob_bytes = 0;
+  bool blob_borrowed = false;  // tables live in the device's plan area (host-buffer path)
   bsp::SpgemmUnit* d_units = nullptr;
   bsp::SpgemmStep* d_steps = nullptr;
   int32_t* d_cta_begin = nullptr;
@@ -299,6 +308,7 @@ struct bsp_attn_plan {
   uint64_t timeout_ns = 0;
   void* d_blob = nullptr;    // units | chunks | cta_begin | counters (zeroed)
   size_t blob_bytes = 0;
+  bool blob_borrowed = false;  // tables and merge workspace belong to the device (host-buffer path)
   float* d_work = nullptr;
   bsp::AttnUnit* d_units = nullptr;
   bsp::AttnChunk* d_chunks = nullptr;
@@ -324,6 +334,7 @@ struct bsp_spmm_plan {
   uint64_t timeout_ns = 0;
   void* d_blob = nullptr;  // units | cta_begin | steps
   size_t blob_bytes = 0;
+  bool blob_borrowed = false;  // tables live in the device's plan area (host-buffer path)
   bsp::SpmmUnit* d_units = nullptr;
   int32_t* d_cta_begin = nullptr;
   int32_t* d_steps = nullptr;
@@ -355,6 +366,7 @@ struct bsp_sddmm_plan {
   uint64_t timeout_ns = 0;
   void* d_blob = nullptr;
   size_t blob_bytes = 0;
+  bool blob_borrowed = false;  // tables live in the device's plan area (host-buffer path)
   bsp::SddmmUnit* d_units = nullptr;
   int32_t* d_cta_begin = nullptr;
   std::vector<bsp::SddmmUnit> h_units;
@@ -404,8 +416,9 @@ int rowstack_max_stages();
 bsp_status launch_spmm_rowstack(const bsp_spmm_plan* p, const bsp_bsr_desc* A, const void* B,
                                 int64_t ldb, void* C, int64_t ldc, cudaStream_t stream,
                                 void* const* peer_c = nullptr, int n_peers = 0);
+// stage_lists false: units and per-CTA stage counts only (h_stage_list empty)
 bsp_status plan_spmm_pair(bsp_spmm_plan* p, const int32_t* row_ptr, const int32_t* col_idx,
-                          int sm_count, int max_smem, const bsp_spmm_opts* opts);
+                          int sm_count, int max_smem, const bsp_spmm_opts* opts, bool stage_lists = true);
 bsp_status launch_spmm_pair(const bsp_spmm_plan* p, const bsp_bsr_desc* A, const void* B, int64_t ldb,
                             void* C, int64_t ldc, cudaStream_t stream, void* const* peer_c = nullptr,
                             int n_peers = 0);
@@ -424,5 +437,5 @@ bsp_status launch_attn(const bsp_attn_plan* p, const void* Q, int64_t ldq, const
                        cudaStream_t stream);
 int attn_smem_bytes(int d);
 bsp_status plan_spmm_rowstack(bsp_spmm_plan* p, const int32_t* row_ptr, const int32_t* col_idx,
-                              int sm_count, int max_smem, const bsp_spmm_opts* opts);
+                              int sm_count, int max_smem, const bsp_spmm_opts* opts, bool stage_lists = true);
 }  // namespace bsp

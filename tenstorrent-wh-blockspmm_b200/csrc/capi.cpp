@@ -145,6 +145,68 @@ static bsp_status upload_blob(const std::vector<std::pair<const void*, size_t>>&
   return BSP_OK;
 }
 
+// Plan tables of a temporary plan of the host-buffer path: packed into the
+// device's pinned staging and copied on `stream` into its plan area, both
+// grow-only, so no per-call allocation, free or synchronous copy.  The caller
+// synchronises before the next host-buffer call reuses them.
+static bsp_status upload_blob_borrowed(bsp_device* dev,
+                                       const std::vector<std::pair<const void*, size_t>>& parts,
+                                       cudaStream_t stream, void** blob, size_t* bytes,
+                                       std::vector<void*>* ptrs) {
+  size_t total = 0;
+  for (auto& pr : parts) total += align256(pr.second);
+  total = std::max<size_t>(total, 256);
+  if (dev->plan_ws_bytes < total) {
+    if (dev->plan_ws) cudaFree(dev->plan_ws);
+    dev->plan_ws = nullptr;
+    dev->plan_ws_bytes = 0;
+    if (cudaMalloc(&dev->plan_ws, total) != cudaSuccess)
+      return set_error(BSP_ERR_ALLOC, "cudaMalloc of the plan-table area failed");
+    dev->plan_ws_bytes = total;
+  }
+  if (dev->pinned_bytes < total) {
+    if (dev->pinned) cudaFreeHost(dev->pinned);
+    dev->pinned = nullptr;
+    dev->pinned_bytes = 0;
+    if (cudaHostAlloc(&dev->pinned, total, cudaHostAllocDefault) != cudaSuccess)
+      return set_error(BSP_ERR_ALLOC, "cudaHostAlloc of the plan-table staging failed");
+    dev->pinned_bytes = total;
+  }
+  uint8_t* h = static_cast<uint8_t*>(dev->pinned);
+  size_t off = 0;
+  ptrs->clear();
+  for (auto& pr : parts) {
+    if (pr.second) memcpy(h + off, pr.first, pr.second);
+    ptrs->push_back(static_cast<uint8_t*>(dev->plan_ws) + off);
+    off += align256(pr.second);
+  }
+  bsp_status st = cuda_check(cudaMemcpyAsync(dev->plan_ws, h, total, cudaMemcpyHostToDevice, stream),
+                             "upload plan tables");
+  if (st != BSP_OK) return st;
+  *blob = dev->plan_ws;
+  *bytes = total;
+  return BSP_OK;
+}
+
+// Copy / compute streams and events of the host-buffer path (created once).
+static bsp_status host_streams(bsp_device* dev, size_t n_events) {
+  if (!dev->s_h2d) {
+    bsp_status s = cuda_check(cudaStreamCreateWithFlags(&dev->s_h2d, cudaStreamNonBlocking), "cudaStreamCreate");
+    if (s == BSP_OK) s = cuda_check(cudaStreamCreateWithFlags(&dev->s_comp, cudaStreamNonBlocking), "cudaStreamCreate");
+    if (s == BSP_OK) s = cuda_check(cudaStreamCreateWithFlags(&dev->s_d2h, cudaStreamNonBlocking), "cudaStreamCreate");
+    if (s != BSP_OK) return s;
+  }
+  while (dev->ev_in.size() < n_events) {
+    cudaEvent_t a = nullptr, b = nullptr;
+    bsp_status s = cuda_check(cudaEventCreateWithFlags(&a, cudaEventDisableTiming), "cudaEventCreate");
+    if (s == BSP_OK) s = cuda_check(cudaEventCreateWithFlags(&b, cudaEventDisableTiming), "cudaEventCreate");
+    if (s != BSP_OK) return s;
+    dev->ev_in.push_back(a);
+    dev->ev_out.push_back(b);
+  }
+  return BSP_OK;
+}
+
 static bsp_status ws_reserve(bsp_device* dev, size_t bytes) {
   if (dev->ws_bytes >= bytes) return BSP_OK;
   if (dev->ws) cudaFree(dev->ws);
@@ -222,6 +284,13 @@ bsp_status bsp_device_close(bsp_device* dev) {
   if (dev->d_status) cudaFree(dev->d_status);
   if (dev->ws) cudaFree(dev->ws);
   if (dev->pinned) cudaFreeHost(dev->pinned);
+  if (dev->plan_ws) cudaFree(dev->plan_ws);
+  if (dev->aux_ws) cudaFree(dev->aux_ws);
+  for (cudaEvent_t e : dev->ev_in) cudaEventDestroy(e);
+  for (cudaEvent_t e : dev->ev_out) cudaEventDestroy(e);
+  if (dev->s_h2d) cudaStreamDestroy(dev->s_h2d);
+  if (dev->s_comp) cudaStreamDestroy(dev->s_comp);
+  if (dev->s_d2h) cudaStreamDestroy(dev->s_d2h);
   delete dev;
   return BSP_OK;
 }
@@ -250,10 +319,25 @@ bsp_status bsp_device_synchronize(bsp_device* dev) {
 }
 
 // ---------------------------------------------------------------- SpMM ----
+// Plan creation; `borrow` (host-buffer path only) keeps the tables in the
+// device's plan area, uploaded on `stream`.
+static bsp_status spmm_plan_create_impl(bsp_device* dev, const bsp_bsr_desc* A, const int32_t* host_row_ptr,
+                                        const int32_t* host_col_idx, int64_t N, bsp_dtype c_type,
+                                        bsp_strategy strategy, const bsp_spmm_opts* opts, bool borrow,
+                                        cudaStream_t stream, bsp_spmm_plan** out);
+
 bsp_status bsp_spmm_plan_create(bsp_device* dev, const bsp_bsr_desc* A, const int32_t* host_row_ptr,
                                 const int32_t* host_col_idx, int64_t N, bsp_dtype c_type,
                                 bsp_strategy strategy, const bsp_spmm_opts* opts,
                                 bsp_spmm_plan** out) {
+  return spmm_plan_create_impl(dev, A, host_row_ptr, host_col_idx, N, c_type, strategy, opts, false, nullptr,
+                               out);
+}
+
+static bsp_status spmm_plan_create_impl(bsp_device* dev, const bsp_bsr_desc* A, const int32_t* host_row_ptr,
+                                        const int32_t* host_col_idx, int64_t N, bsp_dtype c_type,
+                                        bsp_strategy strategy, const bsp_spmm_opts* opts, bool borrow,
+                                        cudaStream_t stream, bsp_spmm_plan** out) {
   if (!dev || !out) return set_error(BSP_ERR_INVALID_ARG, "null argument");
   *out = nullptr;
   bsp_status s = check_desc(A, false);
@@ -281,12 +365,15 @@ bsp_status bsp_spmm_plan_create(bsp_device* dev, const bsp_bsr_desc* A, const in
     return s;
   }
   std::vector<void*> ptrs;
-  s = upload_blob({{p->h_units.data(), p->h_units.size() * sizeof(SpmmUnit)},
-                   {p->h_cta_begin.data(), p->h_cta_begin.size() * sizeof(int32_t)},
-                   {p->h_steps.data(), p->h_steps.size() * sizeof(int32_t)},
-                   {p->h_stage_list.data(), p->h_stage_list.size() * sizeof(int32_t)},
-                   {p->h_cta_stage_begin.data(), p->h_cta_stage_begin.size() * sizeof(int32_t)}},
-                  &p->d_blob, &p->blob_bytes, &ptrs);
+  const std::vector<std::pair<const void*, size_t>> parts = {
+      {p->h_units.data(), p->h_units.size() * sizeof(SpmmUnit)},
+      {p->h_cta_begin.data(), p->h_cta_begin.size() * sizeof(int32_t)},
+      {p->h_steps.data(), p->h_steps.size() * sizeof(int32_t)},
+      {p->h_stage_list.data(), p->h_stage_list.size() * sizeof(int32_t)},
+      {p->h_cta_stage_begin.data(), p->h_cta_stage_begin.size() * sizeof(int32_t)}};
+  s = borrow ? upload_blob_borrowed(dev, parts, stream, &p->d_blob, &p->blob_bytes, &ptrs)
+             : upload_blob(parts, &p->d_blob, &p->blob_bytes, &ptrs);
+  p->blob_borrowed = borrow;
   if (s != BSP_OK) {
     delete p;
     return s;
@@ -391,7 +478,7 @@ bsp_status bsp_ipc_close(bsp_device* dev, void* base) {
 
 bsp_status bsp_spmm_plan_destroy(bsp_spmm_plan* plan) {
   if (!plan) return BSP_OK;
-  if (plan->d_blob) cudaFree(plan->d_blob);
+  if (plan->d_blob && !plan->blob_borrowed) cudaFree(plan->d_blob);
   delete plan;
   return BSP_OK;
 }
@@ -453,10 +540,11 @@ struct SpmmLaunchCtx {
   const void* B;
   void* C;
   int64_t N;
+  cudaStream_t stream;
 };
 static bsp_status spmm_launch_ctx(const void* v) {
   const SpmmLaunchCtx* c = static_cast<const SpmmLaunchCtx*>(v);
-  return bsp_spmm_execute(c->p, c->A, c->B, c->N, c->C, c->N, nullptr);
+  return bsp_spmm_execute(c->p, c->A, c->B, c->N, c->C, c->N, c->stream);
 }
 
 static bsp_status spmm_host_impl(bsp_device* dev, int64_t M, int64_t K, int32_t R, int32_t C,
@@ -475,34 +563,69 @@ static bsp_status spmm_host_impl(bsp_device* dev, int64_t M, int64_t K, int32_t 
   const size_t b_C = align256(sizeof(uint16_t) * M * N);
   bsp_status s = ws_reserve(dev, b_val + b_rp + b_ci + b_B + b_C);
   if (s != BSP_OK) return s;
+  // Column panels of B and C: the copy of panel j + 1 in and of panel j - 1
+  // out overlap panel j's kernel (the copy engines run both directions at
+  // once).  Profiling calls time one whole-width kernel instead.
+  int P = 1;
+  if (iters == 0)
+    for (int q : {4, 2})
+      if (N % (256 * q) == 0 && N / q >= 512) {
+        P = q;
+        break;
+      }
+  const int64_t Np = N / P;
+  s = host_streams(dev, static_cast<size_t>(P));
+  if (s != BSP_OK) return s;
   uint8_t* w = static_cast<uint8_t*>(dev->ws);
   void* d_val = w;
   int32_t* d_rp = reinterpret_cast<int32_t*>(w + b_val);
   int32_t* d_ci = reinterpret_cast<int32_t*>(w + b_val + b_rp);
-  void* d_B = w + b_val + b_rp + b_ci;
-  void* d_C = w + b_val + b_rp + b_ci + b_B;
-  cudaStream_t stream = nullptr;
-  if ((s = cuda_check(cudaMemcpyAsync(d_B, B, sizeof(uint16_t) * K * N, cudaMemcpyHostToDevice, stream), "H2D B")) != BSP_OK) return s;
-  if ((s = cuda_check(cudaMemcpyAsync(d_rp, row_ptr, sizeof(int32_t) * (nbr + 1), cudaMemcpyHostToDevice, stream), "H2D row_ptr")) != BSP_OK) return s;
-  if (nnzb > 0) {
-    if ((s = cuda_check(cudaMemcpyAsync(d_ci, col_idx, sizeof(int32_t) * nnzb, cudaMemcpyHostToDevice, stream), "H2D col_idx")) != BSP_OK) return s;
-    if ((s = cuda_check(cudaMemcpyAsync(d_val, values, sizeof(uint16_t) * nnzb * R * C, cudaMemcpyHostToDevice, stream), "H2D values")) != BSP_OK) return s;
+  uint16_t* d_B = reinterpret_cast<uint16_t*>(w + b_val + b_rp + b_ci);
+  uint16_t* d_C = reinterpret_cast<uint16_t*>(w + b_val + b_rp + b_ci + b_B);
+  cudaStream_t sh = dev->s_h2d, sc = dev->s_comp, sd = dev->s_d2h;
+  const size_t pitch = sizeof(uint16_t) * N, pw = sizeof(uint16_t) * Np;
+  auto run = [&]() -> bsp_status {
+    bsp_status st;
+    if ((st = cuda_check(cudaMemcpyAsync(d_rp, row_ptr, sizeof(int32_t) * (nbr + 1), cudaMemcpyHostToDevice, sh), "H2D row_ptr")) != BSP_OK) return st;
+    if (nnzb > 0) {
+      if ((st = cuda_check(cudaMemcpyAsync(d_ci, col_idx, sizeof(int32_t) * nnzb, cudaMemcpyHostToDevice, sh), "H2D col_idx")) != BSP_OK) return st;
+      if ((st = cuda_check(cudaMemcpyAsync(d_val, values, sizeof(uint16_t) * nnzb * R * C, cudaMemcpyHostToDevice, sh), "H2D values")) != BSP_OK) return st;
+    }
+    for (int j = 0; j < P; ++j) {
+      if ((st = cuda_check(cudaMemcpy2DAsync(d_B + j * Np, pitch, B + j * Np, pitch, pw, K, cudaMemcpyHostToDevice, sh), "H2D B")) != BSP_OK) return st;
+      if ((st = cuda_check(cudaEventRecord(dev->ev_in[j], sh), "cudaEventRecord")) != BSP_OK) return st;
+    }
+    // the plan is built on the host while B streams in
+    bsp_bsr_desc A{M, K, R, C, nnzb, d_rp, d_ci, d_val};
+    bsp_spmm_plan* p = nullptr;
+    st = spmm_plan_create_impl(dev, &A, row_ptr, col_idx, Np, BSP_BF16, strategy, opts, true, sc, &p);
+    if (st != BSP_OK) return st;
+    for (int j = 0; j < P && st == BSP_OK; ++j) {
+      st = cuda_check(cudaStreamWaitEvent(sc, dev->ev_in[j], 0), "cudaStreamWaitEvent");
+      if (st == BSP_OK) st = bsp_spmm_execute(p, &A, d_B + j * Np, N, d_C + j * Np, N, sc);
+      if (st == BSP_OK) st = cuda_check(cudaEventRecord(dev->ev_out[j], sc), "cudaEventRecord");
+      if (st == BSP_OK) st = cuda_check(cudaStreamWaitEvent(sd, dev->ev_out[j], 0), "cudaStreamWaitEvent");
+      if (st == BSP_OK)
+        st = cuda_check(cudaMemcpy2DAsync(C_out + j * Np, pitch, d_C + j * Np, pitch, pw, M, cudaMemcpyDeviceToHost, sd), "D2H C");
+    }
+    if (st == BSP_OK && iters > 0) {
+      const SpmmLaunchCtx ctx{p, &A, d_B, d_C, N, sc};
+      st = time_launches(iters, ms_out, sc, spmm_launch_ctx, &ctx);
+    }
+    if (st == BSP_OK) st = cuda_check(cudaStreamSynchronize(sd), "sync");
+    if (st == BSP_OK) st = cuda_check(cudaStreamSynchronize(sc), "sync");
+    bsp_spmm_plan_destroy(p);
+    return st;
+  };
+  s = run();
+  if (s != BSP_OK) {
+    // nothing of this call may still run when the workspace is reused
+    cudaStreamSynchronize(sh);
+    cudaStreamSynchronize(sc);
+    cudaStreamSynchronize(sd);
+    return s;
   }
-  bsp_bsr_desc A{M, K, R, C, nnzb, d_rp, d_ci, d_val};
-  bsp_spmm_plan* p = nullptr;
-  s = bsp_spmm_plan_create(dev, &A, row_ptr, col_idx, N, BSP_BF16, strategy, opts, &p);
-  if (s != BSP_OK) return s;
-  s = bsp_spmm_execute(p, &A, d_B, N, d_C, N, stream);
-  if (s == BSP_OK && iters > 0) {
-    const SpmmLaunchCtx ctx{p, &A, d_B, d_C, N};
-    s = time_launches(iters, ms_out, stream, spmm_launch_ctx, &ctx);
-  }
-  if (s == BSP_OK)
-    s = cuda_check(cudaMemcpyAsync(C_out, d_C, sizeof(uint16_t) * M * N, cudaMemcpyDeviceToHost, stream), "D2H C");
-  if (s == BSP_OK) s = cuda_check(cudaStreamSynchronize(stream), "sync");
-  bsp_spmm_plan_destroy(p);
-  if (s == BSP_OK) s = bsp_device_synchronize(dev);
-  return s;
+  return bsp_device_synchronize(dev);
 }
 
 bsp_status bsp_spmm_host(bsp_device* dev, int64_t M, int64_t K, int32_t R, int32_t C, int64_t nnzb,
@@ -524,10 +647,23 @@ bsp_status bsp_spmm_host_profile(bsp_device* dev, int64_t M, int64_t K, int32_t 
 }
 
 // --------------------------------------------------------------- SDDMM ----
+static bsp_status sddmm_plan_create_impl(bsp_device* dev, const bsp_bsr_desc* mask,
+                                         const int32_t* host_row_ptr, const int32_t* host_col_idx, int64_t K,
+                                         bsp_strategy strategy, const bsp_sddmm_opts* opts, bool borrow,
+                                         cudaStream_t stream, bsp_sddmm_plan** out);
+
 bsp_status bsp_sddmm_plan_create(bsp_device* dev, const bsp_bsr_desc* mask,
                                  const int32_t* host_row_ptr, const int32_t* host_col_idx,
                                  int64_t K, bsp_strategy strategy, const bsp_sddmm_opts* opts,
                                  bsp_sddmm_plan** out) {
+  return sddmm_plan_create_impl(dev, mask, host_row_ptr, host_col_idx, K, strategy, opts, false, nullptr,
+                                out);
+}
+
+static bsp_status sddmm_plan_create_impl(bsp_device* dev, const bsp_bsr_desc* mask,
+                                         const int32_t* host_row_ptr, const int32_t* host_col_idx, int64_t K,
+                                         bsp_strategy strategy, const bsp_sddmm_opts* opts, bool borrow,
+                                         cudaStream_t stream, bsp_sddmm_plan** out) {
   if (!dev || !out) return set_error(BSP_ERR_INVALID_ARG, "null argument");
   *out = nullptr;
   bsp_status s = check_desc(mask, false);
@@ -552,10 +688,13 @@ bsp_status bsp_sddmm_plan_create(bsp_device* dev, const bsp_bsr_desc* mask,
     return s;
   }
   std::vector<void*> ptrs;
-  s = upload_blob({{p->h_units.data(), p->h_units.size() * sizeof(SddmmUnit)},
-                   {p->h_cta_begin.data(), p->h_cta_begin.size() * sizeof(int32_t)},
-                   {p->h_rs_units.data(), p->h_rs_units.size() * sizeof(SddmmRsUnit)}},
-                  &p->d_blob, &p->blob_bytes, &ptrs);
+  const std::vector<std::pair<const void*, size_t>> parts = {
+      {p->h_units.data(), p->h_units.size() * sizeof(SddmmUnit)},
+      {p->h_cta_begin.data(), p->h_cta_begin.size() * sizeof(int32_t)},
+      {p->h_rs_units.data(), p->h_rs_units.size() * sizeof(SddmmRsUnit)}};
+  s = borrow ? upload_blob_borrowed(dev, parts, stream, &p->d_blob, &p->blob_bytes, &ptrs)
+             : upload_blob(parts, &p->d_blob, &p->blob_bytes, &ptrs);
+  p->blob_borrowed = borrow;
   if (s != BSP_OK) {
     delete p;
     return s;
@@ -586,7 +725,7 @@ bsp_status bsp_sddmm_execute(const bsp_sddmm_plan* plan, const bsp_bsr_desc* mas
 
 bsp_status bsp_sddmm_plan_destroy(bsp_sddmm_plan* plan) {
   if (!plan) return BSP_OK;
-  if (plan->d_blob) cudaFree(plan->d_blob);
+  if (plan->d_blob && !plan->blob_borrowed) cudaFree(plan->d_blob);
   delete plan;
   return BSP_OK;
 }
@@ -629,10 +768,11 @@ struct SddmmLaunchCtx {
   const void* B;
   void* out;
   int64_t K, N;
+  cudaStream_t stream;
 };
 static bsp_status sddmm_launch_ctx(const void* v) {
   const SddmmLaunchCtx* c = static_cast<const SddmmLaunchCtx*>(v);
-  return bsp_sddmm_execute(c->p, c->mask, c->A, c->K, c->B, c->N, c->out, nullptr);
+  return bsp_sddmm_execute(c->p, c->mask, c->A, c->K, c->B, c->N, c->out, c->stream);
 }
 
 static bsp_status sddmm_host_impl(bsp_device* dev, int64_t M, int64_t N, int32_t R, int32_t C,
@@ -660,7 +800,12 @@ static bsp_status sddmm_host_impl(bsp_device* dev, int64_t M, int64_t N, int32_t
   int32_t* d_ci = reinterpret_cast<int32_t*>(w + b_out + b_mask + b_rp);
   void* d_A = w + b_out + b_mask + b_rp + b_ci;
   void* d_B = w + b_out + b_mask + b_rp + b_ci + b_A;
-  cudaStream_t stream = nullptr;
+  if ((s = host_streams(dev, 1)) != BSP_OK) return s;
+  cudaStream_t stream = dev->s_comp;
+  struct SyncOnExit {  // nothing of this call may still run when the workspace is reused
+    cudaStream_t st;
+    ~SyncOnExit() { cudaStreamSynchronize(st); }
+  } sync_on_exit{stream};
   if ((s = cuda_check(cudaMemcpyAsync(d_A, A, sizeof(uint16_t) * M * K, cudaMemcpyHostToDevice, stream), "H2D A")) != BSP_OK) return s;
   if ((s = cuda_check(cudaMemcpyAsync(d_B, B, sizeof(uint16_t) * K * N, cudaMemcpyHostToDevice, stream), "H2D B")) != BSP_OK) return s;
   if ((s = cuda_check(cudaMemcpyAsync(d_rp, row_ptr, sizeof(int32_t) * (nbr + 1), cudaMemcpyHostToDevice, stream), "H2D row_ptr")) != BSP_OK) return s;
@@ -672,11 +817,11 @@ static bsp_status sddmm_host_impl(bsp_device* dev, int64_t M, int64_t N, int32_t
   }
   bsp_bsr_desc mask{M, N, R, C, nnzb, d_rp, d_ci, d_mask};
   bsp_sddmm_plan* p = nullptr;
-  s = bsp_sddmm_plan_create(dev, &mask, row_ptr, col_idx, K, strategy, opts, &p);
+  s = sddmm_plan_create_impl(dev, &mask, row_ptr, col_idx, K, strategy, opts, true, stream, &p);
   if (s != BSP_OK) return s;
   s = bsp_sddmm_execute(p, &mask, d_A, K, d_B, N, d_out, stream);
   if (s == BSP_OK && iters > 0) {
-    const SddmmLaunchCtx ctx{p, &mask, d_A, d_B, d_out, K, N};
+    const SddmmLaunchCtx ctx{p, &mask, d_A, d_B, d_out, K, N, stream};
     s = time_launches(iters, ms_out, stream, sddmm_launch_ctx, &ctx);
   }
   if (s == BSP_OK && nnzb > 0)
@@ -714,11 +859,26 @@ static bsp_status spgemm_check_pair(const bsp_bsr_desc* A, const bsp_bsr_desc* B
   return BSP_OK;
 }
 
+static bsp_status spgemm_plan_create_impl(bsp_device* dev, const bsp_bsr_desc* A,
+                                          const int32_t* a_host_row_ptr, const int32_t* a_host_col_idx,
+                                          const bsp_bsr_desc* B, const int32_t* b_host_row_ptr,
+                                          const int32_t* b_host_col_idx, const bsp_spmm_opts* opts,
+                                          bool borrow, cudaStream_t stream, bsp_spgemm_plan** out);
+
 bsp_status bsp_spgemm_plan_create(bsp_device* dev, const bsp_bsr_desc* A,
                                   const int32_t* a_host_row_ptr, const int32_t* a_host_col_idx,
                                   const bsp_bsr_desc* B, const int32_t* b_host_row_ptr,
                                   const int32_t* b_host_col_idx, const bsp_spmm_opts* opts,
                                   bsp_spgemm_plan** out) {
+  return spgemm_plan_create_impl(dev, A, a_host_row_ptr, a_host_col_idx, B, b_host_row_ptr, b_host_col_idx,
+                                 opts, false, nullptr, out);
+}
+
+static bsp_status spgemm_plan_create_impl(bsp_device* dev, const bsp_bsr_desc* A,
+                                          const int32_t* a_host_row_ptr, const int32_t* a_host_col_idx,
+                                          const bsp_bsr_desc* B, const int32_t* b_host_row_ptr,
+                                          const int32_t* b_host_col_idx, const bsp_spmm_opts* opts,
+                                          bool borrow, cudaStream_t stream, bsp_spgemm_plan** out) {
   if (!dev || !out) return set_error(BSP_ERR_INVALID_ARG, "null argument");
   *out = nullptr;
   bsp_status s = check_desc(A, false);
@@ -747,10 +907,13 @@ bsp_status bsp_spgemm_plan_create(bsp_device* dev, const bsp_bsr_desc* A,
     return s;
   }
   std::vector<void*> ptrs;
-  s = upload_blob({{p->h_units.data(), p->h_units.size() * sizeof(SpgemmUnit)},
-                   {p->h_steps.data(), p->h_steps.size() * sizeof(SpgemmStep)},
-                   {p->h_cta_begin.data(), p->h_cta_begin.size() * sizeof(int32_t)}},
-                  &p->d_blob, &p->blob_bytes, &ptrs);
+  const std::vector<std::pair<const void*, size_t>> parts = {
+      {p->h_units.data(), p->h_units.size() * sizeof(SpgemmUnit)},
+      {p->h_steps.data(), p->h_steps.size() * sizeof(SpgemmStep)},
+      {p->h_cta_begin.data(), p->h_cta_begin.size() * sizeof(int32_t)}};
+  s = borrow ? upload_blob_borrowed(dev, parts, stream, &p->d_blob, &p->blob_bytes, &ptrs)
+             : upload_blob(parts, &p->d_blob, &p->blob_bytes, &ptrs);
+  p->blob_borrowed = borrow;
   if (s != BSP_OK) {
     delete p;
     return s;
@@ -789,7 +952,7 @@ bsp_status bsp_spgemm_execute(const bsp_spgemm_plan* plan, const bsp_bsr_desc* A
 
 bsp_status bsp_spgemm_plan_destroy(bsp_spgemm_plan* plan) {
   if (!plan) return BSP_OK;
-  if (plan->d_blob) cudaFree(plan->d_blob);
+  if (plan->d_blob && !plan->blob_borrowed) cudaFree(plan->d_blob);
   delete plan;
   return BSP_OK;
 }
@@ -819,10 +982,11 @@ struct SpgemmLaunchCtx {
   const bsp_bsr_desc* A;
   const bsp_bsr_desc* B;
   void* out;
+  cudaStream_t stream;
 };
 static bsp_status spgemm_launch_ctx(const void* v) {
   const SpgemmLaunchCtx* c = static_cast<const SpgemmLaunchCtx*>(v);
-  return bsp_spgemm_execute(c->p, c->A, c->B, c->out, nullptr);
+  return bsp_spgemm_execute(c->p, c->A, c->B, c->out, c->stream);
 }
 
 bsp_status bsp_spgemm_host(bsp_device* dev, int64_t M, int64_t K, int64_t N, int32_t Ra, int32_t Ca,
@@ -877,7 +1041,12 @@ bsp_status bsp_spgemm_host(bsp_device* dev, int64_t M, int64_t K, int64_t N, int
   int32_t* d_aci = reinterpret_cast<int32_t*>(w + b_av + b_bv + b_ov + b_arp);
   int32_t* d_brp = reinterpret_cast<int32_t*>(w + b_av + b_bv + b_ov + b_arp + b_aci);
   int32_t* d_bci = reinterpret_cast<int32_t*>(w + b_av + b_bv + b_ov + b_arp + b_aci + b_brp);
-  cudaStream_t stream = nullptr;
+  if ((s = host_streams(dev, 1)) != BSP_OK) return s;
+  cudaStream_t stream = dev->s_comp;
+  struct SyncOnExit {  // nothing of this call may still run when the workspace is reused
+    cudaStream_t st;
+    ~SyncOnExit() { cudaStreamSynchronize(st); }
+  } sync_on_exit{stream};
   struct Cp { void* d; const void* h; size_t n; const char* what; };
   const Cp cps[] = {{d_av, a_values, a_blk, "H2D A values"}, {d_bv, b_values, b_blk, "H2D B values"},
                     {d_arp, a_row_ptr, sizeof(int32_t) * (nbr + 1), "H2D A row_ptr"},
@@ -889,7 +1058,7 @@ bsp_status bsp_spgemm_host(bsp_device* dev, int64_t M, int64_t K, int64_t N, int
       return s;
   const bsp_bsr_desc A{M, K, Ra, Ca, a_nnzb, d_arp, d_aci, d_av};
   const bsp_bsr_desc B{K, N, Ca, Cb, b_nnzb, d_brp, d_bci, d_bv};
-  s = bsp_spgemm_plan_create(dev, &A, a_row_ptr, a_col_idx, &B, b_row_ptr, b_col_idx, opts, &p);
+  s = spgemm_plan_create_impl(dev, &A, a_row_ptr, a_col_idx, &B, b_row_ptr, b_col_idx, opts, true, stream, &p);
   if (s != BSP_OK) return s;
   const int64_t n_out = static_cast<int64_t>(p->out_col_idx.size());
   *out_nnzb = n_out;
@@ -899,7 +1068,7 @@ bsp_status bsp_spgemm_host(bsp_device* dev, int64_t M, int64_t K, int64_t N, int
   }
   s = bsp_spgemm_execute(p, &A, &B, d_ov, stream);
   if (s == BSP_OK && iters > 0) {
-    const SpgemmLaunchCtx ctx{p, &A, &B, d_ov};
+    const SpgemmLaunchCtx ctx{p, &A, &B, d_ov, stream};
     s = time_launches(iters, ms_per_launch, stream, spgemm_launch_ctx, &ctx);
   }
   if (s == BSP_OK && n_out > 0)
@@ -917,9 +1086,21 @@ bsp_status bsp_spgemm_host(bsp_device* dev, int64_t M, int64_t K, int64_t N, int
 }
 
 // ----------------------------------------------------------- attention ----
+static bsp_status attn_plan_create_impl(bsp_device* dev, const bsp_bsr_desc* mask,
+                                        const int32_t* host_row_ptr, const int32_t* host_col_idx, int64_t d,
+                                        const bsp_spmm_opts* opts, bool borrow, cudaStream_t stream,
+                                        bsp_attn_plan** out);
+
 bsp_status bsp_attn_plan_create(bsp_device* dev, const bsp_bsr_desc* mask, const int32_t* host_row_ptr,
                                 const int32_t* host_col_idx, int64_t d, const bsp_spmm_opts* opts,
                                 bsp_attn_plan** out) {
+  return attn_plan_create_impl(dev, mask, host_row_ptr, host_col_idx, d, opts, false, nullptr, out);
+}
+
+static bsp_status attn_plan_create_impl(bsp_device* dev, const bsp_bsr_desc* mask,
+                                        const int32_t* host_row_ptr, const int32_t* host_col_idx, int64_t d,
+                                        const bsp_spmm_opts* opts, bool borrow, cudaStream_t stream,
+                                        bsp_attn_plan** out) {
   if (!dev || !out) return set_error(BSP_ERR_INVALID_ARG, "null argument");
   *out = nullptr;
   bsp_status s = check_desc(mask, false);
@@ -943,11 +1124,14 @@ bsp_status bsp_attn_plan_create(bsp_device* dev, const bsp_bsr_desc* mask, const
   }
   std::vector<void*> ptrs;
   const std::vector<int32_t> zeros(static_cast<size_t>(p->n_counters), 0);
-  s = upload_blob({{p->h_units.data(), p->h_units.size() * sizeof(AttnUnit)},
-                   {p->h_chunks.data(), p->h_chunks.size() * sizeof(AttnChunk)},
-                   {p->h_cta_begin.data(), p->h_cta_begin.size() * sizeof(int32_t)},
-                   {zeros.data(), zeros.size() * sizeof(int32_t)}},
-                  &p->d_blob, &p->blob_bytes, &ptrs);
+  const std::vector<std::pair<const void*, size_t>> parts = {
+      {p->h_units.data(), p->h_units.size() * sizeof(AttnUnit)},
+      {p->h_chunks.data(), p->h_chunks.size() * sizeof(AttnChunk)},
+      {p->h_cta_begin.data(), p->h_cta_begin.size() * sizeof(int32_t)},
+      {zeros.data(), zeros.size() * sizeof(int32_t)}};
+  s = borrow ? upload_blob_borrowed(dev, parts, stream, &p->d_blob, &p->blob_bytes, &ptrs)
+             : upload_blob(parts, &p->d_blob, &p->blob_bytes, &ptrs);
+  p->blob_borrowed = borrow;
   if (s != BSP_OK) {
     delete p;
     return s;
@@ -956,10 +1140,24 @@ bsp_status bsp_attn_plan_create(bsp_device* dev, const bsp_bsr_desc* mask, const
   p->d_chunks = static_cast<AttnChunk*>(ptrs[1]);
   p->d_cta_begin = static_cast<int32_t*>(ptrs[2]);
   p->d_counters = static_cast<int32_t*>(ptrs[3]);
-  if (p->n_slots > 0 &&
-      cudaMalloc(&p->d_work, sizeof(float) * 128 * (p->d + 2) * p->n_slots) != cudaSuccess) {
-    bsp_attn_plan_destroy(p);
-    return set_error(BSP_ERR_ALLOC, "cudaMalloc of the attention merge workspace failed");
+  if (p->n_slots > 0) {
+    const size_t wb = sizeof(float) * 128 * (p->d + 2) * p->n_slots;
+    if (borrow) {
+      if (dev->aux_ws_bytes < wb) {
+        if (dev->aux_ws) cudaFree(dev->aux_ws);
+        dev->aux_ws = nullptr;
+        dev->aux_ws_bytes = 0;
+        if (cudaMalloc(&dev->aux_ws, wb) != cudaSuccess) {
+          bsp_attn_plan_destroy(p);
+          return set_error(BSP_ERR_ALLOC, "cudaMalloc of the attention merge workspace failed");
+        }
+        dev->aux_ws_bytes = wb;
+      }
+      p->d_work = static_cast<float*>(dev->aux_ws);
+    } else if (cudaMalloc(&p->d_work, wb) != cudaSuccess) {
+      bsp_attn_plan_destroy(p);
+      return set_error(BSP_ERR_ALLOC, "cudaMalloc of the attention merge workspace failed");
+    }
   }
   *out = p;
   return BSP_OK;
@@ -976,8 +1174,8 @@ bsp_status bsp_attn_execute(const bsp_attn_plan* plan, const void* Q, int64_t ld
 
 bsp_status bsp_attn_plan_destroy(bsp_attn_plan* plan) {
   if (!plan) return BSP_OK;
-  if (plan->d_blob) cudaFree(plan->d_blob);
-  if (plan->d_work) cudaFree(plan->d_work);
+  if (plan->d_blob && !plan->blob_borrowed) cudaFree(plan->d_blob);
+  if (plan->d_work && !plan->blob_borrowed) cudaFree(plan->d_work);
   delete plan;
   return BSP_OK;
 }
@@ -1016,7 +1214,12 @@ bsp_status bsp_attn_host(bsp_device* dev, int64_t S, int64_t d, int64_t nnzb, co
   void *dQ = w, *dK = w + b_m, *dV = w + 2 * b_m, *dO = w + 3 * b_m;
   int32_t* d_rp = reinterpret_cast<int32_t*>(w + 4 * b_m);
   int32_t* d_ci = reinterpret_cast<int32_t*>(w + 4 * b_m + b_rp);
-  cudaStream_t stream = nullptr;
+  if ((s = host_streams(dev, 1)) != BSP_OK) return s;
+  cudaStream_t stream = dev->s_comp;
+  struct SyncOnExit {  // nothing of this call may still run when the workspace is reused
+    cudaStream_t st;
+    ~SyncOnExit() { cudaStreamSynchronize(st); }
+  } sync_on_exit{stream};
   struct Cp { void* d; const void* h; size_t n; const char* what; };
   const Cp cps[] = {{dQ, Q, mat, "H2D Q"}, {dK, K, mat, "H2D K"}, {dV, V, mat, "H2D V"},
                     {d_rp, row_ptr, sizeof(int32_t) * (nbr + 1), "H2D row_ptr"},
@@ -1026,7 +1229,7 @@ bsp_status bsp_attn_host(bsp_device* dev, int64_t S, int64_t d, int64_t nnzb, co
       return s;
   const bsp_bsr_desc mask{S, S, 32, 32, nnzb, d_rp, d_ci, nullptr};
   bsp_attn_plan* p = nullptr;
-  s = bsp_attn_plan_create(dev, &mask, row_ptr, col_idx, d, opts, &p);
+  s = attn_plan_create_impl(dev, &mask, row_ptr, col_idx, d, opts, true, stream, &p);
   if (s != BSP_OK) return s;
   s = bsp_attn_execute(p, dQ, d, dK, d, dV, d, scale, dO, d, stream);
   if (s == BSP_OK) s = cuda_check(cudaMemcpyAsync(O, dO, mat, cudaMemcpyDeviceToHost, stream), "D2H O");

@@ -13,8 +13,11 @@
 #include <algorithm>
 #include <climits>
 #include <cstring>
+#include <cstdlib>
 #include <numeric>
 #include <string>
+#include <system_error>
+#include <thread>
 
 #include "bsp_internal.h"
 
@@ -40,6 +43,56 @@ int slab_height(int R) {
 }
 
 }  // namespace
+
+// Threads for a host planning pass over `items` independent items: at most
+// 16 and the machine's cores, at least `min_items` items each, and the
+// per-thread scratch (`scratch_bytes`) within 256 MB.  BSP_PLANNER_THREADS
+// overrides the count (the plans do not depend on it).
+static int planner_threads(int64_t items, int64_t min_items, int64_t scratch_bytes) {
+  int t = static_cast<int>(std::min<unsigned>(16, std::max(1u, std::thread::hardware_concurrency())));
+  if (const char* env = std::getenv("BSP_PLANNER_THREADS")) {
+    const int v = std::atoi(env);
+    if (v > 0) return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(v, items)));
+  }
+  t = static_cast<int>(std::min<int64_t>(t, std::max<int64_t>(1, items / std::max<int64_t>(1, min_items))));
+  t = static_cast<int>(std::min<int64_t>(t, std::max<int64_t>(1, (int64_t(256) << 20) / std::max<int64_t>(1, scratch_bytes))));
+  return t;
+}
+
+// fn(thread, begin, end) over `nt` contiguous ranges of [0, n); the first
+// failing status (in range order) is returned.
+template <class F>
+static bsp_status parallel_ranges(int64_t n, int nt, F&& fn) {
+  if (nt <= 1) return fn(0, int64_t(0), n);
+  std::vector<bsp_status> res(static_cast<size_t>(nt), BSP_OK);
+  std::vector<std::string> msg(static_cast<size_t>(nt));  // error messages are per thread
+  std::vector<std::thread> th;
+  auto body = [&](int t) {
+    try {
+      res[static_cast<size_t>(t)] = fn(t, n * t / nt, n * (t + 1) / nt);
+      if (res[static_cast<size_t>(t)] != BSP_OK) msg[static_cast<size_t>(t)] = bsp_last_error_string();
+    } catch (const std::bad_alloc&) {
+      res[static_cast<size_t>(t)] = BSP_ERR_ALLOC;
+      msg[static_cast<size_t>(t)] = "host allocation failed in the planner";
+    }
+  };
+  try {
+    for (int t = 1; t < nt; ++t) th.emplace_back(body, t);
+  } catch (const std::system_error&) {
+    for (auto& x : th) x.join();
+    th.clear();
+    return fn(0, int64_t(0), n);  // no threads to be had: one pass
+  }
+  body(0);
+  for (auto& x : th) x.join();
+  for (int t = 0; t < nt; ++t)
+    if (res[static_cast<size_t>(t)] != BSP_OK) return set_error(res[static_cast<size_t>(t)], msg[static_cast<size_t>(t)]);
+  return BSP_OK;
+}
+
+static bsp_status spmm_stage_counts(bsp_spmm_plan* p);
+static bsp_status rowstack_stage_lists(bsp_spmm_plan* p);
+static bsp_status pair_stage_lists(bsp_spmm_plan* p);
 
 // The reference's zig-zag balancer generalised to any item list: items sorted
 // by weight (heaviest first, ties by index), then each pass deals the next
@@ -164,7 +217,9 @@ bsp_status plan_spmm_host(bsp_spmm_plan* p, const int32_t* row_ptr, const int32_
   if (p->strategy == BSP_DDA && o.group_mma != 2 && o.group_mma != 3) {
     if (o.group_mma == 4 || sm_count < 2) return plan_spmm_rowstack(p, row_ptr, col_idx, sm_count, max_smem, opts);
     if (o.group_mma == 5) return plan_spmm_pair(p, row_ptr, col_idx, sm_count, max_smem, opts);
-    bsp_status st1 = plan_spmm_rowstack(p, row_ptr, col_idx, sm_count, max_smem, opts);
+    // Both schedules without their stage lists (the choice needs only the
+    // stage counts); the lists are then built for the winner alone.
+    bsp_status st1 = plan_spmm_rowstack(p, row_ptr, col_idx, sm_count, max_smem, opts, false);
     if (st1 != BSP_OK) return plan_spmm_pair(p, row_ptr, col_idx, sm_count, max_smem, opts);
     auto longest = [](const bsp_spmm_plan* q, int step) {
       int64_t m = 0;
@@ -182,11 +237,16 @@ bsp_status plan_spmm_host(bsp_spmm_plan* p, const int32_t* row_ptr, const int32_
     pair.nnzb = p->nnzb;
     pair.c_type = p->c_type;
     pair.strategy = p->strategy;
-    if (plan_spmm_pair(&pair, row_ptr, col_idx, sm_count, max_smem, opts) != BSP_OK) return BSP_OK;
+    if (plan_spmm_pair(&pair, row_ptr, col_idx, sm_count, max_smem, opts, false) != BSP_OK)
+      return rowstack_stage_lists(p);
     const int64_t s2 = longest(&pair, 2);  // per pair: the leader's list (both lists are equal length)
-    if (4 * s2 < 5 * s1)  // pair time ~ 0.8 x its stages vs single-CTA stages
-      return plan_spmm_pair(p, row_ptr, col_idx, sm_count, max_smem, opts);
-    return BSP_OK;
+    if (4 * s2 < 5 * s1) {  // pair time ~ 0.8 x its stages vs single-CTA stages
+      bsp_device* dev = p->dev;
+      *p = std::move(pair);
+      p->dev = dev;
+      return pair_stage_lists(p);
+    }
+    return rowstack_stage_lists(p);
   }
   p->variant = 0;
 
@@ -343,7 +403,7 @@ bsp_status plan_spmm_host(bsp_spmm_plan* p, const int32_t* row_ptr, const int32_
 // x 256 output columns; its steps are the distinct block-columns of the
 // group's rows, each listing per entry the block to multiply (or -1).
 bsp_status plan_spmm_rowstack(bsp_spmm_plan* p, const int32_t* row_ptr, const int32_t* col_idx,
-                              int sm_count, int max_smem, const bsp_spmm_opts* opts) {
+                              int sm_count, int max_smem, const bsp_spmm_opts* opts, bool stage_lists) {
   bsp_spmm_opts o;
   memset(&o, 0, sizeof(o));
   if (opts) o = *opts;
@@ -485,72 +545,9 @@ bsp_status plan_spmm_rowstack(bsp_spmm_plan* p, const int32_t* row_ptr, const in
   p->tmem_cols = 512;
   p->timeout_ns = static_cast<uint64_t>(o.timeout_ms > 0 ? o.timeout_ms : 2000) * 1000000ull;
 
-  // ---- per-CTA stage lists ----
-  // The kernel's smem ring is in lockstep with each CTA's stage sequence
-  // (stage k uses slot k % stages), so the host can tell exactly which entry
-  // slots still hold an older block and must be zeroed before a stage where
-  // that entry is absent.
-  const bool b3d = (p->N % 64 == 0);
-  const uint32_t all = (1u << G) - 1u;
-  const int W = kRsStageWords;
-  p->h_stage_list.clear();
-  p->h_cta_stage_begin.assign(1, 0);
-  std::vector<uint32_t> dirty(static_cast<size_t>(stages) * nsub);  // per (slot, sub-step)
-  for (int c = 0; c < grid; ++c) {
-    std::fill(dirty.begin(), dirty.end(), all);  // unknown contents until first written
-    int64_t k = 0;
-    for (int32_t ui = p->h_cta_begin[c]; ui < p->h_cta_begin[c + 1]; ++ui) {
-      const SpmmUnit& u = p->h_units[ui];
-      const int nsteps = u.step_end - u.step_begin;
-      if (nsteps == 0) {
-        int32_t e[kRsStageWords] = {RS_F_FIRST | RS_F_LAST | RS_F_EMPTY};
-        p->h_stage_list.insert(p->h_stage_list.end(), e, e + W);
-        ++k;
-        continue;
-      }
-      int slab_off[4] = {0, 0, 0, 0};
-      for (int g = 0; g < G; ++g) slab_off[g] = static_cast<int>((u.row0 + g) % slabs) * Rs;
-      // the unit's (step, k-chunk) sequence, nsub of them per stage
-      const int nitems = nsteps * nkc;
-      for (int s0 = 0; s0 < nitems; s0 += nsub) {
-        const int nin = std::min(nsub, nitems - s0);
-        int32_t e[kRsStageWords];
-        for (int q = 0; q < W; ++q) e[q] = (q >= 5 && q <= 12) ? -1 : 0;
-        uint32_t flags = 0, np = 0;
-        const int slot = static_cast<int>(k % stages);
-        for (int sub = 0; sub < nin; ++sub) {
-          const int s = s0 + sub;
-          const int j = s / nkc, kci = s % nkc;
-          const int32_t* st = &steps[static_cast<size_t>(u.step_begin + j) * stride];
-          uint32_t present = 0;
-          for (int g = 0; g < G; ++g)
-            if (g < u.nrows && st[1 + g] >= 0) {
-              present |= 1u << g;
-              ++np;
-              e[5 + 4 * sub + g] = st[1 + g] * R + slab_off[g];
-            }
-          uint32_t& d = dirty[static_cast<size_t>(slot) * nsub + sub];
-          const uint32_t zero = ~present & all & d;
-          d = present;
-          flags |= (present << (4 * sub)) | (zero << (8 + 4 * sub));
-          e[3 + sub] = st[0] * C + kci * kc;
-          e[2] = kci * kc;  // a stage never mixes k-chunks when nsub == 2 (nkc == 1)
-        }
-        flags |= np << 16;
-        if (s0 == 0) flags |= RS_F_FIRST;
-        if (s0 + nin >= nitems) flags |= RS_F_LAST;
-        if (nin == 2) flags |= RS_F_TWO;
-        e[0] = static_cast<int32_t>(flags);
-        e[1] = b3d ? u.n0 / 64 : u.n0;
-        p->h_stage_list.insert(p->h_stage_list.end(), e, e + W);
-        ++k;
-      }
-    }
-    if (p->h_stage_list.size() / W >= (size_t(1) << 31))
-      return set_error(BSP_ERR_UNSUPPORTED, "schedule too long");
-    p->h_cta_stage_begin.push_back(static_cast<int32_t>(p->h_stage_list.size() / W));
-  }
-  return BSP_OK;
+  bsp_status st = spmm_stage_counts(p);
+  if (st != BSP_OK || !stage_lists) return st;
+  return rowstack_stage_lists(p);
 }
 
 // Row-stacked schedule for CTA pairs (2-SM MMA, spmm_pair.cu).  A pair unit
@@ -562,7 +559,7 @@ bsp_status plan_spmm_rowstack(bsp_spmm_plan* p, const int32_t* row_ptr, const in
 // no slot ever needs clearing.  Units and stage lists are per CTA (the two
 // CTAs of a pair walk the same stage sequence with their own coordinates).
 bsp_status plan_spmm_pair(bsp_spmm_plan* p, const int32_t* row_ptr, const int32_t* col_idx,
-                          int sm_count, int max_smem, const bsp_spmm_opts* opts) {
+                          int sm_count, int max_smem, const bsp_spmm_opts* opts, bool stage_lists) {
   bsp_spmm_opts o;
   memset(&o, 0, sizeof(o));
   if (opts) o = *opts;
@@ -678,13 +675,10 @@ bsp_status plan_spmm_pair(bsp_spmm_plan* p, const int32_t* row_ptr, const int32_
   p->timeout_ns = static_cast<uint64_t>(o.timeout_ms > 0 ? o.timeout_ms : 2000) * 1000000ull;
   p->grid = 2 * npairs;
 
-  // per-CTA units and stage lists (CTA 2c + r = rank r of pair c)
-  const bool b3d = (p->N % 64 == 0);
-  const int W = kRsStageWords;
+  // per-CTA units (CTA 2c + r = rank r of pair c); both CTAs of a pair walk
+  // the same step sequence, each with its own entries and B half
   p->h_units.clear();
   p->h_cta_begin.assign(1, 0);
-  p->h_stage_list.clear();
-  p->h_cta_stage_begin.assign(1, 0);
   for (int c = 0; c < npairs; ++c) {
     for (int r = 0; r < 2; ++r) {
       for (int32_t idx : per[c]) {
@@ -699,10 +693,136 @@ bsp_status plan_spmm_pair(bsp_spmm_plan* p, const int32_t* row_ptr, const int32_
         u.step_end = pu.s_end;
         u.row_mask = (pu.mask >> (r * G)) & ((1 << G) - 1);
         p->h_units.push_back(u);
-        const int nsteps = pu.s_end - pu.s_begin;
+      }
+      p->h_cta_begin.push_back(static_cast<int32_t>(p->h_units.size()));
+    }
+  }
+  if (steps.empty()) {
+    steps.push_back(0);
+    for (int q = 0; q < G2; ++q) steps.push_back(-1);
+  }
+  // one unit record per CTA of each pair unit
+  p->n_units = static_cast<int64_t>(p->h_units.size());
+  bsp_status st = spmm_stage_counts(p);
+  if (st != BSP_OK || !stage_lists) return st;
+  return pair_stage_lists(p);
+}
+
+// Stages in each CTA's list (row-stacked and pair schedules): a unit without
+// blocks takes one empty stage, the others ceil(steps * k-chunks / nsub).
+static bsp_status spmm_stage_counts(bsp_spmm_plan* p) {
+  const int nkc = p->C / p->kc;
+  p->h_cta_stage_begin.assign(1, 0);
+  p->h_stage_list.clear();
+  int64_t total = 0;
+  for (size_t c = 0; c + 1 < p->h_cta_begin.size(); ++c) {
+    for (int32_t ui = p->h_cta_begin[c]; ui < p->h_cta_begin[c + 1]; ++ui) {
+      const int64_t n = static_cast<int64_t>(p->h_units[ui].step_end - p->h_units[ui].step_begin) * nkc;
+      total += n == 0 ? 1 : (n + p->nsub - 1) / p->nsub;
+    }
+    if (total >= (int64_t(1) << 31)) return set_error(BSP_ERR_UNSUPPORTED, "schedule too long");
+    p->h_cta_stage_begin.push_back(static_cast<int32_t>(total));
+  }
+  return BSP_OK;
+}
+
+// The row-stacked kernel's per-CTA stage lists, CTAs split over host threads
+// (each CTA's list depends only on its own units).  The kernel's smem ring is
+// in lockstep with each CTA's stage sequence (stage k uses slot k % stages),
+// so the host can tell exactly which entry slots still hold an older block
+// and must be zeroed before a stage where that entry is absent.
+static bsp_status rowstack_stage_lists(bsp_spmm_plan* p) {
+  const int W = kRsStageWords;
+  const int G = p->G, Rs = p->Rs, R = p->R, C = p->C, kc = p->kc, nkc = C / kc, slabs = R / Rs;
+  const int nsub = p->nsub, stages = p->stages, stride = p->step_stride;
+  const bool b3d = (p->N % 64 == 0);
+  const uint32_t all = (1u << G) - 1u;
+  const int64_t grid = static_cast<int64_t>(p->h_cta_begin.size()) - 1;
+  p->h_stage_list.resize(static_cast<size_t>(p->h_cta_stage_begin.back()) * W);
+  const std::vector<int32_t>& steps = p->h_steps;
+  return parallel_ranges(grid, planner_threads(grid, 4, 0), [&](int, int64_t c0, int64_t c1) {
+    std::vector<uint32_t> dirty(static_cast<size_t>(stages) * nsub);  // per (slot, sub-step)
+    for (int64_t c = c0; c < c1; ++c) {
+      int32_t* out = p->h_stage_list.data() + static_cast<size_t>(p->h_cta_stage_begin[c]) * W;
+      std::fill(dirty.begin(), dirty.end(), all);  // unknown contents until first written
+      int64_t k = 0;
+      for (int32_t ui = p->h_cta_begin[c]; ui < p->h_cta_begin[c + 1]; ++ui) {
+        const SpmmUnit& u = p->h_units[ui];
+        const int nsteps = u.step_end - u.step_begin;
         if (nsteps == 0) {
           int32_t e[kRsStageWords] = {RS_F_FIRST | RS_F_LAST | RS_F_EMPTY};
-          p->h_stage_list.insert(p->h_stage_list.end(), e, e + W);
+          memcpy(out, e, sizeof(e));
+          out += W;
+          ++k;
+          continue;
+        }
+        int slab_off[4] = {0, 0, 0, 0};
+        for (int g = 0; g < G; ++g) slab_off[g] = static_cast<int>((u.row0 + g) % slabs) * Rs;
+        // the unit's (step, k-chunk) sequence, nsub of them per stage
+        const int nitems = nsteps * nkc;
+        for (int s0 = 0; s0 < nitems; s0 += nsub) {
+          const int nin = std::min(nsub, nitems - s0);
+          int32_t e[kRsStageWords];
+          for (int q = 0; q < W; ++q) e[q] = (q >= 5 && q <= 12) ? -1 : 0;
+          uint32_t flags = 0, np = 0;
+          const int slot = static_cast<int>(k % stages);
+          for (int sub = 0; sub < nin; ++sub) {
+            const int s_ = s0 + sub;
+            const int j = s_ / nkc, kci = s_ % nkc;
+            const int32_t* st = &steps[static_cast<size_t>(u.step_begin + j) * stride];
+            uint32_t present = 0;
+            for (int g = 0; g < G; ++g)
+              if (g < u.nrows && st[1 + g] >= 0) {
+                present |= 1u << g;
+                ++np;
+                e[5 + 4 * sub + g] = st[1 + g] * R + slab_off[g];
+              }
+            uint32_t& d = dirty[static_cast<size_t>(slot) * nsub + sub];
+            const uint32_t zero = ~present & all & d;
+            d = present;
+            flags |= (present << (4 * sub)) | (zero << (8 + 4 * sub));
+            e[3 + sub] = st[0] * C + kci * kc;
+            e[2] = kci * kc;  // a stage never mixes k-chunks when nsub == 2 (nkc == 1)
+          }
+          flags |= np << 16;
+          if (s0 == 0) flags |= RS_F_FIRST;
+          if (s0 + nin >= nitems) flags |= RS_F_LAST;
+          if (nin == 2) flags |= RS_F_TWO;
+          e[0] = static_cast<int32_t>(flags);
+          e[1] = b3d ? u.n0 / 64 : u.n0;
+          memcpy(out, e, sizeof(e));
+          out += W;
+          ++k;
+        }
+      }
+    }
+    return BSP_OK;
+  });
+}
+
+// The CTA-pair kernel's per-CTA stage lists (CTA 2c + r = rank r of pair c),
+// CTAs split over host threads.  Every entry slot is loaded at every stage
+// (absent blocks from a zero-filled box above the tensor), so no slot needs
+// clearing.
+static bsp_status pair_stage_lists(bsp_spmm_plan* p) {
+  const int W = kRsStageWords;
+  const int G = p->G, Rs = p->Rs, R = p->R, C = p->C, kc = p->kc, nkc = C / kc, slabs = R / Rs;
+  const int nsub = p->nsub, stride = p->step_stride;
+  const bool b3d = (p->N % 64 == 0);
+  const int64_t grid = static_cast<int64_t>(p->h_cta_begin.size()) - 1;
+  p->h_stage_list.resize(static_cast<size_t>(p->h_cta_stage_begin.back()) * W);
+  const std::vector<int32_t>& steps = p->h_steps;
+  return parallel_ranges(grid, planner_threads(grid, 4, 0), [&](int, int64_t c0, int64_t c1) {
+    for (int64_t cta = c0; cta < c1; ++cta) {
+      const int r = static_cast<int>(cta % 2);
+      int32_t* out = p->h_stage_list.data() + static_cast<size_t>(p->h_cta_stage_begin[cta]) * W;
+      for (int32_t ui = p->h_cta_begin[cta]; ui < p->h_cta_begin[cta + 1]; ++ui) {
+        const SpmmUnit& u = p->h_units[ui];
+        const int nsteps = u.step_end - u.step_begin;
+        if (nsteps == 0) {
+          int32_t e[kRsStageWords] = {RS_F_FIRST | RS_F_LAST | RS_F_EMPTY};
+          memcpy(out, e, sizeof(e));
+          out += W;
           continue;
         }
         int slab_off[4] = {0, 0, 0, 0};
@@ -718,7 +838,7 @@ bsp_status plan_spmm_pair(bsp_spmm_plan* p, const int32_t* row_ptr, const int32_
             if (sub >= nin) continue;
             const int s_ = s0 + sub;
             const int j = s_ / nkc, kci = s_ % nkc;
-            const int32_t* st = &steps[static_cast<size_t>(pu.s_begin + j) * stride];
+            const int32_t* st = &steps[static_cast<size_t>(u.step_begin + j) * stride];
             for (int g = 0; g < G; ++g) {
               const int gg = r * G + g;
               if (g < u.nrows && st[1 + gg] >= 0) e[5 + 4 * sub + g] = st[1 + gg] * R + slab_off[g];
@@ -730,23 +850,14 @@ bsp_status plan_spmm_pair(bsp_spmm_plan* p, const int32_t* row_ptr, const int32_
           if (s0 + nin >= nitems) flags |= RS_F_LAST;
           if (nin == 2) flags |= RS_F_TWO;
           e[0] = static_cast<int32_t>(flags);
-          e[1] = b3d ? pu.n0 / 64 + 2 * r : pu.n0 + 128 * r;
-          p->h_stage_list.insert(p->h_stage_list.end(), e, e + W);
+          e[1] = b3d ? u.n0 / 64 + 2 * r : u.n0 + 128 * r;
+          memcpy(out, e, sizeof(e));
+          out += W;
         }
       }
-      p->h_cta_begin.push_back(static_cast<int32_t>(p->h_units.size()));
-      if (p->h_stage_list.size() / W >= (size_t(1) << 31))
-        return set_error(BSP_ERR_UNSUPPORTED, "schedule too long");
-      p->h_cta_stage_begin.push_back(static_cast<int32_t>(p->h_stage_list.size() / W));
     }
-  }
-  if (steps.empty()) {
-    steps.push_back(0);
-    for (int q = 0; q < G2; ++q) steps.push_back(-1);
-  }
-  // one unit record per CTA of each pair unit
-  p->n_units = static_cast<int64_t>(p->h_units.size());
-  return BSP_OK;
+    return BSP_OK;
+  });
 }
 
 bsp_status plan_sddmm_host(bsp_sddmm_plan* p, const int32_t* row_ptr, const int32_t* col_idx,
@@ -1070,6 +1181,202 @@ static int spgemm_box_count(const SpgemmStep& st) {
   return n;
 }
 
+struct SgBuildCtx {
+  const bsp_spgemm_plan* p;
+  const int32_t *a_rp, *a_ci, *b_rp, *b_ci;
+  int64_t nbk, nbc;
+  int spr, segs_per_col;
+  int64_t n_ent;
+  int nkc;
+};
+
+struct SgBuildOut {
+  std::vector<SpgemmUnit> units;
+  std::vector<int64_t> weight;
+  std::vector<SpgemmStep> steps;  // step_begin of the units counts from this range's first step
+  int64_t n_steps = 0, n_boxes = 0;
+};
+
+// The units and steps of output groups [g_begin, g_end) for nseg_max
+// segments per unit.  count_only: only n_steps (no tables).
+static bsp_status sg_build_groups(const SgBuildCtx& c, int nseg_max, int64_t g_begin, int64_t g_end,
+                                  bool count_only, SgBuildOut* out) {
+  const bsp_spgemm_plan* p = c.p;
+  const int32_t *a_rp = c.a_rp, *a_ci = c.a_ci, *b_rp = c.b_rp, *b_ci = c.b_ci;
+  const int64_t nbk = c.nbk, nbc = c.nbc, n_ent = c.n_ent;
+  const int spr = c.spr, segs_per_col = c.segs_per_col, Ra = p->Ra;
+  auto& units = out->units;
+  auto& weight = out->weight;
+  auto& steps = out->steps;
+  out->n_steps = 0;
+  out->n_boxes = 0;
+  const int cpu = std::max(1, nseg_max / segs_per_col);  // block-columns per unit
+  std::vector<int32_t> colpos(static_cast<size_t>(nbc), -1), colstamp(static_cast<size_t>(nbc), -1);
+  std::vector<int32_t> kstamp(static_cast<size_t>(nbk), -1);
+  std::vector<int32_t> cols, ks;
+  // Per local block-row q of the group (at most 4): A blocks of column k
+  // (a_first / a_cnt into rowpairs[q], valid where a_stamp == g) and the
+  // output index of block-column j (o_idx, valid where o_stamp == g).
+  const int64_t rows_per_group = (kSpgemmEnt + spr - 1) / spr;
+  std::vector<int32_t> a_first_k(static_cast<size_t>(rows_per_group * nbk)),
+      a_cnt_k(static_cast<size_t>(rows_per_group * nbk)), a_stamp(static_cast<size_t>(rows_per_group * nbk), -1);
+  std::vector<int32_t> o_idx, o_stamp;
+  if (!count_only) {
+    o_idx.resize(static_cast<size_t>(rows_per_group * nbc));
+    o_stamp.assign(static_cast<size_t>(rows_per_group * nbc), -1);
+  }
+  // B blocks of the group's k's bucketed by unit (counting sort), k ascending
+  std::vector<int32_t> cb_off, cb_k, cb_b, fill;
+  std::vector<std::vector<int32_t>> bl(kSpgemmMaxSeg);  // B blocks of row k per unit column
+  // (k, A block) of each distinct block-row of the group, sorted by k (stable)
+  std::vector<std::vector<std::pair<int32_t, int32_t>>> rowpairs;
+  for (int64_t g = g_begin; g < g_end; ++g) {
+    const int32_t g32 = static_cast<int32_t>(g);
+    const int64_t e0 = g * kSpgemmEnt, e1 = std::min<int64_t>(n_ent, e0 + kSpgemmEnt);
+    const int64_t r0 = e0 / spr, r1 = (e1 - 1) / spr + 1;  // block-rows [r0, r1)
+    cols.clear();
+    for (int64_t i = r0; i < r1; ++i)
+      for (int32_t q = p->out_row_ptr[i]; q < p->out_row_ptr[i + 1]; ++q) {
+        const int32_t j = p->out_col_idx[q];
+        if (!count_only) {
+          const size_t oi = static_cast<size_t>((i - r0) * nbc + j);
+          o_stamp[oi] = g32;
+          o_idx[oi] = q;
+        }
+        if (colstamp[j] != g32) {
+          colstamp[j] = g32;
+          cols.push_back(j);
+        }
+      }
+    if (cols.empty()) continue;
+    std::sort(cols.begin(), cols.end());
+    for (size_t q = 0; q < cols.size(); ++q) colpos[cols[q]] = static_cast<int32_t>(q);
+    const int64_t nchunks = (static_cast<int64_t>(cols.size()) + cpu - 1) / cpu;
+    rowpairs.resize(static_cast<size_t>(r1 - r0));
+    ks.clear();
+    for (int64_t i = r0; i < r1; ++i) {
+      auto& v = rowpairs[static_cast<size_t>(i - r0)];
+      v.clear();
+      for (int32_t a = a_rp[i]; a < a_rp[i + 1]; ++a) {
+        v.push_back({a_ci[a], a});
+        if (kstamp[a_ci[a]] != g32) {
+          kstamp[a_ci[a]] = g32;
+          ks.push_back(a_ci[a]);
+        }
+      }
+      std::stable_sort(v.begin(), v.end(),
+                       [](const std::pair<int32_t, int32_t>& x, const std::pair<int32_t, int32_t>& y) {
+                         return x.first < y.first;
+                       });
+      for (size_t t = 0; t < v.size(); ++t) {
+        const size_t ai = static_cast<size_t>((i - r0) * nbk + v[t].first);
+        if (a_stamp[ai] != g32) {
+          a_stamp[ai] = g32;
+          a_first_k[ai] = static_cast<int32_t>(t);
+          a_cnt_k[ai] = 0;
+        }
+        ++a_cnt_k[ai];
+      }
+    }
+    std::sort(ks.begin(), ks.end());
+    cb_off.assign(static_cast<size_t>(nchunks + 1), 0);
+    for (int32_t k : ks)
+      for (int32_t b = b_rp[k]; b < b_rp[k + 1]; ++b) ++cb_off[static_cast<size_t>(colpos[b_ci[b]] / cpu + 1)];
+    for (int64_t q = 0; q < nchunks; ++q) cb_off[q + 1] += cb_off[q];
+    cb_k.resize(static_cast<size_t>(cb_off[nchunks]));
+    cb_b.resize(static_cast<size_t>(cb_off[nchunks]));
+    fill.assign(cb_off.begin(), cb_off.end() - 1);
+    for (int32_t k : ks)
+      for (int32_t b = b_rp[k]; b < b_rp[k + 1]; ++b) {
+        const size_t at = static_cast<size_t>(fill[static_cast<size_t>(colpos[b_ci[b]] / cpu)]++);
+        cb_k[at] = k;
+        cb_b[at] = b;
+      }
+    for (int64_t ch = 0; ch < nchunks; ++ch) {
+      SpgemmUnit u;
+      memset(&u, 0, sizeof(u));
+      const int64_t j0 = ch * cpu;
+      const int ncols = static_cast<int>(std::min<int64_t>(cpu, static_cast<int64_t>(cols.size()) - j0));
+      u.n_ent = static_cast<int32_t>(e1 - e0);
+      u.nseg = std::min(nseg_max, ncols * segs_per_col);
+      if (!count_only) {
+        // segments slice-major: segment s is 32-column slice s / ncols of
+        // column s % ncols, so that a slice of consecutive stored blocks of a
+        // row of B lands in consecutive segments (one TMA box)
+        for (int s_ = 0; s_ < kSpgemmMaxSeg; ++s_) u.seg_x[s_] = s_ < u.nseg ? (s_ / ncols) * 32 : 0;
+        for (int e = 0; e < kSpgemmEnt; ++e) {
+          const int64_t E = e0 + e;
+          u.ent_r[e] = E < e1 ? static_cast<int32_t>(E % spr) * 32 : 0;
+          for (int s_ = 0; s_ < kSpgemmMaxSeg; ++s_) {
+            u.out_blk[e][s_] = -1;
+            if (E >= e1 || s_ >= u.nseg) continue;
+            const int32_t j = cols[static_cast<size_t>(j0 + s_ % ncols)];
+            const size_t oi = static_cast<size_t>((E / spr - r0) * nbc + j);
+            if (o_stamp[oi] == g32) u.out_blk[e][s_] = o_idx[oi];
+          }
+        }
+      }
+      u.step_begin = static_cast<int32_t>(out->n_steps);
+      if (out->n_steps >= (int64_t(1) << 31) - 4096)
+        return set_error(BSP_ERR_UNSUPPORTED, "SpGEMM schedule too large");
+      for (int32_t t0 = cb_off[ch]; t0 < cb_off[ch + 1];) {
+        const int32_t k = cb_k[t0];
+        int32_t t1 = t0;
+        // B blocks of row k per unit column, A blocks of column k per entry
+        for (auto& l : bl) l.clear();
+        int lb_max = 0;
+        for (; t1 < cb_off[ch + 1] && cb_k[t1] == k; ++t1) {
+          auto& l = bl[static_cast<size_t>(colpos[b_ci[cb_b[t1]]] - j0)];
+          l.push_back(cb_b[t1]);
+          lb_max = std::max(lb_max, static_cast<int>(l.size()));
+        }
+        t0 = t1;
+        int32_t a_first[kSpgemmEnt], a_cnt[kSpgemmEnt];
+        int la_max = 0;
+        for (int e = 0; e < kSpgemmEnt; ++e) {
+          a_first[e] = 0;
+          a_cnt[e] = 0;
+          const int64_t E = e0 + e;
+          if (E >= e1) continue;
+          const size_t ai = static_cast<size_t>((E / spr - r0) * nbk + k);
+          if (a_stamp[ai] != g32) continue;
+          a_first[e] = a_first_k[ai];
+          a_cnt[e] = a_cnt_k[ai];
+          la_max = std::max(la_max, static_cast<int>(a_cnt[e]));
+        }
+        if (count_only) {
+          out->n_steps += static_cast<int64_t>(la_max) * lb_max;
+          continue;
+        }
+        for (int la = 0; la < la_max; ++la)
+          for (int lb = 0; lb < lb_max; ++lb) {
+            int32_t ay[kSpgemmEnt], bb[kSpgemmMaxSeg], bt[kSpgemmMaxSeg];
+            for (int e = 0; e < kSpgemmEnt; ++e) {
+              ay[e] = -1;
+              if (la < a_cnt[e]) {
+                const auto& v = rowpairs[static_cast<size_t>((e0 + e) / spr - r0)];
+                ay[e] = v[static_cast<size_t>(a_first[e] + la)].second * Ra + u.ent_r[e];
+              }
+            }
+            for (int s_ = 0; s_ < u.nseg; ++s_) {
+              const auto& l = bl[static_cast<size_t>(s_ % ncols)];
+              bb[s_] = lb < static_cast<int>(l.size()) ? l[static_cast<size_t>(lb)] : -1;
+              bt[s_] = s_ / ncols;
+            }
+            steps.push_back(spgemm_boxes(ay, bb, bt, u.nseg, p->la_log2, p->lb_log2));
+            out->n_boxes += spgemm_box_count(steps.back());
+            ++out->n_steps;
+          }
+      }
+      u.n_steps = static_cast<int32_t>(out->n_steps - u.step_begin);
+      if (u.n_steps == 0 || count_only) continue;  // (an empty unit cannot happen: every unit column has a product)
+      units.push_back(u);
+      weight.push_back(static_cast<int64_t>(u.n_steps) * c.nkc + 2);
+    }
+  }
+  return BSP_OK;
+}
+
 bsp_status plan_spgemm_host(bsp_spgemm_plan* p, const int32_t* a_rp, const int32_t* a_ci,
                             const int32_t* b_rp, const int32_t* b_ci, int sm_count, int max_smem,
                             const bsp_spmm_opts* opts) {
@@ -1092,28 +1399,47 @@ bsp_status plan_spgemm_host(bsp_spgemm_plan* p, const int32_t* a_rp, const int32
   st = check_pattern(b_rp, b_ci, nbk, nbc, p->nnzb_b);
   if (st != BSP_OK) return st;
 
-  // ---- output pattern (symbolic product) ----
+  // ---- output pattern (symbolic product), block-rows split over threads ----
+  // (int32 stamps: one per output block-column and thread, so the thread
+  // count also stays under a 256 MB budget for them)
+  const int nt_sym = planner_threads(nbr, 64, nbc * 4);
+  std::vector<std::vector<int32_t>> sym_cols(static_cast<size_t>(nt_sym));
+  std::vector<int64_t> sym_pairs(static_cast<size_t>(nt_sym), 0);
   p->out_row_ptr.assign(static_cast<size_t>(nbr + 1), 0);
-  p->out_col_idx.clear();
-  std::vector<int64_t> stamp(static_cast<size_t>(nbc), -1);
-  int64_t pairs = 0;
-  for (int64_t i = 0; i < nbr; ++i) {
-    const size_t start = p->out_col_idx.size();
-    for (int32_t a = a_rp[i]; a < a_rp[i + 1]; ++a) {
-      const int32_t k = a_ci[a];
-      pairs += b_rp[k + 1] - b_rp[k];
-      for (int32_t b = b_rp[k]; b < b_rp[k + 1]; ++b) {
-        const int32_t j = b_ci[b];
-        if (stamp[j] != i) {
-          stamp[j] = i;
-          p->out_col_idx.push_back(j);
+  st = parallel_ranges(nbr, nt_sym, [&](int t, int64_t i0, int64_t i1) {
+    std::vector<int32_t> stamp(static_cast<size_t>(nbc), -1);
+    auto& oc = sym_cols[static_cast<size_t>(t)];
+    for (int64_t i = i0; i < i1; ++i) {
+      const size_t start = oc.size();
+      for (int32_t a = a_rp[i]; a < a_rp[i + 1]; ++a) {
+        const int32_t k = a_ci[a];
+        sym_pairs[static_cast<size_t>(t)] += b_rp[k + 1] - b_rp[k];
+        for (int32_t b = b_rp[k]; b < b_rp[k + 1]; ++b) {
+          const int32_t j = b_ci[b];
+          if (stamp[j] != static_cast<int32_t>(i)) {
+            stamp[j] = static_cast<int32_t>(i);
+            oc.push_back(j);
+          }
         }
       }
+      std::sort(oc.begin() + static_cast<std::ptrdiff_t>(start), oc.end());
+      p->out_row_ptr[i + 1] = static_cast<int32_t>(oc.size() - start);  // row length for now
     }
-    std::sort(p->out_col_idx.begin() + static_cast<std::ptrdiff_t>(start), p->out_col_idx.end());
-    if (p->out_col_idx.size() >= (size_t(1) << 31))
-      return set_error(BSP_ERR_UNSUPPORTED, "output has too many blocks");
-    p->out_row_ptr[i + 1] = static_cast<int32_t>(p->out_col_idx.size());
+    return BSP_OK;
+  });
+  if (st != BSP_OK) return st;
+  int64_t pairs = 0, out_total = 0;
+  for (int t = 0; t < nt_sym; ++t) {
+    pairs += sym_pairs[static_cast<size_t>(t)];
+    out_total += static_cast<int64_t>(sym_cols[static_cast<size_t>(t)].size());
+  }
+  if (out_total >= (int64_t(1) << 31)) return set_error(BSP_ERR_UNSUPPORTED, "output has too many blocks");
+  for (int64_t i = 0; i < nbr; ++i) p->out_row_ptr[i + 1] += p->out_row_ptr[i];
+  p->out_col_idx.clear();
+  p->out_col_idx.reserve(static_cast<size_t>(out_total));
+  for (auto& v : sym_cols) {
+    p->out_col_idx.insert(p->out_col_idx.end(), v.begin(), v.end());
+    std::vector<int32_t>().swap(v);
   }
   p->pairs = pairs;
   const int64_t out_nnzb = static_cast<int64_t>(p->out_col_idx.size());
@@ -1135,175 +1461,72 @@ bsp_status plan_spgemm_host(bsp_spgemm_plan* p, const int32_t* a_rp, const int32
   while (p->la_log2 < 2 && (int64_t(32) << (p->la_log2 + 1)) <= p->nnzb_a * Ra) ++p->la_log2;
   p->lb_log2 = 0;
   while (p->lb_log2 < 3 && (int64_t(1) << (p->lb_log2 + 1)) <= p->nnzb_b) ++p->lb_log2;
-  // The unit list and step table for nseg_max segments per unit.
-  auto build = [&](int nseg_max, std::vector<SpgemmUnit>& units, std::vector<int64_t>& weight,
-                   std::vector<SpgemmStep>& steps, int64_t& n_boxes) -> bsp_status {
-    n_boxes = 0;
-    units.clear();
-    weight.clear();
-    steps.clear();
-    const int cpu = std::max(1, nseg_max / segs_per_col);  // block-columns per unit
-    std::vector<int64_t> colpos(static_cast<size_t>(nbc), -1), colstamp(static_cast<size_t>(nbc), -1);
-    std::vector<int64_t> kstamp(static_cast<size_t>(nbk), -1);
-    std::vector<int32_t> cols, ks;
-    std::vector<std::vector<int32_t>> chunk_k;
-    std::vector<int32_t> lastk;
-    std::vector<std::vector<int32_t>> bl(kSpgemmMaxSeg);  // B blocks of row k per unit column
-    // (k, A block) of each distinct block-row of the group, sorted by k (stable)
-    std::vector<std::vector<std::pair<int32_t, int32_t>>> rowpairs;
-    for (int64_t g = 0; g < ngroups; ++g) {
-      const int64_t e0 = g * kSpgemmEnt, e1 = std::min<int64_t>(n_ent, e0 + kSpgemmEnt);
-      const int64_t r0 = e0 / spr, r1 = (e1 - 1) / spr + 1;  // block-rows [r0, r1)
-      cols.clear();
-      for (int64_t i = r0; i < r1; ++i)
-        for (int32_t q = p->out_row_ptr[i]; q < p->out_row_ptr[i + 1]; ++q) {
-          const int32_t j = p->out_col_idx[q];
-          if (colstamp[j] != g) {
-            colstamp[j] = g;
-            cols.push_back(j);
-          }
-        }
-      if (cols.empty()) continue;
-      std::sort(cols.begin(), cols.end());
-      for (size_t c = 0; c < cols.size(); ++c) colpos[cols[c]] = static_cast<int64_t>(c);
-      const int64_t nchunks = (static_cast<int64_t>(cols.size()) + cpu - 1) / cpu;
-      rowpairs.assign(static_cast<size_t>(r1 - r0), {});
-      ks.clear();
-      for (int64_t i = r0; i < r1; ++i) {
-        auto& v = rowpairs[static_cast<size_t>(i - r0)];
-        for (int32_t a = a_rp[i]; a < a_rp[i + 1]; ++a) {
-          v.push_back({a_ci[a], a});
-          if (kstamp[a_ci[a]] != g) {
-            kstamp[a_ci[a]] = g;
-            ks.push_back(a_ci[a]);
-          }
-        }
-        std::stable_sort(v.begin(), v.end(),
-                         [](const std::pair<int32_t, int32_t>& x, const std::pair<int32_t, int32_t>& y) {
-                           return x.first < y.first;
-                         });
+
+  const SgBuildCtx ctx{p, a_rp, a_ci, b_rp, b_ci, nbk, nbc, spr, segs_per_col, n_ent, nkc};
+  // Groups split over threads; each range's units and steps are appended in
+  // range order, so the schedule does not depend on the thread count.
+  const int64_t scratch_per_thread = (nbc + nbk) * 48;
+  auto run = [&](int nseg, bool count_only, std::vector<SpgemmUnit>* units, std::vector<int64_t>* weight,
+                 int64_t* n_steps, int64_t* n_boxes) -> bsp_status {
+    const int nt = planner_threads(ngroups, 8, scratch_per_thread);
+    std::vector<SgBuildOut> parts(static_cast<size_t>(nt));
+    bsp_status s2 = parallel_ranges(ngroups, nt, [&](int t, int64_t g0, int64_t g1) {
+      return sg_build_groups(ctx, nseg, g0, g1, count_only, &parts[static_cast<size_t>(t)]);
+    });
+    if (s2 != BSP_OK) return s2;
+    *n_steps = 0;
+    *n_boxes = 0;
+    int64_t n_units = 0;
+    for (const auto& q : parts) {
+      *n_steps += q.n_steps;
+      *n_boxes += q.n_boxes;
+      n_units += static_cast<int64_t>(q.units.size());
+    }
+    if (*n_steps >= (int64_t(1) << 31) - 4096) return set_error(BSP_ERR_UNSUPPORTED, "SpGEMM schedule too large");
+    if (count_only) return BSP_OK;
+    units->clear();
+    weight->clear();
+    units->reserve(static_cast<size_t>(n_units));
+    weight->reserve(static_cast<size_t>(n_units));
+    p->h_steps.clear();
+    p->h_steps.reserve(static_cast<size_t>(*n_steps));
+    for (auto& q : parts) {
+      const int32_t off = static_cast<int32_t>(p->h_steps.size());
+      for (SpgemmUnit u : q.units) {
+        u.step_begin += off;
+        units->push_back(u);
       }
-      std::sort(ks.begin(), ks.end());
-      chunk_k.assign(static_cast<size_t>(nchunks), {});
-      lastk.assign(static_cast<size_t>(nchunks), -1);
-      for (int32_t k : ks)
-        for (int32_t b = b_rp[k]; b < b_rp[k + 1]; ++b) {
-          const int64_t c = colpos[b_ci[b]] / cpu;
-          if (lastk[c] != k) {
-            lastk[c] = k;
-            chunk_k[c].push_back(k);
-          }
-        }
-      for (int64_t c = 0; c < nchunks; ++c) {
-        SpgemmUnit u;
-        memset(&u, 0, sizeof(u));
-        const int64_t j0 = c * cpu;
-        const int ncols = static_cast<int>(std::min<int64_t>(cpu, static_cast<int64_t>(cols.size()) - j0));
-        u.n_ent = static_cast<int32_t>(e1 - e0);
-        u.nseg = std::min(nseg_max, ncols * segs_per_col);
-        // segments slice-major: segment s is 32-column slice s / ncols of
-        // column s % ncols, so that a slice of consecutive stored blocks of a
-        // row of B lands in consecutive segments (one TMA box)
-        for (int s_ = 0; s_ < kSpgemmMaxSeg; ++s_) u.seg_x[s_] = s_ < u.nseg ? (s_ / ncols) * 32 : 0;
-        for (int e = 0; e < kSpgemmEnt; ++e) {
-          const int64_t E = e0 + e;
-          u.ent_r[e] = E < e1 ? static_cast<int32_t>(E % spr) * 32 : 0;
-          for (int s_ = 0; s_ < kSpgemmMaxSeg; ++s_) {
-            u.out_blk[e][s_] = -1;
-            if (E >= e1 || s_ >= u.nseg) continue;
-            const int64_t i = E / spr;
-            const int32_t j = cols[static_cast<size_t>(j0 + s_ % ncols)];
-            const int32_t* lo = p->out_col_idx.data() + p->out_row_ptr[i];
-            const int32_t* hi = p->out_col_idx.data() + p->out_row_ptr[i + 1];
-            const int32_t* it = std::lower_bound(lo, hi, j);
-            if (it != hi && *it == j) u.out_blk[e][s_] = static_cast<int32_t>(it - p->out_col_idx.data());
-          }
-        }
-        u.step_begin = static_cast<int32_t>(steps.size());
-        if (steps.size() >= (size_t(1) << 31) - 4096)
-          return set_error(BSP_ERR_UNSUPPORTED, "SpGEMM schedule too large");
-        for (int32_t k : chunk_k[c]) {
-          // A blocks of column k per entry, B blocks of row k per unit column
-          int32_t a_first[kSpgemmEnt], a_cnt[kSpgemmEnt];
-          int la_max = 0;
-          for (int e = 0; e < kSpgemmEnt; ++e) {
-            a_first[e] = 0;
-            a_cnt[e] = 0;
-            const int64_t E = e0 + e;
-            if (E >= e1) continue;
-            const auto& v = rowpairs[static_cast<size_t>(E / spr - r0)];
-            auto it = std::lower_bound(v.begin(), v.end(), std::make_pair(k, INT32_MIN));
-            a_first[e] = static_cast<int32_t>(it - v.begin());
-            while (it != v.end() && it->first == k) {
-              ++a_cnt[e];
-              ++it;
-            }
-            la_max = std::max(la_max, static_cast<int>(a_cnt[e]));
-          }
-          for (auto& l : bl) l.clear();
-          int lb_max = 0;
-          for (int32_t b = b_rp[k]; b < b_rp[k + 1]; ++b) {
-            const int64_t pos = colpos[b_ci[b]];
-            if (pos / cpu != c) continue;
-            auto& l = bl[static_cast<size_t>(pos - j0)];
-            l.push_back(b);
-            lb_max = std::max(lb_max, static_cast<int>(l.size()));
-          }
-          for (int la = 0; la < la_max; ++la)
-            for (int lb = 0; lb < lb_max; ++lb) {
-              int32_t ay[kSpgemmEnt], bb[kSpgemmMaxSeg], bt[kSpgemmMaxSeg];
-              for (int e = 0; e < kSpgemmEnt; ++e) {
-                ay[e] = -1;
-                if (la < a_cnt[e]) {
-                  const auto& v = rowpairs[static_cast<size_t>((e0 + e) / spr - r0)];
-                  ay[e] = v[static_cast<size_t>(a_first[e] + la)].second * Ra + u.ent_r[e];
-                }
-              }
-              for (int s_ = 0; s_ < u.nseg; ++s_) {
-                const auto& l = bl[static_cast<size_t>(s_ % ncols)];
-                bb[s_] = lb < static_cast<int>(l.size()) ? l[static_cast<size_t>(lb)] : -1;
-                bt[s_] = s_ / ncols;
-              }
-              steps.push_back(spgemm_boxes(ay, bb, bt, u.nseg, p->la_log2, p->lb_log2));
-              n_boxes += spgemm_box_count(steps.back());
-            }
-        }
-        u.n_steps = static_cast<int32_t>(steps.size()) - u.step_begin;
-        if (u.n_steps == 0) continue;  // cannot happen: every unit column has a product
-        units.push_back(u);
-        weight.push_back(static_cast<int64_t>(u.n_steps) * nkc + 2);
-      }
+      weight->insert(weight->end(), q.weight.begin(), q.weight.end());
+      p->h_steps.insert(p->h_steps.end(), q.steps.begin(), q.steps.end());
+      std::vector<SpgemmStep>().swap(q.steps);
     }
     return BSP_OK;
   };
   // MMA N = 256 (8 segments) unless the caller asks for 128; when 256-wide
   // tiles would be mostly empty, N = 128 is taken if its schedule moves fewer
   // operand bytes (a step costs about its bytes: the smem fill rate bounds it).
+  // The choice needs only step counts, so only the chosen width is built.
   std::vector<SpgemmUnit> units;
   std::vector<int64_t> weight;
   int nseg_max = (o.n_tiles == 1) ? 4 : 8;
-  st = build(nseg_max, units, weight, p->h_steps, p->n_boxes);
-  if (st != BSP_OK) return st;
-  if (o.n_tiles == 0 && !p->h_steps.empty()) {
-    const double fill = static_cast<double>(pairs) * spr * segs_per_col /
-                        (static_cast<double>(p->h_steps.size()) * kSpgemmEnt * 8);
+  if (o.n_tiles == 0) {
+    int64_t n8 = 0, b8 = 0;
+    st = run(8, true, nullptr, nullptr, &n8, &b8);
+    if (st != BSP_OK) return st;
+    const double fill = n8 > 0 ? static_cast<double>(pairs) * spr * segs_per_col /
+                                     (static_cast<double>(n8) * kSpgemmEnt * 8)
+                               : 1.0;
     if (fill < 0.5) {
-      std::vector<SpgemmUnit> u4;
-      std::vector<int64_t> w4;
-      std::vector<SpgemmStep> s4;
-      int64_t b4 = 0;
-      st = build(4, u4, w4, s4, b4);
+      int64_t n4 = 0, b4 = 0;
+      st = run(4, true, nullptr, nullptr, &n4, &b4);
       if (st != BSP_OK) return st;
       auto sub = [&](int n) { return static_cast<double>(kSpgemmEnt * 32 * kc * 2 + n * kc * 64); };
-      if (static_cast<double>(s4.size()) * sub(4) < static_cast<double>(p->h_steps.size()) * sub(8)) {
-        units.swap(u4);
-        weight.swap(w4);
-        p->h_steps.swap(s4);
-        p->n_boxes = b4;
-        nseg_max = 4;
-      }
+      if (static_cast<double>(n4) * sub(4) < static_cast<double>(n8) * sub(8)) nseg_max = 4;
     }
   }
+  int64_t n_steps_total = 0;
+  st = run(nseg_max, false, &units, &weight, &n_steps_total, &p->n_boxes);
+  if (st != BSP_OK) return st;
   p->nseg_max = nseg_max;
   p->n_steps = static_cast<int64_t>(p->h_steps.size());
 

@@ -237,3 +237,23 @@ def test_unit_width_choice():
     ci = np.array([c for r in rows for c in r], np.int32)
     p = bsp.inspect_spgemm_plan(n * 32, n * 32, n * 32, 32, 32, 32, rp, ci, rp, ci)
     assert p["nseg_max"] == 8
+
+
+@pytest.mark.parametrize("Ra,Cb", [(32, 32), (64, 32), (32, 64)])
+def test_plan_independent_of_planner_threads(monkeypatch, Ra, Cb):
+    """The planner splits block-rows and row groups over host threads and
+    appends the pieces in order: the output pattern, units, steps and CTA
+    ranges are the same for any thread count."""
+    rng = np.random.default_rng(31 + Ra + Cb)
+    arp, aci = rand_pattern(rng, 96, 80, 0.06, empty_rows=(5, 6), repeats=2)
+    brp, bci = rand_pattern(rng, 80, 90, 0.06, empty_rows=(3,), repeats=1)
+    plans = []
+    for threads in ("1", "3", "7"):
+        monkeypatch.setenv("BSP_PLANNER_THREADS", threads)
+        plans.append(bsp.inspect_spgemm_plan(96 * Ra, 80 * 32, 90 * Cb, Ra, 32, Cb, arp, aci, brp, bci))
+    for p in plans[1:]:
+        for key in ("out_row_ptr", "out_col_idx", "unit_table", "step_table", "cta_begin"):
+            assert np.array_equal(p[key], plans[0][key]), key
+        assert all(p[k] == plans[0][k] for k in bsp.SPGEMM_INFO_KEYS)
+    monkeypatch.setenv("BSP_PLANNER_THREADS", "4")
+    check_case(rng, 96 * Ra, 80 * 32, 90 * Cb, Ra, 32, Cb, arp, aci, brp, bci)

@@ -626,7 +626,7 @@ class DevOp:
         if self.kind == "spgemm":
             return "spgemm_tcgen05"
         if self.kind == "sddmm":
-            return "sddmm_bsr_tcgen05"
+            return "sddmm_rowstack_tcgen05" if self.plan.info().get("variant", 0) == 1 else "sddmm_bsr_tcgen05"
         return {1: "spmm_rowstack_tcgen05", 2: "spmm_pair_tcgen05"}.get(self.plan.info().get("variant", 0),
                                                                       "spmm_bsr_tcgen05")
 
@@ -635,15 +635,14 @@ class DevOp:
 
 
 def strategy_for(op, name):
-    """`--strategy auto`: DDA (row-stacked, N = 256 MMAs) for SpMM with N >= 256,
-    SnF (swap-AB, 128-column tiles) for narrower B, CDA for SDDMM."""
+    """`--strategy auto`: DDA for SpMM (row-stacked: N = 256 MMAs, or N = 128
+    tiles for a B of at most 128 columns; measured faster than the swap-AB SnF
+    kernel on config 4's P V, 49 vs 74 us), CDA for SDDMM."""
     import bsp
 
     if name != "auto":
         return bsp.STRATEGIES[name]
-    if op["kind"] in ("sddmm", "attn", "spgemm"):
-        return bsp.DDA
-    return bsp.DDA if op["N"] >= 256 else bsp.SNF
+    return bsp.DDA
 
 
 def run_bsp(args):

@@ -361,7 +361,7 @@ class SddmmPlan:
     def info(self) -> dict:
         arr = (ctypes.c_int64 * 16)()
         _check(lib().bsp_sddmm_plan_info(self.handle, arr))
-        keys = ["units", "ctas", "_2", "_3", "slab", "kc", "stages", "_7", "plan_bytes",
+        keys = ["units", "ctas", "_2", "_3", "slab", "kc", "stages", "keep_a", "plan_bytes",
                 "smem_bytes", "tmem_cols", "variant", "_12", "nseg_max", "producers"]
         return {k: int(arr[i]) for i, k in enumerate(keys) if not k.startswith("_")}
 
@@ -712,7 +712,7 @@ def inspect_sddmm_plan(M, N, R, C, row_ptr, col_idx, K, strategy=NAIVE, opts=Non
     cta = np.zeros(int(info[1]) + 1, np.int32)
     _check(lib().bsp_sddmm_plan_inspect(*args, _ptr(units), _ptr(cta)))
     return dict(units=int(info[0]), ctas=int(info[1]), slab=int(info[4]), kc=int(info[5]),
-                stages=int(info[6]), variant=int(info[11]), nseg_max=int(info[13]),
+                stages=int(info[6]), keep_a=int(info[7]), variant=int(info[11]), nseg_max=int(info[13]),
                 producers=int(info[14]), unit_table=units[: int(info[0])], cta_begin=cta)
 
 

@@ -738,6 +738,7 @@ bsp_status bsp_sddmm_plan_info(const bsp_sddmm_plan* p, int64_t info[16]) {
   info[4] = p->Rs;
   info[5] = p->kc;
   info[6] = p->stages;
+  info[7] = p->keep_a;
   info[8] = static_cast<int64_t>(p->blob_bytes);
   info[9] = p->smem_bytes;
   info[10] = p->tmem_cols;

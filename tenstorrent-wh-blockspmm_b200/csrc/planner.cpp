@@ -174,6 +174,27 @@ static void contiguous_split(int64_t n, int parts, std::vector<std::vector<int32
   }
 }
 
+// Contiguous runs of items with about equal total weight: part p ends at the
+// first item where the running total reaches (p + 1) / parts of the whole.
+static void contiguous_weighted_split(const std::vector<int64_t>& weight, int parts,
+                                      std::vector<std::vector<int32_t>>* per_part) {
+  per_part->assign(parts, {});
+  int64_t total = 0;
+  for (int64_t w : weight) total += w;
+  int64_t acc = 0;
+  int p = 0;
+  const int64_t n = static_cast<int64_t>(weight.size());
+  for (int64_t i = 0; i < n; ++i) {
+    // keep at least one item for every later part
+    while (p < parts - 1 && acc * parts >= total * (p + 1) && n - i >= parts - p - 1 &&
+           !(*per_part)[p].empty())
+      ++p;
+    if (p < parts - 1 && n - i == parts - p - 1 && !(*per_part)[p].empty()) ++p;
+    (*per_part)[p].push_back(static_cast<int32_t>(i));
+    acc += weight[static_cast<size_t>(i)];
+  }
+}
+
 static bsp_status check_pattern(const int32_t* row_ptr, const int32_t* col_idx, int64_t nbr,
                                 int64_t nbc, int64_t nnzb) {
   if (row_ptr[0] != 0) return set_error(BSP_ERR_INVALID_ARG, "row_ptr[0] must be 0");
@@ -217,6 +238,9 @@ bsp_status plan_spmm_host(bsp_spmm_plan* p, const int32_t* row_ptr, const int32_
   if (p->strategy == BSP_DDA && o.group_mma != 2 && o.group_mma != 3) {
     if (o.group_mma == 4 || sm_count < 2) return plan_spmm_rowstack(p, row_ptr, col_idx, sm_count, max_smem, opts);
     if (o.group_mma == 5) return plan_spmm_pair(p, row_ptr, col_idx, sm_count, max_smem, opts);
+    // a pair CTA loads one 128-column half of a 256-column tile: with N <= 128
+    // one of the two would load nothing but out-of-range zeros
+    if (p->N <= 128) return plan_spmm_rowstack(p, row_ptr, col_idx, sm_count, max_smem, opts);
     // Both schedules without their stage lists (the choice needs only the
     // stage counts); the lists are then built for the winner alone.
     bsp_status st1 = plan_spmm_rowstack(p, row_ptr, col_idx, sm_count, max_smem, opts, false);
@@ -415,14 +439,17 @@ bsp_status plan_spmm_rowstack(bsp_spmm_plan* p, const int32_t* row_ptr, const in
   const int kc = (C % 64 == 0) ? 64 : 32;
   const int nkc = C / kc;
   const int64_t n_entries = nbr * slabs;
-  const int ntiles = static_cast<int>((p->N + 255) / 256);
+  // 256-column tiles (MMA N = 256); a B of at most 128 columns gets 128-column
+  // tiles (MMA N = 128) instead of a 256-column box half out of range
+  const int tile_n = p->N <= 128 ? 128 : 256;
+  const int ntiles = static_cast<int>((p->N + tile_n - 1) / tile_n);
   if (n_entries >= (int64_t(1) << 31))
     return set_error(BSP_ERR_UNSUPPORTED, "too many block-rows");
   p->variant = 1;
   p->Rs = Rs;
   p->kc = kc;
   p->G = G;
-  p->NT = 2;  // 256 columns = two 128-column tiles
+  p->NT = tile_n / 128;  // 128-column tiles per unit
   p->stacked = 1;
   const int stride = 1 + G;
   p->step_stride = stride;
@@ -471,15 +498,15 @@ bsp_status plan_spmm_rowstack(bsp_spmm_plan* p, const int32_t* row_ptr, const in
       u.row0 = static_cast<int32_t>(e0);
       u.nrows = nent;
       u.r_off = 0;
-      u.n0 = t * 256;
+      u.n0 = t * tile_n;
       u.nt = 1;
       u.step_begin = s_begin;
       u.step_end = s_end;
       u.row_mask = mask;
       units.push_back(u);
-      const int64_t smem_in = int64_t(nkc) * ((s_end - s_begin) * int64_t(kc) * 256 * 2 +
-                                              a_loads * int64_t(Rs) * kc * 2 / std::max(1, 1));
-      weight.push_back(smem_in + int64_t(nent) * Rs * 256 * esz + 4096);
+      const int64_t smem_in = int64_t(nkc) * ((s_end - s_begin) * int64_t(kc) * tile_n * 2 +
+                                              a_loads * int64_t(Rs) * kc * 2);
+      weight.push_back(smem_in + int64_t(nent) * Rs * tile_n * esz + 4096);
     }
   }
   p->n_steps = static_cast<int64_t>(steps.size() / stride);
@@ -508,7 +535,7 @@ bsp_status plan_spmm_rowstack(bsp_spmm_plan* p, const int32_t* row_ptr, const in
   // on B200 that beats the deeper one-step ring at every density from 5%.
   int nsub = 1;
   if (kc == 32 && nkc == 1 && o.steps_per_stage != 1) nsub = 2;
-  const int sub_bytes = 4 * kc * 128 + G * Rs * kc * 2;
+  const int sub_bytes = (tile_n / 64) * kc * 128 + G * Rs * kc * 2;
   p->sub_bytes = sub_bytes;
   p->nsub = nsub;
   int stage_bytes = nsub * sub_bytes;
@@ -542,7 +569,7 @@ bsp_status plan_spmm_rowstack(bsp_spmm_plan* p, const int32_t* row_ptr, const in
     p->xfer_off = 1024 + stages * stage_bytes;
     p->smem_bytes += 16384;
   }
-  p->tmem_cols = 512;
+  p->tmem_cols = 2 * tile_n;
   p->timeout_ns = static_cast<uint64_t>(o.timeout_ms > 0 ? o.timeout_ms : 2000) * 1000000ull;
 
   bsp_status st = spmm_stage_counts(p);
@@ -1070,8 +1097,12 @@ bsp_status plan_sddmm_rowstack(bsp_sddmm_plan* p, const int32_t* row_ptr, const 
   grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(grid, units.size())));
   std::vector<std::vector<int32_t>> per;
   if (o.no_load_balance || p->strategy == BSP_DDA) {
-    // CDA: a row group's units stay together on one CTA (A rows reused from L2)
+    // CDA: a row group's units stay together on one CTA (A rows reused)
     contiguous_split(static_cast<int64_t>(units.size()), grid, &per);
+  } else if (p->strategy == BSP_SNF) {
+    // SnF: contiguous runs balanced by weight, so each CTA loads a row
+    // group's A tile once and streams the group's B segments past it
+    contiguous_weighted_split(weight, grid, &per);
   } else {
     serpentine_order(weight, grid, &per);
   }
@@ -1085,18 +1116,48 @@ bsp_status plan_sddmm_rowstack(bsp_sddmm_plan* p, const int32_t* row_ptr, const 
   p->n_units = static_cast<int64_t>(units.size());
   p->grid = grid;
 
-  int stage_bytes = 128 * kc * 2 + nseg_max * kc * 64;
-  stage_bytes = (stage_bytes + 1023) / 1024 * 1024;
-  const int max_stages = std::min(sddmm_rowstack_max_stages(), (max_smem - 2048) / stage_bytes);
+  // Resident A (CDA and SnF; opts.group_rows = -1 turns it off): two
+  // 128 x K A tiles beside a ring of B-only stages, when K <= 256 and at
+  // least two stages still fit.
+  const int a_tile = 128 * static_cast<int>(K) * 2;
+  const int b_stage = (nseg_max * kc * 64 + 1023) / 1024 * 1024;
+  p->keep_a = (p->strategy == BSP_DDA || p->strategy == BSP_SNF) && o.group_rows != -1 && K <= 256 &&
+                      (max_smem - 2048 - 2 * a_tile) / b_stage >= 2
+                  ? 1
+                  : 0;
+  if (p->keep_a) {
+    // runs of equal row0 in each CTA's list: pad[0] = run index << 1 | first, pad[1] = last
+    for (int c = 0; c < grid; ++c) {
+      int32_t run = -1;
+      for (int32_t ui = p->h_cta_begin[c]; ui < p->h_cta_begin[c + 1]; ++ui) {
+        SddmmRsUnit& u = p->h_rs_units[ui];
+        const bool first = ui == p->h_cta_begin[c] || u.row0 != p->h_rs_units[ui - 1].row0;
+        if (first) {
+          ++run;
+          if (ui > p->h_cta_begin[c]) p->h_rs_units[ui - 1].pad[1] = 1;
+        }
+        u.pad[0] = (run << 1) | (first ? 1 : 0);
+        u.pad[1] = 0;
+      }
+      if (p->h_cta_begin[c + 1] > p->h_cta_begin[c]) p->h_rs_units[p->h_cta_begin[c + 1] - 1].pad[1] = 1;
+    }
+  }
+
+  const int stage_bytes = p->keep_a ? b_stage : (128 * kc * 2 + nseg_max * kc * 64 + 1023) / 1024 * 1024;
+  const int ring_smem = max_smem - 2048 - (p->keep_a ? 2 * a_tile : 0);
+  const int max_stages = std::min(sddmm_rowstack_max_stages(), ring_smem / stage_bytes);
   if (max_stages < 2) return set_error(BSP_ERR_UNSUPPORTED, "stage too large for the pipeline");
   int nprod = 1, stages = max_stages;
   if (o.producers > 0) {
     nprod = std::min({o.producers, sddmm_rowstack_max_producers(), max_stages});
     stages = max_stages / nprod * nprod;
   } else {
+    // More producer warps beat one more stage here (measured on B200 with the
+    // config 4 mask: one producer over 5 stages 35 us, two over 4 and three
+    // over 3 both 29 us), so up to one stage of the ring is given up for them.
     for (int q = 2; q <= std::min(sddmm_rowstack_max_producers(), max_stages); ++q) {
       const int sq = max_stages / q * q;
-      if (sq >= stages - (stages > 6 ? 1 : 0)) {
+      if (sq >= 2 && sq >= max_stages - 1) {
         nprod = q;
         stages = sq;
       }
@@ -1105,7 +1166,7 @@ bsp_status plan_sddmm_rowstack(bsp_sddmm_plan* p, const int32_t* row_ptr, const 
   p->nprod = nprod;
   p->stage_bytes = stage_bytes;
   p->stages = stages;
-  p->smem_bytes = 2048 + stages * stage_bytes;
+  p->smem_bytes = 2048 + (p->keep_a ? 2 * a_tile : 0) + stages * stage_bytes;
   p->tmem_cols = pow2_at_least(2 * 32 * nseg_max);
   p->timeout_ns = static_cast<uint64_t>(o.timeout_ms > 0 ? o.timeout_ms : 2000) * 1000000ull;
   return BSP_OK;
@@ -1738,7 +1799,7 @@ void spmm_plan_traffic(const bsp_spmm_plan& p, int64_t out[4]) {
     return;
   }
   const size_t W = kRsStageWords;
-  const int64_t b_cols = p.variant == 2 ? 128 : 256;  // a pair CTA loads half of the 256 columns
+  const int64_t b_cols = p.variant == 2 ? 128 : 128 * p.NT;  // a pair CTA loads half of the 256 columns
   for (size_t k = 0; k + W <= p.h_stage_list.size(); k += W) {
     const uint32_t flags = static_cast<uint32_t>(p.h_stage_list[k]);
     if (flags & RS_F_EMPTY) continue;

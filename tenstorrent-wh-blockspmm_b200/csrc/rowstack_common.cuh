@@ -81,14 +81,15 @@ __device__ __forceinline__ void rs_epilogue(const SpmmKernelParams& p, RsSmemHea
       const int e = un.row0 + g;
       const int64_t row = static_cast<int64_t>(e / slabs) * p.R + (e % slabs) * p.Rs + rrow;
       const bool present = (un.row_mask >> g) & 1;
+      const int nchunk = p.acc_cols / 32;  // 32-column chunks of the unit's tile
 #pragma unroll 1
-      for (int c = 0; c < kRsN / 32; ++c) {
+      for (int c = 0; c < nchunk; ++c) {
         const int n = un.n0 + c * 32;
         if (n >= p.N) break;
         uint32_t v[32];
         if (present) {
           tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
-                                 static_cast<uint32_t>(acc * kRsN + c * 32),
+                                 static_cast<uint32_t>(acc * p.acc_cols + c * 32),
                              v);
           tmem_ld_wait();
         } else {
@@ -137,7 +138,7 @@ __device__ __forceinline__ void rs_epilogue(const SpmmKernelParams& p, RsSmemHea
         }
         // flush the staged 128-byte segments after the segment's last chunk
         if (staged && (c % kChunksPerFlush == kChunksPerFlush - 1 || n + 32 >= p.N ||
-                       c == kRsN / 32 - 1)) {
+                       c == nchunk - 1)) {
           __syncwarp();
           const int nseg0 = un.n0 + (c - c % kChunksPerFlush) * 32;  // first column of the segment
           const int64_t row_w = row - lane;                             // the warp's first row

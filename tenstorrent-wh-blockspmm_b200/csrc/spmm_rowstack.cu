@@ -15,7 +15,8 @@
 //           one CTA's shared memory;
 //   MMA N = 256 dense columns (MN-major B operand, four 64-column 128B-swizzle
 //           boxes from one 3-D TMA load), so every A block is reused across
-//           256 columns (the store-and-forward reuse of in0);
+//           256 columns (the store-and-forward reuse of in0); a B of at most
+//           128 columns takes 128-column tiles (N = 128, two boxes) instead;
 //   MMA K = C, in chunks of kc per pipeline stage, 16 per MMA.
 // The fp32 accumulator (128 lanes = output rows x 256 columns) sits in TMEM,
 // double-buffered; an epilogue thread owns one output row and writes 32
@@ -51,7 +52,8 @@ __device__ __forceinline__ void rs_producer(const SpmmKernelParams& p, RsSmemHea
   const int n = p.cta_stage_begin[blockIdx.x + 1] - k_begin;
   const uint32_t a_slot = static_cast<uint32_t>(p.Rs * p.kc * 2);
   const uint32_t b_blk = static_cast<uint32_t>(p.kc * 128);  // one 64-column block
-  const uint32_t b_bytes = 4u * b_blk;
+  const uint32_t nb = 2u * static_cast<uint32_t>(p.NT);        // 64-column blocks per tile (4 or 2)
+  const uint32_t b_bytes = nb * b_blk;
   const uint32_t sub_bytes = static_cast<uint32_t>(p.sub_bytes);
   int stage = pw;
   uint32_t phase = 0;
@@ -125,7 +127,8 @@ __device__ __forceinline__ void rs_producer(const SpmmKernelParams& p, RsSmemHea
               tma_load_3d_pred(qb, &p.tm_b, 0, ky, bz, full, is0);
             } else {
 #pragma unroll
-              for (int h = 0; h < 4; ++h) tma_load_2d_pred(qb + h * b_blk, &p.tm_b, bz + h * 64, ky, full, is0);
+              for (int h = 0; h < 4; ++h)
+                if (h < static_cast<int>(nb)) tma_load_2d_pred(qb + h * b_blk, &p.tm_b, bz + h * 64, ky, full, is0);
             }
 #pragma unroll
             for (int g = 0; g < kRsMaxG; ++g)
@@ -168,8 +171,8 @@ __device__ __forceinline__ void rs_mma(const SpmmKernelParams& p, RsSmemHeader* 
   // A (stacked entries): K-major, rows of kc*2 bytes; B: MN-major 128B swizzle,
   // LBO = one 64-column block (kc rows x 128 B), SBO = 8 k-rows; a 16-row
   // k-step of B is 2048 bytes, a 16-column k-step of A is 32 bytes.
-  const uint32_t idesc = idesc_bf16_f32(128, kRsN, /*a K-major*/ 0, /*b MN-major*/ 1);
-  const uint32_t b_bytes = static_cast<uint32_t>(4 * p.kc * 128);
+  const uint32_t idesc = idesc_bf16_f32(128, p.acc_cols, /*a K-major*/ 0, /*b MN-major*/ 1);
+  const uint32_t b_bytes = static_cast<uint32_t>(2 * p.NT * p.kc * 128);
   const uint32_t a_sbo = (p.a_swizzle_mode == 2) ? 1024u : 512u;
   const uint64_t adesc0 = smem_desc(stage0 + b_bytes, 16u, a_sbo, static_cast<uint32_t>(p.a_swizzle_mode));
   const uint64_t bdesc0 = smem_desc(stage0, static_cast<uint32_t>(p.kc * 128), 1024u, 2u);
@@ -191,7 +194,7 @@ __device__ __forceinline__ void rs_mma(const SpmmKernelParams& p, RsSmemHeader* 
                       mbar_wait_bounded(baddr(&hdr->acc_empty[acc]), acc_phase ^ 1u, ctl, ST_TIMEOUT_MMA)))
         break;
       tc_fence_after();
-      d0 = tmem_base + static_cast<uint32_t>(acc * kRsN);
+      d0 = tmem_base + static_cast<uint32_t>(acc * p.acc_cols);
     }
     if (!(info & RS_EMPTY)) {
       const uint64_t ad = adesc0 + soff, bd = bdesc0 + soff;
@@ -331,7 +334,7 @@ bsp_status launch_spmm_rowstack(const bsp_spmm_plan* p, const bsp_bsr_desc* A, c
   if (b3d) {
     const uint64_t dims[3] = {64, static_cast<uint64_t>(p->K), static_cast<uint64_t>(p->N / 64)};
     const uint64_t strides[2] = {static_cast<uint64_t>(ldb) * 2, 128};
-    const uint32_t box[3] = {64, static_cast<uint32_t>(p->kc), 4};
+    const uint32_t box[3] = {64, static_cast<uint32_t>(p->kc), static_cast<uint32_t>(2 * p->NT)};
     st = encode_nd(dev, &kp.tm_b, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, B, dims, strides, box,
                    CU_TENSOR_MAP_SWIZZLE_128B);
   } else {
@@ -352,14 +355,14 @@ bsp_status launch_spmm_rowstack(const bsp_spmm_plan* p, const bsp_bsr_desc* A, c
   kp.kc = p->kc;
   kp.nkc = p->C / p->kc;
   kp.G = p->G;
-  kp.NT = 2;
+  kp.NT = p->NT;  // 128-column tiles per unit: 2 (MMA N = 256) or 1 (N = 128)
   kp.step_stride = p->step_stride;
   kp.c_f32 = f32;
   kp.stages = p->stages;
   kp.stage_bytes = p->stage_bytes;
-  kp.b_bytes = 4 * p->kc * 128;
+  kp.b_bytes = 2 * p->NT * p->kc * 128;
   kp.a_swizzle_mode = p->kc == 64 ? 2 : 4;
-  kp.acc_cols = kRsN;
+  kp.acc_cols = 128 * p->NT;
   kp.stacked = 1;
   kp.tmem_cols = p->tmem_cols;
   kp.N = static_cast<int32_t>(p->N);

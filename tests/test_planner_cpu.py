@@ -155,8 +155,26 @@ def _sddmm_rowstack_keys(plan, rp, ci, R, C):
     return seen
 
 
-@pytest.mark.parametrize("strategy", ["naive", "dda"])
-@pytest.mark.parametrize("R,C,K", [(32, 32, 256), (64, 32, 96), (32, 96, 64), (512, 64, 128)])
+def _check_resident_a_runs(plan):
+    """Resident-A schedules: in each CTA's list, pad[0] = run << 1 | first
+    marks runs of equal row0 (run counting from 0 per CTA) and pad[1] the
+    last unit of each run; other schedules leave both words 0."""
+    u, cta = plan["unit_table"], plan["cta_begin"]
+    if not plan["keep_a"]:
+        assert np.all(u[:, 2] == 0) and np.all(u[:, 3] == 0)
+        return
+    for c in range(len(cta) - 1):
+        run = -1
+        for i in range(cta[c], cta[c + 1]):
+            first = i == cta[c] or u[i, 0] != u[i - 1, 0]
+            run += int(first)
+            assert u[i, 2] == (run << 1) | int(first)
+            last = i == cta[c + 1] - 1 or u[i + 1, 0] != u[i, 0]
+            assert u[i, 3] == int(last)
+
+
+@pytest.mark.parametrize("strategy", ["naive", "dda", "snf"])
+@pytest.mark.parametrize("R,C,K", [(32, 32, 256), (64, 32, 96), (32, 96, 64), (512, 64, 128), (32, 32, 512)])
 def test_sddmm_rowstack_schedule_covers_every_tile_once(strategy, R, C, K):
     M, N = 4 * max(R, 128), 8 * C
     rng = np.random.default_rng(R * 7 + C)
@@ -167,6 +185,35 @@ def test_sddmm_rowstack_schedule_covers_every_tile_once(strategy, R, C, K):
     assert len(seen) == int(rp[-1]) * (C // 32) * (R // 32)
     assert all(v == 1 for v in seen.values())
     assert plan["cta_begin"][-1] == plan["units"]
+    # the A tile stays resident for CDA and SnF while two 128 x K tiles fit
+    assert plan["keep_a"] == int(strategy != "naive" and K <= 256)
+    _check_resident_a_runs(plan)
+
+
+@pytest.mark.parametrize("n_tiles", [0, 1])
+def test_sddmm_snf_contiguous_runs_balanced_by_weight(n_tiles):
+    """SnF deals contiguous runs of units whose weights are about equal, so a
+    row group's A tile is loaded once per CTA run; group_rows = -1 turns the
+    resident tile off without changing the schedule."""
+    R = C = 32
+    M, N, K = 4096, 4096, 128
+    rng = np.random.default_rng(5)
+    rp, ci, _ = rand_bsr(rng, M, N, R, C, 0.1)
+    plan = bsp.inspect_sddmm_plan(M, N, R, C, rp, ci, K, bsp.SNF, opts=bsp.make_opts(n_tiles=n_tiles))
+    u, cta = plan["unit_table"], plan["cta_begin"]
+    # the CTA lists concatenate to the planner's unit order (row0 nondecreasing)
+    assert np.all(np.diff(u[:, 0]) >= 0)
+    w = u[:, 1].astype(np.int64) * (K // plan["kc"]) + 2
+    loads = np.array([w[cta[c]:cta[c + 1]].sum() for c in range(len(cta) - 1)])
+    assert loads.max() - loads.min() <= 2 * w.max()
+    a_loads = int((u[:, 2] & 1).sum())
+    assert a_loads <= len(np.unique(u[:, 0])) + plan["ctas"]
+    _check_resident_a_runs(plan)
+    off = bsp.inspect_sddmm_plan(M, N, R, C, rp, ci, K, bsp.SNF,
+                                 opts=bsp.make_opts(n_tiles=n_tiles, group_rows=-1))
+    assert off["keep_a"] == 0 and np.array_equal(off["cta_begin"], cta)
+    assert np.array_equal(off["unit_table"][:, [0, 1]], u[:, [0, 1]])
+    assert np.array_equal(off["unit_table"][:, 4:], u[:, 4:])
 
 
 def test_sddmm_rowstack_repeated_columns_get_their_own_layer():

@@ -14,7 +14,7 @@ from helpers import assert_bf16_close, pcc, rand_bsr, rand_dense
 
 pytestmark = pytest.mark.gpu
 
-STRATS = ["naive", "dda"]
+STRATS = ["naive", "dda", "snf"]
 
 # (M, N, K, R, C, density, with_mask_values)
 CASES = [
@@ -131,3 +131,36 @@ def test_sddmm_identity_mask_known_answer():
     for b in range(4):
         expect = np.diag(np.diag(full[b * R:(b + 1) * R, b * C:(b + 1) * C]))
         np.testing.assert_allclose(out[b], expect, rtol=1e-2, atol=1e-6)
+
+
+@pytest.mark.parametrize("K", [64, 128, 256])
+@pytest.mark.parametrize("strategy", ["dda", "snf"])
+def test_sddmm_resident_a_matches_streamed_a(K, strategy):
+    """The resident-A kernel form (one A tile load per run of a row group's
+    units) gives bit-identical output to the form that streams A with every
+    stage (opts.group_rows = -1): same MMAs in the same order."""
+    import bsp
+
+    M, N, R, C = 2048, 4096, 32, 32
+    rng = np.random.default_rng(K)
+    rp, ci, mv = rand_bsr(rng, M, N, R, C, 0.15)
+    Ah = rand_dense(rng, M, K, "normal", 1 / 16)
+    Bh = rand_dense(rng, K, N, "normal", 1 / 16)
+    A, B = bsp.to_device_bf16(Ah), bsp.to_device_bf16(Bh)
+    mask = bsp.DeviceBSR.from_host(M, N, R, C, rp, ci, mv)
+    outs = []
+    # several producer warps loading A tiles (producers = 3, or N = 128 units
+    # with a deep ring), with few CTAs so that each runs many row groups,
+    # exercise the in-order issue and the final drain of the resident tiles
+    for opts in (bsp.make_opts(group_rows=-1), bsp.make_opts(), bsp.make_opts(producers=3),
+                 bsp.make_opts(n_tiles=1), bsp.make_opts(producers=3, max_ctas=7),
+                 bsp.make_opts(n_tiles=1, max_ctas=5)):
+        plan = bsp.SddmmPlan(bsp.device(), mask, K, bsp.STRATEGIES[strategy], opts)
+        outs.append((plan.info()["keep_a"], bsp.to_host_bits(bsp.sddmm(mask, A, B, strategy=bsp.STRATEGIES[strategy], opts=opts))))
+        plan.close()
+    bsp.device().synchronize()
+    assert [o[0] for o in outs] == [0, 1, 1, 1, 1, 1]
+    for o in outs[1:]:
+        assert np.array_equal(o[1], outs[0][1])
+    gold = oracle.sddmm_bf16(rp, ci, mv, M, N, R, C, Ah, Bh, K)
+    assert_bf16_close(outs[1][1], gold)

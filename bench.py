@@ -972,6 +972,70 @@ def table1_patterns():
     return out
 
 
+def table3_cases():
+    """The reference's Table 3 density sweep (block_sddmm/inc/profiling_suite.hpp
+    SDDMMSweepDensity): SDDMM with M = N = K = 8192, R = C = 256 and a random
+    mask of round(32 * 32 * d) blocks, d in {5, 10, 25, 50, 75} %."""
+    S, R = 8192, 256
+    nb = S // R
+    out = []
+    for d in (5, 10, 25, 50, 75):
+        rng = np.random.default_rng(3000 + d)
+        n = max(1, int(round(nb * nb * d / 100.0)))
+        occ = np.zeros(nb * nb, bool)
+        occ[rng.choice(nb * nb, n, replace=False)] = True
+        rp, ci = _pattern_from_occupancy(occ.reshape(nb, nb))
+        out.append((f"SDDMM_R256_d{d}", R, rp, ci, S))
+    return out
+
+
+def run_ablation_sddmm(args, dev, flush):
+    """Table 3: SDDMM Naive / CDA / SnF (and their no-LB variants) on the
+    reference's density sweep; effective FLOPs 2 nnzb R C K + nnzb R C."""
+    import torch
+
+    import bsp
+
+    strategies = [("Naive", bsp.NAIVE, {}), ("CDA", bsp.DDA, {}), ("SnF", bsp.SNF, {}),
+                  ("Naive_no_lb", bsp.NAIVE, dict(no_load_balance=1))]
+    rng = np.random.default_rng(4321)
+    A = B = None
+    for name, R, rp, ci, S in table3_cases():
+        if args.cases and name not in args.cases.split(","):
+            continue
+        if A is None:
+            A = bsp.to_device_bf16(uniform_bf16(rng, (S, S)))
+            B = bsp.to_device_bf16(uniform_bf16(rng, (S, S)))
+        mask = bsp.DeviceBSR.from_host(S, S, R, R, rp, ci, None)
+        out = torch.empty(ci.size * R * R, dtype=torch.bfloat16, device="cuda")
+        flops = 2.0 * ci.size * R * R * S + ci.size * R * R
+        for sname, strat, o in strategies:
+            plan = bsp.SddmmPlan(dev, mask, S, strat, bsp.make_opts(**o))
+            ts = []
+            try:
+                for it in range(args.warmup + args.steps):
+                    flush.zero_()
+                    e0 = torch.cuda.Event(enable_timing=True)
+                    e1 = torch.cuda.Event(enable_timing=True)
+                    e0.record()
+                    plan.execute(mask, A, B, out)
+                    e1.record()
+                    torch.cuda.synchronize()
+                    if it >= args.warmup:
+                        ts.append(e0.elapsed_time(e1))
+                dev.synchronize()
+            except bsp.BspError as err:
+                print(json.dumps({"case": name, "strategy": sname, "error": str(err)}), flush=True)
+                plan.close()
+                continue
+            ms = float(np.median(ts))
+            info = plan.info()
+            print(json.dumps({"case": name, "strategy": sname, "R": R, "nnzb": int(ci.size), "K": S,
+                              "units": info["units"], "keep_a": info["keep_a"], "ms": ms,
+                              "tflops": flops / (ms * 1e-3) / 1e12}), flush=True)
+            plan.close()
+
+
 def run_ablation(args):
     """Per-strategy operand traffic and throughput on the Table 1 cases: the
     counterpart of the reference's count_dram_reads.py (in0 = A, in1 = B reads
@@ -988,6 +1052,7 @@ def run_ablation(args):
                   ("Naive_no_lb", bsp.NAIVE, dict(no_load_balance=1)), ("SnF_no_lb", bsp.SNF, dict(no_load_balance=1)),
                   ("DDA_no_lb", bsp.DDA, dict(no_load_balance=1))]
     rng = np.random.default_rng(1234)
+    run_ablation_sddmm(args, dev, flush)
     for name, R, rp, ci, S in table1_patterns():
         if args.cases and name not in args.cases.split(","):
             continue
@@ -1045,7 +1110,8 @@ def main():
     ap.add_argument("--nccl-exchange", action="store_true",
                     help="cfg5 with N > 1: exchange C panels by NCCL send/recv instead of the fused kernel")
     ap.add_argument("--ablation", action="store_true",
-                    help="per-strategy operand traffic and TFLOP/s on the reference's Table 1 cases")
+                    help="per-strategy TFLOP/s on the reference's Table 3 SDDMM density sweep and operand "
+                         "traffic and TFLOP/s on its Table 1 SpMM cases")
     ap.add_argument("--cases", default="", help="--ablation: comma-separated case names")
     args = ap.parse_args()
     if args.warmup < 3:

@@ -972,6 +972,42 @@ def table1_patterns():
     return out
 
 
+def fig4_patterns():
+    """The reference's Fig. 4 semi-sparse cases (paper_reproduce/reproduce_fig4.sh;
+    block_spmm/inc/profiling_suite.hpp PatternD{5,10,25,50}[_128]): DDA at
+    M = N = K = 8192 with R = C in {128, 256}, density d in {5, 10, 25, 50} %
+    (round(d * blocks) blocks) and four fills: Row (row-major order), Col
+    (column-major order), Multi-diag (diagonals 0, +1, -1, ...) and Random
+    (seeded, distinct positions)."""
+    S = 8192
+    out = []
+    for R in (128, 256):
+        nb = S // R
+        for d in (5, 10, 25, 50):
+            n = max(1, int(round(nb * nb * d / 100.0)))
+            occ_row = np.zeros((nb, nb), bool)
+            occ_row.flat[:n] = True
+            occ_col = np.zeros((nb, nb), bool)
+            occ_col.T.flat[:n] = True
+            occ_diag = np.zeros((nb, nb), bool)
+            placed, dd = 0, 0
+            while placed < n:
+                for t in range(nb):
+                    i, j = (t, t + dd) if dd >= 0 else (t - dd, t)
+                    if i < nb and j < nb and placed < n:
+                        occ_diag[i, j] = True
+                        placed += 1
+                dd = -dd + 1 if dd <= 0 else -dd
+            rng = np.random.default_rng(5000 + R + d)
+            occ_rand = np.zeros(nb * nb, bool)
+            occ_rand[rng.choice(nb * nb, n, replace=False)] = True
+            for pname, occ in (("Row", occ_row), ("Col", occ_col), ("MultiDiag", occ_diag),
+                               ("Random", occ_rand.reshape(nb, nb))):
+                rp, ci = _pattern_from_occupancy(occ)
+                out.append((f"Fig4_{pname}_R{R}_d{d}", R, rp, ci, S))
+    return out
+
+
 def table3_cases():
     """The reference's Table 3 density sweep (block_sddmm/inc/profiling_suite.hpp
     SDDMMSweepDensity): SDDMM with M = N = K = 8192, R = C = 256 and a random
@@ -1001,7 +1037,7 @@ def run_ablation_sddmm(args, dev, flush):
     rng = np.random.default_rng(4321)
     A = B = None
     for name, R, rp, ci, S in table3_cases():
-        if args.cases and name not in args.cases.split(","):
+        if args.cases and not any(name.startswith(c) for c in args.cases.split(",")):
             continue
         if A is None:
             A = bsp.to_device_bf16(uniform_bf16(rng, (S, S)))
@@ -1053,8 +1089,10 @@ def run_ablation(args):
                   ("DDA_no_lb", bsp.DDA, dict(no_load_balance=1))]
     rng = np.random.default_rng(1234)
     run_ablation_sddmm(args, dev, flush)
-    for name, R, rp, ci, S in table1_patterns():
-        if args.cases and name not in args.cases.split(","):
+    cases = [(c, strategies) for c in table1_patterns()]
+    cases += [(c, [("DDA", bsp.DDA, {})]) for c in fig4_patterns()]  # Fig. 4 reports DDA only
+    for (name, R, rp, ci, S), case_strategies in cases:
+        if args.cases and not any(name.startswith(c) for c in args.cases.split(",")):
             continue
         vals = uniform_bf16(rng, (ci.size * R, R))
         B = uniform_bf16(rng, (S, S))
@@ -1064,7 +1102,7 @@ def run_ablation(args):
         flops = 2.0 * ci.size * R * R * S
         a_once = 2 * ci.size * R * R
         b_once = 2 * np.unique(ci).size * R * S
-        for sname, strat, o in strategies:
+        for sname, strat, o in case_strategies:
             opts = bsp.make_opts(**o)
             tr = bsp.spmm_plan_traffic(S, S, R, R, rp, ci, S, strat, opts=opts, sm_count=dev.sm_count)
             plan = bsp.SpmmPlan(dev, A, S, strat, bsp.BF16, opts)
@@ -1112,7 +1150,7 @@ def main():
     ap.add_argument("--ablation", action="store_true",
                     help="per-strategy TFLOP/s on the reference's Table 3 SDDMM density sweep and operand "
                          "traffic and TFLOP/s on its Table 1 SpMM cases")
-    ap.add_argument("--cases", default="", help="--ablation: comma-separated case names")
+    ap.add_argument("--cases", default="", help="--ablation: comma-separated case names or name prefixes")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -301,6 +301,22 @@ void bsr_sddmm_multicore_CDA(bsr_matrix<bfloat16>& sampling_mask, dense_matrix<b
                                             BSP_DDA, "bsr_sddmm_multicore_CDA");
 }
 
+// block_sddmm/inc/host_code/bsr_sddmm_multicore_SnF_C.cpp: the reference's
+// unfinished store-and-forward SDDMM (excluded from its build by
+// block_sddmm/inc/host_code/CMakeLists.txt:7, not in its registries).  Here it
+// runs: each CTA keeps a row group's 128 x K panel of c resident while the
+// group's d segments stream past, over contiguous runs of units balanced by
+// weight.  Not added to the registries below, so their indices stay the
+// reference's.
+template <bool verbose = false, bool is_profiling = false>
+void bsr_sddmm_multicore_SnF(bsr_matrix<bfloat16>& sampling_mask, dense_matrix<bfloat16>& c,
+                             dense_matrix<bfloat16>& d, bsr_matrix<bfloat16>& output, uint32_t M,
+                             uint32_t N, uint32_t K, uint32_t R, uint32_t C_block, uint32_t B,
+                             IDevice* device) {
+  bsp::detail::sddmm<verbose, is_profiling>(sampling_mask, c, d, output, M, N, K, R, C_block, B, device,
+                                            BSP_SNF, "bsr_sddmm_multicore_SnF");
+}
+
 // block_sddmm/inc/host_code.hpp:104-115
 using SDDMMHostCodeFunctionPtr = void (*)(bsr_matrix<bfloat16>& sampling_mask, dense_matrix<bfloat16>& c,
                                           dense_matrix<bfloat16>& d, bsr_matrix<bfloat16>& output,

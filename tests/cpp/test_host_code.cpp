@@ -122,7 +122,10 @@ int main(int argc, char** argv) {
       const auto mv = bits(mask.data), cv = bits(c.data), dv = bits(d.data);
       bsp_oracle_sddmm_bf16(M, N, R, C, mask.indptr.data(), mask.indices.data(), mv.data(), K,
                             cv.data(), dv.data(), gold.data(), 0, M / R);
-      for (auto& entry : bsr_sddmm_host_code::HostCodeRegistryVerbose) {
+      std::vector<std::pair<bsr_sddmm_host_code::SDDMMHostCodeFunctionPtr, std::string>> entries(
+          std::begin(bsr_sddmm_host_code::HostCodeRegistryVerbose), std::end(bsr_sddmm_host_code::HostCodeRegistryVerbose));
+      entries.push_back({bsr_sddmm_host_code::bsr_sddmm_multicore_SnF<true, false>, "bsr_sddmm_multicore_SnF"});
+      for (auto& entry : entries) {
         bsr_matrix<bfloat16> out;
         entry.first(mask, c, d, out, M, N, K, R, C, 1, device);
         const Scores s = compare(out.data, gold);

@@ -397,10 +397,13 @@ __device__ __forceinline__ void at_softmax(const AttnKernelParams& p, AtSmemHead
       const int slot0 = __ldg(&p.units[u].slot0);
       const int part = __ldg(&p.units[u].part);
       const int cnt = __ldg(&p.units[u].counter);
+      // Slot layout: O as d/4 float4 columns of 128 rows (float4 j of row r at
+      // j * 128 + r, so a warp's access to one column is 512 contiguous
+      // bytes), then the 128 running maxima and the 128 row sums.
       const int64_t slot_floats = 128 * static_cast<int64_t>(p.d + 2);
       const float* base0 = p.work + slot0 * slot_floats;
       float* ws = p.work + (slot0 + part) * slot_floats;
-      float4* wrow = reinterpret_cast<float4*>(ws + static_cast<int64_t>(r) * p.d);
+      float4* wcol = reinterpret_cast<float4*>(ws) + r;
 #pragma unroll 1
       for (int c = 0; c < gd; ++c) {
         uint32_t o[32];
@@ -408,8 +411,8 @@ __device__ __forceinline__ void at_softmax(const AttnKernelParams& p, AtSmemHead
         tmem_ld_wait();
 #pragma unroll
         for (int i = 0; i < 8; ++i)
-          __stcg(wrow + 8 * c + i, make_float4(__uint_as_float(o[4 * i]), __uint_as_float(o[4 * i + 1]),
-                                               __uint_as_float(o[4 * i + 2]), __uint_as_float(o[4 * i + 3])));
+          __stcg(wcol + (8 * c + i) * 128, make_float4(__uint_as_float(o[4 * i]), __uint_as_float(o[4 * i + 1]),
+                                                       __uint_as_float(o[4 * i + 2]), __uint_as_float(o[4 * i + 3])));
       }
       __stcg(ws + 128 * p.d + r, m_used);
       __stcg(ws + 128 * p.d + 128 + r, l);
@@ -452,20 +455,24 @@ __device__ __forceinline__ void at_softmax(const AttnKernelParams& p, AtSmemHead
           float acc[32];
 #pragma unroll
           for (int i = 0; i < 32; ++i) acc[i] = w_self * __uint_as_float(o[i]);
+          // two other parts per round trip to L2 (16 loads in flight)
 #pragma unroll 1
-          for (int k = 0; k < n_parts; ++k) {
-            if (wk[k] == 0.f) continue;
-            const float4* src =
-                reinterpret_cast<const float4*>(base0 + k * slot_floats + static_cast<int64_t>(r) * p.d) + 8 * c;
-            float4 t[8];
-#pragma unroll
-            for (int i = 0; i < 8; ++i) t[i] = __ldcg(src + i);
+          for (int k0 = 0; k0 < n_parts; k0 += 2) {
+            const float w0 = wk[k0], w1 = k0 + 1 < n_parts ? wk[k0 + 1] : 0.f;
+            const float4* src0 = reinterpret_cast<const float4*>(base0 + k0 * slot_floats) + (8 * c) * 128 + r;
+            const float4* src1 = src0 + slot_floats / 4;
+            float4 t0[8], t1[8];
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
-              acc[4 * i] += wk[k] * t[i].x;
-              acc[4 * i + 1] += wk[k] * t[i].y;
-              acc[4 * i + 2] += wk[k] * t[i].z;
-              acc[4 * i + 3] += wk[k] * t[i].w;
+              t0[i] = w0 != 0.f ? __ldcg(src0 + i * 128) : make_float4(0.f, 0.f, 0.f, 0.f);
+              t1[i] = w1 != 0.f ? __ldcg(src1 + i * 128) : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              acc[4 * i] += w0 * t0[i].x + w1 * t1[i].x;
+              acc[4 * i + 1] += w0 * t0[i].y + w1 * t1[i].y;
+              acc[4 * i + 2] += w0 * t0[i].z + w1 * t1[i].z;
+              acc[4 * i + 3] += w0 * t0[i].w + w1 * t1[i].w;
             }
           }
           if (row < p.S) store_row_bf16(orow + 4 * c, acc, inv);

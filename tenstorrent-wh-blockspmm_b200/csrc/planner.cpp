@@ -15,6 +15,7 @@
 #include <cstring>
 #include <cstdlib>
 #include <numeric>
+#include <queue>
 #include <string>
 #include <system_error>
 #include <thread>
@@ -1701,11 +1702,15 @@ bsp_status plan_attn_host(bsp_attn_plan* p, const int32_t* row_ptr, const int32_
   }
   p->n_chunks = static_cast<int64_t>(p->h_chunks.size());
   int grid = o.max_ctas > 0 ? std::min(o.max_ctas, sm_count) : sm_count;
-  // Split units: by default only into CTAs that would otherwise stay idle --
-  // while there are fewer work items than CTAs, the item with the most
-  // chunks is cut into one more part (at most 16), so every CTA runs one
-  // item.  n_tiles > 0 instead cuts every unit into parts of about that many
-  // chunks; group_rows = -1 never splits.
+  // Split units.  Cost model (fitted to B200 timings, d = 128): a chunk keeps
+  // the tensor pipe busy ~1.55 us; a unit's epilogue costs ~1.3 us, a split
+  // part's (partial write, counter, and on the last part the merge) about
+  // 5 + 2 * (parts - 1) us, on the critical path of its CTA.  By default several target lengths are tried:
+  // every unit longer than the target is cut into parts of about that length,
+  // all items are dealt longest first, and the split with the smallest
+  // estimated makespan is kept.  n_tiles > 0 instead cuts every unit into
+  // parts of about that many chunks; group_rows = -1 never splits.
+  constexpr int64_t kChunkNs = 1550, kEpiNs = 1300, kSplitEpiNs = 5000, kSplitPartNs = 2000;
   std::vector<int64_t> np_of(p->h_units.size(), 1);
   if (o.group_rows >= 0 && o.n_tiles > 0) {
     for (size_t i = 0; i < p->h_units.size(); ++i) {
@@ -1713,22 +1718,51 @@ bsp_status plan_attn_host(bsp_attn_plan* p, const int32_t* row_ptr, const int32_
       if (n > o.n_tiles + o.n_tiles / 4)
         np_of[i] = std::min<int64_t>(kAttnMaxParts, (n + o.n_tiles - 1) / o.n_tiles);
     }
-  } else if (o.group_rows >= 0) {
-    int64_t items = static_cast<int64_t>(p->h_units.size());
-    std::vector<std::pair<double, size_t>> heap;  // (chunks per part, unit)
-    for (size_t i = 0; i < p->h_units.size(); ++i) heap.push_back({double(p->h_units[i].n_chunks), i});
-    std::make_heap(heap.begin(), heap.end());
-    while (items < grid && !heap.empty()) {
-      std::pop_heap(heap.begin(), heap.end());
-      auto top = heap.back();
-      heap.pop_back();
-      const size_t i = top.second;
-      const int64_t n = p->h_units[i].n_chunks;
-      if (np_of[i] >= kAttnMaxParts || n < 2 * (np_of[i] + 1) || top.first < 4.0) break;
-      ++np_of[i];
-      ++items;
-      heap.push_back({double(n) / double(np_of[i]), i});
-      std::push_heap(heap.begin(), heap.end());
+  } else if (o.group_rows >= 0 && !p->h_units.empty()) {
+    int64_t total = 0, longest = 0;
+    for (const AttnUnit& u : p->h_units) {
+      total += u.n_chunks * kChunkNs + kEpiNs;
+      longest = std::max<int64_t>(longest, u.n_chunks);
+    }
+    // makespan of dealing the items longest first to the least-loaded CTA
+    auto makespan = [&](const std::vector<int64_t>& np) {
+      std::vector<int64_t> items;
+      for (size_t i = 0; i < p->h_units.size(); ++i) {
+        const int64_t n = p->h_units[i].n_chunks;
+        for (int64_t k = 0; k < np[i]; ++k) {
+          const int64_t len = n * (k + 1) / np[i] - n * k / np[i];
+          items.push_back(len * kChunkNs + (np[i] > 1 ? kSplitEpiNs + kSplitPartNs * (np[i] - 1) : kEpiNs));
+        }
+      }
+      std::sort(items.begin(), items.end(), std::greater<int64_t>());
+      std::priority_queue<int64_t, std::vector<int64_t>, std::greater<int64_t>> load;
+      for (int c = 0; c < grid; ++c) load.push(0);
+      int64_t worst = 0;
+      for (int64_t w : items) {
+        int64_t l = load.top();
+        load.pop();
+        l += w;
+        worst = std::max(worst, l);
+        load.push(l);
+      }
+      return worst;
+    };
+    int64_t best = makespan(np_of);
+    std::vector<int64_t> cand(p->h_units.size());
+    const double avg_chunks = static_cast<double>(total) / grid / kChunkNs;
+    for (double f : {0.6, 0.75, 0.9, 1.0, 1.1, 1.2, 1.3, 1.4, 1.5, 1.75, 2.0, 2.5}) {
+      const int64_t target = std::max<int64_t>(2, static_cast<int64_t>(avg_chunks * f));
+      if (target >= longest) continue;
+      for (size_t i = 0; i < p->h_units.size(); ++i) {
+        const int64_t n = p->h_units[i].n_chunks;
+        cand[i] = n > target ? std::min<int64_t>({kAttnMaxParts, n / 2, (n + target - 1) / target}) : 1;
+        cand[i] = std::max<int64_t>(1, cand[i]);
+      }
+      const int64_t m = makespan(cand);
+      if (m < best) {
+        best = m;
+        np_of = cand;
+      }
     }
   }
   std::vector<AttnUnit> parts;

@@ -24,7 +24,9 @@
  * Streams are passed as `void*` (a cudaStream_t; NULL = legacy default stream).
  * Execute calls are stream-ordered and asynchronous; device-side errors (a
  * kernel wait that timed out) are latched in the device and reported by
- * bsp_device_synchronize / bsp_device_get_error.
+ * bsp_device_synchronize / bsp_device_get_error.  A plan whose units were
+ * split (split-K SpMM, split attention units) keeps a workspace and counters
+ * that one launch uses at a time: run a plan's launches on one stream.
  */
 #ifndef BSP_H_
 #define BSP_H_
@@ -87,7 +89,10 @@ typedef struct bsp_bsr_desc {
 typedef struct bsp_spmm_opts {
   int32_t no_load_balance; /* 1: contiguous unit split, the reference's *_no_lb
                               variants (block_spmm/inc/host_code.hpp:113-161) */
-  int32_t group_rows;      /* DDA: block-rows per row group (B-slice sharing) */
+  int32_t group_rows;      /* DDA swap-AB kernel: block-rows per row group (B-slice
+                              sharing).  -1 turns off: split-K of long units (SpMM
+                              row-stacked and pair kernels), the resident A tile
+                              (SDDMM CDA / SnF), unit splitting (attention) */
   int32_t n_tiles;         /* SNF/DDA: 128-column tiles per work unit (A reuse) */
   int32_t max_ctas;        /* cap on persistent CTAs (default: all SMs) */
   int32_t timeout_ms;      /* bound on every in-kernel wait (default 2000) */

@@ -71,6 +71,12 @@ struct SpmmKernelParams {
   // where each epilogue warp stages 32 rows x 128 bytes of C, so that peer
   // stores leave as whole 128-byte lines; 0 = no area (16-byte peer stores)
   int32_t xfer_off;
+  // split-K (row-stacked kernels): a unit with nt & 0xFF = n parts > 1 is part
+  // (nt >> 8) & 0xFF of n; its partial tile goes to workspace slot r_off + part
+  // (acc_cols / 4 float4 columns of 128 rows), and the part that takes the
+  // last count of split_counters[r_off] sums the n partials and stores C
+  float* split_ws;
+  int32_t* split_counters;
 };
 
 // Row-stacked kernel stage descriptor (16 words), precomputed by the planner
@@ -331,6 +337,12 @@ struct bsp_spmm_plan {
   int32_t xfer_off = 0;     // row-stacked: shared-memory staging area for peer stores (0: none)
   int32_t step_stride = 2;  // int32 words per step-table entry (1 + G)
   int64_t n_units = 0, n_steps = 0;
+  // split-K (row-stacked kernels): units cut into parts whose partial tiles
+  // meet in a workspace of n_split_slots tiles (128 rows x acc columns fp32)
+  int64_t n_split_slots = 0;
+  int32_t split_units = 0;
+  float* d_split_ws = nullptr;       // owned unless blob_borrowed
+  int32_t* d_split_counters = nullptr;  // in the blob (zeroed), one per slot
   uint64_t timeout_ns = 0;
   void* d_blob = nullptr;  // units | cta_begin | steps
   size_t blob_bytes = 0;

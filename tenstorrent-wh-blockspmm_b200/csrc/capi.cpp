@@ -365,12 +365,14 @@ static bsp_status spmm_plan_create_impl(bsp_device* dev, const bsp_bsr_desc* A, 
     return s;
   }
   std::vector<void*> ptrs;
+  const std::vector<int32_t> zeros(static_cast<size_t>(p->n_split_slots), 0);  // split-K counters
   const std::vector<std::pair<const void*, size_t>> parts = {
       {p->h_units.data(), p->h_units.size() * sizeof(SpmmUnit)},
       {p->h_cta_begin.data(), p->h_cta_begin.size() * sizeof(int32_t)},
       {p->h_steps.data(), p->h_steps.size() * sizeof(int32_t)},
       {p->h_stage_list.data(), p->h_stage_list.size() * sizeof(int32_t)},
-      {p->h_cta_stage_begin.data(), p->h_cta_stage_begin.size() * sizeof(int32_t)}};
+      {p->h_cta_stage_begin.data(), p->h_cta_stage_begin.size() * sizeof(int32_t)},
+      {zeros.data(), zeros.size() * sizeof(int32_t)}};
   s = borrow ? upload_blob_borrowed(dev, parts, stream, &p->d_blob, &p->blob_bytes, &ptrs)
              : upload_blob(parts, &p->d_blob, &p->blob_bytes, &ptrs);
   p->blob_borrowed = borrow;
@@ -383,6 +385,28 @@ static bsp_status spmm_plan_create_impl(bsp_device* dev, const bsp_bsr_desc* A, 
   p->d_steps = static_cast<int32_t*>(ptrs[2]);
   p->d_stage_list = static_cast<int4*>(ptrs[3]);
   p->d_cta_stage_begin = static_cast<int32_t*>(ptrs[4]);
+  p->d_split_counters = static_cast<int32_t*>(ptrs[5]);
+  if (p->n_split_slots > 0) {
+    // partial tiles of split units: 128 rows x the tile's accumulator columns
+    const int64_t acc_cols = p->variant == 2 ? 256 : 128 * p->NT;
+    const size_t wb = sizeof(float) * 128 * static_cast<size_t>(acc_cols) * static_cast<size_t>(p->n_split_slots);
+    if (borrow) {
+      if (dev->aux_ws_bytes < wb) {
+        if (dev->aux_ws) cudaFree(dev->aux_ws);
+        dev->aux_ws = nullptr;
+        dev->aux_ws_bytes = 0;
+        if (cudaMalloc(&dev->aux_ws, wb) != cudaSuccess) {
+          bsp_spmm_plan_destroy(p);
+          return set_error(BSP_ERR_ALLOC, "cudaMalloc of the split-K workspace failed");
+        }
+        dev->aux_ws_bytes = wb;
+      }
+      p->d_split_ws = static_cast<float*>(dev->aux_ws);
+    } else if (cudaMalloc(reinterpret_cast<void**>(&p->d_split_ws), wb) != cudaSuccess) {
+      bsp_spmm_plan_destroy(p);
+      return set_error(BSP_ERR_ALLOC, "cudaMalloc of the split-K workspace failed");
+    }
+  }
   *out = p;
   return BSP_OK;
 }
@@ -479,6 +503,7 @@ bsp_status bsp_ipc_close(bsp_device* dev, void* base) {
 bsp_status bsp_spmm_plan_destroy(bsp_spmm_plan* plan) {
   if (!plan) return BSP_OK;
   if (plan->d_blob && !plan->blob_borrowed) cudaFree(plan->d_blob);
+  if (plan->d_split_ws && !plan->blob_borrowed) cudaFree(plan->d_split_ws);
   delete plan;
   return BSP_OK;
 }

@@ -427,6 +427,74 @@ bsp_status plan_spmm_host(bsp_spmm_plan* p, const int32_t* row_ptr, const int32_
 // consecutive entries form the 128 rows of one MMA.  A unit is one entry group
 // x 256 output columns; its steps are the distinct block-columns of the
 // group's rows, each listing per entry the block to multiply (or -1).
+// Split-K for the row-stacked kernels: a long unit is cut into parts over
+// consecutive ranges of its steps; each part accumulates a partial tile, and
+// the part that finishes last adds the others' partials (left in a workspace
+// by them) and stores the tile.  parts[i] (1 = whole) for units of balancer
+// weight weight[i] and nsteps[i] steps: several target part weights are
+// tried (cut every unit above the target into parts of about that weight),
+// and the cut whose serpentine deal has the shortest makespan is kept if it
+// beats the uncut deal by 3%.  Each part is charged its partial's write plus
+// the final sum's read of all n partials: the merge is bound by L2 round
+// trips on the merging CTA's critical path, so parts are also capped at 4
+// (a 16-part merge of config 5's longest rows cost more than it balanced).
+static std::vector<int32_t> choose_splits(const std::vector<int64_t>& weight, const std::vector<int32_t>& nsteps,
+                                          int ctas, int64_t partial_bytes) {
+  constexpr int kMaxSplit = 4, kMinPartSteps = 4;
+  const size_t n = weight.size();
+  std::vector<int32_t> best(n, 1);
+  if (n == 0 || ctas < 2) return best;
+  auto makespan = [&](const std::vector<int32_t>& np) {
+    std::vector<int64_t> items;
+    for (size_t i = 0; i < n; ++i)
+      for (int k = 0; k < np[i]; ++k) {
+        const int64_t lo = int64_t(nsteps[i]) * k / np[i], hi = int64_t(nsteps[i]) * (k + 1) / np[i];
+        items.push_back(np[i] == 1 ? weight[i]
+                                   : weight[i] * (hi - lo) / std::max(1, nsteps[i]) + (1 + np[i]) * partial_bytes);
+      }
+    const int grid = static_cast<int>(std::min<int64_t>(ctas, static_cast<int64_t>(items.size())));
+    std::vector<std::vector<int32_t>> per;
+    serpentine_order(items, grid, &per);
+    int64_t worst = 0;
+    for (const auto& v : per) {
+      int64_t t = 0;
+      for (int32_t idx : v) t += items[static_cast<size_t>(idx)];
+      worst = std::max(worst, t);
+    }
+    return worst;
+  };
+  const int64_t base = makespan(best);
+  int64_t best_m = base, total = 0;
+  for (int64_t w : weight) total += w;
+  std::vector<int32_t> cand(n);
+  for (double f : {0.1, 0.15, 0.2, 0.3, 0.4, 0.5, 0.6, 0.75, 0.9, 1.0, 1.1, 1.25, 1.5, 2.0}) {
+    const int64_t target = std::max<int64_t>(1, static_cast<int64_t>(static_cast<double>(total) / ctas * f));
+    bool any = false;
+    for (size_t i = 0; i < n; ++i) {
+      cand[i] = 1;
+      if (weight[i] > target && nsteps[i] >= 2 * kMinPartSteps) {
+        const int64_t want = (weight[i] + target - 1) / target;
+        cand[i] = static_cast<int32_t>(std::min<int64_t>({kMaxSplit, nsteps[i] / kMinPartSteps, want}));
+        any |= cand[i] > 1;
+      }
+    }
+    if (!any) continue;
+    // no deal beats the mean load with the parts' added traffic: skip the
+    // deal when even that bound cannot improve on the best so far
+    int64_t added = 0;
+    for (size_t i = 0; i < n; ++i)
+      if (cand[i] > 1) added += int64_t(cand[i]) * (1 + cand[i]) * partial_bytes;
+    if ((total + added) / ctas >= best_m) continue;
+    const int64_t m = makespan(cand);
+    if (m < best_m) {
+      best_m = m;
+      best = cand;
+    }
+  }
+  if (best_m * 100 > base * 97) std::fill(best.begin(), best.end(), 1);
+  return best;
+}
+
 bsp_status plan_spmm_rowstack(bsp_spmm_plan* p, const int32_t* row_ptr, const int32_t* col_idx,
                               int sm_count, int max_smem, const bsp_spmm_opts* opts, bool stage_lists) {
   bsp_spmm_opts o;
@@ -516,6 +584,37 @@ bsp_status plan_spmm_rowstack(bsp_spmm_plan* p, const int32_t* row_ptr, const in
     for (int q = 0; q < G; ++q) steps.push_back(-1);
   }
   int grid = o.max_ctas > 0 ? std::min(o.max_ctas, sm_count) : sm_count;
+  // split-K (not with the contiguous split; opts.group_rows = -1 turns it off)
+  p->n_split_slots = 0;
+  p->split_units = 0;
+  if (!o.no_load_balance && o.group_rows != -1) {
+    std::vector<int32_t> nst(units.size());
+    for (size_t i = 0; i < units.size(); ++i) nst[i] = units[i].step_end - units[i].step_begin;
+    const std::vector<int32_t> np = choose_splits(weight, nst, grid, int64_t(128) * tile_n * 4);
+    std::vector<SpmmUnit> su;
+    std::vector<int64_t> sw;
+    for (size_t i = 0; i < units.size(); ++i) {
+      if (np[i] == 1) {
+        su.push_back(units[i]);
+        sw.push_back(weight[i]);
+        continue;
+      }
+      for (int k = 0; k < np[i]; ++k) {
+        SpmmUnit v = units[i];
+        v.step_begin = units[i].step_begin + static_cast<int32_t>(int64_t(nst[i]) * k / np[i]);
+        v.step_end = units[i].step_begin + static_cast<int32_t>(int64_t(nst[i]) * (k + 1) / np[i]);
+        v.nt = np[i] | (k << 8);
+        v.r_off = static_cast<int32_t>(p->n_split_slots);
+        su.push_back(v);
+        sw.push_back(weight[i] * (v.step_end - v.step_begin) / std::max(1, nst[i]) +
+                     (1 + np[i]) * int64_t(128) * tile_n * 4);
+      }
+      p->n_split_slots += np[i];
+      ++p->split_units;
+    }
+    units.swap(su);
+    weight.swap(sw);
+  }
   grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(grid, units.size())));
   std::vector<std::vector<int32_t>> per;
   if (o.no_load_balance)
@@ -617,6 +716,7 @@ bsp_status plan_spmm_pair(bsp_spmm_plan* p, const int32_t* row_ptr, const int32_
     int nent;
     int32_t s_begin, s_end, n0;
     int32_t mask;  // present entries (bit g of the 2G)
+    int32_t np = 1, part = 0, slot0 = 0;  // split-K: part of np; rank r's slots start at slot0 + r * np
   };
   std::vector<PairUnit> units;
   std::vector<int64_t> weight;
@@ -654,7 +754,7 @@ bsp_status plan_spmm_pair(bsp_spmm_plan* p, const int32_t* row_ptr, const int32_
     }
     const int32_t s_end = static_cast<int32_t>(steps.size() / stride);
     for (int t = 0; t < ntiles; ++t) {
-      units.push_back({e0, nent, s_begin, s_end, t * 256, mask});
+      units.push_back({e0, nent, s_begin, s_end, t * 256, mask, 1, 0, 0});
       // bytes staged per CTA: B half + all entry slots per step, plus its C rows
       weight.push_back(int64_t(s_end - s_begin) * nkc * (int64_t(kc) * 128 * 2 + int64_t(G) * Rs * kc * 2) +
                        int64_t(G) * Rs * 256 * esz + 4096);
@@ -662,6 +762,37 @@ bsp_status plan_spmm_pair(bsp_spmm_plan* p, const int32_t* row_ptr, const int32_
   }
   p->n_steps = static_cast<int64_t>(steps.size() / stride);
   int npairs = (o.max_ctas > 0 ? std::min(o.max_ctas, sm_count) : sm_count) / 2;
+  // split-K over pair units (each rank keeps its own partial tile)
+  p->n_split_slots = 0;
+  p->split_units = 0;
+  if (!o.no_load_balance && o.group_rows != -1) {
+    std::vector<int32_t> nst(units.size());
+    for (size_t i = 0; i < units.size(); ++i) nst[i] = units[i].s_end - units[i].s_begin;
+    const std::vector<int32_t> np = choose_splits(weight, nst, npairs, int64_t(128) * 256 * 4);
+    std::vector<PairUnit> su;
+    std::vector<int64_t> sw;
+    for (size_t i = 0; i < units.size(); ++i) {
+      if (np[i] == 1) {
+        su.push_back(units[i]);
+        sw.push_back(weight[i]);
+        continue;
+      }
+      for (int k = 0; k < np[i]; ++k) {
+        PairUnit v = units[i];
+        v.s_begin = units[i].s_begin + static_cast<int32_t>(int64_t(nst[i]) * k / np[i]);
+        v.s_end = units[i].s_begin + static_cast<int32_t>(int64_t(nst[i]) * (k + 1) / np[i]);
+        v.np = np[i];
+        v.part = k;
+        v.slot0 = static_cast<int32_t>(p->n_split_slots);
+        su.push_back(v);
+        sw.push_back(weight[i] * (v.s_end - v.s_begin) / std::max(1, nst[i]) + (1 + np[i]) * int64_t(128) * 256 * 4);
+      }
+      p->n_split_slots += 2 * np[i];
+      ++p->split_units;
+    }
+    units.swap(su);
+    weight.swap(sw);
+  }
   npairs = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(npairs, units.size())));
   std::vector<std::vector<int32_t>> per;
   if (o.no_load_balance)
@@ -714,9 +845,9 @@ bsp_status plan_spmm_pair(bsp_spmm_plan* p, const int32_t* row_ptr, const int32_
         SpmmUnit u;
         u.row0 = static_cast<int32_t>(pu.e0 + r * G);
         u.nrows = std::max(0, std::min(G, pu.nent - r * G));
-        u.r_off = 0;
+        u.r_off = pu.np > 1 ? pu.slot0 + r * pu.np : 0;
         u.n0 = pu.n0;
-        u.nt = 1;
+        u.nt = pu.np | (pu.part << 8);
         u.step_begin = pu.s_begin;
         u.step_end = pu.s_end;
         u.row_mask = (pu.mask >> (r * G)) & ((1 << G) - 1);

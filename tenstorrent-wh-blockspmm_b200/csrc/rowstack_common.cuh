@@ -26,9 +26,11 @@ struct RsSmemHeader {
   uint64_t acc_full[2];
   uint64_t acc_empty[2];
   uint64_t drain;
+  uint64_t merge_bar;   // the epilogue warps, split-K merge
   uint32_t info[kRsMaxStages];
   uint32_t tmem_base;
   int abort_flag;
+  int merge_flag;       // this part takes the last count: it stores the tile
 };
 static_assert(sizeof(RsSmemHeader) <= 1024, "header must fit its 1 KiB slot");
 
@@ -69,6 +71,10 @@ __device__ __forceinline__ void rs_epilogue(const SpmmKernelParams& p, RsSmemHea
   constexpr int kChunksPerFlush = 128 / (32 * kEsz);  // 32-column chunks per 128-byte segment
   const bool staged = p.n_peers > 0 && p.xfer_off > 0;
   uint4* xf = reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(hdr) + p.xfer_off) + q * (32 * 8);
+  const int lrow = 32 * q + lane;  // row of the unit's 128-row tile
+  const int64_t slot_floats = 128 * static_cast<int64_t>(p.acc_cols);
+  const int nchunk = p.acc_cols / 32;  // 32-column chunks of the unit's tile
+  int mp = 0;                          // merge-barrier rounds
   SpmmUnit nxt;
   if (u_begin < u_end) nxt = p.units[u_begin];
 #pragma unroll 1
@@ -77,20 +83,89 @@ __device__ __forceinline__ void rs_epilogue(const SpmmKernelParams& p, RsSmemHea
     if (u + 1 < u_end) nxt = p.units[u + 1];
     if (!mbar_wait_bounded(baddr(&hdr->acc_full[acc]), acc_phase, ctl, ST_TIMEOUT_EPILOGUE)) break;
     tc_fence_after();
-    if (g < un.nrows) {
+    const bool present = g < un.nrows && ((un.row_mask >> g) & 1);
+    const uint32_t t_acc = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * p.acc_cols);
+    // Split-K: every part leaves its partial tile in its workspace slot
+    // (float4 j of row r at j * 128 + r: 512-byte warp accesses); the part
+    // that takes the last count sums the parts' partials and stores C.
+    const int n_parts = un.nt & 0xFF;
+    const float* parts_ws = nullptr;
+    bool store = true;
+    if (n_parts > 1) {
+      const int part = (un.nt >> 8) & 0xFF;
+      float4* own = reinterpret_cast<float4*>(p.split_ws + (un.r_off + part) * slot_floats) + lrow;
+#pragma unroll 1
+      for (int c = 0; c < nchunk; ++c) {
+        uint32_t v[32];
+        if (present) {
+          tmem_ld_32x32b_x32(t_acc + static_cast<uint32_t>(c * 32), v);
+          tmem_ld_wait();
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = 0u;
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          __stcg(own + (8 * c + i) * 128, make_float4(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1]),
+                                                      __uint_as_float(v[4 * i + 2]), __uint_as_float(v[4 * i + 3])));
+      }
+      // two rounds of the epilogue warps' merge barrier (bounded waits): all
+      // partial rows written and fenced, then the counter result published
+      __threadfence();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(baddr(&hdr->merge_bar));
+      bool ok = mbar_wait_bounded(baddr(&hdr->merge_bar), static_cast<uint32_t>(mp & 1), ctl, ST_TIMEOUT_EPILOGUE);
+      ++mp;
+      if (!__all_sync(0xffffffffu, ok)) break;
+      if (q == 0 && lane == 0) hdr->merge_flag = atomicAdd(p.split_counters + un.r_off, 1) == n_parts - 1 ? 1 : 0;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(baddr(&hdr->merge_bar));
+      ok = mbar_wait_bounded(baddr(&hdr->merge_bar), static_cast<uint32_t>(mp & 1), ctl, ST_TIMEOUT_EPILOGUE);
+      ++mp;
+      if (!__all_sync(0xffffffffu, ok)) break;
+      store = *reinterpret_cast<volatile int*>(&hdr->merge_flag) != 0;
+      if (store) {
+        __threadfence();
+        parts_ws = p.split_ws + un.r_off * slot_floats;
+        if (q == 0 && lane == 0) p.split_counters[un.r_off] = 0;  // ready for the next launch
+      }
+    }
+    if (store && g < un.nrows) {
       const int e = un.row0 + g;
       const int64_t row = static_cast<int64_t>(e / slabs) * p.R + (e % slabs) * p.Rs + rrow;
-      const bool present = (un.row_mask >> g) & 1;
-      const int nchunk = p.acc_cols / 32;  // 32-column chunks of the unit's tile
 #pragma unroll 1
       for (int c = 0; c < nchunk; ++c) {
         const int n = un.n0 + c * 32;
         if (n >= p.N) break;
         uint32_t v[32];
-        if (present) {
-          tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
-                                 static_cast<uint32_t>(acc * p.acc_cols + c * 32),
-                             v);
+        if (parts_ws) {
+          // the sum of the parts' partials (at most 4: all loads of the
+          // chunk in flight together, one round trip to L2)
+          float a[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) a[i] = 0.f;
+          if (present) {
+            float4 t[4][8];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const float4* src = reinterpret_cast<const float4*>(parts_ws + k * slot_floats) + (8 * c) * 128 + lrow;
+#pragma unroll
+              for (int i = 0; i < 8; ++i) t[k][i] = k < n_parts ? __ldcg(src + i * 128) : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+#pragma unroll
+              for (int i = 0; i < 8; ++i) {
+                a[4 * i] += t[k][i].x;
+                a[4 * i + 1] += t[k][i].y;
+                a[4 * i + 2] += t[k][i].z;
+                a[4 * i + 3] += t[k][i].w;
+              }
+          }
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = __float_as_uint(a[i]);
+        } else if (present) {
+          tmem_ld_32x32b_x32(t_acc + static_cast<uint32_t>(c * 32), v);
           tmem_ld_wait();
         } else {
 #pragma unroll

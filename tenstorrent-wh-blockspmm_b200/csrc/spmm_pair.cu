@@ -254,6 +254,7 @@ __global__ void __launch_bounds__(kRsThreads, 1) spmm_pair_tcgen05(const __grid_
       mbar_init(baddr(&hdr->acc_empty[a]), 8);  // 4 epilogue warps per CTA of the pair
     }
     mbar_init(baddr(&hdr->drain), 1);
+    mbar_init(baddr(&hdr->merge_bar), 4);  // this CTA's epilogue warps (split-K merge)
     hdr->abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&p.tm_a);
@@ -370,6 +371,8 @@ bsp_status launch_spmm_pair(const bsp_spmm_plan* p, const bsp_bsr_desc* A, const
     kp.cta_stage_begin = p->d_cta_stage_begin;
     kp.sub_bytes = p->sub_bytes;
     kp.xfer_off = p->xfer_off;
+    kp.split_ws = p->d_split_ws;
+    kp.split_counters = p->d_split_counters;
     p->kp_valid = true;
     p->kp_a = A->values;
     p->kp_b = B;

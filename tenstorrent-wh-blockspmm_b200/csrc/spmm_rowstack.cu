@@ -251,6 +251,7 @@ __global__ void __launch_bounds__(kRsThreads, 1) spmm_rowstack_tcgen05(const __g
       mbar_init(baddr(&hdr->acc_empty[a]), 4);
     }
     mbar_init(baddr(&hdr->drain), 1);
+    mbar_init(baddr(&hdr->merge_bar), 4);  // the epilogue warps (split-K merge)
     hdr->abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&p.tm_a);
@@ -372,6 +373,8 @@ bsp_status launch_spmm_rowstack(const bsp_spmm_plan* p, const bsp_bsr_desc* A, c
   kp.cta_stage_begin = p->d_cta_stage_begin;
   kp.sub_bytes = p->sub_bytes;
   kp.xfer_off = p->xfer_off;
+  kp.split_ws = p->d_split_ws;
+  kp.split_counters = p->d_split_counters;
   p->kp_valid = true;
   p->kp_a = A->values;
   p->kp_b = B;

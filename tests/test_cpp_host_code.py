@@ -33,4 +33,4 @@ def test_host_code_registries_on_gpu(tmp_path):
     assert "FAIL" not in r.stdout
     assert r.stdout.count("PASS") >= 6 * 6 + 10 * 3 + 3 + 1
     assert "bsp::spgemm" in r.stdout and "bsp::attention_step" in r.stdout
-    assert r.stdout.count("bsr_sddmm_multicore_SnF") == 10
+    assert r.stdout.count("PASS bsr_sddmm_multicore_SnF") == 10

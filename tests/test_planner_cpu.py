@@ -41,10 +41,29 @@ def test_spmm_schedule_covers_work_exactly_once(shape, strategy, opts):
         Rs = plan["slab"]
         slabs = R // Rs
         assert G * Rs == 128
-        covered = {}
+        tile_n = 128 * plan["n_tiles"]          # 256, or 128 when N <= 128
+        assert tile_n == (128 if N <= 128 else 256)
+        # units, or split-K parts of units: part (nt >> 8) of nt & 0xFF, slot r_off + part
+        tiles, slots = {}, set()
         for u in units:
-            row0, nent, _, n0, nt, sb, se, mask = (int(x) for x in u)
-            assert n0 % 256 == 0 and nt == 1
+            row0, nent, r_off, n0, nt, sb, se, mask = (int(x) for x in u)
+            assert n0 % tile_n == 0
+            n_parts, part = nt & 0xFF, (nt >> 8) & 0xFF
+            assert 1 <= n_parts <= 16 and part < n_parts
+            if n_parts > 1:
+                assert r_off + part not in slots and se - sb >= 1
+                slots.add(r_off + part)
+            else:
+                assert r_off == 0
+            tiles.setdefault((row0, n0), []).append((part, n_parts, r_off, sb, se, nent, mask))
+        covered = {}
+        for (row0, n0), parts in tiles.items():
+            parts.sort()
+            n_parts = parts[0][1]
+            assert [q[0] for q in parts] == list(range(n_parts))
+            assert all(q[1] == n_parts and q[2] == parts[0][2] and q[5:] == parts[0][5:] for q in parts)
+            assert all(a[4] == b[3] for a, b in zip(parts, parts[1:]))   # consecutive step ranges
+            sb, se, nent, mask = parts[0][3], parts[-1][4], parts[0][5], parts[0][6]
             blocks = {g: [] for g in range(G)}
             for s in range(sb, se):
                 for g in range(G):
@@ -57,7 +76,7 @@ def test_spmm_schedule_covers_work_exactly_once(shape, strategy, opts):
                 covered[(e, n0)] = covered.get((e, n0), 0) + 1
                 assert sorted(blocks[g]) == _row_blocks(rp, e // slabs)
                 assert bool((mask >> g) & 1) == (rp[e // slabs + 1] > rp[e // slabs])
-        assert len(covered) == nbr * slabs * ((N + 255) // 256)
+        assert len(covered) == nbr * slabs * ((N + tile_n - 1) // tile_n)
         assert all(v == 1 for v in covered.values())
         _check_stage_list(plan, rp, ci, R, C, Rs, slabs, G)
     else:
@@ -188,6 +207,37 @@ def test_sddmm_rowstack_schedule_covers_every_tile_once(strategy, R, C, K):
     # the A tile stays resident for CDA and SnF while two 128 x K tiles fit
     assert plan["keep_a"] == int(strategy != "naive" and K <= 256)
     _check_resident_a_runs(plan)
+
+
+@pytest.mark.parametrize("group_mma", [4, 5])
+def test_split_k_cuts_long_units(group_mma):
+    """A few very long block-rows (Zipf-like) make split-K worthwhile: the
+    planner cuts their units into parts over consecutive step ranges (each at
+    least 4 steps), which evens out the CTAs' step counts; opts.group_rows =
+    -1 keeps every unit whole."""
+    R = C = 32
+    M, K, N = 8192, 8192, 128 if group_mma == 4 else 256
+    nbr, nbc = M // R, K // C
+    rng = np.random.default_rng(17)
+    rows = [sorted(rng.choice(nbc, 200 if i < 8 else 6, replace=False)) for i in range(nbr)]
+    rp = np.concatenate([[0], np.cumsum([len(r) for r in rows])]).astype(np.int32)
+    ci = np.concatenate(rows).astype(np.int32)
+
+    def stats(plan):
+        u, cta = plan["unit_table"], plan["cta_begin"]
+        steps = u[:, 6] - u[:, 5]
+        per = [int(steps[cta[c]:cta[c + 1]].sum()) for c in range(len(cta) - 1)]
+        return u, steps, max(per)
+
+    split = bsp.inspect_spmm_plan(M, K, R, C, rp, ci, N, bsp.DDA, opts=bsp.make_opts(group_mma=group_mma))
+    whole = bsp.inspect_spmm_plan(M, K, R, C, rp, ci, N, bsp.DDA,
+                                  opts=bsp.make_opts(group_mma=group_mma, group_rows=-1))
+    u, steps, worst = stats(split)
+    uw, _, worst_whole = stats(whole)
+    parts = (u[:, 4] & 0xFF) > 1
+    assert parts.any() and not ((uw[:, 4] & 0xFF) > 1).any()
+    assert steps[parts].min() >= 4
+    assert worst < worst_whole
 
 
 @pytest.mark.parametrize("n_tiles", [0, 1])
@@ -326,6 +376,11 @@ def test_pair_schedule_covers_work_exactly_once(shape, opts):
             assert k == len(rows)
     assert len(seen) == int(rp[-1]) * slabs * nkc * ((N + 255) // 256)
     assert all(v == 1 for v in seen.values())
+    # split-K parts: each CTA's partial has its own workspace slot (rank r of
+    # a pair unit cut into n parts uses slots r_off .. r_off + n - 1)
+    slots = [int(u[2]) + ((int(u[4]) >> 8) & 0xFF) for u in units if (int(u[4]) & 0xFF) > 1]
+    assert len(slots) == len(set(slots))
+    assert all((int(u[4]) & 0xFF) >= 1 for u in units)
 
 
 def test_dda_picks_pair_kernel_only_where_it_pays():

@@ -258,3 +258,50 @@ def test_pair_kernel_empty_first_units(R, nonempty_rows, no_lb):
         dev.synchronize()
         assert_bf16_close(bsp.to_host_bits(C), gold, what=f"pair R={R}")
     plan.close()
+
+
+def _skewed_rows(rng, nbr, nbc, heavy, heavy_len, light_len):
+    rows = [sorted(rng.choice(nbc, heavy_len if i in heavy else light_len, replace=False)) for i in range(nbr)]
+    rp = np.concatenate([[0], np.cumsum([len(r) for r in rows])]).astype(np.int32)
+    return rp, np.concatenate(rows).astype(np.int32)
+
+
+@pytest.mark.parametrize("variant,N", [("dda_1cta", 128), ("dda_1cta", 256), ("dda_pair", 256), ("dda", 200)])
+@pytest.mark.parametrize("c_f32", [False, True])
+def test_spmm_split_k_parity(variant, N, c_f32):
+    """Block-rows far longer than the rest get split-K: parts of a unit over
+    consecutive step ranges leave fp32 partial tiles in the plan's workspace
+    and the last part to finish sums them and stores C.  The result matches
+    the oracle, and a second launch of the same plan (counters reset by the
+    merging parts) gives the same bits."""
+    import torch
+
+    bsp = _bsp()
+    R = C = 32
+    M, K = 4096, 8192
+    rng = np.random.default_rng(N + 7 * c_f32)
+    rp, ci = _skewed_rows(rng, M // R, K // C, heavy={3, 4, 5, 40, 41, 90}, heavy_len=230, light_len=5)
+    vals = oracle.f32_to_bf16(rng.uniform(-1, 1, ci.size * R * C).astype(np.float32))
+    B = rand_dense(rng, K, N)
+    sid, opts = _sv(bsp, variant)
+    plan_info = bsp.inspect_spmm_plan(M, K, R, C, rp, ci, N, sid, opts=opts)
+    assert ((plan_info["unit_table"][:, 4] & 0xFF) > 1).any()       # split-K is in the plan
+    A = bsp.DeviceBSR.from_host(M, K, R, C, rp, ci, vals)
+    Bd = bsp.to_device_bf16(B)
+    dev = bsp.device()
+    ctype = bsp.F32 if c_f32 else bsp.BF16
+    plan = bsp.SpmmPlan(dev, A, N, sid, ctype, opts)
+    outs = []
+    for _ in range(2):
+        Cd = torch.full((M, N), float("nan"), dtype=torch.float32 if c_f32 else torch.bfloat16, device="cuda")
+        plan.execute(A, Bd, Cd)
+        dev.synchronize()
+        outs.append(Cd.cpu().numpy() if c_f32 else bsp.to_host_bits(Cd))
+    plan.close()
+    assert np.array_equal(outs[0], outs[1])
+    if c_f32:
+        gold = oracle.spmm_f32(rp, ci, oracle.bf16_to_f32(vals), M, K, R, C, oracle.bf16_to_f32(B), N)
+        assert normwise(outs[0], gold) <= 1e-5
+    else:
+        gold = oracle.spmm_bf16(rp, ci, vals, M, K, R, C, B, N)
+        assert_bf16_close(outs[0], gold, what=f"split-K {variant} N={N}")

@@ -491,6 +491,27 @@ static std::vector<int32_t> choose_splits(const std::vector<int64_t>& weight, co
       best = cand;
     }
   }
+  // Equal-sized units leave the deal's last round part-filled (n mod ctas
+  // units): halving only the m heaviest units, m = ctas * ceil(n / ctas) - n
+  // (or one round more), makes the item count a multiple of the CTAs.
+  {
+    std::vector<int32_t> order(n);
+    std::iota(order.begin(), order.end(), 0);
+    std::stable_sort(order.begin(), order.end(), [&](int32_t a, int32_t b) { return weight[a] > weight[b]; });
+    const int64_t nn = static_cast<int64_t>(n);
+    const int64_t m1 = (nn + ctas - 1) / ctas * ctas - nn;
+    for (int64_t m : {m1, m1 + ctas}) {
+      if (m <= 0 || m > nn) continue;
+      std::fill(cand.begin(), cand.end(), 1);
+      for (int64_t r = 0; r < m; ++r)
+        if (nsteps[static_cast<size_t>(order[r])] >= 2 * kMinPartSteps) cand[static_cast<size_t>(order[r])] = 2;
+      const int64_t m_span = makespan(cand);
+      if (m_span < best_m) {
+        best_m = m_span;
+        best = cand;
+      }
+    }
+  }
   if (best_m * 100 > base * 97) std::fill(best.begin(), best.end(), 1);
   return best;
 }

@@ -31,19 +31,28 @@ def _free_port():
     return port
 
 
-def _case():
+def _case(kind="zipf"):
     import bench
 
     rng = np.random.default_rng(5)
-    M = K = 2048
-    N, R, C = 512, 64, 64
-    rp, ci = bench.gen_zipf_pattern(M // R, K // C, 0.05, 1.1, rng)
+    if kind == "skewed":
+        # a few block-rows far longer than the rest: each rank's plan cuts
+        # their units (split-K), and the merging part's stores reach both GPUs
+        M, K, N, R, C = 4096, 8192, 256, 32, 32
+        heavy = {3, 4, 5, 70, 71, 100}
+        rows = [sorted(rng.choice(K // C, 230 if i in heavy else 5, replace=False)) for i in range(M // R)]
+        rp = np.concatenate([[0], np.cumsum([len(r) for r in rows])]).astype(np.int32)
+        ci = np.concatenate(rows).astype(np.int32)
+    else:
+        M = K = 2048
+        N, R, C = 512, 64, 64
+        rp, ci = bench.gen_zipf_pattern(M // R, K // C, 0.05, 1.1, rng)
     vals = bench.uniform_bf16(rng, (ci.size * R, C)).reshape(-1)
     B = bench.uniform_bf16(rng, (K, N))
     return M, K, N, R, C, rp, ci, vals, B
 
 
-def _worker(rank, ws, port, q, fused):
+def _worker(rank, ws, port, q, fused, kind="zipf"):
     from datetime import timedelta
 
     import torch
@@ -61,7 +70,7 @@ def _worker(rank, ws, port, q, fused):
         os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
         dist.init_process_group("nccl", rank=rank, world_size=ws, timeout=timedelta(seconds=60),
                                 device_id=torch.device("cuda", rank))
-        M, K, N, R, C, rp, ci, vals, B = _case()
+        M, K, N, R, C, rp, ci, vals, B = _case(kind)
         dev = bsp.device(rank)
         sh = bsp_dist.ShardedSpmm(dev, M, K, R, C, rp, ci, vals, N, rank, ws, bsp.DDA, fused=fused)
         Bd = bsp.to_device_bf16(B, rank)
@@ -82,8 +91,9 @@ def _worker(rank, ws, port, q, fused):
         q.put((rank, False, repr(e), None))
 
 
+@pytest.mark.parametrize("kind", ["zipf", "skewed"])
 @pytest.mark.parametrize("fused", [True, False], ids=["fused-epilogue-stores", "nccl-send-recv"])
-def test_sharded_spmm_two_gpus(fused):
+def test_sharded_spmm_two_gpus(fused, kind):
     import torch
     import torch.multiprocessing as mp
 
@@ -93,7 +103,7 @@ def test_sharded_spmm_two_gpus(fused):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, ws, port, q, fused)) for r in range(ws)]
+    procs = [ctx.Process(target=_worker, args=(r, ws, port, q, fused, kind)) for r in range(ws)]
     for p in procs:
         p.start()
     res = [q.get(timeout=300) for _ in range(ws)]

@@ -438,8 +438,12 @@ bsp_status plan_spmm_host(bsp_spmm_plan* p, const int32_t* row_ptr, const int32_
 // the final sum's read of all n partials: the merge is bound by L2 round
 // trips on the merging CTA's critical path, so parts are also capped at 4
 // (a 16-part merge of config 5's longest rows cost more than it balanced).
+static void ordered_greedy(const std::vector<int64_t>& weight, int parts,
+                           std::vector<std::vector<int32_t>>* per_part);
+// ordered: the units are dealt in their given order (ordered_greedy), the
+// parts of a cut unit in its place; otherwise by the serpentine balancer.
 static std::vector<int32_t> choose_splits(const std::vector<int64_t>& weight, const std::vector<int32_t>& nsteps,
-                                          int ctas, int64_t partial_bytes) {
+                                          int ctas, int64_t partial_bytes, bool ordered = false) {
   constexpr int kMaxSplit = 4, kMinPartSteps = 4;
   const size_t n = weight.size();
   std::vector<int32_t> best(n, 1);
@@ -454,7 +458,8 @@ static std::vector<int32_t> choose_splits(const std::vector<int64_t>& weight, co
       }
     const int grid = static_cast<int>(std::min<int64_t>(ctas, static_cast<int64_t>(items.size())));
     std::vector<std::vector<int32_t>> per;
-    serpentine_order(items, grid, &per);
+    if (ordered) ordered_greedy(items, grid, &per);
+    else serpentine_order(items, grid, &per);
     int64_t worst = 0;
     for (const auto& v : per) {
       int64_t t = 0;
@@ -605,13 +610,31 @@ bsp_status plan_spmm_rowstack(bsp_spmm_plan* p, const int32_t* row_ptr, const in
     for (int q = 0; q < G; ++q) steps.push_back(-1);
   }
   int grid = o.max_ctas > 0 ? std::min(o.max_ctas, sm_count) : sm_count;
+  // When B does not fit in L2 (with room for A), the units run tile by tile:
+  // units in column-tile-major order, each dealt to the least-loaded CTA in
+  // that order, so all CTAs work on one B panel (K x tile_n) at a time and
+  // it is read from DRAM about once instead of once per row group.
+  const bool l2_order = !o.no_load_balance && ntiles > 1 && p->K * p->N * 2 > (int64_t(64) << 20);
+  if (l2_order) {
+    std::vector<int32_t> idx(units.size());
+    std::iota(idx.begin(), idx.end(), 0);
+    std::stable_sort(idx.begin(), idx.end(), [&](int32_t a, int32_t b) { return units[a].n0 < units[b].n0; });
+    std::vector<SpmmUnit> su(units.size());
+    std::vector<int64_t> sw(units.size());
+    for (size_t i = 0; i < idx.size(); ++i) {
+      su[i] = units[static_cast<size_t>(idx[i])];
+      sw[i] = weight[static_cast<size_t>(idx[i])];
+    }
+    units.swap(su);
+    weight.swap(sw);
+  }
   // split-K (not with the contiguous split; opts.group_rows = -1 turns it off)
   p->n_split_slots = 0;
   p->split_units = 0;
   if (!o.no_load_balance && o.group_rows != -1) {
     std::vector<int32_t> nst(units.size());
     for (size_t i = 0; i < units.size(); ++i) nst[i] = units[i].step_end - units[i].step_begin;
-    const std::vector<int32_t> np = choose_splits(weight, nst, grid, int64_t(128) * tile_n * 4);
+    const std::vector<int32_t> np = choose_splits(weight, nst, grid, int64_t(128) * tile_n * 4, l2_order);
     std::vector<SpmmUnit> su;
     std::vector<int64_t> sw;
     for (size_t i = 0; i < units.size(); ++i) {
@@ -640,6 +663,8 @@ bsp_status plan_spmm_rowstack(bsp_spmm_plan* p, const int32_t* row_ptr, const in
   std::vector<std::vector<int32_t>> per;
   if (o.no_load_balance)
     contiguous_split(static_cast<int64_t>(units.size()), grid, &per);
+  else if (l2_order)
+    ordered_greedy(weight, grid, &per);
   else
     serpentine_order(weight, grid, &per);
   p->h_units.clear();
@@ -783,13 +808,23 @@ bsp_status plan_spmm_pair(bsp_spmm_plan* p, const int32_t* row_ptr, const int32_
   }
   p->n_steps = static_cast<int64_t>(steps.size() / stride);
   int npairs = (o.max_ctas > 0 ? std::min(o.max_ctas, sm_count) : sm_count) / 2;
+  // B larger than L2: pair units run tile by tile (see plan_spmm_rowstack)
+  const bool l2_order = !o.no_load_balance && ntiles > 1 && p->K * p->N * 2 > (int64_t(64) << 20);
+  if (l2_order) {
+    std::stable_sort(units.begin(), units.end(), [](const PairUnit& a, const PairUnit& b) { return a.n0 < b.n0; });
+    // weights follow the units: recompute them in the new order
+    weight.clear();
+    for (const PairUnit& u : units)
+      weight.push_back(int64_t(u.s_end - u.s_begin) * nkc * (int64_t(kc) * 128 * 2 + int64_t(G) * Rs * kc * 2) +
+                       int64_t(G) * Rs * 256 * esz + 4096);
+  }
   // split-K over pair units (each rank keeps its own partial tile)
   p->n_split_slots = 0;
   p->split_units = 0;
   if (!o.no_load_balance && o.group_rows != -1) {
     std::vector<int32_t> nst(units.size());
     for (size_t i = 0; i < units.size(); ++i) nst[i] = units[i].s_end - units[i].s_begin;
-    const std::vector<int32_t> np = choose_splits(weight, nst, npairs, int64_t(128) * 256 * 4);
+    const std::vector<int32_t> np = choose_splits(weight, nst, npairs, int64_t(128) * 256 * 4, l2_order);
     std::vector<PairUnit> su;
     std::vector<int64_t> sw;
     for (size_t i = 0; i < units.size(); ++i) {
@@ -818,6 +853,8 @@ bsp_status plan_spmm_pair(bsp_spmm_plan* p, const int32_t* row_ptr, const int32_
   std::vector<std::vector<int32_t>> per;
   if (o.no_load_balance)
     contiguous_split(static_cast<int64_t>(units.size()), npairs, &per);
+  else if (l2_order)
+    ordered_greedy(weight, npairs, &per);
   else
     serpentine_order(weight, npairs, &per);
 

@@ -391,3 +391,19 @@ def test_dda_picks_pair_kernel_only_where_it_pays():
         rp, ci, _ = rand_bsr(rng, 4096, 4096, 32, 32, p)
         plan = bsp.inspect_spmm_plan(4096, 4096, 32, 32, rp, ci, 4096, bsp.DDA)
         assert plan["variant"] == want, (p, plan["variant"])
+
+
+def test_large_b_runs_tile_by_tile():
+    """When B (K x N bf16) exceeds 64 MiB the row-stacked plan deals its units
+    in column-tile order (each CTA's list has nondecreasing n0), so that the
+    CTAs share one B panel in L2 at a time; a B that fits keeps the
+    serpentine deal (tiles interleaved on a CTA)."""
+    R = C = 32
+    rng = np.random.default_rng(23)
+    M, K = 16384, 32768
+    rp, ci, _ = rand_bsr(rng, M, K, R, C, 0.005)
+    for N, tile_major in ((2048, True), (1024, False)):
+        plan = bsp.inspect_spmm_plan(M, K, R, C, rp, ci, N, bsp.DDA, opts=bsp.make_opts(group_mma=4))
+        u, cta = plan["unit_table"], plan["cta_begin"]
+        ordered = all(np.all(np.diff(u[cta[c]:cta[c + 1], 3]) >= 0) for c in range(len(cta) - 1))
+        assert ordered == tile_major, N

@@ -305,3 +305,17 @@ def test_spmm_split_k_parity(variant, N, c_f32):
     else:
         gold = oracle.spmm_bf16(rp, ci, vals, M, K, R, C, B, N)
         assert_bf16_close(outs[0], gold, what=f"split-K {variant} N={N}")
+
+
+@pytest.mark.parametrize("variant", ["dda_1cta", "dda_pair"])
+def test_spmm_large_b_tile_order_parity(variant):
+    """B of 128 MiB (more than fits in L2 beside A): the plan deals its units
+    tile by tile (and may cut long ones); the result matches the oracle."""
+    bsp = _bsp()
+    M, K, N, R, C = 1024, 32768, 2048, 32, 32
+    rng = np.random.default_rng(41)
+    rp, ci, vals = rand_bsr(rng, M, K, R, C, 0.01)
+    B = rand_dense(rng, K, N)
+    gold = oracle.spmm_bf16(rp, ci, vals, M, K, R, C, B, N)
+    out = _run(bsp, M, K, N, R, C, rp, ci, vals, B, variant)
+    assert_bf16_close(out, gold, what=f"large B {variant}")

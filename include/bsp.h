@@ -214,10 +214,13 @@ bsp_status bsp_spmm_host_profile(bsp_device* dev, int64_t M, int64_t K, int32_t 
  *     overlap on the GPU (other streams or host threads on the same device)
  *     race on it.
  *   - The first call on a device looks up the array's device address
- *     (cudaGetSymbolAddress) with that device current; make that first call
- *     before any stream capture.
- *   - The call is synchronous: it returns after the kernel has finished, and
- *     reports kernel wait timeouts as BSP_ERR_TIMEOUT.
+ *     (cudaGetSymbolAddress) with that device current.
+ *   - The call is synchronous: it waits for its stream and reads the status
+ *     word back with a blocking copy, so it must not be called while any
+ *     stream is capturing.  It reports kernel wait timeouts as
+ *     BSP_ERR_TIMEOUT.
+ *   - c_type BSP_BF16 or BSP_F32; A->values 16-byte aligned (as
+ *     bsp_spmm_plan_create requires); BSP_ERR_INVALID_ARG otherwise.
  * strategy must be BSP_NAIVE or BSP_SNF.  The device is the current CUDA
  * device; no bsp_device is needed. */
 bsp_status bsp_spmm_noalloc(const bsp_bsr_desc* A, const int32_t* host_row_ptr,

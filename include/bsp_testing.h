@@ -78,6 +78,23 @@ bsp_status bsp_attn_plan_inspect(int64_t S, int64_t d, int64_t nnzb, const int32
                                  int32_t max_smem, int64_t info[16], int32_t* units_out,
                                  int32_t* chunks_out, int32_t* cta_begin_out);
 
+/* Device address and size of a row-stacked SpMM plan's split-K counters:
+ * *counters points at two sets of *per_set int32 counters; the next launch
+ * uses set *next_set and zeroes the other one before any of its waits.
+ * (Tests overwrite the idle set to stand for counts that a launch which gave
+ * up after a timeout left behind.)  *counters is NULL without split-K. */
+bsp_status bsp_testing_spmm_counters(const bsp_spmm_plan* plan, void** counters, int64_t* per_set,
+                                     int32_t* next_set);
+
+/* Fault injection for the bounded-wait tests of row-stacked (single-CTA DDA)
+ * plans: stage_plus_one = k + 1 makes CTA 0's producer leave its k-th pipeline
+ * stage unissued on every later launch of `plan` (0 turns it off).  The MMA
+ * warp's wait for that stage then runs out after the plan's timeout_ms, every
+ * role drains its own copies and MMAs, TMEM is freed, and
+ * bsp_device_synchronize reports BSP_ERR_TIMEOUT; the device stays usable.
+ * No barrier is left unbounded and no memory access changes. */
+bsp_status bsp_testing_spmm_drop_stage(bsp_spmm_plan* plan, int32_t stage_plus_one);
+
 #ifdef __cplusplus
 }
 #endif

@@ -57,6 +57,7 @@ def lib():
         _lib.bsp_oracle_spgemm_symbolic.argtypes = [I, I, P, P, P, P, P, P]
         _lib.bsp_oracle_spgemm_symbolic.restype = _i64
         _lib.bsp_oracle_spgemm_bf16.argtypes = [I, I, I, I, P, P, P, P, P, P, P, P, P]
+        _lib.bsp_oracle_rand_fill.argtypes = [ctypes.c_uint32, I, P, I, P]
     return _lib
 
 
@@ -203,6 +204,16 @@ def attention_bf16(indptr, indices, S, d, Q, K, V, scale, rows=None, use_ref=Fal
     if use_ref:
         return ref_spmm_bf16(urp, uci, Pb, S, S, R, R, _c(V, np.uint16).reshape(S, d), d)
     return spmm_bf16(urp, uci, Pb, S, S, R, R, _c(V, np.uint16).reshape(S, d), d)
+
+
+def rand_fill(seed: int, n_unit: int, n_signed: int):
+    """(unit, signed) float32 arrays drawn as the reference's generators draw
+    them after srand(seed): n_unit values rand()/RAND_MAX, then n_signed values
+    of the RAND content kind (see bsp_oracle_rand_fill)."""
+    u = np.empty(max(n_unit, 1), np.float32)
+    s = np.empty(max(n_signed, 1), np.float32)
+    lib().bsp_oracle_rand_fill(seed, n_unit, _ptr(u), n_signed, _ptr(s))
+    return u[:n_unit], s[:n_signed]
 
 
 def serpentine(n: int, parts: int):

@@ -333,3 +333,12 @@ void bsp_oracle_sddmm_bf16_mt(int64_t H, int64_t W, int64_t R, int64_t C, const 
   job_t j = {1, H, W, R, C, 0, K, indptr, indices, mask_data, B, A, out_blocks, row_begin, row_end};
   run_split(j, nthreads);
 }
+
+/* Restates the reference generators' draws (see bsp_oracle.h): one srand, then
+ * the unit-interval draws, then the signed RAND draws, in that order. */
+void bsp_oracle_rand_fill(uint32_t seed, int64_t n_unit, float* unit_out, int64_t n_signed,
+                          float* signed_out) {
+  srand(seed);
+  for (int64_t i = 0; i < n_unit; ++i) unit_out[i] = (float)rand() / (float)RAND_MAX;
+  for (int64_t i = 0; i < n_signed; ++i) signed_out[i] = (float)(RAND_MAX / 2 - rand()) / 2048.0f;
+}

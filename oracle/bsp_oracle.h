@@ -76,6 +76,17 @@ void bsp_oracle_sddmm_bf16_mt(int64_t H, int64_t W, int64_t R, int64_t C, const 
                               const uint16_t* A, const uint16_t* B, uint16_t* out_blocks,
                               int64_t row_begin, int64_t row_end, int32_t nthreads);
 
+/* The reference's value generators, which draw from the C library rand()
+ * after srand(seed).  First n_unit values rand() / RAND_MAX in float (the block
+ * data of test_random_hang / _v2, block_spmm/inc/test_suite.hpp:584-646), then
+ * n_signed values of the RAND content kind, float(RAND_MAX / 2 - rand()) / 2048
+ * (sparse_common/bsr_matrix.hpp:23-24 and 54-55): the dense operand of
+ * make_frozen_case (block_spmm/inc/profiling_suite.hpp:69-91) is n_signed =
+ * K * N such values after srand(42).  Either output may be NULL when its count
+ * is 0.  Uses the process-wide rand() state (not thread-safe). */
+void bsp_oracle_rand_fill(uint32_t seed, int64_t n_unit, float* unit_out, int64_t n_signed,
+                          float* signed_out);
+
 #ifdef __cplusplus
 }
 #endif

@@ -139,6 +139,9 @@ def lib():
         "bsp_attn_plan_inspect": (S, [I64, I64, I64, P, P, ctypes.POINTER(Opts), I32, I32, P, P, P, P]),
         "bsp_spmm_plan_traffic": (S, [I64, I64, I32, I32, I64, P, P, I64, S, ctypes.POINTER(Opts), I32, I32,
                                       P, P]),
+        "bsp_testing_spmm_counters": (S, [P, ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(I64),
+                                          ctypes.POINTER(I32)]),
+        "bsp_testing_spmm_drop_stage": (S, [P, I32]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)

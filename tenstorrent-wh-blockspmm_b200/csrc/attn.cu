@@ -498,6 +498,10 @@ __global__ void __launch_bounds__(kAtThreads, 1) attn_tcgen05(const __grid_const
   const int lane = threadIdx.x & 31;
   const int u_begin = p.cta_begin[blockIdx.x];
   const int u_end = p.cta_begin[blockIdx.x + 1];
+  // zero the other launch parity's counters (before any wait of this launch)
+  if (p.counters_next != nullptr)
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < p.n_counters; i += gridDim.x * blockDim.x)
+      p.counters_next[i] = 0;
 
   if (threadIdx.x == 32) {
     mbar_init(baddr(&hdr->q_full), 1);
@@ -576,7 +580,13 @@ bsp_status launch_attn(const bsp_attn_plan* p, const void* Q, int64_t ldq, const
   kp.chunks = p->d_chunks;
   kp.cta_begin = p->d_cta_begin;
   kp.work = p->d_work;
-  kp.counters = p->d_counters;
+  {
+    // alternate counter sets by launch; this launch zeroes the other one
+    const uint32_t par = p->launch_parity & 1u;
+    kp.n_counters = static_cast<int32_t>(p->n_counters);
+    kp.counters = p->d_counters ? p->d_counters + par * p->n_counters : nullptr;
+    kp.counters_next = p->d_counters ? p->d_counters + (par ^ 1u) * p->n_counters : nullptr;
+  }
   kp.o = static_cast<uint16_t*>(O);
   kp.ldo = ldo;
   kp.status = dev->d_status;
@@ -588,6 +598,7 @@ bsp_status launch_attn(const bsp_attn_plan* p, const void* Q, int64_t ldq, const
   cudaError_t e = cudaFuncSetAttribute(attn_tcgen05, cudaFuncAttributeMaxDynamicSharedMemorySize, p->smem_bytes);
   if (e != cudaSuccess) return cuda_check(e, "cudaFuncSetAttribute(attn)");
   attn_tcgen05<<<p->grid, kAtThreads, p->smem_bytes, stream>>>(kp);
+  p->launch_parity ^= 1u;
   return cuda_check(cudaGetLastError(), "attention kernel launch");
 }
 

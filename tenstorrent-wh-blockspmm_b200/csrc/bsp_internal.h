@@ -74,9 +74,19 @@ struct SpmmKernelParams {
   // split-K (row-stacked kernels): a unit with nt & 0xFF = n parts > 1 is part
   // (nt >> 8) & 0xFF of n; its partial tile goes to workspace slot r_off + part
   // (acc_cols / 4 float4 columns of 128 rows), and the part that takes the
-  // last count of split_counters[r_off] sums the n partials and stores C
+  // last count of split_counters[r_off] sums the n partials and stores C.
+  // The plan holds two counter sets used by alternate launches: every launch
+  // zeroes the other set (split_counters_next, n_split_counters entries) before
+  // any of its waits, so a launch that gave up after a timeout, with counts
+  // left behind, cannot disturb the launch after next.
   float* split_ws;
   int32_t* split_counters;
+  int32_t* split_counters_next;
+  int32_t n_split_counters;
+  // Testing only (bsp_testing_spmm_drop_stage): k + 1 makes CTA 0's producer
+  // leave its k-th pipeline stage unissued (no copy, no arrive), so that the
+  // MMA warp's bounded wait on it runs out; 0 = off.
+  int32_t debug_drop_stage;
 };
 
 // Row-stacked kernel stage descriptor (16 words), precomputed by the planner
@@ -246,6 +256,8 @@ struct AttnKernelParams {
   uint64_t timeout_ns;
   float* work;           // split units: per slot 128 x d partial O, then 128 maxima, 128 sums
   int32_t* counters;     // split units: parts finished (the merging part resets it to 0)
+  int32_t* counters_next;  // the other launch parity's counters, zeroed by this launch
+  int32_t n_counters;
   int32_t S, d;
   float scale_log2;      // softmax scale * log2(e)
   int32_t tmem_cols;
@@ -312,14 +324,15 @@ struct bsp_attn_plan {
   int64_t n_units = 0, n_chunks = 0;
   int64_t n_slots = 0, n_counters = 0;  // workspace slots and counters of split units
   uint64_t timeout_ns = 0;
-  void* d_blob = nullptr;    // units | chunks | cta_begin | counters (zeroed)
+  void* d_blob = nullptr;    // units | chunks | cta_begin | 2 x counters (zeroed)
   size_t blob_bytes = 0;
   bool blob_borrowed = false;  // tables and merge workspace belong to the device (host-buffer path)
   float* d_work = nullptr;
   bsp::AttnUnit* d_units = nullptr;
   bsp::AttnChunk* d_chunks = nullptr;
   int32_t* d_cta_begin = nullptr;
-  int32_t* d_counters = nullptr;
+  int32_t* d_counters = nullptr;  // two sets of n_counters, alternate launches
+  mutable uint32_t launch_parity = 0;
   std::vector<bsp::AttnUnit> h_units;
   std::vector<bsp::AttnChunk> h_chunks;
   std::vector<int32_t> h_cta_begin;
@@ -342,7 +355,9 @@ struct bsp_spmm_plan {
   int64_t n_split_slots = 0;
   int32_t split_units = 0;
   float* d_split_ws = nullptr;       // owned unless blob_borrowed
-  int32_t* d_split_counters = nullptr;  // in the blob (zeroed), one per slot
+  int32_t* d_split_counters = nullptr;  // in the blob (zeroed): two sets of one per slot
+  mutable uint32_t launch_parity = 0;   // which counter set the next launch uses
+  int32_t debug_drop_stage = 0;         // testing only, see SpmmKernelParams
   uint64_t timeout_ns = 0;
   void* d_blob = nullptr;  // units | cta_begin | steps
   size_t blob_bytes = 0;
@@ -450,4 +465,16 @@ bsp_status launch_attn(const bsp_attn_plan* p, const void* Q, int64_t ldq, const
 int attn_smem_bytes(int d);
 bsp_status plan_spmm_rowstack(bsp_spmm_plan* p, const int32_t* row_ptr, const int32_t* col_idx,
                               int sm_count, int max_smem, const bsp_spmm_opts* opts, bool stage_lists = true);
+
+// Split-K counters of the next launch of a row-stacked plan: the set of this
+// launch's parity, and the other set, which the launch zeroes for the one after.
+inline void select_split_counters(const bsp_spmm_plan* p, SpmmKernelParams& k) {
+  const int64_t n = p->n_split_slots;
+  const uint32_t par = p->launch_parity & 1u;
+  k.n_split_counters = static_cast<int32_t>(n);
+  k.split_counters = p->d_split_counters ? p->d_split_counters + par * n : nullptr;
+  k.split_counters_next = p->d_split_counters ? p->d_split_counters + (par ^ 1u) * n : nullptr;
+  k.debug_drop_stage = p->debug_drop_stage;
+  p->launch_parity ^= 1u;
+}
 }  // namespace bsp

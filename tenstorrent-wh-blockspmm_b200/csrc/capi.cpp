@@ -365,7 +365,8 @@ static bsp_status spmm_plan_create_impl(bsp_device* dev, const bsp_bsr_desc* A, 
     return s;
   }
   std::vector<void*> ptrs;
-  const std::vector<int32_t> zeros(static_cast<size_t>(p->n_split_slots), 0);  // split-K counters
+  // split-K counters: two sets, used by alternate launches (each launch zeroes the other)
+  const std::vector<int32_t> zeros(2 * static_cast<size_t>(p->n_split_slots), 0);
   const std::vector<std::pair<const void*, size_t>> parts = {
       {p->h_units.data(), p->h_units.size() * sizeof(SpmmUnit)},
       {p->h_cta_begin.data(), p->h_cta_begin.size() * sizeof(int32_t)},
@@ -1149,7 +1150,8 @@ static bsp_status attn_plan_create_impl(bsp_device* dev, const bsp_bsr_desc* mas
     return s;
   }
   std::vector<void*> ptrs;
-  const std::vector<int32_t> zeros(static_cast<size_t>(p->n_counters), 0);
+  // split-unit counters: two sets, used by alternate launches (each launch zeroes the other)
+  const std::vector<int32_t> zeros(2 * static_cast<size_t>(p->n_counters), 0);
   const std::vector<std::pair<const void*, size_t>> parts = {
       {p->h_units.data(), p->h_units.size() * sizeof(AttnUnit)},
       {p->h_chunks.data(), p->h_chunks.size() * sizeof(AttnChunk)},
@@ -1306,6 +1308,23 @@ bsp_status bsp_serpentine_assign(int64_t n, int32_t parts, int32_t* owner, int32
 #include "bsp_testing.h"
 
 extern "C" {
+
+bsp_status bsp_testing_spmm_counters(const bsp_spmm_plan* plan, void** counters, int64_t* per_set,
+                                     int32_t* next_set) {
+  if (!plan || !counters || !per_set || !next_set) return set_error(BSP_ERR_INVALID_ARG, "null argument");
+  *counters = plan->n_split_slots > 0 ? plan->d_split_counters : nullptr;
+  *per_set = plan->n_split_slots;
+  *next_set = static_cast<int32_t>(plan->launch_parity & 1u);
+  return BSP_OK;
+}
+
+bsp_status bsp_testing_spmm_drop_stage(bsp_spmm_plan* plan, int32_t stage_plus_one) {
+  if (!plan || stage_plus_one < 0) return set_error(BSP_ERR_INVALID_ARG, "bad arguments");
+  if (plan->variant != 1)
+    return set_error(BSP_ERR_UNSUPPORTED, "stage dropping is built into the row-stacked kernel only");
+  plan->debug_drop_stage = stage_plus_one;
+  return BSP_OK;
+}
 
 bsp_status bsp_spmm_plan_inspect(int64_t M, int64_t K, int32_t R, int32_t C, int64_t nnzb,
                                  const int32_t* row_ptr, const int32_t* col_idx, int64_t N,

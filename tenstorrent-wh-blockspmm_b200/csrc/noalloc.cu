@@ -81,8 +81,13 @@ extern "C" bsp_status bsp_spmm_noalloc(const bsp_bsr_desc* A, const int32_t* hos
   if (strategy != BSP_NAIVE && strategy != BSP_SNF)
     return set_error(BSP_ERR_UNSUPPORTED, "bsp_spmm_noalloc runs the Naive and SnF strategies");
   if (A->R <= 0 || A->C <= 0 || A->rows <= 0 || A->cols <= 0 || A->nnzb < 0 ||
-      (A->nnzb > 0 && !A->values))
+      (A->nnzb > 0 && !A->values) || A->rows % A->R || A->cols % A->C || !A->row_ptr ||
+      (A->nnzb > 0 && !A->col_idx))
     return set_error(BSP_ERR_INVALID_ARG, "bad BSR descriptor");
+  if (A->values && reinterpret_cast<uintptr_t>(A->values) % 16)
+    return set_error(BSP_ERR_INVALID_ARG, "BSR values must be 16-byte aligned");
+  if (c_type != BSP_BF16 && c_type != BSP_F32)
+    return set_error(BSP_ERR_INVALID_ARG, "C type must be BSP_BF16 or BSP_F32");
   if (ldb < N || ldc < N) return set_error(BSP_ERR_INVALID_ARG, "leading dimensions must be >= N");
   int ordinal = 0;
   void* scratch = nullptr;

@@ -43,6 +43,14 @@ enum : uint32_t {
 
 __device__ __forceinline__ uint32_t baddr(const uint64_t* b) { return smem_u32(b); }
 
+// Zero the other launch parity's split-K counters (grid-stride, before any
+// wait of this launch, so it completes even when the launch gives up later).
+__device__ __forceinline__ void rs_clear_next_counters(const SpmmKernelParams& p) {
+  if (p.split_counters_next == nullptr) return;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < p.n_split_counters; i += gridDim.x * blockDim.x)
+    p.split_counters_next[i] = 0;
+}
+
 static __device__ __noinline__ bool rs_drain_wait(uint32_t bar, uint32_t parity, const WaitCtl& ctl) {
   int zero = 0;
   WaitCtl c2{&zero, ctl.status, ctl.timeout_ns};

@@ -243,6 +243,7 @@ __global__ void __launch_bounds__(kRsThreads, 1) spmm_pair_tcgen05(const __grid_
   const uint32_t rank = cluster_rank();
   const int u_begin = p.cta_begin[blockIdx.x];
   const int u_end = p.cta_begin[blockIdx.x + 1];
+  rs_clear_next_counters(p);
 
   if (threadIdx.x == 32) {
     for (int s = 0; s < p.stages; ++s) {
@@ -372,8 +373,7 @@ bsp_status launch_spmm_pair(const bsp_spmm_plan* p, const bsp_bsr_desc* A, const
     kp.sub_bytes = p->sub_bytes;
     kp.xfer_off = p->xfer_off;
     kp.split_ws = p->d_split_ws;
-    kp.split_counters = p->d_split_counters;
-    p->kp_valid = true;
+      p->kp_valid = true;
     p->kp_a = A->values;
     p->kp_b = B;
     p->kp_c = C;
@@ -382,6 +382,7 @@ bsp_status launch_spmm_pair(const bsp_spmm_plan* p, const bsp_bsr_desc* A, const
   }
   kp.n_peers = n_peers;
   for (int i = 0; i < kMaxPeers; ++i) kp.peer_c[i] = i < n_peers ? peer_c[i] : nullptr;
+  select_split_counters(p, kp);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(p->grid));
   cfg.blockDim = dim3(kRsThreads);

@@ -78,6 +78,16 @@ __device__ __forceinline__ void rs_producer(const SpmmKernelParams& p, RsSmemHea
       ok = mbar_wait_bounded(baddr(&hdr->empty[stage]), phase ^ 1u, ctl, ST_TIMEOUT_PRODUCER);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
+      if (p.debug_drop_stage != 0 && blockIdx.x == 0 && k0 + j * P == p.debug_drop_stage - 1) {
+        // testing: leave this stage unissued (nothing armed, nothing to drain);
+        // the MMA warp's bounded wait on it runs out and the launch gives up
+        stage += P;
+        if (stage >= p.stages) {
+          stage -= p.stages;
+          phase ^= 1u;
+        }
+        continue;
+      }
       const uint32_t sb = stage0 + static_cast<uint32_t>(stage) * p.stage_bytes;
       const uint32_t zero = (flags >> 8) & 0xFFu;
       if (zero) {
@@ -240,6 +250,7 @@ __global__ void __launch_bounds__(kRsThreads, 1) spmm_rowstack_tcgen05(const __g
   const int lane = threadIdx.x & 31;
   const int u_begin = p.cta_begin[blockIdx.x];
   const int u_end = p.cta_begin[blockIdx.x + 1];
+  rs_clear_next_counters(p);
 
   if (threadIdx.x == 32) {
     for (int s = 0; s < p.stages; ++s) {
@@ -315,6 +326,7 @@ bsp_status launch_spmm_rowstack(const bsp_spmm_plan* p, const bsp_bsr_desc* A, c
   if (p->kp_valid && p->kp_a == A->values && p->kp_b == B && p->kp_c == C && p->kp_ldb == ldb &&
       p->kp_ldc == ldc) {
     set_peers(p->kp);
+    select_split_counters(p, p->kp);
     kern<<<p->grid, kRsThreads, p->smem_bytes, stream>>>(p->kp);
     return cuda_check(cudaGetLastError(), "spmm rowstack kernel launch");
   }
@@ -374,7 +386,6 @@ bsp_status launch_spmm_rowstack(const bsp_spmm_plan* p, const bsp_bsr_desc* A, c
   kp.sub_bytes = p->sub_bytes;
   kp.xfer_off = p->xfer_off;
   kp.split_ws = p->d_split_ws;
-  kp.split_counters = p->d_split_counters;
   p->kp_valid = true;
   p->kp_a = A->values;
   p->kp_b = B;
@@ -382,6 +393,7 @@ bsp_status launch_spmm_rowstack(const bsp_spmm_plan* p, const bsp_bsr_desc* A, c
   p->kp_ldb = ldb;
   p->kp_ldc = ldc;
   set_peers(kp);
+  select_split_counters(p, kp);
   kern<<<p->grid, kRsThreads, p->smem_bytes, stream>>>(kp);
   return cuda_check(cudaGetLastError(), "spmm rowstack kernel launch");
 }

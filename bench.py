@@ -767,11 +767,7 @@ def run_bsp(args):
         "higher_is_better": True, "scaling": "strong" if sharded else "weak", "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic (seeded numpy, BASELINE config shapes and value distributions)",
-        "config": {"workload": WORKLOAD_DESC[args.workload], "name": args.workload,
-                   "strategy": args.strategy, "c_dtype": "bf16", "accumulate": "fp32",
-                   "l2": "flushed (256 MiB write) before every timed launch",
-                   "per_rank": ("row panels of one problem, balanced by nonzero blocks" if sharded
-                                else "independent copy per rank") if ws > 1 else None},
+        "config": bench_config(args, ws),
         "roofline": roof, "cpu_baseline": cpu, "e2e": e2e,
         "gpu_launches": args.steps * len(runs), "clocks": clocks, "per_op": per,
     }
@@ -785,6 +781,17 @@ def run_bsp(args):
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def bench_config(args, ws):
+    """The workload description both arms print (the same dict, so that the
+    two lines name the same workload)."""
+    sharded = args.workload == "cfg5"
+    return {"workload": WORKLOAD_DESC[args.workload], "name": args.workload,
+            "strategy": args.strategy, "c_dtype": "bf16", "accumulate": "fp32",
+            "l2": "flushed (256 MiB write) before every timed launch",
+            "per_rank": ("row panels of one problem, balanced by nonzero blocks" if sharded
+                         else "independent copy per rank") if ws > 1 else None}
 
 
 def _pinned(a):
@@ -923,8 +930,7 @@ def run_reference(args):
            "ms_per_step": tot_t / args.steps * 1e3, "higher_is_better": True,
            "scaling": "strong" if args.workload == "cfg5" else "weak", "vs_baseline": None,
            "dtype": "bf16", "data": "synthetic",
-           "config": {"workload": WORKLOAD_DESC[args.workload], "name": args.workload,
-                      "strategy": "cpu golden"},
+           "config": bench_config(args, ws),
            "cpu_baseline": {"value": v, "unit": "TFLOP/s", "cores": cpu_threads_used(ops, threads),
                             "kind": kind,
                             "sample": sample + ", every step"},

@@ -12,7 +12,12 @@ import pytest
 import oracle
 
 GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
-FIXTURES = sorted(glob.glob(os.path.join(GOLDEN, "*.npz")))
+# fixtures storing their inputs; the reference's structural fixtures (frozen
+# patterns, hang and deadlock repros) store a seed instead and are pinned below
+SEEDED = ("spmm_frozen_profiling_suite", "spmm_test_random_hang", "spmm_test_random_hang_v2",
+          "sddmm_deadlock_sweepK_0")
+FIXTURES = sorted(f for f in glob.glob(os.path.join(GOLDEN, "*.npz"))
+                  if os.path.basename(f)[:-4] not in SEEDED)
 
 
 def test_fixtures_present():
@@ -150,3 +155,80 @@ def test_bf16_rounding_is_nearest_even():
     assert oracle.bf16_to_f32(b)[2] == 1.0 + 2 ** -6  # tie to even (up)
     assert oracle.bf16_to_f32(b)[3] == -2.5
     assert np.isinf(oracle.bf16_to_f32(b)[4])
+
+
+# ---- the reference's structural fixtures (patterns read from its headers) ----
+def _sub_rows(ip, ix, vals, R, C, blocks):
+    sub_ip, sub_ix, sub_v = [0], [], []
+    vv = vals.reshape(-1, R * C)
+    for b in blocks:
+        sub_ix.append(ix[ip[b]:ip[b + 1]])
+        sub_v.append(vv[ip[b]:ip[b + 1]])
+        sub_ip.append(sub_ip[-1] + int(ip[b + 1] - ip[b]))
+    return (np.array(sub_ip, np.int32), np.concatenate(sub_ix).astype(np.int32),
+            np.concatenate(sub_v).reshape(-1))
+
+
+def test_rand_fill_restates_reference_generator():
+    """oracle.rand_fill draws what the reference's RAND content kind draws
+    after srand(seed) (live against the compiled reference generator when
+    built here, and against the first values stored in the fixtures)."""
+    _, s = oracle.rand_fill(42, 0, 4096)
+    z = np.load(os.path.join(GOLDEN, "spmm_frozen_profiling_suite.npz"))
+    tag = sorted({k.split("__")[0] for k in z.files if "__" in k})[0]
+    assert np.array_equal(oracle.f32_to_bf16(s)[:256], z[f"{tag}__b_head"])
+    if oracle.ref_available():
+        assert np.array_equal(s, oracle.ref_generate_dense(64, 64, oracle.RAND, seed=42).ravel())
+
+
+FROZEN_PIN = ["M8192_N8192_K8192_R32_C32_dppm30", "M8192_N8192_K8192_R32_C32_dppm3000",
+              "M8192_N8192_K8192_R64_C64_dppm600", "M8192_N8192_K8192_R128_C128_dppm50000",
+              "M8192_N8192_K512_R256_C256_dppm100000", "M8192_N1024_K8192_R256_C256_dppm100000"]
+
+
+@pytest.mark.parametrize("tag", FROZEN_PIN)
+def test_oracle_reproduces_frozen_pattern_golden(tag):
+    """Bit-exact: the oracle on the sampled rows and columns of a frozen
+    profiling pattern equals the reference golden stored for them."""
+    z = np.load(os.path.join(GOLDEN, "spmm_frozen_profiling_suite.npz"))
+    assert len({k.split("__")[0] for k in z.files if "__" in k}) == 36
+    M, N, K, R, C, _ = (int(x) for x in z[f"{tag}__shape"])
+    ip, ix, rows, cols = z[f"{tag}__indptr"], z[f"{tag}__indices"], z[f"{tag}__rows"], z[f"{tag}__cols"]
+    _, s = oracle.rand_fill(int(z["b_seed"]), 0, K * N)
+    B = oracle.f32_to_bf16(s.reshape(K, N)[:, cols])
+    vals = np.full(ix.size * R * C, 0x3F80, np.uint16)
+    blocks = np.unique(rows // R)
+    sip, six, sv = _sub_rows(ip, ix, vals, R, C, blocks)
+    out = oracle.spmm_bf16(sip, six, sv, blocks.size * R, K, R, C, B, cols.size, threads=4)
+    pos = {int(b): i for i, b in enumerate(blocks)}
+    sel = np.array([pos[int(r) // R] * R + int(r) % R for r in rows])
+    assert np.array_equal(out[sel], z[f"{tag}__out"])
+
+
+@pytest.mark.parametrize("name", ["spmm_test_random_hang", "spmm_test_random_hang_v2"])
+def test_oracle_reproduces_hang_pattern_golden(name):
+    z = np.load(os.path.join(GOLDEN, name + ".npz"))
+    M, K, R, C, N = (int(z[k]) for k in ("H", "W", "R", "C", "N"))
+    u, s = oracle.rand_fill(int(z["seed"]), z["indices"].size * R * C, K * N)
+    out = oracle.spmm_bf16(z["indptr"], z["indices"], oracle.f32_to_bf16(u), M, K, R, C,
+                           oracle.f32_to_bf16(s).reshape(K, N), N, threads=4)
+    assert np.array_equal(out[np.ix_(z["rows"], z["cols"])], z["out"])
+
+
+def test_oracle_reproduces_sddmm_deadlock_golden():
+    z = np.load(os.path.join(GOLDEN, "sddmm_deadlock_sweepK_0.npz"))
+    M, N, R, C, K = (int(z[k]) for k in ("H", "W", "R", "C", "K"))
+    ip, ix = z["indptr"], z["indices"]
+    nb = ix.size
+    _, s = oracle.rand_fill(int(z["seed"]), 0, nb * R * C + M * K + K * N)
+    mask = oracle.f32_to_bf16(s[:nb * R * C] * np.float32(2.0 ** int(z["mask_scale_log2"])))
+    A = oracle.f32_to_bf16(s[nb * R * C:nb * R * C + M * K]).reshape(M, K)
+    B = oracle.f32_to_bf16(s[nb * R * C + M * K:]).reshape(K, N)
+    # only the sampled blocks' block-rows
+    brs = np.unique(np.searchsorted(ip, z["blocks"], side="right") - 1)
+    out = np.zeros(nb * R * C, np.uint16)
+    for b in brs:
+        o = oracle.sddmm_bf16(ip, ix, mask, M, N, R, C, A, B, K, threads=4, rows=(int(b), int(b) + 1))
+        out[ip[b] * R * C:ip[b + 1] * R * C] = o[ip[b] * R * C:ip[b + 1] * R * C]
+    got = out.reshape(nb, R, C)[z["blocks"]][:, z["rows"]][:, :, z["cols"]]
+    assert np.array_equal(got, z["out"])

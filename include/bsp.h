@@ -123,6 +123,33 @@ int bsp_device_sm_count(const bsp_device* dev);
 const char* bsp_last_error_string(void);
 const char* bsp_status_string(bsp_status s);
 
+/* ---- device storage -------------------------------------------------------
+ * Device buffers: the reference's buffer helper sparse_common::MakeBuffer
+ * (sparse_common/host_code_utils.cpp:5-18, a tt-metal DRAM or L1 buffer) and
+ * its blocking EnqueueWriteBuffer / EnqueueReadBuffer
+ * (block_spmm/inc/host_code/bsr_spmm_multicore_load_balanced_new_DM.cpp:
+ * 140-144, 499-505).  alloc: `bytes` of device memory on dev (256-byte
+ * aligned), free: release it; write / read: blocking host <-> device copies. */
+bsp_status bsp_buffer_alloc(bsp_device* dev, int64_t bytes, void** ptr);
+bsp_status bsp_buffer_free(bsp_device* dev, void* ptr);
+bsp_status bsp_buffer_write(bsp_device* dev, void* dst_device, const void* src_host, int64_t bytes);
+bsp_status bsp_buffer_read(bsp_device* dev, void* dst_host, const void* src_device, int64_t bytes);
+
+/* A persistent device copy of a host BSR matrix (the reference uploads A's
+ * blocks, indptr and indices into fresh buffers on every call,
+ * load_balanced_new_DM.cpp:140-144 and 502-505; here one upload serves any
+ * number of plans and executes).  Checks the pattern (row_ptr starts at 0,
+ * ends at nnzb and never decreases; column indices in range), copies it with
+ * the values (host_values NULL: a pattern-only SDDMM mask) into ONE device
+ * allocation and fills *out: row_ptr at the allocation's start, col_idx and
+ * the values each at a 256-byte boundary.  Synchronous.  Free it with
+ * bsp_bsr_free, which releases the allocation and zeroes the descriptor;
+ * pass it only descriptors that bsp_bsr_upload filled. */
+bsp_status bsp_bsr_upload(bsp_device* dev, int64_t rows, int64_t cols, int32_t R, int32_t C, int64_t nnzb,
+                          const int32_t* host_row_ptr, const int32_t* host_col_idx,
+                          const uint16_t* host_values, bsp_bsr_desc* out);
+bsp_status bsp_bsr_free(bsp_device* dev, bsp_bsr_desc* desc);
+
 /* ---- SpMM: C[M x N] = A_bsr[M x K] * B[K x N] ---------------------------
  * Replaces HostCodeFunctionPtr (block_spmm/inc/host_code.hpp:165-177) and the
  * three planners behind it.  A plan is the reference planner's output (row

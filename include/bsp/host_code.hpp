@@ -21,6 +21,7 @@
 
 #include <cstdint>
 #include <cstdio>
+#include <memory>
 #include <stdexcept>
 #include <string>
 #include <utility>
@@ -57,6 +58,73 @@ inline void check(bsp_status s, const char* what) {
     throw std::runtime_error(std::string(what) + ": " + bsp_status_string(s) + ": " +
                              bsp_last_error_string());
 }
+
+// ---- device buffers (the reference's sparse_common::MakeBuffer) ------------
+// A device allocation of `size` bytes on one device, freed when the last
+// shared_ptr to it goes: the role of the tt-metal Buffer that the reference's
+// MakeBuffer returns (sparse_common/host_code_utils.cpp:5-18).  page_size is
+// kept for callers that read it back; device memory is not paged here.
+class Buffer {
+ public:
+  Buffer(IDevice* device, uint64_t size, uint64_t page_size) : dev_(device), size_(size), page_(page_size) {
+    check(bsp_buffer_alloc(dev_->handle(), static_cast<int64_t>(size), &ptr_), "MakeBuffer");
+  }
+  ~Buffer() { bsp_buffer_free(dev_->handle(), ptr_); }
+  Buffer(const Buffer&) = delete;
+  Buffer& operator=(const Buffer&) = delete;
+  void* address() const { return ptr_; }
+  uint64_t size() const { return size_; }
+  uint64_t page_size() const { return page_; }
+  IDevice* device() const { return dev_; }
+
+ private:
+  IDevice* dev_;
+  void* ptr_ = nullptr;
+  uint64_t size_, page_;
+};
+
+// Host <-> device copies of a whole buffer (the reference's EnqueueWriteBuffer
+// / EnqueueReadBuffer, load_balanced_new_DM.cpp:499-505).  Both complete before
+// they return, whatever `blocking` says.
+template <typename T>
+void EnqueueWriteBuffer(Buffer& buf, const std::vector<T>& src, bool /*blocking*/ = true) {
+  if (src.size() * sizeof(T) > buf.size()) throw std::runtime_error("bsp: EnqueueWriteBuffer: source larger than buffer");
+  check(bsp_buffer_write(buf.device()->handle(), buf.address(), src.data(),
+                         static_cast<int64_t>(src.size() * sizeof(T))),
+        "EnqueueWriteBuffer");
+}
+template <typename T>
+void EnqueueReadBuffer(Buffer& buf, std::vector<T>& dst, bool /*blocking*/ = true) {
+  dst.resize(buf.size() / sizeof(T));
+  check(bsp_buffer_read(buf.device()->handle(), dst.data(), buf.address(),
+                        static_cast<int64_t>(dst.size() * sizeof(T))),
+        "EnqueueReadBuffer");
+}
+
+// A BSR matrix resident on the device (bsp_bsr_upload / bsp_bsr_free): upload
+// once, then run any number of plans on desc().
+class DeviceBsr {
+ public:
+  DeviceBsr(IDevice* device, const bsr_matrix<bfloat16>& a, bool with_values = true) : dev_(device) {
+    std::vector<uint16_t> v;
+    if (with_values) {
+      v.resize(a.data.size());
+      for (size_t i = 0; i < v.size(); ++i) v[i] = a.data[i].to_uint16();
+    }
+    check(bsp_bsr_upload(dev_->handle(), static_cast<int64_t>(a.H), static_cast<int64_t>(a.W),
+                         static_cast<int32_t>(a.R), static_cast<int32_t>(a.C), static_cast<int64_t>(a.nblocks),
+                         a.indptr.data(), a.indices.data(), with_values ? v.data() : nullptr, &desc_),
+          "bsp_bsr_upload");
+  }
+  ~DeviceBsr() { bsp_bsr_free(dev_->handle(), &desc_); }
+  DeviceBsr(const DeviceBsr&) = delete;
+  DeviceBsr& operator=(const DeviceBsr&) = delete;
+  const bsp_bsr_desc& desc() const { return desc_; }
+
+ private:
+  IDevice* dev_;
+  bsp_bsr_desc desc_{};
+};
 
 namespace detail {
 
@@ -181,9 +249,31 @@ inline dense_matrix<bfloat16> attention_step(bsr_matrix<bfloat16>& mask, dense_m
 
 }  // namespace bsp
 
+namespace sparse_common {
+
+// sparse_common/host_code_utils.cpp:5-11: `size` bytes with pages of
+// `page_size` bytes.  `sram` asked tt-metal for core-local L1; a B200 has no
+// addressable equivalent for a buffer (its 126 MB L2 caches device memory by
+// itself), so the buffer is device memory either way.
+inline std::shared_ptr<bsp::Buffer> MakeBuffer(bsp::IDevice* device, uint32_t size, uint32_t page_size,
+                                               bool /*sram*/ = false) {
+  return std::make_shared<bsp::Buffer>(device, size, page_size);
+}
+
+// sparse_common/host_code_utils.cpp:13-18: n_tiles 32 x 32 tiles of
+// element_size-byte elements.
+inline std::shared_ptr<bsp::Buffer> MakeBuffer(bsp::IDevice* device, uint32_t n_tiles, size_t element_size,
+                                               bool sram = false) {
+  const uint32_t tile = static_cast<uint32_t>(element_size) * 32u * 32u;
+  return MakeBuffer(device, tile * n_tiles, sram ? tile * n_tiles : tile, sram);
+}
+
+}  // namespace sparse_common
+
 namespace bsr_host_code {
 
 using bsp::IDevice;
+using sparse_common::MakeBuffer;
 
 // Paper name "Naive" (block_spmm/inc/host_code.hpp:36-50).
 template <bool verbose = false, bool is_profiling = false, bool use_optimal_noc = true>

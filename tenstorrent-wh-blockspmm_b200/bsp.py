@@ -142,6 +142,12 @@ def lib():
         "bsp_testing_spmm_counters": (S, [P, ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(I64),
                                           ctypes.POINTER(I32)]),
         "bsp_testing_spmm_drop_stage": (S, [P, I32]),
+        "bsp_bsr_upload": (S, [P, I64, I64, I32, I32, I64, P, P, P, ctypes.POINTER(BsrDesc)]),
+        "bsp_bsr_free": (S, [P, ctypes.POINTER(BsrDesc)]),
+        "bsp_buffer_alloc": (S, [P, I64, ctypes.POINTER(ctypes.c_void_p)]),
+        "bsp_buffer_free": (S, [P, P]),
+        "bsp_buffer_write": (S, [P, P, P, I64]),
+        "bsp_buffer_read": (S, [P, P, P, I64]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)

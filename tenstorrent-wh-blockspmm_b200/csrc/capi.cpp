@@ -318,6 +318,113 @@ bsp_status bsp_device_synchronize(bsp_device* dev) {
   return BSP_OK;
 }
 
+// ------------------------------------------------ device storage ----
+namespace {
+struct OnDevice {  // make `ordinal` current for a call, put the caller's device back after
+  int prev = -1;
+  explicit OnDevice(int ordinal) {
+    if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+    if (prev != ordinal) cudaSetDevice(ordinal);
+  }
+  ~OnDevice() {
+    int cur = -1;
+    if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+  }
+};
+}  // namespace
+
+bsp_status bsp_buffer_alloc(bsp_device* dev, int64_t bytes, void** ptr) {
+  if (!dev || !ptr || bytes < 0) return set_error(BSP_ERR_INVALID_ARG, "bad arguments");
+  *ptr = nullptr;
+  OnDevice on(dev->ordinal);
+  if (cudaMalloc(ptr, static_cast<size_t>(std::max<int64_t>(bytes, 1))) != cudaSuccess) {
+    *ptr = nullptr;
+    return set_error(BSP_ERR_ALLOC, "cudaMalloc of " + std::to_string(bytes) + " bytes failed");
+  }
+  return BSP_OK;
+}
+
+bsp_status bsp_buffer_free(bsp_device* dev, void* ptr) {
+  if (!dev) return set_error(BSP_ERR_INVALID_ARG, "null device");
+  if (!ptr) return BSP_OK;
+  OnDevice on(dev->ordinal);
+  return cuda_check(cudaFree(ptr), "cudaFree");
+}
+
+bsp_status bsp_buffer_write(bsp_device* dev, void* dst, const void* src, int64_t bytes) {
+  if (!dev || (bytes > 0 && (!dst || !src)) || bytes < 0) return set_error(BSP_ERR_INVALID_ARG, "bad arguments");
+  if (bytes == 0) return BSP_OK;
+  OnDevice on(dev->ordinal);
+  return cuda_check(cudaMemcpy(dst, src, static_cast<size_t>(bytes), cudaMemcpyHostToDevice), "buffer write");
+}
+
+bsp_status bsp_buffer_read(bsp_device* dev, void* dst, const void* src, int64_t bytes) {
+  if (!dev || (bytes > 0 && (!dst || !src)) || bytes < 0) return set_error(BSP_ERR_INVALID_ARG, "bad arguments");
+  if (bytes == 0) return BSP_OK;
+  OnDevice on(dev->ordinal);
+  return cuda_check(cudaMemcpy(dst, src, static_cast<size_t>(bytes), cudaMemcpyDeviceToHost), "buffer read");
+}
+
+bsp_status bsp_bsr_upload(bsp_device* dev, int64_t rows, int64_t cols, int32_t R, int32_t C, int64_t nnzb,
+                          const int32_t* host_row_ptr, const int32_t* host_col_idx, const uint16_t* host_values,
+                          bsp_bsr_desc* out) {
+  if (!dev || !out || !host_row_ptr || (nnzb > 0 && !host_col_idx))
+    return set_error(BSP_ERR_INVALID_ARG, "null argument");
+  memset(out, 0, sizeof(*out));
+  if (R <= 0 || C <= 0 || rows <= 0 || cols <= 0 || nnzb < 0 || rows % R || cols % C)
+    return set_error(BSP_ERR_INVALID_ARG, "bad BSR shape (rows % R and cols % C must be 0)");
+  const int64_t nbr = rows / R, nbc = cols / C;
+  if (host_row_ptr[0] != 0 || host_row_ptr[nbr] != nnzb)
+    return set_error(BSP_ERR_INVALID_ARG, "row_ptr must start at 0 and end at nnzb");
+  for (int64_t i = 0; i < nbr; ++i)
+    if (host_row_ptr[i + 1] < host_row_ptr[i]) return set_error(BSP_ERR_INVALID_ARG, "row_ptr must not decrease");
+  for (int64_t b = 0; b < nnzb; ++b)
+    if (host_col_idx[b] < 0 || host_col_idx[b] >= nbc)
+      return set_error(BSP_ERR_INVALID_ARG, "column index out of range");
+  // one allocation: row_ptr at its start, col_idx, then the values at a
+  // 256-byte boundary (TMA wants 16, the kernels' boxes read 128-byte rows)
+  const size_t rp_bytes = sizeof(int32_t) * static_cast<size_t>(nbr + 1);
+  const size_t ci_off = align256(rp_bytes);
+  const size_t ci_bytes = sizeof(int32_t) * static_cast<size_t>(std::max<int64_t>(nnzb, 1));
+  const size_t v_off = ci_off + align256(ci_bytes);
+  const size_t v_bytes = host_values ? 2 * static_cast<size_t>(nnzb) * R * C : 0;
+  OnDevice on(dev->ordinal);
+  void* base = nullptr;
+  if (cudaMalloc(&base, v_off + std::max<size_t>(v_bytes, 16)) != cudaSuccess)
+    return set_error(BSP_ERR_ALLOC, "cudaMalloc of the BSR matrix failed");
+  uint8_t* b8 = static_cast<uint8_t*>(base);
+  bsp_status s = cuda_check(cudaMemcpy(b8, host_row_ptr, rp_bytes, cudaMemcpyHostToDevice), "upload row_ptr");
+  if (s == BSP_OK && nnzb > 0)
+    s = cuda_check(cudaMemcpy(b8 + ci_off, host_col_idx, sizeof(int32_t) * nnzb, cudaMemcpyHostToDevice),
+                   "upload col_idx");
+  if (s == BSP_OK && v_bytes > 0)
+    s = cuda_check(cudaMemcpy(b8 + v_off, host_values, v_bytes, cudaMemcpyHostToDevice), "upload values");
+  if (s != BSP_OK) {
+    cudaFree(base);
+    return s;
+  }
+  out->rows = rows;
+  out->cols = cols;
+  out->R = R;
+  out->C = C;
+  out->nnzb = nnzb;
+  out->row_ptr = reinterpret_cast<const int32_t*>(b8);
+  out->col_idx = reinterpret_cast<const int32_t*>(b8 + ci_off);
+  out->values = host_values ? b8 + v_off : nullptr;
+  return BSP_OK;
+}
+
+bsp_status bsp_bsr_free(bsp_device* dev, bsp_bsr_desc* desc) {
+  if (!dev || !desc) return set_error(BSP_ERR_INVALID_ARG, "null argument");
+  bsp_status s = BSP_OK;
+  if (desc->row_ptr) {
+    OnDevice on(dev->ordinal);
+    s = cuda_check(cudaFree(const_cast<int32_t*>(desc->row_ptr)), "cudaFree (BSR)");
+  }
+  memset(desc, 0, sizeof(*desc));
+  return s;
+}
+
 // ---------------------------------------------------------------- SpMM ----
 // Plan creation; `borrow` (host-buffer path only) keeps the tables in the
 // device's plan area, uploaded on `stream`.

@@ -25,7 +25,7 @@ import numpy as np
 import pytest
 
 import oracle
-from helpers import TOL, assert_bf16_close, normwise
+from helpers import TOL, assert_bf16_close
 
 pytestmark = pytest.mark.gpu
 
@@ -69,13 +69,17 @@ def _rows_oracle(ip, ix, vals, K, R, C, B, blocks, cols):
 
 
 def _product_check(Cd, ip, ix, vals, R, C, Bd, seed):
-    """||C v - A (B v)|| / ||A (B v)||, with B v and C v on the GPU in fp32 and
-    A (B v) on the host in fp64."""
+    """||C v - A (B v)|| / || |C| |v| || for a random sign vector v, with B v
+    and C v on the GPU in fp32 and A (B v) on the host in fp64.  The
+    denominator (row sums of |C|) has no cancellation, so the bound holds for
+    rows whose signed sum nearly cancels; rounding C to bf16 alone gives at
+    most 2^-9 here."""
     import torch
 
     N = Bd.shape[1]
     v = torch.from_numpy(np.random.default_rng(seed).choice([-1.0, 1.0], N).astype(np.float32)).cuda()
     cv = (Cd.float() @ v).double().cpu().numpy()
+    scale = Cd.float().abs().sum(1).double().cpu().numpy()
     w = (Bd.float() @ v).double().cpu().numpy()
     y = np.zeros(Cd.shape[0], np.float64)
     blocks = oracle.bf16_to_f32(vals).reshape(-1, R, C).astype(np.float64)
@@ -83,7 +87,8 @@ def _product_check(Cd, ip, ix, vals, R, C, Bd, seed):
     if ix.size:
         contrib = np.einsum("brc,bc->br", blocks, w.reshape(-1, C)[ix])
         np.add.at(y.reshape(-1, R), rows, contrib)
-    return normwise(cv, y)
+    den = np.linalg.norm(scale)
+    return 0.0 if den == 0 else float(np.linalg.norm(cv - y) / den)
 
 
 @pytest.mark.parametrize("tag", FROZEN_TAGS)

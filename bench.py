@@ -645,6 +645,72 @@ def strategy_for(op, name):
     return bsp.DDA
 
 
+SHARDED_WORKLOADS = ("sweep", "cfg1", "cfg3", "cfg4", "cfg5")
+
+
+def is_sharded(workload, ws):
+    """At N > 1 the BASELINE configs split ONE problem across the GPUs: SpMM
+    output row-panels / SDDMM mask row-panels balanced by nonzero blocks."""
+    return ws > 1 and workload in SHARDED_WORKLOADS
+
+
+def _panel_op(op, br0, br1):
+    """The host op restricted to block-rows [br0, br1) (for its byte count)."""
+    rp = np.asarray(op["rp"], dtype=np.int64)
+    d = dict(op)
+    d["rp"] = (rp[br0:br1 + 1] - rp[br0]).astype(np.int32)
+    d["ci"] = np.asarray(op["ci"])[rp[br0]:rp[br1]]
+    d["M"] = (br1 - br0) * op["R"]
+    return d
+
+
+class ShardOp:
+    """One op of the workload split over the ranks (this rank's panel)."""
+
+    def __init__(self, op, dev, strategy, rank, ws, local):
+        import torch
+
+        import bsp
+        import bsp_dist
+
+        self.op, self.kind = op, op["kind"]
+        if self.kind == "spmm":
+            self.sh = bsp_dist.ShardedSpmm(dev, op["M"], op["K"], op["R"], op["C"], op["rp"], op["ci"], op["vals"],
+                                           op["N"], rank, ws, strategy, fused=True)
+            self.B = bsp.to_device_bf16(op["B"], local)
+            self.out = torch.empty((op["M"], op["N"]), dtype=torch.bfloat16, device="cuda")
+            self.sh.attach(self.out)   # collective: map the peers' copies of this C
+            br0, br1 = int(self.sh.bounds[rank]), int(self.sh.bounds[rank + 1])
+            self.kernel = "spmm_rowstack_tcgen05 / spmm_pair_tcgen05 (row panel)"
+        else:
+            self.sh = bsp_dist.ShardedSddmm(dev, op["M"], op["N"], op["K"], op["R"], op["C"], op["rp"], op["ci"],
+                                            op["mvals"], rank, ws, strategy)
+            self.A = bsp.to_device_bf16(op["A"], local)
+            self.B = bsp.to_device_bf16(op["B"], local)
+            self.out = torch.empty(max(int(op["rp"][-1]) * op["R"] * op["C"], 8), dtype=torch.bfloat16,
+                                   device="cuda")
+            br0, br1 = self.sh.br0, self.sh.br1
+            self.kernel = "sddmm_rowstack_tcgen05 (mask row panel)"
+        self.panel = _panel_op(op, br0, br1)
+        self.flops = self.sh.flops
+        self.bytes = op_bytes(self.panel) if br1 > br0 else 0
+
+    def compute(self, stream):
+        if self.kind == "spmm":
+            self.sh.compute(self.B, self.out, stream)
+        else:
+            self.sh.compute(self.A, self.B, self.out, stream)
+
+    def replicated(self, stream):
+        if self.kind == "spmm":
+            self.sh.run(self.B, self.out, stream, replicate=True, sync_before=False)
+        else:
+            self.sh.run(self.A, self.B, self.out, stream, replicate=True)
+
+    def close(self):
+        self.sh.close()
+
+
 def run_bsp(args):
     import torch
 
@@ -656,50 +722,39 @@ def run_bsp(args):
     dev = bsp.device(local)
     stream = torch.cuda.current_stream()
     flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device="cuda")
-    sharded = args.workload == "cfg5"
-    ops = workload_ops(args.workload, rank)
+    sharded = is_sharded(args.workload, ws)
+    ops = workload_ops(args.workload, 0 if sharded else rank)   # one problem when sharded
 
-    shard = None
-    if sharded:
-        import bsp_dist
-
-        op = ops[0]
-        shard = bsp_dist.ShardedSpmm(dev, op["M"], op["K"], op["R"], op["C"], op["rp"], op["ci"],
-                                     op["vals"], op["N"], rank, ws, strategy_for(op, args.strategy),
-                                     fused=not args.nccl_exchange if ws > 1 else None)
-        Bd = bsp.to_device_bf16(op["B"], local)
-        Cfull = torch.empty((op["M"], op["N"]), dtype=torch.bfloat16, device="cuda")
-        shard.attach(Cfull)
-        kname = ("spmm_rowstack_tcgen05 (epilogue stores each C tile into every GPU's C over NVLink)"
-                 if shard.fused else "spmm_rowstack_tcgen05 + NCCL send/recv of C row-panels")
-        runs = [dict(op=op, flops=shard.flops, bytes=op_bytes(op), times=[], name=op["name"],
-                     fn=lambda s: shard.run(Bd, Cfull, s, replicate=ws > 1, sync_before=False),
-                     kernel=kname)]
-    else:
-        runs = []
-        for op in ops:
+    runs = []
+    for op in ops:
+        if sharded:
+            so = ShardOp(op, dev, strategy_for(op, args.strategy), rank, ws, local)
+            runs.append(dict(op=op, dev=so, flops=so.flops, bytes=so.bytes, times=[], rtimes=[],
+                             name=op["name"], fn=so.compute, rfn=so.replicated, kernel=so.kernel))
+        else:
             d = DevOp(op, dev, strategy_for(op, args.strategy), local)
-            runs.append(dict(op=op, dev=d, flops=op_flops(op), bytes=op_bytes(op), times=[],
-                             name=op["name"], fn=d.run, kernel=d.kernel(), plan=d.plan.info()))
+            runs.append(dict(op=op, dev=d, flops=op_flops(op), bytes=op_bytes(op), times=[], name=op["name"],
+                             fn=d.run, kernel=d.kernel(), plan=d.plan.info()))
 
-    sync = torch.zeros(1, dtype=torch.float32, device="cuda") if (sharded and dist is not None) else None
+    sync = torch.zeros(1, dtype=torch.float32, device="cuda") if dist is not None else None
 
-    def step(record):
+    def step(record, key="times", fn="fn"):
         for r in runs:
             flush.zero_()
-            if sync is not None:
+            if sync is not None and sharded:
                 # line the ranks' streams up (outside the timed events): every
-                # rank's step then starts together and no rank's time includes
-                # waiting for a peer that is still flushing
+                # rank's op then starts together, no rank's time includes
+                # waiting for a peer that is still flushing, and no rank
+                # stores into a peer's C that the peer still reads
                 dist.all_reduce(sync)
             if record:
                 e0 = torch.cuda.Event(enable_timing=True)
                 e1 = torch.cuda.Event(enable_timing=True)
                 e0.record(stream)
-            r["fn"](stream)
+            r[fn](stream)
             if record:
                 e1.record(stream)
-                r["times"].append((e0, e1))
+                r[key].append((e0, e1))
 
     for _ in range(args.warmup):
         step(False)
@@ -735,6 +790,24 @@ def run_bsp(args):
     f_all = reduce_over_ranks(total_f, dist, "sum")
     value = f_all / t_all / 1e12
 
+    replicated = None
+    if sharded:
+        # the same step with C replicated on every GPU: the SpMM epilogue
+        # stores each C tile into every peer's C over NVLink (one small NCCL
+        # all-reduce after the kernel marks completion); SDDMM panels travel
+        # by NCCL send/receive
+        for _ in range(max(1, args.warmup // 2)):
+            step(False, fn="rfn")
+        barrier(dist)
+        for _ in range(args.steps):
+            step(True, key="rtimes", fn="rfn")
+        barrier(dist)
+        rt = sum(a.elapsed_time(b) * 1e-3 for r in runs for a, b in r["rtimes"])
+        rt = reduce_over_ranks(rt, dist, "max")
+        replicated = {"value": f_all / rt / 1e12, "unit": "TFLOP/s", "ms_per_step": rt / args.steps * 1e3,
+                      "exchange": "SpMM: C tiles stored into every peer's C by the kernel's epilogue over NVLink "
+                                  "(CUDA IPC), one NCCL all-reduce per op; SDDMM: NCCL send/recv of block ranges"}
+
     # dominant launch = the op with the largest share of device time
     di = int(np.argmax([d["ms"] for d in per]))
     dom, dom_run = per[di], runs[di]
@@ -744,12 +817,12 @@ def run_bsp(args):
     else:
         roof = {"bound": "hbm", "achieved": dom["gbs"], "peak": peaks["hbm_gbs"],
                 "unit": "GB/s", "frac": dom["gbs"] / peaks["hbm_gbs"]}
-    roof["traffic"] = traffic_for(args.workload, dom["name"])
+    roof["traffic"] = traffic_for(args.workload, dom["name"]) if not sharded else None
     roof["peak_src"] = peaks["src"]
     roof["kernel"] = f"{dom_run['kernel']} ({dom['name']})"
     roof["algorithmic"] = dom_run["bytes"] if dom["bound"] == "hbm" else dom_run["flops"]
 
-    e2e = run_e2e(args, runs, dev, dist, shard)
+    e2e = run_e2e(args, runs, dev, dist, sharded, rank, ws)
 
     cpu = None
     if ws == 1 and not args.no_cpu:
@@ -771,13 +844,12 @@ def run_bsp(args):
         "roofline": roof, "cpu_baseline": cpu, "e2e": e2e,
         "gpu_launches": args.steps * len(runs), "clocks": clocks, "per_op": per,
     }
+    if replicated is not None:
+        out["replicated"] = replicated
     if rank == 0:
         print(json.dumps(out), flush=True)
     for r in runs:
-        if "dev" in r:
-            r["dev"].close()
-    if shard is not None:
-        shard.close()
+        r["dev"].close()
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
@@ -786,12 +858,12 @@ def run_bsp(args):
 def bench_config(args, ws):
     """The workload description both arms print (the same dict, so that the
     two lines name the same workload)."""
-    sharded = args.workload == "cfg5"
     return {"workload": WORKLOAD_DESC[args.workload], "name": args.workload,
             "strategy": args.strategy, "c_dtype": "bf16", "accumulate": "fp32",
             "l2": "flushed (256 MiB write) before every timed launch",
-            "per_rank": ("row panels of one problem, balanced by nonzero blocks" if sharded
-                         else "independent copy per rank") if ws > 1 else None}
+            "per_rank": ("row panels of one problem, balanced by nonzero blocks; C left row-sharded "
+                         "(the replicated-C step is reported under 'replicated')"
+                         if is_sharded(args.workload, ws) else "independent copy per rank") if ws > 1 else None}
 
 
 def _pinned(a):
@@ -800,81 +872,78 @@ def _pinned(a):
     return torch.from_numpy(np.ascontiguousarray(a)).pin_memory().numpy()
 
 
-def run_e2e(args, runs, dev, dist, shard):
-    """The same metric end to end through the public API with host buffers:
-    every step copies the inputs from pinned host memory and reads the result
-    back (bsp_spmm_host / bsp_sddmm_host; cfg5: the B and A-panel copies, the
-    sharded SpMM with its NCCL exchange, and the full C back to the host)."""
+def run_e2e(args, runs, dev, dist, sharded, rank, ws):
+    """The same metric end to end through the public C ABI with host buffers:
+    every step copies the inputs in from pinned host memory and the results
+    back.  SpMM ops go through one bsp_spmm_host_batch call per step (the
+    jobs' copies in, kernels and copies out pipelined over the copy engines in
+    both directions); SDDMM / attention / SpGEMM ops through their host-buffer
+    calls.  Sharded (N > 1): each rank's jobs are its row panels (A panel and
+    the whole B in, its C panel out)."""
     import torch
 
     import bsp
 
     steps = max(1, min(args.steps, args.e2e_steps))
     h2d = d2h = 0
-    if shard is not None:
-        op = runs[0]["op"]
-        hB = torch.from_numpy(np.ascontiguousarray(op["B"]).view(np.int16)).pin_memory()
-        hv = None
-        if shard.A is not None:
-            hv = torch.from_numpy(np.ascontiguousarray(shard.panel.values).view(np.int16)).pin_memory()
-        hout = torch.empty((op["M"], op["N"]), dtype=torch.int16).pin_memory()
-        Bd = torch.empty((op["K"], op["N"]), dtype=torch.bfloat16, device="cuda")
-        Cfull = torch.empty((op["M"], op["N"]), dtype=torch.bfloat16, device="cuda")
-        shard.attach(Cfull)   # collective: map the peers' copies of this C
-        h2d = hB.numel() * 2 + (hv.numel() * 2 if hv is not None else 0)
-        d2h = hout.numel() * 2
-
-        def one():
-            Bd.view(torch.int16).copy_(hB, non_blocking=True)
-            if hv is not None:
-                shard.A.values.view(torch.int16).copy_(hv, non_blocking=True)
-            shard.run(Bd, Cfull, None, replicate=dist is not None)
-            hout.copy_(Cfull.view(torch.int16), non_blocking=True)
-            torch.cuda.synchronize()
-    else:
-        host = []
-        for r in runs:
-            op = r["op"]
-            if op["kind"] == "attn":
-                hc = dict(rp=_pinned(op["rp"]), ci=_pinned(op["ci"]), Q=_pinned(op["Q"]), K=_pinned(op["K"]),
-                          V=_pinned(op["V"]))
-                h2d += sum(hc[k].nbytes for k in hc)
-                d2h += 2 * op["S"] * op["d"]
-            elif op["kind"] == "spgemm":
-                hc = dict(rp=_pinned(op["rp"]), ci=_pinned(op["ci"]), v=_pinned(op["vals"]),
-                          brp=_pinned(op["brp"]), bci=_pinned(op["bci"]), bv=_pinned(op["bvals"]))
-                h2d += sum(hc[k].nbytes for k in hc)
-                d2h += 4 * (op["M"] // op["Ra"] + 1) + op["out_nnzb"] * (4 + 2 * op["Ra"] * op["Cb"])
-            elif op["kind"] == "spmm":
-                hc = dict(rp=_pinned(op["rp"]), ci=_pinned(op["ci"]), v=_pinned(op["vals"]),
-                          B=_pinned(op["B"]),
-                          out=torch.empty((op["M"], op["N"]), dtype=torch.int16).pin_memory()
-                          .numpy().view(np.uint16))
-                h2d += hc["rp"].nbytes + hc["ci"].nbytes + hc["v"].nbytes + hc["B"].nbytes
+    batch, others = [], []
+    for r in runs:
+        op = r["op"]
+        src = r["dev"].panel if sharded else op
+        if op["kind"] == "spmm":
+            rp, ci = _pinned(src["rp"]), _pinned(src["ci"])
+            b0 = int(np.asarray(op["rp"])[int(r["dev"].sh.bounds[rank])]) if sharded else 0
+            R, C = op["R"], op["C"]
+            vals = _pinned(np.asarray(op["vals"]).reshape(-1)[b0 * R * C:(b0 + int(rp[-1])) * R * C])
+            job = dict(M=src["M"], K=op["K"], R=R, C=C, row_ptr=rp, col_idx=ci, values=vals, B=_pinned(op["B"]),
+                       N=op["N"], out=torch.empty((src["M"], op["N"]), dtype=torch.int16).pin_memory()
+                       .numpy().view(np.uint16))
+            h2d += rp.nbytes + ci.nbytes + vals.nbytes + job["B"].nbytes
+            d2h += job["out"].nbytes
+            if src["M"] > 0:
+                batch.append(job)
+        elif op["kind"] == "sddmm":
+            if sharded:
+                sh = r["dev"].sh
+                R = op["R"]
+                A = _pinned(np.asarray(op["A"])[sh.br0 * R:sh.br1 * R])
+                mv = None
             else:
-                nv = int(op["rp"][-1]) * op["R"] * op["C"]
-                hc = dict(rp=_pinned(op["rp"]), ci=_pinned(op["ci"]), A=_pinned(op["A"]), B=_pinned(op["B"]),
-                          out=torch.empty(max(nv, 1), dtype=torch.int16).pin_memory()
-                          .numpy().view(np.uint16)[:nv])
-                h2d += hc["rp"].nbytes + hc["ci"].nbytes + hc["A"].nbytes + hc["B"].nbytes
-            if "out" in hc:
-                d2h += hc["out"].nbytes
-            host.append((op, hc, strategy_for(op, args.strategy)))
+                A, mv = _pinned(op["A"]), None
+            rp, ci = _pinned(src["rp"]), _pinned(src["ci"])
+            nv = int(rp[-1]) * op["R"] * op["C"]
+            hc = dict(rp=rp, ci=ci, A=A, B=_pinned(op["B"]), M=src["M"],
+                      out=torch.empty(max(nv, 1), dtype=torch.int16).pin_memory().numpy().view(np.uint16)[:nv])
+            h2d += rp.nbytes + ci.nbytes + A.nbytes + hc["B"].nbytes
+            d2h += hc["out"].nbytes
+            if nv > 0:
+                others.append((op, hc, mv))
+        elif op["kind"] == "attn":
+            hc = dict(rp=_pinned(op["rp"]), ci=_pinned(op["ci"]), Q=_pinned(op["Q"]), K=_pinned(op["K"]),
+                      V=_pinned(op["V"]))
+            h2d += sum(hc[k].nbytes for k in hc)
+            d2h += 2 * op["S"] * op["d"]
+            others.append((op, hc, None))
+        else:
+            hc = dict(rp=_pinned(op["rp"]), ci=_pinned(op["ci"]), v=_pinned(op["vals"]),
+                      brp=_pinned(op["brp"]), bci=_pinned(op["bci"]), bv=_pinned(op["bvals"]))
+            h2d += sum(hc[k].nbytes for k in hc)
+            d2h += 4 * (op["M"] // op["Ra"] + 1) + op["out_nnzb"] * (4 + 2 * op["Ra"] * op["Cb"])
+            others.append((op, hc, None))
+    strat = bsp.STRATEGIES[args.strategy] if args.strategy != "auto" else bsp.DDA
 
-        def one():
-            for op, hc, strat in host:
-                if op["kind"] == "attn":
-                    bsp.attn_host(op["S"], op["d"], hc["rp"], hc["ci"], hc["Q"], hc["K"], hc["V"], op["scale"],
-                                  dev=dev)
-                elif op["kind"] == "spgemm":
-                    bsp.spgemm_host(op["M"], op["K"], op["N"], op["Ra"], op["Ca"], op["Cb"], hc["rp"],
-                                    hc["ci"], hc["v"], hc["brp"], hc["bci"], hc["bv"], dev=dev)
-                elif op["kind"] == "spmm":
-                    bsp.spmm_host(op["M"], op["K"], op["R"], op["C"], hc["rp"], hc["ci"], hc["v"], hc["B"],
-                                  op["N"], strategy=strat, dev=dev, out=hc["out"])
-                else:
-                    bsp.sddmm_host(op["M"], op["N"], op["R"], op["C"], hc["rp"], hc["ci"], None, hc["A"],
-                                   hc["B"], op["K"], strategy=strat, dev=dev, out=hc["out"])
+    def one():
+        if batch:
+            bsp.spmm_host_batch(batch, strategy=strat, dev=dev)
+        for op, hc, mv in others:
+            if op["kind"] == "attn":
+                bsp.attn_host(op["S"], op["d"], hc["rp"], hc["ci"], hc["Q"], hc["K"], hc["V"], op["scale"], dev=dev)
+            elif op["kind"] == "spgemm":
+                bsp.spgemm_host(op["M"], op["K"], op["N"], op["Ra"], op["Ca"], op["Cb"], hc["rp"], hc["ci"],
+                                hc["v"], hc["brp"], hc["bci"], hc["bv"], dev=dev)
+            else:
+                bsp.sddmm_host(hc["M"], op["N"], op["R"], op["C"], hc["rp"], hc["ci"], mv, hc["A"], hc["B"],
+                               op["K"], strategy=strat, dev=dev, out=hc["out"])
 
     one()  # warm (workspace growth, first touch of pinned pages)
     barrier(dist)
@@ -885,10 +954,10 @@ def run_e2e(args, runs, dev, dist, shard):
     f = reduce_over_ranks(sum(r["flops"] for r in runs) * steps, dist, "sum")
     return {"value": f / t / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": int(h2d),
             "d2h_bytes_per_step": int(d2h), "steps": steps,
-            "path": ("bsp_dist.ShardedSpmm (host B and A values in, NCCL exchange, full C out)"
-                     if shard is not None else
-                     "bsp_spmm_host / bsp_sddmm_host / bsp_attn_host / bsp_spgemm_host (C ABI, host buffers; SpGEMM "
-                     "plans C's pattern on the host every call, as bsr_matrix::spgemm does)")}
+            "path": ("bsp_spmm_host_batch (C ABI, host buffers: every SpMM of the step in one pipelined call)"
+                     " / bsp_sddmm_host / bsp_attn_host / bsp_spgemm_host"
+                     + ("; per rank: its row panels (A panel and all of B in, its C panel out)" if sharded
+                        else ""))}
 
 
 def traffic_for(workload, name):

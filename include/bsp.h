@@ -225,6 +225,31 @@ bsp_status bsp_spmm_host_profile(bsp_device* dev, int64_t M, int64_t K, int32_t 
                                  uint16_t* C_out, bsp_strategy strategy, const bsp_spmm_opts* opts,
                                  int32_t iters, double* ms_per_launch);
 
+/* Several independent host-buffer SpMMs in one call (each job as
+ * bsp_spmm_host: host arrays in, the whole of C_out written, bf16).  The
+ * reference runs one product per host-code call and blocks on each
+ * (block_spmm/inc/host_code/bsr_spmm_multicore_load_balanced_new_DM.cpp:
+ * 499-535); here every job's inputs are queued on a copy stream first, the
+ * plans are built on the host while they travel, and each job's kernel runs as
+ * soon as its inputs have landed, so job k's C travels to the host while the
+ * inputs of jobs k+1... still come in (PCIe copies in both directions at
+ * once).  Device buffers for all jobs come from the device's grow-only
+ * workspace.  Returns after every C_out is written. */
+typedef struct bsp_spmm_host_job {
+  int64_t M, K;          /* A is M x K with R x C blocks */
+  int32_t R, C;
+  int64_t nnzb;
+  const int32_t* row_ptr;  /* host, M/R + 1 */
+  const int32_t* col_idx;  /* host, nnzb */
+  const uint16_t* values;  /* host, nnzb * R * C bf16 */
+  const uint16_t* B;       /* host, K x N bf16, row-major */
+  int64_t N;
+  uint16_t* C_out;         /* host, M x N bf16, row-major */
+} bsp_spmm_host_job;
+
+bsp_status bsp_spmm_host_batch(bsp_device* dev, int32_t n_jobs, const bsp_spmm_host_job* jobs,
+                               bsp_strategy strategy, const bsp_spmm_opts* opts);
+
 /* SpMM that allocates no device memory.  No counterpart in the reference.
  *
  * For callers that cannot call cudaMalloc: code whose device memory is owned

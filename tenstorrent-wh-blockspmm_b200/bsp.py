@@ -55,6 +55,15 @@ class BsrDesc(ctypes.Structure):
     ]
 
 
+class SpmmHostJob(ctypes.Structure):
+    """bsp_spmm_host_job: one product of bsp_spmm_host_batch (host arrays)."""
+    _fields_ = [
+        ("M", ctypes.c_int64), ("K", ctypes.c_int64), ("R", ctypes.c_int32), ("C", ctypes.c_int32),
+        ("nnzb", ctypes.c_int64), ("row_ptr", ctypes.c_void_p), ("col_idx", ctypes.c_void_p),
+        ("values", ctypes.c_void_p), ("B", ctypes.c_void_p), ("N", ctypes.c_int64), ("C_out", ctypes.c_void_p),
+    ]
+
+
 class Opts(ctypes.Structure):
     _fields_ = [
         ("no_load_balance", ctypes.c_int32), ("group_rows", ctypes.c_int32),
@@ -142,6 +151,7 @@ def lib():
         "bsp_testing_spmm_counters": (S, [P, ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(I64),
                                           ctypes.POINTER(I32)]),
         "bsp_testing_spmm_drop_stage": (S, [P, I32]),
+        "bsp_spmm_host_batch": (S, [P, I32, ctypes.POINTER(SpmmHostJob), S, ctypes.POINTER(Opts)]),
         "bsp_bsr_upload": (S, [P, I64, I64, I32, I32, I64, P, P, P, ctypes.POINTER(BsrDesc)]),
         "bsp_bsr_free": (S, [P, ctypes.POINTER(BsrDesc)]),
         "bsp_buffer_alloc": (S, [P, I64, ctypes.POINTER(ctypes.c_void_p)]),
@@ -353,6 +363,30 @@ def spmm_host(M, K, R, C, row_ptr, col_idx, values, B, N, strategy=NAIVE, opts=N
     _check(lib().bsp_spmm_host(dev.handle, M, K, R, C, int(rp[-1]), _ptr(rp), _ptr(ci), _ptr(v),
                                _ptr(b), N, _ptr(o), strategy, ctypes.byref(opt)))
     return o
+
+
+def spmm_host_batch(jobs, strategy=NAIVE, opts=None, dev: Device = None):
+    """Several host-buffer SpMMs in one pipelined call (bsp_spmm_host_batch).
+    jobs: sequence of dicts with M, K, R, C, row_ptr, col_idx, values, B, N and
+    optionally out (a uint16 M x N array to write); returns the outputs."""
+    dev = dev or device(0)
+    keep, arr = [], (SpmmHostJob * max(len(jobs), 1))()
+    outs = []
+    for k, j in enumerate(jobs):
+        rp = np.ascontiguousarray(j["row_ptr"], dtype=np.int32)
+        ci = np.ascontiguousarray(j["col_idx"], dtype=np.int32)
+        v = np.ascontiguousarray(j["values"], dtype=np.uint16)
+        b = np.ascontiguousarray(j["B"], dtype=np.uint16)
+        o = j.get("out")
+        if o is None:
+            o = np.empty((j["M"], j["N"]), dtype=np.uint16)
+        keep += [rp, ci, v, b, o]
+        outs.append(o)
+        arr[k] = SpmmHostJob(j["M"], j["K"], j["R"], j["C"], int(rp[-1]), _ptr(rp), _ptr(ci), _ptr(v), _ptr(b),
+                             j["N"], _ptr(o))
+    opt = opts if opts is not None else Opts()
+    _check(lib().bsp_spmm_host_batch(dev.handle, len(jobs), arr, strategy, ctypes.byref(opt)))
+    return outs
 
 
 # ------------------------------------------------------------------- SDDMM --

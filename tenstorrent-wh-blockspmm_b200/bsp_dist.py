@@ -228,18 +228,29 @@ class ShardedSpmm:
             self.compute(B, C_full, stream)
             return
         if self.fused:
+            import torch
             import torch.distributed as dist
 
             if self.peer is None or self.peer[2] != C_full.data_ptr():
                 raise RuntimeError("ShardedSpmm: attach(C_full) first (fused replication)")
+            cur = torch.cuda.current_stream()
+            if stream is not None and not isinstance(stream, torch.cuda.Stream):
+                raise ValueError("ShardedSpmm.run (fused): pass a torch.cuda.Stream or None")
+            s = cur if stream is None else stream
+            # the collectives run on the current stream: order the kernels
+            # after the first one and the second one after the kernels
             if sync_before:
                 dist.all_reduce(self._sync, group=self.group)
+            if s != cur:
+                s.wait_stream(cur)
             row_bytes = self.peer[3]
             for part in self.parts:
                 if part is not None:
                     r0, view, plan = part
                     plan.execute_replicated(view, B, C_full[r0:r0 + view.rows],
-                                            [p + r0 * row_bytes for p in self.peer[1]], stream)
+                                            [p + r0 * row_bytes for p in self.peer[1]], s)
+            if s != cur:
+                cur.wait_stream(s)
             dist.all_reduce(self._sync, group=self.group)   # every rank's stores have landed
             return
         reqs = []
@@ -260,3 +271,60 @@ class ShardedSpmm:
             if part is not None:
                 part[2].close()
         self.parts = []
+
+
+class ShardedSddmm:
+    """out = mask (.) (A @ B) with the mask's block-rows sharded over the ranks.
+
+    The mask row-panels are split like the SpMM's (contiguous block-row ranges
+    of equal nonzero-block count).  Rank r holds the whole B (K x N) and uses
+    the rows of A of its panel; its output blocks are a contiguous range of the
+    output (blocks are stored block-row by block-row), so ``compute`` writes
+    straight into that range of a full-size output buffer.  ``run`` with
+    ``replicate`` then exchanges the ranges by NCCL send/receive, so every rank
+    ends with the whole output.
+    """
+
+    def __init__(self, dev: "bsp.Device", M: int, N: int, K: int, R: int, C: int, row_ptr, col_idx,
+                 mask_values, rank: int, world_size: int, strategy=bsp.DDA, opts=None, group=None):
+        self.M, self.N, self.K, self.R, self.C = M, N, K, R, C
+        self.rank, self.world_size, self.group = rank, world_size, group
+        rp = np.asarray(row_ptr, dtype=np.int64)
+        self.bounds = shard_bounds(row_ptr, world_size)
+        self.block_bounds = [int(rp[int(b)]) for b in self.bounds]
+        br0, br1 = int(self.bounds[rank]), int(self.bounds[rank + 1])
+        self.br0, self.br1 = br0, br1
+        self.panel = row_panel(row_ptr, col_idx, mask_values, R, C, br0, br1)
+        self.nnzb = int(self.panel.row_ptr[-1])
+        self.mask = self.plan = None
+        if self.nnzb > 0:
+            self.mask = bsp.DeviceBSR.from_host((br1 - br0) * R, N, R, C, self.panel.row_ptr, self.panel.col_idx,
+                                                self.panel.values, dev.ordinal)
+            self.plan = bsp.SddmmPlan(dev, self.mask, K, strategy, opts)
+
+    @property
+    def flops(self) -> float:
+        """Effective FLOPs of this rank's panel (the reference's SDDMM count)."""
+        return 2.0 * self.nnzb * self.R * self.C * self.K + self.nnzb * self.R * self.C
+
+    def compute(self, A_full, B, out_full, stream=None) -> None:
+        """This rank's output blocks: out_full[blocks of the panel]."""
+        if self.plan is None:
+            return
+        R, C = self.R, self.C
+        b0, b1 = self.block_bounds[self.rank], self.block_bounds[self.rank + 1]
+        self.plan.execute(self.mask, A_full[self.br0 * R:self.br1 * R], B, out_full[b0 * R * C:b1 * R * C], stream)
+
+    def run(self, A_full, B, out_full, stream=None, replicate=True) -> None:
+        self.compute(A_full, B, out_full, stream)
+        if not replicate or self.world_size == 1:
+            return
+        blocks = out_full[:self.block_bounds[-1] * self.R * self.C].view(-1, self.R * self.C)
+        ranges = [(self.block_bounds[r], self.block_bounds[r + 1]) for r in range(self.world_size)]
+        for req in start_exchange(blocks, ranges, self.rank, self.world_size, self.group):
+            req.wait()
+
+    def close(self):
+        if self.plan is not None:
+            self.plan.close()
+            self.plan = None

@@ -441,6 +441,36 @@ bsp_status bsp_spmm_plan_create(bsp_device* dev, const bsp_bsr_desc* A, const in
                                out);
 }
 
+// The device tables of a planned SpMM, in upload order: units, CTA offsets,
+// steps, stage list, CTA stage offsets, and two zeroed sets of split-K
+// counters (used by alternate launches; each launch zeroes the other set).
+static std::vector<std::pair<const void*, size_t>> spmm_table_parts(const bsp_spmm_plan& p,
+                                                                    std::vector<int32_t>* zeros) {
+  zeros->assign(2 * static_cast<size_t>(p.n_split_slots), 0);
+  return {{p.h_units.data(), p.h_units.size() * sizeof(SpmmUnit)},
+          {p.h_cta_begin.data(), p.h_cta_begin.size() * sizeof(int32_t)},
+          {p.h_steps.data(), p.h_steps.size() * sizeof(int32_t)},
+          {p.h_stage_list.data(), p.h_stage_list.size() * sizeof(int32_t)},
+          {p.h_cta_stage_begin.data(), p.h_cta_stage_begin.size() * sizeof(int32_t)},
+          {zeros->data(), zeros->size() * sizeof(int32_t)}};
+}
+
+static void spmm_bind_tables(bsp_spmm_plan* p, const std::vector<void*>& ptrs) {
+  p->d_units = static_cast<SpmmUnit*>(ptrs[0]);
+  p->d_cta_begin = static_cast<int32_t*>(ptrs[1]);
+  p->d_steps = static_cast<int32_t*>(ptrs[2]);
+  p->d_stage_list = static_cast<int4*>(ptrs[3]);
+  p->d_cta_stage_begin = static_cast<int32_t*>(ptrs[4]);
+  p->d_split_counters = static_cast<int32_t*>(ptrs[5]);
+}
+
+// Bytes of the split-K partial tiles: 128 rows x the tile's accumulator
+// columns, fp32, per workspace slot.
+static size_t spmm_split_ws_bytes(const bsp_spmm_plan& p) {
+  const int64_t acc_cols = p.variant == 2 ? 256 : 128 * p.NT;
+  return sizeof(float) * 128 * static_cast<size_t>(acc_cols) * static_cast<size_t>(p.n_split_slots);
+}
+
 static bsp_status spmm_plan_create_impl(bsp_device* dev, const bsp_bsr_desc* A, const int32_t* host_row_ptr,
                                         const int32_t* host_col_idx, int64_t N, bsp_dtype c_type,
                                         bsp_strategy strategy, const bsp_spmm_opts* opts, bool borrow,
@@ -472,15 +502,8 @@ static bsp_status spmm_plan_create_impl(bsp_device* dev, const bsp_bsr_desc* A, 
     return s;
   }
   std::vector<void*> ptrs;
-  // split-K counters: two sets, used by alternate launches (each launch zeroes the other)
-  const std::vector<int32_t> zeros(2 * static_cast<size_t>(p->n_split_slots), 0);
-  const std::vector<std::pair<const void*, size_t>> parts = {
-      {p->h_units.data(), p->h_units.size() * sizeof(SpmmUnit)},
-      {p->h_cta_begin.data(), p->h_cta_begin.size() * sizeof(int32_t)},
-      {p->h_steps.data(), p->h_steps.size() * sizeof(int32_t)},
-      {p->h_stage_list.data(), p->h_stage_list.size() * sizeof(int32_t)},
-      {p->h_cta_stage_begin.data(), p->h_cta_stage_begin.size() * sizeof(int32_t)},
-      {zeros.data(), zeros.size() * sizeof(int32_t)}};
+  std::vector<int32_t> zeros;
+  const auto parts = spmm_table_parts(*p, &zeros);
   s = borrow ? upload_blob_borrowed(dev, parts, stream, &p->d_blob, &p->blob_bytes, &ptrs)
              : upload_blob(parts, &p->d_blob, &p->blob_bytes, &ptrs);
   p->blob_borrowed = borrow;
@@ -488,16 +511,9 @@ static bsp_status spmm_plan_create_impl(bsp_device* dev, const bsp_bsr_desc* A, 
     delete p;
     return s;
   }
-  p->d_units = static_cast<SpmmUnit*>(ptrs[0]);
-  p->d_cta_begin = static_cast<int32_t*>(ptrs[1]);
-  p->d_steps = static_cast<int32_t*>(ptrs[2]);
-  p->d_stage_list = static_cast<int4*>(ptrs[3]);
-  p->d_cta_stage_begin = static_cast<int32_t*>(ptrs[4]);
-  p->d_split_counters = static_cast<int32_t*>(ptrs[5]);
+  spmm_bind_tables(p, ptrs);
   if (p->n_split_slots > 0) {
-    // partial tiles of split units: 128 rows x the tile's accumulator columns
-    const int64_t acc_cols = p->variant == 2 ? 256 : 128 * p->NT;
-    const size_t wb = sizeof(float) * 128 * static_cast<size_t>(acc_cols) * static_cast<size_t>(p->n_split_slots);
+    const size_t wb = spmm_split_ws_bytes(*p);
     if (borrow) {
       if (dev->aux_ws_bytes < wb) {
         if (dev->aux_ws) cudaFree(dev->aux_ws);
@@ -767,6 +783,155 @@ bsp_status bsp_spmm_host(bsp_device* dev, int64_t M, int64_t K, int32_t R, int32
                          const bsp_spmm_opts* opts) {
   return spmm_host_impl(dev, M, K, R, C, nnzb, row_ptr, col_idx, values, B, N, C_out, strategy,
                         opts, 0, nullptr);
+}
+
+bsp_status bsp_spmm_host_batch(bsp_device* dev, int32_t n_jobs, const bsp_spmm_host_job* jobs,
+                               bsp_strategy strategy, const bsp_spmm_opts* opts) {
+  if (!dev || n_jobs < 0 || (n_jobs > 0 && !jobs)) return set_error(BSP_ERR_INVALID_ARG, "null argument");
+  if (n_jobs == 0) return BSP_OK;
+  // device layout of each job: values | row_ptr | col_idx | B | C
+  std::vector<size_t> off(static_cast<size_t>(n_jobs) + 1, 0);
+  for (int32_t k = 0; k < n_jobs; ++k) {
+    const bsp_spmm_host_job& j = jobs[k];
+    if (!j.row_ptr || !j.B || !j.C_out || (j.nnzb > 0 && (!j.col_idx || !j.values)))
+      return set_error(BSP_ERR_INVALID_ARG, "job " + std::to_string(k) + ": null argument");
+    if (j.R <= 0 || j.C <= 0 || j.M <= 0 || j.K <= 0 || j.N <= 0 || j.M % j.R || j.K % j.C || j.nnzb < 0)
+      return set_error(BSP_ERR_INVALID_ARG, "job " + std::to_string(k) + ": bad dimensions");
+    off[k + 1] = off[k] + align256(sizeof(uint16_t) * j.nnzb * j.R * j.C) +
+                 align256(sizeof(int32_t) * (j.M / j.R + 1)) + align256(sizeof(int32_t) * std::max<int64_t>(j.nnzb, 1)) +
+                 align256(sizeof(uint16_t) * j.K * j.N) + align256(sizeof(uint16_t) * j.M * j.N);
+  }
+  bsp_status s = ws_reserve(dev, off[n_jobs]);
+  if (s == BSP_OK) s = host_streams(dev, static_cast<size_t>(n_jobs));
+  if (s != BSP_OK) return s;
+  cudaStream_t sh = dev->s_h2d, sc = dev->s_comp, sd = dev->s_d2h;
+  struct Dev {
+    void* val;
+    int32_t *rp, *ci;
+    uint16_t *B, *C;
+  };
+  std::vector<Dev> d(static_cast<size_t>(n_jobs));
+  std::vector<bsp_spmm_plan*> plans(static_cast<size_t>(n_jobs), nullptr);
+  auto run = [&]() -> bsp_status {
+    bsp_status st = BSP_OK;
+    // 1. every job's inputs go in on the copy stream, in job order
+    for (int32_t k = 0; k < n_jobs && st == BSP_OK; ++k) {
+      const bsp_spmm_host_job& j = jobs[k];
+      uint8_t* w = static_cast<uint8_t*>(dev->ws) + off[k];
+      const size_t b_val = align256(sizeof(uint16_t) * j.nnzb * j.R * j.C);
+      const size_t b_rp = align256(sizeof(int32_t) * (j.M / j.R + 1));
+      const size_t b_ci = align256(sizeof(int32_t) * std::max<int64_t>(j.nnzb, 1));
+      const size_t b_B = align256(sizeof(uint16_t) * j.K * j.N);
+      d[k] = Dev{w, reinterpret_cast<int32_t*>(w + b_val), reinterpret_cast<int32_t*>(w + b_val + b_rp),
+                 reinterpret_cast<uint16_t*>(w + b_val + b_rp + b_ci),
+                 reinterpret_cast<uint16_t*>(w + b_val + b_rp + b_ci + b_B)};
+      st = cuda_check(cudaMemcpyAsync(d[k].rp, j.row_ptr, sizeof(int32_t) * (j.M / j.R + 1), cudaMemcpyHostToDevice, sh),
+                      "H2D row_ptr");
+      if (st == BSP_OK && j.nnzb > 0)
+        st = cuda_check(cudaMemcpyAsync(d[k].ci, j.col_idx, sizeof(int32_t) * j.nnzb, cudaMemcpyHostToDevice, sh),
+                        "H2D col_idx");
+      if (st == BSP_OK && j.nnzb > 0)
+        st = cuda_check(cudaMemcpyAsync(d[k].val, j.values, sizeof(uint16_t) * j.nnzb * j.R * j.C,
+                                        cudaMemcpyHostToDevice, sh), "H2D values");
+      if (st == BSP_OK)
+        st = cuda_check(cudaMemcpyAsync(d[k].B, j.B, sizeof(uint16_t) * j.K * j.N, cudaMemcpyHostToDevice, sh), "H2D B");
+      if (st == BSP_OK) st = cuda_check(cudaEventRecord(dev->ev_in[k], sh), "cudaEventRecord");
+    }
+    if (st != BSP_OK) return st;
+    // 2. the plans are built on the host while the inputs stream in
+    for (int32_t k = 0; k < n_jobs; ++k) {
+      const bsp_spmm_host_job& j = jobs[k];
+      bsp_spmm_plan* p = new (std::nothrow) bsp_spmm_plan();
+      if (!p) return set_error(BSP_ERR_ALLOC, "host allocation failed");
+      plans[k] = p;
+      p->dev = dev;
+      p->M = j.M;
+      p->K = j.K;
+      p->N = j.N;
+      p->R = j.R;
+      p->C = j.C;
+      p->nnzb = j.nnzb;
+      p->c_type = BSP_BF16;
+      p->strategy = strategy;
+      p->blob_borrowed = true;
+      st = plan_spmm_host(p, j.row_ptr, j.col_idx, dev->sm_count, dev->max_smem_optin, opts);
+      if (st != BSP_OK) return st;
+    }
+    // 3. all plan tables in one upload (device plan area + pinned staging),
+    //    one split-K workspace serving the plans in turn on the compute stream
+    std::vector<std::vector<int32_t>> zeros(static_cast<size_t>(n_jobs));
+    std::vector<std::vector<std::pair<const void*, size_t>>> parts(static_cast<size_t>(n_jobs));
+    size_t total = 0, split_ws = 0;
+    for (int32_t k = 0; k < n_jobs; ++k) {
+      parts[k] = spmm_table_parts(*plans[k], &zeros[k]);
+      for (auto& pr : parts[k]) total += align256(pr.second);
+      if (plans[k]->n_split_slots > 0) split_ws = std::max(split_ws, spmm_split_ws_bytes(*plans[k]));
+    }
+    total = std::max<size_t>(total, 256);
+    if (dev->plan_ws_bytes < total) {
+      if (dev->plan_ws) cudaFree(dev->plan_ws);
+      dev->plan_ws = nullptr;
+      dev->plan_ws_bytes = 0;
+      if (cudaMalloc(&dev->plan_ws, total) != cudaSuccess)
+        return set_error(BSP_ERR_ALLOC, "cudaMalloc of the plan-table area failed");
+      dev->plan_ws_bytes = total;
+    }
+    if (dev->pinned_bytes < total) {
+      if (dev->pinned) cudaFreeHost(dev->pinned);
+      dev->pinned = nullptr;
+      dev->pinned_bytes = 0;
+      if (cudaHostAlloc(&dev->pinned, total, cudaHostAllocDefault) != cudaSuccess)
+        return set_error(BSP_ERR_ALLOC, "cudaHostAlloc of the plan-table staging failed");
+      dev->pinned_bytes = total;
+    }
+    if (split_ws > dev->aux_ws_bytes) {
+      if (dev->aux_ws) cudaFree(dev->aux_ws);
+      dev->aux_ws = nullptr;
+      dev->aux_ws_bytes = 0;
+      if (cudaMalloc(&dev->aux_ws, split_ws) != cudaSuccess)
+        return set_error(BSP_ERR_ALLOC, "cudaMalloc of the split-K workspace failed");
+      dev->aux_ws_bytes = split_ws;
+    }
+    uint8_t* h = static_cast<uint8_t*>(dev->pinned);
+    size_t o = 0;
+    for (int32_t k = 0; k < n_jobs; ++k) {
+      std::vector<void*> ptrs;
+      for (auto& pr : parts[k]) {
+        if (pr.second) memcpy(h + o, pr.first, pr.second);
+        ptrs.push_back(static_cast<uint8_t*>(dev->plan_ws) + o);
+        o += align256(pr.second);
+      }
+      spmm_bind_tables(plans[k], ptrs);
+      plans[k]->d_blob = dev->plan_ws;
+      if (plans[k]->n_split_slots > 0) plans[k]->d_split_ws = static_cast<float*>(dev->aux_ws);
+    }
+    st = cuda_check(cudaMemcpyAsync(dev->plan_ws, h, total, cudaMemcpyHostToDevice, sc), "upload plan tables");
+    // 4. each job's kernel once its inputs are in; its C goes out while the
+    //    later jobs' inputs still come in (the copy engines run both ways)
+    for (int32_t k = 0; k < n_jobs && st == BSP_OK; ++k) {
+      const bsp_spmm_host_job& j = jobs[k];
+      bsp_bsr_desc A{j.M, j.K, j.R, j.C, j.nnzb, d[k].rp, d[k].ci, d[k].val};
+      st = cuda_check(cudaStreamWaitEvent(sc, dev->ev_in[k], 0), "cudaStreamWaitEvent");
+      if (st == BSP_OK) st = bsp_spmm_execute(plans[k], &A, d[k].B, j.N, d[k].C, j.N, sc);
+      if (st == BSP_OK) st = cuda_check(cudaEventRecord(dev->ev_out[k], sc), "cudaEventRecord");
+      if (st == BSP_OK) st = cuda_check(cudaStreamWaitEvent(sd, dev->ev_out[k], 0), "cudaStreamWaitEvent");
+      if (st == BSP_OK)
+        st = cuda_check(cudaMemcpyAsync(j.C_out, d[k].C, sizeof(uint16_t) * j.M * j.N, cudaMemcpyDeviceToHost, sd),
+                        "D2H C");
+    }
+    if (st == BSP_OK) st = cuda_check(cudaStreamSynchronize(sd), "sync");
+    if (st == BSP_OK) st = cuda_check(cudaStreamSynchronize(sc), "sync");
+    return st;
+  };
+  s = run();
+  if (s != BSP_OK) {
+    cudaStreamSynchronize(sh);
+    cudaStreamSynchronize(sc);
+    cudaStreamSynchronize(sd);
+  }
+  for (bsp_spmm_plan* p : plans) bsp_spmm_plan_destroy(p);
+  if (s != BSP_OK) return s;
+  return bsp_device_synchronize(dev);
 }
 
 bsp_status bsp_spmm_host_profile(bsp_device* dev, int64_t M, int64_t K, int32_t R, int32_t C,

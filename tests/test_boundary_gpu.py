@@ -86,3 +86,24 @@ def test_bsr_upload_pattern_only_mask_and_rejects_bad_patterns():
         st = L.bsp_bsr_upload(dev.handle, M, N, R, R, int(rp[-1]), r_.ctypes.data, c_.ctypes.data, None,
                               ctypes.byref(desc))
         assert st == bsp.BSP_ERR_INVALID_ARG and desc.row_ptr is None
+
+
+@pytest.mark.parametrize("strategy", ["naive", "dda"])
+def test_spmm_host_batch_matches_oracle(strategy):
+    """bsp_spmm_host_batch: several products of different shapes, block sizes
+    and densities (split-K and CTA-pair plans among them) in one pipelined
+    call, each equal to the oracle; a second call reuses the workspace."""
+    import bsp
+
+    rng = np.random.default_rng(23)
+    jobs, golds = [], []
+    for M, K, N, R, C, p in [(4096, 4096, 1024, 32, 32, 0.5), (1024, 2048, 256, 64, 64, 0.2),
+                             (2048, 1024, 512, 32, 32, 0.01), (512, 512, 96, 32, 64, 0.3)]:
+        rp, ci, vals = rand_bsr(rng, M, K, R, C, p, empty_rows=(1,))
+        B = rand_dense(rng, K, N)
+        jobs.append(dict(M=M, K=K, R=R, C=C, row_ptr=rp, col_idx=ci, values=vals, B=B, N=N))
+        golds.append(oracle.spmm_bf16(rp, ci, vals, M, K, R, C, B, N))
+    for _ in range(2):
+        outs = bsp.spmm_host_batch(jobs, strategy=bsp.STRATEGIES[strategy])
+        for k, (o, g) in enumerate(zip(outs, golds)):
+            assert_bf16_close(o, g, what=f"batch job {k} {strategy}")

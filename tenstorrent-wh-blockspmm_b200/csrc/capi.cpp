@@ -853,8 +853,9 @@ bsp_status bsp_spmm_host_batch(bsp_device* dev, int32_t n_jobs, const bsp_spmm_h
       p->nnzb = j.nnzb;
       p->c_type = BSP_BF16;
       p->strategy = strategy;
-      p->blob_borrowed = true;
       st = plan_spmm_host(p, j.row_ptr, j.col_idx, dev->sm_count, dev->max_smem_optin, opts);
+      // after planning: the planner may replace the whole plan object (CTA pairs)
+      p->blob_borrowed = true;
       if (st != BSP_OK) return st;
     }
     // 3. all plan tables in one upload (device plan area + pinned staging),

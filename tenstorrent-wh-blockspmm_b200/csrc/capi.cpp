@@ -7,6 +7,7 @@
 #include <cstring>
 #include <new>
 #include <string>
+#include <thread>
 #include <vector>
 
 #include "bsp_internal.h"
@@ -838,7 +839,8 @@ bsp_status bsp_spmm_host_batch(bsp_device* dev, int32_t n_jobs, const bsp_spmm_h
       if (st == BSP_OK) st = cuda_check(cudaEventRecord(dev->ev_in[k], sh), "cudaEventRecord");
     }
     if (st != BSP_OK) return st;
-    // 2. the plans are built on the host while the inputs stream in
+    // 2. the plans are built on the host, one thread per job, while the
+    //    inputs stream in
     for (int32_t k = 0; k < n_jobs; ++k) {
       const bsp_spmm_host_job& j = jobs[k];
       bsp_spmm_plan* p = new (std::nothrow) bsp_spmm_plan();
@@ -853,10 +855,23 @@ bsp_status bsp_spmm_host_batch(bsp_device* dev, int32_t n_jobs, const bsp_spmm_h
       p->nnzb = j.nnzb;
       p->c_type = BSP_BF16;
       p->strategy = strategy;
-      st = plan_spmm_host(p, j.row_ptr, j.col_idx, dev->sm_count, dev->max_smem_optin, opts);
-      // after planning: the planner may replace the whole plan object (CTA pairs)
-      p->blob_borrowed = true;
-      if (st != BSP_OK) return st;
+    }
+    {
+      std::vector<bsp_status> pst(static_cast<size_t>(n_jobs), BSP_OK);
+      std::vector<std::string> pmsg(static_cast<size_t>(n_jobs));
+      std::vector<std::thread> th;
+      for (int32_t k = 0; k < n_jobs; ++k)
+        th.emplace_back([&, k]() {
+          pst[k] = plan_spmm_host(plans[k], jobs[k].row_ptr, jobs[k].col_idx, dev->sm_count, dev->max_smem_optin,
+                                  opts);
+          if (pst[k] != BSP_OK) pmsg[k] = g_last_error;  // this worker's message
+        });
+      for (auto& t : th) t.join();
+      for (int32_t k = 0; k < n_jobs; ++k) {
+        // after planning: the planner may replace the whole plan object (CTA pairs)
+        plans[k]->blob_borrowed = true;
+        if (pst[k] != BSP_OK) return set_error(pst[k], "job " + std::to_string(k) + ": " + pmsg[k]);
+      }
     }
     // 3. all plan tables in one upload (device plan area + pinned staging),
     //    one split-K workspace serving the plans in turn on the compute stream

@@ -19,7 +19,6 @@
 #include <string>
 #include <system_error>
 #include <thread>
-#include <tuple>
 
 #include "bsp_internal.h"
 
@@ -93,27 +92,6 @@ static bsp_status parallel_ranges(int64_t n, int nt, F&& fn) {
 }
 
 static bsp_status spmm_stage_counts(bsp_spmm_plan* p);
-
-// Column tiles per L2 panel when B does not fit in L2 (see l2_panel_key):
-// $BSP_L2_PANEL_TILES when set (>= 1), else as many tiles as keep the panel
-// (K rows x tiles * tile_n columns of B) within 64 MiB.
-static int l2_panel_tiles(int64_t K, int64_t tile_n) {
-  if (const char* e = std::getenv("BSP_L2_PANEL_TILES")) {
-    const int v = std::atoi(e);
-    if (v >= 1) return v;
-  }
-  const int64_t panel = K * tile_n * 2;
-  return static_cast<int>(std::max<int64_t>(1, (int64_t(64) << 20) / std::max<int64_t>(panel, 1)));
-}
-
-// Sort key of a unit in the L2 order: column panel, then row group, then
-// tile.  Dealt in this order to the least-loaded CTA, all CTAs work inside one
-// panel of B at a time (read from DRAM about once), and the tiles of one row
-// group run at about the same time on neighbouring CTAs, so that its A blocks
-// come from DRAM about once per panel instead of once per tile.
-static std::tuple<int64_t, int64_t, int64_t> l2_panel_key(int64_t n0, int64_t row0, int64_t tile_n, int panel) {
-  return {n0 / (tile_n * panel), row0, n0};
-}
 static bsp_status rowstack_stage_lists(bsp_spmm_plan* p);
 static bsp_status pair_stage_lists(bsp_spmm_plan* p);
 
@@ -640,11 +618,7 @@ bsp_status plan_spmm_rowstack(bsp_spmm_plan* p, const int32_t* row_ptr, const in
   if (l2_order) {
     std::vector<int32_t> idx(units.size());
     std::iota(idx.begin(), idx.end(), 0);
-    const int panel = l2_panel_tiles(p->K, tile_n);
-    std::stable_sort(idx.begin(), idx.end(), [&](int32_t a, int32_t b) {
-      return l2_panel_key(units[a].n0, units[a].row0, tile_n, panel) <
-             l2_panel_key(units[b].n0, units[b].row0, tile_n, panel);
-    });
+    std::stable_sort(idx.begin(), idx.end(), [&](int32_t a, int32_t b) { return units[a].n0 < units[b].n0; });
     std::vector<SpmmUnit> su(units.size());
     std::vector<int64_t> sw(units.size());
     for (size_t i = 0; i < idx.size(); ++i) {
@@ -837,10 +811,7 @@ bsp_status plan_spmm_pair(bsp_spmm_plan* p, const int32_t* row_ptr, const int32_
   // B larger than L2: pair units run tile by tile (see plan_spmm_rowstack)
   const bool l2_order = !o.no_load_balance && ntiles > 1 && p->K * p->N * 2 > (int64_t(64) << 20);
   if (l2_order) {
-    const int panel = l2_panel_tiles(p->K, 256);
-    std::stable_sort(units.begin(), units.end(), [&](const PairUnit& a, const PairUnit& b) {
-      return l2_panel_key(a.n0, a.e0, 256, panel) < l2_panel_key(b.n0, b.e0, 256, panel);
-    });
+    std::stable_sort(units.begin(), units.end(), [](const PairUnit& a, const PairUnit& b) { return a.n0 < b.n0; });
     // weights follow the units: recompute them in the new order
     weight.clear();
     for (const PairUnit& u : units)

@@ -290,6 +290,15 @@ struct bsp_device {
   size_t aux_ws_bytes = 0;
   cudaStream_t s_h2d = nullptr, s_comp = nullptr, s_d2h = nullptr;
   std::vector<cudaEvent_t> ev_in, ev_out;
+  // bsp_spmm_host_batch: per job slot, a grow-only device area for the plan
+  // tables and split-K partials and a pinned staging area for the tables
+  struct BatchSlot {
+    void* d = nullptr;
+    size_t d_bytes = 0;
+    void* h = nullptr;
+    size_t h_bytes = 0;
+  };
+  std::vector<BatchSlot> batch_slots;
 };
 
 struct bsp_spgemm_plan {

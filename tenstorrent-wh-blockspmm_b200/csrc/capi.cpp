@@ -287,6 +287,10 @@ bsp_status bsp_device_close(bsp_device* dev) {
   if (dev->pinned) cudaFreeHost(dev->pinned);
   if (dev->plan_ws) cudaFree(dev->plan_ws);
   if (dev->aux_ws) cudaFree(dev->aux_ws);
+  for (auto& sl : dev->batch_slots) {
+    if (sl.d) cudaFree(sl.d);
+    if (sl.h) cudaFreeHost(sl.h);
+  }
   for (cudaEvent_t e : dev->ev_in) cudaEventDestroy(e);
   for (cudaEvent_t e : dev->ev_out) cudaEventDestroy(e);
   if (dev->s_h2d) cudaStreamDestroy(dev->s_h2d);
@@ -790,9 +794,10 @@ bsp_status bsp_spmm_host_batch(bsp_device* dev, int32_t n_jobs, const bsp_spmm_h
                                bsp_strategy strategy, const bsp_spmm_opts* opts) {
   if (!dev || n_jobs < 0 || (n_jobs > 0 && !jobs)) return set_error(BSP_ERR_INVALID_ARG, "null argument");
   if (n_jobs == 0) return BSP_OK;
+  const size_t nj = static_cast<size_t>(n_jobs);
   // device layout of each job: values | row_ptr | col_idx | B | C
-  std::vector<size_t> off(static_cast<size_t>(n_jobs) + 1, 0);
-  for (int32_t k = 0; k < n_jobs; ++k) {
+  std::vector<size_t> off(nj + 1, 0);
+  for (size_t k = 0; k < nj; ++k) {
     const bsp_spmm_host_job& j = jobs[k];
     if (!j.row_ptr || !j.B || !j.C_out || (j.nnzb > 0 && (!j.col_idx || !j.values)))
       return set_error(BSP_ERR_INVALID_ARG, "job " + std::to_string(k) + ": null argument");
@@ -802,133 +807,125 @@ bsp_status bsp_spmm_host_batch(bsp_device* dev, int32_t n_jobs, const bsp_spmm_h
                  align256(sizeof(int32_t) * (j.M / j.R + 1)) + align256(sizeof(int32_t) * std::max<int64_t>(j.nnzb, 1)) +
                  align256(sizeof(uint16_t) * j.K * j.N) + align256(sizeof(uint16_t) * j.M * j.N);
   }
-  bsp_status s = ws_reserve(dev, off[n_jobs]);
-  if (s == BSP_OK) s = host_streams(dev, static_cast<size_t>(n_jobs));
+  bsp_status s = ws_reserve(dev, off[nj]);
+  if (s == BSP_OK) s = host_streams(dev, nj);
   if (s != BSP_OK) return s;
+  if (dev->batch_slots.size() < nj) dev->batch_slots.resize(nj);
   cudaStream_t sh = dev->s_h2d, sc = dev->s_comp, sd = dev->s_d2h;
   struct Dev {
     void* val;
     int32_t *rp, *ci;
     uint16_t *B, *C;
   };
-  std::vector<Dev> d(static_cast<size_t>(n_jobs));
-  std::vector<bsp_spmm_plan*> plans(static_cast<size_t>(n_jobs), nullptr);
+  std::vector<Dev> d(nj);
+  std::vector<bsp_spmm_plan*> plans(nj, nullptr);
+  for (size_t k = 0; k < nj; ++k) {
+    const bsp_spmm_host_job& j = jobs[k];
+    bsp_spmm_plan* p = new (std::nothrow) bsp_spmm_plan();
+    if (!p) {
+      for (bsp_spmm_plan* q : plans) delete q;
+      return set_error(BSP_ERR_ALLOC, "host allocation failed");
+    }
+    plans[k] = p;
+    p->dev = dev;
+    p->M = j.M;
+    p->K = j.K;
+    p->N = j.N;
+    p->R = j.R;
+    p->C = j.C;
+    p->nnzb = j.nnzb;
+    p->c_type = BSP_BF16;
+    p->strategy = strategy;
+  }
+  // 1. every job is planned on its own host thread from the start
+  std::vector<bsp_status> pst(nj, BSP_OK);
+  std::vector<std::string> pmsg(nj);
+  std::vector<std::thread> th;
+  for (size_t k = 0; k < nj; ++k)
+    th.emplace_back([&, k]() {
+      pst[k] = plan_spmm_host(plans[k], jobs[k].row_ptr, jobs[k].col_idx, dev->sm_count, dev->max_smem_optin, opts);
+      if (pst[k] != BSP_OK) pmsg[k] = g_last_error;  // this worker's message
+    });
+  size_t joined = 0;
+  auto join_upto = [&](size_t k) {  // threads 0..k done
+    for (; joined <= k && joined < nj; ++joined) th[joined].join();
+  };
+  size_t queued = 0;  // jobs whose inputs are queued on the copy stream
+  auto queue_inputs = [&](size_t k) -> bsp_status {
+    const bsp_spmm_host_job& j = jobs[k];
+    uint8_t* w = static_cast<uint8_t*>(dev->ws) + off[k];
+    const size_t b_val = align256(sizeof(uint16_t) * j.nnzb * j.R * j.C);
+    const size_t b_rp = align256(sizeof(int32_t) * (j.M / j.R + 1));
+    const size_t b_ci = align256(sizeof(int32_t) * std::max<int64_t>(j.nnzb, 1));
+    const size_t b_B = align256(sizeof(uint16_t) * j.K * j.N);
+    d[k] = Dev{w, reinterpret_cast<int32_t*>(w + b_val), reinterpret_cast<int32_t*>(w + b_val + b_rp),
+               reinterpret_cast<uint16_t*>(w + b_val + b_rp + b_ci),
+               reinterpret_cast<uint16_t*>(w + b_val + b_rp + b_ci + b_B)};
+    bsp_status st = cuda_check(cudaMemcpyAsync(d[k].rp, j.row_ptr, sizeof(int32_t) * (j.M / j.R + 1),
+                                               cudaMemcpyHostToDevice, sh), "H2D row_ptr");
+    if (st == BSP_OK && j.nnzb > 0)
+      st = cuda_check(cudaMemcpyAsync(d[k].ci, j.col_idx, sizeof(int32_t) * j.nnzb, cudaMemcpyHostToDevice, sh),
+                      "H2D col_idx");
+    if (st == BSP_OK && j.nnzb > 0)
+      st = cuda_check(cudaMemcpyAsync(d[k].val, j.values, sizeof(uint16_t) * j.nnzb * j.R * j.C,
+                                      cudaMemcpyHostToDevice, sh), "H2D values");
+    if (st == BSP_OK)
+      st = cuda_check(cudaMemcpyAsync(d[k].B, j.B, sizeof(uint16_t) * j.K * j.N, cudaMemcpyHostToDevice, sh), "H2D B");
+    return st;
+  };
   auto run = [&]() -> bsp_status {
     bsp_status st = BSP_OK;
-    // 1. every job's inputs go in on the copy stream, in job order
-    for (int32_t k = 0; k < n_jobs && st == BSP_OK; ++k) {
-      const bsp_spmm_host_job& j = jobs[k];
-      uint8_t* w = static_cast<uint8_t*>(dev->ws) + off[k];
-      const size_t b_val = align256(sizeof(uint16_t) * j.nnzb * j.R * j.C);
-      const size_t b_rp = align256(sizeof(int32_t) * (j.M / j.R + 1));
-      const size_t b_ci = align256(sizeof(int32_t) * std::max<int64_t>(j.nnzb, 1));
-      const size_t b_B = align256(sizeof(uint16_t) * j.K * j.N);
-      d[k] = Dev{w, reinterpret_cast<int32_t*>(w + b_val), reinterpret_cast<int32_t*>(w + b_val + b_rp),
-                 reinterpret_cast<uint16_t*>(w + b_val + b_rp + b_ci),
-                 reinterpret_cast<uint16_t*>(w + b_val + b_rp + b_ci + b_B)};
-      st = cuda_check(cudaMemcpyAsync(d[k].rp, j.row_ptr, sizeof(int32_t) * (j.M / j.R + 1), cudaMemcpyHostToDevice, sh),
-                      "H2D row_ptr");
-      if (st == BSP_OK && j.nnzb > 0)
-        st = cuda_check(cudaMemcpyAsync(d[k].ci, j.col_idx, sizeof(int32_t) * j.nnzb, cudaMemcpyHostToDevice, sh),
-                        "H2D col_idx");
-      if (st == BSP_OK && j.nnzb > 0)
-        st = cuda_check(cudaMemcpyAsync(d[k].val, j.values, sizeof(uint16_t) * j.nnzb * j.R * j.C,
-                                        cudaMemcpyHostToDevice, sh), "H2D values");
-      if (st == BSP_OK)
-        st = cuda_check(cudaMemcpyAsync(d[k].B, j.B, sizeof(uint16_t) * j.K * j.N, cudaMemcpyHostToDevice, sh), "H2D B");
-      if (st == BSP_OK) st = cuda_check(cudaEventRecord(dev->ev_in[k], sh), "cudaEventRecord");
-    }
-    if (st != BSP_OK) return st;
-    // 2. the plans are built on the host, one thread per job, while the
-    //    inputs stream in
-    for (int32_t k = 0; k < n_jobs; ++k) {
-      const bsp_spmm_host_job& j = jobs[k];
-      bsp_spmm_plan* p = new (std::nothrow) bsp_spmm_plan();
-      if (!p) return set_error(BSP_ERR_ALLOC, "host allocation failed");
-      plans[k] = p;
-      p->dev = dev;
-      p->M = j.M;
-      p->K = j.K;
-      p->N = j.N;
-      p->R = j.R;
-      p->C = j.C;
-      p->nnzb = j.nnzb;
-      p->c_type = BSP_BF16;
-      p->strategy = strategy;
-    }
-    {
-      std::vector<bsp_status> pst(static_cast<size_t>(n_jobs), BSP_OK);
-      std::vector<std::string> pmsg(static_cast<size_t>(n_jobs));
-      std::vector<std::thread> th;
-      for (int32_t k = 0; k < n_jobs; ++k)
-        th.emplace_back([&, k]() {
-          pst[k] = plan_spmm_host(plans[k], jobs[k].row_ptr, jobs[k].col_idx, dev->sm_count, dev->max_smem_optin,
-                                  opts);
-          if (pst[k] != BSP_OK) pmsg[k] = g_last_error;  // this worker's message
-        });
-      for (auto& t : th) t.join();
-      for (int32_t k = 0; k < n_jobs; ++k) {
-        // after planning: the planner may replace the whole plan object (CTA pairs)
-        plans[k]->blob_borrowed = true;
-        if (pst[k] != BSP_OK) return set_error(pst[k], "job " + std::to_string(k) + ": " + pmsg[k]);
+    for (size_t k = 0; k < nj && st == BSP_OK; ++k) {
+      // 2. keep the copy engine one job ahead: the inputs of job k + 1 go in
+      //    before job k's tables, so that waiting for plan k never idles it
+      for (; queued <= k + 1 && queued < nj && st == BSP_OK; ++queued) st = queue_inputs(queued);
+      if (st != BSP_OK) return st;
+      join_upto(k);
+      bsp_spmm_plan* p = plans[k];
+      p->blob_borrowed = true;  // after planning: the planner may replace the plan object (CTA pairs)
+      if (pst[k] != BSP_OK) return set_error(pst[k], "job " + std::to_string(k) + ": " + pmsg[k]);
+      // 3. job k's tables (and split-K partials) in its slot, copied in
+      //    behind its inputs on the same stream
+      std::vector<int32_t> zeros;
+      const auto parts = spmm_table_parts(*p, &zeros);
+      size_t tb = 0;
+      for (auto& pr : parts) tb += align256(pr.second);
+      tb = std::max<size_t>(tb, 256);
+      const size_t sw = p->n_split_slots > 0 ? spmm_split_ws_bytes(*p) : 0;
+      bsp_device::BatchSlot& sl = dev->batch_slots[k];
+      if (sl.d_bytes < tb + sw) {
+        if (sl.d) cudaFree(sl.d);  // synchronises: only while the slot grows
+        sl.d = nullptr;
+        sl.d_bytes = 0;
+        if (cudaMalloc(&sl.d, tb + sw) != cudaSuccess) return set_error(BSP_ERR_ALLOC, "cudaMalloc of a batch slot failed");
+        sl.d_bytes = tb + sw;
       }
-    }
-    // 3. all plan tables in one upload (device plan area + pinned staging),
-    //    one split-K workspace serving the plans in turn on the compute stream
-    std::vector<std::vector<int32_t>> zeros(static_cast<size_t>(n_jobs));
-    std::vector<std::vector<std::pair<const void*, size_t>>> parts(static_cast<size_t>(n_jobs));
-    size_t total = 0, split_ws = 0;
-    for (int32_t k = 0; k < n_jobs; ++k) {
-      parts[k] = spmm_table_parts(*plans[k], &zeros[k]);
-      for (auto& pr : parts[k]) total += align256(pr.second);
-      if (plans[k]->n_split_slots > 0) split_ws = std::max(split_ws, spmm_split_ws_bytes(*plans[k]));
-    }
-    total = std::max<size_t>(total, 256);
-    if (dev->plan_ws_bytes < total) {
-      if (dev->plan_ws) cudaFree(dev->plan_ws);
-      dev->plan_ws = nullptr;
-      dev->plan_ws_bytes = 0;
-      if (cudaMalloc(&dev->plan_ws, total) != cudaSuccess)
-        return set_error(BSP_ERR_ALLOC, "cudaMalloc of the plan-table area failed");
-      dev->plan_ws_bytes = total;
-    }
-    if (dev->pinned_bytes < total) {
-      if (dev->pinned) cudaFreeHost(dev->pinned);
-      dev->pinned = nullptr;
-      dev->pinned_bytes = 0;
-      if (cudaHostAlloc(&dev->pinned, total, cudaHostAllocDefault) != cudaSuccess)
-        return set_error(BSP_ERR_ALLOC, "cudaHostAlloc of the plan-table staging failed");
-      dev->pinned_bytes = total;
-    }
-    if (split_ws > dev->aux_ws_bytes) {
-      if (dev->aux_ws) cudaFree(dev->aux_ws);
-      dev->aux_ws = nullptr;
-      dev->aux_ws_bytes = 0;
-      if (cudaMalloc(&dev->aux_ws, split_ws) != cudaSuccess)
-        return set_error(BSP_ERR_ALLOC, "cudaMalloc of the split-K workspace failed");
-      dev->aux_ws_bytes = split_ws;
-    }
-    uint8_t* h = static_cast<uint8_t*>(dev->pinned);
-    size_t o = 0;
-    for (int32_t k = 0; k < n_jobs; ++k) {
+      if (sl.h_bytes < tb) {
+        if (sl.h) cudaFreeHost(sl.h);
+        sl.h = nullptr;
+        sl.h_bytes = 0;
+        if (cudaHostAlloc(&sl.h, tb, cudaHostAllocDefault) != cudaSuccess)
+          return set_error(BSP_ERR_ALLOC, "cudaHostAlloc of a batch slot failed");
+        sl.h_bytes = tb;
+      }
       std::vector<void*> ptrs;
-      for (auto& pr : parts[k]) {
-        if (pr.second) memcpy(h + o, pr.first, pr.second);
-        ptrs.push_back(static_cast<uint8_t*>(dev->plan_ws) + o);
+      size_t o = 0;
+      for (auto& pr : parts) {
+        if (pr.second) memcpy(static_cast<uint8_t*>(sl.h) + o, pr.first, pr.second);
+        ptrs.push_back(static_cast<uint8_t*>(sl.d) + o);
         o += align256(pr.second);
       }
-      spmm_bind_tables(plans[k], ptrs);
-      plans[k]->d_blob = dev->plan_ws;
-      if (plans[k]->n_split_slots > 0) plans[k]->d_split_ws = static_cast<float*>(dev->aux_ws);
-    }
-    st = cuda_check(cudaMemcpyAsync(dev->plan_ws, h, total, cudaMemcpyHostToDevice, sc), "upload plan tables");
-    // 4. each job's kernel once its inputs are in; its C goes out while the
-    //    later jobs' inputs still come in (the copy engines run both ways)
-    for (int32_t k = 0; k < n_jobs && st == BSP_OK; ++k) {
+      spmm_bind_tables(p, ptrs);
+      p->d_blob = sl.d;
+      if (sw) p->d_split_ws = reinterpret_cast<float*>(static_cast<uint8_t*>(sl.d) + tb);
+      st = cuda_check(cudaMemcpyAsync(sl.d, sl.h, tb, cudaMemcpyHostToDevice, sh), "upload plan tables");
+      if (st == BSP_OK) st = cuda_check(cudaEventRecord(dev->ev_in[k], sh), "cudaEventRecord");
+      // 4. job k's kernel once its inputs and tables are in; its C goes out
+      //    while the later jobs' inputs still come in (copies run both ways)
       const bsp_spmm_host_job& j = jobs[k];
       bsp_bsr_desc A{j.M, j.K, j.R, j.C, j.nnzb, d[k].rp, d[k].ci, d[k].val};
-      st = cuda_check(cudaStreamWaitEvent(sc, dev->ev_in[k], 0), "cudaStreamWaitEvent");
-      if (st == BSP_OK) st = bsp_spmm_execute(plans[k], &A, d[k].B, j.N, d[k].C, j.N, sc);
+      if (st == BSP_OK) st = cuda_check(cudaStreamWaitEvent(sc, dev->ev_in[k], 0), "cudaStreamWaitEvent");
+      if (st == BSP_OK) st = bsp_spmm_execute(p, &A, d[k].B, j.N, d[k].C, j.N, sc);
       if (st == BSP_OK) st = cuda_check(cudaEventRecord(dev->ev_out[k], sc), "cudaEventRecord");
       if (st == BSP_OK) st = cuda_check(cudaStreamWaitEvent(sd, dev->ev_out[k], 0), "cudaStreamWaitEvent");
       if (st == BSP_OK)
@@ -940,12 +937,16 @@ bsp_status bsp_spmm_host_batch(bsp_device* dev, int32_t n_jobs, const bsp_spmm_h
     return st;
   };
   s = run();
+  join_upto(nj - 1);
   if (s != BSP_OK) {
     cudaStreamSynchronize(sh);
     cudaStreamSynchronize(sc);
     cudaStreamSynchronize(sd);
   }
-  for (bsp_spmm_plan* p : plans) bsp_spmm_plan_destroy(p);
+  for (bsp_spmm_plan* p : plans) {
+    if (p) p->blob_borrowed = true;  // tables live in the device's batch slots
+    bsp_spmm_plan_destroy(p);
+  }
   if (s != BSP_OK) return s;
   return bsp_device_synchronize(dev);
 }

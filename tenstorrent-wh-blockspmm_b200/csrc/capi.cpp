@@ -790,6 +790,15 @@ bsp_status bsp_spmm_host(bsp_device* dev, int64_t M, int64_t K, int32_t R, int32
                         opts, 0, nullptr);
 }
 
+// Copies n16 16-byte words from mapped pinned host memory into device memory
+// with the SMs rather than a copy engine, so that a small plan table does not
+// queue behind the large input copies already on the engine.
+__global__ void fetch_mapped_words(uint4* __restrict__ dst, const uint4* __restrict__ src, size_t n16) {
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n16;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x)
+    dst[i] = src[i];
+}
+
 bsp_status bsp_spmm_host_batch(bsp_device* dev, int32_t n_jobs, const bsp_spmm_host_job* jobs,
                                bsp_strategy strategy, const bsp_spmm_opts* opts) {
   if (!dev || n_jobs < 0 || (n_jobs > 0 && !jobs)) return set_error(BSP_ERR_INVALID_ARG, "null argument");
@@ -871,21 +880,21 @@ bsp_status bsp_spmm_host_batch(bsp_device* dev, int32_t n_jobs, const bsp_spmm_h
                                       cudaMemcpyHostToDevice, sh), "H2D values");
     if (st == BSP_OK)
       st = cuda_check(cudaMemcpyAsync(d[k].B, j.B, sizeof(uint16_t) * j.K * j.N, cudaMemcpyHostToDevice, sh), "H2D B");
+    if (st == BSP_OK) st = cuda_check(cudaEventRecord(dev->ev_in[k], sh), "cudaEventRecord");
     return st;
   };
   auto run = [&]() -> bsp_status {
     bsp_status st = BSP_OK;
+    // 2. every job's inputs go onto the copy stream at once
+    for (; queued < nj && st == BSP_OK; ++queued) st = queue_inputs(queued);
     for (size_t k = 0; k < nj && st == BSP_OK; ++k) {
-      // 2. keep the copy engine one job ahead: the inputs of job k + 1 go in
-      //    before job k's tables, so that waiting for plan k never idles it
-      for (; queued <= k + 1 && queued < nj && st == BSP_OK; ++queued) st = queue_inputs(queued);
-      if (st != BSP_OK) return st;
       join_upto(k);
       bsp_spmm_plan* p = plans[k];
       p->blob_borrowed = true;  // after planning: the planner may replace the plan object (CTA pairs)
       if (pst[k] != BSP_OK) return set_error(pst[k], "job " + std::to_string(k) + ": " + pmsg[k]);
-      // 3. job k's tables (and split-K partials) in its slot, copied in
-      //    behind its inputs on the same stream
+      // 3. job k's tables (and split-K partials) in its slot; the tables are
+      //    fetched from mapped pinned memory by a small kernel on the compute
+      //    stream, not queued behind the input copies on the copy engine
       std::vector<int32_t> zeros;
       const auto parts = spmm_table_parts(*p, &zeros);
       size_t tb = 0;
@@ -904,7 +913,7 @@ bsp_status bsp_spmm_host_batch(bsp_device* dev, int32_t n_jobs, const bsp_spmm_h
         if (sl.h) cudaFreeHost(sl.h);
         sl.h = nullptr;
         sl.h_bytes = 0;
-        if (cudaHostAlloc(&sl.h, tb, cudaHostAllocDefault) != cudaSuccess)
+        if (cudaHostAlloc(&sl.h, tb, cudaHostAllocMapped) != cudaSuccess)
           return set_error(BSP_ERR_ALLOC, "cudaHostAlloc of a batch slot failed");
         sl.h_bytes = tb;
       }
@@ -918,10 +927,14 @@ bsp_status bsp_spmm_host_batch(bsp_device* dev, int32_t n_jobs, const bsp_spmm_h
       spmm_bind_tables(p, ptrs);
       p->d_blob = sl.d;
       if (sw) p->d_split_ws = reinterpret_cast<float*>(static_cast<uint8_t*>(sl.d) + tb);
-      st = cuda_check(cudaMemcpyAsync(sl.d, sl.h, tb, cudaMemcpyHostToDevice, sh), "upload plan tables");
-      if (st == BSP_OK) st = cuda_check(cudaEventRecord(dev->ev_in[k], sh), "cudaEventRecord");
-      // 4. job k's kernel once its inputs and tables are in; its C goes out
-      //    while the later jobs' inputs still come in (copies run both ways)
+      void* h_dev = nullptr;
+      st = cuda_check(cudaHostGetDevicePointer(&h_dev, sl.h, 0), "cudaHostGetDevicePointer");
+      if (st != BSP_OK) return st;
+      fetch_mapped_words<<<static_cast<unsigned>(std::max(1, dev->sm_count)), 256, 0, sc>>>(
+          static_cast<uint4*>(sl.d), static_cast<const uint4*>(h_dev), tb / 16);
+      st = cuda_check(cudaGetLastError(), "plan table fetch");
+      // 4. job k's kernel once its inputs are in; its C goes out while the
+      //    later jobs' inputs still come in (the copies run both ways)
       const bsp_spmm_host_job& j = jobs[k];
       bsp_bsr_desc A{j.M, j.K, j.R, j.C, j.nnzb, d[k].rp, d[k].ci, d[k].val};
       if (st == BSP_OK) st = cuda_check(cudaStreamWaitEvent(sc, dev->ev_in[k], 0), "cudaStreamWaitEvent");

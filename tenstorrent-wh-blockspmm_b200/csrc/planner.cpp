@@ -50,7 +50,9 @@ int slab_height(int R) {
 // per-thread scratch (`scratch_bytes`) within 256 MB.  BSP_PLANNER_THREADS
 // overrides the count (the plans do not depend on it).
 static int planner_threads(int64_t items, int64_t min_items, int64_t scratch_bytes) {
-  int t = static_cast<int>(std::min<unsigned>(16, std::max(1u, std::thread::hardware_concurrency())));
+  // the core count is read once (the C library parses /sys on every query)
+  static const unsigned cores = std::max(1u, std::thread::hardware_concurrency());
+  int t = static_cast<int>(std::min<unsigned>(16, cores));
   if (const char* env = std::getenv("BSP_PLANNER_THREADS")) {
     const int v = std::atoi(env);
     if (v > 0) return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(v, items)));
@@ -244,15 +246,7 @@ bsp_status plan_spmm_host(bsp_spmm_plan* p, const int32_t* row_ptr, const int32_
     if (p->N <= 128) return plan_spmm_rowstack(p, row_ptr, col_idx, sm_count, max_smem, opts);
     // Both schedules without their stage lists (the choice needs only the
     // stage counts); the lists are then built for the winner alone.
-    bsp_status st1 = plan_spmm_rowstack(p, row_ptr, col_idx, sm_count, max_smem, opts, false);
-    if (st1 != BSP_OK) return plan_spmm_pair(p, row_ptr, col_idx, sm_count, max_smem, opts);
-    auto longest = [](const bsp_spmm_plan* q, int step) {
-      int64_t m = 0;
-      for (size_t c = 0; c + step < q->h_cta_stage_begin.size(); c += step)
-        m = std::max<int64_t>(m, q->h_cta_stage_begin[c + 1] - q->h_cta_stage_begin[c]);
-      return m;
-    };
-    const int64_t s1 = longest(p, 1);
+    // The two are built at once, the pair schedule on a second host thread.
     bsp_spmm_plan pair;
     pair.M = p->M;
     pair.K = p->K;
@@ -262,8 +256,20 @@ bsp_status plan_spmm_host(bsp_spmm_plan* p, const int32_t* row_ptr, const int32_
     pair.nnzb = p->nnzb;
     pair.c_type = p->c_type;
     pair.strategy = p->strategy;
-    if (plan_spmm_pair(&pair, row_ptr, col_idx, sm_count, max_smem, opts, false) != BSP_OK)
-      return rowstack_stage_lists(p);
+    bsp_status st2 = BSP_OK;
+    std::thread pair_thread(
+        [&]() { st2 = plan_spmm_pair(&pair, row_ptr, col_idx, sm_count, max_smem, opts, false); });
+    bsp_status st1 = plan_spmm_rowstack(p, row_ptr, col_idx, sm_count, max_smem, opts, false);
+    pair_thread.join();
+    if (st1 != BSP_OK) return plan_spmm_pair(p, row_ptr, col_idx, sm_count, max_smem, opts);
+    auto longest = [](const bsp_spmm_plan* q, int step) {
+      int64_t m = 0;
+      for (size_t c = 0; c + step < q->h_cta_stage_begin.size(); c += step)
+        m = std::max<int64_t>(m, q->h_cta_stage_begin[c + 1] - q->h_cta_stage_begin[c]);
+      return m;
+    };
+    const int64_t s1 = longest(p, 1);
+    if (st2 != BSP_OK) return rowstack_stage_lists(p);
     const int64_t s2 = longest(&pair, 2);  // per pair: the leader's list (both lists are equal length)
     if (4 * s2 < 5 * s1) {  // pair time ~ 0.8 x its stages vs single-CTA stages
       bsp_device* dev = p->dev;

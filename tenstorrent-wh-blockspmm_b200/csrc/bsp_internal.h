@@ -3,7 +3,6 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
-#include <stdlib.h>
 
 #include <string>
 #include <vector>
@@ -88,10 +87,6 @@ struct SpmmKernelParams {
   // leave its k-th pipeline stage unissued (no copy, no arrive), so that the
   // MMA warp's bounded wait on it runs out; 0 = off.
   int32_t debug_drop_stage;
-  // L2 prefetch distance of the row-stacked producers, in a producer's own
-  // stages: while issuing stage j it prefetches the operand tiles of its stage
-  // j + pf_dist into L2 (0 = off)
-  int32_t pf_dist;
 };
 
 // Row-stacked kernel stage descriptor (16 words), precomputed by the planner
@@ -372,7 +367,6 @@ struct bsp_spmm_plan {
   int32_t* d_split_counters = nullptr;  // in the blob (zeroed): two sets of one per slot
   mutable uint32_t launch_parity = 0;   // which counter set the next launch uses
   int32_t debug_drop_stage = 0;         // testing only, see SpmmKernelParams
-  int32_t pf_dist = 0;                  // row-stacked kernels: L2 prefetch distance (stages)
   uint64_t timeout_ns = 0;
   void* d_blob = nullptr;  // units | cta_begin | steps
   size_t blob_bytes = 0;
@@ -490,8 +484,6 @@ inline void select_split_counters(const bsp_spmm_plan* p, SpmmKernelParams& k) {
   k.split_counters = p->d_split_counters ? p->d_split_counters + par * n : nullptr;
   k.split_counters_next = p->d_split_counters ? p->d_split_counters + (par ^ 1u) * n : nullptr;
   k.debug_drop_stage = p->debug_drop_stage;
-  k.pf_dist = p->pf_dist;
-  if (const char* e = std::getenv("BSP_PREFETCH")) k.pf_dist = std::atoi(e);
   p->launch_parity ^= 1u;
 }
 }  // namespace bsp

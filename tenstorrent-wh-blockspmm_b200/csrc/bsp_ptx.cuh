@@ -159,26 +159,6 @@ __device__ __forceinline__ void tma_load_3d_pred(uint32_t smem_dst, const void* 
       : "memory");
 }
 
-// L2 prefetch of a tensor tile (no shared-memory destination, no barrier):
-// warms L2 for a later load of the same box.  Predicated on `issue`.
-__device__ __forceinline__ void tma_prefetch_2d_pred(const void* tmap, int32_t x, int32_t y, uint32_t issue) {
-  asm volatile(
-      "{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %3, 0;\n\t"
-      "@q cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];\n\t}" ::"l"(
-          reinterpret_cast<uint64_t>(tmap)),
-      "r"(x), "r"(y), "r"(issue)
-      : "memory");
-}
-__device__ __forceinline__ void tma_prefetch_3d_pred(const void* tmap, int32_t x, int32_t y, int32_t z,
-                                                     uint32_t issue) {
-  asm volatile(
-      "{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %4, 0;\n\t"
-      "@q cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];\n\t}" ::"l"(
-          reinterpret_cast<uint64_t>(tmap)),
-      "r"(x), "r"(y), "r"(z), "r"(issue)
-      : "memory");
-}
-
 __device__ __forceinline__ void tma_load_2d_hint(uint32_t smem_dst, const void* tmap, int32_t x,
                                                  int32_t y, uint32_t bar, uint64_t policy) {
   asm volatile(

@@ -93,35 +93,6 @@ __device__ __forceinline__ void pr_producer(const SpmmKernelParams& p, RsSmemHea
 #pragma unroll
       for (int i = 1; i < 8; ++i)
         if (lane == i) my_ay = ay[i];
-      if (p.pf_dist > 0) {
-        // warm L2 for this producer's stage j + pf_dist of the current batch:
-        // lanes 0..7 its present A blocks, lanes 8/9 the B halves of its sub-steps
-        const int jf = j + p.pf_dist;
-        const int src = jf & 31;
-        const uint32_t ff = static_cast<uint32_t>(__shfl_sync(0xffffffffu, w0.x, src));
-        const int fbz = __shfl_sync(0xffffffffu, w0.y, src);
-        const int fax = __shfl_sync(0xffffffffu, w0.z, src);
-        const int fky0 = __shfl_sync(0xffffffffu, w0.w, src);
-        const int fky1 = __shfl_sync(0xffffffffu, w1.x, src);
-        int fay = __shfl_sync(0xffffffffu, w1.y, src);
-        const int fa1 = __shfl_sync(0xffffffffu, w1.z, src);
-        const int fa2 = __shfl_sync(0xffffffffu, w1.w, src);
-        const int fa3 = __shfl_sync(0xffffffffu, w2.x, src);
-        const int fa4 = __shfl_sync(0xffffffffu, w2.y, src);
-        const int fa5 = __shfl_sync(0xffffffffu, w2.z, src);
-        const int fa6 = __shfl_sync(0xffffffffu, w2.w, src);
-        const int fa7 = __shfl_sync(0xffffffffu, w3.x, src);
-        fay = lane == 1 ? fa1 : lane == 2 ? fa2 : lane == 3 ? fa3 : lane == 4 ? fa4 : lane == 5 ? fa5
-              : lane == 6 ? fa6 : lane == 7 ? fa7 : fay;
-        const bool fon = jf < cnt && !(ff & RS_EMPTY);
-        const uint32_t fsub = (ff & RS_TWO) ? 2u : 1u;
-        const bool aon = fon && lane < 8 && (lane & 3) < G && static_cast<uint32_t>(lane >> 2) < fsub && fay >= 0;
-        tma_prefetch_2d_pred(&p.tm_a, fax, fay, aon ? 1u : 0u);
-        if (p.b3d) {
-          const bool bon = fon && (lane == 8 || lane == 9) && static_cast<uint32_t>(lane - 8) < fsub;
-          tma_prefetch_3d_pred(&p.tm_b, 0, lane == 9 ? fky1 : fky0, fbz, bon ? 1u : 0u);
-        }
-      }
       const uint32_t sb = stage0 + static_cast<uint32_t>(stage) * p.stage_bytes;
       const uint32_t full_local = baddr(&hdr->full[stage]);
       const uint32_t full = mapa_shared(full_local, 0);

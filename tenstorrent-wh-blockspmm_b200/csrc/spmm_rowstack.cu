@@ -101,36 +101,6 @@ __device__ __forceinline__ void rs_producer(const SpmmKernelParams& p, RsSmemHea
         }
         fence_proxy_async_smem();
       }
-      if (p.pf_dist > 0) {
-        // warm L2 for this producer's stage j + pf_dist of the current batch
-        // (lane 0/1: the B slices of its two sub-steps; lanes 8..15: its A blocks)
-        const int jf = j + p.pf_dist;
-        const int src = jf & 31;
-        const uint32_t ff = static_cast<uint32_t>(__shfl_sync(0xffffffffu, w0.x, src));
-        const int fbz = __shfl_sync(0xffffffffu, w0.y, src);
-        const int fax = __shfl_sync(0xffffffffu, w0.z, src);
-        const int fky0 = __shfl_sync(0xffffffffu, w0.w, src);
-        const int fky1 = __shfl_sync(0xffffffffu, w1.x, src);
-        int fay = __shfl_sync(0xffffffffu, w1.y, src);
-        const int fa1 = __shfl_sync(0xffffffffu, w1.z, src);
-        const int fa2 = __shfl_sync(0xffffffffu, w1.w, src);
-        const int fa3 = __shfl_sync(0xffffffffu, w2.x, src);
-        const int fa4 = __shfl_sync(0xffffffffu, w2.y, src);
-        const int fa5 = __shfl_sync(0xffffffffu, w2.z, src);
-        const int fa6 = __shfl_sync(0xffffffffu, w2.w, src);
-        const int fa7 = __shfl_sync(0xffffffffu, w3.x, src);
-        const int ai = lane - 8;
-        fay = ai == 1 ? fa1 : ai == 2 ? fa2 : ai == 3 ? fa3 : ai == 4 ? fa4 : ai == 5 ? fa5 : ai == 6 ? fa6
-              : ai == 7 ? fa7 : fay;
-        const bool fon = jf < cnt && !(ff & RS_EMPTY);
-        const uint32_t fsub = (ff & RS_TWO) ? 2u : 1u;
-        if (p.b3d) {
-          const bool bon = fon && lane < 2 && static_cast<uint32_t>(lane) < fsub;
-          tma_prefetch_3d_pred(&p.tm_b, 0, lane == 1 ? fky1 : fky0, fbz, bon ? 1u : 0u);
-        }
-        const bool aon = fon && ai >= 0 && ai < 8 && ((ff >> ai) & 1u) && static_cast<uint32_t>(ai >> 2) < fsub;
-        tma_prefetch_2d_pred(&p.tm_a, fax, fay, aon ? 1u : 0u);
-      }
       // coordinates of this stage (all lanes take part in the shuffles)
       const int bz = __shfl_sync(0xffffffffu, w0.y, j);
       const int ax = __shfl_sync(0xffffffffu, w0.z, j);

@@ -627,8 +627,8 @@ class DevOp:
             return "spgemm_tcgen05"
         if self.kind == "sddmm":
             return "sddmm_rowstack_tcgen05" if self.plan.info().get("variant", 0) == 1 else "sddmm_bsr_tcgen05"
-        return {1: "spmm_rowstack_tcgen05", 2: "spmm_pair_tcgen05"}.get(self.plan.info().get("variant", 0),
-                                                                      "spmm_bsr_tcgen05")
+        return {1: "spmm_rowstack_tcgen05", 2: "spmm_pair_tcgen05", 3: "spmm_twin_tcgen05"}.get(
+            self.plan.info().get("variant", 0), "spmm_bsr_tcgen05")
 
     def close(self):
         self.plan.close()

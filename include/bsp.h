@@ -96,9 +96,12 @@ typedef struct bsp_spmm_opts {
   int32_t n_tiles;         /* SNF/DDA: 128-column tiles per work unit (A reuse) */
   int32_t max_ctas;        /* cap on persistent CTAs (default: all SMs) */
   int32_t timeout_ms;      /* bound on every in-kernel wait (default 2000) */
-  int32_t group_mma;       /* DDA: 1 (default) one MMA over the row group's stacked
-                              blocks, absent blocks zero-filled; 2 one MMA per
-                              present block */
+  int32_t group_mma;       /* DDA: 0/1 (default) the planner's choice of the
+                              row-stacked kernels; 2 one MMA per present block
+                              (swap-AB); 4 single-CTA row stacks; 5 row stacks
+                              on CTA pairs; 6 twin units on CTA pairs (two row
+                              groups of one column tile share each B slice;
+                              32-wide blocks and N > 128, else as 5) */
   int32_t producers;       /* TMA-issuing warps per CTA (default: as many as fit) */
   int32_t steps_per_stage; /* DDA: block-columns per pipeline stage, 1 or 2
                               (default 2 for 32-wide blocks, else 1) */
@@ -196,7 +199,7 @@ bsp_status bsp_ipc_close(bsp_device* dev, void* base);
  * kernel) [1]=ctas [2]=entries per CTA [3]=n_tiles [4]=sub-row height
  * [5]=k chunk [6]=pipeline stages [7]=steps [8]=plan device bytes [9]=shared
  * memory per CTA [10]=TMEM columns [11]=kernel variant (0 swap-AB, 1 row-
- * stacked, 2 row-stacked on CTA pairs) [12]=producer warps [15]=int32 words
+ * stacked, 2 row-stacked on CTA pairs, 3 twin units on CTA pairs) [12]=producer warps [15]=int32 words
  * per step-table entry. */
 bsp_status bsp_spmm_plan_info(const bsp_spmm_plan* plan, int64_t info[16]);
 

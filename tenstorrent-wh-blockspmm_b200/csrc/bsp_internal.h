@@ -108,6 +108,25 @@ enum : int32_t {
 };
 constexpr int kRsStageWords = 16;
 
+// Twin stage descriptor (CTA-pair kernel, variant 3): a stage is one
+// block-column of a twin, two pair units (a: entries 0..3, b: 4..7 of this
+// CTA) of the same column tile stepping through the union of their columns
+// and sharing each B slice.
+//   w[0] flags: bits 0-7 entry slots to load (present block or zero box),
+//        TW_F_* bits below
+//   w[1] bz: first 64-column block of this CTA's half of the tile
+//   w[3] ky: B row of the block-column (column * 32)
+//   w[4..11] ay[s]: A row of slot s's block slab, or -32 (zero box)
+enum : int32_t {
+  TW_F_MMA_A = 1 << 8,     // unit a multiplies at this stage
+  TW_F_MMA_B = 1 << 9,     // unit b multiplies at this stage
+  TW_F_FIRST_A = 1 << 16,  // first stage of unit a (its accumulator starts)
+  TW_F_LAST_A = 1 << 17,   // last stage of unit a (its accumulator is complete)
+  TW_F_FIRST_B = 1 << 18,
+  TW_F_LAST_B = 1 << 19,
+  TW_F_EMPTY = 1 << 20,    // nothing to load or multiply (both units without blocks)
+};
+
 // ---- SDDMM schedule ---------------------------------------------------------
 // One unit = one block-row slab (Rs rows) x up to 4 output segments, each 32
 // consecutive output columns of one mask block.
@@ -454,6 +473,11 @@ bsp_status launch_spmm_rowstack(const bsp_spmm_plan* p, const bsp_bsr_desc* A, c
                                 void* const* peer_c = nullptr, int n_peers = 0);
 // stage_lists false: units and per-CTA stage counts only (h_stage_list empty)
 bsp_status plan_spmm_pair(bsp_spmm_plan* p, const int32_t* row_ptr, const int32_t* col_idx,
+                          int sm_count, int max_smem, const bsp_spmm_opts* opts, bool stage_lists = true);
+// twin units on CTA pairs (variant 3): 32 x 32-wide blocks (C == 32,
+// R % 32 == 0) and N > 128; the caller falls back to plan_spmm_pair otherwise
+bool spmm_twin_eligible(const bsp_spmm_plan* p);
+bsp_status plan_spmm_twin(bsp_spmm_plan* p, const int32_t* row_ptr, const int32_t* col_idx,
                           int sm_count, int max_smem, const bsp_spmm_opts* opts, bool stage_lists = true);
 bsp_status launch_spmm_pair(const bsp_spmm_plan* p, const bsp_bsr_desc* A, const void* B, int64_t ldb,
                             void* C, int64_t ldc, cudaStream_t stream, void* const* peer_c = nullptr,

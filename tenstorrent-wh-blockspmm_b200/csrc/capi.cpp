@@ -472,7 +472,7 @@ static void spmm_bind_tables(bsp_spmm_plan* p, const std::vector<void*>& ptrs) {
 // Bytes of the split-K partial tiles: 128 rows x the tile's accumulator
 // columns, fp32, per workspace slot.
 static size_t spmm_split_ws_bytes(const bsp_spmm_plan& p) {
-  const int64_t acc_cols = p.variant == 2 ? 256 : 128 * p.NT;
+  const int64_t acc_cols = p.variant >= 2 ? 256 : 128 * p.NT;
   return sizeof(float) * 128 * static_cast<size_t>(acc_cols) * static_cast<size_t>(p.n_split_slots);
 }
 
@@ -550,7 +550,7 @@ bsp_status bsp_spmm_execute(const bsp_spmm_plan* plan, const bsp_bsr_desc* A, co
     return set_error(BSP_ERR_INVALID_ARG, "A does not match the plan's pattern");
   if (ldb < plan->N || ldc < plan->N)
     return set_error(BSP_ERR_INVALID_ARG, "leading dimensions must be >= N");
-  if (plan->variant == 2)
+  if (plan->variant == 2 || plan->variant == 3)
     return launch_spmm_pair(plan, A, B, ldb, C, ldc, static_cast<cudaStream_t>(stream));
   if (plan->variant == 1)
     return launch_spmm_rowstack(plan, A, B, ldb, C, ldc, static_cast<cudaStream_t>(stream));
@@ -568,7 +568,7 @@ bsp_status bsp_spmm_execute_replicated(const bsp_spmm_plan* plan, const bsp_bsr_
     return set_error(BSP_ERR_INVALID_ARG, "A does not match the plan's pattern");
   if (ldb < plan->N || ldc < plan->N)
     return set_error(BSP_ERR_INVALID_ARG, "leading dimensions must be >= N");
-  if (plan->variant == 2)
+  if (plan->variant == 2 || plan->variant == 3)
     return launch_spmm_pair(plan, A, B, ldb, C, ldc, static_cast<cudaStream_t>(stream), peer_C, n_peers);
   if (plan->variant != 1)
     return set_error(BSP_ERR_UNSUPPORTED, "replicated output needs a DDA (row-stacked) plan");

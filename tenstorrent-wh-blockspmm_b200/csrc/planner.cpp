@@ -241,6 +241,9 @@ bsp_status plan_spmm_host(bsp_spmm_plan* p, const int32_t* row_ptr, const int32_
   if (p->strategy == BSP_DDA && o.group_mma != 2 && o.group_mma != 3) {
     if (o.group_mma == 4 || sm_count < 2) return plan_spmm_rowstack(p, row_ptr, col_idx, sm_count, max_smem, opts);
     if (o.group_mma == 5) return plan_spmm_pair(p, row_ptr, col_idx, sm_count, max_smem, opts);
+    if (o.group_mma == 6)
+      return spmm_twin_eligible(p) ? plan_spmm_twin(p, row_ptr, col_idx, sm_count, max_smem, opts)
+                                   : plan_spmm_pair(p, row_ptr, col_idx, sm_count, max_smem, opts);
     // a pair CTA loads one 128-column half of a 256-column tile: with N <= 128
     // one of the two would load nothing but out-of-range zeros
     if (p->N <= 128) return plan_spmm_rowstack(p, row_ptr, col_idx, sm_count, max_smem, opts);
@@ -1074,6 +1077,241 @@ static bsp_status pair_stage_lists(bsp_spmm_plan* p) {
           if (nin == 2) flags |= RS_F_TWO;
           e[0] = static_cast<int32_t>(flags);
           e[1] = b3d ? u.n0 / 64 + 2 * r : u.n0 + 128 * r;
+          memcpy(out, e, sizeof(e));
+          out += W;
+        }
+      }
+    }
+    return BSP_OK;
+  });
+}
+
+// ---- twin units on CTA pairs (variant 3) -------------------------------------
+bool spmm_twin_eligible(const bsp_spmm_plan* p) { return p->C == 32 && p->R % 32 == 0 && p->N > 128; }
+
+// Two pair units (row groups g and g + 1 of 8 entries, the same 256-column
+// tile) run as one work item on a CTA pair: their steps are the union of
+// their columns, each B slice is loaded once for both, and each unit keeps
+// its own accumulator (TMEM columns 0-255 and 256-511 of both CTAs).  A unit
+// multiplies only at the columns where one of its entries holds a block; its
+// absent entries of such a column are zero boxes.  Items are dealt longest
+// first to the least-loaded pair.
+bsp_status plan_spmm_twin(bsp_spmm_plan* p, const int32_t* row_ptr, const int32_t* col_idx,
+                          int sm_count, int max_smem, const bsp_spmm_opts* opts, bool stage_lists) {
+  bsp_spmm_opts o;
+  memset(&o, 0, sizeof(o));
+  if (opts) o = *opts;
+  const int R = p->R, Rs = 32, slabs = R / 32, G = 4, G2 = 8;
+  const int64_t nbr = p->M / R;
+  const int64_t n_entries = nbr * slabs;
+  const int ntiles = static_cast<int>((p->N + 255) / 256);
+  if (n_entries >= (int64_t(1) << 31)) return set_error(BSP_ERR_UNSUPPORTED, "too many block-rows");
+  p->variant = 3;
+  p->Rs = Rs;
+  p->kc = 32;
+  p->G = G;
+  p->NT = 2;
+  p->stacked = 1;
+  p->nsub = 1;
+  const int stride = 1 + 2 * G2;  // column, then the block of each of the 16 entries (or -1)
+  p->step_stride = stride;
+  p->n_split_slots = 0;
+  p->split_units = 0;
+  std::vector<int32_t>& steps = p->h_steps;
+  steps.clear();
+  struct Twin {
+    int64_t e0;      // first entry of unit a (unit b: e0 + 8)
+    int nent_a, nent_b;
+    int32_t s_begin, s_end, n0;
+    int32_t mask;    // present entries: bits 0-7 unit a, 8-15 unit b
+  };
+  std::vector<Twin> twins;
+  std::vector<int64_t> weight;
+  const int esz = p->c_type == BSP_F32 ? 4 : 2;
+  std::vector<std::pair<int32_t, int32_t>> items;
+  std::vector<int8_t> item_g;
+  for (int64_t e0 = 0; e0 < n_entries; e0 += 2 * G2) {
+    const int nent = static_cast<int>(std::min<int64_t>(2 * G2, n_entries - e0));
+    const int32_t s_begin = static_cast<int32_t>(steps.size() / stride);
+    int32_t mask = 0;
+    int64_t mmas = 0;
+    items.clear();
+    item_g.clear();
+    for (int g = 0; g < nent; ++g) {
+      const int64_t i = (e0 + g) / slabs;
+      if (row_ptr[i + 1] > row_ptr[i]) mask |= 1 << g;
+      for (int32_t b = row_ptr[i]; b < row_ptr[i + 1]; ++b) {
+        items.push_back({col_idx[b], b});
+        item_g.push_back(static_cast<int8_t>(g));
+      }
+    }
+    std::vector<int32_t> order(items.size());
+    std::iota(order.begin(), order.end(), 0);
+    std::stable_sort(order.begin(), order.end(),
+                     [&](int32_t a, int32_t b) { return items[a].first < items[b].first; });
+    int64_t cur = -1;
+    for (int32_t k : order) {
+      const int g = item_g[k];
+      // a column repeated in a row of an entry opens a further step
+      const bool open = cur >= 0 && steps[cur * stride] == items[k].first && steps[cur * stride + 1 + g] < 0;
+      if (!open) {
+        cur = static_cast<int64_t>(steps.size() / stride);
+        steps.push_back(items[k].first);
+        for (int q = 0; q < 2 * G2; ++q) steps.push_back(-1);
+      }
+      steps[cur * stride + 1 + g] = items[k].second;
+    }
+    const int32_t s_end = static_cast<int32_t>(steps.size() / stride);
+    for (int32_t s = s_begin; s < s_end; ++s) {
+      bool ua = false, ub = false;
+      for (int g = 0; g < G2; ++g) ua |= steps[static_cast<size_t>(s) * stride + 1 + g] >= 0;
+      for (int g = G2; g < 2 * G2; ++g) ub |= steps[static_cast<size_t>(s) * stride + 1 + g] >= 0;
+      mmas += (ua ? 1 : 0) + (ub ? 1 : 0);
+    }
+    for (int t = 0; t < ntiles; ++t) {
+      twins.push_back({e0, std::min(nent, G2), std::max(0, nent - G2), s_begin, s_end, t * 256, mask});
+      // per step: both units' MMAs (~2 x 156 cycles each) vs the stage's
+      // staging; per item: two 128 x 256 tiles of C per CTA
+      weight.push_back(mmas * 2 * 32 * 128 * 2 + int64_t(s_end - s_begin) * 8192 + 2 * int64_t(G) * Rs * 256 * esz +
+                       8192);
+    }
+  }
+  p->n_steps = static_cast<int64_t>(steps.size() / stride);
+  int npairs = (o.max_ctas > 0 ? std::min(o.max_ctas, sm_count) : sm_count) / 2;
+  npairs = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(npairs, twins.size())));
+  std::vector<std::vector<int32_t>> per;
+  if (o.no_load_balance)
+    contiguous_split(static_cast<int64_t>(twins.size()), npairs, &per);
+  else
+    lpt_order(weight, npairs, &per);
+  // ring: one block-column per stage, B half (8 KB) + 8 entry slots (2 KB each)
+  const int a_slot = Rs * 32 * 2;
+  const int stage_bytes = 2 * 32 * 128 + G2 * a_slot;
+  p->sub_bytes = stage_bytes;
+  const int max_stages = std::min(rowstack_max_stages(), (max_smem - 2048 - 16384) / stage_bytes);
+  if (max_stages < 2) return set_error(BSP_ERR_UNSUPPORTED, "twin stages do not fit in shared memory");
+  int nprod = 1, stages = max_stages;
+  if (o.producers > 0) {
+    nprod = std::min({o.producers, rowstack_max_producers(), max_stages});
+    stages = max_stages / nprod * nprod;
+  } else {
+    for (int q = 2; q <= std::min(rowstack_max_producers(), max_stages); ++q) {
+      const int sq = max_stages / q * q;
+      if (sq >= stages - (stages > 6 ? 1 : 0)) {
+        nprod = q;
+        stages = sq;
+      }
+    }
+  }
+  p->nprod = nprod;
+  p->stage_bytes = stage_bytes;
+  p->stages = stages;
+  p->xfer_off = 1024 + stages * stage_bytes;  // staging for replicated launches
+  p->smem_bytes = 2048 + stages * stage_bytes + 16384;
+  p->tmem_cols = 512;
+  p->timeout_ns = static_cast<uint64_t>(o.timeout_ms > 0 ? o.timeout_ms : 2000) * 1000000ull;
+  p->grid = 2 * npairs;
+  // per CTA: the unit records of its twins in order, unit a then unit b (the
+  // epilogue alternates accumulators 0 / 1 with them); both carry the twin's
+  // step range
+  p->h_units.clear();
+  p->h_cta_begin.assign(1, 0);
+  for (int c = 0; c < npairs; ++c) {
+    for (int r = 0; r < 2; ++r) {
+      for (int32_t idx : per[c]) {
+        const Twin& tw = twins[idx];
+        for (int x = 0; x < 2; ++x) {
+          const int nent = x ? tw.nent_b : tw.nent_a;
+          SpmmUnit u;
+          u.row0 = static_cast<int32_t>(tw.e0 + x * G2 + r * G);
+          u.nrows = std::max(0, std::min(G, nent - r * G));
+          u.r_off = 0;
+          u.n0 = tw.n0;
+          u.nt = 1;
+          u.step_begin = tw.s_begin;
+          u.step_end = tw.s_end;
+          u.row_mask = (tw.mask >> (x * G2 + r * G)) & ((1 << G) - 1);
+          p->h_units.push_back(u);
+        }
+      }
+      p->h_cta_begin.push_back(static_cast<int32_t>(p->h_units.size()));
+    }
+  }
+  if (steps.empty()) {
+    steps.push_back(0);
+    for (int q = 0; q < 2 * G2; ++q) steps.push_back(-1);
+  }
+  p->n_units = static_cast<int64_t>(p->h_units.size());
+  // stage counts: one stage per union step of each twin (one for an empty twin)
+  p->h_cta_stage_begin.assign(1, 0);
+  p->h_stage_list.clear();
+  int64_t total = 0;
+  for (size_t c = 0; c + 1 < p->h_cta_begin.size(); ++c) {
+    for (int32_t ui = p->h_cta_begin[c]; ui < p->h_cta_begin[c + 1]; ui += 2) {
+      const int64_t n = p->h_units[ui].step_end - p->h_units[ui].step_begin;
+      total += n == 0 ? 1 : n;
+    }
+    if (total >= (int64_t(1) << 31)) return set_error(BSP_ERR_UNSUPPORTED, "schedule too long");
+    p->h_cta_stage_begin.push_back(static_cast<int32_t>(total));
+  }
+  if (!stage_lists) return BSP_OK;
+  const int W = kRsStageWords;
+  const bool b3d = (p->N % 64 == 0);
+  const int64_t grid = static_cast<int64_t>(p->h_cta_begin.size()) - 1;
+  p->h_stage_list.resize(static_cast<size_t>(p->h_cta_stage_begin.back()) * W);
+  return parallel_ranges(grid, planner_threads(grid, 4, 0), [&](int, int64_t c0, int64_t c1) {
+    for (int64_t cta = c0; cta < c1; ++cta) {
+      const int r = static_cast<int>(cta % 2);
+      int32_t* out = p->h_stage_list.data() + static_cast<size_t>(p->h_cta_stage_begin[cta]) * W;
+      for (int32_t ui = p->h_cta_begin[cta]; ui < p->h_cta_begin[cta + 1]; ui += 2) {
+        const SpmmUnit& ua = p->h_units[ui];
+        const int nsteps = ua.step_end - ua.step_begin;
+        const int32_t bz = b3d ? ua.n0 / 64 + 2 * r : ua.n0 + 128 * r;
+        if (nsteps == 0) {
+          int32_t e[kRsStageWords] = {TW_F_FIRST_A | TW_F_LAST_A | TW_F_FIRST_B | TW_F_LAST_B | TW_F_EMPTY, bz};
+          memcpy(out, e, sizeof(e));
+          out += W;
+          continue;
+        }
+        // each unit's first and last multiplying step (pair-wide: all 8 entries)
+        int first[2] = {-1, -1}, last[2] = {-1, -1};
+        for (int s = 0; s < nsteps; ++s) {
+          const int32_t* st = &steps[static_cast<size_t>(ua.step_begin + s) * stride];
+          for (int x = 0; x < 2; ++x) {
+            bool any = false;
+            for (int g = 0; g < G2; ++g) any |= st[1 + x * G2 + g] >= 0;
+            if (any) {
+              if (first[x] < 0) first[x] = s;
+              last[x] = s;
+            }
+          }
+        }
+        for (int s = 0; s < nsteps; ++s) {
+          const int32_t* st = &steps[static_cast<size_t>(ua.step_begin + s) * stride];
+          int32_t e[kRsStageWords];
+          for (int q = 0; q < W; ++q) e[q] = 0;
+          uint32_t flags = 0;
+          for (int x = 0; x < 2; ++x) {
+            // a unit without blocks opens and closes on the twin's first stage
+            const bool fx = first[x] < 0 ? s == 0 : s == first[x];
+            const bool lx = first[x] < 0 ? s == 0 : s == last[x];
+            if (fx) flags |= x ? TW_F_FIRST_B : TW_F_FIRST_A;
+            if (lx) flags |= x ? TW_F_LAST_B : TW_F_LAST_A;
+            bool any = false;
+            for (int g = 0; g < G2; ++g) any |= st[1 + x * G2 + g] >= 0;
+            if (!any) continue;
+            flags |= x ? TW_F_MMA_B : TW_F_MMA_A;
+            const SpmmUnit& u = p->h_units[ui + x];
+            for (int g = 0; g < G; ++g) {
+              const int slot = 4 * x + g;
+              flags |= 1u << slot;
+              const int32_t blk = g < u.nrows ? st[1 + x * G2 + r * G + g] : -1;
+              e[4 + slot] = blk >= 0 ? blk * R + static_cast<int>((u.row0 + g) % slabs) * Rs : -Rs;
+            }
+          }
+          e[0] = static_cast<int32_t>(flags);
+          e[1] = bz;
+          e[3] = st[0] * 32;
           memcpy(out, e, sizeof(e));
           out += W;
         }
@@ -2028,6 +2266,22 @@ void spmm_plan_traffic(const bsp_spmm_plan& p, int64_t out[4]) {
     return;
   }
   const size_t W = kRsStageWords;
+  if (p.variant == 3) {
+    // twins: one block-column per stage; this CTA's B half, and the A slots
+    // of the units that multiply there (present blocks; zero boxes not counted)
+    for (size_t k = 0; k + W <= p.h_stage_list.size(); k += W) {
+      const uint32_t flags = static_cast<uint32_t>(p.h_stage_list[k]);
+      if (flags & TW_F_EMPTY) continue;
+      out[1] += kc * 128 * 2;
+      out[3] += 2;
+      for (int s = 0; s < 8; ++s)
+        if (((flags >> s) & 1u) && p.h_stage_list[k + 4 + s] >= 0) {
+          out[0] += Rs * kc * 2;
+          out[2] += 1;
+        }
+    }
+    return;
+  }
   const int64_t b_cols = p.variant == 2 ? 128 : 128 * p.NT;  // a pair CTA loads half of the 256 columns
   for (size_t k = 0; k + W <= p.h_stage_list.size(); k += W) {
     const uint32_t flags = static_cast<uint32_t>(p.h_stage_list[k]);

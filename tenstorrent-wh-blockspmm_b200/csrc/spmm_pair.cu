@@ -292,6 +292,245 @@ __global__ void __launch_bounds__(kRsThreads, 1) spmm_pair_tcgen05(const __grid_
   }
 }
 
+// ---- twin units (variant 3) ---------------------------------------------------
+// Two pair units of one column tile share every B slice: a stage is one
+// block-column (this CTA's B half, then unit a's four entry slots, then unit
+// b's); each unit multiplies into its own accumulator (TMEM columns 0-255 /
+// 256-511) at the columns where it holds a block.  One B load thus serves up
+// to twice the MMA work of a plain pair stage in the same shared memory.
+
+// Producer warp pw of CTA `rank`: stages pw, pw + nprod, ... of the twin sequence.
+__device__ __forceinline__ void tw_producer(const SpmmKernelParams& p, RsSmemHeader* hdr, uint32_t stage0,
+                                           const WaitCtl& ctl, int pw, int lane, uint32_t rank) {
+  const int P = p.nprod;
+  const int k_begin = p.cta_stage_begin[blockIdx.x];
+  const int n = p.cta_stage_begin[blockIdx.x + 1] - k_begin;
+  const uint32_t a_slot = static_cast<uint32_t>(p.Rs * p.kc * 2);
+  const uint32_t b_half = static_cast<uint32_t>(2 * p.kc * 128);
+  const uint32_t is0 = (lane == 0 && rank == 0) ? 1u : 0u;
+  int stage = pw;
+  uint32_t phase = 0;
+  uint32_t armed = 0, armed_parity = 0;
+  bool ok = true;
+#pragma unroll 1
+  for (int k0 = pw; k0 < n && ok; k0 += 32 * P) {
+    int4 w0 = make_int4(0, 0, 0, 0), w1 = w0, w2 = w0;
+    const int kl = k0 + lane * P;
+    if (kl < n) {
+      const int4* e = p.stage_list + 4 * static_cast<size_t>(k_begin + kl);
+      w0 = __ldg(e);
+      w1 = __ldg(e + 1);
+      w2 = __ldg(e + 2);
+    }
+    const int cnt = min(32, (n - k0 + P - 1) / P);
+#pragma unroll 1
+    for (int j = 0; j < cnt; ++j) {
+      const uint32_t flags = static_cast<uint32_t>(__shfl_sync(0xffffffffu, w0.x, j));
+      ok = __all_sync(0xffffffffu, mbar_wait_bounded(baddr(&hdr->empty[stage]), phase ^ 1u, ctl,
+                                                     ST_TIMEOUT_PRODUCER));
+      if (!ok) break;
+      const int bz = __shfl_sync(0xffffffffu, w0.y, j);
+      const int ky = __shfl_sync(0xffffffffu, w0.w, j);
+      int ay = __shfl_sync(0xffffffffu, w1.x, j);  // slots 0..7 from w1.x .. w2.w
+      const int a1 = __shfl_sync(0xffffffffu, w1.y, j);
+      const int a2 = __shfl_sync(0xffffffffu, w1.z, j);
+      const int a3 = __shfl_sync(0xffffffffu, w1.w, j);
+      const int a4 = __shfl_sync(0xffffffffu, w2.x, j);
+      const int a5 = __shfl_sync(0xffffffffu, w2.y, j);
+      const int a6 = __shfl_sync(0xffffffffu, w2.z, j);
+      const int a7 = __shfl_sync(0xffffffffu, w2.w, j);
+      ay = lane == 1 ? a1 : lane == 2 ? a2 : lane == 3 ? a3 : lane == 4 ? a4 : lane == 5 ? a5 : lane == 6 ? a6
+           : lane == 7 ? a7 : ay;
+      const uint32_t sb = stage0 + static_cast<uint32_t>(stage) * p.stage_bytes;
+      const uint32_t full_local = baddr(&hdr->full[stage]);
+      const uint32_t full = mapa_shared(full_local, 0);
+      if (rank == 0 && lane == 0) hdr->info[stage] = flags;
+      __syncwarp();
+      const uint32_t loads = (flags & TW_F_EMPTY) ? 0u : (flags & 0xFFu);
+      // bytes both CTAs land on the leader's full barrier (the same slot
+      // pattern in both: a unit multiplies, or not, on both halves)
+      const uint32_t tx = (flags & TW_F_EMPTY) ? 0u : 2u * (b_half + static_cast<uint32_t>(__popc(loads)) * a_slot);
+      mbar_arrive_expect_tx_pred(full_local, tx, is0);
+      if (!(flags & TW_F_EMPTY)) {
+        const bool a_on = lane < 8 && ((loads >> lane) & 1u);
+        tma_load_2d_pair_pred(sb + b_half + static_cast<uint32_t>(lane & 7) * a_slot, &p.tm_a, 0, ay, full,
+                              a_on ? 1u : 0u);
+        if (p.b3d) {
+          tma_load_3d_pair_pred(sb, &p.tm_b, 0, ky, bz, full, lane == 8 ? 1u : 0u);
+        } else {
+          const bool b_on = lane == 8 || lane == 9;
+          tma_load_2d_pair_pred(sb + static_cast<uint32_t>(lane & 1) * (b_half / 2), &p.tm_b, bz + (lane & 1) * 64, ky,
+                                full, b_on ? 1u : 0u);
+        }
+      }
+      armed |= 1u << stage;
+      armed_parity = (armed_parity & ~(1u << stage)) | (phase << stage);
+      stage += P;
+      if (stage >= p.stages) {
+        stage -= p.stages;
+        phase ^= 1u;
+      }
+    }
+  }
+  if (rank == 0 && lane == 0) {
+#pragma unroll 1
+    for (int s = 0; s < p.stages; ++s)
+      if (armed & (1u << s)) rs_drain_wait(baddr(&hdr->full[s]), (armed_parity >> s) & 1u, ctl);
+  }
+  if (lane == 0) {
+#pragma unroll 1
+    for (int s = 0; s < p.stages; ++s)
+      if (armed & (1u << s)) rs_drain_wait(baddr(&hdr->empty[s]), (armed_parity >> s) & 1u, ctl);
+  }
+  __syncwarp();
+}
+
+// MMA warp of the leader: for each stage, each unit that multiplies there
+// issues its two k-steps into its accumulator; the stage is released by one
+// commit (both CTAs) when any MMA was issued, by plain arrives otherwise.
+__device__ __forceinline__ void tw_mma(const SpmmKernelParams& p, RsSmemHeader* hdr, uint32_t stage0,
+                                      uint32_t tmem_base, int n_units, const WaitCtl& ctl, int lane) {
+  int stage = 0;
+  uint32_t phase = 0;
+  uint32_t acc_phase[2] = {0u, 0u};
+  bool started[2] = {false, false};
+  bool any_mma[2] = {false, false};
+  int units_left = n_units;
+  const uint32_t idesc = idesc_bf16_f32(256, kRsN, /*a K-major*/ 0, /*b MN-major*/ 1);
+  const uint32_t b_half = static_cast<uint32_t>(2 * p.kc * 128);
+  const uint32_t a_slot = static_cast<uint32_t>(p.Rs * p.kc * 2);
+  const uint32_t a_sbo = (p.a_swizzle_mode == 2) ? 1024u : 512u;
+  const uint64_t adesc0 = smem_desc(stage0 + b_half, 16u, a_sbo, static_cast<uint32_t>(p.a_swizzle_mode));
+  const uint64_t bdesc0 = smem_desc(stage0, static_cast<uint32_t>(p.kc * 128), 1024u, 2u);
+  const uint32_t stage16 = static_cast<uint32_t>(p.stage_bytes) >> 4;
+  const uint32_t unit16 = (4u * a_slot) >> 4;  // unit b's slots follow unit a's
+  const uint32_t full0 = baddr(&hdr->full[0]);
+  const uint32_t empty0 = baddr(&hdr->empty[0]);
+  uint32_t soff = 0;
+  const uint32_t is0 = lane == 0 ? 1u : 0u;
+#pragma unroll 1
+  while (units_left > 0) {
+    if (!__all_sync(0xffffffffu, mbar_wait_bounded(full0 + stage * 8, phase, ctl, ST_TIMEOUT_MMA))) break;
+    tc_fence_after();
+    const uint32_t info = hdr->info[stage];
+    bool ok = true;
+    bool issued = false;
+#pragma unroll
+    for (int x = 0; x < 2; ++x) {
+      if (info & (x ? TW_F_FIRST_B : TW_F_FIRST_A)) {
+        ok = __all_sync(0xffffffffu, mbar_wait_bounded(baddr(&hdr->acc_empty[x]), acc_phase[x] ^ 1u, ctl,
+                                                       ST_TIMEOUT_MMA));
+        if (!ok) break;
+        tc_fence_after();
+        started[x] = false;
+        any_mma[x] = false;
+      }
+      if (info & (x ? TW_F_MMA_B : TW_F_MMA_A)) {
+        const uint64_t ad = adesc0 + soff + static_cast<uint32_t>(x) * unit16, bd = bdesc0 + soff;
+        const uint32_t d = tmem_base + static_cast<uint32_t>(x * kRsN);
+        mma_bf16_pair_pred(d, ad, bd, idesc, started[x] ? 1u : 0u, is0);
+        mma_bf16_pair_pred(d, ad + 2u, bd + 128u, idesc, 1u, is0);
+        started[x] = true;
+        any_mma[x] = true;
+        issued = true;
+      }
+    }
+    if (!ok) break;
+    if (issued) {
+      mma_commit_pair_both_pred(empty0 + stage * 8, is0);
+    } else if (lane == 0) {
+      // nothing multiplied (an empty twin): plain arrives on both CTAs
+      const uint32_t e_local = empty0 + stage * 8;
+      mbar_arrive(e_local);
+      mbar_remote_arrive(mapa_shared(e_local, 1));
+    }
+#pragma unroll
+    for (int x = 0; x < 2; ++x) {
+      if (!(info & (x ? TW_F_LAST_B : TW_F_LAST_A))) continue;
+      const uint32_t f_local = baddr(&hdr->acc_full[x]);
+      if (any_mma[x]) {
+        mma_commit_pair_both_pred(f_local, is0);
+      } else if (lane == 0) {
+        // a unit without blocks: its accumulator is not read (zero rows)
+        mbar_arrive(f_local);
+        mbar_remote_arrive(mapa_shared(f_local, 1));
+      }
+      acc_phase[x] ^= 1u;
+      --units_left;
+    }
+    __syncwarp();
+    soff += stage16;
+    if (++stage == p.stages) {
+      stage = 0;
+      soff = 0;
+      phase ^= 1u;
+    }
+  }
+  if (lane == 0) {
+    mma_commit_pair_local(baddr(&hdr->drain));
+    rs_drain_wait(baddr(&hdr->drain), 0, ctl);
+  }
+  __syncwarp();
+}
+
+template <bool kF32>
+__global__ void __launch_bounds__(kRsThreads, 1) spmm_twin_tcgen05(const __grid_constant__ SpmmKernelParams p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  uint8_t* gbase = smem_raw + (base - raw);
+  RsSmemHeader* hdr = reinterpret_cast<RsSmemHeader*>(gbase);
+  const uint32_t stage0 = base + 1024u;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();
+  const int u_begin = p.cta_begin[blockIdx.x];
+  const int u_end = p.cta_begin[blockIdx.x + 1];
+
+  if (threadIdx.x == 32) {
+    for (int s = 0; s < p.stages; ++s) {
+      mbar_init(baddr(&hdr->full[s]), 1);
+      mbar_init(baddr(&hdr->empty[s]), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(baddr(&hdr->acc_full[a]), 1);
+      mbar_init(baddr(&hdr->acc_empty[a]), 8);  // 4 epilogue warps per CTA of the pair
+    }
+    mbar_init(baddr(&hdr->drain), 1);
+    mbar_init(baddr(&hdr->merge_bar), 4);
+    hdr->abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&p.tm_a);
+    tma_prefetch_desc(&p.tm_b);
+  }
+  if (warp == kRsMmaWarp) {
+    tmem_alloc_pair(smem_u32(&hdr->tmem_base), static_cast<uint32_t>(p.tmem_cols));
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // both CTAs' barriers exist before any cross-CTA arrive or copy
+  tc_fence_after();
+  const uint32_t tmem_base = hdr->tmem_base;
+  const WaitCtl ctl{&hdr->abort_flag, p.status, p.timeout_ns};
+
+  if (warp == kRsMmaWarp) {
+    if (rank == 0) tw_mma(p, hdr, stage0, tmem_base, u_end - u_begin, ctl, lane);
+  } else if (warp < kRsEpi0) {
+    if (warp - kRsProd0 < p.nprod) tw_producer(p, hdr, stage0, ctl, warp - kRsProd0, lane, rank);
+  } else {
+    const uint32_t leader_acc_empty = rank == 0 ? 0u : mapa_shared(baddr(&hdr->acc_empty[0]), 0);
+    rs_epilogue<kF32>(p, hdr, tmem_base, u_begin, u_end, ctl, warp, lane, leader_acc_empty);
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // the leader's MMAs into this CTA's TMEM are done before it is freed
+  if (warp == kRsMmaWarp) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, static_cast<uint32_t>(p.tmem_cols));
+  }
+}
+
 }  // namespace
 
 bsp_status launch_spmm_pair(const bsp_spmm_plan* p, const bsp_bsr_desc* A, const void* B, int64_t ldb,
@@ -307,7 +546,8 @@ bsp_status launch_spmm_pair(const bsp_spmm_plan* p, const bsp_bsr_desc* A, const
   if (reinterpret_cast<uintptr_t>(C) % 16 || (ldc * (f32 ? 4 : 2)) % 16)
     return set_error(BSP_ERR_INVALID_ARG, "C must be 16-byte aligned with 16-byte row pitch");
   if (p->grid % 2) return set_error(BSP_ERR_STATE, "CTA-pair plan with an odd grid");
-  auto kern = f32 ? spmm_pair_tcgen05<true> : spmm_pair_tcgen05<false>;
+  auto kern = p->variant == 3 ? (f32 ? spmm_twin_tcgen05<true> : spmm_twin_tcgen05<false>)
+                              : (f32 ? spmm_pair_tcgen05<true> : spmm_pair_tcgen05<false>);
   if (!p->attr_set) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, p->smem_bytes);
     if (e != cudaSuccess) return cuda_check(e, "cudaFuncSetAttribute(spmm pair)");

@@ -37,7 +37,8 @@ ONE_BF16 = 0x3F80
 # kernels of the SpMM path: the reference's three strategies, plus the two
 # DDA kernels forced explicitly ("dda" picks between them by estimated cost)
 SPMM_VARIANTS = {"naive": ("naive", {}), "snf": ("snf", {}), "dda": ("dda", {}),
-                 "dda_1cta": ("dda", {"group_mma": 4}), "dda_pair": ("dda", {"group_mma": 5})}
+                 "dda_1cta": ("dda", {"group_mma": 4}), "dda_pair": ("dda", {"group_mma": 5}),
+                 "dda_twin": ("dda", {"group_mma": 6})}
 
 
 def _spmm_dev(bsp, A, Bd, name):

@@ -25,7 +25,8 @@ def _bsp():
 # strategy names of the reference plus the two DDA kernels forced explicitly
 # (plain "dda" picks between them by estimated cost)
 VARIANTS = {"naive": ("naive", {}), "snf": ("snf", {}), "dda": ("dda", {}),
-            "dda_1cta": ("dda", {"group_mma": 4}), "dda_pair": ("dda", {"group_mma": 5})}
+            "dda_1cta": ("dda", {"group_mma": 4}), "dda_pair": ("dda", {"group_mma": 5}),
+            "dda_twin": ("dda", {"group_mma": 6})}
 STRATS = list(VARIANTS)
 
 

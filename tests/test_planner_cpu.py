@@ -407,3 +407,75 @@ def test_large_b_runs_tile_by_tile():
         u, cta = plan["unit_table"], plan["cta_begin"]
         ordered = all(np.all(np.diff(u[cta[c]:cta[c + 1], 3]) >= 0) for c in range(len(cta) - 1))
         assert ordered == tile_major, N
+
+
+TW_MMA = (1 << 8, 1 << 9)
+TW_FIRST = (1 << 16, 1 << 18)
+TW_LAST = (1 << 17, 1 << 19)
+TW_EMPTY = 1 << 20
+TWIN_SHAPES = [(1024, 1024, 512, 32, 32, 0.1), (2048, 1024, 256, 32, 32, 0.5), (800, 512, 384, 32, 32, 0.3),
+               (1024, 1024, 256, 64, 32, 0.2), (512, 512, 256, 32, 32, 0.0), (4096, 4096, 4096, 32, 32, 0.01)]
+
+
+@pytest.mark.parametrize("shape", TWIN_SHAPES, ids=[f"{s[0]}x{s[1]}x{s[2]}R{s[3]}p{s[4]}" for s in TWIN_SHAPES])
+def test_twin_schedule_multiplies_every_block_once_per_tile(shape):
+    """Twin units (variant 3): per CTA, the unit records come as (a, b)
+    pairs sharing one step range; replaying each CTA's stage list, every
+    block of each unit's entries is loaded into its slot exactly once per
+    column tile at a stage where its unit multiplies, each unit's FIRST and
+    LAST flags bracket its multiplying stages, and the two CTAs of a pair
+    walk the same flags."""
+    M, K, N, R, C, p = shape
+    rng = np.random.default_rng(int(M + N + 7 * R + 100 * p))
+    rp, ci, _ = rand_bsr(rng, M, K, R, C, p, empty_rows=(1,))
+    plan = bsp.inspect_spmm_plan(M, K, R, C, rp, ci, N, bsp.DDA, opts=bsp.make_opts(group_mma=6))
+    assert plan["variant"] == 3
+    units, cta, st, csb = plan["unit_table"], plan["cta_begin"], plan["stage_table"], plan["cta_stage_begin"]
+    slabs = R // 32
+    loaded = {}
+    for c in range(len(cta) - 1):
+        r = c % 2
+        k = int(csb[c])
+        assert (cta[c + 1] - cta[c]) % 2 == 0
+        for ui in range(int(cta[c]), int(cta[c + 1]), 2):
+            ua, ub = units[ui], units[ui + 1]
+            assert ua[5] == ub[5] and ua[6] == ub[6] and ua[3] == ub[3]    # same steps, same tile
+            nsteps = max(1, int(ua[6] - ua[5]))
+            open_ = [False, False]
+            done = [False, False]
+            for s in range(nsteps):
+                w = st[k + s]
+                flags = int(w[0]) & 0xFFFFFFFF
+                if c % 2 == 1:   # the pair's CTAs share the flag bits above the slot mask
+                    assert (flags & ~0xFF) == (int(st[int(csb[c - 1]) + (k - int(csb[c])) + s][0]) & ~0xFF)
+                for x in range(2):
+                    if flags & TW_FIRST[x]:
+                        assert not open_[x] and not done[x]
+                        open_[x] = True
+                    if flags & TW_MMA[x]:
+                        assert open_[x]
+                        u = (ua, ub)[x]
+                        for g in range(4):
+                            assert (flags >> (4 * x + g)) & 1
+                            ay = int(w[4 + 4 * x + g])
+                            if ay >= 0:
+                                assert g < u[1]
+                                blk, slab = divmod(ay, R)
+                                e = int(u[0]) + g
+                                assert slab == (e % slabs) * 32
+                                i = e // slabs
+                                assert rp[i] <= blk < rp[i + 1]
+                                key = (e, blk, int(u[3]))
+                                assert key not in loaded
+                                loaded[key] = True
+                    if flags & TW_LAST[x]:
+                        assert open_[x]
+                        open_[x] = False
+                        done[x] = True
+            assert done == [True, True]
+            k += nsteps
+    # every (entry slab, block, tile) exactly once
+    n_tiles = (N + 255) // 256
+    want = {(i * slabs + sl, b, t * 256) for i in range(M // R) for b in range(int(rp[i]), int(rp[i + 1]))
+            for sl in range(slabs) for t in range(n_tiles)}
+    assert set(loaded) == want

@@ -126,6 +126,9 @@ enum : int32_t {
   TW_F_LAST_B = 1 << 19,
   TW_F_EMPTY = 1 << 20,    // nothing to load or multiply (both units without blocks)
 };
+// Unit record flag (SpmmUnit::nt bit 16): this split-K part of the unit never
+// multiplies, its accumulator holds nothing of the unit, its partial is zero.
+constexpr int32_t kUnitNoAcc = 1 << 16;
 
 // ---- SDDMM schedule ---------------------------------------------------------
 // One unit = one block-row slab (Rs rows) x up to 4 output segments, each 32

@@ -1178,12 +1178,43 @@ bsp_status plan_spmm_twin(bsp_spmm_plan* p, const int32_t* row_ptr, const int32_
   }
   p->n_steps = static_cast<int64_t>(steps.size() / stride);
   int npairs = (o.max_ctas > 0 ? std::min(o.max_ctas, sm_count) : sm_count) / 2;
-  npairs = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(npairs, twins.size())));
+  // split-K over twins (both units' partials meet in the plan's workspace):
+  // parts of consecutive union steps, kept only when they shorten the deal
+  struct TwinPart {
+    int32_t twin, part, np;
+    int32_t s_begin, s_end;
+    int32_t slot0;  // unit a's slots (rank r: slot0 + r * np), unit b's follow at slot0 + 2 * np
+  };
+  std::vector<TwinPart> parts;
+  std::vector<int64_t> pw;
+  {
+    std::vector<int32_t> nst(twins.size());
+    for (size_t i = 0; i < twins.size(); ++i) nst[i] = twins[i].s_end - twins[i].s_begin;
+    std::vector<int32_t> np(twins.size(), 1);
+    if (!o.no_load_balance && o.group_rows != -1)
+      np = choose_splits(weight, nst, std::max(1, npairs), 2 * int64_t(128) * 256 * 4);
+    for (size_t i = 0; i < twins.size(); ++i) {
+      int32_t slot0 = 0;
+      if (np[i] > 1) {
+        slot0 = static_cast<int32_t>(p->n_split_slots);
+        p->n_split_slots += 4 * np[i];
+        ++p->split_units;
+      }
+      for (int k = 0; k < np[i]; ++k) {
+        const int32_t lo = twins[i].s_begin + static_cast<int32_t>(int64_t(nst[i]) * k / np[i]);
+        const int32_t hi = twins[i].s_begin + static_cast<int32_t>(int64_t(nst[i]) * (k + 1) / np[i]);
+        parts.push_back({static_cast<int32_t>(i), k, np[i], lo, hi, slot0});
+        pw.push_back(np[i] == 1 ? weight[i]
+                                : weight[i] * (hi - lo) / std::max(1, nst[i]) + (1 + np[i]) * 2 * int64_t(128) * 256 * 4);
+      }
+    }
+  }
+  npairs = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(npairs, parts.size())));
   std::vector<std::vector<int32_t>> per;
   if (o.no_load_balance)
-    contiguous_split(static_cast<int64_t>(twins.size()), npairs, &per);
+    contiguous_split(static_cast<int64_t>(parts.size()), npairs, &per);
   else
-    lpt_order(weight, npairs, &per);
+    serpentine_order(pw, npairs, &per);
   // ring: one block-column per stage, B half (8 KB) + 8 entry slots (2 KB each)
   const int a_slot = Rs * 32 * 2;
   const int stage_bytes = 2 * 32 * 128 + G2 * a_slot;
@@ -1219,17 +1250,22 @@ bsp_status plan_spmm_twin(bsp_spmm_plan* p, const int32_t* row_ptr, const int32_
   for (int c = 0; c < npairs; ++c) {
     for (int r = 0; r < 2; ++r) {
       for (int32_t idx : per[c]) {
-        const Twin& tw = twins[idx];
+        const TwinPart& tp = parts[static_cast<size_t>(idx)];
+        const Twin& tw = twins[static_cast<size_t>(tp.twin)];
         for (int x = 0; x < 2; ++x) {
           const int nent = x ? tw.nent_b : tw.nent_a;
+          // does unit x multiply anywhere in this part (pair-wide)?
+          bool acc = false;
+          for (int32_t s = tp.s_begin; s < tp.s_end && !acc; ++s)
+            for (int g = 0; g < G2; ++g) acc |= steps[static_cast<size_t>(s) * stride + 1 + x * G2 + g] >= 0;
           SpmmUnit u;
           u.row0 = static_cast<int32_t>(tw.e0 + x * G2 + r * G);
           u.nrows = std::max(0, std::min(G, nent - r * G));
-          u.r_off = 0;
+          u.r_off = tp.np > 1 ? tp.slot0 + x * 2 * tp.np + r * tp.np : 0;
           u.n0 = tw.n0;
-          u.nt = 1;
-          u.step_begin = tw.s_begin;
-          u.step_end = tw.s_end;
+          u.nt = tp.np | (tp.part << 8) | (tp.np > 1 && !acc ? kUnitNoAcc : 0);
+          u.step_begin = tp.s_begin;
+          u.step_end = tp.s_end;
           u.row_mask = (tw.mask >> (x * G2 + r * G)) & ((1 << G) - 1);
           p->h_units.push_back(u);
         }

@@ -92,6 +92,8 @@ __device__ __forceinline__ void rs_epilogue(const SpmmKernelParams& p, RsSmemHea
     if (!mbar_wait_bounded(baddr(&hdr->acc_full[acc]), acc_phase, ctl, ST_TIMEOUT_EPILOGUE)) break;
     tc_fence_after();
     const bool present = g < un.nrows && ((un.row_mask >> g) & 1);
+    // a split part that never multiplied leaves a zero partial (twin units)
+    const bool acc_ok = present && !(un.nt & kUnitNoAcc);
     const uint32_t t_acc = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * p.acc_cols);
     // Split-K: every part leaves its partial tile in its workspace slot
     // (float4 j of row r at j * 128 + r: 512-byte warp accesses); the part
@@ -105,7 +107,7 @@ __device__ __forceinline__ void rs_epilogue(const SpmmKernelParams& p, RsSmemHea
 #pragma unroll 1
       for (int c = 0; c < nchunk; ++c) {
         uint32_t v[32];
-        if (present) {
+        if (acc_ok) {
           tmem_ld_32x32b_x32(t_acc + static_cast<uint32_t>(c * 32), v);
           tmem_ld_wait();
         } else {

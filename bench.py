@@ -71,7 +71,8 @@ WORKLOAD_DESC = {
     "cfg3": "BASELINE config 3: BSR SDDMM 4096x256 x 256x4096 under a 4096x4096 mask, 32x32 blocks, p=0.05",
     "cfg4": "BASELINE config 4: SDDMM Q K^T + SpMM P V, seq 16384, head 128, 32x32 blocks, band+global+Zipf mask",
     "cfg5": "BASELINE config 5: BSR SpMM 65536x65536 (64x64 blocks, Zipf(1.1) rows, 1% mean) x 65536x8192, "
-            "row panels sharded by nnz blocks + NCCL exchange of C",
+            "row panels sharded by nnz blocks (C row-sharded in value; replicated on every GPU by the "
+            "kernel's epilogue peer stores under 'replicated')",
     "attn": "BASELINE config 4 shapes, fused: O = softmax(Q K^T / sqrt(128) on the band+global+Zipf mask) V, "
             "seq 16384, head 128, 32x32 blocks, Q/K/V ~ N(0,1)",
     "spgemm": "SpGEMM (bsr_matrix::spgemm): banded 16384x16384 BSR (32x32 blocks, half-width 32 blocks) "

@@ -43,6 +43,14 @@ bsp_status bsp_spmm_plan_traffic(int64_t M, int64_t K, int32_t R, int32_t C, int
 /* units_out[info[0] * info[12]]: info[11] == 0 (swap-AB kernel): 12 words per
  * unit (row, r_off, nseg, pad, blk[4], col[4]); info[11] == 1 (row-stacked
  * kernel): 44 words per unit (row0, nseg, pad[2], seg_col[8], blk[4][8]). */
+/* Row-stacked SpMM plans: the stacking order of the block-rows (entry e of
+ * the stack, a unit's row0 + g, is block-row rows_out[e]).  *n_out = 0 when
+ * the plan stacks consecutive block-rows; rows_out may be NULL to query n. */
+bsp_status bsp_spmm_plan_entry_rows(int64_t M, int64_t K, int32_t R, int32_t C, int64_t nnzb,
+                                    const int32_t* row_ptr, const int32_t* col_idx, int64_t N,
+                                    bsp_strategy strategy, const bsp_spmm_opts* opts, int32_t sm_count,
+                                    int32_t max_smem, int32_t* rows_out, int64_t* n_out);
+
 bsp_status bsp_sddmm_plan_inspect(int64_t M, int64_t N, int32_t R, int32_t C, int64_t nnzb,
                                   const int32_t* row_ptr, const int32_t* col_idx, int64_t K,
                                   bsp_strategy strategy, const bsp_sddmm_opts* opts,

@@ -35,7 +35,7 @@ EXPORTS = [
     "bsp_ipc_close", "bsp_spgemm_plan_create", "bsp_spgemm_pattern", "bsp_spgemm_execute",
     "bsp_spgemm_plan_destroy", "bsp_spgemm_plan_info", "bsp_spgemm_host", "bsp_spgemm_plan_inspect",
     "bsp_attn_plan_create", "bsp_attn_execute", "bsp_attn_plan_destroy", "bsp_attn_plan_info",
-    "bsp_attn_host", "bsp_attn_plan_inspect", "bsp_spmm_plan_traffic",
+    "bsp_attn_host", "bsp_attn_plan_inspect", "bsp_spmm_plan_traffic", "bsp_spmm_plan_entry_rows",
 ]
 IPC_HANDLE_BYTES = 64
 
@@ -148,6 +148,8 @@ def lib():
         "bsp_attn_plan_inspect": (S, [I64, I64, I64, P, P, ctypes.POINTER(Opts), I32, I32, P, P, P, P]),
         "bsp_spmm_plan_traffic": (S, [I64, I64, I32, I32, I64, P, P, I64, S, ctypes.POINTER(Opts), I32, I32,
                                       P, P]),
+        "bsp_spmm_plan_entry_rows": (S, [I64, I64, I32, I32, I64, P, P, I64, S, ctypes.POINTER(Opts), I32, I32,
+                                         P, ctypes.POINTER(I64)]),
         "bsp_testing_spmm_counters": (S, [P, ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(I64),
                                           ctypes.POINTER(I32)]),
         "bsp_testing_spmm_drop_stage": (S, [P, I32]),
@@ -721,6 +723,16 @@ def inspect_spmm_plan(M, K, R, C, row_ptr, col_idx, N, strategy=NAIVE, c_type=BF
     d = {k: int(info[i]) for i, k in enumerate(keys)}
     d.update(unit_table=units, cta_begin=cta, step_table=steps[: int(info[7])],
              stage_table=stages[: int(info[13])], cta_stage_begin=cta_st)
+    # row-stacked plans: stacking order of the block-rows (None = consecutive)
+    d["entry_rows"] = None
+    if d["variant"] == 1:
+        n = ctypes.c_int64(0)
+        eargs = (M, K, R, C, int(rp[-1]), _ptr(rp), _ptr(ci), N, strategy, ctypes.byref(o), sm_count, max_smem)
+        _check(lib().bsp_spmm_plan_entry_rows(*eargs, None, ctypes.byref(n)))
+        if n.value > 0:
+            rows = np.zeros(n.value, np.int32)
+            _check(lib().bsp_spmm_plan_entry_rows(*eargs, _ptr(rows), ctypes.byref(n)))
+            d["entry_rows"] = rows
     return d
 
 

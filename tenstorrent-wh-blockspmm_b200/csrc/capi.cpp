@@ -457,7 +457,8 @@ static std::vector<std::pair<const void*, size_t>> spmm_table_parts(const bsp_sp
           {p.h_steps.data(), p.h_steps.size() * sizeof(int32_t)},
           {p.h_stage_list.data(), p.h_stage_list.size() * sizeof(int32_t)},
           {p.h_cta_stage_begin.data(), p.h_cta_stage_begin.size() * sizeof(int32_t)},
-          {zeros->data(), zeros->size() * sizeof(int32_t)}};
+          {zeros->data(), zeros->size() * sizeof(int32_t)},
+          {p.h_entry_rows.data(), p.h_entry_rows.size() * sizeof(int32_t)}};
 }
 
 static void spmm_bind_tables(bsp_spmm_plan* p, const std::vector<void*>& ptrs) {
@@ -467,6 +468,7 @@ static void spmm_bind_tables(bsp_spmm_plan* p, const std::vector<void*>& ptrs) {
   p->d_stage_list = static_cast<int4*>(ptrs[3]);
   p->d_cta_stage_begin = static_cast<int32_t*>(ptrs[4]);
   p->d_split_counters = static_cast<int32_t*>(ptrs[5]);
+  p->d_entry_rows = p->h_entry_rows.empty() ? nullptr : static_cast<int32_t*>(ptrs[6]);
 }
 
 // Bytes of the split-K partial tiles: 128 rows x the tile's accumulator
@@ -1680,6 +1682,28 @@ bsp_status bsp_spmm_plan_traffic(int64_t M, int64_t K, int32_t R, int32_t C, int
   if (s != BSP_OK) return s;
   bsp_spmm_plan_info(&p, info);
   spmm_plan_traffic(p, traffic);
+  return BSP_OK;
+}
+
+bsp_status bsp_spmm_plan_entry_rows(int64_t M, int64_t K, int32_t R, int32_t C, int64_t nnzb,
+                                    const int32_t* row_ptr, const int32_t* col_idx, int64_t N,
+                                    bsp_strategy strategy, const bsp_spmm_opts* opts, int32_t sm_count,
+                                    int32_t max_smem, int32_t* rows_out, int64_t* n_out) {
+  if (!row_ptr || !n_out || (nnzb > 0 && !col_idx) || R <= 0 || C <= 0)
+    return set_error(BSP_ERR_INVALID_ARG, "bad arguments");
+  bsp_spmm_plan p;
+  p.M = M;
+  p.K = K;
+  p.N = N;
+  p.R = R;
+  p.C = C;
+  p.nnzb = nnzb;
+  p.strategy = strategy;
+  bsp_status s = plan_spmm_host(&p, row_ptr, col_idx, sm_count, max_smem, opts);
+  if (s != BSP_OK) return s;
+  *n_out = static_cast<int64_t>(p.h_entry_rows.size());
+  if (rows_out && !p.h_entry_rows.empty())
+    memcpy(rows_out, p.h_entry_rows.data(), p.h_entry_rows.size() * sizeof(int32_t));
   return BSP_OK;
 }
 

@@ -564,6 +564,38 @@ bsp_status plan_spmm_rowstack(bsp_spmm_plan* p, const int32_t* row_ptr, const in
   const int esz = p->c_type == BSP_F32 ? 4 : 2;
   std::vector<std::pair<int32_t, int32_t>> items;  // (col, g * 2^24-free: block id)
   std::vector<int8_t> item_g;
+  // Stacking order.  The G block-rows of a unit step through the union of
+  // their block-columns, so rows of very different lengths (power-law rows)
+  // stacked together leave most slots of the long row's steps empty.  Rows
+  // stacked by length (longest first) are kept when that shortens the total
+  // of the unions by 5% or more.
+  p->h_entry_rows.clear();
+  if (slabs == 1 && G > 1 && nbr > G && !o.no_load_balance) {
+    const int64_t nbc = p->K / C;
+    std::vector<int64_t> stamp(static_cast<size_t>(nbc), -1);
+    auto union_total = [&](const std::vector<int32_t>* order) {
+      int64_t tot = 0;
+      for (int64_t e0 = 0; e0 < nbr; e0 += G)
+        for (int64_t e = e0; e < std::min<int64_t>(nbr, e0 + G); ++e) {
+          const int64_t i = order ? (*order)[static_cast<size_t>(e)] : e;
+          for (int32_t b = row_ptr[i]; b < row_ptr[i + 1]; ++b)
+            if (stamp[static_cast<size_t>(col_idx[b])] != e0) {
+              stamp[static_cast<size_t>(col_idx[b])] = e0;
+              ++tot;
+            }
+        }
+      return tot;
+    };
+    const int64_t t_id = union_total(nullptr);
+    std::fill(stamp.begin(), stamp.end(), -1);
+    std::vector<int32_t> by_len(static_cast<size_t>(nbr));
+    std::iota(by_len.begin(), by_len.end(), 0);
+    std::stable_sort(by_len.begin(), by_len.end(), [&](int32_t a, int32_t b) {
+      return row_ptr[a + 1] - row_ptr[a] > row_ptr[b + 1] - row_ptr[b];
+    });
+    if (union_total(&by_len) * 100 <= t_id * 95) p->h_entry_rows.swap(by_len);
+  }
+  const std::vector<int32_t>& perm = p->h_entry_rows;
   for (int64_t e0 = 0; e0 < n_entries; e0 += G) {
     const int nent = static_cast<int>(std::min<int64_t>(G, n_entries - e0));
     const int32_t s_begin = static_cast<int32_t>(steps.size() / stride);
@@ -571,7 +603,7 @@ bsp_status plan_spmm_rowstack(bsp_spmm_plan* p, const int32_t* row_ptr, const in
     items.clear();
     item_g.clear();
     for (int g = 0; g < nent; ++g) {
-      const int64_t i = (e0 + g) / slabs;
+      const int64_t i = perm.empty() ? (e0 + g) / slabs : perm[static_cast<size_t>(e0 + g)];
       if (row_ptr[i + 1] > row_ptr[i]) mask |= 1 << g;
       for (int32_t b = row_ptr[i]; b < row_ptr[i + 1]; ++b) {
         items.push_back({col_idx[b], b});
@@ -624,10 +656,21 @@ bsp_status plan_spmm_rowstack(bsp_spmm_plan* p, const int32_t* row_ptr, const in
   // that order, so all CTAs work on one B panel (K x tile_n) at a time and
   // it is read from DRAM about once instead of once per row group.
   const bool l2_order = !o.no_load_balance && ntiles > 1 && p->K * p->N * 2 > (int64_t(64) << 20);
+  {
+    const char* eh = getenv("BSP_L2_HINT");
+    p->l2_hint = l2_order && eh ? atoi(eh) : 0;
+  }
   if (l2_order) {
     std::vector<int32_t> idx(units.size());
     std::iota(idx.begin(), idx.end(), 0);
-    std::stable_sort(idx.begin(), idx.end(), [&](int32_t a, int32_t b) { return units[a].n0 < units[b].n0; });
+    const char* evw = getenv("BSP_L2_WAVE");
+    const int64_t wave = static_cast<int64_t>(evw ? std::max(1, atoi(evw)) : 1) * tile_n;
+    std::stable_sort(idx.begin(), idx.end(), [&](int32_t a, int32_t b) {
+      const int64_t wa = units[a].n0 / wave, wb = units[b].n0 / wave;
+      if (wa != wb) return wa < wb;
+      if (units[a].row0 != units[b].row0) return units[a].row0 < units[b].row0;
+      return units[a].n0 < units[b].n0;
+    });
     std::vector<SpmmUnit> su(units.size());
     std::vector<int64_t> sw(units.size());
     for (size_t i = 0; i < idx.size(); ++i) {
@@ -643,7 +686,21 @@ bsp_status plan_spmm_rowstack(bsp_spmm_plan* p, const int32_t* row_ptr, const in
   if (!o.no_load_balance && o.group_rows != -1) {
     std::vector<int32_t> nst(units.size());
     for (size_t i = 0; i < units.size(); ++i) nst[i] = units[i].step_end - units[i].step_begin;
-    const std::vector<int32_t> np = choose_splits(weight, nst, grid, int64_t(128) * tile_n * 4, l2_order);
+    std::vector<int32_t> np;
+    if (l2_order) {
+      const char* ev = getenv("BSP_L2_CUT");
+      const double f = ev ? atof(ev) : 0.0;
+      if (f > 0) {
+        int64_t total = 0;
+        for (int64_t w : weight) total += w;
+        const int64_t cap = std::max<int64_t>(1, static_cast<int64_t>(double(total) / ntiles / grid * f));
+        np.assign(units.size(), 1);
+        for (size_t i = 0; i < units.size(); ++i)
+          if (weight[i] > cap && nst[i] >= 8)
+            np[i] = static_cast<int32_t>(std::min<int64_t>({64, nst[i] / 4, (weight[i] + cap - 1) / cap}));
+      }
+    }
+    if (np.empty()) np = choose_splits(weight, nst, grid, int64_t(128) * tile_n * 4, l2_order);
     std::vector<SpmmUnit> su;
     std::vector<int64_t> sw;
     for (size_t i = 0; i < units.size(); ++i) {

@@ -82,6 +82,7 @@ __device__ __forceinline__ void rs_epilogue(const SpmmKernelParams& p, RsSmemHea
   const int lrow = 32 * q + lane;  // row of the unit's 128-row tile
   const int64_t slot_floats = 128 * static_cast<int64_t>(p.acc_cols);
   const int nchunk = p.acc_cols / 32;  // 32-column chunks of the unit's tile
+  const bool c_stream = (p.l2_hint & 2) != 0;  // C lines leave L2 first (B does not fit in L2)
   int mp = 0;                          // merge-barrier rounds
   SpmmUnit nxt;
   if (u_begin < u_end) nxt = p.units[u_begin];
@@ -141,7 +142,7 @@ __device__ __forceinline__ void rs_epilogue(const SpmmKernelParams& p, RsSmemHea
       }
     }
     if (store && g < un.nrows) {
-      const int e = un.row0 + g;
+      const int e = p.entry_rows ? __ldg(p.entry_rows + un.row0 + g) : un.row0 + g;
       const int64_t row = static_cast<int64_t>(e / slabs) * p.R + (e % slabs) * p.Rs + rrow;
 #pragma unroll 1
       for (int c = 0; c < nchunk; ++c) {
@@ -149,28 +150,33 @@ __device__ __forceinline__ void rs_epilogue(const SpmmKernelParams& p, RsSmemHea
         if (n >= p.N) break;
         uint32_t v[32];
         if (parts_ws) {
-          // the sum of the parts' partials (at most 4: all loads of the
-          // chunk in flight together, one round trip to L2)
+          // the sum of the parts' partials, in part order: the loads of four
+          // partials' chunk are in flight together (one L2 round trip each)
           float a[32];
 #pragma unroll
           for (int i = 0; i < 32; ++i) a[i] = 0.f;
           if (present) {
-            float4 t[4][8];
+#pragma unroll 1
+            for (int k0 = 0; k0 < n_parts; k0 += 4) {
+              float4 t[4][8];
 #pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              const float4* src = reinterpret_cast<const float4*>(parts_ws + k * slot_floats) + (8 * c) * 128 + lrow;
+              for (int k = 0; k < 4; ++k) {
+                const float4* src =
+                    reinterpret_cast<const float4*>(parts_ws + (k0 + k) * slot_floats) + (8 * c) * 128 + lrow;
 #pragma unroll
-              for (int i = 0; i < 8; ++i) t[k][i] = k < n_parts ? __ldcg(src + i * 128) : make_float4(0.f, 0.f, 0.f, 0.f);
-            }
-#pragma unroll
-            for (int k = 0; k < 4; ++k)
-#pragma unroll
-              for (int i = 0; i < 8; ++i) {
-                a[4 * i] += t[k][i].x;
-                a[4 * i + 1] += t[k][i].y;
-                a[4 * i + 2] += t[k][i].z;
-                a[4 * i + 3] += t[k][i].w;
+                for (int i = 0; i < 8; ++i)
+                  t[k][i] = k0 + k < n_parts ? __ldcg(src + i * 128) : make_float4(0.f, 0.f, 0.f, 0.f);
               }
+#pragma unroll
+              for (int k = 0; k < 4; ++k)
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                  a[4 * i] += t[k][i].x;
+                  a[4 * i + 1] += t[k][i].y;
+                  a[4 * i + 2] += t[k][i].z;
+                  a[4 * i + 3] += t[k][i].w;
+                }
+            }
           }
 #pragma unroll
           for (int i = 0; i < 32; ++i) v[i] = __float_as_uint(a[i]);
@@ -189,7 +195,8 @@ __device__ __forceinline__ void rs_epilogue(const SpmmKernelParams& p, RsSmemHea
           for (int i = 0; i < 8; ++i) {
             const uint4 val = make_uint4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
             if (n + 4 * i < p.N) {
-              reinterpret_cast<uint4*>(dst)[i] = val;
+              if (c_stream) __stcs(reinterpret_cast<uint4*>(dst) + i, val);
+              else reinterpret_cast<uint4*>(dst)[i] = val;
               if (!staged) {
 #pragma unroll 1
                 for (int pp = 0; pp < p.n_peers; ++pp)
@@ -211,7 +218,8 @@ __device__ __forceinline__ void rs_epilogue(const SpmmKernelParams& p, RsSmemHea
             }
             const uint4 val = make_uint4(w[0], w[1], w[2], w[3]);
             if (n + 8 * i < p.N) {
-              reinterpret_cast<uint4*>(dst)[i] = val;
+              if (c_stream) __stcs(reinterpret_cast<uint4*>(dst) + i, val);
+              else reinterpret_cast<uint4*>(dst)[i] = val;
               if (!staged) {
 #pragma unroll 1
                 for (int pp = 0; pp < p.n_peers; ++pp)

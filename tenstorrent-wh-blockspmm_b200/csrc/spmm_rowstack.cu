@@ -60,6 +60,10 @@ __device__ __forceinline__ void rs_producer(const SpmmKernelParams& p, RsSmemHea
   uint32_t armed = 0, armed_parity = 0;
   bool ok = true;
   const uint32_t is0 = lane == 0 ? 1u : 0u;
+  // L2 priorities when B does not fit in L2: A blocks (read once per column
+  // tile) leave first, the B panel that the CTAs share stays longest
+  const bool hint_a = (p.l2_hint & 1) != 0, hint_b = (p.l2_hint & 4) != 0;
+  const uint64_t pol_a = hint_a ? l2_policy_evict_first() : 0, pol_b = hint_b ? l2_policy_evict_last() : 0;
 #pragma unroll 1
   for (int k0 = pw; k0 < n && ok; k0 += 32 * P) {
     int4 w0 = make_int4(0, 0, 0, 0), w1 = w0, w2 = w0, w3 = w0;
@@ -134,7 +138,8 @@ __device__ __forceinline__ void rs_producer(const SpmmKernelParams& p, RsSmemHea
             const uint32_t qb = sb + q * sub_bytes;
             const int ky = q ? ky1 : ky0;
             if (p.b3d) {
-              tma_load_3d_pred(qb, &p.tm_b, 0, ky, bz, full, is0);
+              if (hint_b) tma_load_3d_pred_hint(qb, &p.tm_b, 0, ky, bz, full, is0, pol_b);
+              else tma_load_3d_pred(qb, &p.tm_b, 0, ky, bz, full, is0);
             } else {
 #pragma unroll
               for (int h = 0; h < 4; ++h)
@@ -142,8 +147,10 @@ __device__ __forceinline__ void rs_producer(const SpmmKernelParams& p, RsSmemHea
             }
 #pragma unroll
             for (int g = 0; g < kRsMaxG; ++g)
-              if ((flags >> (4 * q + g)) & 1u)
-                tma_load_2d_pred(qb + b_bytes + g * a_slot, &p.tm_a, ax, ay[4 * q + g], full, is0);
+              if ((flags >> (4 * q + g)) & 1u) {
+                if (hint_a) tma_load_2d_pred_hint(qb + b_bytes + g * a_slot, &p.tm_a, ax, ay[4 * q + g], full, is0, pol_a);
+                else tma_load_2d_pred(qb + b_bytes + g * a_slot, &p.tm_a, ax, ay[4 * q + g], full, is0);
+              }
           }
         }
         armed |= 1u << stage;
@@ -386,6 +393,7 @@ bsp_status launch_spmm_rowstack(const bsp_spmm_plan* p, const bsp_bsr_desc* A, c
   kp.sub_bytes = p->sub_bytes;
   kp.xfer_off = p->xfer_off;
   kp.split_ws = p->d_split_ws;
+  kp.entry_rows = p->d_entry_rows;
   p->kp_valid = true;
   p->kp_a = A->values;
   p->kp_b = B;

@@ -32,6 +32,41 @@ def test_spmm_schedule_covers_work_exactly_once(shape, strategy, opts):
     rp, ci, _ = rand_bsr(rng, M, K, R, C, p)
     plan = bsp.inspect_spmm_plan(M, K, R, C, rp, ci, N, bsp.STRATEGIES[strategy],
                                  opts=bsp.make_opts(**opts))
+    _check_spmm_schedule(plan, rp, ci, M, N, R, C)
+
+
+def _power_law_rows(rng, nbr, nbc, density, s=1.1):
+    """Block-row lengths following Zipf's law over ranks (rows shuffled),
+    columns uniform: the shape of config 5."""
+    w = np.arange(1, nbr + 1, dtype=np.float64) ** -s
+    counts = np.minimum(nbc, np.maximum(1, np.round(w * density * nbr * nbc / w.sum()))).astype(int)
+    counts = counts[rng.permutation(nbr)]
+    rp = np.zeros(nbr + 1, np.int32)
+    rp[1:] = np.cumsum(counts)
+    ci = np.concatenate([np.sort(rng.choice(nbc, size=c, replace=False)) for c in counts]).astype(np.int32)
+    return rp, ci
+
+
+@pytest.mark.parametrize("R,N", [(64, 512), (32, 296), (32, 128)])
+def test_power_law_rows_stack_by_length(R, N):
+    """Rows of very different lengths are stacked longest first (fewer
+    union steps); the schedule still covers every block once per tile."""
+    M = K = 8192
+    rng = np.random.default_rng(R + N)
+    rp, ci = _power_law_rows(rng, M // R, K // R, 0.02)
+    plan = bsp.inspect_spmm_plan(M, K, R, R, rp, ci, N, bsp.DDA, opts=bsp.make_opts(group_mma=4))
+    er = plan["entry_rows"]
+    assert plan["variant"] == 1 and er is not None
+    assert sorted(er.tolist()) == list(range(M // R))
+    lens = np.diff(rp)[er]
+    assert np.all(lens[:-1] >= lens[1:])
+    _check_spmm_schedule(plan, rp, ci, M, N, R, R)
+    # consecutive stacking of the same pattern needs more steps
+    flat = bsp.inspect_spmm_plan(M, K, R, R, rp, ci, N, bsp.DDA, opts=bsp.make_opts(group_mma=4, no_load_balance=1))
+    assert flat["entry_rows"] is None and flat["steps"] > plan["steps"]
+
+
+def _check_spmm_schedule(plan, rp, ci, M, N, R, C):
     units, cta, steps = plan["unit_table"], plan["cta_begin"], plan["step_table"]
     assert cta[0] == 0 and cta[-1] == len(units) and np.all(np.diff(cta) >= 0)
     assert plan["ctas"] <= 148 and plan["stages"] >= 2
@@ -71,8 +106,9 @@ def test_spmm_schedule_covers_work_exactly_once(shape, strategy, opts):
                     if b >= 0:
                         blocks[g].append(int(b))
                         assert ci[b] == steps[s, 0]
+            er = plan["entry_rows"]
             for g in range(nent):
-                e = row0 + g
+                e = row0 + g if er is None else int(er[row0 + g])
                 covered[(e, n0)] = covered.get((e, n0), 0) + 1
                 assert sorted(blocks[g]) == _row_blocks(rp, e // slabs)
                 assert bool((mask >> g) & 1) == (rp[e // slabs + 1] > rp[e // slabs])

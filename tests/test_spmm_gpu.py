@@ -320,3 +320,49 @@ def test_spmm_large_b_tile_order_parity(variant):
     gold = oracle.spmm_bf16(rp, ci, vals, M, K, R, C, B, N)
     out = _run(bsp, M, K, N, R, C, rp, ci, vals, B, variant)
     assert_bf16_close(out, gold, what=f"large B {variant}")
+
+
+def _power_law_rows(rng, nbr, nbc, density, s=1.1):
+    w = np.arange(1, nbr + 1, dtype=np.float64) ** -s
+    counts = np.minimum(nbc, np.maximum(1, np.round(w * density * nbr * nbc / w.sum()))).astype(int)
+    counts = counts[rng.permutation(nbr)]
+    rows = [np.sort(rng.choice(nbc, size=c, replace=False)) for c in counts]
+    rp = np.concatenate([[0], np.cumsum(counts)]).astype(np.int32)
+    return rp, np.concatenate(rows).astype(np.int32)
+
+
+@pytest.mark.parametrize("R,N,c_f32", [(64, 512, False), (32, 296, False), (32, 256, True), (64, 128, True)])
+def test_spmm_length_ordered_stacking_parity(R, N, c_f32):
+    """Power-law block-row lengths: the row-stacked kernel stacks rows longest
+    first (the plan's entry order maps stack entries to block-rows and the
+    epilogue writes each entry's rows where they belong).  All of C matches
+    the oracle, empty rows included, and a relaunch gives the same bits."""
+    import torch
+
+    bsp = _bsp()
+    M = K = 8192
+    rng = np.random.default_rng(R * 3 + N + c_f32)
+    rp, ci = _power_law_rows(rng, M // R, K // R, 0.02)
+    vals = oracle.f32_to_bf16(rng.uniform(-1, 1, ci.size * R * R).astype(np.float32))
+    B = rand_dense(rng, K, N)
+    sid, opts = _sv(bsp, "dda_1cta")
+    info = bsp.inspect_spmm_plan(M, K, R, R, rp, ci, N, sid, opts=opts)
+    assert info["entry_rows"] is not None
+    A = bsp.DeviceBSR.from_host(M, K, R, R, rp, ci, vals)
+    Bd = bsp.to_device_bf16(B)
+    dev = bsp.device()
+    plan = bsp.SpmmPlan(dev, A, N, sid, bsp.F32 if c_f32 else bsp.BF16, opts)
+    outs = []
+    for _ in range(2):
+        Cd = torch.full((M, N), float("nan"), dtype=torch.float32 if c_f32 else torch.bfloat16, device="cuda")
+        plan.execute(A, Bd, Cd)
+        dev.synchronize()
+        outs.append(Cd.cpu().numpy() if c_f32 else bsp.to_host_bits(Cd))
+    plan.close()
+    assert np.array_equal(outs[0], outs[1])
+    if c_f32:
+        gold = oracle.spmm_f32(rp, ci, oracle.bf16_to_f32(vals), M, K, R, R, oracle.bf16_to_f32(B), N)
+        assert normwise(outs[0], gold) <= 1e-5
+    else:
+        gold = oracle.spmm_bf16(rp, ci, vals, M, K, R, R, B, N)
+        assert_bf16_close(outs[0], gold, what=f"length-ordered stacking R={R} N={N}")

@@ -93,7 +93,11 @@ typedef struct bsp_spmm_opts {
                               sharing).  -1 turns off: split-K of long units (SpMM
                               row-stacked and pair kernels), the resident A tile
                               (SDDMM CDA / SnF), unit splitting (attention) */
-  int32_t n_tiles;         /* SNF/DDA: 128-column tiles per work unit (A reuse) */
+  int32_t n_tiles;         /* SNF/DDA swap-AB: 128-column tiles per work unit
+                              (A reuse).  DDA row-stacked kernel: 4 = wide
+                              units of 512 columns in one accumulator (N a
+                              multiple of 512; each A block loaded once per
+                              512 columns), otherwise 256 */
   int32_t max_ctas;        /* cap on persistent CTAs (default: all SMs) */
   int32_t timeout_ms;      /* bound on every in-kernel wait (default 2000) */
   int32_t group_mma;       /* DDA: 0/1 (default) the planner's choice of the

@@ -87,13 +87,12 @@ struct SpmmKernelParams {
   // leave its k-th pipeline stage unissued (no copy, no arrive), so that the
   // MMA warp's bounded wait on it runs out; 0 = off.
   int32_t debug_drop_stage;
+  // Accumulators in TMEM: 1 = one of acc_cols columns (wide units of 512
+  // columns), anything else = two (double-buffered, acc_cols each).
+  int32_t n_acc;
   // Row-stacked kernel: stacking order of the block-rows.  Entry e of the
   // stack (unit row0 + g) is block-row entry_rows[e]; nullptr = identity.
   const int32_t* entry_rows;
-  // L2 eviction priorities (row-stacked kernels, plans whose B does not fit
-  // in L2): bit 0 = A loads evict-first, bit 1 = C stores streaming
-  // (evict-first), bit 2 = B loads evict-last.
-  int32_t l2_hint;
 };
 
 // Row-stacked kernel stage descriptor (16 words), precomputed by the planner
@@ -396,7 +395,7 @@ struct bsp_spmm_plan {
   int32_t* d_split_counters = nullptr;  // in the blob (zeroed): two sets of one per slot
   mutable uint32_t launch_parity = 0;   // which counter set the next launch uses
   int32_t debug_drop_stage = 0;         // testing only, see SpmmKernelParams
-  int32_t l2_hint = 0;                  // see SpmmKernelParams::l2_hint
+  int32_t n_acc = 2;                    // row-stacked: TMEM accumulators (1: wide units)
   std::vector<int32_t> h_entry_rows;    // row-stacked: stacking order (empty = identity)
   int32_t* d_entry_rows = nullptr;      // in the blob
   uint64_t timeout_ns = 0;
@@ -521,7 +520,6 @@ inline void select_split_counters(const bsp_spmm_plan* p, SpmmKernelParams& k) {
   k.split_counters = p->d_split_counters ? p->d_split_counters + par * n : nullptr;
   k.split_counters_next = p->d_split_counters ? p->d_split_counters + (par ^ 1u) * n : nullptr;
   k.debug_drop_stage = p->debug_drop_stage;
-  k.l2_hint = p->l2_hint;
   p->launch_parity ^= 1u;
 }
 }  // namespace bsp

@@ -159,27 +159,6 @@ __device__ __forceinline__ void tma_load_3d_pred(uint32_t smem_dst, const void* 
       : "memory");
 }
 
-__device__ __forceinline__ void tma_load_2d_pred_hint(uint32_t smem_dst, const void* tmap, int32_t x,
-                                                      int32_t y, uint32_t bar, uint32_t issue, uint64_t policy) {
-  asm volatile(
-      "{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %5, 0;\n\t"
-      "@q cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
-      " [%0], [%1, {%2, %3}], [%4], %6;\n\t}" ::"r"(smem_dst),
-      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(bar), "r"(issue), "l"(policy)
-      : "memory");
-}
-
-__device__ __forceinline__ void tma_load_3d_pred_hint(uint32_t smem_dst, const void* tmap, int32_t x,
-                                                      int32_t y, int32_t z, uint32_t bar, uint32_t issue,
-                                                      uint64_t policy) {
-  asm volatile(
-      "{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %6, 0;\n\t"
-      "@q cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
-      " [%0], [%1, {%2, %3, %4}], [%5], %7;\n\t}" ::"r"(smem_dst),
-      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(z), "r"(bar), "r"(issue), "l"(policy)
-      : "memory");
-}
-
 __device__ __forceinline__ void tma_load_2d_hint(uint32_t smem_dst, const void* tmap, int32_t x,
                                                  int32_t y, uint32_t bar, uint64_t policy) {
   asm volatile(

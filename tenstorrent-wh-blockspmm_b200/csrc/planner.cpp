@@ -540,12 +540,18 @@ bsp_status plan_spmm_rowstack(bsp_spmm_plan* p, const int32_t* row_ptr, const in
   const int Rs = (R % 128 == 0) ? 128 : (R % 64 == 0) ? 64 : 32;
   const int slabs = R / Rs;
   const int G = 128 / Rs;
-  const int kc = (C % 64 == 0) ? 64 : 32;
+  // Wide units (opts.n_tiles = 4, N a multiple of 512): 512 output columns
+  // in one accumulator (all of TMEM, no double buffering), two N = 256 MMAs
+  // per k-step, 32-deep k-chunks so that a stage (a 512-column B slice and the
+  // entries' blocks) stays at 40 KB.  Each A block is then loaded once per 512
+  // columns instead of once per 256.
+  const bool wide = o.n_tiles == 4 && p->N % 512 == 0;
+  const int kc = (C % 64 == 0 && !wide) ? 64 : 32;
   const int nkc = C / kc;
   const int64_t n_entries = nbr * slabs;
   // 256-column tiles (MMA N = 256); a B of at most 128 columns gets 128-column
   // tiles (MMA N = 128) instead of a 256-column box half out of range
-  const int tile_n = p->N <= 128 ? 128 : 256;
+  const int tile_n = wide ? 512 : p->N <= 128 ? 128 : 256;
   const int ntiles = static_cast<int>((p->N + tile_n - 1) / tile_n);
   if (n_entries >= (int64_t(1) << 31))
     return set_error(BSP_ERR_UNSUPPORTED, "too many block-rows");
@@ -656,10 +662,6 @@ bsp_status plan_spmm_rowstack(bsp_spmm_plan* p, const int32_t* row_ptr, const in
   // that order, so all CTAs work on one B panel (K x tile_n) at a time and
   // it is read from DRAM about once instead of once per row group.
   const bool l2_order = !o.no_load_balance && ntiles > 1 && p->K * p->N * 2 > (int64_t(64) << 20);
-  // Such plans also give their A blocks (read once per column tile) and C
-  // lines (written once) the first L2 evictions, so that the B panel all
-  // CTAs share stays longer (about 1% on config 5).
-  p->l2_hint = l2_order ? 3 : 0;
   if (l2_order) {
     std::vector<int32_t> idx(units.size());
     std::iota(idx.begin(), idx.end(), 0);
@@ -728,7 +730,7 @@ bsp_status plan_spmm_rowstack(bsp_spmm_plan* p, const int32_t* row_ptr, const in
   // carries two consecutive steps so that each hand-off moves four MMAs:
   // on B200 that beats the deeper one-step ring at every density from 5%.
   int nsub = 1;
-  if (kc == 32 && nkc == 1 && o.steps_per_stage != 1) nsub = 2;
+  if (kc == 32 && nkc == 1 && o.steps_per_stage != 1 && !wide) nsub = 2;
   const int sub_bytes = (tile_n / 64) * kc * 128 + G * Rs * kc * 2;
   p->sub_bytes = sub_bytes;
   p->nsub = nsub;
@@ -763,7 +765,8 @@ bsp_status plan_spmm_rowstack(bsp_spmm_plan* p, const int32_t* row_ptr, const in
     p->xfer_off = 1024 + stages * stage_bytes;
     p->smem_bytes += 16384;
   }
-  p->tmem_cols = 2 * tile_n;
+  p->tmem_cols = wide ? 512 : 2 * tile_n;
+  p->n_acc = wide ? 1 : 2;
   p->timeout_ns = static_cast<uint64_t>(o.timeout_ms > 0 ? o.timeout_ms : 2000) * 1000000ull;
 
   bsp_status st = spmm_stage_counts(p);

@@ -82,7 +82,6 @@ __device__ __forceinline__ void rs_epilogue(const SpmmKernelParams& p, RsSmemHea
   const int lrow = 32 * q + lane;  // row of the unit's 128-row tile
   const int64_t slot_floats = 128 * static_cast<int64_t>(p.acc_cols);
   const int nchunk = p.acc_cols / 32;  // 32-column chunks of the unit's tile
-  const bool c_stream = (p.l2_hint & 2) != 0;  // C lines leave L2 first (B does not fit in L2)
   int mp = 0;                          // merge-barrier rounds
   SpmmUnit nxt;
   if (u_begin < u_end) nxt = p.units[u_begin];
@@ -195,8 +194,7 @@ __device__ __forceinline__ void rs_epilogue(const SpmmKernelParams& p, RsSmemHea
           for (int i = 0; i < 8; ++i) {
             const uint4 val = make_uint4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
             if (n + 4 * i < p.N) {
-              if (c_stream) __stcs(reinterpret_cast<uint4*>(dst) + i, val);
-              else reinterpret_cast<uint4*>(dst)[i] = val;
+              reinterpret_cast<uint4*>(dst)[i] = val;
               if (!staged) {
 #pragma unroll 1
                 for (int pp = 0; pp < p.n_peers; ++pp)
@@ -218,8 +216,7 @@ __device__ __forceinline__ void rs_epilogue(const SpmmKernelParams& p, RsSmemHea
             }
             const uint4 val = make_uint4(w[0], w[1], w[2], w[3]);
             if (n + 8 * i < p.N) {
-              if (c_stream) __stcs(reinterpret_cast<uint4*>(dst) + i, val);
-              else reinterpret_cast<uint4*>(dst)[i] = val;
+              reinterpret_cast<uint4*>(dst)[i] = val;
               if (!staged) {
 #pragma unroll 1
                 for (int pp = 0; pp < p.n_peers; ++pp)
@@ -258,7 +255,7 @@ __device__ __forceinline__ void rs_epilogue(const SpmmKernelParams& p, RsSmemHea
       if (acc_empty_leader) mbar_remote_arrive(acc_empty_leader + static_cast<uint32_t>(acc) * 8u);
       else mbar_arrive(baddr(&hdr->acc_empty[acc]));
     }
-    acc ^= 1;
+    if (p.n_acc != 1) acc ^= 1;
     if (acc == 0) acc_phase ^= 1u;
   }
   // peer stores are visible system-wide before this CTA retires

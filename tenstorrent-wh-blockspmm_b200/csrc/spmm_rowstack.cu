@@ -60,10 +60,6 @@ __device__ __forceinline__ void rs_producer(const SpmmKernelParams& p, RsSmemHea
   uint32_t armed = 0, armed_parity = 0;
   bool ok = true;
   const uint32_t is0 = lane == 0 ? 1u : 0u;
-  // L2 priorities when B does not fit in L2: A blocks (read once per column
-  // tile) leave first, the B panel that the CTAs share stays longest
-  const bool hint_a = (p.l2_hint & 1) != 0, hint_b = (p.l2_hint & 4) != 0;
-  const uint64_t pol_a = hint_a ? l2_policy_evict_first() : 0, pol_b = hint_b ? l2_policy_evict_last() : 0;
 #pragma unroll 1
   for (int k0 = pw; k0 < n && ok; k0 += 32 * P) {
     int4 w0 = make_int4(0, 0, 0, 0), w1 = w0, w2 = w0, w3 = w0;
@@ -138,8 +134,7 @@ __device__ __forceinline__ void rs_producer(const SpmmKernelParams& p, RsSmemHea
             const uint32_t qb = sb + q * sub_bytes;
             const int ky = q ? ky1 : ky0;
             if (p.b3d) {
-              if (hint_b) tma_load_3d_pred_hint(qb, &p.tm_b, 0, ky, bz, full, is0, pol_b);
-              else tma_load_3d_pred(qb, &p.tm_b, 0, ky, bz, full, is0);
+              tma_load_3d_pred(qb, &p.tm_b, 0, ky, bz, full, is0);
             } else {
 #pragma unroll
               for (int h = 0; h < 4; ++h)
@@ -147,10 +142,8 @@ __device__ __forceinline__ void rs_producer(const SpmmKernelParams& p, RsSmemHea
             }
 #pragma unroll
             for (int g = 0; g < kRsMaxG; ++g)
-              if ((flags >> (4 * q + g)) & 1u) {
-                if (hint_a) tma_load_2d_pred_hint(qb + b_bytes + g * a_slot, &p.tm_a, ax, ay[4 * q + g], full, is0, pol_a);
-                else tma_load_2d_pred(qb + b_bytes + g * a_slot, &p.tm_a, ax, ay[4 * q + g], full, is0);
-              }
+              if ((flags >> (4 * q + g)) & 1u)
+                tma_load_2d_pred(qb + b_bytes + g * a_slot, &p.tm_a, ax, ay[4 * q + g], full, is0);
           }
         }
         armed |= 1u << stage;
@@ -188,7 +181,12 @@ __device__ __forceinline__ void rs_mma(const SpmmKernelParams& p, RsSmemHeader* 
   // A (stacked entries): K-major, rows of kc*2 bytes; B: MN-major 128B swizzle,
   // LBO = one 64-column block (kc rows x 128 B), SBO = 8 k-rows; a 16-row
   // k-step of B is 2048 bytes, a 16-column k-step of A is 32 bytes.
-  const uint32_t idesc = idesc_bf16_f32(128, p.acc_cols, /*a K-major*/ 0, /*b MN-major*/ 1);
+  // MMA N is the accumulator's width up to 256; a 512-column accumulator
+  // takes two MMAs per k-step, the second on B's columns 256..511 (four
+  // 64-column blocks further on in the slice)
+  const uint32_t idesc = idesc_bf16_f32(128, min(p.acc_cols, 256), /*a K-major*/ 0, /*b MN-major*/ 1);
+  const bool two_halves = p.acc_cols > 256;
+  const uint32_t bhalf16 = static_cast<uint32_t>(4 * p.kc * 128) >> 4;
   const uint32_t b_bytes = static_cast<uint32_t>(2 * p.NT * p.kc * 128);
   const uint32_t a_sbo = (p.a_swizzle_mode == 2) ? 1024u : 512u;
   const uint64_t adesc0 = smem_desc(stage0 + b_bytes, 16u, a_sbo, static_cast<uint32_t>(p.a_swizzle_mode));
@@ -218,6 +216,12 @@ __device__ __forceinline__ void rs_mma(const SpmmKernelParams& p, RsSmemHeader* 
 #pragma unroll
       for (int k = 0; k < kKS; ++k)
         mma_bf16_pred(d0, ad + k * 2u, bd + k * 128u, idesc, (k > 0 || !first) ? 1u : 0u, is0);
+      if (two_halves) {
+#pragma unroll
+        for (int k = 0; k < kKS; ++k)
+          mma_bf16_pred(d0 + 256u, ad + k * 2u, bd + bhalf16 + k * 128u, idesc, (k > 0 || !first) ? 1u : 0u,
+                        is0);
+      }
       if (info & RS_TWO) {
 #pragma unroll
         for (int k = 0; k < kKS; ++k)
@@ -227,7 +231,7 @@ __device__ __forceinline__ void rs_mma(const SpmmKernelParams& p, RsSmemHeader* 
     mma_commit_pred(empty0 + stage * 8, is0);
     if (info & RS_LAST) {
       mma_commit_pred(baddr(&hdr->acc_full[acc]), is0);
-      acc ^= 1;
+      if (p.n_acc != 1) acc ^= 1;
       if (acc == 0) acc_phase ^= 1u;
       --units_left;
     }
@@ -394,6 +398,7 @@ bsp_status launch_spmm_rowstack(const bsp_spmm_plan* p, const bsp_bsr_desc* A, c
   kp.xfer_off = p->xfer_off;
   kp.split_ws = p->d_split_ws;
   kp.entry_rows = p->d_entry_rows;
+  kp.n_acc = p->n_acc;
   p->kp_valid = true;
   p->kp_a = A->values;
   p->kp_b = B;

@@ -13,6 +13,7 @@ from helpers import rand_bsr
 # kernel (variant 2) by estimated cost; group_mma=4 / 5 force one of them.
 STRATS = [("naive", {}), ("snf", {}), ("dda", dict(group_mma=4)), ("dda", dict(group_mma=4, steps_per_stage=1)),
           ("dda", dict(group_mma=2)), ("dda", dict(group_mma=3)), ("snf", dict(no_load_balance=1)),
+          ("dda", dict(group_mma=4, n_tiles=4)),
           ("dda", dict(group_mma=4, no_load_balance=1, producers=2))]
 
 SHAPES = [(1024, 1024, 256, 32, 32, 0.1), (512, 768, 200, 32, 32, 0.3), (512, 512, 384, 64, 64, 0.4),
@@ -76,8 +77,10 @@ def _check_spmm_schedule(plan, rp, ci, M, N, R, C):
         Rs = plan["slab"]
         slabs = R // Rs
         assert G * Rs == 128
-        tile_n = 128 * plan["n_tiles"]          # 256, or 128 when N <= 128
-        assert tile_n == (128 if N <= 128 else 256)
+        tile_n = 128 * plan["n_tiles"]          # 256, or 128 when N <= 128, or 512 (wide units)
+        wide = plan["tmem_cols"] == 512 and tile_n == 512
+        assert tile_n == (512 if wide else 128 if N <= 128 else 256)
+        assert not wide or (N % 512 == 0 and plan["kc"] == 32 and plan["nsub"] == 1)
         # units, or split-K parts of units: part (nt >> 8) of nt & 0xFF, slot r_off + part
         tiles, slots = {}, set()
         for u in units:

@@ -26,8 +26,9 @@ def _bsp():
 # (plain "dda" picks between them by estimated cost)
 VARIANTS = {"naive": ("naive", {}), "snf": ("snf", {}), "dda": ("dda", {}),
             "dda_1cta": ("dda", {"group_mma": 4}), "dda_pair": ("dda", {"group_mma": 5}),
-            "dda_twin": ("dda", {"group_mma": 6})}
-STRATS = list(VARIANTS)
+            "dda_twin": ("dda", {"group_mma": 6}), "dda_wide": ("dda", {"group_mma": 4, "n_tiles": 4})}
+# dda_wide only differs from dda_1cta when N is a multiple of 512 (its own test)
+STRATS = [v for v in VARIANTS if v != "dda_wide"]
 
 
 def _sv(bsp, name, **extra):
@@ -366,3 +367,46 @@ def test_spmm_length_ordered_stacking_parity(R, N, c_f32):
     else:
         gold = oracle.spmm_bf16(rp, ci, vals, M, K, R, R, B, N)
         assert_bf16_close(outs[0], gold, what=f"length-ordered stacking R={R} N={N}")
+
+
+@pytest.mark.parametrize("R,N,c_f32,skew", [(64, 512, False, False), (32, 1024, False, False), (64, 1024, True, False),
+                                          (32, 512, False, True), (64, 512, True, True)])
+def test_spmm_wide_units_parity(R, N, c_f32, skew):
+    """Wide units (opts.n_tiles = 4): 512 output columns in one TMEM
+    accumulator, two N = 256 MMAs per k-step, 32-deep k-chunks.  With skewed
+    rows the plan also cuts long units (split-K partials of 512 columns).
+    All of C matches the oracle and a relaunch gives the same bits."""
+    import torch
+
+    bsp = _bsp()
+    M, K = 2048, 8192
+    rng = np.random.default_rng(R + N + 5 * c_f32 + 11 * skew)
+    if skew:
+        rp, ci = _skewed_rows(rng, M // R, K // R, heavy={1, 2, 9, 30}, heavy_len=100, light_len=3)
+        vals = oracle.f32_to_bf16(rng.uniform(-1, 1, ci.size * R * R).astype(np.float32))
+    else:
+        rp, ci, vals = rand_bsr(rng, M, K, R, R, 0.05)
+    B = rand_dense(rng, K, N)
+    sid, opts = _sv(bsp, "dda_wide")
+    info = bsp.inspect_spmm_plan(M, K, R, R, rp, ci, N, sid, opts=opts)
+    assert info["n_tiles"] == 4 and info["tmem_cols"] == 512
+    if skew:
+        assert ((info["unit_table"][:, 4] & 0xFF) > 1).any()
+    A = bsp.DeviceBSR.from_host(M, K, R, R, rp, ci, vals)
+    Bd = bsp.to_device_bf16(B)
+    dev = bsp.device()
+    plan = bsp.SpmmPlan(dev, A, N, sid, bsp.F32 if c_f32 else bsp.BF16, opts)
+    outs = []
+    for _ in range(2):
+        Cd = torch.full((M, N), float("nan"), dtype=torch.float32 if c_f32 else torch.bfloat16, device="cuda")
+        plan.execute(A, Bd, Cd)
+        dev.synchronize()
+        outs.append(Cd.cpu().numpy() if c_f32 else bsp.to_host_bits(Cd))
+    plan.close()
+    assert np.array_equal(outs[0], outs[1])
+    if c_f32:
+        gold = oracle.spmm_f32(rp, ci, oracle.bf16_to_f32(vals), M, K, R, R, oracle.bf16_to_f32(B), N)
+        assert normwise(outs[0], gold) <= 1e-5
+    else:
+        gold = oracle.spmm_bf16(rp, ci, vals, M, K, R, R, B, N)
+        assert_bf16_close(outs[0], gold, what=f"wide units R={R} N={N} skew={skew}")

@@ -852,8 +852,12 @@ bsp_status bsp_spmm_host_batch(bsp_device* dev, int32_t n_jobs, const bsp_spmm_h
   std::vector<bsp_status> pst(nj, BSP_OK);
   std::vector<std::string> pmsg(nj);
   std::vector<std::thread> th;
+  // the jobs' planners share the cores
+  static const int cores = static_cast<int>(std::max(1u, std::thread::hardware_concurrency()));
+  const int cap = std::max(1, cores / static_cast<int>(nj));
   for (size_t k = 0; k < nj; ++k)
-    th.emplace_back([&, k]() {
+    th.emplace_back([&, k, cap]() {
+      set_planner_thread_cap(cap);
       pst[k] = plan_spmm_host(plans[k], jobs[k].row_ptr, jobs[k].col_idx, dev->sm_count, dev->max_smem_optin, opts);
       if (pst[k] != BSP_OK) pmsg[k] = g_last_error;  // this worker's message
     });

@@ -49,10 +49,18 @@ int slab_height(int R) {
 // 16 and the machine's cores, at least `min_items` items each, and the
 // per-thread scratch (`scratch_bytes`) within 256 MB.  BSP_PLANNER_THREADS
 // overrides the count (the plans do not depend on it).
+// A planning thread may carry a cap on the threads it spawns (the batch path
+// plans several patterns at once and shares the cores among them).
+static thread_local int tl_thread_cap = 0;
+
+void set_planner_thread_cap(int cap) { tl_thread_cap = cap; }
+int planner_thread_cap() { return tl_thread_cap; }
+
 static int planner_threads(int64_t items, int64_t min_items, int64_t scratch_bytes) {
   // the core count is read once (the C library parses /sys on every query)
   static const unsigned cores = std::max(1u, std::thread::hardware_concurrency());
   int t = static_cast<int>(std::min<unsigned>(16, cores));
+  if (tl_thread_cap > 0) t = std::min(t, tl_thread_cap);
   if (const char* env = std::getenv("BSP_PLANNER_THREADS")) {
     const int v = std::atoi(env);
     if (v > 0) return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(v, items)));
@@ -260,8 +268,11 @@ bsp_status plan_spmm_host(bsp_spmm_plan* p, const int32_t* row_ptr, const int32_
     pair.c_type = p->c_type;
     pair.strategy = p->strategy;
     bsp_status st2 = BSP_OK;
-    std::thread pair_thread(
-        [&]() { st2 = plan_spmm_pair(&pair, row_ptr, col_idx, sm_count, max_smem, opts, false); });
+    const int cap = tl_thread_cap;
+    std::thread pair_thread([&, cap]() {
+      tl_thread_cap = cap;
+      st2 = plan_spmm_pair(&pair, row_ptr, col_idx, sm_count, max_smem, opts, false);
+    });
     bsp_status st1 = plan_spmm_rowstack(p, row_ptr, col_idx, sm_count, max_smem, opts, false);
     pair_thread.join();
     if (st1 != BSP_OK) return plan_spmm_pair(p, row_ptr, col_idx, sm_count, max_smem, opts);
@@ -1008,7 +1019,9 @@ static bsp_status rowstack_stage_lists(bsp_spmm_plan* p) {
   const int64_t grid = static_cast<int64_t>(p->h_cta_begin.size()) - 1;
   p->h_stage_list.resize(static_cast<size_t>(p->h_cta_stage_begin.back()) * W);
   const std::vector<int32_t>& steps = p->h_steps;
-  return parallel_ranges(grid, planner_threads(grid, 4, 0), [&](int, int64_t c0, int64_t c1) {
+  // a thread pays for itself from a few thousand stages on
+  const int64_t nst = p->h_cta_stage_begin.back();
+  return parallel_ranges(grid, planner_threads(std::min<int64_t>(grid, nst / 4096), 1, 0), [&](int, int64_t c0, int64_t c1) {
     std::vector<uint32_t> dirty(static_cast<size_t>(stages) * nsub);  // per (slot, sub-step)
     for (int64_t c = c0; c < c1; ++c) {
       int32_t* out = p->h_stage_list.data() + static_cast<size_t>(p->h_cta_stage_begin[c]) * W;
@@ -1080,7 +1093,9 @@ static bsp_status pair_stage_lists(bsp_spmm_plan* p) {
   const int64_t grid = static_cast<int64_t>(p->h_cta_begin.size()) - 1;
   p->h_stage_list.resize(static_cast<size_t>(p->h_cta_stage_begin.back()) * W);
   const std::vector<int32_t>& steps = p->h_steps;
-  return parallel_ranges(grid, planner_threads(grid, 4, 0), [&](int, int64_t c0, int64_t c1) {
+  // a thread pays for itself from a few thousand stages on
+  const int64_t nst = p->h_cta_stage_begin.back();
+  return parallel_ranges(grid, planner_threads(std::min<int64_t>(grid, nst / 4096), 1, 0), [&](int, int64_t c0, int64_t c1) {
     for (int64_t cta = c0; cta < c1; ++cta) {
       const int r = static_cast<int>(cta % 2);
       int32_t* out = p->h_stage_list.data() + static_cast<size_t>(p->h_cta_stage_begin[cta]) * W;
@@ -1337,7 +1352,9 @@ bsp_status plan_spmm_twin(bsp_spmm_plan* p, const int32_t* row_ptr, const int32_
   const bool b3d = (p->N % 64 == 0);
   const int64_t grid = static_cast<int64_t>(p->h_cta_begin.size()) - 1;
   p->h_stage_list.resize(static_cast<size_t>(p->h_cta_stage_begin.back()) * W);
-  return parallel_ranges(grid, planner_threads(grid, 4, 0), [&](int, int64_t c0, int64_t c1) {
+  // a thread pays for itself from a few thousand stages on
+  const int64_t nst = p->h_cta_stage_begin.back();
+  return parallel_ranges(grid, planner_threads(std::min<int64_t>(grid, nst / 4096), 1, 0), [&](int, int64_t c0, int64_t c1) {
     for (int64_t cta = c0; cta < c1; ++cta) {
       const int r = static_cast<int>(cta % 2);
       int32_t* out = p->h_stage_list.data() + static_cast<size_t>(p->h_cta_stage_begin[cta]) * W;

@@ -769,8 +769,9 @@ bsp_status plan_spmm_rowstack(bsp_spmm_plan* p, const int32_t* row_ptr, const in
   p->stage_bytes = stage_bytes;
   p->stages = stages;
   p->smem_bytes = 2048 + stages * stage_bytes;
-  // A 16 KiB staging area for replicated (multi-GPU) launches, when it fits
-  // beside the ring without costing a stage.
+  // A 16 KiB staging area through which the epilogue stores C (and its peer
+  // copies) as whole 128-byte lines, when it fits beside the ring without
+  // costing a stage.
   p->xfer_off = 0;
   if (p->smem_bytes + 16384 <= max_smem) {
     p->xfer_off = 1024 + stages * stage_bytes;
@@ -948,7 +949,7 @@ bsp_status plan_spmm_pair(bsp_spmm_plan* p, const int32_t* row_ptr, const int32_
   p->nprod = nprod;
   p->stage_bytes = stage_bytes;
   p->stages = stages;
-  p->xfer_off = 1024 + stages * stage_bytes;  // staging for replicated launches
+  p->xfer_off = 1024 + stages * stage_bytes;  // staging area of the C stores
   p->smem_bytes = 2048 + stages * stage_bytes + 16384;
   p->tmem_cols = 512;
   p->timeout_ns = static_cast<uint64_t>(o.timeout_ms > 0 ? o.timeout_ms : 2000) * 1000000ull;
@@ -1294,7 +1295,7 @@ bsp_status plan_spmm_twin(bsp_spmm_plan* p, const int32_t* row_ptr, const int32_
   p->nprod = nprod;
   p->stage_bytes = stage_bytes;
   p->stages = stages;
-  p->xfer_off = 1024 + stages * stage_bytes;  // staging for replicated launches
+  p->xfer_off = 1024 + stages * stage_bytes;  // staging area of the C stores
   p->smem_bytes = 2048 + stages * stage_bytes + 16384;
   p->tmem_cols = 512;
   p->timeout_ns = static_cast<uint64_t>(o.timeout_ms > 0 ? o.timeout_ms : 2000) * 1000000ull;

@@ -72,12 +72,15 @@ __device__ __forceinline__ void rs_epilogue(const SpmmKernelParams& p, RsSmemHea
   const int slabs = p.R / p.Rs;
   int acc = 0;
   uint32_t acc_phase = 0;
-  // Peer copies of C leave as whole 128-byte row segments: the warp's 32 rows
-  // x 128 bytes are staged in shared memory (16-byte pieces XOR-swizzled by
-  // row), then each store instruction writes 4 rows x 128 contiguous bytes.
+  // C (and its peer copies) leaves as whole 128-byte row segments: the
+  // warp's 32 rows x 128 bytes are staged in shared memory (16-byte pieces
+  // XOR-swizzled by row), then each store instruction writes 4 rows x 128
+  // contiguous bytes.  A thread storing its own row directly would make every
+  // warp store touch 32 lines with 16 bytes each, which costs ~4 us per
+  // 128 x 256 tile and bounds the low-density launches.
   constexpr int kEsz = kF32 ? 4 : 2;
   constexpr int kChunksPerFlush = 128 / (32 * kEsz);  // 32-column chunks per 128-byte segment
-  const bool staged = p.n_peers > 0 && p.xfer_off > 0;
+  const bool staged = p.xfer_off > 0;
   uint4* xf = reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(hdr) + p.xfer_off) + q * (32 * 8);
   const int lrow = 32 * q + lane;  // row of the unit's 128-row tile
   const int64_t slot_floats = 128 * static_cast<int64_t>(p.acc_cols);
@@ -193,13 +196,11 @@ __device__ __forceinline__ void rs_epilogue(const SpmmKernelParams& p, RsSmemHea
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
             const uint4 val = make_uint4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
-            if (n + 4 * i < p.N) {
+            if (!staged && n + 4 * i < p.N) {
               reinterpret_cast<uint4*>(dst)[i] = val;
-              if (!staged) {
 #pragma unroll 1
-                for (int pp = 0; pp < p.n_peers; ++pp)
-                  reinterpret_cast<uint4*>(static_cast<float*>(p.peer_c[pp]) + eo)[i] = val;
-              }
+              for (int pp = 0; pp < p.n_peers; ++pp)
+                reinterpret_cast<uint4*>(static_cast<float*>(p.peer_c[pp]) + eo)[i] = val;
             }
             if (staged) xf[lane * 8 + ((piece0 + i) ^ (lane & 7))] = val;
           }
@@ -215,13 +216,11 @@ __device__ __forceinline__ void rs_epilogue(const SpmmKernelParams& p, RsSmemHea
               w[h] = *reinterpret_cast<const uint32_t*>(&b2);
             }
             const uint4 val = make_uint4(w[0], w[1], w[2], w[3]);
-            if (n + 8 * i < p.N) {
+            if (!staged && n + 8 * i < p.N) {
               reinterpret_cast<uint4*>(dst)[i] = val;
-              if (!staged) {
 #pragma unroll 1
-                for (int pp = 0; pp < p.n_peers; ++pp)
-                  reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.peer_c[pp]) + eo)[i] = val;
-              }
+              for (int pp = 0; pp < p.n_peers; ++pp)
+                reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.peer_c[pp]) + eo)[i] = val;
             }
             if (staged) xf[lane * 8 + ((piece0 + i) ^ (lane & 7))] = val;
           }
@@ -240,6 +239,7 @@ __device__ __forceinline__ void rs_epilogue(const SpmmKernelParams& p, RsSmemHea
             if (col < p.N && pc < (c % kChunksPerFlush + 1) * (32 * kEsz / 16)) {
               const uint4 val = xf[r * 8 + (pc ^ (r & 7))];
               const int64_t off = (row_w + r) * p.ldc + col;
+              *reinterpret_cast<uint4*>(static_cast<uint8_t*>(p.c_ptr) + off * kEsz) = val;
 #pragma unroll 1
               for (int pp = 0; pp < p.n_peers; ++pp)
                 *reinterpret_cast<uint4*>(static_cast<uint8_t*>(p.peer_c[pp]) + off * kEsz) = val;

@@ -511,7 +511,6 @@ int attn_smem_bytes(int d);
 // Cap on the threads the planner spawns from the calling thread (0 = none;
 // inherited by the planner's own helper threads).
 void set_planner_thread_cap(int cap);
-int planner_thread_cap();
 bsp_status plan_spmm_rowstack(bsp_spmm_plan* p, const int32_t* row_ptr, const int32_t* col_idx,
                               int sm_count, int max_smem, const bsp_spmm_opts* opts, bool stage_lists = true);
 

@@ -54,7 +54,6 @@ int slab_height(int R) {
 static thread_local int tl_thread_cap = 0;
 
 void set_planner_thread_cap(int cap) { tl_thread_cap = cap; }
-int planner_thread_cap() { return tl_thread_cap; }
 
 static int planner_threads(int64_t items, int64_t min_items, int64_t scratch_bytes) {
   // the core count is read once (the C library parses /sys on every query)

@@ -242,9 +242,10 @@ bsp_status plan_spmm_host(bsp_spmm_plan* p, const int32_t* row_ptr, const int32_
   // DDA: group_mma 4 forces the single-CTA row-stacked kernel, 5 the CTA-pair
   // kernel (2-SM MMA).  By default both schedules are built and the one with
   // the shorter estimated critical path wins: a pair stage moves twice the
-  // rows for ~0.8x the time of a single-CTA stage (measured on B200), but
-  // pairing 8 block-rows instead of 4 widens each unit's column union, which
-  // costs more than it saves below ~30% block density.
+  // rows for ~0.74x the time of a single-CTA stage (measured on B200 from
+  // 10% density up), but pairing 8 block-rows instead of 4 widens each
+  // unit's column union, which costs more than it saves below ~20% block
+  // density.
   if (p->strategy == BSP_DDA && o.group_mma != 2 && o.group_mma != 3) {
     if (o.group_mma == 4 || sm_count < 2) return plan_spmm_rowstack(p, row_ptr, col_idx, sm_count, max_smem, opts);
     if (o.group_mma == 5) return plan_spmm_pair(p, row_ptr, col_idx, sm_count, max_smem, opts);
@@ -284,7 +285,7 @@ bsp_status plan_spmm_host(bsp_spmm_plan* p, const int32_t* row_ptr, const int32_
     const int64_t s1 = longest(p, 1);
     if (st2 != BSP_OK) return rowstack_stage_lists(p);
     const int64_t s2 = longest(&pair, 2);  // per pair: the leader's list (both lists are equal length)
-    if (4 * s2 < 5 * s1) {  // pair time ~ 0.8 x its stages vs single-CTA stages
+    if (74 * s2 < 100 * s1) {  // pair time ~ 0.74 x its stages vs single-CTA stages
       bsp_device* dev = p->dev;
       *p = std::move(pair);
       p->dev = dev;
@@ -1082,61 +1083,95 @@ static bsp_status rowstack_stage_lists(bsp_spmm_plan* p) {
 }
 
 // The CTA-pair kernel's per-CTA stage lists (CTA 2c + r = rank r of pair c),
-// CTAs split over host threads.  Every entry slot is loaded at every stage
-// (absent blocks from a zero-filled box above the tensor), so no slot needs
-// clearing.
+// built a pair at a time over host threads.  The host replays each CTA's smem
+// ring: a slot is loaded when its entry has a block in the sub-step, or when
+// it is absent but still holds an older block (then from a box above the A
+// tensor, which the TMA fills with zeros); absent slots that are already zero
+// are not touched.  So every shared-memory write stays a TMA write.  Flags
+// bits 0..7 mark the slots to load.  Both CTAs' copies complete on the
+// leader's full barrier, so the leader's descriptor carries the pair's count
+// of loaded slots (bits 16..20), from which it arms the barrier.
 static bsp_status pair_stage_lists(bsp_spmm_plan* p) {
   const int W = kRsStageWords;
   const int G = p->G, Rs = p->Rs, R = p->R, C = p->C, kc = p->kc, nkc = C / kc, slabs = R / Rs;
-  const int nsub = p->nsub, stride = p->step_stride;
+  const int nsub = p->nsub, stride = p->step_stride, stages = p->stages;
   const bool b3d = (p->N % 64 == 0);
-  const int64_t grid = static_cast<int64_t>(p->h_cta_begin.size()) - 1;
+  const uint32_t all = (1u << G) - 1u;
+  const int64_t npairs = (static_cast<int64_t>(p->h_cta_begin.size()) - 1) / 2;
   p->h_stage_list.resize(static_cast<size_t>(p->h_cta_stage_begin.back()) * W);
   const std::vector<int32_t>& steps = p->h_steps;
   // a thread pays for itself from a few thousand stages on
   const int64_t nst = p->h_cta_stage_begin.back();
-  return parallel_ranges(grid, planner_threads(std::min<int64_t>(grid, nst / 4096), 1, 0), [&](int, int64_t c0, int64_t c1) {
-    for (int64_t cta = c0; cta < c1; ++cta) {
-      const int r = static_cast<int>(cta % 2);
-      int32_t* out = p->h_stage_list.data() + static_cast<size_t>(p->h_cta_stage_begin[cta]) * W;
-      for (int32_t ui = p->h_cta_begin[cta]; ui < p->h_cta_begin[cta + 1]; ++ui) {
-        const SpmmUnit& u = p->h_units[ui];
-        const int nsteps = u.step_end - u.step_begin;
-        if (nsteps == 0) {
-          int32_t e[kRsStageWords] = {RS_F_FIRST | RS_F_LAST | RS_F_EMPTY};
-          memcpy(out, e, sizeof(e));
-          out += W;
-          continue;
-        }
-        int slab_off[4] = {0, 0, 0, 0};
-        for (int g = 0; g < G; ++g) slab_off[g] = static_cast<int>((u.row0 + g) % slabs) * Rs;
-        const int nitems = nsteps * nkc;
-        for (int s0 = 0; s0 < nitems; s0 += nsub) {
-          const int nin = std::min(nsub, nitems - s0);
-          int32_t e[kRsStageWords];
-          for (int q = 0; q < W; ++q) e[q] = 0;
-          uint32_t flags = 0;
-          for (int sub = 0; sub < nsub; ++sub) {
-            for (int g = 0; g < 4; ++g) e[5 + 4 * sub + g] = -Rs;  // absent: a box above the tensor
-            if (sub >= nin) continue;
-            const int s_ = s0 + sub;
-            const int j = s_ / nkc, kci = s_ % nkc;
-            const int32_t* st = &steps[static_cast<size_t>(u.step_begin + j) * stride];
-            for (int g = 0; g < G; ++g) {
-              const int gg = r * G + g;
-              if (g < u.nrows && st[1 + gg] >= 0) e[5 + 4 * sub + g] = st[1 + gg] * R + slab_off[g];
-            }
-            e[3 + sub] = st[0] * C + kci * kc;
-            e[2] = kci * kc;
+  return parallel_ranges(npairs, planner_threads(std::min<int64_t>(npairs, nst / 4096), 1, 0),
+                         [&](int, int64_t c0, int64_t c1) {
+    std::vector<uint32_t> dirty(static_cast<size_t>(stages) * nsub);  // per (slot, sub-step)
+    for (int64_t pc = c0; pc < c1; ++pc) {
+      for (int r = 0; r < 2; ++r) {
+        const int64_t cta = 2 * pc + r;
+        int32_t* out = p->h_stage_list.data() + static_cast<size_t>(p->h_cta_stage_begin[cta]) * W;
+        std::fill(dirty.begin(), dirty.end(), all);  // unknown contents until first written
+        int64_t k = 0;
+        for (int32_t ui = p->h_cta_begin[cta]; ui < p->h_cta_begin[cta + 1]; ++ui) {
+          const SpmmUnit& u = p->h_units[ui];
+          const int nsteps = u.step_end - u.step_begin;
+          if (nsteps == 0) {
+            int32_t e[kRsStageWords] = {RS_F_FIRST | RS_F_LAST | RS_F_EMPTY};
+            memcpy(out, e, sizeof(e));
+            out += W;
+            ++k;
+            continue;
           }
-          if (s0 == 0) flags |= RS_F_FIRST;
-          if (s0 + nin >= nitems) flags |= RS_F_LAST;
-          if (nin == 2) flags |= RS_F_TWO;
-          e[0] = static_cast<int32_t>(flags);
-          e[1] = b3d ? u.n0 / 64 + 2 * r : u.n0 + 128 * r;
-          memcpy(out, e, sizeof(e));
-          out += W;
+          int slab_off[4] = {0, 0, 0, 0};
+          for (int g = 0; g < G; ++g) slab_off[g] = static_cast<int>((u.row0 + g) % slabs) * Rs;
+          const int nitems = nsteps * nkc;
+          for (int s0 = 0; s0 < nitems; s0 += nsub) {
+            const int nin = std::min(nsub, nitems - s0);
+            int32_t e[kRsStageWords];
+            for (int q = 0; q < W; ++q) e[q] = (q >= 5 && q <= 12) ? -1 : 0;
+            uint32_t flags = 0;
+            const int slot = static_cast<int>(k % stages);
+            for (int sub = 0; sub < nin; ++sub) {
+              const int s_ = s0 + sub;
+              const int j = s_ / nkc, kci = s_ % nkc;
+              const int32_t* st = &steps[static_cast<size_t>(u.step_begin + j) * stride];
+              uint32_t present = 0;
+              for (int g = 0; g < G; ++g) {
+                const int gg = r * G + g;
+                if (g < u.nrows && st[1 + gg] >= 0) {
+                  present |= 1u << g;
+                  e[5 + 4 * sub + g] = st[1 + gg] * R + slab_off[g];
+                }
+              }
+              uint32_t& d = dirty[static_cast<size_t>(slot) * nsub + sub];
+              const uint32_t stale = ~present & all & d;  // zero-filled by a box above the tensor
+              for (int g = 0; g < G; ++g)
+                if ((stale >> g) & 1u) e[5 + 4 * sub + g] = -Rs;
+              d = present;
+              flags |= (present | stale) << (4 * sub);
+              e[3 + sub] = st[0] * C + kci * kc;
+              e[2] = kci * kc;
+            }
+            if (s0 == 0) flags |= RS_F_FIRST;
+            if (s0 + nin >= nitems) flags |= RS_F_LAST;
+            if (nin == 2) flags |= RS_F_TWO;
+            e[0] = static_cast<int32_t>(flags);
+            e[1] = b3d ? u.n0 / 64 + 2 * r : u.n0 + 128 * r;
+            memcpy(out, e, sizeof(e));
+            out += W;
+            ++k;
+          }
         }
+      }
+      // the leader's descriptors carry the pair's count of loaded slots
+      int32_t* lead = p->h_stage_list.data() + static_cast<size_t>(p->h_cta_stage_begin[2 * pc]) * W;
+      const int32_t* peer = p->h_stage_list.data() + static_cast<size_t>(p->h_cta_stage_begin[2 * pc + 1]) * W;
+      const int64_t n_lead = p->h_cta_stage_begin[2 * pc + 1] - p->h_cta_stage_begin[2 * pc];
+      const int64_t n_peer = p->h_cta_stage_begin[2 * pc + 2] - p->h_cta_stage_begin[2 * pc + 1];
+      if (n_lead != n_peer) return set_error(BSP_ERR_STATE, "pair stage lists differ in length");
+      for (int64_t i = 0; i < n_lead; ++i) {
+        const uint32_t fl = static_cast<uint32_t>(lead[i * W]), fp = static_cast<uint32_t>(peer[i * W]);
+        const uint32_t np = static_cast<uint32_t>(__builtin_popcount(fl & 0xFFu) + __builtin_popcount(fp & 0xFFu));
+        lead[i * W] = static_cast<int32_t>(fl | (np << 16));
       }
     }
     return BSP_OK;

@@ -11,13 +11,15 @@
 //     n0 + 128 r .. +127 of the slice (its half of the N operand).  Each CTA
 //     therefore stages half the B bytes of the single-CTA kernel, and the
 //     smem ring is twice as deep.
-//   * Every entry slot is loaded at every step; an absent block is a TMA box
-//     entirely above the A tensor, which the TMA fills with zeros.  Each stage
-//     moves a fixed number of bytes and no slot ever needs clearing, so all
-//     shared-memory writes come from the TMA (async proxy).
+//   * A slot is loaded when its entry has a block in the step, or when it is
+//     absent but still holds an older block: then from a TMA box entirely
+//     above the A tensor, which the TMA fills with zeros.  Absent slots that
+//     are already zero are skipped (the planner replays each CTA's ring).
+//     Every shared-memory write is thus a TMA write (async proxy).
 //   * Only the leader (rank 0) waits on the full barriers: both CTAs' TMA
 //     loads complete on the leader's barrier, armed by the leader with both
-//     CTAs' bytes.  The leader issues the MMAs and commits to the empty and
+//     CTAs' bytes (its stage descriptor carries the pair's count of loaded
+//     slots).  The leader issues the MMAs and commits to the empty and
 //     accumulator barriers of both CTAs at once (multicast commit arrive).
 //   * Each CTA's epilogue reads its own TMEM lanes and writes its rows of C;
 //     the peer's epilogue warps arrive on the leader's acc_empty barrier.
@@ -47,8 +49,6 @@ __device__ __forceinline__ void pr_producer(const SpmmKernelParams& p, RsSmemHea
   const uint32_t b_half = 2u * b_blk;
   const uint32_t sub_bytes = static_cast<uint32_t>(p.sub_bytes);
   const int G = p.G;
-  // bytes both CTAs land on the leader's full barrier for one sub-step
-  const uint32_t tx_sub = 2u * (b_half + static_cast<uint32_t>(G) * a_slot);
   const uint32_t is0 = (lane == 0 && rank == 0) ? 1u : 0u;
   // lanes 0..7: A slot (sub = lane / 4, entry g = lane % 4); lanes 8..11: B
   // (sub = (lane - 8) / 2, 64-column box h = lane % 2; 3-D boxes use lanes 8, 10)
@@ -100,9 +100,12 @@ __device__ __forceinline__ void pr_producer(const SpmmKernelParams& p, RsSmemHea
         hdr->info[stage] = flags & static_cast<uint32_t>(RS_FIRST | RS_LAST | RS_EMPTY | RS_TWO);
       __syncwarp();
       const uint32_t nsub = (flags & RS_EMPTY) ? 0u : ((flags & RS_TWO) ? 2u : 1u);
-      mbar_arrive_expect_tx_pred(full_local, nsub * tx_sub, is0);
+      // the leader arms its barrier with both CTAs' bytes: B halves and the
+      // pair's loaded slots
+      const uint32_t np_pair = (flags >> 16) & 0x1Fu;
+      mbar_arrive_expect_tx_pred(full_local, nsub * 2u * b_half + np_pair * a_slot, is0);
       if (nsub > 0) {
-        const bool a_on = lane < 8 && a_g < G && static_cast<uint32_t>(a_sub) < nsub;
+        const bool a_on = lane < 8 && a_g < G && static_cast<uint32_t>(a_sub) < nsub && ((flags >> lane) & 1u);
         tma_load_2d_pair_pred(sb + static_cast<uint32_t>(a_sub) * sub_bytes + b_half + a_g * a_slot, &p.tm_a,
                               ax, my_ay, full, a_on ? 1u : 0u);
         const int ky = b_sub ? ky1 : ky0;

@@ -52,9 +52,9 @@ def test_config2_sweep_full_parity(i, p):
     info = plan.info()
     insp = bsp.inspect_spmm_plan(M, K, R, C, op["rp"], op["ci"], N, strategy, sm_count=dev.sm_count)
     assert insp["variant"] == info["variant"] and insp["units"] == info["units"]
-    # the plan the benchmark times: CTA pairs at p = 0.5, single CTAs below;
+    # the plan the benchmark times: CTA pairs from p = 0.25, single CTAs below;
     # split-K fills the balancer's last round at p = 0.25 and 0.5
-    assert info["variant"] == (2 if p >= 0.5 else 1), info
+    assert info["variant"] == (2 if p >= 0.25 else 1), info
     if p >= 0.25:
         assert _split_k_present(insp)
     gold = oracle.spmm_bf16(op["rp"], op["ci"], op["vals"], M, K, R, C, op["B"], N)

@@ -360,8 +360,11 @@ PAIR_OPTS = [dict(group_mma=5), dict(group_mma=5, steps_per_stage=1),
 def test_pair_schedule_covers_work_exactly_once(shape, opts):
     """CTA-pair plans: CTA 2c+r of pair c holds entries r*G.. of each pair
     unit; both CTAs walk stage lists of equal length; every entry's blocks
-    appear once per 256-column chunk, each at the TMA row of its block, and
-    every absent slot points at a box above the A tensor (zero fill)."""
+    appear once per 256-column chunk, each at the TMA row of its block; an
+    absent slot that still holds an older block of that CTA's ring is loaded
+    from a box above the A tensor (zero fill), other absent slots are
+    skipped, and the leader's descriptor carries the pair's count of loaded
+    slots (its barrier's bytes)."""
     M, K, N, R, C, p = shape
     rng = np.random.default_rng(int(M + K + N + R + 1000 * p))
     rp, ci, _ = rand_bsr(rng, M, K, R, C, p)
@@ -379,8 +382,11 @@ def test_pair_schedule_covers_work_exactly_once(shape, opts):
         peer = range(cta[2 * pc + 1], cta[2 * pc + 2])
         assert len(lead) == len(peer)
         assert cst[2 * pc + 1] - cst[2 * pc] == cst[2 * pc + 2] - cst[2 * pc + 1]
+        presents = [[], []]
         for r, rng_u in enumerate((lead, peer)):
             rows = st[cst[2 * pc + r]:cst[2 * pc + r + 1]]
+            S = plan["stages"]
+            state = np.full((S, 2), (1 << G) - 1, dtype=np.int64)  # slot contents unknown at start
             k = 0
             for ui in rng_u:
                 row0, nent, _, n0, _, sb, se, mask = (int(x) for x in units[ui])
@@ -388,6 +394,7 @@ def test_pair_schedule_covers_work_exactly_once(shape, opts):
                 items = [(j, kci) for j in range(sb, se) for kci in range(nkc)]
                 if not items:
                     assert rows[k, 0] & (FIRST | LAST | EMPTY) == FIRST | LAST | EMPTY
+                    presents[r].append(0)
                     k += 1
                     continue
                 i = 0
@@ -396,23 +403,39 @@ def test_pair_schedule_covers_work_exactly_once(shape, opts):
                     n_in = 2 if f & TWO else 1
                     assert n_in <= nsub and bool(f & FIRST) == (i == 0) and not f & EMPTY
                     assert rows[k, 1] == (n0 // 64 + 2 * r if N % 64 == 0 else n0 + 128 * r)
+                    n_present = 0
                     for q in range(n_in):
                         j, kci = items[i + q]
                         assert rows[k, 3 + q] == steps[j, 0] * C + kci * kc
+                        load = (f >> (4 * q)) & 0xF
+                        assert (f >> (8 + 4 * q)) & 0xF == 0
+                        slot = k % S
+                        present = 0
                         for g in range(4):
                             ay = int(rows[k, 5 + 4 * q + g])
                             b = int(steps[j, 1 + r * G + g]) if g < G else -1
                             if g < nent and b >= 0:
+                                present |= 1 << g
+                                assert (load >> g) & 1
                                 assert ci[b] == steps[j, 0] and rp[(row0 + g) // slabs] <= b < rp[(row0 + g) // slabs + 1]
                                 assert ay == b * R + ((row0 + g) % slabs) * Rs
                                 key = (b, (row0 + g) % slabs, kci, n0)
                                 seen[key] = seen.get(key, 0) + 1
+                            elif (load >> g) & 1:
+                                # stale slot: a zero box, and only where the ring slot held a block
+                                assert ay == -Rs and (state[slot, q] >> g) & 1
                             else:
-                                assert ay == -Rs
+                                assert ay == -1 and not (g < G and (state[slot, q] >> g) & 1)
+                        n_present += bin(load).count("1")
+                        state[slot, q] = present
+                    presents[r].append(n_present)
                     i += n_in
                     assert bool(f & LAST) == (i >= len(items))
                     k += 1
             assert k == len(rows)
+        lead_rows = st[cst[2 * pc]:cst[2 * pc + 1]]
+        for k in range(len(lead_rows)):
+            assert (int(lead_rows[k, 0]) >> 16) & 0x1F == presents[0][k] + presents[1][k]
     assert len(seen) == int(rp[-1]) * slabs * nkc * ((N + 255) // 256)
     assert all(v == 1 for v in seen.values())
     # split-K parts: each CTA's partial has its own workspace slot (rank r of
@@ -425,7 +448,7 @@ def test_pair_schedule_covers_work_exactly_once(shape, opts):
 def test_dda_picks_pair_kernel_only_where_it_pays():
     """Dense-enough patterns go to the CTA-pair kernel, sparse ones stay on
     the single-CTA kernel (the pair's wider column unions cost more there)."""
-    for p, want in [(0.05, 1), (0.5, 2)]:
+    for p, want in [(0.05, 1), (0.1, 1), (0.25, 2), (0.5, 2)]:
         rng = np.random.default_rng(77)
         rp, ci, _ = rand_bsr(rng, 4096, 4096, 32, 32, p)
         plan = bsp.inspect_spmm_plan(4096, 4096, 32, 32, rp, ci, 4096, bsp.DDA)

@@ -425,7 +425,9 @@ bsp_status bsp_attn_host(bsp_device* dev, int64_t S, int64_t d, int64_t nnzb, co
  * count (a generalisation of the reference's serpentine balancer,
  * block_spmm/inc/host_code/bsr_spmm_multicore_load_balanced_new_DM.cpp:346-393,
  * to ranges, so that each GPU's C row-panel is contiguous for the all-gather).
- * bounds[parts + 1]: GPU p owns block-rows [bounds[p], bounds[p+1]). */
+ * A range weighs its blocks plus one per row; the ranges minimise the
+ * heaviest one, and among such splits each range takes about its share of
+ * the rest.  bounds[parts + 1]: GPU p owns block-rows [bounds[p], bounds[p+1]). */
 bsp_status bsp_partition_rows(const int32_t* row_ptr, int64_t n_block_rows, int32_t parts,
                               int64_t* bounds);
 

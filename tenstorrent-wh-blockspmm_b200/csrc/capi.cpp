@@ -1580,17 +1580,59 @@ bsp_status bsp_partition_rows(const int32_t* row_ptr, int64_t n_block_rows, int3
                               int64_t* bounds) {
   if (!row_ptr || !bounds || parts < 1 || n_block_rows < 0)
     return set_error(BSP_ERR_INVALID_ARG, "bad arguments");
-  // Balance blocks plus one unit per row (every row costs its C writes).
-  const int64_t total = row_ptr[n_block_rows] + n_block_rows;
-  bounds[0] = 0;
-  int64_t r = 0;
-  for (int p = 1; p < parts; ++p) {
-    const int64_t target = total * p / parts;
-    while (r < n_block_rows && row_ptr[r] + r < target) ++r;
-    bounds[p] = r;
+  // Balance blocks plus one unit per row (every row costs its C writes).  The
+  // ranges minimise the heaviest range (a row of a thousand blocks next to a
+  // cut otherwise lands whole on one range), and among those that reach the
+  // minimum, each range takes about its share of what is left.
+  const int64_t n = n_block_rows;
+  auto wt = [&](int64_t i) { return int64_t(row_ptr[i + 1]) - row_ptr[i] + 1; };
+  const int64_t total = int64_t(row_ptr[n]) - row_ptr[0] + n;
+  int64_t lo = 0, hi = std::max<int64_t>(total, 1);
+  for (int64_t i = 0; i < n; ++i) lo = std::max(lo, wt(i));
+  auto ranges_needed = [&](int64_t cap) {
+    int64_t cnt = 0, w = 0;
+    for (int64_t i = 0; i < n; ++i) {
+      if (w + wt(i) > cap) {
+        ++cnt;
+        w = 0;
+      }
+      w += wt(i);
+    }
+    return cnt + (w > 0 ? 1 : 0);
+  };
+  while (lo < hi) {
+    const int64_t mid = lo + (hi - lo) / 2;
+    if (ranges_needed(mid) <= parts) hi = mid;
+    else lo = mid + 1;
   }
-  bounds[parts] = n_block_rows;
-  for (int p = 1; p <= parts; ++p) bounds[p] = std::max(bounds[p], bounds[p - 1]);
+  const int64_t cap = lo;
+  // need[i]: ranges that rows [i, n) take at the cap (greedy, two pointers)
+  std::vector<int64_t> need(static_cast<size_t>(n) + 1, 0);
+  {
+    int64_t j = n, w = 0;
+    for (int64_t i = n - 1; i >= 0; --i) {
+      w += wt(i);
+      while (w > cap) {
+        --j;
+        w -= wt(j);
+      }
+      need[static_cast<size_t>(i)] = 1 + need[static_cast<size_t>(j)];
+    }
+  }
+  bounds[0] = 0;
+  int64_t r = 0, left = total;
+  for (int p = 0; p + 1 < parts; ++p) {
+    const int64_t share = left / (parts - p);
+    int64_t w = 0;
+    while (r < n && w + wt(r) <= cap &&
+           (need[static_cast<size_t>(r)] > parts - p - 1 || 2 * (w + wt(r)) <= 2 * share + wt(r))) {
+      w += wt(r);
+      ++r;
+    }
+    left -= w;
+    bounds[p + 1] = r;
+  }
+  bounds[parts] = n;
   return BSP_OK;
 }
 

@@ -464,7 +464,7 @@ static void ordered_greedy(const std::vector<int64_t>& weight, int parts,
 // parts of a cut unit in its place; otherwise by the serpentine balancer.
 static std::vector<int32_t> choose_splits(const std::vector<int64_t>& weight, const std::vector<int32_t>& nsteps,
                                           int ctas, int64_t partial_bytes, bool ordered = false) {
-  constexpr int kMaxSplit = 4, kMinPartSteps = 4;
+  constexpr int kMaxSplit = 8, kMinPartSteps = 4;
   const size_t n = weight.size();
   std::vector<int32_t> best(n, 1);
   if (n == 0 || ctas < 2) return best;

@@ -456,8 +456,10 @@ bsp_status plan_spmm_host(bsp_spmm_plan* p, const int32_t* row_ptr, const int32_
 // and the cut whose serpentine deal has the shortest makespan is kept if it
 // beats the uncut deal by 3%.  Each part is charged its partial's write plus
 // the final sum's read of all n partials: the merge is bound by L2 round
-// trips on the merging CTA's critical path, so parts are also capped at 4
-// (a 16-part merge of config 5's longest rows cost more than it balanced).
+// trips on the merging CTA's critical path, so parts are also capped at 8
+// (16-part merges of config 5's longest rows cost more than they balanced;
+// 8 parts leave one GPU's config 5 unchanged and shorten the slowest CTA of
+// an 8-GPU row panel holding a 1000-block row by 16%).
 static void ordered_greedy(const std::vector<int64_t>& weight, int parts,
                            std::vector<std::vector<int32_t>>* per_part);
 // ordered: the units are dealt in their given order (ordered_greedy), the

@@ -54,6 +54,35 @@ def test_serpentine_matches_oracle(n, parts):
         assert np.array_equal(o1, o2) and np.array_equal(s1, s2)
 
 
+def _min_heaviest_range(w, parts):
+    """Brute force: the least possible weight of the heaviest of `parts`
+    contiguous ranges of w (dynamic programming over cut points)."""
+    n = len(w)
+    pre = np.concatenate([[0], np.cumsum(w)])
+    INF = float("inf")
+    best = [[INF] * (n + 1) for _ in range(parts + 1)]
+    best[0][0] = 0
+    for k in range(1, parts + 1):
+        for j in range(n + 1):
+            best[k][j] = min(max(best[k - 1][i], pre[j] - pre[i]) for i in range(j + 1))
+    return best[parts][n]
+
+
+def test_partition_rows_minimises_the_heaviest_range():
+    """Power-law rows next to the cuts: the ranges reach the least possible
+    heaviest range (blocks + one per row), and no range is over it."""
+    rng = np.random.default_rng(5)
+    for _ in range(40):
+        nbr = int(rng.integers(1, 40))
+        cnt = (rng.zipf(1.3, nbr).clip(0, 400) * rng.integers(0, 2, nbr)).astype(np.int64)
+        rp = np.concatenate([[0], np.cumsum(cnt)]).astype(np.int32)
+        for parts in (1, 2, 3, 5, 8):
+            b = bsp.partition_rows(rp, parts)
+            assert b[0] == 0 and b[-1] == nbr and np.all(np.diff(b) >= 0)
+            w = [int(rp[b[i + 1]] - rp[b[i]] + (b[i + 1] - b[i])) for i in range(parts)]
+            assert max(w) == _min_heaviest_range(cnt + 1, parts), (cnt.tolist(), parts, w)
+
+
 def test_partition_rows_properties():
     rng = np.random.default_rng(0)
     for _ in range(50):

@@ -241,7 +241,8 @@ bsp_status bsp_spmm_host_profile(bsp_device* dev, int64_t M, int64_t K, int32_t 
  * soon as its inputs have landed, so job k's C travels to the host while the
  * inputs of jobs k+1... still come in (PCIe copies in both directions at
  * once).  A job whose N is a multiple of 512 (and at least 1024) runs as two
- * column panels of one plan, with B and C copied panel by panel.  Device
+ * column panels of one plan (four from N = 8192), with B and C copied panel
+ * by panel.  Device
  * buffers for all jobs come from the device's grow-only workspace.  Returns
  * after every C_out is written. */
 typedef struct bsp_spmm_host_job {

@@ -819,17 +819,21 @@ bsp_status bsp_spmm_host_batch(bsp_device* dev, int32_t n_jobs, const bsp_spmm_h
                  align256(sizeof(uint16_t) * j.K * j.N) + align256(sizeof(uint16_t) * j.M * j.N);
   }
   bsp_status s = ws_reserve(dev, off[nj]);
-  if (s == BSP_OK) s = host_streams(dev, 2 * nj);
+  if (s == BSP_OK) s = host_streams(dev, 4 * nj);
   if (s != BSP_OK) return s;
   if (dev->batch_slots.size() < nj) dev->batch_slots.resize(nj);
-  // A job whose N is a multiple of 512 (from 1024) runs as two column panels
-  // of one plan: the first panel's kernel starts when that half of B is in,
-  // and the first half of C goes back while the second half of B still
-  // arrives, so less of the step is spent with one copy direction idle (the
-  // sweep's e2e: 24 -> 25 TF/s; four panels measured the same as two).
+  // A wide job runs as 2 or 4 column panels of one plan (whole 256-column
+  // tiles; 2 panels from N = 1024, 4 from N = 8192): the first panel's
+  // kernel starts when that panel of B is in, and each panel of C goes back
+  // while later panels of B still arrive, so less of the step is spent with
+  // one copy direction idle (the sweep's e2e: 24 -> 25 TF/s; four panels of
+  // its N = 4096 measured no better than two).
   std::vector<int> panels(nj, 1);
-  for (size_t k = 0; k < nj; ++k)
-    if (jobs[k].N % 512 == 0 && jobs[k].N >= 1024) panels[k] = 2;
+  for (size_t k = 0; k < nj; ++k) {
+    const int64_t n = jobs[k].N;
+    if (n % 2048 == 0 && n >= 8192) panels[k] = 4;
+    else if (n % 512 == 0 && n >= 1024) panels[k] = 2;
+  }
   cudaStream_t sh = dev->s_h2d, sc = dev->s_comp, sd = dev->s_d2h;
   struct Dev {
     void* val;
@@ -896,7 +900,7 @@ bsp_status bsp_spmm_host_batch(bsp_device* dev, int32_t n_jobs, const bsp_spmm_h
       if (st == BSP_OK)
         st = cuda_check(cudaMemcpyAsync(d[k].B, j.B, sizeof(uint16_t) * j.K * j.N, cudaMemcpyHostToDevice, sh),
                         "H2D B");
-      if (st == BSP_OK) st = cuda_check(cudaEventRecord(dev->ev_in[2 * k], sh), "cudaEventRecord");
+      if (st == BSP_OK) st = cuda_check(cudaEventRecord(dev->ev_in[4 * k], sh), "cudaEventRecord");
     } else {
       const size_t pitch = sizeof(uint16_t) * static_cast<size_t>(j.N), part = pitch / panels[k];
       for (int h = 0; h < panels[k] && st == BSP_OK; ++h) {
@@ -904,7 +908,7 @@ bsp_status bsp_spmm_host_batch(bsp_device* dev, int32_t n_jobs, const bsp_spmm_h
                                           reinterpret_cast<const uint8_t*>(j.B) + h * part, pitch, part,
                                           static_cast<size_t>(j.K), cudaMemcpyHostToDevice, sh),
                         "H2D B panel");
-        if (st == BSP_OK) st = cuda_check(cudaEventRecord(dev->ev_in[2 * k + h], sh), "cudaEventRecord");
+        if (st == BSP_OK) st = cuda_check(cudaEventRecord(dev->ev_in[4 * k + h], sh), "cudaEventRecord");
       }
     }
     return st;
@@ -965,7 +969,7 @@ bsp_status bsp_spmm_host_batch(bsp_device* dev, int32_t n_jobs, const bsp_spmm_h
       bsp_bsr_desc A{j.M, j.K, j.R, j.C, j.nnzb, d[k].rp, d[k].ci, d[k].val};
       const int64_t nh = j.N / panels[k];
       for (int h = 0; h < panels[k] && st == BSP_OK; ++h) {
-        const size_t e = 2 * k + static_cast<size_t>(h);
+        const size_t e = 4 * k + static_cast<size_t>(h);
         st = cuda_check(cudaStreamWaitEvent(sc, dev->ev_in[e], 0), "cudaStreamWaitEvent");
         if (st == BSP_OK) st = bsp_spmm_execute(p, &A, d[k].B + h * nh, j.N, d[k].C + h * nh, j.N, sc);
         if (st == BSP_OK) st = cuda_check(cudaEventRecord(dev->ev_out[e], sc), "cudaEventRecord");

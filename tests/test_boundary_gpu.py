@@ -97,8 +97,10 @@ def test_spmm_host_batch_matches_oracle(strategy):
 
     rng = np.random.default_rng(23)
     jobs, golds = [], []
+    # N = 1024 and 8192 run as 2 and 4 column panels of one plan
     for M, K, N, R, C, p in [(4096, 4096, 1024, 32, 32, 0.5), (1024, 2048, 256, 64, 64, 0.2),
-                             (2048, 1024, 512, 32, 32, 0.01), (512, 512, 96, 32, 64, 0.3)]:
+                             (2048, 1024, 512, 32, 32, 0.01), (512, 512, 96, 32, 64, 0.3),
+                             (512, 1024, 8192, 64, 64, 0.2)]:
         rp, ci, vals = rand_bsr(rng, M, K, R, C, p, empty_rows=(1,))
         B = rand_dense(rng, K, N)
         jobs.append(dict(M=M, K=K, R=R, C=C, row_ptr=rp, col_idx=ci, values=vals, B=B, N=N))
